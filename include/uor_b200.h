@@ -1,0 +1,266 @@
+/*
+ * uor_b200.h -- C ABI of the B200 exact-GEMM library (libuor_b200.so).
+ *
+ * A drop-in for the exact-accumulation GEMM path of uor-matmul (the Rust crate
+ * UOR-Foundation/uor-matmul). Each entry point below names the reference
+ * interface it replaces (path:line in that crate). The semantics are the
+ * reference's: every product is accumulated exactly, the result is encoded
+ * exactly once (saturate, wrap, or round-to-nearest-even for floats), and the
+ * bytes written are the bytes the reference writes for the same inputs.
+ *
+ * Conventions
+ *   - Plain pointers and sizes; no C++ or framework types cross this boundary.
+ *   - Sizes and lengths are in ELEMENTS of the named dtype; strides are signed
+ *     element strides (Strides { rs, cs }, crates/uor-matmul-core/src/layout.rs:29).
+ *   - i128 values are 16-byte little-endian two's complement.
+ *   - Trop<E> is the reference's repr(C) { E value; bool finite } struct
+ *     (crates/uor-matmul-core/src/tropical.rs:61-70): 2, 4, 8, 16 bytes for
+ *     E = i8, i16, i32, i64. The semiring zero stores value 0 and finite 0.
+ *   - Pointers are host pointers unless the call sets UOR_B200_DEVICE_POINTERS.
+ *     Host-pointer calls stage operands through the context's device buffers.
+ *   - Every call is synchronous (returns after the result is in C) unless the
+ *     call sets UOR_B200_ASYNC, which is honoured only with device pointers;
+ *     an asynchronous call's device status is reported by uor_b200_ctx_sync.
+ *   - The library never reads C when beta is zero (epilogue.rs:73-77) and never
+ *     when a tropical beta is the semiring zero (epilogue.rs:166-170).
+ */
+#ifndef UOR_B200_H
+#define UOR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+
+/* 1 and 2 are NotAProduct's two variants (crates/uor-matmul-core/src/error.rs:104-131),
+ * reported where Triple::new reports them (layout.rs:534-561). The others have no
+ * reference counterpart except UOR_B200_DOES_NOT_FIT, which is the slice face's
+ * `does_not_fit` panic (crates/uor-matmul/src/slice.rs:104-116) returned as a code. */
+typedef enum uor_b200_status {
+    UOR_B200_OK = 0,
+    UOR_B200_NONCONFORMANT = 1,    /* NotAProduct::Nonconformant */
+    UOR_B200_OUTPUT_ALIASES = 2,   /* NotAProduct::OutputAliasesItself */
+    UOR_B200_DEVICE_ERROR = 3,     /* a CUDA runtime error */
+    UOR_B200_TIMEOUT = 4,          /* a bounded device wait ran out */
+    UOR_B200_NCCL_ERROR = 5,       /* reserved for collective-backed calls */
+    UOR_B200_DOES_NOT_FIT = 6,     /* a buffer does not hold the view its caller described */
+    UOR_B200_INVALID_ARGUMENT = 7, /* unknown enum value, or a null pointer with extent */
+    UOR_B200_UNSUPPORTED = 8       /* an element/output pair outside the reference's surface */
+} uor_b200_status;
+
+/* EncodeMode, crates/uor-matmul-core/src/policy.rs:20-48. */
+typedef enum uor_b200_encode {
+    UOR_B200_NEAREST = 0,     /* default: round half to even; saturate integers */
+    UOR_B200_TOWARD_ZERO = 1,
+    UOR_B200_SATURATING = 2,
+    UOR_B200_WRAPPING = 3
+} uor_b200_encode;
+
+/* Element and output types. */
+typedef enum uor_b200_dtype {
+    UOR_B200_I8 = 1,
+    UOR_B200_I16 = 2,
+    UOR_B200_I32 = 3,
+    UOR_B200_I64 = 4,
+    UOR_B200_I128 = 5,
+    UOR_B200_F32 = 6,
+    UOR_B200_F64 = 7,
+    UOR_B200_TROP_I8 = 8,
+    UOR_B200_TROP_I16 = 9,
+    UOR_B200_TROP_I32 = 10,
+    UOR_B200_TROP_I64 = 11
+} uor_b200_dtype;
+
+/* ----------------------------------------------------------------- context */
+
+/* A device, a stream, device workspaces, and a status word for bounded waits.
+ * Distinct contexts may be used from distinct threads concurrently. */
+typedef struct uor_b200_ctx uor_b200_ctx;
+
+uor_b200_ctx *uor_b200_ctx_create(int device);
+void uor_b200_ctx_destroy(uor_b200_ctx *ctx);
+/* Run this context's work on `stream` (a cudaStream_t); NULL restores its own. */
+int uor_b200_ctx_set_stream(uor_b200_ctx *ctx, void *stream);
+/* Upper bound on any single device-side wait, in nanoseconds (default 2 s). */
+int uor_b200_ctx_set_wait_budget_ns(uor_b200_ctx *ctx, uint64_t ns);
+/* Wait for the context's stream; report a device timeout or error. */
+int uor_b200_ctx_sync(uor_b200_ctx *ctx);
+
+/* Which factorization ran: the analogue of Route / RouteCensus
+ * (crates/uor-matmul-gemm/src/kernel.rs:419-484). */
+typedef enum uor_b200_kernel {
+    UOR_B200_KERNEL_NONE = 0,          /* nothing to compute (m == 0 or n == 0) */
+    UOR_B200_KERNEL_I8_TCGEN05 = 1,    /* K1: s8 x s8 -> s32 TMEM, exact epilogue */
+    UOR_B200_KERNEL_LIMB_TCGEN05 = 2,  /* K2: byte-sliced limb GEMMs, exact recombination */
+    UOR_B200_KERNEL_TROPICAL = 3,      /* K4: packed max-plus on CUDA cores */
+    UOR_B200_KERNEL_CODED_TCGEN05 = 4, /* K5: codebook decode feeding K1's MMA */
+    UOR_B200_KERNEL_FLOAT_EXACT = 5,   /* K6+K7: exact float, one rounding */
+    UOR_B200_KERNEL_EPILOGUE_ONLY = 6  /* k == 0: C := encode(beta * C) */
+} uor_b200_kernel;
+
+typedef struct uor_b200_route {
+    uint32_t kernel;      /* uor_b200_kernel */
+    uint32_t tile_m, tile_n, tile_k;
+    uint32_t k_chunks;    /* exact reduction chunks (lane depth, kernel.rs:1431) */
+    uint32_t a_layout;    /* 0 K-major, 1 MN-major, 2 gathered to K-major */
+    uint32_t b_layout;
+    uint32_t ctas;        /* CTAs launched per chunk */
+} uor_b200_route;
+
+#define UOR_B200_DEVICE_POINTERS 1u
+#define UOR_B200_ASYNC 2u
+
+/* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)
+ * plus where the pointers live. A NULL call means: Nearest, host pointers,
+ * the default context of the current device. */
+typedef struct uor_b200_call {
+    uint32_t encode;        /* uor_b200_encode */
+    uint32_t flags;         /* UOR_B200_DEVICE_POINTERS | UOR_B200_ASYNC */
+    uor_b200_ctx *ctx;      /* NULL: the current device's default context */
+    uor_b200_route *route;  /* optional out */
+} uor_b200_call;
+
+/* ------------------------------------------------------------------- views */
+
+/* MatView / MatViewMut (layout.rs:158-219): a buffer of `len` elements borrowed
+ * as rows x cols with arbitrary strides. The origin is placed so that the
+ * lowest offset the view reaches is element 0 of the buffer (layout.rs:178-199). */
+typedef struct uor_b200_view {
+    const void *data;
+    size_t len;
+    size_t rows, cols;
+    ptrdiff_t rs, cs;
+} uor_b200_view;
+
+typedef struct uor_b200_view_mut {
+    void *data;
+    size_t len;
+    size_t rows, cols;
+    ptrdiff_t rs, cs;
+} uor_b200_view_mut;
+
+/* --------------------------------------------------------- integer family */
+
+/* The view API's default entry: gemm_auto(&mut Triple, &Linear{alpha, beta},
+ * GemmOptions, &mut Scratch) (crates/uor-matmul-gemm/src/kernel.rs:523-558,
+ * re-exported as uor_matmul::gemm, crates/uor-matmul/src/lib.rs:135).
+ * elem in {I8, I16, I32, I64}; out in {I8, I16, I32, I64, I128}.
+ * Errors as Triple::new (layout.rs:534-561); DOES_NOT_FIT as MatView::new's None. */
+int uor_b200_gemm(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view *a,
+                  const uor_b200_view *b, const uor_b200_view_mut *c, int64_t alpha,
+                  int64_t beta, const uor_b200_call *call);
+
+/* slice::gemm_ex (crates/uor-matmul/src/slice.rs:144-178): row-major with
+ * leading dimensions; `scratch` is the caller's panel offer, accepted and
+ * ignored (the offer never changes bytes, slice.rs:23-41). */
+int uor_b200_slice_gemm_ex(uor_b200_dtype elem, uor_b200_dtype out, size_t m, size_t k, size_t n,
+                           int64_t alpha, const void *a, size_t a_len, size_t lda, const void *b,
+                           size_t b_len, size_t ldb, int64_t beta, void *c, size_t c_len,
+                           size_t ldc, void *scratch, size_t scratch_len,
+                           const uor_b200_call *call);
+
+/* slice::gemm (slice.rs:184-199): contiguous, alpha 1, beta 0. */
+int uor_b200_slice_gemm(uor_b200_dtype elem, uor_b200_dtype out, size_t m, size_t k, size_t n,
+                        const void *a, size_t a_len, const void *b, size_t b_len, void *c,
+                        size_t c_len, void *scratch, size_t scratch_len,
+                        const uor_b200_call *call);
+
+/* slice::gemm_ex_full / gemm_full (slice.rs:221-283): the accumulator offer is
+ * accepted and ignored as well. */
+int uor_b200_slice_gemm_ex_full(uor_b200_dtype elem, uor_b200_dtype out, size_t m, size_t k,
+                                size_t n, int64_t alpha, const void *a, size_t a_len, size_t lda,
+                                const void *b, size_t b_len, size_t ldb, int64_t beta, void *c,
+                                size_t c_len, size_t ldc, void *panels, size_t panels_len,
+                                void *accumulators, size_t accumulators_len,
+                                const uor_b200_call *call);
+
+/* The canonical W8A8 instantiation, monomorphised: slice::gemm::<i8, i32> and
+ * slice::gemm_ex::<i8, i32>. */
+int uor_b200_gemm_i8_i32(size_t m, size_t k, size_t n, const int8_t *a, const int8_t *b,
+                         int32_t *c, const uor_b200_call *call);
+int uor_b200_gemm_ex_i8_i32(size_t m, size_t k, size_t n, int64_t alpha, const int8_t *a,
+                            size_t lda, const int8_t *b, size_t ldb, int64_t beta, int32_t *c,
+                            size_t ldc, const uor_b200_call *call);
+
+/* ----------------------------------------------------------- float family */
+
+/* gemm_float_packed over a Triple (crates/uor-matmul-gemm/src/float.rs:1824)
+ * with Linear: C := RNE-once(alpha * exact(A B) + beta * C).
+ * elem in {F32, F64}; out in {F32, F64}. */
+int uor_b200_gemm_float(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view *a,
+                        const uor_b200_view *b, const uor_b200_view_mut *c, int64_t alpha,
+                        int64_t beta, const uor_b200_call *call);
+
+/* slice::gemm_float_ex / gemm_float (slice.rs:304-429); pa/pb are the caller's
+ * PackedCode caches (16 bytes each), accepted and ignored. */
+int uor_b200_slice_gemm_float_ex(uor_b200_dtype elem, uor_b200_dtype out, size_t m, size_t k,
+                                 size_t n, int64_t alpha, const void *a, size_t a_len, size_t lda,
+                                 const void *b, size_t b_len, size_t ldb, int64_t beta, void *c,
+                                 size_t c_len, size_t ldc, void *pa, size_t pa_len, void *pb,
+                                 size_t pb_len, const uor_b200_call *call);
+
+/* raw::sgemm / raw::dgemm (crates/uor-matmul/src/raw.rs:45-90): matrixmultiply's
+ * signature with exact integer alpha/beta and arbitrary (even negative) strides;
+ * a pointer names element (0,0). m == 0 or n == 0 returns at once, and a view
+ * that cannot exist returns without writing (raw.rs:137-148). */
+int uor_b200_sgemm(size_t m, size_t k, size_t n, int64_t alpha, const float *a, ptrdiff_t rsa,
+                   ptrdiff_t csa, const float *b, ptrdiff_t rsb, ptrdiff_t csb, int64_t beta,
+                   float *c, ptrdiff_t rsc, ptrdiff_t csc, const uor_b200_call *call);
+int uor_b200_dgemm(size_t m, size_t k, size_t n, int64_t alpha, const double *a, ptrdiff_t rsa,
+                   ptrdiff_t csa, const double *b, ptrdiff_t rsb, ptrdiff_t csb, int64_t beta,
+                   double *c, ptrdiff_t rsc, ptrdiff_t csc, const uor_b200_call *call);
+
+/* -------------------------------------------------------- tropical family */
+
+/* A Trop<i64> scalar for MaxPlus (crates/uor-matmul-gemm/src/epilogue.rs:137-186). */
+typedef struct uor_b200_trop {
+    int64_t value;
+    uint32_t finite; /* 0: the semiring zero (-inf) */
+} uor_b200_trop;
+
+/* driver::gemm over Alphabet<Trop<E>, _> with MaxPlus{alpha, beta}
+ * (crates/uor-matmul-gemm/src/driver.rs:67-182): C := (alpha (x) A(x)B) (+) (beta (x) C)
+ * in (max, +). elem in {TROP_I8, TROP_I16}; out in {TROP_I8 .. TROP_I64}. */
+int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view *a,
+                           const uor_b200_view *b, const uor_b200_view_mut *c,
+                           uor_b200_trop alpha, uor_b200_trop beta, const uor_b200_call *call);
+
+/* ----------------------------------------------------------- codec family */
+
+/* coded_gemm (crates/uor-matmul-gemm/src/coded.rs:98-142) with B a CodedMatrix
+ * (crates/uor-matmul-codec/src/matrix.rs:15-219) of Packed<Grid<N>, P> codes
+ * (codecs.rs:80-196): B is k x n, each byte holds P sub-codes of 8/P bits, low
+ * sub-code first; element (r, c) decodes table[sub % N] with
+ * sub = (codes[r * (n / P) + c / P] >> ((8 / P) * (c % P))) & mask.
+ * A is a dense i8 view; out in {I8 .. I128}. P in {1, 2}; 1 <= N <= 256. */
+int uor_b200_coded_gemm(uor_b200_dtype out, const uor_b200_view *a, const uint8_t *codes,
+                        size_t codes_len, size_t k, size_t n, uint32_t per_byte,
+                        const int8_t *table, size_t table_len, const uor_b200_view_mut *c,
+                        int64_t alpha, int64_t beta, const uor_b200_call *call);
+
+/* gemm_tabulated's product (crates/uor-matmul-gemm/src/tabulated.rs:600-660, 2555):
+ * the same codec with W coded n x k (one coded row per output column), C = A W^T. */
+int uor_b200_tabulated_gemm(uor_b200_dtype out, const uor_b200_view *a, const uint8_t *codes,
+                            size_t codes_len, size_t k, size_t n, uint32_t per_byte,
+                            const int8_t *table, size_t table_len, const uor_b200_view_mut *c,
+                            int64_t alpha, int64_t beta, const uor_b200_call *call);
+
+/* ----------------------------------------------------------------- misc */
+
+const char *uor_b200_status_string(int status);
+/* ABI version: major * 10000 + minor * 100 + patch. */
+int uor_b200_version(void);
+/* Self-test of the bounded-wait path: launches a kernel that waits on a barrier
+ * nothing will complete, with the given budget; returns UOR_B200_TIMEOUT when
+ * the wait gave up as designed, and leaves the context usable. */
+int uor_b200_selftest_wait_timeout(uor_b200_ctx *ctx, uint64_t budget_ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UOR_B200_H */

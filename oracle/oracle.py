@@ -60,6 +60,7 @@ def lib():
         _LIB.uor_oracle_coded_gemm.argtypes = [I, Z, Z, Z, L, P, D, D, P, I, P, Z, I, L, P, D, D,
                                                I, I]
         _LIB.uor_oracle_max_threads.restype = I
+        _LIB.uor_oracle_gemm_i8_blocked.argtypes = [Z, Z, Z, L, P, P, L, P, Z, I, I]
     return _LIB
 
 
@@ -103,6 +104,12 @@ def gemm_int(a: View, b: View, c: View, alpha=1, beta=0, mode=NEAREST, threads=0
     obits = out_bits or _bits_of(c.arr.dtype)
     lib().uor_oracle_gemm_int(ebits, obits, a.rows, a.cols, b.cols, alpha, a.ptr(), a.rs, a.cs,
                               b.ptr(), b.rs, b.cs, beta, c.ptr(), c.rs, c.cs, mode, threads)
+
+
+def gemm_i8_blocked(a, b, c, m, k, n, alpha=1, beta=0, ldc=None, mode=NEAREST, threads=0):
+    """The blocked s8 restatement (contiguous row-major operands), for CPU timing."""
+    lib().uor_oracle_gemm_i8_blocked(m, k, n, alpha, a.ctypes.data, b.ctypes.data, beta,
+                                     c.ctypes.data, n if ldc is None else ldc, mode, threads)
 
 
 def gemm_float(a: View, b: View, c: View, alpha=1, beta=0, mode=NEAREST, threads=0):

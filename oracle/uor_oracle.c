@@ -632,6 +632,71 @@ int uor_oracle_gemm_float(int e64, int o64, size_t m, size_t k, size_t n, int64_
     return 0;
 }
 
+/*
+ * A blocked restatement of the reference's kernel traversal for s8 x s8
+ * (kernel.rs:1016-1377 with the I8_I32 tile family): B is packed K-major once
+ * (pack_columns, kernel.rs:1703), each dot product runs in s32 lanes over chunks
+ * of at most lane_depth = 131071 products (spec.rs:232-243) and folds into an
+ * int64, then the Linear epilogue and encode run once per cell. Same bytes as
+ * uor_oracle_gemm_int; it exists to time the CPU baseline fairly.
+ * Row-major contiguous A (m x k) and B (k x n); C row-major with ldc.
+ */
+__attribute__((target("avx2"))) static int64_t dot_i8_avx2(const int8_t *x, const int8_t *y,
+                                                           size_t k) {
+    int64_t total = 0;
+    for (size_t p0 = 0; p0 < k; p0 += 131071) {
+        size_t end = p0 + 131071 < k ? p0 + 131071 : k;
+        int32_t s = 0;
+        for (size_t p = p0; p < end; p++) s += (int32_t)x[p] * (int32_t)y[p];
+        total += s;
+    }
+    return total;
+}
+
+static int64_t dot_i8_generic(const int8_t *x, const int8_t *y, size_t k) {
+    int64_t total = 0;
+    for (size_t p0 = 0; p0 < k; p0 += 131071) {
+        size_t end = p0 + 131071 < k ? p0 + 131071 : k;
+        int32_t s = 0;
+        for (size_t p = p0; p < end; p++) s += (int32_t)x[p] * (int32_t)y[p];
+        total += s;
+    }
+    return total;
+}
+
+int uor_oracle_gemm_i8_blocked(size_t m, size_t k, size_t n, int64_t alpha, const int8_t *a,
+                               const int8_t *b, int64_t beta, int32_t *c, size_t ldc, int mode,
+                               int threads) {
+    if (m == 0 || n == 0) return 0;
+    set_threads(threads);
+    int8_t *bt = (int8_t *)malloc(n * k + 64);
+    if (!bt) return -1;
+    long long nn = (long long)n;
+#pragma omp parallel for schedule(static)
+    for (long long jj = 0; jj < nn; jj++)
+        for (size_t p = 0; p < k; p++) bt[(size_t)jj * k + p] = b[p * n + (size_t)jj];
+    int avx2 = __builtin_cpu_supports("avx2");
+    long long mm = (long long)m;
+    const size_t JB = 64;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (long long ii = 0; ii < mm; ii++) {
+        size_t i = (size_t)ii;
+        for (size_t j0 = 0; j0 < n; j0 += JB) {
+            size_t j1 = j0 + JB < n ? j0 + JB : n;
+            for (size_t j = j0; j < j1; j++) {
+                int64_t acc = avx2 ? dot_i8_avx2(a + i * k, bt + j * k, k)
+                                   : dot_i8_generic(a + i * k, bt + j * k, k);
+                i128 tot = sat_mul_i128((i128)acc, alpha);
+                if (beta != 0)
+                    tot = (i128)((u128)tot + (u128)sat_mul_i128((i128)c[i * ldc + j], beta));
+                c[i * ldc + j] = (int32_t)encode_i128_into(tot, out_min(32), out_max(32), mode);
+            }
+        }
+    }
+    free(bt);
+    return 0;
+}
+
 /* The number of OpenMP threads a parallel region gets, for the baseline record. */
 int uor_oracle_max_threads(void) {
 #ifdef _OPENMP

@@ -1,0 +1,111 @@
+"""CPU-side checks of the C ABI: the library loads, exports every declared
+symbol, and performs the reference's host-side validation (MatView::new,
+Triple::new) before touching a device. No compute call runs here."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+import uor_b200 as U
+from oracle import oracle as orc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in os.listdir(os.path.join(ROOT, "include")):
+        if h.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", h)).read()
+            names |= set(re.findall(r"\b(uor_b200_[a-z0-9_]+)\s*\(", src))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    exported = set(U.exported_symbols())
+    declared = declared_symbols()
+    assert declared, "the headers declare entry points"
+    missing = declared - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+
+
+def test_version_and_status_strings():
+    assert U.lib().uor_b200_version() >= 100
+    assert "nonconformant" in U.status_string(U.NONCONFORMANT)
+    assert "aliases" in U.status_string(U.OUTPUT_ALIASES)
+
+
+def test_corpus_matches_reference_generator():
+    # validate/tests/common/mod.rs:9-19, restated independently in oracle.corpus_fill
+    raw = U.corpus(1, U.CORPUS_RAW, 1000)
+    assert np.array_equal(raw, orc.corpus_fill(1, 1000))
+    i8 = U.corpus(2, U.CORPUS_I8, 1000)
+    assert np.array_equal(i8, orc.corpus_fill(2, 1000).astype(np.uint8).view(np.int8))
+    nib = U.corpus(3, U.CORPUS_NIBBLES, 1001)
+    v = orc.corpus_fill(3, 1001) & np.uint64(0xF)
+    assert nib[0] == (v[0] | (v[1] << np.uint64(4)))
+    assert nib[-1] == v[-1]
+
+
+def _gemm_status(m, k, n, a_len, b_len, c_len, rsa, csa, rsb, csb, rsc, csc, am=None, bk=None,
+                 cn=None):
+    a = np.zeros(max(a_len, 1), np.int8)
+    b = np.zeros(max(b_len, 1), np.int8)
+    c = np.zeros(max(c_len, 1), np.int32)
+    A = U.View(a.ctypes.data, a_len, m if am is None else am, k, rsa, csa)
+    B = U.View(b.ctypes.data, b_len, k if bk is None else bk, n, rsb, csb)
+    C = U.View(c.ctypes.data, c_len, m, n if cn is None else cn, rsc, csc)
+    call = U.make_call()
+    import ctypes
+    return U.lib().uor_b200_gemm(U.I8, U.I32, ctypes.byref(A), ctypes.byref(B), ctypes.byref(C),
+                                 1, 0, ctypes.byref(call))
+
+
+def test_nonconformant_is_reported_before_any_device_work():
+    assert _gemm_status(2, 3, 4, 6, 12, 8, 3, 1, 4, 1, 4, 1, bk=2) == U.NONCONFORMANT
+    assert _gemm_status(2, 3, 4, 6, 12, 8, 3, 1, 4, 1, 4, 1, cn=3) == U.NONCONFORMANT
+
+
+def test_short_buffer_does_not_fit():
+    assert _gemm_status(2, 3, 4, 5, 12, 8, 3, 1, 4, 1, 4, 1) == U.DOES_NOT_FIT
+    assert _gemm_status(2, 3, 4, 6, 12, 7, 3, 1, 4, 1, 4, 1) == U.DOES_NOT_FIT
+
+
+def test_empty_products_need_no_device():
+    assert _gemm_status(0, 3, 4, 0, 12, 0, 3, 1, 4, 1, 4, 1) == U.OK
+    assert _gemm_status(2, 3, 0, 6, 0, 0, 3, 1, 0, 1, 0, 1) == U.OK
+
+
+def test_unsupported_pairs_are_refused():
+    import ctypes
+    a = np.zeros(4, np.int8)
+    v = U.View(a.ctypes.data, 4, 2, 2, 2, 1)
+    call = U.make_call()
+    # f32 output from an integer element is outside the reference's surface
+    assert U.lib().uor_b200_gemm(U.I8, U.F32, ctypes.byref(v), ctypes.byref(v), ctypes.byref(v),
+                                 1, 0, ctypes.byref(call)) == U.UNSUPPORTED
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_alias_and_placement_agree_with_the_reference_rules(seed):
+    """Strides::self_aliases and place (layout.rs:116, 178), restated in the oracle,
+    against the library: an aliasing output is refused; a placeable, non-aliasing
+    one gets past validation (and then needs a device, which CPU runs lack)."""
+    rng = np.random.default_rng(seed)
+    for _ in range(40):
+        m, n = (int(x) for x in rng.integers(0, 6, size=2))
+        rsc, csc = (int(x) for x in rng.integers(-7, 8, size=2))
+        lo_hi = orc.extent(m, n, rsc, csc)
+        span = 0 if lo_hi is None else lo_hi[1] - lo_hi[0] + 1
+        c_len = span + int(rng.integers(0, 2))
+        st = _gemm_status(m, 1, n, m, n, c_len, 1, 1, n, 1, rsc, csc)
+        placed = orc.place(c_len, m, n, rsc, csc) is not None
+        if not placed:
+            assert st == U.DOES_NOT_FIT, (m, n, rsc, csc, c_len)
+        elif orc.self_aliases(m, n, rsc, csc):
+            assert st == U.OUTPUT_ALIASES, (m, n, rsc, csc)
+        elif m == 0 or n == 0:
+            assert st == U.OK
+        else:
+            assert st in (U.OK, U.DEVICE_ERROR), (m, n, rsc, csc, st)

@@ -1,0 +1,17 @@
+// int_gemm.h -- device-pointer drivers of the integer family.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include "internal.h"
+#include "int_epilogue.cuh"
+
+namespace uor {
+
+// s8 x s8 GEMM through K1. Pointers are device pointers to element (0,0);
+// strides are element strides. The Linear epilogue `epi` writes C.
+int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
+                const int8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc,
+                ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
+                uor_b200_route* route);
+
+}  // namespace uor

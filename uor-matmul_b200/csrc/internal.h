@@ -1,0 +1,66 @@
+// internal.h -- host-side plumbing shared by the C ABI translation units.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+#include "../../include/uor_b200.h"
+
+struct uor_b200_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;  // the stream work is issued on
+    cudaStream_t own_stream = nullptr;
+    int* d_status = nullptr;        // device status word for bounded waits
+    uint64_t budget_ns = 2000000000ull;
+    int sm_count = 148;
+    std::mutex mu;
+    // Growable device buffers: workspace (gathers, chunk partials) and the
+    // three staging slots host-pointer calls copy operands through.
+    void* buf[4] = {nullptr, nullptr, nullptr, nullptr};
+    size_t cap[4] = {0, 0, 0, 0};
+};
+
+namespace uor {
+
+enum Slot { SLOT_WS = 0, SLOT_A = 1, SLOT_B = 2, SLOT_C = 3 };
+
+// A device buffer of at least `bytes` in the given slot (grown with cudaMalloc;
+// the previous contents are not kept).
+void* ctx_buffer(uor_b200_ctx* ctx, int slot, size_t bytes, int* status);
+
+// The default context of the current device (created on first use).
+uor_b200_ctx* default_ctx(int* status);
+
+// Resolve the call's context and make its device current.
+uor_b200_ctx* resolve_ctx(const uor_b200_call* call, int* status);
+
+// After device work: synchronise (unless async) and fold the status word in.
+int finish_call(uor_b200_ctx* ctx, const uor_b200_call* call);
+
+int cuda_status(cudaError_t e);
+
+// cuTensorMapEncodeTiled for a 2-D uint8 tensor with 128-byte swizzle.
+// dim0 is the contiguous dimension; stride1 is the byte stride of dim1.
+bool make_tmap_u8(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                  uint64_t stride1, uint32_t box0, uint32_t box1);
+
+// A view after placement: origin pointer and the reach of the view in elements.
+struct Placed {
+    const uint8_t* origin;  // element (0,0)
+    ptrdiff_t lo, hi;        // lowest/highest offsets the view reaches (elements)
+    size_t rows, cols;
+    ptrdiff_t rs, cs;
+};
+
+// Strides::extent (layout.rs:71-102); false when the reach overflows.
+bool view_extent(size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs, ptrdiff_t* lo,
+                 ptrdiff_t* hi);
+// place (layout.rs:178-199): the origin index of a view inside `len` elements.
+bool view_place(size_t len, size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs, size_t* origin);
+// Strides::self_aliases (layout.rs:116-140).
+bool self_aliases(size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs);
+
+size_t dtype_size(uor_b200_dtype t);
+
+}  // namespace uor
