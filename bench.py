@@ -38,7 +38,7 @@ METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--size", type=int, default=SIZE)
@@ -53,51 +53,56 @@ def env_rank():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region (SM clock, reasons)."""
+    """SM clock and throttle reasons sampled through NVML during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
-        self.path = None
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
 
     def start(self):
+        import threading
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
+            return
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for name, bit in self.REASONS.items():
+                        if r & bit:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
+                time.sleep(0.002)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        time.sleep(0.01)
 
     def stop(self):
-        if not self.proc:
+        if not self._thread:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = []
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
+        self._stop.set()
+        self._thread.join()
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples),
+                "source": "NVML, every 2 ms during the timed region"}
 
 
 def cpu_baseline(size, budget_s=12.0):
@@ -156,6 +161,33 @@ def load_traffic():
         return None
 
 
+def run_e2e(args, U, torch, dist, ctx, stream, m, k, n, rank, world):
+    """The same product through the public call with pinned HOST buffers: every
+    step copies A and B in and C out inside the timed region."""
+    ops_per_step = 2.0 * m * k * n
+    Ah = torch.from_numpy(U.corpus(1, U.CORPUS_I8, m * k)).pin_memory()
+    Bh = torch.from_numpy(U.corpus(2 + 1000 * rank, U.CORPUS_I8, k * n)).pin_memory()
+    Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
+    U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx)  # warm the staging buffers
+    if dist:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    return {"value": world * args.e2e_steps * ops_per_step / (e2e_ms / 1e3) / 1e12,
+            "unit": "TOPS", "h2d_bytes_per_step": m * k + k * n, "d2h_bytes_per_step": 4 * m * n,
+            "ms_per_step": e2e_ms / args.e2e_steps}
+
+
 def main():
     args = parse()
     rank, world, local = env_rank()
@@ -181,7 +213,8 @@ def main():
          for s in range(sets)]
     C = torch.empty(m * n, dtype=torch.int32, device="cuda")
     ctx = U.Context(local)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     route = U.Route()
 
@@ -230,27 +263,10 @@ def main():
     ms_per_step = elapsed_ms / args.steps
 
     # ---- end to end through the C ABI with pinned host buffers
-    Ah = torch.from_numpy(U.corpus(1, U.CORPUS_I8, m * k)).pin_memory()
-    Bh = torch.from_numpy(U.corpus(2 + 1000 * rank, U.CORPUS_I8, k * n)).pin_memory()
-    Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
-    U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx)  # warm the staging buffers
-    if dist:
-        dist.barrier()
-    t0 = time.perf_counter()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * args.e2e_steps * ops_per_step / (e2e_ms / 1e3) / 1e12
-    del t0
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e = run_e2e(args, U, torch, dist, ctx, stream, m, k, n, rank, world)
+    del A, B, C
 
     peaks = {}
     try:
@@ -282,8 +298,7 @@ def main():
                      "frac": achieved / peak, "peak_source": peak_src,
                      "traffic": traffic.get("bytes_per_launch") if traffic else None,
                      "algorithmic_bytes": m * k + k * n + 4 * m * n},
-        "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": m * k + k * n,
-                "d2h_bytes_per_step": 4 * m * n, "ms_per_step": e2e_ms / args.e2e_steps},
+        "e2e": e2e,
         "gpu_launches": args.steps,
         "clocks": clk,
     }

@@ -83,7 +83,8 @@ typedef struct uor_b200_ctx uor_b200_ctx;
 
 uor_b200_ctx *uor_b200_ctx_create(int device);
 void uor_b200_ctx_destroy(uor_b200_ctx *ctx);
-/* Run this context's work on `stream` (a cudaStream_t); NULL restores its own. */
+/* Run this context's work on `stream` (a cudaStream_t); NULL is CUDA's legacy
+ * default stream. A new context runs on a private non-blocking stream. */
 int uor_b200_ctx_set_stream(uor_b200_ctx *ctx, void *stream);
 /* Upper bound on any single device-side wait, in nanoseconds (default 2 s). */
 int uor_b200_ctx_set_wait_budget_ns(uor_b200_ctx *ctx, uint64_t ns);

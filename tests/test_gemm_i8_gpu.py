@@ -107,7 +107,7 @@ def test_outputs_and_modes(out, mode):
 
 
 def test_layouts_transposed_gathered_and_negative():
-    m, k, n = 150, 200, 170
+    m, k, n = 160, 200, 170  # m * 1 byte is a multiple of 16: A^T is TMA-readable
     a, b = i8(7, m * k), i8(8, k * n)
     base = want_plain(a, b, m, k, n)
     at = np.ascontiguousarray(a.reshape(m, k).T).reshape(-1)   # A^T stored k x m

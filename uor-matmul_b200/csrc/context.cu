@@ -231,7 +231,7 @@ void uor_b200_ctx_destroy(uor_b200_ctx* ctx) {
 
 int uor_b200_ctx_set_stream(uor_b200_ctx* ctx, void* stream) {
     if (!ctx) return UOR_B200_INVALID_ARGUMENT;
-    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    ctx->stream = static_cast<cudaStream_t>(stream);  // NULL is the legacy default stream
     return UOR_B200_OK;
 }
 
