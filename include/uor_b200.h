@@ -49,7 +49,8 @@ typedef enum uor_b200_status {
     UOR_B200_NCCL_ERROR = 5,       /* reserved for collective-backed calls */
     UOR_B200_DOES_NOT_FIT = 6,     /* a buffer does not hold the view its caller described */
     UOR_B200_INVALID_ARGUMENT = 7, /* unknown enum value, or a null pointer with extent */
-    UOR_B200_UNSUPPORTED = 8       /* an element/output pair outside the reference's surface */
+    UOR_B200_UNSUPPORTED = 8,      /* an element/output pair outside the reference's surface */
+    UOR_B200_SCRATCH_LIMIT = 9     /* the no-allocation entry needs more than its fixed scratch */
 } uor_b200_status;
 
 /* EncodeMode, crates/uor-matmul-core/src/policy.rs:20-48. */
@@ -249,6 +250,34 @@ int uor_b200_tabulated_gemm(uor_b200_dtype out, const uor_b200_view *a, const ui
                             size_t codes_len, size_t k, size_t n, uint32_t per_byte,
                             const int8_t *table, size_t table_len, const uor_b200_view_mut *c,
                             int64_t alpha, int64_t beta, const uor_b200_call *call);
+
+/* ------------------------------------------------- no-allocation variant */
+
+/* Size of the fixed device scratch the no-allocation entry point uses. */
+#define UOR_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* Exact i8 x i8 GEMM (gemm_ex semantics, row-major, device pointers) that never
+ * allocates memory. This entry point has no counterpart in the reference; it exists
+ * for callers that cannot let a library call cudaMalloc: callers that budget every
+ * byte of device memory once at start-up (an inference server's fixed pool, another
+ * allocator owning the device), callers built on the reference's own zero-allocation
+ * contract, and code that must not make allocating CUDA calls at all.
+ *
+ * Reductions deeper than one s32 lane (k > 131071) are cut into exact chunks whose
+ * partial sums live in one static device array of UOR_B200_NOALLOC_SCRATCH_BYTES,
+ * which every GPU that loads this library holds until the process exits. A product
+ * needing more (chunks * m * n * 4 bytes + 256) is refused with UOR_B200_SCRATCH_LIMIT.
+ * The first call on a device looks up the array's device address (set-up done once
+ * per device); make that first call before any stream capture. Every call shares the
+ * array, so calls that overlap on the GPU (other streams, other threads) race on it:
+ * serialise them. Operands must be TMA-readable as given (16-byte-aligned pointers,
+ * lda and ldb multiples of 16) or the call returns UOR_B200_UNSUPPORTED. Runs on
+ * `stream` (NULL = legacy default stream) and returns after the result is in C.
+ * out in {I8, I16, I32, I64, I128}; encode as uor_b200_encode. */
+int uor_b200_gemm_ex_i8_noalloc(uor_b200_dtype out, size_t m, size_t k, size_t n,
+                                int64_t alpha, const int8_t *a, size_t lda, const int8_t *b,
+                                size_t ldb, int64_t beta, void *c, size_t ldc, uint32_t encode,
+                                void *stream);
 
 /* ----------------------------------------------------------------- misc */
 

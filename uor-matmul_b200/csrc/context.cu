@@ -266,6 +266,7 @@ const char* uor_b200_status_string(int s) {
     case UOR_B200_DOES_NOT_FIT: return "a buffer does not hold the view described";
     case UOR_B200_INVALID_ARGUMENT: return "invalid argument";
     case UOR_B200_UNSUPPORTED: return "element/output pair not supported";
+    case UOR_B200_SCRATCH_LIMIT: return "the product needs more than the fixed no-allocation scratch";
     default: return "unknown status";
     }
 }
