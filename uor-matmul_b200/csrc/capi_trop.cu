@@ -1,0 +1,92 @@
+// capi_trop.cu -- the tropical family's C ABI (driver::gemm over Trop<E> with MaxPlus).
+#include <climits>
+#include "internal.h"
+#include "staging.h"
+#include "tropical.cuh"
+
+using namespace uor;
+
+namespace {
+
+int trop_bytes(uor_b200_dtype t) {
+    switch (t) {
+    case UOR_B200_TROP_I8: return 1;
+    case UOR_B200_TROP_I16: return 2;
+    case UOR_B200_TROP_I32: return 4;
+    case UOR_B200_TROP_I64: return 8;
+    default: return 0;
+    }
+}
+
+}  // namespace
+
+extern "C" int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out,
+                                      const uor_b200_view* a, const uor_b200_view* b,
+                                      const uor_b200_view_mut* c, uor_b200_trop alpha,
+                                      uor_b200_trop beta, const uor_b200_call* call) {
+    if (!a || !b || !c) return UOR_B200_INVALID_ARGUMENT;
+    const int eb = trop_bytes(elem), ob = trop_bytes(out);
+    if (!eb || !ob) return UOR_B200_UNSUPPORTED;
+    const int mode = call ? (int)call->encode : MODE_NEAREST;
+    if (mode < 0 || mode > 3) return UOR_B200_INVALID_ARGUMENT;
+    Operand A, B, C;
+    int st;
+    if ((st = place_view(a->data, a->len, a->rows, a->cols, a->rs, a->cs, dtype_size(elem), &A)))
+        return st;
+    if ((st = place_view(b->data, b->len, b->rows, b->cols, b->rs, b->cs, dtype_size(elem), &B)))
+        return st;
+    if ((st = place_view(c->data, c->len, c->rows, c->cols, c->rs, c->cs, dtype_size(out), &C)))
+        return st;
+    if (a->cols != b->rows || c->rows != a->rows || c->cols != b->cols) return UOR_B200_NONCONFORMANT;
+    if (self_aliases(c->rows, c->cols, c->rs, c->cs)) return UOR_B200_OUTPUT_ALIASES;
+    uor_b200_route local{};
+    uor_b200_route* route = call && call->route ? call->route : &local;
+    *route = uor_b200_route{};
+    const size_t m = a->rows, k = a->cols, n = b->cols;
+    if (m == 0 || n == 0) return UOR_B200_OK;
+    if (m > (size_t)INT_MAX / 2 || n > (size_t)INT_MAX / 2 || k > (size_t)INT_MAX / 2)
+        return UOR_B200_UNSUPPORTED;
+
+    uor_b200_ctx* ctx = resolve_ctx(call, &st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
+    const uint8_t *da = nullptr, *db = nullptr;
+    OutStage cs;
+    if ((st = stage_in(ctx, SLOT_A, A, dev, &da))) return st;
+    if ((st = stage_in(ctx, SLOT_B, B, dev, &db))) return st;
+    if ((st = stage_out_begin(ctx, C, dev, beta.finite != 0, &cs))) return st;
+
+    TropEpi e{};
+    e.alpha = alpha.value;
+    e.beta = beta.value;
+    e.alpha_finite = alpha.finite != 0;
+    e.beta_finite = beta.finite != 0;
+    e.mode = mode;
+    e.obytes = ob;
+    e.c = cs.dev_origin;
+    e.rsc = C.rs;
+    e.csc = C.cs;
+    e.m = (int)m;
+    e.n = (int)n;
+    route->kernel = UOR_B200_KERNEL_TROPICAL;
+    cudaError_t err;
+    if (eb == 1) {
+        void* ws = ctx_buffer(ctx, SLOT_WS, trop_i8_workspace((int)m, (int)k, (int)n), &st);
+        if (!ws) return st;
+        route->tile_m = 128;
+        route->tile_n = 128;
+        route->tile_k = 32;
+        err = trop_i8_launch(da, A.rs, A.cs, db, B.rs, B.cs, (int)m, (int)k, (int)n, ws, e,
+                             ctx->stream);
+    } else {
+        route->tile_m = 16;
+        route->tile_n = 16;
+        err = trop_generic_launch(da, A.rs, A.cs, db, B.rs, B.cs, eb, (int)m, (int)k, (int)n, e,
+                                  ctx->stream);
+    }
+    if (err != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    if ((st = stage_out_end(ctx, cs))) return st;
+    if (!dev) return uor_b200_ctx_sync(ctx);
+    return finish_call(ctx, call);
+}
