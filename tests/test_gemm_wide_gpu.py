@@ -1,0 +1,107 @@
+"""K2/K3 (byte-sliced i16 / i32 / i64 GEMM with exact recombination) against the
+oracle and the reference's CX-10 NumPy vectors."""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import uor_b200 as U
+from oracle import oracle as orc
+from gpu_util import i128_values, needs_gpu, oracle_int, out_array, torch
+
+pytestmark = [pytest.mark.gpu, needs_gpu]
+
+MANIFEST = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "cx_manifest.json")))
+ELEM = {16: U.I16, 32: U.I32, 64: U.I64}
+NP = {16: np.int16, 32: np.int32, 64: np.int64}
+
+
+def cx10_cases():
+    s = MANIFEST["cx10"]["seed"]
+    for case in MANIFEST["cx10"]["cases"]:
+        m, k, n = (case["shape"][x] for x in "mkn")
+        states, s = orc.xorshift_stream(s, m * k + k * n)
+        vals = (states >> np.uint64(33)).astype(np.int64) % 1000 - 500
+        yield case, vals[: m * k], vals[m * k:]
+
+
+@pytest.mark.parametrize("idx", range(len(MANIFEST["cx10"]["cases"])))
+def test_cx10_i64_wrapping_on_gpu(idx):
+    case, a, b = list(cx10_cases())[idx]
+    m, k, n = (case["shape"][x] for x in "mkn")
+    c = np.zeros(max(m * n, 1), np.int64)
+    if m and n:
+        U.slice_gemm_ex(U.I64, U.I64, m, k, n, 1, a, k, b, n, 0, c, n, encode=U.WRAPPING)
+    got = c[: m * n].astype("<i8")
+    assert "sha256:" + hashlib.sha256(got.tobytes()).hexdigest() == case["expected_sha256"]
+
+
+def rand_full(rng, bits, count):
+    info = np.iinfo(NP[bits])
+    return rng.integers(info.min, info.max, size=count, endpoint=True).astype(NP[bits])
+
+
+@pytest.mark.parametrize("bits", [16, 32, 64])
+@pytest.mark.parametrize("out", [U.I32, U.I64, U.I128])
+def test_random_full_range(bits, out):
+    rng = np.random.default_rng(bits * 10 + out)
+    for (m, k, n) in [(1, 1, 1), (13, 17, 19), (130, 300, 270)]:
+        a, b = rand_full(rng, bits, m * k), rand_full(rng, bits, k * n)
+        c0 = out_array(out, m * n)
+        c0[:] = rng.integers(-1000, 1000, size=c0.size)
+        for alpha, beta, mode in [(1, 0, U.NEAREST), (3, -1, U.WRAPPING), (-(2**63), 5, U.NEAREST),
+                                  (2**62, 2**62, U.SATURATING)]:
+            got, want = c0.copy(), c0.copy()
+            route = U.Route()
+            U.gemm(ELEM[bits], out, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), alpha,
+                   beta, mode, route=route)
+            oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), alpha, beta,
+                       mode, out)
+            if out == U.I128:
+                assert i128_values(got) == i128_values(want), (m, k, n, alpha, beta, mode)
+            else:
+                assert np.array_equal(got, want), (m, k, n, alpha, beta, mode)
+            assert route.kernel == 2
+
+
+def test_deep_i32_chunks_and_strides():
+    rng = np.random.default_rng(5)
+    m, k, n = 40, 30000, 24
+    a, b = rand_full(rng, 32, m * k), rand_full(rng, 32, k * n)
+    got = np.zeros(m * n * 2, np.int64)
+    want = got.copy()
+    route = U.Route()
+    # B read as its own transpose: stored n x k
+    bt = np.ascontiguousarray(b.reshape(k, n).T).reshape(-1)
+    U.gemm(U.I32, U.I128, a, (m, k, k, 1), bt, (k, n, 1, k), got, (m, n, n, 1), route=route)
+    oracle_int(a, (m, k, k, 1, 0), bt, (k, n, 1, k, 0), want, (m, n, n, 1, 0), 1, 0, U.NEAREST,
+               U.I128)
+    assert i128_values(got) == i128_values(want)
+    assert route.k_chunks >= 3
+
+
+@pytest.mark.slow
+def test_config4_full_size():
+    """1024 x 65536 x 1024, i32 full range -> exact i128: sampled cells against the
+    oracle and a Freivalds checksum modulo 2^64."""
+    m, n, k = 1024, 1024, 65536
+    a = U.corpus(4, U.CORPUS_I32_FULL, m * k)
+    b = U.corpus(5, U.CORPUS_I32_FULL, k * n)
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    tc = torch.zeros(m * n * 2, dtype=torch.int64, device="cuda")
+    route = U.Route()
+    U.gemm(U.I32, U.I128, ta, (m, k, k, 1), tb, (k, n, n, 1), tc, (m, n, n, 1), route=route)
+    c = tc.cpu().numpy()
+    vals = i128_values(c)
+    for (i, j) in [(0, 0), (m - 1, n - 1), (517, 33)]:
+        w = np.zeros(2, np.int64)
+        orc.gemm_int(orc.View(a, 1, k, k, 1, i * k), orc.View(b, k, 1, n, 1, j),
+                     orc.View(w, 1, 1, 1, 1), out_bits=128)
+        assert vals[i * n + j] == i128_values(w)[0], (i, j)
+    x = np.random.default_rng(0).integers(-1, 2, size=n).astype(np.int64)
+    low = c[0::2].reshape(m, n)  # C mod 2^64
+    lhs = low @ x
+    rhs = a.reshape(m, k).astype(np.int64) @ (b.reshape(k, n).astype(np.int64) @ x)
+    assert np.array_equal(lhs, rhs)

@@ -42,7 +42,6 @@ int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Opera
     *route = uor_b200_route{};
     const size_t m = A.rows, k = A.cols, n = B.cols;
     if (m == 0 || n == 0) return UOR_B200_OK;
-    if (elem != UOR_B200_I8) return UOR_B200_UNSUPPORTED;
 
     int st = UOR_B200_OK;
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
@@ -56,9 +55,13 @@ int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Opera
     if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs)) != UOR_B200_OK) return st;
 
     const LinearEpi epi{alpha, beta, mode, kind};
-    st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs,
-                     reinterpret_cast<const int8_t*>(db), B.rs, B.cs, cs.dev_origin, C.rs, C.cs,
-                     m, k, n, epi, route);
+    if (elem == UOR_B200_I8)
+        st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs,
+                         reinterpret_cast<const int8_t*>(db), B.rs, B.cs, cs.dev_origin, C.rs,
+                         C.cs, m, k, n, epi, route);
+    else
+        st = run_wide_gemm(ctx, (int)dtype_size(elem), da, A.rs, A.cs, db, B.rs, B.cs,
+                           cs.dev_origin, C.rs, C.cs, m, k, n, epi, route);
     if (st != UOR_B200_OK) return st;
     if ((st = stage_out_end(ctx, cs)) != UOR_B200_OK) return st;
     if (!dev) return uor_b200_ctx_sync(ctx);

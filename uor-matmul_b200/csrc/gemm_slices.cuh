@@ -1,0 +1,52 @@
+// gemm_slices.cuh -- the slice-pair tensor-core GEMM shared by the wide-integer
+// (K2) and exact-float (K6) paths.
+//
+// Both operands arrive as stacks of int8 "slices" (byte planes of a wider integer,
+// or signed digits of a scaled float significand), K-major, padded so that no tile
+// crosses a slice: A slices are [La][mp][kp] (mp a multiple of 128), B slices are
+// [Lb][np][kp] (B transposed, np a multiple of 256). The product is organised in
+// groups of slice pairs (s, t) that share a weight -- a diagonal s + t = d -- and
+// every work unit (group, reduction chunk, 128x256 tile) accumulates all pairs of
+// its group over its chunk in one s32 TMEM accumulator, then writes the s32 partial
+// sums to partial[chunk][group][m][n]. The host sizes the chunk so that no partial
+// can overflow; a family-specific kernel then combines the partials exactly.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace uor {
+
+constexpr int KS_BM = 128;
+constexpr int KS_BN = 256;
+constexpr int KS_BK = 128;
+constexpr int KS_STAGES = 4;
+constexpr int KS_THREADS = 192;
+constexpr int KS_A_BYTES = KS_BM * KS_BK;
+constexpr int KS_B_BYTES = KS_BN * KS_BK;
+constexpr int KS_STAGE_BYTES = KS_A_BYTES + KS_B_BYTES;
+constexpr int KS_SMEM_BYTES = KS_STAGES * KS_STAGE_BYTES + 1024 + 256;
+constexpr int KS_MAX_GROUPS = 40;
+constexpr int KS_MAX_PAIRS = 256;
+
+struct KSParams {
+    int m, n;                 // output extent
+    int mp, np;               // padded rows per slice in the A and B stacks
+    int tiles_m, tiles_n, num_tiles, group_m;
+    int num_chunks, kb_per_chunk, num_kb;  // reduction blocks per chunk, in total
+    int num_groups;
+    int32_t* partial;         // [num_chunks][num_groups][m][n]
+    int* status;
+    uint64_t budget_ns;
+    int pair_begin[KS_MAX_GROUPS + 1];
+    uint8_t pair_a[KS_MAX_PAIRS];
+    uint8_t pair_b[KS_MAX_PAIRS];
+    uint32_t pair_idesc[KS_MAX_PAIRS];
+};
+
+// tmA: dims {k, La * mp}, box {128, 128}; tmB: dims {k, Lb * np}, box {128, 256};
+// both uint8 with 128-byte swizzle.
+cudaError_t ks_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const KSParams& p,
+                      int grid, cudaStream_t stream);
+
+}  // namespace uor

@@ -14,4 +14,11 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
                 ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
                 uor_b200_route* route);
 
+// i16 / i32 / i64 GEMM (eb = element bytes) by byte slicing through the slice-pair
+// kernel and an exact recombination in the element's accumulator.
+int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
+                  const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc,
+                  ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
+                  uor_b200_route* route);
+
 }  // namespace uor

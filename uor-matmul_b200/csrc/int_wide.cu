@@ -1,0 +1,313 @@
+// int_wide.cu -- K2/K3: exact i16 / i32 / i64 GEMM by byte slicing.
+//
+// Replaces the exact lanes of Kernelized for i16 / i32 / i64
+// (crates/uor-matmul-gemm/src/kernel.rs:224-399; the I16_I64, I32_I64, I64_I128 tile
+// families of isa/portable.rs:91-130), which fold every product (lane_depth = 1 for
+// i32) into i128, or into Limbs<3> for i64 (alphabet.rs:618-637).
+//
+// An L-byte integer is the exact sum of its two's-complement bytes:
+//   x = sum_{s < L-1} u_s 256^s + s_{L-1} 256^(L-1)   (u_s unsigned, s_{L-1} signed),
+// so A B = sum_{s,t} 256^(s+t) A_s B_t with A_s, B_t int8 matrices. The slice-pair
+// kernel (gemm_slices.cu) accumulates every pair on a diagonal d = s + t exactly in
+// s32 over a reduction chunk short enough that no partial can overflow, and
+// `wide_reduce` adds the partials back as sum_q sum_d partial * 2^(8 d) in 192-bit
+// two's complement, then runs the Linear epilogue in the element's own accumulator
+// (i128 for i16/i32, Limbs<3> for i64) and encodes once.
+#include <climits>
+#include "int_gemm.h"
+#include "aux.cuh"
+#include "gemm_slices.cuh"
+#include "ptx.cuh"
+
+namespace uor {
+
+// ------------------------------------------------------------ slicing kernels
+
+// A (m x k, eb-byte elements, strided view) -> As[L][mp][kp], byte s of each element.
+__global__ void slice_a_kernel(uint8_t* __restrict__ as, int L, int mp, int kp,
+                               const uint8_t* __restrict__ a, int64_t rsa, int64_t csa, int eb,
+                               int m, int k) {
+    const int64_t total = static_cast<int64_t>(mp) * kp;
+    const int64_t plane = total;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(idx / kp), p = static_cast<int>(idx % kp);
+        uint64_t v = 0;
+        if (i < m && p < k) {
+            const uint8_t* e = a + (static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa) * eb;
+            for (int s = 0; s < eb; ++s) v |= static_cast<uint64_t>(e[s]) << (8 * s);
+        }
+        for (int s = 0; s < L; ++s) as[s * plane + idx] = static_cast<uint8_t>(v >> (8 * s));
+    }
+}
+
+// B (k x n, strided view) -> Bs[L][np][kp] (transposed), through a 32 x 32 shared tile.
+__global__ void slice_b_kernel(uint8_t* __restrict__ bs, int L, int np, int kp,
+                               const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, int eb,
+                               int k, int n) {
+    __shared__ uint64_t tile[32][33];
+    const int p0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    for (int r = ty; r < 32; r += 8) {
+        const int p = p0 + r, j = j0 + tx;
+        uint64_t v = 0;
+        if (p < k && j < n) {
+            const uint8_t* e = b + (static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb) * eb;
+            for (int s = 0; s < eb; ++s) v |= static_cast<uint64_t>(e[s]) << (8 * s);
+        }
+        tile[r][tx] = v;
+    }
+    __syncthreads();
+    const int64_t plane = static_cast<int64_t>(np) * kp;
+    for (int r = ty; r < 32; r += 8) {
+        const int j = j0 + r, p = p0 + tx;
+        if (j < np && p < kp) {
+            const uint64_t v = tile[tx][r];
+            for (int s = 0; s < L; ++s)
+                bs[s * plane + static_cast<int64_t>(j) * kp + p] = static_cast<uint8_t>(v >> (8 * s));
+        }
+    }
+}
+
+// ------------------------------------------------------------ exact recombination
+
+struct L3 {
+    uint64_t w[3];
+};
+
+__device__ __forceinline__ void l3_add(L3& x, const L3& y) {
+    uint64_t c = 0;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const uint64_t s = x.w[i] + y.w[i];
+        const uint64_t c1 = s < x.w[i];
+        const uint64_t s2 = s + c;
+        const uint64_t c2 = s2 < s;
+        x.w[i] = s2;
+        c = c1 | c2;
+    }
+}
+
+__device__ __forceinline__ L3 l3_of(i128 v) {
+    L3 r;
+    r.w[0] = static_cast<uint64_t>(static_cast<u128>(v));
+    r.w[1] = static_cast<uint64_t>(static_cast<u128>(v) >> 64);
+    r.w[2] = v < 0 ? ~0ull : 0ull;
+    return r;
+}
+
+// v * 2^sh, two's complement modulo 2^192, for 0 <= sh < 192.
+__device__ __forceinline__ L3 l3_shifted(int64_t v, int sh) {
+    const uint64_t x0 = static_cast<uint64_t>(v), ext = v < 0 ? ~0ull : 0ull;
+    L3 y;
+    if (sh >= 128) {
+        y.w[0] = 0;
+        y.w[1] = 0;
+        y.w[2] = x0 << (sh - 128);
+    } else if (sh >= 64) {
+        const int s = sh - 64;
+        y.w[0] = 0;
+        y.w[1] = x0 << s;
+        y.w[2] = s ? (ext << s) | (x0 >> (64 - s)) : ext;
+    } else {
+        const int s = sh;
+        y.w[0] = x0 << s;
+        y.w[1] = s ? (ext << s) | (x0 >> (64 - s)) : ext;
+        y.w[2] = s ? (ext << s) | (ext >> (64 - s)) : ext;
+    }
+    return y;
+}
+
+__device__ __forceinline__ L3 l3_neg(L3 x) {
+    L3 r;
+    uint64_t c = 1;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const uint64_t s = ~x.w[i] + c;
+        c = (c && s == 0) ? 1 : 0;
+        r.w[i] = s;
+    }
+    return r;
+}
+
+// ScaleExact for Limbs (epilogue.rs:307-329): double-and-add modulo 2^192.
+__device__ __forceinline__ L3 l3_scale(L3 x, int64_t f) {
+    const bool negf = f < 0;
+    uint64_t mag = negf ? 0ull - static_cast<uint64_t>(f) : static_cast<uint64_t>(f);
+    L3 acc = {{0, 0, 0}};
+    L3 add = negf ? l3_neg(x) : x;
+    while (mag) {
+        if (mag & 1) l3_add(acc, add);
+        L3 d = add;
+        l3_add(add, d);
+        mag >>= 1;
+    }
+    return acc;
+}
+
+// EncodeFrom<Limbs<3>> for a machine integer (acc.rs:405-444).
+__device__ __forceinline__ i128 l3_encode(L3 x, int bits, int mode) {
+    const i128 low = static_cast<i128>((static_cast<u128>(x.w[1]) << 64) | x.w[0]);
+    if (mode == MODE_WRAPPING) return low;
+    const bool neg = (x.w[2] >> 63) != 0;
+    const L3 mag3 = neg ? l3_neg(x) : x;
+    const i128 mx = bits >= 128 ? i128_max() : ((static_cast<i128>(1) << (bits - 1)) - 1);
+    const i128 mn = bits >= 128 ? i128_min() : (-mx - 1);
+    if (mag3.w[2] != 0) return neg ? mn : mx;
+    const u128 mag = (static_cast<u128>(mag3.w[1]) << 64) | mag3.w[0];
+    const u128 limit = neg ? static_cast<u128>(0) - static_cast<u128>(mn) : static_cast<u128>(mx);
+    if (mag > limit) return neg ? mn : mx;
+    return neg ? static_cast<i128>(static_cast<u128>(0) - mag) : static_cast<i128>(mag);
+}
+
+struct WideEpi {
+    LinearEpi lin;
+    int limbs3;  // 1: i64 elements (Limbs<3> accumulator); 0: i16/i32 (i128 accumulator)
+};
+
+// Group g is the diagonal d = g, weighted 2^(8 g).
+__global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks, int groups,
+                                   size_t m, size_t n, void* c, int64_t rsc, int64_t csc,
+                                   WideEpi e) {
+    const size_t total = m * n;
+    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        L3 acc = {{0, 0, 0}};
+        for (int q = 0; q < chunks; ++q)
+            for (int g = 0; g < groups; ++g) {
+                const int32_t v = part[(static_cast<size_t>(q) * groups + g) * total + idx];
+                if (v) {
+                    const L3 t = l3_shifted(v, 8 * g);
+                    l3_add(acc, t);
+                }
+            }
+        const size_t i = idx / n, j = idx - (idx / n) * n;
+        const int64_t off = static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j) * csc;
+        const LinearEpi& L = e.lin;
+        i128 outv;
+        if (e.limbs3) {
+            L3 tot = L.alpha == 1 ? acc : l3_scale(acc, L.alpha);
+            if (L.beta != 0) {
+                const L3 pr = l3_scale(l3_of(load_out(c, L.kind, off)), L.beta);
+                l3_add(tot, pr);
+            }
+            outv = l3_encode(tot, out_bits(L.kind), L.mode);
+        } else {
+            const i128 a = static_cast<i128>((static_cast<u128>(acc.w[1]) << 64) | acc.w[0]);
+            i128 tot = L.alpha == 1 ? a : sat_mul(a, L.alpha);
+            if (L.beta != 0)
+                tot = static_cast<i128>(static_cast<u128>(tot) +
+                                        static_cast<u128>(sat_mul(load_out(c, L.kind, off), L.beta)));
+            outv = encode_int(tot, out_bits(L.kind), L.mode);
+        }
+        store_out(c, L.kind, off, outv);
+    }
+}
+
+// ------------------------------------------------------------ driver
+
+static inline size_t rup(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
+                  const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc,
+                  ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
+                  uor_b200_route* route) {
+    cudaStream_t s = ctx->stream;
+    if (route) {
+        *route = uor_b200_route{};
+        route->tile_m = KS_BM;
+        route->tile_n = KS_BN;
+        route->tile_k = KS_BK;
+    }
+    if (m == 0 || n == 0) return UOR_B200_OK;
+    if (m > (size_t)INT_MAX / 4 || n > (size_t)INT_MAX / 4 || k > (size_t)INT_MAX / 4)
+        return UOR_B200_UNSUPPORTED;
+    if (k == 0) {
+        if (route) route->kernel = UOR_B200_KERNEL_EPILOGUE_ONLY;
+        return cuda_status(epilogue_only(c, rsc, csc, m, n, epi, s));
+    }
+    const int L = eb;
+    // Slice pairs grouped by diagonal; under Wrapping into <= 64-bit outputs the
+    // diagonals at or above the output width vanish modulo 2^bits.
+    const int max_prod_uu = 255 * 255, max_prod_us = 255 * 128, max_prod_ss = 128 * 128;
+    const int obits = out_bits(epi.kind);
+    KSParams p{};
+    int npairs = 0, ngroups = 0;
+    int64_t worst = 1;
+    for (int d = 0; d <= 2 * L - 2; ++d) {
+        if (epi.mode == MODE_WRAPPING && obits <= 64 && 8 * d >= obits) break;
+        p.pair_begin[ngroups] = npairs;
+        int64_t sum = 0;
+        for (int sa = 0; sa < L; ++sa) {
+            const int sb = d - sa;
+            if (sb < 0 || sb >= L) continue;
+            const bool as = sa == L - 1, bs = sb == L - 1;
+            p.pair_a[npairs] = static_cast<uint8_t>(sa);
+            p.pair_b[npairs] = static_cast<uint8_t>(sb);
+            p.pair_idesc[npairs] = idesc_i8(KS_BM, KS_BN, as, bs, false, false);
+            sum += as && bs ? max_prod_ss : (as || bs ? max_prod_us : max_prod_uu);
+            ++npairs;
+        }
+        ++ngroups;
+        if (sum > worst) worst = sum;
+    }
+    p.pair_begin[ngroups] = npairs;
+    p.num_groups = ngroups;
+    // The longest reduction a diagonal's s32 lane holds exactly, in whole blocks.
+    const int64_t lane = (static_cast<int64_t>(INT_MAX) / worst) / KS_BK;
+    const int num_kb = static_cast<int>((k + KS_BK - 1) / KS_BK);
+    p.kb_per_chunk = static_cast<int>(lane < num_kb ? lane : num_kb);
+    p.num_chunks = (num_kb + p.kb_per_chunk - 1) / p.kb_per_chunk;
+    p.num_kb = num_kb;
+    p.m = static_cast<int>(m);
+    p.n = static_cast<int>(n);
+    p.mp = static_cast<int>(rup(m, KS_BM));
+    p.np = static_cast<int>(rup(n, KS_BN));
+    p.tiles_m = p.mp / KS_BM;
+    p.tiles_n = p.np / KS_BN;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
+    p.status = ctx->d_status;
+    p.budget_ns = ctx->budget_ns;
+
+    const size_t kp = rup(k, 16);
+    const size_t a_bytes = rup((size_t)L * p.mp * kp, 256);
+    const size_t b_bytes = rup((size_t)L * p.np * kp, 256);
+    const size_t part_bytes = (size_t)p.num_chunks * ngroups * m * n * sizeof(int32_t);
+    int st = UOR_B200_OK;
+    uint8_t* ws = static_cast<uint8_t*>(
+        ctx_buffer(ctx, SLOT_WS, a_bytes + b_bytes + rup(part_bytes, 256), &st));
+    if (!ws) return st;
+    uint8_t* as = ws;
+    uint8_t* bs = ws + a_bytes;
+    int32_t* part = reinterpret_cast<int32_t*>(ws + a_bytes + b_bytes);
+    p.partial = part;
+
+    {
+        const int64_t total = static_cast<int64_t>(p.mp) * kp;
+        const int grid = static_cast<int>(total / 256 + 1 < 148 * 32 ? total / 256 + 1 : 148 * 32);
+        slice_a_kernel<<<grid, 256, 0, s>>>(as, L, p.mp, (int)kp, a, rsa, csa, eb, (int)m, (int)k);
+        dim3 g2((p.np + 31) / 32, (unsigned)((kp + 31) / 32));
+        slice_b_kernel<<<g2, dim3(32, 8), 0, s>>>(bs, L, p.np, (int)kp, b, rsb, csb, eb, (int)k,
+                                                  (int)n);
+    }
+    CUtensorMap tmA, tmB;
+    if (!make_tmap_u8(&tmA, as, k, (uint64_t)L * p.mp, kp, 128, 128) ||
+        !make_tmap_u8(&tmB, bs, k, (uint64_t)L * p.np, kp, 128, 256))
+        return UOR_B200_DEVICE_ERROR;
+    const int units = ngroups * p.num_chunks * p.num_tiles;
+    const int grid = units < ctx->sm_count ? units : ctx->sm_count;
+    if (route) {
+        route->kernel = UOR_B200_KERNEL_LIMB_TCGEN05;
+        route->k_chunks = (uint32_t)p.num_chunks;
+        route->ctas = (uint32_t)grid;
+    }
+    if (ks_launch(tmA, tmB, p, grid, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    WideEpi we{epi, eb == 8 ? 1 : 0};
+    const size_t total = m * n;
+    const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+    wide_reduce_kernel<<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, m, n, c, rsc, csc, we);
+    return cuda_status(cudaGetLastError());
+}
+
+}  // namespace uor
