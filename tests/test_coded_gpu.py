@@ -1,0 +1,129 @@
+"""K5 (codebook decode fused into the tensor-core pipeline) against the oracle's
+coded_gemm / gemm_tabulated restatement."""
+import numpy as np
+import pytest
+
+import uor_b200 as U
+from oracle import oracle as orc
+from gpu_util import i128_values, needs_gpu, out_array, torch
+
+pytestmark = [pytest.mark.gpu, needs_gpu]
+
+
+def make_codes(rng, rows, cols, P):
+    bits = 8 // P
+    subs = rng.integers(0, 1 << bits, size=(rows, cols))
+    codes = np.zeros((rows, cols // P), np.uint8)
+    for e in range(P):
+        codes |= (subs[:, e::P] << (bits * e)).astype(np.uint8)
+    return codes.reshape(-1)
+
+
+def run(m, k, n, P, N, orientation, out=U.I32, alpha=1, beta=0, mode=U.NEAREST, seed=0,
+        av=None):
+    rng = np.random.default_rng(seed)
+    a = rng.integers(-128, 128, size=m * k).astype(np.int8)
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    codes = make_codes(rng, rows, cols, P)
+    table = rng.integers(-128, 128, size=N).astype(np.int8)
+    c0 = out_array(out, m * n)
+    c0[:] = rng.integers(-1000, 1000, size=c0.size)
+    got, want = c0.copy(), c0.copy()
+    route = U.Route()
+    av = av or (m, k, k, 1)
+    U.coded_gemm(out, a, av, codes, k, n, P, table, got, (m, n, n, 1), alpha, beta, mode,
+                 route=route, tabulated=orientation == 1)
+    obits = {U.I32: 32, U.I64: 64, U.I128: 128, U.I16: 16, U.I8: 8}[out]
+    origin = -orc.extent(*av)[0]
+    if out != U.I128:
+        orc.coded_gemm(orc.View(a, *av, origin), codes, P, table, orc.View(want, m, n, n, 1), k,
+                       n, orientation, alpha, beta, mode)
+    else:  # 16-byte cells held as int64 pairs
+        orc.lib().uor_oracle_coded_gemm(128, m, k, n, alpha, a.ctypes.data + origin, av[2], av[3],
+                                        codes.ctypes.data, P, table.ctypes.data, N, orientation,
+                                        beta, want.ctypes.data, n, 1, mode, 0)
+    if out == U.I128:
+        return i128_values(got), i128_values(want), route
+    return got, want, route
+
+
+def test_nibble_order_gpu():
+    # codec/tests/codec.rs:91: low nibble first
+    table = (np.arange(16) * 3 - 20).astype(np.int8)
+    codes = np.zeros(16, np.uint8)
+    codes[0], codes[1] = 0x21, 0x43  # row 0 of a 1 x 32 coded matrix: elements 1, 2, 3, 4, 0...
+    a = np.array([1], np.int8)
+    c = np.zeros(32, np.int32)
+    U.coded_gemm(U.I32, a, (1, 1, 1, 1), codes, 1, 32, 2, table, c, (1, 32, 32, 1))
+    assert c[:5].tolist() == [int(table[1]), int(table[2]), int(table[3]), int(table[4]),
+                              int(table[0])]
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("shape", [(1, 32, 32), (3, 64, 96), (129, 160, 288), (300, 512, 256),
+                                   (200, 8192, 64)])
+def test_fused_nibbles(orientation, shape):
+    m, k, n = shape
+    got, want, route = run(m, k, n, 2, 16, orientation, seed=m + n)
+    assert np.array_equal(got, want)
+    assert route.kernel == 4 and route.b_layout != 3
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+def test_short_table_alpha_beta_outputs(orientation):
+    for out in (U.I8, U.I32, U.I64, U.I128):
+        for alpha, beta, mode in [(3, -1, U.NEAREST), (-(2**63), 2**62, U.WRAPPING)]:
+            got, want, _ = run(70, 96, 64, 2, 7, orientation, out, alpha, beta, mode, seed=out)
+            assert (got == want) if out == U.I128 else np.array_equal(got, want), (out, alpha)
+
+
+@pytest.mark.parametrize("P,N", [(1, 200), (4, 4), (8, 2), (2, 16)])
+def test_other_packings_and_ragged(P, N):
+    # n = 24 is not a multiple of 32 (rows the TMA cannot address): the decoded route
+    m, k, n = 33, 40, 24
+    for orientation in (0, 1):
+        got, want, route = run(m, k, n, P, N, orientation, seed=P * 10 + N)
+        assert np.array_equal(got, want), (P, N, orientation)
+
+
+def test_strided_activations_gathered():
+    m, k, n = 64, 96, 64
+    got, want, route = run(m, k, n, 2, 16, 0, av=(m, k, 1, m), seed=9)
+    assert np.array_equal(got, want)
+    assert route.a_layout == 2
+
+
+def test_codes_must_describe_the_shape():
+    a = np.zeros(4, np.int8)
+    codes = np.zeros(3, np.uint8)
+    c = np.zeros(4, np.int32)
+    with pytest.raises(U.DoesNotFit):
+        U.coded_gemm(U.I32, a, (1, 4, 4, 1), codes, 4, 4, 2, np.zeros(16, np.int8), c,
+                     (1, 4, 4, 1))
+
+
+@pytest.mark.slow
+def test_config2_full_size_checksum():
+    """2048 x 8192 activations, 8192 x 8192 nibble codes, 16-entry table (salts 1, 2, 7)."""
+    m, k, n = 2048, 8192, 8192
+    a = U.corpus(1, U.CORPUS_I8, m * k)
+    codes = U.corpus(2, U.CORPUS_NIBBLES, k * n)
+    table = U.corpus(7, U.CORPUS_I8, 16)
+    ta, tcodes, ttab = (torch.from_numpy(x).cuda() for x in (a, codes, table))
+    tc = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    route = U.Route()
+    U.coded_gemm(U.I32, ta, (m, k, k, 1), tcodes, k, n, 2, ttab, tc, (m, n, n, 1), route=route)
+    assert route.kernel == 4 and route.b_layout == 1
+    # independent decode of the nibbles (low first) for the checksum
+    lo = (tcodes & 0xF).long()
+    hi = (tcodes >> 4).long()
+    sub = torch.stack([lo, hi], dim=1).reshape(k, n)
+    bdec = ttab.long()[sub].double()
+    x = torch.randint(-1, 2, (n,), device="cuda").double()
+    lhs = tc.view(m, n).double() @ x
+    rhs = ta.view(m, k).double() @ (bdec @ x)
+    assert torch.equal(lhs, rhs)
+    # a few cells exactly, from the independent decode
+    for (i, j) in [(0, 0), (m - 1, n - 1), (1000, 4097)]:
+        want = int((ta[i * k:(i + 1) * k].long() * ttab.long()[sub[:, j]]).sum())
+        assert int(tc[i * n + j]) == want

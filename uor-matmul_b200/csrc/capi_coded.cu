@@ -1,0 +1,251 @@
+// capi_coded.cu -- the codec tier's C ABI: coded_gemm (codes k x n) and the product
+// of gemm_tabulated (codes n x k), over Packed<Grid<N>, P> codes.
+#include <climits>
+#include <cstring>
+#include "aux.cuh"
+#include "gemm_coded.cuh"
+#include "gemm_i8.cuh"
+#include "int_gemm.h"
+#include "internal.h"
+#include "staging.h"
+#include "ptx.cuh"
+
+using namespace uor;
+
+namespace {
+
+// Decode a Packed<Grid<N>, P> coded matrix to a dense row-major int8 k x n matrix
+// (used only off the fused path: P != 2, N > 16, or rows the TMA cannot read).
+__global__ void decode_dense_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
+                                    const int8_t* __restrict__ table, int N, int P,
+                                    int orientation, int k, int n) {
+    const int64_t total = static_cast<int64_t>(k) * n;
+    const int bits = 8 / P;
+    const unsigned mask = bits >= 8 ? 0xFFu : ((1u << bits) - 1u);
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+        // CodedMatrix::at (matrix.rs:202-207) on the codec's own rows and columns
+        const int row = orientation == 0 ? p : j, col = orientation == 0 ? j : p;
+        const int cols = orientation == 0 ? n : k;
+        const uint8_t code = codes[static_cast<int64_t>(row) * (cols / P) + col / P];
+        const unsigned sub = (code >> (bits * (col % P))) & mask;
+        out[idx] = table[sub % N];
+    }
+}
+
+int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* codes,
+                 size_t codes_len, size_t k, size_t n, uint32_t per_byte, const int8_t* table,
+                 size_t table_len, const uor_b200_view_mut* c, int64_t alpha, int64_t beta,
+                 const uor_b200_call* call, int orientation) {
+    int kind;
+    switch (out) {
+    case UOR_B200_I8: kind = OUT_I8; break;
+    case UOR_B200_I16: kind = OUT_I16; break;
+    case UOR_B200_I32: kind = OUT_I32; break;
+    case UOR_B200_I64: kind = OUT_I64; break;
+    case UOR_B200_I128: kind = OUT_I128; break;
+    default: return UOR_B200_UNSUPPORTED;
+    }
+    if (!a || !c) return UOR_B200_INVALID_ARGUMENT;
+    const int mode = call ? (int)call->encode : MODE_NEAREST;
+    if (mode < 0 || mode > 3) return UOR_B200_INVALID_ARGUMENT;
+    // Packed::new (codecs.rs:166-172): P divides 8; a Grid with no entries decodes nothing.
+    if (per_byte == 0 || 8 % per_byte != 0 || table_len == 0 || table_len > 256 || !table)
+        return UOR_B200_INVALID_ARGUMENT;
+    // CodedMatrix::new (matrix.rs:36-60): the codes describe exactly the declared shape.
+    const size_t rows = orientation == 0 ? k : n, cols = orientation == 0 ? n : k;
+    if (cols % per_byte != 0 || rows * (cols / per_byte) != codes_len) return UOR_B200_DOES_NOT_FIT;
+    Operand A, C;
+    int st;
+    if ((st = place_view(a->data, a->len, a->rows, a->cols, a->rs, a->cs, 1, &A))) return st;
+    if ((st = place_view(c->data, c->len, c->rows, c->cols, c->rs, c->cs, dtype_size(out), &C)))
+        return st;
+    // CodedTriple::new / TabulatedTriple::new: conformance, then aliasing.
+    if (a->cols != k || c->rows != a->rows || c->cols != n) return UOR_B200_NONCONFORMANT;
+    if (self_aliases(c->rows, c->cols, c->rs, c->cs)) return UOR_B200_OUTPUT_ALIASES;
+    uor_b200_route local{};
+    uor_b200_route* route = call && call->route ? call->route : &local;
+    *route = uor_b200_route{};
+    const size_t m = a->rows;
+    if (m == 0 || n == 0) return UOR_B200_OK;
+    if (m > (size_t)INT_MAX / 2 || n > (size_t)INT_MAX / 2 || k > (size_t)INT_MAX / 2)
+        return UOR_B200_UNSUPPORTED;
+    if (codes_len && !codes) return UOR_B200_INVALID_ARGUMENT;
+
+    uor_b200_ctx* ctx = resolve_ctx(call, &st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
+    cudaStream_t s = ctx->stream;
+
+    // The 16-entry effective table the fused decode uses: table[v % N].
+    int8_t tab[256];
+    const size_t tl = table_len < 256 ? table_len : 256;
+    if (dev) {
+        if (cudaMemcpy(tab, table, tl, cudaMemcpyDeviceToHost) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+    } else {
+        std::memcpy(tab, table, tl);
+    }
+
+    const uint8_t* da = nullptr;
+    OutStage cs;
+    if ((st = stage_in(ctx, SLOT_A, A, dev, &da))) return st;
+    const uint8_t* dcodes = codes;
+    if (!dev && codes_len) {
+        uint8_t* d = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_B, codes_len, &st));
+        if (!d) return st;
+        if (cudaMemcpyAsync(d, codes, codes_len, cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+        dcodes = d;
+    }
+    if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs))) return st;
+    const LinearEpi epi{alpha, beta, mode, kind};
+
+    const bool fused = per_byte == 2 && table_len <= 16 && k > 0 &&
+                       (orientation == 0 ? (n % 32 == 0) : (k % 32 == 0)) &&
+                       (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
+    if (!fused) {
+        // Off the fused path (P != 2, N > 16, or code rows the TMA cannot address):
+        // decode to a dense row-major k x n int8 matrix in the auxiliary slot, then K1.
+        uint8_t* buf = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, 256 + k * n, &st));
+        if (!buf) return st;
+        int8_t* dtable = reinterpret_cast<int8_t*>(buf);
+        int8_t* dense = reinterpret_cast<int8_t*>(buf + 256);
+        if (cudaMemcpyAsync(dtable, tab, tl, cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+        if (cudaStreamSynchronize(s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        if (k) {
+            const int64_t total = (int64_t)k * n;
+            const int grid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+            decode_dense_kernel<<<grid, 256, 0, s>>>(dense, dcodes, dtable, (int)table_len,
+                                                     (int)per_byte, orientation, (int)k, (int)n);
+        }
+        st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs, dense,
+                         (ptrdiff_t)n, 1, cs.dev_origin, C.rs, C.cs, m, k, n, epi, route);
+        if (st) return st;
+        route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
+        route->b_layout = 3;  // decoded to a dense workspace first
+    } else {
+        K5Params p{};
+        p.m = (int)m;
+        p.n = (int)n;
+        p.k = (int)k;
+        p.orientation = orientation;
+        for (int w = 0; w < 4; ++w) {
+            uint32_t word = 0;
+            for (int bpos = 0; bpos < 4; ++bpos)
+                word |= (uint32_t)(uint8_t)tab[(4 * w + bpos) % table_len] << (8 * bpos);
+            p.table[w] = word;
+        }
+        // Activations as the N operand: K-major rows of A, gathered if TMA cannot read them.
+        const uint8_t* xa = da;
+        uint64_t xstride = 0;
+        bool gathered = false;
+        const size_t ldk = (k + 15) / 16 * 16;
+        const bool a_ok = (reinterpret_cast<uintptr_t>(da) & 15u) == 0 && (k == 1 || A.cs == 1) &&
+                          (m == 1 || (A.rs > 0 && (size_t)A.rs >= k && (A.rs & 15) == 0));
+        const bool chunked = (int64_t)k > K1_LANE_DEPTH;
+        const int chunks = chunked ? (int)((k + K1_CHUNK_K - 1) / K1_CHUNK_K) : 1;
+        const size_t g_bytes = a_ok ? 0 : (m * ldk + 255) / 256 * 256;
+        const size_t p_bytes = chunked ? (size_t)chunks * m * n * 4 : 0;
+        uint8_t* ws = nullptr;
+        if (g_bytes + p_bytes) {
+            ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, g_bytes + p_bytes, &st));
+            if (!ws) return st;
+        }
+        if (a_ok) {
+            xstride = m == 1 ? ldk : (uint64_t)A.rs;
+        } else {
+            if (gather_2d(ws, ldk, da, m, k, A.rs, A.cs, 1, s) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+            xa = ws;
+            xstride = ldk;
+            gathered = true;
+        }
+        CUtensorMap tmX, tmC;
+        bool ok = make_tmap_u8(&tmX, xa, k, m, xstride, 128, 256);
+        if (orientation == 0)
+            ok = ok && make_tmap_u8(&tmC, dcodes, n / 2, k, n / 2, 64, 128, false);
+        else
+            ok = ok && make_tmap_u8(&tmC, dcodes, k / 2, n, k / 2, 64, 128, false);
+        if (!ok) return UOR_B200_DEVICE_ERROR;
+        p.tiles_j = (int)((n + K5_BM - 1) / K5_BM);
+        p.tiles_i = (int)((m + K5_BN - 1) / K5_BN);
+        p.num_tiles = p.tiles_j * p.tiles_i;
+        p.group_j = p.tiles_j < 16 ? p.tiles_j : 16;
+        p.idesc = idesc_i8(K5_BM, K5_BN, true, true, orientation == 0, false);
+        p.status = ctx->d_status;
+        p.budget_ns = ctx->budget_ns;
+        const int grid = p.num_tiles < ctx->sm_count ? p.num_tiles : ctx->sm_count;
+        route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
+        route->tile_m = K5_BM;
+        route->tile_n = K5_BN;
+        route->tile_k = K5_BK;
+        route->k_chunks = (uint32_t)chunks;
+        route->ctas = (uint32_t)grid;
+        route->a_layout = gathered ? 2 : 0;
+        route->b_layout = orientation == 0 ? 1 : 0;
+        if (!chunked) {
+            p.num_kb = (int)((k + K5_BK - 1) / K5_BK);
+            p.c = cs.dev_origin;
+            p.rsc = C.rs;
+            p.csc = C.cs;
+            p.epi = epi;
+            p.fast = kind == OUT_I32 && alpha == 1 && beta == 0;
+            if (k5_launch(tmX, tmC, p, grid, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        } else {
+            // Deep reductions: exact s32 chunk planes, folded by reduce_chunks. The codes
+            // and activations are re-based per chunk through the TMA coordinates' origin.
+            int32_t* part = reinterpret_cast<int32_t*>(ws + g_bytes);
+            for (int q = 0; q < chunks; ++q) {
+                const size_t k0 = (size_t)q * K1_CHUNK_K;
+                const size_t kl = (k - k0) < (size_t)K1_CHUNK_K ? (k - k0) : (size_t)K1_CHUNK_K;
+                CUtensorMap tX, tC;
+                bool ok2 = make_tmap_u8(&tX, xa + k0, kl, m, xstride, 128, 256);
+                if (orientation == 0)
+                    ok2 = ok2 && make_tmap_u8(&tC, dcodes + k0 * (n / 2), n / 2, kl, n / 2, 64, 128,
+                                              false);
+                else
+                    ok2 = ok2 && make_tmap_u8(&tC, dcodes + k0 / 2, kl / 2 + (kl & 1), n, k / 2, 64,
+                                              128, false);
+                if (!ok2) return UOR_B200_DEVICE_ERROR;
+                p.num_kb = (int)((kl + K5_BK - 1) / K5_BK);
+                p.c = part + (size_t)q * m * n;
+                p.rsc = (int64_t)n;
+                p.csc = 1;
+                p.epi = LinearEpi{1, 0, MODE_NEAREST, OUT_I32};
+                p.fast = 1;
+                if (k5_launch(tX, tC, p, grid, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+            }
+            if (reduce_chunks(part, chunks, m, n, cs.dev_origin, C.rs, C.cs, epi, s) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+        }
+    }
+    if ((st = stage_out_end(ctx, cs))) return st;
+    if (!dev) return uor_b200_ctx_sync(ctx);
+    return finish_call(ctx, call);
+}
+
+}  // namespace
+
+extern "C" {
+
+int uor_b200_coded_gemm(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* codes,
+                        size_t codes_len, size_t k, size_t n, uint32_t per_byte,
+                        const int8_t* table, size_t table_len, const uor_b200_view_mut* c,
+                        int64_t alpha, int64_t beta, const uor_b200_call* call) {
+    return coded_common(out, a, codes, codes_len, k, n, per_byte, table, table_len, c, alpha, beta,
+                        call, 0);
+}
+
+int uor_b200_tabulated_gemm(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* codes,
+                            size_t codes_len, size_t k, size_t n, uint32_t per_byte,
+                            const int8_t* table, size_t table_len, const uor_b200_view_mut* c,
+                            int64_t alpha, int64_t beta, const uor_b200_call* call) {
+    return coded_common(out, a, codes, codes_len, k, n, per_byte, table, table_len, c, alpha, beta,
+                        call, 1);
+}
+
+}  // extern "C"

@@ -30,16 +30,4 @@ int uor_b200_dgemm(size_t, size_t, size_t, int64_t, const double*, ptrdiff_t, pt
     return UOR_B200_UNSUPPORTED;
 }
 
-int uor_b200_coded_gemm(uor_b200_dtype, const uor_b200_view*, const uint8_t*, size_t, size_t,
-                        size_t, uint32_t, const int8_t*, size_t, const uor_b200_view_mut*, int64_t,
-                        int64_t, const uor_b200_call*) {
-    return UOR_B200_UNSUPPORTED;
-}
-
-int uor_b200_tabulated_gemm(uor_b200_dtype, const uor_b200_view*, const uint8_t*, size_t, size_t,
-                            size_t, uint32_t, const int8_t*, size_t, const uor_b200_view_mut*,
-                            int64_t, int64_t, const uor_b200_call*) {
-    return UOR_B200_UNSUPPORTED;
-}
-
 }  // extern "C"

@@ -109,7 +109,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool make_tmap_u8(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
-                  uint64_t stride1, uint32_t box0, uint32_t box1) {
+                  uint64_t stride1, uint32_t box0, uint32_t box1, bool swizzle128) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {dim0, dim1};
@@ -117,7 +117,8 @@ bool make_tmap_u8(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t di
     cuuint32_t box[2] = {box0, box1};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -220,7 +221,7 @@ void uor_b200_ctx_destroy(uor_b200_ctx* ctx) {
     cudaGetDevice(&prev);
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 5; ++i)
         if (ctx->buf[i]) cudaFree(ctx->buf[i]);
     if (ctx->d_status) cudaFree(ctx->d_status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);

@@ -1,0 +1,44 @@
+// gemm_coded.cuh -- K5: exact GEMM against a nibble-coded operand, decoded in the
+// MMA pipeline (no dense copy of the coded operand ever reaches HBM).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "int_epilogue.cuh"
+
+namespace uor {
+
+constexpr int K5_BM = 128;  // decoded weight columns j per tile (TMEM lanes)
+constexpr int K5_BN = 256;  // activation rows i per tile (TMEM columns)
+constexpr int K5_BK = 128;  // reduction per stage
+constexpr int K5_STAGES = 4;
+constexpr int K5_DEC_WARPS = 8;
+constexpr int K5_THREADS = 32 * (6 + K5_DEC_WARPS);  // TMA, MMA, 4 epilogue, decoders
+constexpr int K5_W_BYTES = K5_BM * K5_BK;            // decoded weights, 16 KiB
+constexpr int K5_X_BYTES = K5_BN * K5_BK;            // activations, 32 KiB
+constexpr int K5_C_BYTES = K5_BM * K5_BK / 2;        // codes, 8 KiB
+constexpr int K5_STAGE_BYTES = K5_W_BYTES + K5_X_BYTES + K5_C_BYTES;
+constexpr int K5_SMEM_BYTES = K5_STAGES * K5_STAGE_BYTES + 1024 + 256;
+
+struct K5Params {
+    int m, n, k;            // C is m x n; activations m x k; weights k x n (decoded)
+    int tiles_j, tiles_i, num_tiles, group_j;
+    int num_kb;
+    int orientation;        // 0: codes k x n (coded_gemm); 1: codes n x k (tabulated)
+    uint32_t table[4];      // 16 decoded int8 values, table[v % N] for v in 0..15
+    void* c;
+    int64_t rsc, csc;
+    LinearEpi epi;
+    int fast;               // s32 output, alpha 1, beta 0
+    uint32_t idesc;
+    int* status;
+    uint64_t budget_ns;
+};
+
+// tmX: activations K-major, dims {k, m}, box {128, 256}, 128-byte swizzle.
+// tmC: codes, no swizzle, box {64 bytes, 128 rows}:
+//   orientation 0: dims {n/2, k}; orientation 1: dims {k/2, n}.
+cudaError_t k5_launch(const CUtensorMap& tmX, const CUtensorMap& tmC, const K5Params& p, int grid,
+                      cudaStream_t stream);
+
+}  // namespace uor

@@ -15,15 +15,16 @@ struct uor_b200_ctx {
     uint64_t budget_ns = 2000000000ull;
     int sm_count = 148;
     std::mutex mu;
-    // Growable device buffers: workspace (gathers, chunk partials) and the
-    // three staging slots host-pointer calls copy operands through.
-    void* buf[4] = {nullptr, nullptr, nullptr, nullptr};
-    size_t cap[4] = {0, 0, 0, 0};
+    // Growable device buffers: workspace (gathers, chunk partials), the three
+    // staging slots host-pointer calls copy operands through, and an auxiliary
+    // buffer for operands a path rebuilds (decoded codes).
+    void* buf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t cap[5] = {0, 0, 0, 0, 0};
 };
 
 namespace uor {
 
-enum Slot { SLOT_WS = 0, SLOT_A = 1, SLOT_B = 2, SLOT_C = 3 };
+enum Slot { SLOT_WS = 0, SLOT_A = 1, SLOT_B = 2, SLOT_C = 3, SLOT_AUX = 4 };
 
 // A device buffer of at least `bytes` in the given slot (grown with cudaMalloc;
 // the previous contents are not kept).
@@ -43,7 +44,7 @@ int cuda_status(cudaError_t e);
 // cuTensorMapEncodeTiled for a 2-D uint8 tensor with 128-byte swizzle.
 // dim0 is the contiguous dimension; stride1 is the byte stride of dim1.
 bool make_tmap_u8(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
-                  uint64_t stride1, uint32_t box0, uint32_t box1);
+                  uint64_t stride1, uint32_t box0, uint32_t box1, bool swizzle128 = true);
 
 // A view after placement: origin pointer and the reach of the view in elements.
 struct Placed {
