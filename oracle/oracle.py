@@ -249,6 +249,7 @@ class _Complete:
 
     def __init__(self, min_exp):
         self.min_exp, self.v = min_exp, 0
+        self.limbs = 67 if min_exp == -2148 else 10  # low limbs of Complete<L, MIN_EXP>
         self.nan = self.pinf = self.ninf = False
 
     def is_nan(self):
@@ -258,8 +259,10 @@ class _Complete:
         return not (self.nan or self.pinf or self.ninf)
 
     def add(self, sign, mag, exp):
+        """Complete::add_scaled (acc.rs:939-998): a coordinate below bit 0 or past the
+        last low limb is dropped whole; the register is wide enough for the rest."""
         sh = exp - self.min_exp
-        if sh < 0 or mag == 0:
+        if sh < 0 or mag == 0 or sh // 64 >= self.limbs:
             return
         self.v += (-1 if sign else 1) * (mag << sh)
 

@@ -379,9 +379,12 @@ typedef struct {
     int nan, pinf, ninf;
 } cacc;
 
+/* The register is L low limbs plus one signed extension word (acc.rs:469-476;
+ * L = 10 for f32, 67 for f64, generated.rs:116-126), held here as L + 1 limbs of
+ * one two's complement integer. */
 static void cacc_init(cacc *x, int is64) {
     memset(x, 0, sizeof(*x));
-    x->nl = is64 ? 70 : 12;
+    x->nl = is64 ? 68 : 11;
     x->min_exp = is64 ? -2148 : -298;
 }
 
@@ -391,6 +394,10 @@ static void cacc_add_scaled(cacc *x, u128 mag, int exp, int negative) {
     long shift = (long)exp - x->min_exp;
     if (shift < 0) return;
     int at = (int)(shift / 64), bit = (int)(shift % 64);
+    /* A coordinate past the last low limb names no stored bit: dropped whole
+     * (acc.rs:977-982). Parts reaching the extension word land there; parts past
+     * it are dropped (add_at, acc.rs:157-187). */
+    if (at >= x->nl - 1) return;
     /* mag * 2^bit spread over three words (radix_spread_u128, acc.rs:528-547) */
     uint64_t parts[3];
     if (bit == 0) {

@@ -1,0 +1,182 @@
+"""K6 + K7 (exact float GEMM, one rounding) against the oracle, bit for bit."""
+import struct
+
+import numpy as np
+import pytest
+
+import uor_b200 as U
+from oracle import oracle as orc
+from oracle.oracle import View
+from float_data import config3
+from gpu_util import needs_gpu, torch
+
+pytestmark = [pytest.mark.gpu, needs_gpu]
+
+FT = {U.F32: np.float32, U.F64: np.float64}
+UT = {U.F32: np.uint32, U.F64: np.uint64}
+
+
+def run_both(elem, out, a, b, m, k, n, alpha=1, beta=0, c0=None, mode=U.NEAREST, av=None,
+             bv=None):
+    av = av or (m, k, k, 1)
+    bv = bv or (k, n, n, 1)
+    c0 = np.zeros(m * n, FT[out]) if c0 is None else c0
+    got, want = c0.copy(), c0.copy()
+    route = U.Route()
+    U.gemm_float(elem, out, a, av, b, bv, got, (m, n, n, 1), alpha, beta, mode, route=route)
+    oa = -orc.extent(*av)[0]
+    ob = -orc.extent(*bv)[0]
+    orc.gemm_float(View(a, *av, oa), View(b, *bv, ob), View(want, m, n, n, 1), alpha=alpha,
+                   beta=beta, mode=mode)
+    return got.view(UT[out]), want.view(UT[out]), route
+
+
+def f32b(x):
+    return struct.unpack("<I", struct.pack("<f", x))[0]
+
+
+def gpu_f32(a, b, m, k, n, alpha=1, beta=0, c=None, mode=U.NEAREST):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    c = np.zeros(m * n, np.float32) if c is None else np.asarray(c, np.float32).copy()
+    U.gemm_float(U.F32, U.F32, a, (m, k, k, 1), b, (k, n, n, 1), c, (m, n, n, 1), alpha, beta,
+                 mode)
+    return c.view(np.uint32).tolist()
+
+
+def test_float_kats_on_gpu():
+    # epilogue.rs:411-518 and the encode/decode KATs, through the device path
+    for mode in (U.NEAREST, U.TOWARD_ZERO, U.SATURATING, U.WRAPPING):
+        assert gpu_f32([0.5], [1.0], 1, 1, 1, -(2**63), 2**62, [1.0], mode) == [0]
+    big = float(np.finfo(np.float32).max)
+    assert gpu_f32([big], [big], 1, 1, 1, 2**63 - 1) == [f32b(float("inf"))]
+    assert gpu_f32([big], [big], 1, 1, 1, -(2**63)) == [f32b(float("-inf"))]
+    for mode in (U.TOWARD_ZERO, U.SATURATING, U.WRAPPING):
+        assert gpu_f32([big], [big], 1, 1, 1, 2**63 - 1, mode=mode) == [f32b(big)]
+    assert gpu_f32([float("inf")], [1.0], 1, 1, 1, -1) == [f32b(float("-inf"))]
+    assert gpu_f32([float("inf")], [1.0], 1, 1, 1, 0) == [0x7FC00000]
+    assert gpu_f32([float("inf")], [0.0], 1, 1, 1) == [0x7FC00000]
+    assert gpu_f32([float("inf"), float("inf")], [1.0, -1.0], 1, 2, 1) == [0x7FC00000]
+    assert gpu_f32([1.5, 1.5], [2.0, -2.0], 1, 2, 1) == [0]
+    e = 2.0 ** -24
+    assert gpu_f32([1.0, e, e], [1.0, 1.0, 1.0], 1, 3, 1) == [f32b(1.0 + 2.0 ** -23)]
+
+
+def rand_bits(rng, count, f64, specials):
+    if f64:
+        x = rng.integers(0, 2**64, size=count, dtype=np.uint64).view(np.float64).copy()
+    else:
+        x = rng.integers(0, 2**32, size=count, dtype=np.uint64).astype(np.uint32).view(
+            np.float32).copy()
+    if not specials:
+        x[~np.isfinite(x)] = 1.0
+    return x
+
+
+@pytest.mark.parametrize("elem,out", [(U.F32, U.F32), (U.F64, U.F64), (U.F32, U.F64),
+                                      (U.F64, U.F32)])
+def test_random_bit_patterns_and_specials(elem, out):
+    """Uniform random bit patterns: every exponent (the direct route), NaN, +-inf,
+    subnormals, zeros."""
+    rng = np.random.default_rng(elem * 10 + out)
+    for (m, k, n) in [(1, 1, 1), (5, 7, 3), (9, 33, 17)]:
+        for specials in (True, False):
+            a = rand_bits(rng, m * k, elem == U.F64, specials)
+            b = rand_bits(rng, k * n, elem == U.F64, specials)
+            c0 = rand_bits(rng, m * n, out == U.F64, False)
+            for alpha, beta, mode in [(1, 0, U.NEAREST), (3, -2, U.TOWARD_ZERO),
+                                      (-1, 1, U.NEAREST)]:
+                got, want, _ = run_both(elem, out, a, b, m, k, n, alpha, beta, c0, mode)
+                assert np.array_equal(got, want), (m, k, n, specials, alpha, beta, mode)
+
+
+@pytest.mark.parametrize("elem,out", [(U.F32, U.F32), (U.F64, U.F64), (U.F32, U.F64)])
+@pytest.mark.parametrize("shape", [(3, 10, 7), (130, 96, 270), (64, 700, 40)])
+def test_moderate_exponents_tensor_route(elem, out, shape):
+    """Exponent spans small enough for the digit route (K6 on the tensor cores)."""
+    m, k, n = shape
+    rng = np.random.default_rng(m + k + n)
+    a = (rng.standard_normal(m * k) * np.exp2(rng.integers(-8, 8, m * k))).astype(FT[elem])
+    b = (rng.standard_normal(k * n) * np.exp2(rng.integers(-8, 8, k * n))).astype(FT[elem])
+    b[::5] = 0.0
+    c0 = rng.standard_normal(m * n).astype(FT[out])
+    for alpha, beta, mode in [(1, 0, U.NEAREST), (-3, 2, U.NEAREST), (2**40, -1, U.TOWARD_ZERO)]:
+        got, want, route = run_both(elem, out, a, b, m, k, n, alpha, beta, c0, mode)
+        assert np.array_equal(got, want), (alpha, beta, mode)
+        if elem == U.F32:
+            assert route.kernel == 5 and route.tile_m == 128
+
+
+def test_nonfinite_on_the_tensor_route():
+    m, k, n = 70, 200, 90
+    rng = np.random.default_rng(7)
+    a = rng.standard_normal(m * k).astype(np.float32)
+    b = rng.standard_normal(k * n).astype(np.float32)
+    a[5 * k + 3] = np.inf
+    a[9 * k + 10] = -np.inf
+    b[3 * n + 4] = 0.0
+    b[100 * n + 7] = np.nan
+    b[50 * n + 11] = -np.inf
+    got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, 1, 0)
+    assert np.array_equal(got, want)
+    assert route.tile_m == 128
+
+
+def test_config3_cancellation_moderate():
+    m, k, n = 96, 256, 130
+    a, b = config3(m, k, n)
+    got, want, route = run_both(U.F32, U.F32, a.reshape(-1), b.reshape(-1), m, k, n)
+    assert np.array_equal(got, want)
+    for j in range(0, n, 10):
+        assert got[(j % m) * n + j] == 0, "an exactly cancelling row encodes +0"
+
+
+def test_register_drop_quirk_on_gpu():
+    a = np.array([1.0], np.float32)
+    b = np.array([2.0], np.float32)
+    for prior in (2.0 ** 400, 1.5 * 2.0 ** -297, 3.0):
+        c = np.array([prior], np.float64)
+        w = c.copy()
+        U.gemm_float(U.F32, U.F64, a, (1, 1, 1, 1), b, (1, 1, 1, 1), c, (1, 1, 1, 1), 1, 1)
+        orc.gemm_float(View(a, 1, 1, 1, 1), View(b, 1, 1, 1, 1), View(w, 1, 1, 1, 1), beta=1)
+        assert c.view(np.uint64)[0] == w.view(np.uint64)[0]
+
+
+def test_raw_faces_negative_strides():
+    m, k, n = 20, 30, 25
+    rng = np.random.default_rng(3)
+    for dt, fn in ((np.float32, U.sgemm), (np.float64, U.dgemm)):
+        a = rng.standard_normal(m * k).astype(dt)
+        b = rng.standard_normal(k * n).astype(dt)
+        c = rng.standard_normal(m * n).astype(dt)
+        want = c.copy()
+        # B walked backwards: origin at the last row, rsb = -n
+        fn(m, k, n, 3, a, k, 1, b, -n, 1, -1, c, n, 1, origin=(0, (k - 1) * n, 0))
+        orc.gemm_float(View(a, m, k, k, 1), View(b, k, n, -n, 1, (k - 1) * n),
+                       View(want, m, n, n, 1), alpha=3, beta=-1)
+        assert np.array_equal(c.view(np.uint8), want.view(np.uint8))
+    # an aliasing output returns without writing (raw.rs:146-148)
+    c = np.arange(4, dtype=np.float32)
+    U.sgemm(2, 1, 2, 1, np.ones(2, np.float32), 1, 1, np.ones(2, np.float32), 2, 1, 0, c, 0, 1)
+    assert c.tolist() == [0.0, 1.0, 2.0, 3.0]
+
+
+@pytest.mark.slow
+def test_config3_full_size_sampled():
+    m = k = n = 4096
+    a, b = config3(m, k, n)
+    ta = torch.from_numpy(a).reshape(-1).cuda()
+    tb = torch.from_numpy(b).reshape(-1).cuda()
+    tc = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    route = U.Route()
+    U.gemm_float(U.F32, U.F32, ta, (m, k, k, 1), tb, (k, n, n, 1), tc, (m, n, n, 1), route=route)
+    assert route.kernel == 5 and route.tile_m == 128
+    c = tc.cpu().numpy().view(np.uint32)
+    cells = [(0, 0), (0, 1), (m - 1, n - 1), (123, 4000), (3000, 30), (40, 40)]
+    for (i, j) in cells:
+        w = np.zeros(1, np.float32)
+        orc.gemm_float(View(a.reshape(-1), 1, k, k, 1, i * k), View(b.reshape(-1), k, 1, n, 1, j),
+                       View(w, 1, 1, 1, 1))
+        assert c[i * n + j] == w.view(np.uint32)[0], (i, j)
+    for j in range(0, n, 10):
+        assert c[(j % m) * n + j] == 0

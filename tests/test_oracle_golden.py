@@ -331,3 +331,18 @@ def test_float_epilogue_kats():
     # correctly rounded, not BLAS-rounded: 1 + 2^-24 + 2^-24 rounds to 1 + 2^-23
     e = 2.0 ** -24
     assert run_f32([1.0, e, e], [1.0, 1.0, 1.0], 1, 3, 1) == [f32bits(1.0 + 2.0 ** -23)]
+
+
+def test_complete_register_drops_out_of_range_coordinates():
+    """Complete::add_scaled (acc.rs:939-998) drops a coordinate whose lowest bit is
+    below the register or whose first limb is past its last low limb. Reachable only
+    through beta * C with f32 elements and an f64 output: C = 2^400 or 1.5 * 2^-297
+    contributes nothing, while C = 3 contributes."""
+    a = np.array([1.0], np.float32)
+    b = np.array([2.0], np.float32)
+    for prior, want in ((2.0 ** 400, 2.0), (1.5 * 2.0 ** -297, 2.0), (3.0, 5.0)):
+        c = np.array([prior], np.float64)
+        orc.gemm_float(View(a, 1, 1, 1, 1), View(b, 1, 1, 1, 1), View(c, 1, 1, 1, 1), beta=1)
+        twin = orc.float_gemm_py([[1.0]], [[2.0]], 1, 1, [[prior]], False, True)[0][0]
+        assert int(c.view(np.uint64)[0]) == twin
+        assert c[0] == want

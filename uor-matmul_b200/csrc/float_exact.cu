@@ -1,0 +1,836 @@
+// float_exact.cu -- K6 + K7: exact float GEMM, rounded once.
+//
+// Replaces gemm_float / gemm_float_packed / raw::sgemm / raw::dgemm
+// (crates/uor-matmul/src/slice.rs:304-465, raw.rs:45-160, crates/uor-matmul-gemm/src/
+// float.rs:1761-1917): C := encode(alpha * exact(A B) + beta * C), with the product
+// semantics of Element::mac for floats (alphabet.rs:856-886: NaN absorbs, inf * 0 is
+// NaN, +inf and -inf make NaN), the Linear epilogue over the complete accumulator
+// (Complete::scale / combine, acc.rs:1028-1244) and the one correctly rounded encode
+// (acc.rs:1734-1868).
+//
+// Tensor-core route (K6): every row i of A and column j of B is scaled to an exact
+// integer, x = +-mant * 2^(exp - lo), with lo the lowest set-bit exponent of that
+// row (column); the integers are cut into L signed base-256 digits in [-128, 127],
+// so A B = sum_{s,t} 2^(8 (s+t)) A_s B_t * 2^(lo_i + lo_j). The digit-pair products
+// run on the slice-pair kernel (gemm_slices.cu), one s32 accumulator per diagonal
+// s + t and reduction chunk, exactly. K7 (`fx_reduce_kernel`) rebuilds each cell's
+// exact integer in 768-bit two's complement, applies alpha, adds beta * C exactly
+// (out-of-window bits of the smaller term are jammed into a sticky bit, which cannot
+// change the rounding because that term is then far below the result's last bit),
+// and encodes once. Non-finite inputs are resolved by a separate flags kernel that
+// visits only rows and columns holding them.
+//
+// Direct route: when a row or column spans more than 16 digits, each cell is
+// accumulated in the reference's own fixed-point register (L low limbs plus an
+// extension word) on CUDA cores. Exact, and slow; it exists so that no input has
+// to be refused.
+#include <climits>
+#include "aux.cuh"
+#include "float_exact.h"
+#include "gemm_slices.cuh"
+#include "ptx.cuh"
+
+namespace uor {
+
+// ------------------------------------------------------------ decoding
+
+struct FDec {
+    int kind;  // 0 finite, 1 infinite, 2 NaN
+    int sign;
+    uint64_t mant;
+    int exp;
+};
+
+// FloatElement::decode (alphabet.rs:905-946).
+__device__ __forceinline__ FDec fdecode(const uint8_t* base, int64_t idx, bool f64) {
+    FDec d;
+    if (f64) {
+        const uint64_t bits = reinterpret_cast<const uint64_t*>(base)[idx];
+        const uint64_t frac = bits & 0xFFFFFFFFFFFFFull, biased = (bits >> 52) & 0x7FF;
+        d.sign = static_cast<int>(bits >> 63);
+        if (biased == 0x7FF) {
+            d.kind = frac ? 2 : 1, d.mant = 0, d.exp = 0;
+            return d;
+        }
+        d.kind = 0;
+        if (biased == 0) d.mant = frac, d.exp = 1 - 1023 - 52;
+        else d.mant = frac | (1ull << 52), d.exp = static_cast<int>(biased) - 1023 - 52;
+    } else {
+        const uint32_t bits = reinterpret_cast<const uint32_t*>(base)[idx];
+        const uint32_t frac = bits & 0x7FFFFF, biased = (bits >> 23) & 0xFF;
+        d.sign = static_cast<int>(bits >> 31);
+        if (biased == 0xFF) {
+            d.kind = frac ? 2 : 1, d.mant = 0, d.exp = 0;
+            return d;
+        }
+        d.kind = 0;
+        if (biased == 0) d.mant = frac, d.exp = 1 - 127 - 23;
+        else d.mant = frac | 0x800000u, d.exp = static_cast<int>(biased) - 127 - 23;
+    }
+    return d;
+}
+
+// Product flags of one term (alphabet.rs:862-873): bit 0 NaN, bit 1 +inf, bit 2 -inf.
+__device__ __forceinline__ int term_flags(const FDec& a, const FDec& b) {
+    if (a.kind == 2 || b.kind == 2) return 1;
+    if (a.kind == 1 || b.kind == 1) {
+        const FDec& inf = a.kind == 1 ? a : b;
+        const FDec& other = a.kind == 1 ? b : a;
+        if (other.kind == 0 && other.mant == 0) return 1;
+        return (inf.sign != other.sign) ? 4 : 2;
+    }
+    return 0;
+}
+
+// ------------------------------------------------------------ big integers
+
+constexpr int BW = 12;  // 768-bit two's complement window
+struct Big {
+    uint64_t w[BW];
+};
+
+__device__ __forceinline__ void big_zero(Big& x) {
+#pragma unroll
+    for (int i = 0; i < BW; ++i) x.w[i] = 0;
+}
+__device__ __forceinline__ bool big_neg(const Big& x) { return (x.w[BW - 1] >> 63) != 0; }
+__device__ __forceinline__ bool big_is_zero(const Big& x) {
+    uint64_t o = 0;
+#pragma unroll
+    for (int i = 0; i < BW; ++i) o |= x.w[i];
+    return o == 0;
+}
+__device__ __forceinline__ void big_negate(Big& x) {
+    uint64_t c = 1;
+#pragma unroll
+    for (int i = 0; i < BW; ++i) {
+        const uint64_t s = ~x.w[i] + c;
+        c = (c && s == 0) ? 1 : 0;
+        x.w[i] = s;
+    }
+}
+__device__ __forceinline__ void big_add(Big& x, const Big& y) {
+    uint64_t c = 0;
+#pragma unroll
+    for (int i = 0; i < BW; ++i) {
+        const uint64_t s = x.w[i] + y.w[i];
+        const uint64_t c1 = s < x.w[i];
+        const uint64_t s2 = s + c;
+        const uint64_t c2 = s2 < s;
+        x.w[i] = s2;
+        c = c1 | c2;
+    }
+}
+// x += v * 2^sh (v signed 64-bit, 0 <= sh < 64 * (BW - 2)).
+__device__ __forceinline__ void big_add_i64_shl(Big& x, int64_t v, int sh) {
+    const int wi = sh >> 6, b = sh & 63;
+    const uint64_t ext = v < 0 ? ~0ull : 0ull;
+    const uint64_t lo = static_cast<uint64_t>(v) << b;
+    const uint64_t hi = b ? (static_cast<uint64_t>(v) >> (64 - b)) | (ext << b) : ext;
+    uint64_t c = 0;
+    for (int i = wi; i < BW; ++i) {
+        const uint64_t add = i == wi ? lo : (i == wi + 1 ? hi : ext);
+        const uint64_t s = x.w[i] + add;
+        const uint64_t c1 = s < x.w[i];
+        const uint64_t s2 = s + c;
+        const uint64_t c2 = s2 < s;
+        x.w[i] = s2;
+        c = c1 | c2;
+    }
+}
+// x := x * f, exact while the product fits the window (it always does here).
+__device__ __forceinline__ void big_mul_i64(Big& x, int64_t f) {
+    const bool nx = big_neg(x);
+    if (nx) big_negate(x);
+    const uint64_t uf = f < 0 ? 0ull - static_cast<uint64_t>(f) : static_cast<uint64_t>(f);
+    uint64_t carry = 0;
+#pragma unroll
+    for (int i = 0; i < BW; ++i) {
+        const u128 p = static_cast<u128>(x.w[i]) * uf + carry;
+        x.w[i] = static_cast<uint64_t>(p);
+        carry = static_cast<uint64_t>(p >> 64);
+    }
+    if (nx != (f < 0)) big_negate(x);
+}
+__device__ __forceinline__ int big_bitlen(const Big& mag) {
+    for (int i = BW - 1; i >= 0; --i)
+        if (mag.w[i]) return 64 * i + 64 - __clzll(static_cast<long long>(mag.w[i]));
+    return 0;
+}
+// any bit at positions [0, pos)
+__device__ __forceinline__ bool big_any_below(const Big& mag, int pos) {
+    if (pos <= 0) return false;
+    const int full = pos >> 6;
+    for (int i = 0; i < full && i < BW; ++i)
+        if (mag.w[i]) return true;
+    if (full < BW && (pos & 63)) return (mag.w[full] & ((1ull << (pos & 63)) - 1)) != 0;
+    return false;
+}
+// Magnitude shifted: mag * 2^sh for sh >= 0 (into the window), truncation with a
+// sticky flag for sh < 0.
+__device__ __forceinline__ void big_shift_mag(Big& m, int sh, bool* sticky) {
+    *sticky = false;
+    if (sh == 0) return;
+    Big r;
+    big_zero(r);
+    if (sh > 0) {
+        const int ws = sh >> 6, bs = sh & 63;
+        for (int i = BW - 1; i >= ws; --i) {
+            const uint64_t lo = m.w[i - ws] << bs;
+            const uint64_t carry = (bs && i - ws - 1 >= 0) ? (m.w[i - ws - 1] >> (64 - bs)) : 0;
+            r.w[i] = lo | carry;
+        }
+    } else {
+        const int d = -sh;
+        *sticky = big_any_below(m, d);
+        const int ws = d >> 6, bs = d & 63;
+        for (int i = 0; i + ws < BW; ++i) {
+            const uint64_t lo = m.w[i + ws] >> bs;
+            const uint64_t hi = (bs && i + ws + 1 < BW) ? (m.w[i + ws + 1] << (64 - bs)) : 0;
+            r.w[i] = lo | hi;
+        }
+    }
+    m = r;
+}
+
+// Word-array helpers for the encode (magnitudes, little-endian words).
+template <int NW>
+__device__ __forceinline__ int words_bitlen(const uint64_t (&m)[NW]) {
+    for (int i = NW - 1; i >= 0; --i)
+        if (m[i]) return 64 * i + 64 - __clzll(static_cast<long long>(m[i]));
+    return 0;
+}
+template <int NW>
+__device__ __forceinline__ int words_bit(const uint64_t (&m)[NW], int pos) {
+    if (pos < 0 || pos >= 64 * NW) return 0;
+    return static_cast<int>((m[pos >> 6] >> (pos & 63)) & 1);
+}
+template <int NW>
+__device__ __forceinline__ bool words_any_below(const uint64_t (&m)[NW], int pos) {
+    if (pos <= 0) return false;
+    const int full = pos >> 6;
+    for (int i = 0; i < full && i < NW; ++i)
+        if (m[i]) return true;
+    if (full < NW && (pos & 63)) return (m[full] & ((1ull << (pos & 63)) - 1)) != 0;
+    return false;
+}
+template <int NW>
+__device__ __forceinline__ void words_negate(uint64_t (&x)[NW]) {
+    uint64_t c = 1;
+    for (int i = 0; i < NW; ++i) {
+        const uint64_t s = ~x[i] + c;
+        c = (c && s == 0) ? 1 : 0;
+        x[i] = s;
+    }
+}
+
+// The correctly rounded encode (acc.rs:1734-1868) of the exact value W * 2^unit_exp
+// (W two's complement over NW words). min_exp_e is the element register's bit-0
+// exponent: a result whose last bit would fall below it encodes +0, as the
+// reference's register index does.
+template <int NW>
+__device__ uint64_t encode_words(const uint64_t (&Win)[NW], int unit_exp, bool out64, int mode,
+                                 int min_exp_e) {
+    const int MANT = out64 ? 52 : 23, EXPO = out64 ? 11 : 8;
+    const int P = MANT + 1;
+    const int BIAS = (1 << (EXPO - 1)) - 1;
+    const int SUB = 1 - BIAS - MANT;
+    const uint64_t sign_bit = out64 ? (1ull << 63) : (1ull << 31);
+    const uint64_t exp_all = (1ull << EXPO) - 1;
+    uint64_t mag[NW];
+    for (int i = 0; i < NW; ++i) mag[i] = Win[i];
+    const bool neg = (mag[NW - 1] >> 63) != 0;
+    if (neg) words_negate(mag);
+    const int bl = words_bitlen(mag);
+    if (bl == 0) return 0;  // exact zero encodes +0
+    const int exp = unit_exp + bl - 1;
+    int lsb_exp = exp - (P - 1) < SUB ? SUB : exp - (P - 1);
+    if (lsb_exp - min_exp_e < 0) return 0;
+    const int lsb = lsb_exp - unit_exp;
+    uint64_t sig = 0;
+    for (int q = 0; q < P; ++q) sig |= static_cast<uint64_t>(words_bit(mag, lsb + q)) << q;
+    bool round_bit = false, sticky = false;
+    if (lsb_exp - min_exp_e != 0) {
+        round_bit = words_bit(mag, lsb - 1) != 0;
+        sticky = words_any_below(mag, lsb - 1);
+    }
+    const bool inc = mode == MODE_NEAREST && round_bit && (sticky || (sig & 1));
+    sig += inc ? 1 : 0;
+    if (sig >> P) {
+        sig >>= 1;
+        lsb_exp += 1;
+    }
+    const uint64_t s = neg ? sign_bit : 0;
+    if (sig == 0) return s;
+    const int top = 63 - __clzll(static_cast<long long>(sig));
+    const int value_exp = lsb_exp + top;
+    if ((sig >> (P - 1)) == 1) {
+        const int biased = value_exp + BIAS;
+        if (biased >= static_cast<int>(exp_all)) {
+            if (mode == MODE_NEAREST) return s | (exp_all << MANT);
+            return s | ((exp_all - 1) << MANT) | ((1ull << MANT) - 1);
+        }
+        return s | (static_cast<uint64_t>(biased) << MANT) | (sig & ((1ull << MANT) - 1));
+    }
+    return s | sig;
+}
+
+__device__ __forceinline__ uint64_t nan_bits(bool out64) {
+    return out64 ? 0x7FF8000000000000ull : 0x7FC00000ull;
+}
+__device__ __forceinline__ uint64_t inf_bits(bool out64, bool neg) {
+    return out64 ? ((neg ? 1ull << 63 : 0) | 0x7FF0000000000000ull)
+                 : ((neg ? 1ull << 31 : 0) | 0x7F800000ull);
+}
+
+// Complete::scale's flag rules (acc.rs:1028-1069) on (flags, finite part).
+// Returns true when the finite part must be multiplied by f.
+__device__ __forceinline__ bool scale_flags(int& fl, bool& zero_out, int64_t f) {
+    const bool nan = (fl & 1) || ((fl & 6) == 6);
+    zero_out = false;
+    if (nan || f == 1) return false;
+    if (f == 0) {
+        zero_out = true;
+        if (fl & 6) fl = 1;
+        return false;
+    }
+    if (fl & 6) {
+        if (f < 0) fl = (fl & 1) | ((fl & 2) << 1) | ((fl & 4) >> 1);
+        return false;
+    }
+    return true;
+}
+
+// Store raw bits into an f32/f64 output cell.
+__device__ __forceinline__ void store_float(void* c, bool out64, int64_t off, uint64_t bits) {
+    if (out64) reinterpret_cast<uint64_t*>(c)[off] = bits;
+    else reinterpret_cast<uint32_t*>(c)[off] = static_cast<uint32_t>(bits);
+}
+
+// Place a magnitude at window shift sh. Bit 0 of the window is reserved: a term
+// placed whole (sh >= 1) leaves it clear; a term cut at the window's bottom keeps
+// its bits from position 1 up and sets bit 0 when anything was cut (a jammed sticky
+// bit that only decides rounding, as that term is then far below the result).
+__device__ __forceinline__ void place_jammed(Big& mag, int sh) {
+    bool cut = false, unused = false;
+    if (sh >= 1) {
+        big_shift_mag(mag, sh, &unused);
+        return;
+    }
+    big_shift_mag(mag, sh - 1, &cut);  // keep the bits from position 1 - sh up
+    big_shift_mag(mag, 1, &unused);    // make room for the jam bit
+    if (cut) mag.w[0] |= 1;
+}
+
+// beta * C, then the combine and the encode, for one cell whose product part is the
+// exact X * 2^ex with flags fl (alpha already applied).
+__device__ void finish_float(const FxEpi& e, int64_t off, Big& X, int ex, int fl) {
+    int pf = 0;
+    i128 Y = 0;
+    int ey = 0;
+    if (e.beta != 0) {
+        const FDec d = fdecode(static_cast<const uint8_t*>(e.c), off, e.out64);
+        if (d.kind == 2) pf = 1;
+        else if (d.kind == 1) pf = d.sign ? 4 : 2;
+        else {
+            // Complete::of (acc.rs:1007-1020) through add_scaled's placement rules.
+            const int sh = d.exp - e.min_exp_e;
+            if (d.mant != 0 && sh >= 0 && (sh >> 6) < e.limbs_e) {
+                Y = d.sign ? -static_cast<i128>(d.mant) : static_cast<i128>(d.mant);
+                ey = d.exp;
+            }
+        }
+        bool zy;
+        if (scale_flags(pf, zy, e.beta)) Y = Y * static_cast<i128>(e.beta);
+        if (zy) Y = 0;
+    }
+    const int flags = fl | pf;
+    if (flags) {
+        const bool nan = (flags & 1) || ((flags & 6) == 6);
+        store_float(e.c, e.out64, off, nan ? nan_bits(e.out64) : inf_bits(e.out64, (flags & 4) != 0));
+        return;
+    }
+    // Exact sum X * 2^ex + Y * 2^ey in a window whose unit is 2^(top - 760 - 1).
+    Big mx = X;
+    const bool nx = big_neg(mx);
+    if (nx) big_negate(mx);
+    const int blx = big_bitlen(mx);
+    const bool ny = Y < 0;
+    const u128 uy = ny ? static_cast<u128>(-Y) : static_cast<u128>(Y);
+    const int bly = uy == 0 ? 0 : (uy >> 64 ? 128 - __clzll(static_cast<long long>(uy >> 64))
+                                           : 64 - __clzll(static_cast<long long>(uy)));
+    if (blx == 0 && bly == 0) {
+        store_float(e.c, e.out64, off, 0);
+        return;
+    }
+    int top = INT_MIN;
+    if (blx) top = ex + blx;
+    if (bly && ey + bly > top) top = ey + bly;
+    const int unit = top - 760 - 1;
+    Big W;
+    big_zero(W);
+    if (blx) {
+        place_jammed(mx, ex - unit);
+        if (nx) big_negate(mx);
+        big_add(W, mx);
+    }
+    if (bly) {
+        Big my;
+        big_zero(my);
+        my.w[0] = static_cast<uint64_t>(uy);
+        my.w[1] = static_cast<uint64_t>(uy >> 64);
+        place_jammed(my, ey - unit);
+        if (ny) big_negate(my);
+        big_add(W, my);
+    }
+    store_float(e.c, e.out64, off, encode_words<BW>(W.w, unit, e.out64, e.mode, e.min_exp_e));
+}
+
+// ------------------------------------------------------------ K6 pre-passes
+
+// One warp per row of A: lowest set-bit and top-bit exponents over finite nonzero
+// elements, and whether the row holds a non-finite element.
+__global__ void fx_rows_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64_t csa, int m,
+                               int k, bool f64, int* __restrict__ lo, uint8_t* __restrict__ nf,
+                               int* __restrict__ gmax) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= m) return;
+    int l = INT_MAX, h = INT_MIN, f = 0;
+    for (int p = lane; p < k; p += 32) {
+        const FDec d = fdecode(a, static_cast<int64_t>(warp) * rsa + static_cast<int64_t>(p) * csa, f64);
+        if (d.kind != 0) f = 1;
+        else if (d.mant) {
+            const int tz = __ffsll(static_cast<long long>(d.mant)) - 1;
+            const int bl = 64 - __clzll(static_cast<long long>(d.mant));
+            l = min(l, d.exp + tz);
+            h = max(h, d.exp + bl - 1);
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        l = min(l, __shfl_xor_sync(0xffffffffu, l, o));
+        h = max(h, __shfl_xor_sync(0xffffffffu, h, o));
+        f |= __shfl_xor_sync(0xffffffffu, f, o);
+    }
+    if (lane == 0) {
+        lo[warp] = l == INT_MAX ? 0 : l;
+        nf[warp] = static_cast<uint8_t>(f);
+        if (l != INT_MAX) atomicMax(&gmax[0], h - l + 1);
+        if (f) atomicOr(&gmax[2], 1);
+    }
+}
+
+// One thread per column of B.
+__global__ void fx_cols_kernel(const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, int k,
+                               int n, bool f64, int* __restrict__ lo, uint8_t* __restrict__ nf,
+                               int* __restrict__ gmax) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    int l = INT_MAX, h = INT_MIN, f = 0;
+    for (int p = 0; p < k; ++p) {
+        const FDec d = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64);
+        if (d.kind != 0) f = 1;
+        else if (d.mant) {
+            const int tz = __ffsll(static_cast<long long>(d.mant)) - 1;
+            const int bl = 64 - __clzll(static_cast<long long>(d.mant));
+            l = min(l, d.exp + tz);
+            h = max(h, d.exp + bl - 1);
+        }
+    }
+    lo[j] = l == INT_MAX ? 0 : l;
+    nf[j] = static_cast<uint8_t>(f);
+    if (l != INT_MAX) atomicMax(&gmax[1], h - l + 1);
+    if (f) atomicOr(&gmax[2], 1);
+}
+
+// Balanced base-256 digits of the exact scaled integer of one element.
+__device__ __forceinline__ i128 fx_scaled(const FDec& d, int lo) {
+    if (d.kind != 0 || d.mant == 0) return 0;
+    const int tz = __ffsll(static_cast<long long>(d.mant)) - 1;
+    const int sh = d.exp + tz - lo;  // >= 0 by the choice of lo
+    const i128 v = static_cast<i128>(d.mant >> tz) << sh;
+    return d.sign ? -v : v;
+}
+
+__global__ void fx_slice_a_kernel(int8_t* __restrict__ as, int L, int mp, int kp,
+                                  const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
+                                  bool f64, int m, int k, const int* __restrict__ lo) {
+    const int64_t plane = static_cast<int64_t>(mp) * kp;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < plane;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(idx / kp), p = static_cast<int>(idx % kp);
+        i128 x = 0;
+        if (i < m && p < k)
+            x = fx_scaled(fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, f64),
+                          lo[i]);
+        for (int s = 0; s < L; ++s) {
+            const int dgt = (static_cast<int>(static_cast<uint64_t>(x) & 255) ^ 128) - 128;
+            as[s * plane + idx] = static_cast<int8_t>(dgt);
+            x = (x - dgt) >> 8;
+        }
+    }
+}
+
+__global__ void fx_slice_b_kernel(int8_t* __restrict__ bs, int L, int np, int kp,
+                                  const uint8_t* __restrict__ b, int64_t rsb, int64_t csb,
+                                  bool f64, int k, int n, const int* __restrict__ lo) {
+    __shared__ i128 tile[32][33];
+    const int p0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    for (int r = ty; r < 32; r += 8) {
+        const int p = p0 + r, j = j0 + tx;
+        i128 x = 0;
+        if (p < k && j < n)
+            x = fx_scaled(fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64),
+                          lo[j]);
+        tile[r][tx] = x;
+    }
+    __syncthreads();
+    const int64_t plane = static_cast<int64_t>(np) * kp;
+    for (int r = ty; r < 32; r += 8) {
+        const int j = j0 + r, p = p0 + tx;
+        if (j < np && p < kp) {
+            i128 x = tile[tx][r];
+            for (int s = 0; s < L; ++s) {
+                const int dgt = (static_cast<int>(static_cast<uint64_t>(x) & 255) ^ 128) - 128;
+                bs[s * plane + static_cast<int64_t>(j) * kp + p] = static_cast<int8_t>(dgt);
+                x = (x - dgt) >> 8;
+            }
+        }
+    }
+}
+
+// Per-cell product flags, visiting only the reductions that touch a non-finite.
+__global__ void fx_flags_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
+                                const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, bool f64,
+                                int m, int k, int n, const uint8_t* __restrict__ rnf,
+                                const uint8_t* __restrict__ cnf, uint8_t* __restrict__ flags) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    for (int i = blockIdx.y; i < m; i += gridDim.y) {
+    int f = 0;
+    if (rnf[i] || cnf[j]) {
+        for (int p = 0; p < k; ++p) {
+            const FDec x = fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, f64);
+            const FDec y = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64);
+            f |= term_flags(x, y);
+        }
+    }
+    flags[static_cast<size_t>(i) * n + j] = static_cast<uint8_t>(f);
+    }
+}
+
+// ------------------------------------------------------------ K7 reduce
+
+__global__ void fx_reduce_kernel(const int32_t* __restrict__ part, int chunks, int groups, int m,
+                                 int n, const int* __restrict__ rlo, const int* __restrict__ clo,
+                                 const uint8_t* __restrict__ flags, FxEpi e) {
+    const size_t total = static_cast<size_t>(m) * n;
+    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+        Big X;
+        big_zero(X);
+        for (int g = 0; g < groups; ++g) {
+            int64_t s = 0;
+            for (int q = 0; q < chunks; ++q) s += part[(static_cast<size_t>(q) * groups + g) * total + idx];
+            if (s) big_add_i64_shl(X, s, 8 * g);
+        }
+        int fl = flags ? flags[idx] : 0;
+        bool zero_out;
+        if (scale_flags(fl, zero_out, e.alpha)) big_mul_i64(X, e.alpha);
+        if (zero_out) big_zero(X);
+        const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+        finish_float(e, off, X, rlo[i] + clo[j], fl);
+    }
+}
+
+// ------------------------------------------------------------ direct route
+
+// The reference's register, Complete<L, MIN_EXP>: L low limbs and an extension word,
+// here as L + 1 words of one two's complement integer (f64: 68 words, in local memory).
+template <int NW>
+__device__ void reg_add_scaled(uint64_t* r, int min_exp, u128 mag, int exp, bool negative) {
+    if (mag == 0) return;
+    const int sh = exp - min_exp;
+    if (sh < 0) return;
+    const int at = sh >> 6, bit = sh & 63;
+    if (at >= NW - 1) return;
+    uint64_t parts[3];
+    if (bit == 0) {
+        parts[0] = static_cast<uint64_t>(mag);
+        parts[1] = static_cast<uint64_t>(mag >> 64);
+        parts[2] = 0;
+    } else {
+        parts[0] = static_cast<uint64_t>(mag << bit);
+        parts[1] = static_cast<uint64_t>(mag >> (64 - bit));
+        parts[2] = static_cast<uint64_t>(mag >> (128 - bit));
+    }
+    if (!negative) {
+        uint64_t c = 0;
+        for (int i = at, q = 0; i < NW && (q < 3 || c); ++i, ++q) {
+            const uint64_t add = q < 3 ? parts[q] : 0;
+            const uint64_t s = r[i] + add;
+            const uint64_t c1 = s < r[i];
+            const uint64_t s2 = s + c;
+            const uint64_t c2 = s2 < s;
+            r[i] = s2;
+            c = c1 | c2;
+        }
+    } else {
+        uint64_t bw = 0;
+        for (int i = at, q = 0; i < NW && (q < 3 || bw); ++i, ++q) {
+            const uint64_t sub = q < 3 ? parts[q] : 0;
+            const uint64_t d = r[i] - sub;
+            const uint64_t b1 = r[i] < sub;
+            const uint64_t d2 = d - bw;
+            const uint64_t b2 = d < bw;
+            r[i] = d2;
+            bw = b1 | b2;
+        }
+    }
+}
+
+template <int NW>
+__global__ void fx_direct_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
+                                 const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, int m,
+                                 int k, int n, FxEpi e) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    for (int i = blockIdx.y; i < m; i += gridDim.y) {
+    uint64_t r[NW];
+    for (int w = 0; w < NW; ++w) r[w] = 0;
+    int fl = 0;
+    for (int p = 0; p < k; ++p) {
+        const FDec x = fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, e.e64);
+        const FDec y = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, e.e64);
+        const int tf = term_flags(x, y);
+        if (tf) fl |= tf;
+        else reg_add_scaled<NW>(r, e.min_exp_e, static_cast<u128>(x.mant) * y.mant, x.exp + y.exp,
+                                x.sign != y.sign);
+    }
+    // Linear::finish in the register itself: scale by alpha (exact: the register
+    // spans the whole terminal expression), then add beta * Complete::of(C).
+    bool zero_out;
+    if (scale_flags(fl, zero_out, e.alpha)) {
+        const bool nr = (r[NW - 1] >> 63) != 0;
+        if (nr) words_negate(r);
+        const uint64_t uf = e.alpha < 0 ? 0ull - static_cast<uint64_t>(e.alpha)
+                                        : static_cast<uint64_t>(e.alpha);
+        uint64_t carry = 0;
+        for (int w = 0; w < NW; ++w) {
+            const u128 pr = static_cast<u128>(r[w]) * uf + carry;
+            r[w] = static_cast<uint64_t>(pr);
+            carry = static_cast<uint64_t>(pr >> 64);
+        }
+        if (nr != (e.alpha < 0)) words_negate(r);
+    }
+    if (zero_out)
+        for (int w = 0; w < NW; ++w) r[w] = 0;
+    const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+    if (e.beta != 0) {
+        const FDec d = fdecode(static_cast<const uint8_t*>(e.c), off, e.out64);
+        int pf = 0;
+        uint64_t q[NW];
+        for (int w = 0; w < NW; ++w) q[w] = 0;
+        if (d.kind == 2) pf = 1;
+        else if (d.kind == 1) pf = d.sign ? 4 : 2;
+        else reg_add_scaled<NW>(q, e.min_exp_e, d.mant, d.exp, d.sign != 0);
+        bool zq;
+        if (scale_flags(pf, zq, e.beta)) {
+            const bool nq = (q[NW - 1] >> 63) != 0;
+            if (nq) words_negate(q);
+            const uint64_t uf = e.beta < 0 ? 0ull - static_cast<uint64_t>(e.beta)
+                                           : static_cast<uint64_t>(e.beta);
+            uint64_t carry = 0;
+            for (int w = 0; w < NW; ++w) {
+                const u128 pr = static_cast<u128>(q[w]) * uf + carry;
+                q[w] = static_cast<uint64_t>(pr);
+                carry = static_cast<uint64_t>(pr >> 64);
+            }
+            if (nq != (e.beta < 0)) words_negate(q);
+        }
+        if (fl || pf) {
+            fl |= pf;
+        } else {
+            uint64_t c = 0;
+            for (int w = 0; w < NW; ++w) {
+                const uint64_t s1 = r[w] + q[w];
+                const uint64_t c1 = s1 < r[w];
+                const uint64_t s2 = s1 + c;
+                const uint64_t c2 = s2 < s1;
+                r[w] = s2;
+                c = c1 | c2;
+            }
+        }
+    }
+    if (fl) {
+        const bool nan = (fl & 1) || ((fl & 6) == 6);
+        store_float(e.c, e.out64, off, nan ? nan_bits(e.out64) : inf_bits(e.out64, (fl & 4) != 0));
+        continue;
+    }
+    store_float(e.c, e.out64, off, encode_words<NW>(r, e.min_exp_e, e.out64, e.mode, e.min_exp_e));
+    }
+}
+
+// ------------------------------------------------------------ driver
+
+static inline size_t rup(size_t x, size_t a) { return (x + a - 1) / a * a; }
+constexpr int FX_MAX_DIGITS = 16;
+
+int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrdiff_t rsa,
+                   ptrdiff_t csa, const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c,
+                   ptrdiff_t rsc, ptrdiff_t csc, size_t m, size_t k, size_t n, int64_t alpha,
+                   int64_t beta, int mode, uor_b200_route* route) {
+    cudaStream_t s = ctx->stream;
+    if (route) *route = uor_b200_route{};
+    if (m == 0 || n == 0) return UOR_B200_OK;
+    if (m > (size_t)INT_MAX / 4 || n > (size_t)INT_MAX / 4 || k > (size_t)INT_MAX / 4)
+        return UOR_B200_UNSUPPORTED;
+    FxEpi e{};
+    e.alpha = alpha;
+    e.beta = beta;
+    e.mode = mode;
+    e.e64 = e64;
+    e.out64 = o64;
+    e.min_exp_e = e64 ? -2148 : -298;
+    e.limbs_e = e64 ? 67 : 10;
+    e.c = c;
+    e.rsc = rsc;
+    e.csc = csc;
+    if (route) {
+        route->kernel = UOR_B200_KERNEL_FLOAT_EXACT;
+        route->tile_m = KS_BM;
+        route->tile_n = KS_BN;
+        route->tile_k = KS_BK;
+    }
+
+    // ---- analysis: per-row / per-column exponent spans and non-finite markers
+    int st = UOR_B200_OK;
+    const size_t an_bytes = rup(m * 4, 256) + rup(n * 4, 256) + rup(m, 256) + rup(n, 256) + 256;
+    uint8_t* an = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, an_bytes, &st));
+    if (!an) return st;
+    int* rlo = reinterpret_cast<int*>(an);
+    int* clo = reinterpret_cast<int*>(an + rup(m * 4, 256));
+    uint8_t* rnf = an + rup(m * 4, 256) + rup(n * 4, 256);
+    uint8_t* cnf = rnf + rup(m, 256);
+    int* gmax = reinterpret_cast<int*>(cnf + rup(n, 256));
+    if (cudaMemsetAsync(gmax, 0, 16, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    if (k > 0) {
+        fx_rows_kernel<<<(int)((m * 32 + 255) / 256), 256, 0, s>>>(a, rsa, csa, (int)m, (int)k, e64,
+                                                                   rlo, rnf, gmax);
+        fx_cols_kernel<<<(int)((n + 127) / 128), 128, 0, s>>>(b, rsb, csb, (int)k, (int)n, e64, clo,
+                                                              cnf, gmax);
+    } else {
+        cudaMemsetAsync(rlo, 0, m * 4, s);
+        cudaMemsetAsync(clo, 0, n * 4, s);
+        cudaMemsetAsync(rnf, 0, m, s);
+        cudaMemsetAsync(cnf, 0, n, s);
+    }
+    int g[4] = {0, 0, 0, 0};
+    if (cudaMemcpyAsync(g, gmax, 16, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return UOR_B200_DEVICE_ERROR;
+    const int La = g[0] ? (g[0] + 2 + 7) / 8 : 0;
+    const int Lb = g[1] ? (g[1] + 2 + 7) / 8 : 0;
+    const bool any_nf = g[2] != 0;
+
+    if (La > FX_MAX_DIGITS || Lb > FX_MAX_DIGITS) {
+        // Direct route: the reference's register per cell on CUDA cores.
+        if (route) route->tile_m = route->tile_n = route->tile_k = 0;
+        dim3 grid((unsigned)((n + 127) / 128), (unsigned)(m < 65535 ? m : 65535));
+        if (e64) fx_direct_kernel<68><<<grid, 128, 0, s>>>(a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, e);
+        else fx_direct_kernel<11><<<grid, 128, 0, s>>>(a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, e);
+        return cuda_status(cudaGetLastError());
+    }
+
+    // ---- digit slices and the slice-pair product
+    KSParams p{};
+    int npairs = 0, ngroups = 0, worst = 1;
+    if (La && Lb) {
+        for (int d = 0; d <= La + Lb - 2; ++d) {
+            p.pair_begin[ngroups] = npairs;
+            int cnt = 0;
+            for (int sa = 0; sa < La; ++sa) {
+                const int sb = d - sa;
+                if (sb < 0 || sb >= Lb) continue;
+                p.pair_a[npairs] = (uint8_t)sa;
+                p.pair_b[npairs] = (uint8_t)sb;
+                p.pair_idesc[npairs] = idesc_i8(KS_BM, KS_BN, true, true, false, false);
+                ++npairs;
+                ++cnt;
+            }
+            ++ngroups;
+            if (cnt > worst) worst = cnt;
+        }
+    }
+    p.pair_begin[ngroups] = npairs;
+    p.num_groups = ngroups;
+    const int num_kb = (int)((k + KS_BK - 1) / KS_BK);
+    // |digit product| <= 2^14; a diagonal of `worst` pairs must stay inside s32.
+    const int64_t lane = (int64_t)INT_MAX / ((int64_t)worst * 16384) / KS_BK;
+    p.kb_per_chunk = (int)(lane < num_kb ? lane : num_kb);
+    if (p.kb_per_chunk < 1) p.kb_per_chunk = 1;
+    p.num_chunks = num_kb ? (num_kb + p.kb_per_chunk - 1) / p.kb_per_chunk : 0;
+    p.num_kb = num_kb;
+    p.m = (int)m;
+    p.n = (int)n;
+    p.mp = (int)rup(m, KS_BM);
+    p.np = (int)rup(n, KS_BN);
+    p.tiles_m = p.mp / KS_BM;
+    p.tiles_n = p.np / KS_BN;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
+    p.status = ctx->d_status;
+    p.budget_ns = ctx->budget_ns;
+    const bool run_mma = npairs > 0 && num_kb > 0;
+
+    const size_t kp = rup(k ? k : 1, 16);
+    const size_t a_bytes = run_mma ? rup((size_t)La * p.mp * kp, 256) : 0;
+    const size_t b_bytes = run_mma ? rup((size_t)Lb * p.np * kp, 256) : 0;
+    const size_t part_bytes = run_mma ? rup((size_t)p.num_chunks * ngroups * m * n * 4, 256) : 0;
+    const size_t flag_bytes = any_nf ? rup(m * n, 256) : 0;
+    uint8_t* ws = static_cast<uint8_t*>(
+        ctx_buffer(ctx, SLOT_WS, a_bytes + b_bytes + part_bytes + flag_bytes + 256, &st));
+    if (!ws) return st;
+    int8_t* as = reinterpret_cast<int8_t*>(ws);
+    int8_t* bs = reinterpret_cast<int8_t*>(ws + a_bytes);
+    int32_t* part = reinterpret_cast<int32_t*>(ws + a_bytes + b_bytes);
+    uint8_t* flags = any_nf ? ws + a_bytes + b_bytes + part_bytes : nullptr;
+    p.partial = part;
+
+    if (any_nf) {
+        dim3 grid((unsigned)((n + 127) / 128), (unsigned)(m < 65535 ? m : 65535));
+        fx_flags_kernel<<<grid, 128, 0, s>>>(a, rsa, csa, b, rsb, csb, e64, (int)m, (int)k, (int)n,
+                                              rnf, cnf, flags);
+    }
+    if (run_mma) {
+        const int64_t total = (int64_t)p.mp * kp;
+        const int grid = (int)(total / 256 + 1 < 148 * 32 ? total / 256 + 1 : 148 * 32);
+        fx_slice_a_kernel<<<grid, 256, 0, s>>>(as, La, p.mp, (int)kp, a, rsa, csa, e64, (int)m,
+                                               (int)k, rlo);
+        dim3 g2((unsigned)(p.np / 32), (unsigned)((kp + 31) / 32));
+        fx_slice_b_kernel<<<g2, dim3(32, 8), 0, s>>>(bs, Lb, p.np, (int)kp, b, rsb, csb, e64,
+                                                     (int)k, (int)n, clo);
+        CUtensorMap tmA, tmB;
+        if (!make_tmap_u8(&tmA, as, k, (uint64_t)La * p.mp, kp, 128, 128) ||
+            !make_tmap_u8(&tmB, bs, k, (uint64_t)Lb * p.np, kp, 128, 256))
+            return UOR_B200_DEVICE_ERROR;
+        const int units = ngroups * p.num_chunks * p.num_tiles;
+        const int grid2 = units < ctx->sm_count ? units : ctx->sm_count;
+        if (route) {
+            route->k_chunks = (uint32_t)p.num_chunks;
+            route->ctas = (uint32_t)grid2;
+            route->a_layout = (uint32_t)La;  // digits per A element
+            route->b_layout = (uint32_t)Lb;
+        }
+        if (ks_launch(tmA, tmB, p, grid2, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    }
+    const size_t total = m * n;
+    const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+    fx_reduce_kernel<<<rgrid, 256, 0, s>>>(part, run_mma ? p.num_chunks : 0, run_mma ? ngroups : 0,
+                                           (int)m, (int)n, rlo, clo, flags, e);
+    return cuda_status(cudaGetLastError());
+}
+
+}  // namespace uor

@@ -268,6 +268,19 @@ def gemm_float(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, 
            "gemm_float")
 
 
+def slice_gemm_float_ex(elem, out, m, k, n, alpha, a, lda, b, ldb, beta, c, ldc, encode=NEAREST,
+                        ctx=None, route=None):
+    """slice::gemm_float_ex (slice.rs:304-356)."""
+    dev = _on_device(a, b, c)
+    pa, la, _ = _buffer(a)
+    pb, lb, _ = _buffer(b)
+    pc, lc, _ = _buffer(c)
+    call = make_call(encode, dev, ctx, route)
+    _check(lib().uor_b200_slice_gemm_float_ex(elem, out, m, k, n, alpha, pa, la, lda, pb, lb, ldb,
+                                              beta, pc, lc, ldc, None, 0, None, 0,
+                                              ctypes.byref(call)), "slice_gemm_float_ex")
+
+
 def sgemm(m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc, csc, origin=(0, 0, 0),
           ctx=None, route=None, encode=NEAREST):
     """raw::sgemm (raw.rs:45-64); `origin` gives the element index of (0,0) in each buffer."""
