@@ -55,4 +55,11 @@ struct K1Params {
 cudaError_t k1_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, bool a_mn, bool b_mn,
                       const K1Params& p, int grid, cudaStream_t stream);
 
+// The same GEMM on CTA pairs (tcgen05 cta_group::2): 256 x 256 tiles, p.tiles_m counts
+// 256-row tiles and p.idesc must describe M256 N256. Grid and cluster size are chosen
+// here (clusters of 2, as many as can be resident).
+cudaError_t k1_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, bool a_mn, bool b_mn,
+                           const K1Params& p, cudaStream_t stream);
+int k1_pair_max_clusters();
+
 }  // namespace uor

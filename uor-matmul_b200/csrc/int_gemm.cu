@@ -96,26 +96,39 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
         route->b_layout = b_layout;
     }
 
+    // Tiles of 256 rows on CTA pairs when there are rows to fill them; 128-row tiles
+    // on single CTAs otherwise. A pair's CTAs each load 128 columns of B.
+    const bool pair = m > 128;
     CUtensorMap tmA, tmB;
     bool ok = a_layout == 0 ? make_tmap_u8(&tmA, a, k, m, a_stride, 128, 128)
                             : make_tmap_u8(&tmA, a, m, k, a_stride, 128, 128);
-    ok = ok && (b_layout == 0 ? make_tmap_u8(&tmB, b, k, n, b_stride, 128, 256)
+    ok = ok && (b_layout == 0 ? make_tmap_u8(&tmB, b, k, n, b_stride, 128, pair ? 128 : 256)
                               : make_tmap_u8(&tmB, b, n, k, b_stride, 128, 128));
     if (!ok) return UOR_B200_DEVICE_ERROR;
 
+    const int bm = pair ? 256 : K1_BM;
     K1Params p{};
     p.m = (int)m;
     p.n = (int)n;
-    p.tiles_m = (int)((m + K1_BM - 1) / K1_BM);
+    p.tiles_m = (int)((m + bm - 1) / bm);
     p.tiles_n = (int)((n + K1_BN - 1) / K1_BN);
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
-    p.idesc = idesc_i8(K1_BM, K1_BN, true, true, a_layout == 1, b_layout == 1);
+    p.idesc = idesc_i8(bm, K1_BN, true, true, a_layout == 1, b_layout == 1);
     p.status = ctx->d_status;
     p.budget_ns = ctx->budget_ns;
-    const int grid = p.num_tiles < ctx->sm_count ? p.num_tiles : ctx->sm_count;
+    int grid = p.num_tiles < ctx->sm_count ? p.num_tiles : ctx->sm_count;
+    if (pair) {
+        const int mc = k1_pair_max_clusters();
+        grid = 2 * (p.num_tiles < mc ? p.num_tiles : mc);
+    }
+    auto launch = [&](const K1Params& q) {
+        return pair ? k1_pair_launch(tmA, tmB, a_layout == 1, b_layout == 1, q, s)
+                    : k1_launch(tmA, tmB, a_layout == 1, b_layout == 1, q, grid, s);
+    };
     if (route) {
         route->kernel = UOR_B200_KERNEL_I8_TCGEN05;
+        route->tile_m = (uint32_t)bm;
         route->k_chunks = (uint32_t)chunks;
         route->ctas = (uint32_t)grid;
     }
@@ -129,7 +142,7 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
         p.epi = epi;
         p.fast = epi.kind == OUT_I32 && epi.alpha == 1 && epi.beta == 0 && csc == 1 &&
                  (m == 1 || (rsc > 0 && (rsc & 3) == 0)) && aligned16(c);
-        return cuda_status(k1_launch(tmA, tmB, a_layout == 1, b_layout == 1, p, grid, s));
+        return cuda_status(launch(p));
     }
 
     // Deep reduction: exact s32 partials per chunk, then one exact fold.
@@ -144,7 +157,7 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
         p.csc = 1;
         p.epi = LinearEpi{1, 0, MODE_NEAREST, OUT_I32};
         p.fast = (n % 4) == 0;
-        cudaError_t e = k1_launch(tmA, tmB, a_layout == 1, b_layout == 1, p, grid, s);
+        cudaError_t e = launch(p);
         if (e != cudaSuccess) return UOR_B200_DEVICE_ERROR;
     }
     return cuda_status(reduce_chunks(part, chunks, m, n, c, rsc, csc, epi, s));
