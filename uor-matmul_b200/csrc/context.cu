@@ -123,6 +123,20 @@ bool make_tmap_u8(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t di
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_s32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                   uint64_t stride1_bytes, uint32_t box0, uint32_t box1) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {dim0, dim1};
+    cuuint64_t strides[1] = {stride1_bytes};
+    cuuint32_t box[2] = {box0, box1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 bool view_extent(size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs, ptrdiff_t* lo,
                  ptrdiff_t* hi) {
     if (rows == 0 || cols == 0) {

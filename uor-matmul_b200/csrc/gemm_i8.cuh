@@ -44,6 +44,7 @@ struct K1Params {
     int64_t rsc, csc;    // output element strides
     LinearEpi epi;
     int fast;            // s32 output, alpha 1, beta 0, unit column stride, 16-byte rows
+    int tma_store;       // pair kernel: fast output written by TMA stores through tmC
     uint32_t idesc;
     int* status;
     uint64_t budget_ns;
@@ -57,9 +58,10 @@ cudaError_t k1_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, bool a_mn,
 
 // The same GEMM on CTA pairs (tcgen05 cta_group::2): 256 x 256 tiles, p.tiles_m counts
 // 256-row tiles and p.idesc must describe M256 N256. Grid and cluster size are chosen
-// here (clusters of 2, as many as can be resident).
-cudaError_t k1_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, bool a_mn, bool b_mn,
-                           const K1Params& p, cudaStream_t stream);
+// here (clusters of 2, as many as can be resident). With p.tma_store, tmC is an s32
+// tensor map of the output (dims {n, m}, box {32, 32}, 128-byte swizzle).
+cudaError_t k1_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                           bool a_mn, bool b_mn, const K1Params& p, cudaStream_t stream);
 int k1_pair_max_clusters();
 
 }  // namespace uor

@@ -24,7 +24,9 @@ constexpr int KP_THREADS = 192;
 constexpr int KP_A_BYTES = 128 * KP_BK;
 constexpr int KP_B_BYTES = 128 * KP_BK;
 constexpr int KP_STAGE_BYTES = KP_A_BYTES + KP_B_BYTES;
-constexpr int KP_SMEM_BYTES = KP_STAGES * KP_STAGE_BYTES + 1024 + 256;
+// Epilogue staging for TMA stores: per epilogue warp two 32 x 32 s32 blocks (4 KiB each).
+constexpr int KP_EPI_BYTES = 4 * 2 * 4096;
+constexpr int KP_SMEM_BYTES = KP_STAGES * KP_STAGE_BYTES + KP_EPI_BYTES + 1024 + 256;
 
 __device__ __forceinline__ void kp_tile(int t, const K1Params& p, int& tm, int& tn) {
     const int group = p.group_m * p.tiles_n;
@@ -39,11 +41,12 @@ __device__ __forceinline__ void kp_tile(int t, const K1Params& p, int& tm, int& 
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(KP_THREADS, 1)
     k1_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const K1Params p) {
+                   const __grid_constant__ CUtensorMap tmC, const K1Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + KP_STAGES * KP_STAGE_BYTES);
+    uint8_t* epi_smem = smem + KP_STAGES * KP_STAGE_BYTES;  // 1 KiB aligned
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + KP_EPI_BYTES);
     const uint32_t full0 = smem_u32(bars);
     const uint32_t empty0 = smem_u32(bars + KP_STAGES);
     const uint32_t tfull0 = smem_u32(bars + 2 * KP_STAGES);
@@ -71,6 +74,7 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (p.tma_store) tma_prefetch_desc(&tmC);
     }
     if (warp == 1) tmem_alloc_pair(smem_u32(tmem_slot), 2 * KP_BN);
     tc_fence_before();
@@ -182,7 +186,9 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
         // ------------------------------------------------------------ epilogue (both CTAs)
         const int quarter = warp & 3;
         const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
-        int local = 0;
+        // Two 4 KiB staging blocks per warp, 128-byte swizzled as the C tensor map expects.
+        uint8_t* stage_w = epi_smem + quarter * 2 * 4096;
+        int local = 0, nstore = 0;
         for (int t = cid; t < p.num_tiles; t += ncl, ++local) {
             const int buf = local & 1;
             const uint32_t aphase = (local >> 1) & 1;
@@ -194,6 +200,7 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
             kp_tile(t, p, tm, tn);
             const int row = tm * KP_BM + row_in_tile;
             const bool row_ok = row < p.m;
+            const int wrow0 = tm * KP_BM + static_cast<int>(rank) * 128 + quarter * 32;
 #pragma unroll 1
             for (int cc = 0; cc < KP_BN / 32; ++cc) {
                 uint32_t r[32];
@@ -202,8 +209,33 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
                 __syncwarp();
                 tmem_ld32(taddr, r);
                 tmem_ld_wait();
+                if (cc == KP_BN / 32 - 1) {
+                    // The accumulator is in registers: hand TMEM back before storing.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty0 + 8 * buf, 0));
+                }
                 const int col0 = tn * KP_BN + cc * 32;
-                if (row_ok && col0 < p.n) {
+                if (p.tma_store) {
+                    if (wrow0 < p.m && col0 < p.n) {
+                        uint8_t* sb = stage_w + (nstore & 1) * 4096;
+                        if (lane == 0) bulk_wait_read<1>();  // this block's previous store has read it
+                        __syncwarp();
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            *reinterpret_cast<int4*>(sb + lane * 128 + ((v ^ (lane & 7)) << 4)) =
+                                make_int4(static_cast<int>(r[4 * v]), static_cast<int>(r[4 * v + 1]),
+                                          static_cast<int>(r[4 * v + 2]),
+                                          static_cast<int>(r[4 * v + 3]));
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmC, smem_u32(sb), col0, wrow0);
+                            bulk_commit();
+                        }
+                        ++nstore;
+                    }
+                } else if (row_ok && col0 < p.n) {
                     if (p.fast && col0 + 32 <= p.n) {
                         int4* dst = reinterpret_cast<int4*>(static_cast<int32_t*>(p.c) +
                                                             static_cast<int64_t>(row) * p.rsc + col0);
@@ -226,10 +258,9 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty0 + 8 * buf, 0));
         }
+        if (lane == 0) bulk_wait_all();  // every store has left shared memory
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -242,8 +273,8 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
 }
 
 template <bool A_MN, bool B_MN>
-static cudaError_t kp_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const K1Params& p,
-                               int max_clusters, cudaStream_t stream) {
+static cudaError_t kp_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                               const K1Params& p, int max_clusters, cudaStream_t stream) {
     auto kern = k1_pair_kernel<A_MN, B_MN>;
     static bool attr_done[64] = {};
     int dev = 0;
@@ -267,7 +298,7 @@ static cudaError_t kp_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmB, c
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p);
+    return cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
 }
 
 // How many CTA pairs of this kernel can be resident at once (queried once per device).
@@ -300,15 +331,15 @@ int k1_pair_max_clusters() {
     return n;
 }
 
-cudaError_t k1_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, bool a_mn, bool b_mn,
-                           const K1Params& p, cudaStream_t stream) {
+cudaError_t k1_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                           bool a_mn, bool b_mn, const K1Params& p, cudaStream_t stream) {
     const int mc = k1_pair_max_clusters();
     if (a_mn) {
-        return b_mn ? kp_launch_t<true, true>(tmA, tmB, p, mc, stream)
-                    : kp_launch_t<true, false>(tmA, tmB, p, mc, stream);
+        return b_mn ? kp_launch_t<true, true>(tmA, tmB, tmC, p, mc, stream)
+                    : kp_launch_t<true, false>(tmA, tmB, tmC, p, mc, stream);
     }
-    return b_mn ? kp_launch_t<false, true>(tmA, tmB, p, mc, stream)
-                : kp_launch_t<false, false>(tmA, tmB, p, mc, stream);
+    return b_mn ? kp_launch_t<false, true>(tmA, tmB, tmC, p, mc, stream)
+                : kp_launch_t<false, false>(tmA, tmB, tmC, p, mc, stream);
 }
 
 }  // namespace uor

@@ -122,9 +122,16 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
         const int mc = k1_pair_max_clusters();
         grid = 2 * (p.num_tiles < mc ? p.num_tiles : mc);
     }
-    auto launch = [&](const K1Params& q) {
-        return pair ? k1_pair_launch(tmA, tmB, a_layout == 1, b_layout == 1, q, s)
-                    : k1_launch(tmA, tmB, a_layout == 1, b_layout == 1, q, grid, s);
+    // The pair kernel writes an s32 output it can describe to TMA with bulk stores.
+    CUtensorMap tmC;
+    auto launch = [&](K1Params q) {
+        if (!pair) return k1_launch(tmA, tmB, a_layout == 1, b_layout == 1, q, grid, s);
+        const int64_t ld = q.rsc;
+        q.tma_store = q.fast && aligned16(q.c) && (m == 1 || (ld > 0 && (ld & 3) == 0 &&
+                                                             ld >= (int64_t)n)) &&
+                      make_tmap_s32(&tmC, q.c, n, m, (uint64_t)(m == 1 ? ((n + 3) / 4 * 4) : ld) * 4,
+                                    32, 32);
+        return k1_pair_launch(tmA, tmB, tmC, a_layout == 1, b_layout == 1, q, s);
     };
     if (route) {
         route->kernel = UOR_B200_KERNEL_I8_TCGEN05;

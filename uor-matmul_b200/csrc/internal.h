@@ -46,6 +46,11 @@ int cuda_status(cudaError_t e);
 bool make_tmap_u8(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
                   uint64_t stride1, uint32_t box0, uint32_t box1, bool swizzle128 = true);
 
+// A 2-D s32 tensor map (dims {dim0, dim1}, byte stride of dim1), for TMA stores of
+// an s32 output; 128-byte swizzle.
+bool make_tmap_s32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                   uint64_t stride1_bytes, uint32_t box0, uint32_t box1);
+
 // A view after placement: origin pointer and the reach of the view in elements.
 struct Placed {
     const uint8_t* origin;  // element (0,0)
