@@ -188,6 +188,7 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
         const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
         // Two 4 KiB staging blocks per warp, 128-byte swizzled as the C tensor map expects.
         uint8_t* stage_w = epi_smem + quarter * 2 * 4096;
+        const uint64_t out_policy = l2_policy_evict_first();  // C is written once, never re-read
         int local = 0, nstore = 0;
         for (int t = cid; t < p.num_tiles; t += ncl, ++local) {
             const int buf = local & 1;
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
                         fence_proxy_async();
                         __syncwarp();
                         if (lane == 0) {
-                            tma_store_2d(&tmC, smem_u32(sb), col0, wrow0);
+                            tma_store_2d_hint(&tmC, smem_u32(sb), col0, wrow0, out_policy);
                             bulk_commit();
                         }
                         ++nstore;

@@ -311,6 +311,15 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                  "r"(src), "r"(x), "r"(y)
                  : "memory");
 }
+// The same store with an L2 eviction-priority hint (the output is written once).
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, uint32_t src, int32_t x,
+                                                  int32_t y, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(src), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
 __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
