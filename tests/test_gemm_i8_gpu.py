@@ -193,6 +193,26 @@ def test_device_pointers_zero_copy():
     assert np.array_equal(tc.cpu().numpy(), want_plain(a, b, m, k, n))
 
 
+def test_host_pointer_pipeline_blocks_are_exact():
+    """Host-pointer calls of at least 4 Mi cells are cut into blocks whose copies
+    overlap the compute; the bytes are those of the whole call, ragged blocks,
+    padded leading dimensions, gaps in the output and a read C included."""
+    m, k, n = 2304, 272, 2048
+    a, b = i8(31, m * k), i8(32, k * n)
+    c0 = np.zeros(m * n, np.int32)
+    got, want, route = run_both(m, k, n, a, (m, k, k, 1), b, (k, n, n, 1), c0, (m, n, n, 1))
+    assert np.array_equal(got, want)
+    assert route.kernel == 1
+    m, k, n, lda, ldb, ldc = 1100, 160, 4160, 176, 4176, 4170
+    a, b = i8(33, m * lda), i8(34, k * ldb)
+    rng = np.random.default_rng(5)
+    c0 = rng.integers(-(2**62), 2**62, size=m * ldc, dtype=np.int64)
+    for alpha, beta, mode in [(3, -2, U.NEAREST), (2**40, 2**30, U.WRAPPING)]:
+        got, want, route = run_both(m, k, n, a, (m, k, lda, 1), b, (k, n, ldb, 1), c0,
+                                    (m, n, ldc, 1), U.I64, alpha, beta, mode)
+        assert np.array_equal(got, want), (alpha, beta)
+
+
 @pytest.mark.slow
 def test_headline_8192_cubed_checksums_and_samples():
     """At the headline size: Freivalds-style checksums (exact in int64) and sampled

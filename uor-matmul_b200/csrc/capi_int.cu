@@ -48,13 +48,17 @@ int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Opera
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
     const bool dev = device_ptrs(call);
+    const LinearEpi epi{alpha, beta, mode, kind};
+    if (!dev && elem == UOR_B200_I8 && i8_pipeline_applies(A, B, C)) {
+        st = run_i8_gemm_pipelined(ctx, A, B, C, epi, route);
+        if (st != UOR_B200_UNSUPPORTED) return st;
+    }
     const uint8_t *da = nullptr, *db = nullptr;
     OutStage cs;
     if ((st = stage_in(ctx, SLOT_A, A, dev, &da)) != UOR_B200_OK) return st;
     if ((st = stage_in(ctx, SLOT_B, B, dev, &db)) != UOR_B200_OK) return st;
     if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs)) != UOR_B200_OK) return st;
 
-    const LinearEpi epi{alpha, beta, mode, kind};
     if (elem == UOR_B200_I8)
         st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs,
                          reinterpret_cast<const int8_t*>(db), B.rs, B.cs, cs.dev_origin, C.rs,

@@ -238,6 +238,9 @@ void uor_b200_ctx_destroy(uor_b200_ctx* ctx) {
     for (int i = 0; i < 5; ++i)
         if (ctx->buf[i]) cudaFree(ctx->buf[i]);
     if (ctx->d_status) cudaFree(ctx->d_status);
+    for (int i = 0; i < ctx->nevents; ++i) cudaEventDestroy(ctx->events[i]);
+    if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
+    if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     cudaGetLastError();
     cudaSetDevice(prev);

@@ -21,4 +21,12 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
                   ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
                   uor_b200_route* route);
 
+struct Operand;
+
+// Host-pointer i8 GEMM with the copies pipelined against the compute (row-major
+// operands with unit column strides, at least 4 Mi output cells).
+bool i8_pipeline_applies(const Operand& A, const Operand& B, const Operand& C);
+int run_i8_gemm_pipelined(uor_b200_ctx* ctx, const Operand& A, const Operand& B, const Operand& C,
+                          const LinearEpi& epi, uor_b200_route* route);
+
 }  // namespace uor

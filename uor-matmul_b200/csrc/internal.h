@@ -20,6 +20,11 @@ struct uor_b200_ctx {
     // buffer for operands a path rebuilds (decoded codes).
     void* buf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     size_t cap[5] = {0, 0, 0, 0, 0};
+    // Host-pointer pipelining: copy-in and copy-out streams and a pool of events,
+    // created on first use.
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    cudaEvent_t events[256] = {};
+    int nevents = 0;
 };
 
 namespace uor {
