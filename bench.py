@@ -1,17 +1,24 @@
 #!/usr/bin/env python3
-"""bench.py -- the headline exact i8 GEMM at 8192^3 on 1..8 B200s.
+"""bench.py -- exact GEMM throughput on 1..8 B200s.
 
-Workload (the i8 headline): C = A B with A, B int8
-8192 x 8192 drawn from the reference's recorded generator (salts 1 and 2),
+Default workload (the i8 headline): C = A B with A, B
+int8 8192 x 8192 drawn from the reference's recorded generator (salts 1 and 2),
 C exact int32, through slice::gemm::<i8, i32>'s C-ABI twin uor_b200_gemm_i8_i32.
-With N GPUs the output is sharded by column blocks (the reference's Partition
-of C into independent tiles, partition.rs:34): rank r owns an 8192-column block
-of an 8192 x 8192 x (8192 N) product and its own B block; A is replicated. No
-collective runs on the data path, so the scaling is weak.
+With N GPUs the output is sharded by column blocks (the reference's Partition of
+C into independent tiles, partition.rs:34): rank r owns an 8192-column block of
+an 8192 x 8192 x (8192 N) product and its own B block; A is replicated. No
+collective runs on the data path, so the scaling is weak. The default line also
+carries the metric's second half, exact f32 GEMM TFLOPS at 8192^3 (config-3
+operand distribution), measured on the same GPU after the headline.
 
 Metric: exact-i8 TOPS = 2 m k n / t, whole job (all ranks' units / max rank time).
 L2: three rotating operand sets (3 x 128 MiB > the 126 MB L2) plus a 256 MiB
 output written every step, so no step reads operands a previous step left in L2.
+
+--workload selects the other BASELINE configs for their own measurement lines
+(i8-512: configs[0]; codec: configs[1]; f32: configs[2]; wide: configs[3];
+trop: configs[4]'s max-plus half). They are opt-in; the driver's line is the
+default.
 
 --impl reference times the reference's CPU path on the host cores instead (the
 Rust crate cannot be built here, so its C restatement in oracle/ stands in).
@@ -22,10 +29,9 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
+from types import SimpleNamespace
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "uor-matmul_b200"))
@@ -33,6 +39,7 @@ sys.path.insert(0, ROOT)
 
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
+WORKLOADS = ("i8", "i8-512", "codec", "f32", "wide", "trop")
 
 
 def parse():
@@ -41,8 +48,11 @@ def parse():
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--size", type=int, default=SIZE)
+    p.add_argument("--workload", default="i8", choices=WORKLOADS)
+    p.add_argument("--size", type=int, default=None, help="square size of i8 / f32 workloads")
     p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--f32-steps", type=int, default=3,
+                   help="timed steps of the exact f32 8192^3 half of the default line (0 skips)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -105,87 +115,550 @@ class Clocks:
                 "source": "NVML, every 2 ms during the timed region"}
 
 
-def cpu_baseline(size, budget_s=12.0):
-    """The reference's CPU path (C restatement, all host threads) on a row sample."""
+def tensor_peak():
+    """The int8 dense denominator: twice the measured bf16 burst GEMM rate."""
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return (2.0 * peaks["bf16_tflops"],
+                "2x measured bf16 burst (int8 dense issues at twice bf16 on B200), of measured")
+    except Exception:
+        return 2.0 * 1590.0, "2x fallback bf16 1.59 PFLOP/s, of fallback"
+
+
+def load_traffic(name):
+    try:
+        return json.load(open(os.path.join(ROOT, "profiles", name))).get("bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- CPU baseline
+
+def sample_rows(total_rows, run_rows, budget_s):
+    """Time the oracle on a growing leading block of rows until it takes about a
+    quarter of the budget; returns (rows, seconds, output of those rows)."""
+    rows = 1
+    while True:
+        t0 = time.perf_counter()
+        out = run_rows(rows)
+        dt = time.perf_counter() - t0
+        if dt * 4 > budget_s or rows >= total_rows:
+            return rows, dt, out
+        rows = min(total_rows, max(rows * 2, int(rows * budget_s / max(dt, 1e-3) / 4)))
+
+
+# ---------------------------------------------------------------- workloads
+
+def wl_i8(args, U, torch, rank, size, sets=3):
+    """configs[4] headline (size 8192) or configs[0] (size 512): i8 x i8 -> i32."""
+    import numpy as np
+    m = k = n = size
+    A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() for s in range(sets)]
+    B = [torch.from_numpy(U.corpus(2 + 100 * s + 1000 * rank, U.CORPUS_I8, k * n)).cuda()
+         for s in range(sets)]
+    C = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=1)
+
+    def step(i, ctx):
+        U.gemm_i8_i32(m, k, n, A[i % sets], B[i % sets], C, ctx=ctx, route=w.route,
+                      asynchronous=True)
+
+    def check(last):
+        # Freivalds check in f64 on the last warm-up output (every partial < 2^53: exact)
+        x = torch.randint(-1, 2, (n,), device="cuda", dtype=torch.float64)
+        s = last % sets
+        lhs = C.view(m, n).double() @ x
+        rhs = A[s].view(m, k).double() @ (B[s].view(k, n).double() @ x)
+        assert torch.equal(lhs, rhs), "checksum mismatch"
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, b = A[0].cpu().numpy(), B[0].cpu().numpy()
+        threads = orc.max_threads()
+
+        def run(rows):
+            c = np.zeros(rows * n, np.int32)
+            orc.gemm_i8_blocked(a[:rows * k], b, c, rows, k, n, threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        assert np.array_equal(c, C[:rows * n].cpu().numpy()), "GPU rows differ from the oracle"
+        return {"value": 2.0 * rows * k * n / dt / 1e12, "unit": "TOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows of the {m}x{k}x{n} product ({dt:.2f} s), blocked "
+                          "C restatement of gemm_auto's s8 path, OpenMP over rows; the GPU's "
+                          "rows were compared bit for bit"}
+
+    def e2e(steps, ctx, stream):
+        Ah = torch.from_numpy(U.corpus(1, U.CORPUS_I8, m * k)).pin_memory()
+        Bh = torch.from_numpy(U.corpus(2 + 1000 * rank, U.CORPUS_I8, k * n)).pin_memory()
+        Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
+        return timed_host(lambda: U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx), steps, stream,
+                          m * k + k * n, 4 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = METRIC if size == SIZE else f"exact i8 GEMM TOPS at {size}^3 (bit-exact, int32 out)"
+    w.unit, w.dtype = "TOPS", "int8"
+    w.config = {"workload": f"i8 x i8 -> i32 GEMM {m}x{k}x{n} per GPU "
+                            f"({'configs[4] headline' if size == SIZE else 'configs[0]' if size == 512 else 'square'}), "
+                            "column-block sharded",
+                "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = (f"{sets} rotating operand sets ({sets * 2 * m * k >> 20} MiB) + "
+            f"{4 * m * n >> 20} MiB output per step")
+    w.algorithmic_bytes = m * k + k * n + 4 * m * n
+    w.traffic = load_traffic("k1_pair_i8_8192_traffic.json") if size == SIZE else None
+    w.flush = sets * 2 * m * k < (256 << 20)
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        ach = w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src,
+                "frac_of_nominal_4500": ach / 4500.0,
+                "traffic": w.traffic, "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_codec(args, U, torch, rank, sets=3):
+    """A 2048 x 8192 i8, B 8192 x 8192 nibble codes through a 16-entry
+    codebook (Packed<Grid<16>, 2>), exact i32 output."""
+    import numpy as np
+    m, k, n = 2048, 8192, 8192
+    A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() for s in range(sets)]
+    Q = [torch.from_numpy(U.corpus(2 + 100 * s + 1000 * rank, U.CORPUS_NIBBLES, k * n)).cuda()
+         for s in range(sets)]
+    table = torch.from_numpy(U.corpus(7, U.CORPUS_I8, 16)).cuda()
+    C = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=1)
+
+    def step(i, ctx):
+        U.coded_gemm(U.I32, A[i % sets], (m, k, k, 1), Q[i % sets], k, n, 2, table, C,
+                     (m, n, n, 1), ctx=ctx, route=w.route, asynchronous=True)
+
+    def dense(s):
+        q = Q[s].to(torch.int64)
+        codes = torch.stack([q & 15, q >> 4], dim=1).reshape(k, n)
+        return table.to(torch.float64)[codes]
+
+    def check(last):
+        s = last % sets
+        x = torch.randint(-1, 2, (n,), device="cuda", dtype=torch.float64)
+        lhs = C.view(m, n).double() @ x
+        rhs = A[s].view(m, k).double() @ (dense(s) @ x)
+        assert torch.equal(lhs, rhs), "checksum mismatch"
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, q, t = A[0].cpu().numpy(), Q[0].cpu().numpy(), table.cpu().numpy()
+        threads = orc.max_threads()
+
+        def run(rows):
+            c = np.zeros(rows * n, np.int32)
+            orc.coded_gemm(orc.View(a, rows, k, k, 1), q, 2, t, orc.View(c, rows, n, n, 1), k, n,
+                           threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        assert np.array_equal(c, C[:rows * n].cpu().numpy()), "GPU rows differ from the oracle"
+        return {"value": 2.0 * rows * k * n / dt / 1e12, "unit": "TOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), C restatement of coded_gemm "
+                          "(per-MAC decode), OpenMP over rows; the GPU's rows were compared"}
+
+    def e2e(steps, ctx, stream):
+        Ah = A[0].cpu().pin_memory()
+        Qh = Q[0].cpu().pin_memory()
+        Th = table.cpu().pin_memory()
+        Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
+        return timed_host(lambda: U.coded_gemm(U.I32, Ah, (m, k, k, 1), Qh, k, n, 2, Th, Ch,
+                                               (m, n, n, 1), ctx=ctx),
+                          steps, stream, m * k + k * n // 2 + 16, 4 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = "exact codec-tier GEMM TOPS, 2048x8192x8192, 4-bit codes (bit-exact, int32 out)"
+    w.unit, w.dtype = "TOPS", "int8 (decoded nibble codes)"
+    w.config = {"workload": "coded_gemm Packed<Grid<16>,2> 2048x8192x8192 per GPU (configs[1]), "
+                            "column-block sharded", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = f"{sets} rotating operand sets ({sets * (m * k + k * n // 2) >> 20} MiB) + 64 MiB output"
+    w.algorithmic_bytes = m * k + k * n // 2 + 4 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        ach = w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_f32(args, U, torch, rank, size, sets=2):
+    """exact f32 GEMM over the wide-exponent corpus with cancellation columns."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from float_data import config3
+    m = k = n = size
+    host = [config3(m, k, n, salt_a=1 + 100 * s, salt_b=2 + 100 * s + 1000 * rank)
+            for s in range(sets)]
+    A = [torch.from_numpy(h[0]).reshape(-1).cuda() for h in host]
+    B = [torch.from_numpy(h[1]).reshape(-1).cuda() for h in host]
+    C = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    # rows + columns analysis, A and B digit slicing, the slice-pair GEMM, the exact reduce
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=6)
+
+    def step(i, ctx):
+        U.gemm_float(U.F32, U.F32, A[i % sets], (m, k, k, 1), B[i % sets], (k, n, n, 1), C,
+                     (m, n, n, 1), ctx=ctx, route=w.route, asynchronous=True)
+
+    def check(last):
+        # Exactness is checked against the oracle by the CPU leg and the GPU tests; here
+        # only a sanity bound: the once-rounded result is within 2^-20 relative of an f64
+        # product on the rows without cancellation.
+        s = last % sets
+        ref = (A[s].view(m, k).double() @ B[s].view(k, n).double())
+        got = C.view(m, n).double()
+        keep = torch.ones(n, dtype=torch.bool, device="cuda")
+        keep[::10] = False
+        err = ((got - ref).abs() / ref.abs().clamp_min(1e-300))[:, keep]
+        bad = float((err > 2.0 ** -20).double().mean())
+        assert bad < 1e-5, f"f32 result far from the f64 product in {bad:.2e} of the cells"
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, b = host[0]
+        threads = orc.max_threads()
+
+        def run(rows):
+            c = np.zeros(rows * n, np.float32)
+            orc.gemm_float(orc.View(a.reshape(-1), rows, k, k, 1), orc.View(b.reshape(-1), k, n, n, 1),
+                           orc.View(c, rows, n, n, 1), threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        got = C[:rows * n].cpu().numpy()
+        assert np.array_equal(c.view(np.uint32), got.view(np.uint32)), "GPU rows differ"
+        return {"value": 2.0 * rows * k * n / dt / 1e12, "unit": "TFLOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), C restatement of the Complete "
+                          "register accumulation (exact_product), OpenMP over rows; the GPU's "
+                          "rows were compared bit for bit"}
+
+    def e2e(steps, ctx, stream):
+        Ah = torch.from_numpy(host[0][0]).reshape(-1).pin_memory()
+        Bh = torch.from_numpy(host[0][1]).reshape(-1).pin_memory()
+        Ch = torch.empty(m * n, dtype=torch.float32).pin_memory()
+        return timed_host(lambda: U.gemm_float(U.F32, U.F32, Ah, (m, k, k, 1), Bh, (k, n, n, 1),
+                                               Ch, (m, n, n, 1), ctx=ctx),
+                          steps, stream, 8 * m * k, 4 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = f"exact f32 GEMM TFLOPS at {size}^3 (bit-exact, rounded once)"
+    w.unit, w.dtype = "TFLOPS", "f32 in, exact int8 digit slices + integer register"
+    w.config = {"workload": f"gemm_float f32 {m}x{k}x{n} per GPU (configs[2] distribution), "
+                            "column-block sharded", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = f"{sets} rotating operand sets ({sets * 8 * m * k >> 20} MiB) + {4 * m * n >> 20} MiB output"
+    w.algorithmic_bytes = 8 * m * k + 4 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        pairs = max(1, w.route.a_layout * w.route.b_layout)
+        ach = pairs * w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "basis": f"int8 slice-pair ops ({w.route.a_layout} x {w.route.b_layout} digit "
+                         "pairs x 2mnk) over the whole call (analysis, slicing, GEMM, reduce)",
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_wide(args, U, torch, rank):
+    """i32 x i32 full range, 1024 x 65536 x 1024, exact i128 output."""
+    import numpy as np
+    m, k, n = 1024, 65536, 1024
+    A = torch.from_numpy(U.corpus(4, U.CORPUS_I32_FULL, m * k)).cuda()
+    B = torch.from_numpy(U.corpus(5 + 1000 * rank, U.CORPUS_I32_FULL, k * n)).cuda()
+    C = torch.zeros(m * n * 2, dtype=torch.int64, device="cuda")
+    # A and B byte slicing, the limb-pair GEMM, the exact recombination
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=4)
+
+    def step(i, ctx):
+        U.gemm(U.I32, U.I128, A, (m, k, k, 1), B, (k, n, n, 1), C, (m, n, n, 1), ctx=ctx,
+               route=w.route, asynchronous=True)
+
+    def check(last):
+        pass  # sums reach 2^78: checked bit for bit by the CPU leg and the GPU tests
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, b = A.cpu().numpy(), B.cpu().numpy()
+        threads = orc.max_threads()
+
+        def run(rows):
+            c = np.zeros(rows * n * 2, np.int64)
+            orc.gemm_int(orc.View(a, rows, k, k, 1), orc.View(b, k, n, n, 1),
+                         orc.View(c, rows, n, n, 1), out_bits=128, threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        assert np.array_equal(c, C[:rows * n * 2].cpu().numpy()), "GPU rows differ"
+        return {"value": 2.0 * rows * k * n / dt / 1e12, "unit": "TOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), C restatement of the i32 -> i128 "
+                          "exact loop, OpenMP over rows; the GPU's rows were compared"}
+
+    def e2e(steps, ctx, stream):
+        Ah, Bh = A.cpu().pin_memory(), B.cpu().pin_memory()
+        Ch = torch.empty(m * n * 2, dtype=torch.int64).pin_memory()
+        return timed_host(lambda: U.gemm(U.I32, U.I128, Ah, (m, k, k, 1), Bh, (k, n, n, 1), Ch,
+                                         (m, n, n, 1), ctx=ctx),
+                          steps, stream, 4 * (m * k + k * n), 16 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = "exact i32 -> i128 GEMM TOPS, 1024x65536x1024 (bit-exact)"
+    w.unit, w.dtype = "TOPS", "int32 in (4 x 4 int8 limb pairs), int128 out"
+    w.config = {"workload": "i32 x i32 -> i128 GEMM 1024x65536x1024 per GPU (configs[3]), "
+                            "column-block sharded", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = "512 MiB of operands per step (> L2)"
+    w.algorithmic_bytes = 4 * (m * k + k * n) + 16 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        ach = 16 * w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "basis": "int8 limb-pair ops (16 x 2mnk) over the whole call "
+                         "(slicing, GEMM, recombination)",
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_trop(args, U, torch, rank):
+    """configs[4]'s max-plus half: Trop<i8> 8192^3 with 5 % -inf, Trop<i32> output."""
+    import numpy as np
+    m = k = n = 8192
+    A = torch.from_numpy(U.corpus(1, U.CORPUS_TROP_I8, m * k)).cuda()
+    B = torch.from_numpy(U.corpus(2 + 1000 * rank, U.CORPUS_TROP_I8, k * n)).cuda()
+    C = torch.zeros(m * n * 8, dtype=torch.uint8, device="cuda")
+    # A and B packing into i16x2 lanes, the max-plus kernel
+    w = SimpleNamespace(route=U.Route(), units=float(m) * k * n, launches=3)
+
+    def step(i, ctx):
+        U.gemm_tropical(U.TROP_I8, U.TROP_I32, A, (m, k, k, 1), B, (k, n, n, 1), C, (m, n, n, 1),
+                        ctx=ctx, route=w.route, asynchronous=True)
+
+    def check(last):
+        pass  # checked bit for bit on rows by the CPU leg and the GPU tests
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        TD = orc.TROP_DTYPES
+        step(0, ctx)
+        ctx.sync()
+        a, b = A.cpu().numpy().view(TD[8]), B.cpu().numpy().view(TD[8])
+        threads = orc.max_threads()
+
+        def run(rows):
+            c = np.zeros(rows * n, TD[32])
+            orc.gemm_trop(orc.View(a, rows, k, k, 1), orc.View(b, k, n, n, 1),
+                          orc.View(c, rows, n, n, 1), ebits=8, obits=32, threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        got = C[:rows * n * 8].cpu().numpy().view(TD[32])
+        ok = np.array_equal(got["f"], c["f"]) and np.array_equal(
+            np.where(got["f"] != 0, got["v"], 0), np.where(c["f"] != 0, c["v"], 0))
+        assert ok, "GPU rows differ from the oracle"
+        return {"value": float(rows) * k * n / dt / 1e12, "unit": "Tterm/s", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), C restatement of driver::gemm's "
+                          "max-plus loop, OpenMP over rows; the GPU's rows were compared"}
+
+    def e2e(steps, ctx, stream):
+        Ah, Bh = A.cpu().pin_memory(), B.cpu().pin_memory()
+        Ch = torch.empty(m * n * 8, dtype=torch.uint8).pin_memory()
+        return timed_host(lambda: U.gemm_tropical(U.TROP_I8, U.TROP_I32, Ah, (m, k, k, 1), Bh,
+                                                  (k, n, n, 1), Ch, (m, n, n, 1), ctx=ctx),
+                          steps, stream, 2 * (m * k + k * n), 8 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = "exact max-plus GEMM Tterm/s, Trop<i8> 8192^3 (bit-exact, Trop<i32> out)"
+    w.unit, w.dtype = "Tterm/s", "int16x2 packed lanes"
+    w.config = {"workload": "Trop<i8> max-plus 8192x8192x8192 per GPU (configs[4]), "
+                            "column-block sharded", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = "256 MiB of operands + 512 MiB output per step (> L2)"
+    w.algorithmic_bytes = 2 * (m * k + k * n) + 8 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        # one packed 16x2 add and one packed 16x2 max per two terms and lane
+        peak = 148 * 128 * 1.965e9 / 1e12
+        ach = w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "alu", "achieved": ach, "peak": peak, "unit": "Tterm/s",
+                "frac": ach / peak,
+                "peak_source": "nominal: 148 SMs x 128 lanes x 1.965 GHz, one packed i16x2 "
+                               "instruction per lane and clock, 2 instructions per 2 terms",
+                "traffic": None, "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def build_workload(name, args, U, torch, rank):
+    if name == "i8":
+        return wl_i8(args, U, torch, rank, args.size or SIZE)
+    if name == "i8-512":
+        return wl_i8(args, U, torch, rank, args.size or 512, sets=1)
+    if name == "codec":
+        return wl_codec(args, U, torch, rank)
+    if name == "f32":
+        return wl_f32(args, U, torch, rank, args.size or 4096)
+    if name == "wide":
+        return wl_wide(args, U, torch, rank)
+    return wl_trop(args, U, torch, rank)
+
+
+# ---------------------------------------------------------------- timing
+
+def timed_host(call, steps, stream, h2d, d2h):
+    """The public call with pinned HOST buffers: every step copies its inputs in and
+    its result out inside the timed region."""
+    import torch
+    call()  # warm the staging buffers
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return {"ms": e0.elapsed_time(e1) / steps, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h}
+
+
+def time_steps(w, ctx, stream, torch, dist, steps, warmup, local):
+    for i in range(warmup):
+        w.step(i, ctx)
+    assert ctx.sync() == 0
+    w.check(warmup - 1)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if w.flush else None
+    clocks = Clocks(local)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(steps):
+        if flush is not None:
+            flush.fill_(i & 0xFF)  # an L2-sized write between steps, outside the step events
+        ev[i][0].record(stream)
+        w.step(warmup + i, ctx)
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    assert ctx.sync() == 0
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    # With an L2 flush between steps the region holds the flushes too: count the steps.
+    elapsed = sum(step_ms) if flush is not None else t_start.elapsed_time(t_end)
+    if dist:
+        t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    return elapsed, step_ms, clk
+
+
+# ---------------------------------------------------------------- reference arm
+
+def reference_arm(args, rank):
+    """The reference's CPU path for the same workload on the host cores (rank 0)."""
+    if rank != 0:
+        return
     import numpy as np
     import uor_b200 as U
     from oracle import oracle as orc
-
+    size = args.size or SIZE
     k = n = size
     b = U.corpus(2, U.CORPUS_I8, k * n)
     threads = orc.max_threads()
-    rows = 8
-    while True:
-        a = U.corpus(1, U.CORPUS_I8, rows * k)
-        c = np.zeros(rows * n, np.int32)
-        t0 = time.perf_counter()
-        orc.gemm_i8_blocked(a, b, c, rows, k, n, threads=threads)
-        dt = time.perf_counter() - t0
-        if dt * 4 > budget_s or rows >= size:
-            break
-        rows = min(size, max(rows * 2, int(rows * budget_s / max(dt, 1e-3) / 2)))
-    tops = 2.0 * rows * k * n / dt / 1e12
-    return {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {size} rows of the {size}^3 product ({dt:.2f} s), "
-                      "blocked C restatement of gemm_auto's s8 path, OpenMP over rows"}
+    a = U.corpus(1, U.CORPUS_I8, size * k)
 
-
-def reference_arm(args, rank):
-    if rank != 0:
-        return
+    def run(r):
+        c = np.zeros(r * n, np.int32)
+        orc.gemm_i8_blocked(a[:r * k], b, c, r, k, n, threads=threads)
+        return c
+    # One bounded sample per step, sized so the whole run stays near two minutes.
+    per_step = max(0.2, min(3.0, 120.0 / (args.warmup + args.steps)))
+    rows, dt, _ = sample_rows(size, run, 4 * per_step)
     steps = []
-    base = None
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(args.size, budget_s=4.0 if i < args.warmup else 8.0)
+        t0 = time.perf_counter()
+        run(rows)
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
-            steps.append(r["value"])
-        base = r
+            steps.append(2.0 * rows * k * n / dt / 1e12)
     v = statistics.median(steps)
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "TOPS",
+    base = {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {size} rows of the {size}^3 product per step ({dt:.2f} s), "
+                      "blocked C restatement of gemm_auto's s8 path, OpenMP over rows"}
+    line = {"impl": "reference", "metric": METRIC if size == SIZE else
+            f"exact i8 GEMM TOPS at {size}^3 (bit-exact, int32 out)", "value": v, "unit": "TOPS",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (reference xorshift corpus, salts 1/2)",
-            "config": {"workload": f"i8 x i8 -> i32 GEMM {args.size}^3 (configs[4] headline)",
-                       "m": args.size, "k": args.size, "n": args.size},
-            "cpu_baseline": dict(base, value=v),
+            "config": {"workload": f"i8 x i8 -> i32 GEMM {size}^3 (configs[4] headline)",
+                       "m": size, "k": size, "n": size},
+            "cpu_baseline": base,
             "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def load_traffic():
-    path = os.path.join(ROOT, "profiles", "k1_i8_8192_traffic.json")
-    try:
-        return json.load(open(path))
-    except Exception:
-        return None
+# ---------------------------------------------------------------- main
 
-
-def run_e2e(args, U, torch, dist, ctx, stream, m, k, n, rank, world):
-    """The same product through the public call with pinned HOST buffers: every
-    step copies A and B in and C out inside the timed region."""
-    ops_per_step = 2.0 * m * k * n
-    Ah = torch.from_numpy(U.corpus(1, U.CORPUS_I8, m * k)).pin_memory()
-    Bh = torch.from_numpy(U.corpus(2 + 1000 * rank, U.CORPUS_I8, k * n)).pin_memory()
-    Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
-    U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx)  # warm the staging buffers
-    if dist:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    return {"value": world * args.e2e_steps * ops_per_step / (e2e_ms / 1e3) / 1e12,
-            "unit": "TOPS", "h2d_bytes_per_step": m * k + k * n, "d2h_bytes_per_step": 4 * m * n,
-            "ms_per_step": e2e_ms / args.e2e_steps}
+def measure(w, args, U, torch, dist, ctx, stream, rank, world, local):
+    elapsed, step_ms, clk = time_steps(w, ctx, stream, torch, dist, args.steps, args.warmup,
+                                       local)
+    value = world * args.steps * w.units / (elapsed / 1e3) / 1e12
+    line = {
+        "metric": w.metric, "value": value, "unit": w.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+        "data": "synthetic (reference xorshift corpus)",
+        "config": dict(w.config, n_total=w.config["n_per_gpu"] * world, l2=w.l2,
+                       parallelism=f"column blocks x{world}, no data-path collective"),
+        "route": w.route.as_dict(),
+        "roofline": w.roofline(statistics.mean(step_ms)),
+        "gpu_launches": w.launches * args.steps,
+        "clocks": clk,
+    }
+    if args.e2e_steps > 0:
+        if dist:
+            dist.barrier()
+        r = w.e2e(args.e2e_steps, ctx, stream)
+        ms = r.pop("ms")
+        if dist:
+            t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        line["e2e"] = dict(value=world * w.units / (ms / 1e3) / 1e12, unit=w.unit,
+                           ms_per_step=ms, **r)
+    else:
+        line["e2e"] = None
+    return line
 
 
 def main():
@@ -195,7 +668,6 @@ def main():
         reference_arm(args, rank)
         return
 
-    import numpy as np
     import torch
     import uor_b200 as U
 
@@ -206,104 +678,30 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=datetime.timedelta(seconds=180))
-    m = k = n = args.size
-    sets = 3
-    A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() for s in range(sets)]
-    B = [torch.from_numpy(U.corpus(2 + 100 * s + 1000 * rank, U.CORPUS_I8, k * n)).cuda()
-         for s in range(sets)]
-    C = torch.empty(m * n, dtype=torch.int32, device="cuda")
     ctx = U.Context(local)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
-    route = U.Route()
 
-    def step(i):
-        U.gemm_i8_i32(m, k, n, A[i % sets], B[i % sets], C, ctx=ctx, route=route,
-                      asynchronous=True)
-
-    for i in range(args.warmup):
-        step(i)
-    assert ctx.sync() == U.OK
-    # correctness gate on the last warm-up output: Freivalds check in f64 (exact here)
-    x = torch.randint(-1, 2, (n,), device="cuda", dtype=torch.float64)
-    s = (args.warmup - 1) % sets
-    lhs = C.view(m, n).double() @ x
-    rhs = A[s].view(m, k).double() @ (B[s].view(k, n).double() @ x)
-    assert torch.equal(lhs, rhs), "checksum mismatch"
-
-    clocks = Clocks(local)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks.start()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for i in range(args.steps):
-        ev[i][0].record(stream)
-        step(args.warmup + i)
-        ev[i][1].record(stream)
-    t_end.record(stream)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    clk = clocks.stop()
-    assert ctx.sync() == U.OK
-    elapsed_ms = t_start.elapsed_time(t_end)
-    kernel_ms = [a.elapsed_time(b) for a, b in ev]
-    if dist:
-        t = torch.tensor([elapsed_ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    ops_per_step = 2.0 * m * k * n
-    value = world * args.steps * ops_per_step / (elapsed_ms / 1e3) / 1e12
-    ms_per_step = elapsed_ms / args.steps
-
-    # ---- end to end through the C ABI with pinned host buffers
-    e2e = None
-    if args.e2e_steps > 0:
-        e2e = run_e2e(args, U, torch, dist, ctx, stream, m, k, n, rank, world)
-    del A, B, C
-
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except Exception:
-        pass
-    if "bf16_tflops" in peaks:
-        peak = 2.0 * peaks["bf16_tflops"]
-        peak_src = "2x measured bf16 burst (int8 dense issues at twice bf16 on B200), of measured"
-    else:
-        peak = 2.0 * 1590.0
-        peak_src = "2x fallback bf16 1.59 PFLOP/s, of fallback"
-    avg_kernel_ms = statistics.mean(kernel_ms)
-    achieved = ops_per_step / (avg_kernel_ms / 1e3) / 1e12
-    traffic = load_traffic()
-
-    line = {
-        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic (reference xorshift corpus)",
-        "config": {"workload": f"i8 x i8 -> i32 GEMM {m}x{k}x{n} per GPU (configs[4] headline), "
-                               "column-block sharded",
-                   "m": m, "k": k, "n_per_gpu": n, "n_total": n * world,
-                   "l2": "3 rotating operand sets (384 MiB) + 256 MiB output per step",
-                   "parallelism": f"column blocks x{world}, no data-path collective"},
-        "route": route.as_dict(),
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOPS",
-                     "frac": achieved / peak, "peak_source": peak_src,
-                     "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                     "algorithmic_bytes": m * k + k * n + 4 * m * n},
-        "e2e": e2e,
-        "gpu_launches": args.steps,
-        "clocks": clk,
-    }
+    w = build_workload(args.workload, args, U, torch, rank)
+    line = measure(w, args, U, torch, dist, ctx, stream, rank, world, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.size)
+        line["cpu_baseline"] = w.cpu(12.0, ctx)
+    del w
+    torch.cuda.empty_cache()
+
+    # The metric's second half: exact f32 GEMM at 8192^3, on every rank's own columns.
+    if args.workload == "i8" and args.f32_steps > 0 and (args.size or SIZE) == SIZE:
+        f = wl_f32(args, U, torch, rank, SIZE, sets=1)
+        sub = argparse.Namespace(**vars(args))
+        sub.steps, sub.warmup, sub.e2e_steps = args.f32_steps, max(3, min(args.warmup, 3)), 0
+        fl = measure(f, sub, U, torch, dist, ctx, stream, rank, world, local)
+        line["f32_exact_8192"] = {k2: fl[k2] for k2 in ("metric", "value", "unit", "ms_per_step",
+                                                        "steps", "warmup", "route", "roofline",
+                                                        "gpu_launches", "clocks")}
+        line["f32_exact_8192"]["config"] = fl["config"]
+        del f
+
     ctx.close()
     if dist:
         dist.barrier()

@@ -215,11 +215,12 @@ def _on_device(*bufs):
 
 # ------------------------------------------------------------------ integer
 
-def gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None, route=None):
+def gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None, route=None,
+         asynchronous=False):
     """uor_matmul::gemm over views: av/bv/cv are (rows, cols, rs, cs) tuples over buffers a/b/c."""
     dev = _on_device(a, b, c)
     A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
-    call = make_call(encode, dev, ctx, route)
+    call = make_call(encode, dev, ctx, route, asynchronous)
     _check(lib().uor_b200_gemm(elem, out, ctypes.byref(A), ctypes.byref(B), ctypes.byref(C),
                                alpha, beta, ctypes.byref(call)), "gemm")
 
@@ -259,10 +260,10 @@ def gemm_i8_i32(m, k, n, a, b, c, ctx=None, route=None, asynchronous=False):
 # ------------------------------------------------------------------ float
 
 def gemm_float(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None,
-               route=None):
+               route=None, asynchronous=False):
     dev = _on_device(a, b, c)
     A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
-    call = make_call(encode, dev, ctx, route)
+    call = make_call(encode, dev, ctx, route, asynchronous)
     _check(lib().uor_b200_gemm_float(elem, out, ctypes.byref(A), ctypes.byref(B),
                                      ctypes.byref(C), alpha, beta, ctypes.byref(call)),
            "gemm_float")
@@ -304,11 +305,11 @@ def dgemm(m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc, csc, origin=(0
 # ------------------------------------------------------------------ tropical
 
 def gemm_tropical(elem, out, a, av, b, bv, c, cv, alpha=(0, True), beta=(0, False),
-                  encode=NEAREST, ctx=None, route=None):
+                  encode=NEAREST, ctx=None, route=None, asynchronous=False):
     """driver::gemm over Trop<E> with MaxPlus{alpha, beta}; scalars are (value, finite)."""
     dev = _on_device(a, b, c)
     A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
-    call = make_call(encode, dev, ctx, route)
+    call = make_call(encode, dev, ctx, route, asynchronous)
     _check(lib().uor_b200_gemm_tropical(elem, out, ctypes.byref(A), ctypes.byref(B),
                                         ctypes.byref(C), Trop(alpha[0], int(alpha[1])),
                                         Trop(beta[0], int(beta[1])), ctypes.byref(call)),
@@ -318,13 +319,13 @@ def gemm_tropical(elem, out, a, av, b, bv, c, cv, alpha=(0, True), beta=(0, Fals
 # ------------------------------------------------------------------ codec
 
 def coded_gemm(out, a, av, codes, k, n, per_byte, table, c, cv, alpha=1, beta=0,
-               encode=NEAREST, ctx=None, route=None, tabulated=False):
+               encode=NEAREST, ctx=None, route=None, tabulated=False, asynchronous=False):
     """coded_gemm (k x n codes) or, with tabulated=True, gemm_tabulated's A W^T (n x k codes)."""
     dev = _on_device(a, codes, table, c)
     A, C = view(a, *av), view(c, *cv)
     pc, lc, _ = _buffer(codes)
     pt, lt, _ = _buffer(table)
-    call = make_call(encode, dev, ctx, route)
+    call = make_call(encode, dev, ctx, route, asynchronous)
     fn = lib().uor_b200_tabulated_gemm if tabulated else lib().uor_b200_coded_gemm
     _check(fn(out, ctypes.byref(A), pc, lc, k, n, per_byte, pt, lt, ctypes.byref(C), alpha, beta,
               ctypes.byref(call)), "coded_gemm")
