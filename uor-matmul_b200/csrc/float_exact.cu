@@ -275,6 +275,87 @@ __device__ uint64_t encode_words(const uint64_t (&Win)[NW], int unit_exp, bool o
     return s | sig;
 }
 
+// Register-resident helpers for a short magnitude (NW words, every index resolved by
+// unrolled selects, so nothing spills to local memory).
+template <int NW>
+__device__ __forceinline__ uint64_t reg_word(const uint64_t (&m)[NW], int i) {
+    uint64_t r = 0;
+#pragma unroll
+    for (int q = 0; q < NW; ++q) r = q == i ? m[q] : r;
+    return r;
+}
+template <int NW>
+__device__ __forceinline__ int reg_bitlen(const uint64_t (&m)[NW]) {
+    int bl = 0;
+#pragma unroll
+    for (int q = 0; q < NW; ++q)
+        if (m[q]) bl = 64 * q + 64 - __clzll(static_cast<long long>(m[q]));
+    return bl;
+}
+// bits [pos, pos + 64) of the magnitude; positions below 0 read as zero (pos > -64).
+template <int NW>
+__device__ __forceinline__ uint64_t reg_window(const uint64_t (&m)[NW], int pos) {
+    if (pos < 0) return m[0] << (-pos);
+    const int wi = pos >> 6, b = pos & 63;
+    const uint64_t lo = reg_word(m, wi);
+    return b ? (lo >> b) | (reg_word(m, wi + 1) << (64 - b)) : lo;
+}
+template <int NW>
+__device__ __forceinline__ bool reg_any_below(const uint64_t (&m)[NW], int pos) {
+    uint64_t acc = 0;
+#pragma unroll
+    for (int q = 0; q < NW; ++q) {
+        if (64 * q + 64 <= pos) acc |= m[q];
+        else if (64 * q < pos) acc |= m[q] & ((1ull << (pos - 64 * q)) - 1);
+    }
+    return acc != 0;
+}
+
+// encode_words for a magnitude held in registers with its sign: the same rounding
+// steps (acc.rs:1734-1868), the significand and round bit read as one 64-bit window.
+template <int NW>
+__device__ uint64_t encode_mag_fast(const uint64_t (&mag)[NW], bool neg, int unit_exp, bool out64,
+                                    int mode, int min_exp_e) {
+    const int MANT = out64 ? 52 : 23, EXPO = out64 ? 11 : 8;
+    const int P = MANT + 1;
+    const int BIAS = (1 << (EXPO - 1)) - 1;
+    const int SUB = 1 - BIAS - MANT;
+    const uint64_t sign_bit = out64 ? (1ull << 63) : (1ull << 31);
+    const uint64_t exp_all = (1ull << EXPO) - 1;
+    const int bl = reg_bitlen(mag);
+    if (bl == 0) return 0;  // exact zero encodes +0
+    const int exp = unit_exp + bl - 1;
+    int lsb_exp = exp - (P - 1) < SUB ? SUB : exp - (P - 1);
+    if (lsb_exp - min_exp_e < 0) return 0;
+    const int lsb = lsb_exp - unit_exp;  // >= bl - P > -64
+    const uint64_t win = reg_window(mag, lsb - 1);
+    uint64_t sig = (win >> 1) & ((1ull << P) - 1);
+    bool round_bit = false, sticky = false;
+    if (lsb_exp - min_exp_e != 0) {
+        round_bit = (win & 1) != 0;
+        sticky = reg_any_below(mag, lsb - 1);
+    }
+    const bool inc = mode == MODE_NEAREST && round_bit && (sticky || (sig & 1));
+    sig += inc ? 1 : 0;
+    if (sig >> P) {
+        sig >>= 1;
+        lsb_exp += 1;
+    }
+    const uint64_t s = neg ? sign_bit : 0;
+    if (sig == 0) return s;
+    const int top = 63 - __clzll(static_cast<long long>(sig));
+    const int value_exp = lsb_exp + top;
+    if ((sig >> (P - 1)) == 1) {
+        const int biased = value_exp + BIAS;
+        if (biased >= static_cast<int>(exp_all)) {
+            if (mode == MODE_NEAREST) return s | (exp_all << MANT);
+            return s | ((exp_all - 1) << MANT) | ((1ull << MANT) - 1);
+        }
+        return s | (static_cast<uint64_t>(biased) << MANT) | (sig & ((1ull << MANT) - 1));
+    }
+    return s | sig;
+}
+
 __device__ __forceinline__ uint64_t nan_bits(bool out64) {
     return out64 ? 0x7FF8000000000000ull : 0x7FC00000ull;
 }
@@ -420,27 +501,42 @@ __global__ void fx_rows_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64
     }
 }
 
-// One thread per column of B.
+// 32 columns of B per block of 32 x 32 threads: lane x owns column j0 + x, warp y
+// walks rows y, y + 32, ...; the warps' results meet in shared memory.
 __global__ void fx_cols_kernel(const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, int k,
                                int n, bool f64, int* __restrict__ lo, uint8_t* __restrict__ nf,
                                int* __restrict__ gmax) {
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= n) return;
+    __shared__ int sl[32][33], sh[32][33], sf[32][33];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int j = blockIdx.x * 32 + tx;
     int l = INT_MAX, h = INT_MIN, f = 0;
-    for (int p = 0; p < k; ++p) {
-        const FDec d = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64);
-        if (d.kind != 0) f = 1;
-        else if (d.mant) {
-            const int tz = __ffsll(static_cast<long long>(d.mant)) - 1;
-            const int bl = 64 - __clzll(static_cast<long long>(d.mant));
-            l = min(l, d.exp + tz);
-            h = max(h, d.exp + bl - 1);
+    if (j < n) {
+        for (int p = ty; p < k; p += 32) {
+            const FDec d = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64);
+            if (d.kind != 0) f = 1;
+            else if (d.mant) {
+                const int tz = __ffsll(static_cast<long long>(d.mant)) - 1;
+                const int bl = 64 - __clzll(static_cast<long long>(d.mant));
+                l = min(l, d.exp + tz);
+                h = max(h, d.exp + bl - 1);
+            }
         }
     }
-    lo[j] = l == INT_MAX ? 0 : l;
-    nf[j] = static_cast<uint8_t>(f);
-    if (l != INT_MAX) atomicMax(&gmax[1], h - l + 1);
-    if (f) atomicOr(&gmax[2], 1);
+    sl[ty][tx] = l;
+    sh[ty][tx] = h;
+    sf[ty][tx] = f;
+    __syncthreads();
+    if (ty == 0 && j < n) {
+        for (int r = 1; r < 32; ++r) {
+            l = min(l, sl[r][tx]);
+            h = max(h, sh[r][tx]);
+            f |= sf[r][tx];
+        }
+        lo[j] = l == INT_MAX ? 0 : l;
+        nf[j] = static_cast<uint8_t>(f);
+        if (l != INT_MAX) atomicMax(&gmax[1], h - l + 1);
+        if (f) atomicOr(&gmax[2], 1);
+    }
 }
 
 // Balanced base-256 digits of the exact scaled integer of one element.
@@ -522,6 +618,64 @@ __global__ void fx_flags_kernel(const uint8_t* __restrict__ a, int64_t rsa, int6
 
 // ------------------------------------------------------------ K7 reduce
 
+// The common cell (beta 0, finite terms): the partials are summed as
+// sum_g s_g 2^(8 g) in 128-bit column sums per 64-bit word (chunk by chunk, every
+// load of a chunk issued before any is used), carried into NG / 8 + 2 words, scaled
+// by alpha and encoded, all in registers. The product needs no window: it is encoded
+// at its own scale, exactly as the windowed path would encode it.
+template <int NG>
+__device__ __forceinline__ void fx_reduce_fast(const int32_t* __restrict__ part, int chunks,
+                                               int groups, size_t total, size_t idx, int ex,
+                                               int64_t off, const FxEpi& e) {
+    constexpr int NQ = (NG + 7) / 8;
+    i128 col[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) col[q] = 0;
+    for (int q = 0; q < chunks; ++q) {
+        const int32_t* pq = part + static_cast<size_t>(q) * groups * total + idx;
+        int32_t v[NG];
+#pragma unroll
+        for (int g = 0; g < NG; ++g) v[g] = g < groups ? __ldg(pq + g * total) : 0;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) col[g >> 3] += static_cast<i128>(v[g]) << (8 * (g & 7));
+    }
+    uint64_t w[NQ + 2];
+    i128 carry = 0;
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+        const i128 t = col[q] + carry;
+        w[q] = static_cast<uint64_t>(static_cast<u128>(t));
+        carry = t >> 64;
+    }
+    w[NQ] = static_cast<uint64_t>(static_cast<u128>(carry));
+    w[NQ + 1] = carry < 0 ? ~0ull : 0ull;
+    bool neg = (w[NQ + 1] >> 63) != 0;
+    if (neg) {
+        uint64_t c = 1;
+#pragma unroll
+        for (int q = 0; q < NQ + 2; ++q) {
+            const uint64_t sv = ~w[q] + c;
+            c = (c && sv == 0) ? 1 : 0;
+            w[q] = sv;
+        }
+    }
+    if (e.alpha != 1) {
+        // alpha 0 encodes +0 (Complete::scale by 0 of a finite value).
+        const uint64_t uf = e.alpha < 0 ? 0ull - static_cast<uint64_t>(e.alpha)
+                                        : static_cast<uint64_t>(e.alpha);
+        uint64_t c = 0;
+#pragma unroll
+        for (int q = 0; q < NQ + 2; ++q) {
+            const u128 pr = static_cast<u128>(w[q]) * uf + c;
+            w[q] = static_cast<uint64_t>(pr);
+            c = static_cast<uint64_t>(pr >> 64);
+        }
+        neg = neg != (e.alpha < 0);
+    }
+    store_float(e.c, e.out64, off, encode_mag_fast<NQ + 2>(w, neg, ex, e.out64, e.mode, e.min_exp_e));
+}
+
+template <int NG>
 __global__ void fx_reduce_kernel(const int32_t* __restrict__ part, int chunks, int groups, int m,
                                  int n, const int* __restrict__ rlo, const int* __restrict__ clo,
                                  const uint8_t* __restrict__ flags, FxEpi e) {
@@ -529,6 +683,11 @@ __global__ void fx_reduce_kernel(const int32_t* __restrict__ part, int chunks, i
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+        if (e.beta == 0 && !(flags && flags[idx])) {
+            const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+            fx_reduce_fast<NG>(part, chunks, groups, total, idx, rlo[i] + clo[j], off, e);
+            continue;
+        }
         Big X;
         big_zero(X);
         for (int g = 0; g < groups; ++g) {
@@ -719,7 +878,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
     if (k > 0) {
         fx_rows_kernel<<<(int)((m * 32 + 255) / 256), 256, 0, s>>>(a, rsa, csa, (int)m, (int)k, e64,
                                                                    rlo, rnf, gmax);
-        fx_cols_kernel<<<(int)((n + 127) / 128), 128, 0, s>>>(b, rsb, csb, (int)k, (int)n, e64, clo,
+        fx_cols_kernel<<<(int)((n + 31) / 32), dim3(32, 32), 0, s>>>(b, rsb, csb, (int)k, (int)n, e64, clo,
                                                               cnf, gmax);
     } else {
         cudaMemsetAsync(rlo, 0, m * 4, s);
@@ -828,8 +987,16 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
     }
     const size_t total = m * n;
     const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-    fx_reduce_kernel<<<rgrid, 256, 0, s>>>(part, run_mma ? p.num_chunks : 0, run_mma ? ngroups : 0,
-                                           (int)m, (int)n, rlo, clo, flags, e);
+    const int rchunks = run_mma ? p.num_chunks : 0, rgroups = run_mma ? ngroups : 0;
+    // Groups are at most 2 * FX_MAX_DIGITS - 1 = 31.
+    if (rgroups <= 8)
+        fx_reduce_kernel<8><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+    else if (rgroups <= 16)
+        fx_reduce_kernel<16><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+    else if (rgroups <= 24)
+        fx_reduce_kernel<24><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+    else
+        fx_reduce_kernel<32><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
     return cuda_status(cudaGetLastError());
 }
 

@@ -23,50 +23,104 @@ namespace uor {
 
 // ------------------------------------------------------------ slicing kernels
 
-// A (m x k, eb-byte elements, strided view) -> As[L][mp][kp], byte s of each element.
-__global__ void slice_a_kernel(uint8_t* __restrict__ as, int L, int mp, int kp,
-                               const uint8_t* __restrict__ a, int64_t rsa, int64_t csa, int eb,
-                               int m, int k) {
-    const int64_t total = static_cast<int64_t>(mp) * kp;
-    const int64_t plane = total;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(idx / kp), p = static_cast<int>(idx % kp);
-        uint64_t v = 0;
-        if (i < m && p < k) {
-            const uint8_t* e = a + (static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa) * eb;
-            for (int s = 0; s < eb; ++s) v |= static_cast<uint64_t>(e[s]) << (8 * s);
+// One eb-byte little-endian element; `aligned` when the buffer is aligned to eb.
+template <int EB>
+__device__ __forceinline__ uint64_t load_elem(const uint8_t* __restrict__ base, int64_t idx,
+                                              bool aligned) {
+    const uint8_t* e = base + idx * EB;
+    if (aligned) {
+        if (EB == 2) return *reinterpret_cast<const uint16_t*>(e);
+        if (EB == 4) return *reinterpret_cast<const uint32_t*>(e);
+        if (EB == 8) return *reinterpret_cast<const uint64_t*>(e);
+    }
+    uint64_t v = 0;
+#pragma unroll
+    for (int s = 0; s < EB; ++s) v |= static_cast<uint64_t>(e[s]) << (8 * s);
+    return v;
+}
+
+// Byte s of four elements, packed little-endian into one word.
+__device__ __forceinline__ uint32_t pack_byte(const uint64_t (&v)[4], int s) {
+    return static_cast<uint32_t>((v[0] >> (8 * s)) & 255) |
+           static_cast<uint32_t>((v[1] >> (8 * s)) & 255) << 8 |
+           static_cast<uint32_t>((v[2] >> (8 * s)) & 255) << 16 |
+           static_cast<uint32_t>((v[3] >> (8 * s)) & 255) << 24;
+}
+
+// A (m x k, EB-byte elements, strided view) -> As[EB][mp][kp], byte s of each element;
+// four consecutive reduction positions per thread, one 4-byte store per slice.
+template <int EB>
+__global__ void slice_a_kernel(uint8_t* __restrict__ as, int mp, int kp,
+                               const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
+                               bool aligned, int m, int k) {
+    const int qpr = kp >> 2;
+    const int64_t total = static_cast<int64_t>(mp) * qpr;
+    const int64_t plane = static_cast<int64_t>(mp) * kp;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(t / qpr);
+        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+        uint64_t v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int p = p0 + c;
+            v[c] = (i < m && p < k) ? load_elem<EB>(a, static_cast<int64_t>(i) * rsa +
+                                                           static_cast<int64_t>(p) * csa, aligned)
+                                    : 0;
         }
-        for (int s = 0; s < L; ++s) as[s * plane + idx] = static_cast<uint8_t>(v >> (8 * s));
+        uint8_t* dst = as + static_cast<int64_t>(i) * kp + p0;
+#pragma unroll
+        for (int s = 0; s < EB; ++s) *reinterpret_cast<uint32_t*>(dst + s * plane) = pack_byte(v, s);
     }
 }
 
-// B (k x n, strided view) -> Bs[L][np][kp] (transposed), through a 32 x 32 shared tile.
-__global__ void slice_b_kernel(uint8_t* __restrict__ bs, int L, int np, int kp,
-                               const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, int eb,
-                               int k, int n) {
-    __shared__ uint64_t tile[32][33];
-    const int p0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+// B (k x n, strided view) -> Bs[EB][np][kp] (transposed) through a shared tile of 128
+// reduction positions x 32 columns: loads run along B's rows, stores along the slices'.
+template <int EB>
+__global__ void slice_b_kernel(uint8_t* __restrict__ bs, int np, int kp,
+                               const uint8_t* __restrict__ b, int64_t rsb, int64_t csb,
+                               bool aligned, int k, int n) {
+    __shared__ uint64_t tile[32][129];
+    const int j0 = blockIdx.x * 32;
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
-    for (int r = ty; r < 32; r += 8) {
-        const int p = p0 + r, j = j0 + tx;
-        uint64_t v = 0;
-        if (p < k && j < n) {
-            const uint8_t* e = b + (static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb) * eb;
-            for (int s = 0; s < eb; ++s) v |= static_cast<uint64_t>(e[s]) << (8 * s);
-        }
-        tile[r][tx] = v;
-    }
-    __syncthreads();
     const int64_t plane = static_cast<int64_t>(np) * kp;
-    for (int r = ty; r < 32; r += 8) {
-        const int j = j0 + r, p = p0 + tx;
-        if (j < np && p < kp) {
-            const uint64_t v = tile[tx][r];
-            for (int s = 0; s < L; ++s)
-                bs[s * plane + static_cast<int64_t>(j) * kp + p] = static_cast<uint8_t>(v >> (8 * s));
+    for (int p0 = blockIdx.y * 128; p0 < kp; p0 += gridDim.y * 128) {
+        for (int r = ty; r < 128; r += 8) {
+            const int p = p0 + r, j = j0 + tx;
+            tile[tx][r] = (p < k && j < n) ? load_elem<EB>(b, static_cast<int64_t>(p) * rsb +
+                                                                  static_cast<int64_t>(j) * csb,
+                                                           aligned)
+                                           : 0;
         }
+        __syncthreads();
+        const int p = p0 + 4 * tx;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int jj = ty * 4 + q, j = j0 + jj;
+            if (j < np && p < kp) {
+                const uint64_t v[4] = {tile[jj][4 * tx], tile[jj][4 * tx + 1], tile[jj][4 * tx + 2],
+                                       tile[jj][4 * tx + 3]};
+                uint8_t* dst = bs + static_cast<int64_t>(j) * kp + p;
+#pragma unroll
+                for (int s = 0; s < EB; ++s)
+                    *reinterpret_cast<uint32_t*>(dst + s * plane) = pack_byte(v, s);
+            }
+        }
+        __syncthreads();
     }
+}
+
+template <int EB>
+static void launch_slicing(uint8_t* as, uint8_t* bs, int mp, int np, int kp, const uint8_t* a,
+                           int64_t rsa, int64_t csa, const uint8_t* b, int64_t rsb, int64_t csb,
+                           int m, int k, int n, cudaStream_t s) {
+    const int64_t quads = static_cast<int64_t>(mp) * (kp / 4);
+    const int grid = static_cast<int>(quads / 256 + 1 < 148 * 16 ? quads / 256 + 1 : 148 * 16);
+    slice_a_kernel<EB><<<grid, 256, 0, s>>>(as, mp, kp, a, rsa, csa,
+                                            reinterpret_cast<uintptr_t>(a) % EB == 0, m, k);
+    const int gy = (kp + 127) / 128 < 65535 ? (kp + 127) / 128 : 65535;
+    slice_b_kernel<EB><<<dim3(np / 32, gy), dim3(32, 8), 0, s>>>(
+        bs, np, kp, b, rsb, csb, reinterpret_cast<uintptr_t>(b) % EB == 0, k, n);
 }
 
 // ------------------------------------------------------------ exact recombination
@@ -94,28 +148,6 @@ __device__ __forceinline__ L3 l3_of(i128 v) {
     r.w[1] = static_cast<uint64_t>(static_cast<u128>(v) >> 64);
     r.w[2] = v < 0 ? ~0ull : 0ull;
     return r;
-}
-
-// v * 2^sh, two's complement modulo 2^192, for 0 <= sh < 192.
-__device__ __forceinline__ L3 l3_shifted(int64_t v, int sh) {
-    const uint64_t x0 = static_cast<uint64_t>(v), ext = v < 0 ? ~0ull : 0ull;
-    L3 y;
-    if (sh >= 128) {
-        y.w[0] = 0;
-        y.w[1] = 0;
-        y.w[2] = x0 << (sh - 128);
-    } else if (sh >= 64) {
-        const int s = sh - 64;
-        y.w[0] = 0;
-        y.w[1] = x0 << s;
-        y.w[2] = s ? (ext << s) | (x0 >> (64 - s)) : ext;
-    } else {
-        const int s = sh;
-        y.w[0] = x0 << s;
-        y.w[1] = s ? (ext << s) | (x0 >> (64 - s)) : ext;
-        y.w[2] = s ? (ext << s) | (ext >> (64 - s)) : ext;
-    }
-    return y;
 }
 
 __device__ __forceinline__ L3 l3_neg(L3 x) {
@@ -165,22 +197,44 @@ struct WideEpi {
     int limbs3;  // 1: i64 elements (Limbs<3> accumulator); 0: i16/i32 (i128 accumulator)
 };
 
-// Group g is the diagonal d = g, weighted 2^(8 g).
+// Group g is the diagonal d = g, weighted 2^(8 g). The partials of a cell are summed
+// in 128-bit column sums per 64-bit word (chunk by chunk, every load of a chunk issued
+// before any is used) and carried into 192-bit two's complement.
+template <int NG>
 __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks, int groups,
                                    size_t m, size_t n, void* c, int64_t rsc, int64_t csc,
                                    WideEpi e) {
+    constexpr int NQ = (NG + 7) / 8;
+    static_assert(NQ <= 2, "at most 16 diagonals");
     const size_t total = m * n;
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        L3 acc = {{0, 0, 0}};
-        for (int q = 0; q < chunks; ++q)
-            for (int g = 0; g < groups; ++g) {
-                const int32_t v = part[(static_cast<size_t>(q) * groups + g) * total + idx];
-                if (v) {
-                    const L3 t = l3_shifted(v, 8 * g);
-                    l3_add(acc, t);
-                }
+        i128 col[NQ];
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) col[q] = 0;
+        for (int q = 0; q < chunks; ++q) {
+            const int32_t* pq = part + static_cast<size_t>(q) * groups * total + idx;
+            int32_t v[NG];
+#pragma unroll
+            for (int g = 0; g < NG; ++g) v[g] = g < groups ? __ldg(pq + g * total) : 0;
+#pragma unroll
+            for (int g = 0; g < NG; ++g) col[g >> 3] += static_cast<i128>(v[g]) << (8 * (g & 7));
+        }
+        L3 acc;
+        {
+            const i128 t0 = col[0];
+            acc.w[0] = static_cast<uint64_t>(static_cast<u128>(t0));
+            i128 carry = t0 >> 64;
+            if (NQ == 2) {
+                const i128 t1 = col[NQ - 1] + carry;
+                acc.w[1] = static_cast<uint64_t>(static_cast<u128>(t1));
+                carry = t1 >> 64;
+                acc.w[2] = static_cast<uint64_t>(static_cast<u128>(carry));
+            } else {
+                acc.w[1] = static_cast<uint64_t>(static_cast<u128>(carry));
+                acc.w[2] = carry < 0 ? ~0ull : 0ull;
             }
+        }
         const size_t i = idx / n, j = idx - (idx / n) * n;
         const int64_t off = static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j) * csc;
         const LinearEpi& L = e.lin;
@@ -283,14 +337,12 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
     int32_t* part = reinterpret_cast<int32_t*>(ws + a_bytes + b_bytes);
     p.partial = part;
 
-    {
-        const int64_t total = static_cast<int64_t>(p.mp) * kp;
-        const int grid = static_cast<int>(total / 256 + 1 < 148 * 32 ? total / 256 + 1 : 148 * 32);
-        slice_a_kernel<<<grid, 256, 0, s>>>(as, L, p.mp, (int)kp, a, rsa, csa, eb, (int)m, (int)k);
-        dim3 g2((p.np + 31) / 32, (unsigned)((kp + 31) / 32));
-        slice_b_kernel<<<g2, dim3(32, 8), 0, s>>>(bs, L, p.np, (int)kp, b, rsb, csb, eb, (int)k,
-                                                  (int)n);
-    }
+    if (eb == 2)
+        launch_slicing<2>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
+    else if (eb == 4)
+        launch_slicing<4>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
+    else
+        launch_slicing<8>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
     CUtensorMap tmA, tmB;
     if (!make_tmap_u8(&tmA, as, k, (uint64_t)L * p.mp, kp, 128, 128) ||
         !make_tmap_u8(&tmB, bs, k, (uint64_t)L * p.np, kp, 128, 256))
@@ -306,7 +358,10 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
     WideEpi we{epi, eb == 8 ? 1 : 0};
     const size_t total = m * n;
     const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-    wide_reduce_kernel<<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, m, n, c, rsc, csc, we);
+    if (ngroups <= 8)
+        wide_reduce_kernel<8><<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, m, n, c, rsc, csc, we);
+    else
+        wide_reduce_kernel<16><<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, m, n, c, rsc, csc, we);
     return cuda_status(cudaGetLastError());
 }
 
