@@ -17,8 +17,9 @@ output written every step, so no step reads operands a previous step left in L2.
 
 --workload selects the other BASELINE configs for their own measurement lines
 (i8-512: configs[0]; codec: configs[1]; f32: configs[2]; wide: configs[3];
-trop: configs[4]'s max-plus half). They are opt-in; the driver's line is the
-default.
+wide-splitk: configs[3] with the reduction split across ranks and one NCCL
+all-reduce of exact limbs, strong scaling; trop: configs[4]'s max-plus half). They
+are opt-in; the driver's line is the default.
 
 --impl reference times the reference's CPU path on the host cores instead (the
 Rust crate cannot be built here, so its C restatement in oracle/ stands in).
@@ -39,7 +40,7 @@ sys.path.insert(0, ROOT)
 
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
-WORKLOADS = ("i8", "i8-512", "codec", "f32", "wide", "trop")
+WORKLOADS = ("i8", "i8-512", "codec", "f32", "wide", "wide-splitk", "trop")
 
 
 def parse():
@@ -511,7 +512,56 @@ def wl_trop(args, U, torch, rank):
     return w
 
 
-def build_workload(name, args, U, torch, rank):
+def wl_wide_splitk(args, U, torch, rank, world):
+    """configs[3] with the reduction split across ranks (strong scaling): each rank's
+    exact partial sum as radix-2^40 limbs, one NCCL all-reduce of 3 m n int64, one
+    finish per rank."""
+    import numpy as np
+    import uor_b200_dist as D
+    m, k, n = 1024, 65536, 1024
+    A = torch.from_numpy(U.corpus(4, U.CORPUS_I32_FULL, m * k)).cuda()
+    B = torch.from_numpy(U.corpus(5, U.CORPUS_I32_FULL, k * n)).cuda()
+    C = torch.zeros(m * n * 2, dtype=torch.int64, device="cuda")
+    # partial (slicing, limb-pair GEMM, recombination into i128, limbs) and finish
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n / world, launches=6)
+
+    def step(i, ctx):
+        D.splitk_gemm(U.I32, U.I128, A, (m, k, k, 1), B, (k, n, n, 1), C, (m, n, n, 1), ctx=ctx)
+
+    def check(last):
+        want = torch.zeros_like(C)
+        U.gemm(U.I32, U.I128, A, (m, k, k, 1), B, (k, n, n, 1), want, (m, n, n, 1))
+        assert torch.equal(C, want), "split-K result differs from the one-device call"
+
+    def cpu(budget_s, ctx):
+        return wl_wide(args, U, torch, rank).cpu(budget_s, ctx)
+
+    w.step, w.check, w.cpu = step, check, cpu
+    w.e2e = None
+    w.metric = "exact i32 -> i128 GEMM TOPS, 1024x65536x1024, split-K (bit-exact)"
+    w.unit, w.dtype = "TOPS", "int32 in (4 x 4 int8 limb pairs), int128 out"
+    w.config = {"workload": "i32 x i32 -> i128 GEMM 1024x65536x1024 in total (configs[3]), "
+                            "reduction split across ranks", "m": m, "k": k, "n_per_gpu": n}
+    w.scaling = "strong"
+    w.parallelism = (f"split-K x{world}: radix-2^40 int64 limbs, one NCCL all-reduce of "
+                     f"{3 * 8 * m * n >> 20} MiB")
+    w.l2 = "512 MiB of operands (> L2)"
+    w.algorithmic_bytes = 4 * (m * k + k * n) // world + 16 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        ach = 16 * w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "basis": "this rank's int8 limb-pair ops (16 x 2mnk / ranks) over the whole "
+                         "step (partial, exchange, finish)",
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def build_workload(name, args, U, torch, rank, world=1):
     if name == "i8":
         return wl_i8(args, U, torch, rank, args.size or SIZE)
     if name == "i8-512":
@@ -522,6 +572,8 @@ def build_workload(name, args, U, torch, rank):
         return wl_f32(args, U, torch, rank, args.size or 4096)
     if name == "wide":
         return wl_wide(args, U, torch, rank)
+    if name == "wide-splitk":
+        return wl_wide_splitk(args, U, torch, rank, world)
     return wl_trop(args, U, torch, rank)
 
 
@@ -636,16 +688,18 @@ def measure(w, args, U, torch, dist, ctx, stream, rank, world, local):
     line = {
         "metric": w.metric, "value": value, "unit": w.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
-        "data": "synthetic (reference xorshift corpus)",
-        "config": dict(w.config, n_total=w.config["n_per_gpu"] * world, l2=w.l2,
-                       parallelism=f"column blocks x{world}, no data-path collective"),
+        "higher_is_better": True, "scaling": getattr(w, "scaling", "weak"), "vs_baseline": None,
+        "dtype": w.dtype, "data": "synthetic (reference xorshift corpus)",
+        "config": dict(w.config, n_total=w.config["n_per_gpu"] * (
+                           world if getattr(w, "scaling", "weak") == "weak" else 1), l2=w.l2,
+                       parallelism=getattr(w, "parallelism",
+                                           f"column blocks x{world}, no data-path collective")),
         "route": w.route.as_dict(),
         "roofline": w.roofline(statistics.mean(step_ms)),
         "gpu_launches": w.launches * args.steps,
         "clocks": clk,
     }
-    if args.e2e_steps > 0:
+    if args.e2e_steps > 0 and w.e2e is not None:
         if dist:
             dist.barrier()
         r = w.e2e(args.e2e_steps, ctx, stream)
@@ -683,7 +737,7 @@ def main():
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
 
-    w = build_workload(args.workload, args, U, torch, rank)
+    w = build_workload(args.workload, args, U, torch, rank, world)
     line = measure(w, args, U, torch, dist, ctx, stream, rank, world, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = w.cpu(12.0, ctx)

@@ -85,7 +85,8 @@ typedef struct uor_b200_ctx uor_b200_ctx;
 uor_b200_ctx *uor_b200_ctx_create(int device);
 void uor_b200_ctx_destroy(uor_b200_ctx *ctx);
 /* Run this context's work on `stream` (a cudaStream_t); NULL is CUDA's legacy
- * default stream. A new context runs on a private non-blocking stream. */
+ * default stream. A new context runs on a private blocking stream: its calls are
+ * ordered with the work the caller queues on the legacy default stream. */
 int uor_b200_ctx_set_stream(uor_b200_ctx *ctx, void *stream);
 /* Upper bound on any single device-side wait, in nanoseconds (default 2 s). */
 int uor_b200_ctx_set_wait_budget_ns(uor_b200_ctx *ctx, uint64_t ns);
@@ -250,6 +251,31 @@ int uor_b200_tabulated_gemm(uor_b200_dtype out, const uor_b200_view *a, const ui
                             size_t codes_len, size_t k, size_t n, uint32_t per_byte,
                             const int8_t *table, size_t table_len, const uor_b200_view_mut *c,
                             int64_t alpha, int64_t beta, const uor_b200_call *call);
+
+/* ------------------------------------------------- split-K across devices */
+
+/* The exact partial sum of one device's share of a split reduction, for an exchange
+ * between devices (NCCL all-reduce, sum of int64). No reference counterpart: the
+ * reference runs on one host; this extends its exact chunk fold (run_chunked_depth,
+ * crates/uor-matmul-gemm/src/kernel.rs:1431) across devices, with the independent
+ * tiles of Partition (partition.rs:34) handling the other axis.
+ *
+ * limbs[(i * n + j) * 3 + t] receives X_ij = sum_p a_ip b_pj (over the views given:
+ * pass A's columns and B's rows of this device's reduction range) as
+ *   X = l0 + l1 2^40 + l2 2^80,  l0, l1 in [0, 2^40),  l2 = X >> 80 (arithmetic),
+ * so elementwise int64 sums over devices stay exact. elem in {I8, I16, I32} (their
+ * accumulator is i128); device pointers required (UOR_B200_DEVICE_POINTERS);
+ * limbs_len counts int64 entries (>= 3 m n). */
+int uor_b200_gemm_partial_limbs(uor_b200_dtype elem, const uor_b200_view *a,
+                                const uor_b200_view *b, int64_t *limbs, size_t limbs_len,
+                                const uor_b200_call *call);
+
+/* C := encode(alpha * X + beta * C) from summed limbs (as above), with the Linear
+ * epilogue of elem's i128 accumulator (epilogue.rs:79-93, 280-288): the total is
+ * encoded once, so a split-K product has the single-device bytes. Device pointers. */
+int uor_b200_limbs_finish(uor_b200_dtype elem, uor_b200_dtype out, const int64_t *limbs,
+                          size_t limbs_len, const uor_b200_view_mut *c, int64_t alpha,
+                          int64_t beta, const uor_b200_call *call);
 
 /* ------------------------------------------------- no-allocation variant */
 

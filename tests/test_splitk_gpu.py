@@ -1,0 +1,115 @@
+"""The split-K exchange on the GPU: partial limbs and the finish kernel against the
+single-device call (bit for bit), one GPU emulating the ranks' ranges; and, where the
+box has two GPUs, two NCCL ranks through uor_b200_dist.splitk_gemm."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import uor_b200 as U
+import uor_b200_dist as D
+from gpu_util import needs_gpu, torch
+
+pytestmark = [pytest.mark.gpu, needs_gpu]
+
+NPT = {U.I8: np.int8, U.I16: np.int16, U.I32: np.int32}
+
+
+def _operands(elem, m, k, n):
+    dt = NPT[elem]
+    a = U.corpus(4, U.CORPUS_I32_FULL, m * k).astype(dt, casting="unsafe")
+    b = U.corpus(5, U.CORPUS_I32_FULL, k * n).astype(dt, casting="unsafe")
+    return torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+
+
+def _prior(out, m, n):
+    w = 2 if out == U.I128 else 1
+    p = U.corpus(3, U.CORPUS_I32_FULL, m * n * w).astype(np.int64)
+    if out != U.I128:
+        p = p.astype({U.I32: np.int32, U.I64: np.int64, U.I16: np.int16}[out], casting="unsafe")
+    return torch.from_numpy(p).cuda()
+
+
+@pytest.mark.parametrize("elem,out,shape,alpha,beta,mode", [
+    (U.I32, U.I128, (64, 4096, 96), 1, 0, U.NEAREST),
+    (U.I32, U.I64, (33, 1000, 17), -3, 2, U.SATURATING),
+    (U.I16, U.I32, (40, 777, 50), 7, -1, U.WRAPPING),
+    (U.I8, U.I32, (128, 300000, 8), 2**40, 1, U.NEAREST),
+    (U.I32, U.I128, (5, 0, 7), 3, -1, U.NEAREST),
+])
+def test_ranges_summed_on_one_gpu_equal_the_whole(elem, out, shape, alpha, beta, mode):
+    m, k, n = shape
+    a, b = _operands(elem, m, k, n)
+    prior = _prior(out, m, n)
+    want = prior.clone()
+    U.gemm(elem, out, a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), alpha, beta, mode)
+    for world in (1, 2, 3):
+        total = torch.zeros(m * n * 3, dtype=torch.int64, device="cuda")
+        for k0, k1 in D.k_ranges(k, world):
+            limbs = torch.full((m * n * 3,), -7, dtype=torch.int64, device="cuda")
+            U.gemm_partial_limbs(elem, a[k0:], (m, k1 - k0, k, 1), b[k0 * n:], (k1 - k0, n, n, 1),
+                                 limbs)
+            total += limbs
+        got = prior.clone()
+        U.limbs_finish(elem, out, total, got, (m, n, n, 1), alpha, beta, mode)
+        assert torch.equal(got, want), (world, shape)
+
+
+def test_partial_limbs_validation():
+    a, b = _operands(U.I32, 4, 8, 4)
+    limbs = torch.zeros(4 * 4 * 3 - 1, dtype=torch.int64, device="cuda")
+    with pytest.raises(U.DoesNotFit):
+        U.gemm_partial_limbs(U.I32, a, (4, 8, 8, 1), b, (8, 4, 4, 1), limbs)
+    limbs = torch.zeros(48, dtype=torch.int64, device="cuda")
+    with pytest.raises(U.NotAProduct):
+        U.gemm_partial_limbs(U.I32, a, (4, 8, 8, 1), b, (7, 4, 4, 1), limbs)
+    with pytest.raises(U.UorError):
+        U.gemm_partial_limbs(U.I64, a, (4, 8, 8, 1), b, (8, 4, 4, 1), limbs)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port):
+    import datetime
+    import torch.distributed as dist
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        ctx = U.Context(rank)
+        m, k, n = 256, 65536, 128
+        a, b = _operands(U.I32, m, k, n)
+        prior = _prior(U.I128, m, n)
+        got = prior.clone()
+        D.splitk_gemm(U.I32, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), 3, -1,
+                      ctx=ctx)
+        torch.cuda.synchronize()
+        want = prior.clone()
+        U.gemm(U.I32, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), 3, -1,
+               ctx=ctx)
+        assert torch.equal(got, want), rank
+        # column blocks with the gather
+        c = torch.zeros(m * n, dtype=torch.int64, device="cuda")
+        D.column_block_gemm(U.I32, U.I64, a, (m, k, k, 1), b, (k, n, n, 1), c, (m, n, n, 1),
+                            ctx=ctx, gather=True)
+        w2 = torch.zeros_like(c)
+        U.gemm(U.I32, U.I64, a, (m, k, k, 1), b, (k, n, n, 1), w2, (m, n, n, 1), ctx=ctx)
+        assert torch.equal(c, w2), rank
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_nccl_ranks_match_one_device():
+    import torch.multiprocessing as mp
+    mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)

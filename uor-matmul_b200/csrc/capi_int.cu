@@ -3,6 +3,7 @@
 // (Triple::new, layout.rs:534-561); everything after it is total.
 #include "internal.h"
 #include "int_gemm.h"
+#include "splitk.cuh"
 #include "staging.h"
 
 using namespace uor;
@@ -33,20 +34,12 @@ bool device_ptrs(const uor_b200_call* call) {
     return call && (call->flags & UOR_B200_DEVICE_POINTERS);
 }
 
-// Everything after validation: stage, compute, stage back.
-int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Operand& B,
-                    const Operand& C, int64_t alpha, int64_t beta, int mode,
-                    const uor_b200_call* call) {
-    uor_b200_route local_route{};
-    uor_b200_route* route = call && call->route ? call->route : &local_route;
-    *route = uor_b200_route{};
+// Everything after validation, with the context locked: stage, compute, stage back.
+int int_gemm_locked(uor_b200_ctx* ctx, uor_b200_dtype elem, int kind, const Operand& A,
+                    const Operand& B, const Operand& C, int64_t alpha, int64_t beta, int mode,
+                    const uor_b200_call* call, uor_b200_route* route) {
     const size_t m = A.rows, k = A.cols, n = B.cols;
-    if (m == 0 || n == 0) return UOR_B200_OK;
-
     int st = UOR_B200_OK;
-    uor_b200_ctx* ctx = resolve_ctx(call, &st);
-    if (!ctx) return st;
-    std::lock_guard<std::mutex> lock(ctx->mu);
     const bool dev = device_ptrs(call);
     const LinearEpi epi{alpha, beta, mode, kind};
     if (!dev && elem == UOR_B200_I8 && i8_pipeline_applies(A, B, C)) {
@@ -70,6 +63,20 @@ int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Opera
     if ((st = stage_out_end(ctx, cs)) != UOR_B200_OK) return st;
     if (!dev) return uor_b200_ctx_sync(ctx);
     return finish_call(ctx, call);
+}
+
+int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Operand& B,
+                    const Operand& C, int64_t alpha, int64_t beta, int mode,
+                    const uor_b200_call* call) {
+    uor_b200_route local_route{};
+    uor_b200_route* route = call && call->route ? call->route : &local_route;
+    *route = uor_b200_route{};
+    if (A.rows == 0 || B.cols == 0) return UOR_B200_OK;
+    int st = UOR_B200_OK;
+    uor_b200_ctx* ctx = resolve_ctx(call, &st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    return int_gemm_locked(ctx, elem, kind, A, B, C, alpha, beta, mode, call, route);
 }
 
 int gemm_views(uor_b200_dtype elem, uor_b200_dtype out, const void* a, size_t a_len, size_t am,
@@ -151,6 +158,85 @@ int uor_b200_gemm_ex_i8_i32(size_t m, size_t k, size_t n, int64_t alpha, const i
     const size_t c_len = m && n ? (m - 1) * ldc + n : 0;
     return uor_b200_slice_gemm_ex(UOR_B200_I8, UOR_B200_I32, m, k, n, alpha, a, a_len, lda, b,
                                   b_len, ldb, beta, c, c_len, ldc, nullptr, 0, call);
+}
+
+int uor_b200_gemm_partial_limbs(uor_b200_dtype elem, const uor_b200_view* a,
+                                const uor_b200_view* b, int64_t* limbs, size_t limbs_len,
+                                const uor_b200_call* call) {
+    if (!a || !b) return UOR_B200_INVALID_ARGUMENT;
+    if (elem != UOR_B200_I8 && elem != UOR_B200_I16 && elem != UOR_B200_I32)
+        return UOR_B200_UNSUPPORTED;
+    if (!device_ptrs(call)) return UOR_B200_INVALID_ARGUMENT;
+    const size_t es = dtype_size(elem);
+    Operand A, B;
+    int st;
+    if ((st = place_view(a->data, a->len, a->rows, a->cols, a->rs, a->cs, es, &A)) != UOR_B200_OK)
+        return st;
+    if ((st = place_view(b->data, b->len, b->rows, b->cols, b->rs, b->cs, es, &B)) != UOR_B200_OK)
+        return st;
+    if (a->cols != b->rows) return UOR_B200_NONCONFORMANT;
+    const size_t m = a->rows, n = b->cols;
+    if (m == 0 || n == 0) return UOR_B200_OK;
+    if (!limbs) return UOR_B200_INVALID_ARGUMENT;
+    if (limbs_len < SPLITK_LIMBS * m * n) return UOR_B200_DOES_NOT_FIT;
+    uor_b200_ctx* ctx = resolve_ctx(call, &st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    uor_b200_route local_route{};
+    uor_b200_route* route = call->route ? call->route : &local_route;
+    *route = uor_b200_route{};
+    // The exact partial sum, as an i128 matrix in a context buffer.
+    void* x = ctx_buffer(ctx, SLOT_AUX, 16 * m * n, &st);
+    if (!x) return st;
+    if (a->cols == 0 && cudaMemsetAsync(x, 0, 16 * m * n, ctx->stream) != cudaSuccess)
+        return UOR_B200_DEVICE_ERROR;
+    Operand X;
+    X.origin = static_cast<const uint8_t*>(x);
+    X.lo = 0;
+    X.hi = static_cast<ptrdiff_t>(m * n) - 1;
+    X.rows = m;
+    X.cols = n;
+    X.rs = static_cast<ptrdiff_t>(n);
+    X.cs = 1;
+    X.es = 16;
+    uor_b200_call inner = *call;
+    inner.flags |= UOR_B200_ASYNC;  // the conversion below still runs on the same stream
+    if ((st = int_gemm_locked(ctx, elem, OUT_I128, A, B, X, 1, 0, MODE_WRAPPING, &inner, route)) !=
+        UOR_B200_OK)
+        return st;
+    if (i128_to_limbs(x, limbs, m * n, ctx->stream) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    return finish_call(ctx, call);
+}
+
+int uor_b200_limbs_finish(uor_b200_dtype elem, uor_b200_dtype out, const int64_t* limbs,
+                          size_t limbs_len, const uor_b200_view_mut* c, int64_t alpha,
+                          int64_t beta, const uor_b200_call* call) {
+    if (!c) return UOR_B200_INVALID_ARGUMENT;
+    if (elem != UOR_B200_I8 && elem != UOR_B200_I16 && elem != UOR_B200_I32)
+        return UOR_B200_UNSUPPORTED;
+    int kind = 0, mode = 0;
+    if (!int_out(out, &kind)) return UOR_B200_UNSUPPORTED;
+    if (call_mode(call, &mode) != UOR_B200_OK) return UOR_B200_INVALID_ARGUMENT;
+    if (!device_ptrs(call)) return UOR_B200_INVALID_ARGUMENT;
+    Operand C;
+    int st;
+    if ((st = place_view(c->data, c->len, c->rows, c->cols, c->rs, c->cs, dtype_size(out), &C)) !=
+        UOR_B200_OK)
+        return st;
+    if (self_aliases(c->rows, c->cols, c->rs, c->cs)) return UOR_B200_OUTPUT_ALIASES;
+    const size_t m = c->rows, n = c->cols;
+    if (m == 0 || n == 0) return UOR_B200_OK;
+    if (!limbs) return UOR_B200_INVALID_ARGUMENT;
+    if (limbs_len < SPLITK_LIMBS * m * n) return UOR_B200_DOES_NOT_FIT;
+    uor_b200_ctx* ctx = resolve_ctx(call, &st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    if (call->route) *call->route = uor_b200_route{};
+    const LinearEpi epi{alpha, beta, mode, kind};
+    if (limbs_finish(limbs, m, n, const_cast<uint8_t*>(C.origin), C.rs, C.cs, epi, ctx->stream) !=
+        cudaSuccess)
+        return UOR_B200_DEVICE_ERROR;
+    return finish_call(ctx, call);
 }
 
 }  // extern "C"

@@ -214,7 +214,10 @@ uor_b200_ctx* uor_b200_ctx_create(int device) {
     auto* ctx = new (std::nothrow) uor_b200_ctx();
     if (!ctx) return nullptr;
     ctx->device = device;
-    bool ok = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) == cudaSuccess &&
+    // A blocking stream: a call on the context's own stream is ordered after work the
+    // caller queued on the legacy default stream (a fill of the output, a copy of an
+    // operand) and before work queued there after it returns.
+    bool ok = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamDefault) == cudaSuccess &&
               cudaMalloc(&ctx->d_status, sizeof(int)) == cudaSuccess &&
               cudaMemset(ctx->d_status, 0, sizeof(int)) == cudaSuccess &&
               cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device) ==

@@ -106,6 +106,8 @@ def lib():
             "uor_b200_gemm_tropical": ([I, I, VP, VP, VP, Trop, Trop, CP], I),
             "uor_b200_coded_gemm": ([I, VP, P, Z, Z, Z, U32, P, Z, VP, L64, L64, CP], I),
             "uor_b200_tabulated_gemm": ([I, VP, P, Z, Z, Z, U32, P, Z, VP, L64, L64, CP], I),
+            "uor_b200_gemm_partial_limbs": ([I, VP, VP, P, Z, CP], I),
+            "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
             "uor_b200_status_string": ([I], ctypes.c_char_p),
             "uor_b200_version": ([], I),
             "uor_b200_selftest_wait_timeout": ([P, U64], I),
@@ -329,6 +331,41 @@ def coded_gemm(out, a, av, codes, k, n, per_byte, table, c, cv, alpha=1, beta=0,
     fn = lib().uor_b200_tabulated_gemm if tabulated else lib().uor_b200_coded_gemm
     _check(fn(out, ctypes.byref(A), pc, lc, k, n, per_byte, pt, lt, ctypes.byref(C), alpha, beta,
               ctypes.byref(call)), "coded_gemm")
+
+
+# ------------------------------------------------------------------ split-K exchange
+
+SPLITK_LIMBS = 3
+
+
+def gemm_partial_limbs(elem, a, av, b, bv, limbs, ctx=None, route=None, asynchronous=False):
+    """Exact partial sum of A B as radix-2^40 int64 limbs [m][n][3] (device buffers)."""
+    if not _on_device(a, b, limbs):
+        raise UorError(INVALID_ARGUMENT, "gemm_partial_limbs takes device buffers")
+    A, B = view(a, *av), view(b, *bv)
+    pl, ll, _ = _buffer(limbs)
+    call = make_call(NEAREST, True, ctx, route, asynchronous)
+    _check(lib().uor_b200_gemm_partial_limbs(elem, ctypes.byref(A), ctypes.byref(B), pl,
+                                             _int64_len(limbs, ll), ctypes.byref(call)),
+           "gemm_partial_limbs")
+
+
+def limbs_finish(elem, out, limbs, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None,
+                 asynchronous=False):
+    """C := encode(alpha X + beta C) from summed limbs (device buffers)."""
+    if not _on_device(limbs, c):
+        raise UorError(INVALID_ARGUMENT, "limbs_finish takes device buffers")
+    C = view(c, *cv)
+    pl, ll, _ = _buffer(limbs)
+    call = make_call(encode, True, ctx, None, asynchronous)
+    _check(lib().uor_b200_limbs_finish(elem, out, pl, _int64_len(limbs, ll), ctypes.byref(C),
+                                       alpha, beta, ctypes.byref(call)), "limbs_finish")
+
+
+def _int64_len(limbs, count):
+    if str(limbs.dtype) not in ("torch.int64", "int64"):
+        raise UorError(INVALID_ARGUMENT, "limbs must be int64")
+    return count
 
 
 # ------------------------------------------------------------------ corpus
