@@ -91,7 +91,7 @@ def test_random_bit_patterns_and_specials(elem, out):
 
 
 @pytest.mark.parametrize("elem,out", [(U.F32, U.F32), (U.F64, U.F64), (U.F32, U.F64)])
-@pytest.mark.parametrize("shape", [(3, 10, 7), (130, 96, 270), (64, 700, 40)])
+@pytest.mark.parametrize("shape", [(3, 10, 7), (130, 96, 270), (64, 700, 40), (257, 64, 130)])
 def test_moderate_exponents_tensor_route(elem, out, shape):
     """Exponent spans small enough for the digit route (K6 on the tensor cores)."""
     m, k, n = shape
@@ -104,7 +104,8 @@ def test_moderate_exponents_tensor_route(elem, out, shape):
         got, want, route = run_both(elem, out, a, b, m, k, n, alpha, beta, c0, mode)
         assert np.array_equal(got, want), (alpha, beta, mode)
         if elem == U.F32:
-            assert route.kernel == 5 and route.tile_m == 128
+            # 256-row tiles on CTA pairs past 128 rows, 128-row tiles below
+            assert route.kernel == 5 and route.tile_m == (256 if m > 128 else 128)
 
 
 def test_nonfinite_on_the_tensor_route():
@@ -170,7 +171,7 @@ def test_config3_full_size_sampled():
     tc = torch.empty(m * n, dtype=torch.float32, device="cuda")
     route = U.Route()
     U.gemm_float(U.F32, U.F32, ta, (m, k, k, 1), tb, (k, n, n, 1), tc, (m, n, n, 1), route=route)
-    assert route.kernel == 5 and route.tile_m == 128
+    assert route.kernel == 5 and route.tile_m == 256 and route.a_layout == 11
     c = tc.cpu().numpy().view(np.uint32)
     cells = [(0, 0), (0, 1), (m - 1, n - 1), (123, 4000), (3000, 30), (40, 40)]
     for (i, j) in cells:

@@ -47,7 +47,7 @@ def rand_full(rng, bits, count):
 @pytest.mark.parametrize("out", [U.I32, U.I64, U.I128])
 def test_random_full_range(bits, out):
     rng = np.random.default_rng(bits * 10 + out)
-    for (m, k, n) in [(1, 1, 1), (13, 17, 19), (130, 300, 270)]:
+    for (m, k, n) in [(1, 1, 1), (13, 17, 19), (130, 300, 270), (300, 200, 261)]:
         a, b = rand_full(rng, bits, m * k), rand_full(rng, bits, k * n)
         c0 = out_array(out, m * n)
         c0[:] = rng.integers(-1000, 1000, size=c0.size)

@@ -137,6 +137,21 @@ bool make_tmap_s32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t d
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_s32_3d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                      uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                      uint32_t box1) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {dim0, dim1, dim2};
+    cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    cuuint32_t box[3] = {box0, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 bool view_extent(size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs, ptrdiff_t* lo,
                  ptrdiff_t* hi) {
     if (rows == 0 || cols == 0) {

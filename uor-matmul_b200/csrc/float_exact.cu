@@ -915,7 +915,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
                 if (sb < 0 || sb >= Lb) continue;
                 p.pair_a[npairs] = (uint8_t)sa;
                 p.pair_b[npairs] = (uint8_t)sb;
-                p.pair_idesc[npairs] = idesc_i8(KS_BM, KS_BN, true, true, false, false);
+                p.pair_sign[npairs] = 3;  // balanced digits are signed on both sides
                 ++npairs;
                 ++cnt;
             }
@@ -934,12 +934,8 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
     p.num_kb = num_kb;
     p.m = (int)m;
     p.n = (int)n;
-    p.mp = (int)rup(m, KS_BM);
+    p.mp = (int)ks_rows_pad(m);
     p.np = (int)rup(n, KS_BN);
-    p.tiles_m = p.mp / KS_BM;
-    p.tiles_n = p.np / KS_BN;
-    p.num_tiles = p.tiles_m * p.tiles_n;
-    p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
     p.status = ctx->d_status;
     p.budget_ns = ctx->budget_ns;
     const bool run_mma = npairs > 0 && num_kb > 0;
@@ -971,19 +967,15 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         dim3 g2((unsigned)(p.np / 32), (unsigned)((kp + 31) / 32));
         fx_slice_b_kernel<<<g2, dim3(32, 8), 0, s>>>(bs, Lb, p.np, (int)kp, b, rsb, csb, e64,
                                                      (int)k, (int)n, clo);
-        CUtensorMap tmA, tmB;
-        if (!make_tmap_u8(&tmA, as, k, (uint64_t)La * p.mp, kp, 128, 128) ||
-            !make_tmap_u8(&tmB, bs, k, (uint64_t)Lb * p.np, kp, 128, 256))
-            return UOR_B200_DEVICE_ERROR;
-        const int units = ngroups * p.num_chunks * p.num_tiles;
-        const int grid2 = units < ctx->sm_count ? units : ctx->sm_count;
         if (route) {
             route->k_chunks = (uint32_t)p.num_chunks;
-            route->ctas = (uint32_t)grid2;
             route->a_layout = (uint32_t)La;  // digits per A element
             route->b_layout = (uint32_t)Lb;
+            route->tile_m = (uint32_t)(m > 128 ? 256 : KS_BM);
         }
-        if (ks_launch(tmA, tmB, p, grid2, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        if ((st = ks_run(as, La, bs, Lb, k, kp, p, ctx->sm_count, s,
+                         route ? &route->ctas : nullptr)) != UOR_B200_OK)
+            return st;
     }
     const size_t total = m * n;
     const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);

@@ -2,10 +2,13 @@
 //
 // Same pipeline as K1 (gemm_i8.cu): warp 0 TMA producer, warp 1 TMEM allocator and
 // single-thread tcgen05.mma issuer, warps 2-5 epilogue, two TMEM accumulators. The
-// difference is the walk: a unit's mainloop visits (reduction block, slice pair)
-// in that order, and each pair carries its own instruction descriptor so that
-// unsigned and signed slices mix exactly (kind::i8 takes u8 or s8 per operand).
+// difference is the walk: a unit's mainloop visits (slice pair, reduction block) in
+// that order -- units running side by side then stream the same slice at the same
+// time, so a band of one slice rather than of every slice of the diagonal lives in
+// L2 -- and each pair carries its own instruction descriptor so that unsigned and
+// signed slices mix exactly (kind::i8 takes u8 or s8 per operand).
 #include "gemm_slices.cuh"
+#include "internal.h"
 #include "ptx.cuh"
 
 namespace uor {
@@ -88,8 +91,8 @@ __global__ void __launch_bounds__(KS_THREADS, 1)
                 const KSUnit w = ks_unit(u, p);
                 const int nb = ks_unit_blocks(p, w.q);
                 const int kb0 = w.q * p.kb_per_chunk;
-                for (int kb = 0; kb < nb && ok; ++kb) {
-                    for (int pr = p.pair_begin[w.g]; pr < p.pair_begin[w.g + 1]; ++pr) {
+                for (int pr = p.pair_begin[w.g]; pr < p.pair_begin[w.g + 1] && ok; ++pr) {
+                    for (int kb = 0; kb < nb; ++kb) {
                         if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
                                        KERR_TIMEOUT_PRODUCER)) {
                             ok = false;
@@ -134,8 +137,8 @@ __global__ void __launch_bounds__(KS_THREADS, 1)
             tc_fence_after();
             const uint32_t d = tmem_base + buf * KS_BN;
             int step = 0;
-            for (int kb = 0; kb < nb && ok; ++kb) {
-                for (int pr = p.pair_begin[w.g]; pr < p.pair_begin[w.g + 1]; ++pr, ++step) {
+            for (int pr = p.pair_begin[w.g]; pr < p.pair_begin[w.g + 1] && ok; ++pr) {
+                for (int kb = 0; kb < nb; ++kb, ++step) {
                     if (!mbar_wait_warp(full0 + 8 * stage, phase, p.budget_ns, p.status,
                                         KERR_TIMEOUT_MMA_FULL)) {
                         ok = false;
@@ -238,6 +241,42 @@ cudaError_t ks_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const KSPa
     }
     ks_kernel<<<grid, KS_THREADS, KS_SMEM_BYTES, stream>>>(tmA, tmB, p);
     return cudaGetLastError();
+}
+
+int ks_run(const void* as, int La, const void* bs, int Lb, size_t k, size_t kp, KSParams& p,
+           int sm_count, cudaStream_t s, uint32_t* ctas) {
+    const bool pair = p.m > 128;
+    const int bm = pair ? 256 : KS_BM;
+    p.tiles_m = p.mp / bm;
+    p.tiles_n = p.np / KS_BN;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
+    for (int pr = 0; pr < p.pair_begin[p.num_groups]; ++pr)
+        p.pair_idesc[pr] = idesc_i8(bm, KS_BN, (p.pair_sign[pr] & 1) != 0,
+                                    (p.pair_sign[pr] & 2) != 0, false, false);
+    CUtensorMap tmA, tmB;
+    if (!make_tmap_u8(&tmA, as, k, static_cast<uint64_t>(La) * p.mp, kp, 128, 128) ||
+        !make_tmap_u8(&tmB, bs, k, static_cast<uint64_t>(Lb) * p.np, kp, 128, pair ? 128 : 256))
+        return UOR_B200_DEVICE_ERROR;
+    const int units = p.num_groups * p.num_chunks * p.num_tiles;
+    cudaError_t e;
+    if (!pair) {
+        const int grid = units < sm_count ? units : sm_count;
+        p.tma_store = 0;
+        if (ctas) *ctas = static_cast<uint32_t>(grid);
+        e = ks_launch(tmA, tmB, p, grid, s);
+    } else {
+        CUtensorMap tmC;
+        const uint64_t planes = static_cast<uint64_t>(p.num_chunks) * p.num_groups;
+        p.tma_store = (p.n % 4) == 0 &&
+                      make_tmap_s32_3d(&tmC, p.partial, p.n, p.m, planes, static_cast<uint64_t>(p.n) * 4,
+                                       static_cast<uint64_t>(p.m) * p.n * 4, 32, 32);
+        if (!p.tma_store) memset(&tmC, 0, sizeof(tmC));
+        const int mc = ks_pair_max_clusters();
+        if (ctas) *ctas = static_cast<uint32_t>(2 * (units < mc ? units : mc));
+        e = ks_pair_launch(tmA, tmB, tmC, p, s);
+    }
+    return e == cudaSuccess ? UOR_B200_OK : UOR_B200_DEVICE_ERROR;
 }
 
 }  // namespace uor

@@ -38,15 +38,38 @@ struct KSParams {
     int32_t* partial;         // [num_chunks][num_groups][m][n]
     int* status;
     uint64_t budget_ns;
+    int tma_store;            // pair kernel: partials written by TMA through a 3-D map
     int pair_begin[KS_MAX_GROUPS + 1];
     uint8_t pair_a[KS_MAX_PAIRS];
     uint8_t pair_b[KS_MAX_PAIRS];
+    uint8_t pair_sign[KS_MAX_PAIRS];  // bit 0: A slice signed, bit 1: B slice signed
     uint32_t pair_idesc[KS_MAX_PAIRS];
 };
+
+// Rows per slice in the A stack: whole tiles of the kernel ks_run will choose.
+inline size_t ks_rows_pad(size_t m) {
+    const size_t t = m > 128 ? 256 : 128;
+    return (m + t - 1) / t * t;
+}
 
 // tmA: dims {k, La * mp}, box {128, 128}; tmB: dims {k, Lb * np}, box {128, 256};
 // both uint8 with 128-byte swizzle.
 cudaError_t ks_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const KSParams& p,
                       int grid, cudaStream_t stream);
+
+// The same product on CTA pairs (tcgen05 cta_group::2): 256 x 256 tiles, mp a multiple
+// of 256, tmB box {128, 128}; with p.tma_store the partials go out through tmC, an s32
+// 3-D map {n, m, chunks * groups} with box {32, 32, 1}.
+cudaError_t ks_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                           const KSParams& p, cudaStream_t stream);
+int ks_pair_max_clusters();
+
+// Runs the slice-pair product: `as` is the A stack [La][mp][kp] (mp = ks_rows_pad(m)),
+// `bs` the B stack [Lb][np][kp] (np a multiple of 256). p holds m, n, mp, np, the
+// groups (pair_begin, pair_a, pair_b, pair_sign), the chunking and the partial buffer;
+// ks_run fills the tiles and instruction descriptors, picks CTA pairs when m > 128,
+// builds the tensor maps and launches on `stream`. Returns a uor_b200_status.
+int ks_run(const void* as, int La, const void* bs, int Lb, size_t k, size_t kp, KSParams& p,
+           int sm_count, cudaStream_t stream, uint32_t* ctas);
 
 }  // namespace uor

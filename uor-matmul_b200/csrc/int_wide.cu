@@ -298,7 +298,7 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
             const bool as = sa == L - 1, bs = sb == L - 1;
             p.pair_a[npairs] = static_cast<uint8_t>(sa);
             p.pair_b[npairs] = static_cast<uint8_t>(sb);
-            p.pair_idesc[npairs] = idesc_i8(KS_BM, KS_BN, as, bs, false, false);
+            p.pair_sign[npairs] = static_cast<uint8_t>((as ? 1 : 0) | (bs ? 2 : 0));
             sum += as && bs ? max_prod_ss : (as || bs ? max_prod_us : max_prod_uu);
             ++npairs;
         }
@@ -315,12 +315,8 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
     p.num_kb = num_kb;
     p.m = static_cast<int>(m);
     p.n = static_cast<int>(n);
-    p.mp = static_cast<int>(rup(m, KS_BM));
+    p.mp = static_cast<int>(ks_rows_pad(m));
     p.np = static_cast<int>(rup(n, KS_BN));
-    p.tiles_m = p.mp / KS_BM;
-    p.tiles_n = p.np / KS_BN;
-    p.num_tiles = p.tiles_m * p.tiles_n;
-    p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
     p.status = ctx->d_status;
     p.budget_ns = ctx->budget_ns;
 
@@ -343,18 +339,12 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
         launch_slicing<4>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
     else
         launch_slicing<8>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
-    CUtensorMap tmA, tmB;
-    if (!make_tmap_u8(&tmA, as, k, (uint64_t)L * p.mp, kp, 128, 128) ||
-        !make_tmap_u8(&tmB, bs, k, (uint64_t)L * p.np, kp, 128, 256))
-        return UOR_B200_DEVICE_ERROR;
-    const int units = ngroups * p.num_chunks * p.num_tiles;
-    const int grid = units < ctx->sm_count ? units : ctx->sm_count;
-    if (route) {
-        route->kernel = UOR_B200_KERNEL_LIMB_TCGEN05;
-        route->k_chunks = (uint32_t)p.num_chunks;
-        route->ctas = (uint32_t)grid;
-    }
-    if (ks_launch(tmA, tmB, p, grid, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    if (route) route->kernel = UOR_B200_KERNEL_LIMB_TCGEN05;
+    if (route) route->k_chunks = (uint32_t)p.num_chunks;
+    if ((st = ks_run(as, L, bs, L, k, kp, p, ctx->sm_count, s, route ? &route->ctas : nullptr)) !=
+        UOR_B200_OK)
+        return st;
+    if (route) route->tile_m = (uint32_t)(p.m > 128 ? 256 : KS_BM);
     WideEpi we{epi, eb == 8 ? 1 : 0};
     const size_t total = m * n;
     const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);

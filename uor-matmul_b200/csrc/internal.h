@@ -55,6 +55,10 @@ bool make_tmap_u8(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t di
 // an s32 output; 128-byte swizzle.
 bool make_tmap_s32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
                    uint64_t stride1_bytes, uint32_t box0, uint32_t box1);
+// s32 3-D map (planes of dim0 x dim1), 128-byte swizzle, box {box0, box1, 1}.
+bool make_tmap_s32_3d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
+                      uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                      uint32_t box1);
 
 // A view after placement: origin pointer and the reach of the view in elements.
 struct Placed {

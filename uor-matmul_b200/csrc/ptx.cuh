@@ -320,6 +320,15 @@ __device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, uint32
         "r"(src), "r"(x), "r"(y), "l"(policy)
         : "memory");
 }
+// 3-D tiled store (x innermost, then y, then z) with an L2 cache hint.
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, uint32_t src, int32_t x,
+                                                  int32_t y, int32_t z, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(src), "r"(x), "r"(y), "r"(z), "l"(policy)
+        : "memory");
+}
 __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

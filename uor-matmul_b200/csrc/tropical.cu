@@ -9,8 +9,9 @@
 // zero as -16384 (the same idea as the reference's packed lane, kernels/src/tropical.rs:91-179,
 // with a sentinel chosen so that a plain wrapping add never overflows: every finite sum is
 // in [-256, 254], every sum touching -inf is at most -16384 + 127, and -inf + -inf is
-// -32768). Then add.s16x2 and max.s16x2 evaluate two terms per instruction, register-
-// blocked 8x8 per thread over 128x128 tiles staged through shared memory with cp.async.
+// -32768). Then one fused add-max per 16x2 pair (__viaddmax_s16x2: max(a + b, acc),
+// wrapping add) evaluates two terms per instruction, register-blocked 8x8 per thread
+// over 128x128 tiles staged through shared memory with cp.async.
 // Any result below -8192 decodes to -inf.
 #include <cuda_runtime.h>
 #include "tropical.cuh"
@@ -137,17 +138,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__device__ __forceinline__ uint32_t add16x2(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("add.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-__device__ __forceinline__ uint32_t max16x2(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("max.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-
 __global__ void __launch_bounds__(TR_THREADS)
     trop_i8_kernel(const uint32_t* __restrict__ at, const int16_t* __restrict__ bt, int mp, int np,
                    int kp, TropEpi e) {
@@ -198,7 +188,7 @@ __global__ void __launch_bounds__(TR_THREADS)
 #pragma unroll
             for (int r = 0; r < 8; ++r)
 #pragma unroll
-                for (int q = 0; q < 4; ++q) acc[r][q] = max16x2(acc[r][q], add16x2(av[r], bv[q]));
+                for (int q = 0; q < 4; ++q) acc[r][q] = __viaddmax_s16x2(av[r], bv[q], acc[r][q]);
         }
         __syncthreads();
     }
