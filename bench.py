@@ -368,12 +368,14 @@ def wl_f32(args, U, torch, rank, size, sets=2):
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
-        pairs = max(1, w.route.a_layout * w.route.b_layout)
+        pairs = max(1, w.route.pairs)
         ach = pairs * w.units / (avg_ms / 1e3) / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src, "traffic": None,
-                "basis": f"int8 slice-pair ops ({w.route.a_layout} x {w.route.b_layout} digit "
-                         "pairs x 2mnk) over the whole call (analysis, slicing, GEMM, reduce)",
+                "basis": f"int8 slice-pair ops executed ({pairs} of {w.route.a_layout} x "
+                         f"{w.route.b_layout} digit pairs x 2mnk; {w.route.fixups} cells "
+                         "recomputed exactly) over the whole call (analysis, slicing, GEMM, "
+                         "interval test, fixups)",
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w

@@ -112,6 +112,8 @@ typedef struct uor_b200_route {
     uint32_t a_layout;    /* 0 K-major, 1 MN-major, 2 gathered to K-major */
     uint32_t b_layout;
     uint32_t ctas;        /* CTAs launched per chunk */
+    uint32_t pairs;       /* int8 slice-pair GEMMs run on the tensor cores (1 for K1) */
+    uint32_t fixups;      /* exact float: cells recomputed exactly after the lazy digits */
 } uor_b200_route;
 
 #define UOR_B200_DEVICE_POINTERS 1u

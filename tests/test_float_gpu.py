@@ -132,6 +132,43 @@ def test_config3_cancellation_moderate():
         assert got[(j % m) * n + j] == 0, "an exactly cancelling row encodes +0"
 
 
+def test_lazy_digits_interval_test_and_exact_fixups():
+    """Wide exponent spans take the lazy route: only the top diagonals run on the tensor
+    cores, each cell is accepted only when both ends of its error interval encode alike,
+    and the rest (here the exactly cancelling cells) are recomputed exactly."""
+    m, k, n = 300, 512, 260
+    a, b = config3(m, k, n)
+    a, b = a.reshape(-1), b.reshape(-1)
+    for alpha, mode in [(1, U.NEAREST), (-3, U.NEAREST), (5, U.TOWARD_ZERO)]:
+        got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, alpha, 0, None, mode)
+        assert np.array_equal(got, want), (alpha, mode)
+        assert route.pairs < route.a_layout * route.b_layout, "the low diagonals were skipped"
+        assert route.fixups >= n // 10, "every cancelling cell is recomputed exactly"
+    # a row and a column of zeros encode +0 without a fixup
+    a2, b2 = a.copy(), b.copy()
+    a2[7 * k:8 * k] = 0.0
+    b2[np.arange(k) * n + 3] = 0.0
+    got, want, route = run_both(U.F32, U.F32, a2, b2, m, k, n)
+    assert np.array_equal(got, want)
+    assert (got.reshape(m, n)[7] == 0).all() and (got.reshape(m, n)[:, 3] == 0).all()
+
+
+def test_lazy_digits_fall_back_when_many_cells_cancel():
+    """Every column cancels one of four rows: more unsure cells than the fixup list
+    holds, so every diagonal runs on the tensor cores after all -- same bytes."""
+    m, k, n = 4, 256, 8192
+    a, b = config3(m, k, n)
+    kk = k - k % 2
+    sign = np.where(np.arange(k) % 2 == 0, 1.0, -1.0).astype(np.float32)
+    for j in range(n):
+        b[:kk, j] = a[j % m, np.arange(kk) ^ 1] * sign[:kk] * np.float32(2.0 ** ((j % 9) - 4))
+    got, want, route = run_both(U.F32, U.F32, a.reshape(-1), np.ascontiguousarray(b).reshape(-1),
+                                m, k, n)
+    assert np.array_equal(got, want)
+    assert route.fixups > 4096
+    assert route.pairs == route.a_layout * route.b_layout
+
+
 def test_register_drop_quirk_on_gpu():
     a = np.array([1.0], np.float32)
     b = np.array([2.0], np.float32)

@@ -471,9 +471,13 @@ __device__ void finish_float(const FxEpi& e, int64_t off, Big& X, int ex, int fl
 
 // One warp per row of A: lowest set-bit and top-bit exponents over finite nonzero
 // elements, and whether the row holds a non-finite element.
+// Spans are recorded per row (0 for a row with no finite nonzero element); gmax[3]
+// collects SPAN_CAP - (smallest nonzero span), gmax[0] the largest span.
+constexpr int SPAN_CAP = 1 << 20;
+
 __global__ void fx_rows_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64_t csa, int m,
-                               int k, bool f64, int* __restrict__ lo, uint8_t* __restrict__ nf,
-                               int* __restrict__ gmax) {
+                               int k, bool f64, int* __restrict__ lo, int* __restrict__ span,
+                               uint8_t* __restrict__ nf, int* __restrict__ gmax) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= m) return;
@@ -495,8 +499,12 @@ __global__ void fx_rows_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64
     }
     if (lane == 0) {
         lo[warp] = l == INT_MAX ? 0 : l;
+        span[warp] = l == INT_MAX ? 0 : h - l + 1;
         nf[warp] = static_cast<uint8_t>(f);
-        if (l != INT_MAX) atomicMax(&gmax[0], h - l + 1);
+        if (l != INT_MAX) {
+            atomicMax(&gmax[0], h - l + 1);
+            atomicMax(&gmax[3], SPAN_CAP - (h - l + 1));
+        }
         if (f) atomicOr(&gmax[2], 1);
     }
 }
@@ -504,8 +512,8 @@ __global__ void fx_rows_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64
 // 32 columns of B per block of 32 x 32 threads: lane x owns column j0 + x, warp y
 // walks rows y, y + 32, ...; the warps' results meet in shared memory.
 __global__ void fx_cols_kernel(const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, int k,
-                               int n, bool f64, int* __restrict__ lo, uint8_t* __restrict__ nf,
-                               int* __restrict__ gmax) {
+                               int n, bool f64, int* __restrict__ lo, int* __restrict__ span,
+                               uint8_t* __restrict__ nf, int* __restrict__ gmax) {
     __shared__ int sl[32][33], sh[32][33], sf[32][33];
     const int tx = threadIdx.x, ty = threadIdx.y;
     const int j = blockIdx.x * 32 + tx;
@@ -533,8 +541,12 @@ __global__ void fx_cols_kernel(const uint8_t* __restrict__ b, int64_t rsb, int64
             f |= sf[r][tx];
         }
         lo[j] = l == INT_MAX ? 0 : l;
+        span[j] = l == INT_MAX ? 0 : h - l + 1;
         nf[j] = static_cast<uint8_t>(f);
-        if (l != INT_MAX) atomicMax(&gmax[1], h - l + 1);
+        if (l != INT_MAX) {
+            atomicMax(&gmax[1], h - l + 1);
+            atomicMax(&gmax[4], SPAN_CAP - (h - l + 1));
+        }
         if (f) atomicOr(&gmax[2], 1);
     }
 }
@@ -704,6 +716,145 @@ __global__ void fx_reduce_kernel(const int32_t* __restrict__ part, int chunks, i
     }
 }
 
+// ------------------------------------------------------------ lazy digits
+//
+// With beta 0 and finite inputs only the diagonals d >= D run on the tensor cores.
+// The rest, R = sum_{d<D} S_d 256^d, is bounded without computing it:
+// |S_d| <= k n_d 2^14 (n_d digit pairs on the diagonal, every digit in [-128, 127]), so
+// |R| / 256^D <= Ebound. The encode of a float is monotone in the exact value, so when
+// alpha (X_hi - Ebound) and alpha (X_hi + Ebound) (at scale 2^(ex + 8 D)) encode to the
+// same bits, so does the exact alpha X; every other cell is listed and recomputed
+// exactly, all diagonals, from the digit slices (fx_fix_kernel).
+
+template <int NW>
+__device__ __forceinline__ uint64_t encode_signed_scaled(uint64_t (&w)[NW], int64_t alpha, int ex,
+                                                         const FxEpi& e) {
+    bool neg = (w[NW - 1] >> 63) != 0;
+    if (neg) {
+        uint64_t c = 1;
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+            const uint64_t sv = ~w[q] + c;
+            c = (c && sv == 0) ? 1 : 0;
+            w[q] = sv;
+        }
+    }
+    if (alpha != 1) {
+        const uint64_t uf = alpha < 0 ? 0ull - static_cast<uint64_t>(alpha)
+                                      : static_cast<uint64_t>(alpha);
+        uint64_t c = 0;
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+            const u128 pr = static_cast<u128>(w[q]) * uf + c;
+            w[q] = static_cast<uint64_t>(pr);
+            c = static_cast<uint64_t>(pr >> 64);
+        }
+        neg = neg != (alpha < 0);
+    }
+    return encode_mag_fast<NW>(w, neg, ex, e.out64, e.mode, e.min_exp_e);
+}
+
+template <int NG>
+__global__ void fx_reduce_lazy_kernel(const int32_t* __restrict__ part, int chunks, int groups,
+                                      int m, int n, const int* __restrict__ rlo,
+                                      const int* __restrict__ clo, const int* __restrict__ rspan,
+                                      const int* __restrict__ cspan, int D, uint64_t ebound,
+                                      FxEpi e, uint32_t* __restrict__ list,
+                                      uint32_t* __restrict__ count, uint32_t limit) {
+    constexpr int NQ = (NG + 7) / 8;
+    constexpr int NW = NQ + 2;
+    const size_t total = static_cast<size_t>(m) * n;
+    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+        const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+        if (rspan[i] == 0 || cspan[j] == 0) {  // a row or column of zeros: the sum is 0
+            store_float(e.c, e.out64, off, 0);
+            continue;
+        }
+        i128 col[NQ];
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) col[q] = 0;
+        for (int q = 0; q < chunks; ++q) {
+            const int32_t* pq = part + static_cast<size_t>(q) * groups * total + idx;
+            int32_t v[NG];
+#pragma unroll
+            for (int g = 0; g < NG; ++g) v[g] = g < groups ? __ldg(pq + g * total) : 0;
+#pragma unroll
+            for (int g = 0; g < NG; ++g) col[g >> 3] += static_cast<i128>(v[g]) << (8 * (g & 7));
+        }
+        uint64_t lo[NW], hi[NW];
+        i128 carry_lo = -static_cast<i128>(ebound), carry_hi = static_cast<i128>(ebound);
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+            const i128 tl = col[q] + carry_lo, th = col[q] + carry_hi;
+            lo[q] = static_cast<uint64_t>(static_cast<u128>(tl));
+            hi[q] = static_cast<uint64_t>(static_cast<u128>(th));
+            carry_lo = tl >> 64;
+            carry_hi = th >> 64;
+        }
+        lo[NQ] = static_cast<uint64_t>(static_cast<u128>(carry_lo));
+        hi[NQ] = static_cast<uint64_t>(static_cast<u128>(carry_hi));
+        lo[NQ + 1] = carry_lo < 0 ? ~0ull : 0ull;
+        hi[NQ + 1] = carry_hi < 0 ? ~0ull : 0ull;
+        const int ex = rlo[i] + clo[j] + 8 * D;
+        const uint64_t blo = encode_signed_scaled<NW>(lo, e.alpha, ex, e);
+        const uint64_t bhi = encode_signed_scaled<NW>(hi, e.alpha, ex, e);
+        if (blo == bhi) {
+            store_float(e.c, e.out64, off, blo);
+        } else {
+            const uint32_t slot = atomicAdd(count, 1u);
+            if (slot < limit) list[slot] = static_cast<uint32_t>(idx);
+        }
+    }
+}
+
+// One warp per listed cell: S_d for every diagonal from the digit slices (4 digit
+// products per dp4a, exact in 32-bit lanes summed in 64 bits), the cell's exact integer
+// in the 768-bit window, alpha, and the encode.
+__global__ void fx_fix_kernel(const uint32_t* __restrict__ list, const uint32_t* __restrict__ count,
+                              uint32_t limit, const int8_t* __restrict__ as, int La, int mp,
+                              const int8_t* __restrict__ bs, int Lb, int np, int kp, int n,
+                              const int* __restrict__ rlo, const int* __restrict__ clo, FxEpi e) {
+    const uint32_t cells = min(*count, limit);
+    const int lane = threadIdx.x & 31;
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    for (uint32_t w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < cells; w += warps) {
+        const uint32_t idx = list[w];
+        const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+        Big X;
+        big_zero(X);
+        for (int d = 0; d <= La + Lb - 2; ++d) {
+            long long acc = 0;
+            const int s0 = d - (Lb - 1) > 0 ? d - (Lb - 1) : 0;
+            const int s1 = d < La - 1 ? d : La - 1;
+            for (int sa = s0; sa <= s1; ++sa) {
+                const int8_t* ar = as + (static_cast<int64_t>(sa) * mp + i) * kp;
+                const int8_t* bc = bs + (static_cast<int64_t>(d - sa) * np + j) * kp;
+                int part = 0;
+                for (int p = lane * 4; p < kp; p += 128) {
+                    part = __dp4a(*reinterpret_cast<const int*>(ar + p),
+                                  *reinterpret_cast<const int*>(bc + p), part);
+                    if (((p >> 7) & 1023) == 1023) {  // stay far inside 32 bits
+                        acc += part;
+                        part = 0;
+                    }
+                }
+                acc += part;
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0 && acc) big_add_i64_shl(X, static_cast<int64_t>(acc), 8 * d);
+        }
+        if (lane == 0) {
+            if (e.alpha != 1) big_mul_i64(X, e.alpha);
+            const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+            store_float(e.c, e.out64, off,
+                        encode_words<BW>(X.w, rlo[i] + clo[j], e.out64, e.mode, e.min_exp_e));
+        }
+    }
+}
+
 // ------------------------------------------------------------ direct route
 
 // The reference's register, Complete<L, MIN_EXP>: L low limbs and an extension word,
@@ -866,28 +1017,32 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
 
     // ---- analysis: per-row / per-column exponent spans and non-finite markers
     int st = UOR_B200_OK;
-    const size_t an_bytes = rup(m * 4, 256) + rup(n * 4, 256) + rup(m, 256) + rup(n, 256) + 256;
+    const size_t an_bytes = 2 * rup(m * 4, 256) + 2 * rup(n * 4, 256) + rup(m, 256) + rup(n, 256) + 256;
     uint8_t* an = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, an_bytes, &st));
     if (!an) return st;
     int* rlo = reinterpret_cast<int*>(an);
-    int* clo = reinterpret_cast<int*>(an + rup(m * 4, 256));
-    uint8_t* rnf = an + rup(m * 4, 256) + rup(n * 4, 256);
+    int* rspan = reinterpret_cast<int*>(an + rup(m * 4, 256));
+    int* clo = reinterpret_cast<int*>(an + 2 * rup(m * 4, 256));
+    int* cspan = reinterpret_cast<int*>(an + 2 * rup(m * 4, 256) + rup(n * 4, 256));
+    uint8_t* rnf = an + 2 * rup(m * 4, 256) + 2 * rup(n * 4, 256);
     uint8_t* cnf = rnf + rup(m, 256);
     int* gmax = reinterpret_cast<int*>(cnf + rup(n, 256));
-    if (cudaMemsetAsync(gmax, 0, 16, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    if (cudaMemsetAsync(gmax, 0, 32, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
     if (k > 0) {
         fx_rows_kernel<<<(int)((m * 32 + 255) / 256), 256, 0, s>>>(a, rsa, csa, (int)m, (int)k, e64,
-                                                                   rlo, rnf, gmax);
-        fx_cols_kernel<<<(int)((n + 31) / 32), dim3(32, 32), 0, s>>>(b, rsb, csb, (int)k, (int)n, e64, clo,
-                                                              cnf, gmax);
+                                                                   rlo, rspan, rnf, gmax);
+        fx_cols_kernel<<<(int)((n + 31) / 32), dim3(32, 32), 0, s>>>(b, rsb, csb, (int)k, (int)n,
+                                                                      e64, clo, cspan, cnf, gmax);
     } else {
         cudaMemsetAsync(rlo, 0, m * 4, s);
         cudaMemsetAsync(clo, 0, n * 4, s);
+        cudaMemsetAsync(rspan, 0, m * 4, s);
+        cudaMemsetAsync(cspan, 0, n * 4, s);
         cudaMemsetAsync(rnf, 0, m, s);
         cudaMemsetAsync(cnf, 0, n, s);
     }
-    int g[4] = {0, 0, 0, 0};
-    if (cudaMemcpyAsync(g, gmax, 16, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+    int g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (cudaMemcpyAsync(g, gmax, 32, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess)
         return UOR_B200_DEVICE_ERROR;
     const int La = g[0] ? (g[0] + 2 + 7) / 8 : 0;
@@ -903,11 +1058,46 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         return cuda_status(cudaGetLastError());
     }
 
-    // ---- digit slices and the slice-pair product
+    // ---- lazy digits: how many low diagonals a typical cell cannot feel
+    const int G = La && Lb ? La + Lb - 1 : 0;
+    auto pairs_on = [&](int d) {
+        int c = 0;
+        for (int sa = 0; sa < La; ++sa)
+            if (d - sa >= 0 && d - sa < Lb) ++c;
+        return c;
+    };
+    int D = 0;
+    uint64_t ebound = 0;
+    if (!e64 && !o64 && beta == 0 && alpha != 0 && !any_nf && G >= 8 && k > 0 &&
+        m * n < (size_t{1} << 32)) {
+        // A cell's integer is near 2^(span_i + span_j) unless its terms cancel; take the
+        // smallest spans, minus a margin, and skip the diagonals whose whole sum stays 16
+        // bits below that cell's last significand bit.
+        const int est = (SPAN_CAP - g[3]) + (SPAN_CAP - g[4]) - 8;
+        const int lk = 64 - __builtin_clzll(static_cast<unsigned long long>(k));
+        const int nmax = La < Lb ? La : Lb;
+        const int ln = 32 - __builtin_clz(static_cast<unsigned>(nmax));
+        const int t = est - 24 - 16 - 14 - lk - ln;
+        D = t >= 0 ? t / 8 + 1 : 0;
+        if (D > G - 1) D = G - 1;
+        if (D < 3) D = 0;
+        if (D) {
+            // |R| / 256^D <= k 2^14 (n_{D-1} / 256 + n_{D-2} / 256^2 + nmax / (256^2 255)),
+            // each term rounded up.
+            const uint64_t kk = k;
+            ebound = kk * 64 * pairs_on(D - 1) + (kk * pairs_on(D - 2) + 3) / 4 +
+                     (kk * nmax + 1019) / 1020 + 1;
+        }
+    }
+
+    // ---- digit slices and the slice-pair product of diagonals d >= d_lo
     KSParams p{};
-    int npairs = 0, ngroups = 0, worst = 1;
-    if (La && Lb) {
-        for (int d = 0; d <= La + Lb - 2; ++d) {
+    int ngroups = 0, npairs = 0;
+    auto build_groups = [&](int d_lo) {
+        npairs = 0;
+        ngroups = 0;
+        int worst = 1;
+        for (int d = d_lo; d < G; ++d) {
             p.pair_begin[ngroups] = npairs;
             int cnt = 0;
             for (int sa = 0; sa < La; ++sa) {
@@ -922,36 +1112,43 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
             ++ngroups;
             if (cnt > worst) worst = cnt;
         }
-    }
-    p.pair_begin[ngroups] = npairs;
-    p.num_groups = ngroups;
-    const int num_kb = (int)((k + KS_BK - 1) / KS_BK);
-    // |digit product| <= 2^14; a diagonal of `worst` pairs must stay inside s32.
-    const int64_t lane = (int64_t)INT_MAX / ((int64_t)worst * 16384) / KS_BK;
-    p.kb_per_chunk = (int)(lane < num_kb ? lane : num_kb);
-    if (p.kb_per_chunk < 1) p.kb_per_chunk = 1;
-    p.num_chunks = num_kb ? (num_kb + p.kb_per_chunk - 1) / p.kb_per_chunk : 0;
-    p.num_kb = num_kb;
+        p.pair_begin[ngroups] = npairs;
+        p.num_groups = ngroups;
+        const int num_kb = (int)((k + KS_BK - 1) / KS_BK);
+        // |digit product| <= 2^14; a diagonal of `worst` pairs must stay inside s32.
+        const int64_t lane = (int64_t)INT_MAX / ((int64_t)worst * 16384) / KS_BK;
+        p.kb_per_chunk = (int)(lane < num_kb ? lane : num_kb);
+        if (p.kb_per_chunk < 1) p.kb_per_chunk = 1;
+        p.num_chunks = num_kb ? (num_kb + p.kb_per_chunk - 1) / p.kb_per_chunk : 0;
+        p.num_kb = num_kb;
+    };
+    build_groups(0);  // sizes the partial planes for every diagonal
+    const int all_chunks = p.num_chunks, all_groups = ngroups;
     p.m = (int)m;
     p.n = (int)n;
     p.mp = (int)ks_rows_pad(m);
     p.np = (int)rup(n, KS_BN);
     p.status = ctx->d_status;
     p.budget_ns = ctx->budget_ns;
-    const bool run_mma = npairs > 0 && num_kb > 0;
+    const bool run_mma = npairs > 0 && p.num_kb > 0;
 
+    const size_t total = m * n;
+    const uint32_t limit = (uint32_t)(total < 4096 ? total : (total / 256 > 4096 ? total / 256 : 4096));
     const size_t kp = rup(k ? k : 1, 16);
     const size_t a_bytes = run_mma ? rup((size_t)La * p.mp * kp, 256) : 0;
     const size_t b_bytes = run_mma ? rup((size_t)Lb * p.np * kp, 256) : 0;
-    const size_t part_bytes = run_mma ? rup((size_t)p.num_chunks * ngroups * m * n * 4, 256) : 0;
+    const size_t part_bytes = run_mma ? rup((size_t)all_chunks * all_groups * m * n * 4, 256) : 0;
     const size_t flag_bytes = any_nf ? rup(m * n, 256) : 0;
-    uint8_t* ws = static_cast<uint8_t*>(
-        ctx_buffer(ctx, SLOT_WS, a_bytes + b_bytes + part_bytes + flag_bytes + 256, &st));
+    const size_t list_bytes = D ? rup((size_t)limit * 4, 256) + 256 : 0;
+    uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(
+        ctx, SLOT_WS, a_bytes + b_bytes + part_bytes + flag_bytes + list_bytes + 256, &st));
     if (!ws) return st;
     int8_t* as = reinterpret_cast<int8_t*>(ws);
     int8_t* bs = reinterpret_cast<int8_t*>(ws + a_bytes);
     int32_t* part = reinterpret_cast<int32_t*>(ws + a_bytes + b_bytes);
     uint8_t* flags = any_nf ? ws + a_bytes + b_bytes + part_bytes : nullptr;
+    uint32_t* count = reinterpret_cast<uint32_t*>(ws + a_bytes + b_bytes + part_bytes + flag_bytes);
+    uint32_t* list = count + 64;
     p.partial = part;
 
     if (any_nf) {
@@ -959,37 +1156,71 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         fx_flags_kernel<<<grid, 128, 0, s>>>(a, rsa, csa, b, rsb, csb, e64, (int)m, (int)k, (int)n,
                                               rnf, cnf, flags);
     }
-    if (run_mma) {
-        const int64_t total = (int64_t)p.mp * kp;
-        const int grid = (int)(total / 256 + 1 < 148 * 32 ? total / 256 + 1 : 148 * 32);
-        fx_slice_a_kernel<<<grid, 256, 0, s>>>(as, La, p.mp, (int)kp, a, rsa, csa, e64, (int)m,
-                                               (int)k, rlo);
-        dim3 g2((unsigned)(p.np / 32), (unsigned)((kp + 31) / 32));
-        fx_slice_b_kernel<<<g2, dim3(32, 8), 0, s>>>(bs, Lb, p.np, (int)kp, b, rsb, csb, e64,
-                                                     (int)k, (int)n, clo);
+    const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+    auto full_reduce = [&]() {
+        const int rchunks = run_mma ? p.num_chunks : 0, rgroups = run_mma ? ngroups : 0;
+        // Groups are at most 2 * FX_MAX_DIGITS - 1 = 31.
+        if (rgroups <= 8)
+            fx_reduce_kernel<8><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+        else if (rgroups <= 16)
+            fx_reduce_kernel<16><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+        else if (rgroups <= 24)
+            fx_reduce_kernel<24><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+        else
+            fx_reduce_kernel<32><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+        return cuda_status(cudaGetLastError());
+    };
+    if (!run_mma) return full_reduce();
+
+    const int64_t atotal = (int64_t)p.mp * kp;
+    const int sgrid = (int)(atotal / 256 + 1 < 148 * 32 ? atotal / 256 + 1 : 148 * 32);
+    fx_slice_a_kernel<<<sgrid, 256, 0, s>>>(as, La, p.mp, (int)kp, a, rsa, csa, e64, (int)m, (int)k,
+                                            rlo);
+    dim3 g2((unsigned)(p.np / 32), (unsigned)((kp + 31) / 32));
+    fx_slice_b_kernel<<<g2, dim3(32, 8), 0, s>>>(bs, Lb, p.np, (int)kp, b, rsb, csb, e64, (int)k,
+                                                 (int)n, clo);
+    if (route) {
+        route->a_layout = (uint32_t)La;  // digits per A element
+        route->b_layout = (uint32_t)Lb;
+        route->tile_m = (uint32_t)(m > 128 ? 256 : KS_BM);
+    }
+    auto run_pairs = [&](int d_lo) {
+        build_groups(d_lo);
         if (route) {
             route->k_chunks = (uint32_t)p.num_chunks;
-            route->a_layout = (uint32_t)La;  // digits per A element
-            route->b_layout = (uint32_t)Lb;
-            route->tile_m = (uint32_t)(m > 128 ? 256 : KS_BM);
+            route->pairs = (uint32_t)npairs;
         }
-        if ((st = ks_run(as, La, bs, Lb, k, kp, p, ctx->sm_count, s,
-                         route ? &route->ctas : nullptr)) != UOR_B200_OK)
-            return st;
+        return ks_run(as, La, bs, Lb, k, kp, p, ctx->sm_count, s, route ? &route->ctas : nullptr);
+    };
+    if (D == 0) {
+        if ((st = run_pairs(0)) != UOR_B200_OK) return st;
+        return full_reduce();
     }
-    const size_t total = m * n;
-    const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-    const int rchunks = run_mma ? p.num_chunks : 0, rgroups = run_mma ? ngroups : 0;
-    // Groups are at most 2 * FX_MAX_DIGITS - 1 = 31.
-    if (rgroups <= 8)
-        fx_reduce_kernel<8><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
-    else if (rgroups <= 16)
-        fx_reduce_kernel<16><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
-    else if (rgroups <= 24)
-        fx_reduce_kernel<24><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
+
+    // Lazy: the top diagonals, the interval test per cell, exact recomputation of the rest.
+    if ((st = run_pairs(D)) != UOR_B200_OK) return st;
+    if (cudaMemsetAsync(count, 0, 4, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    if (ngroups <= 8)
+        fx_reduce_lazy_kernel<8><<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, (int)m, (int)n, rlo, clo, rspan, cspan, D, ebound, e, list, count, limit);
+    else if (ngroups <= 16)
+        fx_reduce_lazy_kernel<16><<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, (int)m, (int)n, rlo, clo, rspan, cspan, D, ebound, e, list, count, limit);
     else
-        fx_reduce_kernel<32><<<rgrid, 256, 0, s>>>(part, rchunks, rgroups, (int)m, (int)n, rlo, clo, flags, e);
-    return cuda_status(cudaGetLastError());
+        fx_reduce_lazy_kernel<24><<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, (int)m, (int)n, rlo, clo, rspan, cspan, D, ebound, e, list, count, limit);
+    uint32_t unsure = 0;
+    if (cudaMemcpyAsync(&unsure, count, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return UOR_B200_DEVICE_ERROR;
+    if (route) route->fixups = unsure;
+    if (unsure == 0) return UOR_B200_OK;
+    if (unsure <= limit) {
+        const uint32_t warps = unsure < 148u * 64u ? unsure : 148u * 64u;
+        fx_fix_kernel<<<(warps + 7) / 8, 256, 0, s>>>(list, count, limit, as, La, p.mp, bs, Lb, p.np,
+                                                      (int)kp, (int)n, rlo, clo, e);
+        return cuda_status(cudaGetLastError());
+    }
+    // Too many cells cancel: every diagonal on the tensor cores after all.
+    if ((st = run_pairs(0)) != UOR_B200_OK) return st;
+    return full_reduce();
 }
 
 }  // namespace uor

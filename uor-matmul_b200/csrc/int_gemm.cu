@@ -138,6 +138,7 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
         route->tile_m = (uint32_t)bm;
         route->k_chunks = (uint32_t)chunks;
         route->ctas = (uint32_t)grid;
+        route->pairs = 1;
     }
 
     if (!chunked) {

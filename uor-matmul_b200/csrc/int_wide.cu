@@ -341,6 +341,7 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
         launch_slicing<8>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
     if (route) route->kernel = UOR_B200_KERNEL_LIMB_TCGEN05;
     if (route) route->k_chunks = (uint32_t)p.num_chunks;
+    if (route) route->pairs = (uint32_t)npairs;
     if ((st = ks_run(as, L, bs, L, k, kp, p, ctx->sm_count, s, route ? &route->ctas : nullptr)) !=
         UOR_B200_OK)
         return st;

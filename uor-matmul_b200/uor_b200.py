@@ -54,7 +54,8 @@ class Route(ctypes.Structure):
     _fields_ = [("kernel", ctypes.c_uint32), ("tile_m", ctypes.c_uint32),
                 ("tile_n", ctypes.c_uint32), ("tile_k", ctypes.c_uint32),
                 ("k_chunks", ctypes.c_uint32), ("a_layout", ctypes.c_uint32),
-                ("b_layout", ctypes.c_uint32), ("ctas", ctypes.c_uint32)]
+                ("b_layout", ctypes.c_uint32), ("ctas", ctypes.c_uint32),
+                ("pairs", ctypes.c_uint32), ("fixups", ctypes.c_uint32)]
 
     def as_dict(self):
         d = {f: getattr(self, f) for f, _ in self._fields_}
