@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < K5_STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(dec0 + 8 * s, K5_DEC_WARPS);
+            mbar_init(dec0 + 8 * s, K5_DEC_WARPS / 2);  // one decoder group per stage
             mbar_init(empty0 + 8 * s, 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -223,37 +223,44 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
         }
     } else {
         // ------------------------------------------------------------ decoders
-        const int dt = threadIdx.x - 6 * 32;  // 0 .. 32 * K5_DEC_WARPS - 1
+        // Two groups of K5_DEC_WARPS / 2 warps take alternate stages, so two stages are
+        // decoded at once while the MMA consumes a third.
+        constexpr int GW = K5_DEC_WARPS / 2;
+        const int grp = (warp - 6) / GW;
+        const int dt = threadIdx.x - (6 + grp * GW) * 32;  // 0 .. 32 * GW - 1
         const uint32_t t0 = p.table[0], t1 = p.table[1], t2 = p.table[2], t3 = p.table[3];
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
+        int it = 0;
         for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                if (!mbar_wait_warp(full0 + 8 * stage, phase, p.budget_ns, p.status,
-                                    KERR_TIMEOUT_MMA_FULL)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t* sw = smem + stage * K5_STAGE_BYTES;
-                const uint8_t* sc = sw + K5_W_BYTES + K5_X_BYTES;
-                // 128 code rows x 8 groups of 8 bytes; each group decodes to one
-                // swizzled 16-byte unit: row r, unit q lands at r*128 + ((q ^ (r&7)) * 16).
+            for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                if ((it & 1) == grp) {
+                    if (!mbar_wait_warp(full0 + 8 * stage, phase, p.budget_ns, p.status,
+                                        KERR_TIMEOUT_MMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sw = smem + stage * K5_STAGE_BYTES;
+                    const uint8_t* sc = sw + K5_W_BYTES + K5_X_BYTES;
+                    // 128 code rows x 8 groups of 8 bytes; each group decodes to one
+                    // swizzled 16-byte unit: row r, unit q lands at r*128 + ((q ^ (r&7)) * 16).
 #pragma unroll
-                for (int rep = 0; rep < (128 * 8) / (32 * K5_DEC_WARPS); ++rep) {
-                    const int u = dt + rep * 32 * K5_DEC_WARPS;
-                    const int r = u >> 3, q = u & 7;
-                    const uint2 cw = *reinterpret_cast<const uint2*>(sc + r * 64 + q * 8);
-                    uint4 o;
-                    o.x = dec4(cw.x & 0xFFFFu, t0, t1, t2, t3);
-                    o.y = dec4(cw.x >> 16, t0, t1, t2, t3);
-                    o.z = dec4(cw.y & 0xFFFFu, t0, t1, t2, t3);
-                    o.w = dec4(cw.y >> 16, t0, t1, t2, t3);
-                    *reinterpret_cast<uint4*>(sw + r * 128 + ((q ^ (r & 7)) << 4)) = o;
+                    for (int rep = 0; rep < (128 * 8) / (32 * GW); ++rep) {
+                        const int u = dt + rep * 32 * GW;
+                        const int r = u >> 3, q = u & 7;
+                        const uint2 cw = *reinterpret_cast<const uint2*>(sc + r * 64 + q * 8);
+                        uint4 o;
+                        o.x = dec4(cw.x & 0xFFFFu, t0, t1, t2, t3);
+                        o.y = dec4(cw.x >> 16, t0, t1, t2, t3);
+                        o.z = dec4(cw.y & 0xFFFFu, t0, t1, t2, t3);
+                        o.w = dec4(cw.y >> 16, t0, t1, t2, t3);
+                        *reinterpret_cast<uint4*>(sw + r * 128 + ((q ^ (r & 7)) << 4)) = o;
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(dec0 + 8 * stage);
                 }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(dec0 + 8 * stage);
                 if (++stage == K5_STAGES) stage = 0, phase ^= 1;
             }
         }
