@@ -11,7 +11,7 @@
 // Per stage: TMA brings 8 KiB of raw codes (no swizzle) and 32 KiB of activations
 // (128-byte swizzle); eight decoder warps turn each 8-byte group of codes (16
 // nibbles) into 16 int8 values with byte permutes against the 16-entry table held
-// in registers, and store them straight into the swizzled operand layout
+// in registers (three permutes per four values), and store them straight into the swizzled operand layout
 // (MN-major for codes laid k x n, K-major for codes laid n x k -- the same index
 // arithmetic either way). fence.proxy.async makes those stores visible to the
 // tensor core. The accumulator is the transposed tile C^T; lanes map to consecutive
@@ -31,14 +31,19 @@ __device__ __forceinline__ void k5_tile(int t, const K5Params& p, int& tj, int& 
     ti = r / rows;
 }
 
-// Four nibbles (low 16 bits, first element lowest) -> four table bytes.
-__device__ __forceinline__ uint32_t dec4(uint32_t g, uint32_t t0, uint32_t t1, uint32_t t2,
-                                         uint32_t t3) {
-    const uint32_t sel = g & 0x7777u;
-    const uint32_t lo = __byte_perm(t0, t1, sel);
-    const uint32_t hi = __byte_perm(t2, t3, sel);
-    const uint32_t mk = __byte_perm(0u, 0xFFFFFFFFu, (g >> 1) & 0x4444u);
-    return (lo & ~mk) | (hi & mk);
+// Eight nibbles (first element lowest) -> eight table bytes (.x: elements 0-3, .y: 4-7).
+// __byte_perm reads three bits of each selector nibble (and only the low 16 bits of the
+// selector), so the code nibbles themselves pick among table[0..7] (t0:t1) and
+// table[8..15] (t2:t3); a third permute takes, byte by byte, the half that the
+// nibble's bit 3 names.
+__device__ __forceinline__ uint2 dec8(uint32_t w, uint32_t t0, uint32_t t1, uint32_t t2,
+                                     uint32_t t3) {
+    const uint32_t pick = ((w >> 1) & 0x44444444u) | 0x32103210u;
+    const uint32_t wh = w >> 16, ph = pick >> 16;
+    uint2 r;
+    r.x = __byte_perm(__byte_perm(t0, t1, w), __byte_perm(t2, t3, w), pick);
+    r.y = __byte_perm(__byte_perm(t0, t1, wh), __byte_perm(t2, t3, wh), ph);
+    return r;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -250,11 +255,9 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
                         const int u = dt + rep * 32 * GW;
                         const int r = u >> 3, q = u & 7;
                         const uint2 cw = *reinterpret_cast<const uint2*>(sc + r * 64 + q * 8);
-                        uint4 o;
-                        o.x = dec4(cw.x & 0xFFFFu, t0, t1, t2, t3);
-                        o.y = dec4(cw.x >> 16, t0, t1, t2, t3);
-                        o.z = dec4(cw.y & 0xFFFFu, t0, t1, t2, t3);
-                        o.w = dec4(cw.y >> 16, t0, t1, t2, t3);
+                        const uint2 d0 = dec8(cw.x, t0, t1, t2, t3);
+                        const uint2 d1 = dec8(cw.y, t0, t1, t2, t3);
+                        const uint4 o = make_uint4(d0.x, d0.y, d1.x, d1.y);
                         *reinterpret_cast<uint4*>(sw + r * 128 + ((q ^ (r & 7)) << 4)) = o;
                     }
                     fence_proxy_async_smem();
