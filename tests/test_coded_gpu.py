@@ -70,10 +70,11 @@ def test_fused_nibbles(orientation, shape):
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
-def test_short_table_alpha_beta_outputs(orientation):
+@pytest.mark.parametrize("m", [70, 260])  # one CTA per tile / CTA pairs
+def test_short_table_alpha_beta_outputs(orientation, m):
     for out in (U.I8, U.I32, U.I64, U.I128):
         for alpha, beta, mode in [(3, -1, U.NEAREST), (-(2**63), 2**62, U.WRAPPING)]:
-            got, want, _ = run(70, 96, 64, 2, 7, orientation, out, alpha, beta, mode, seed=out)
+            got, want, _ = run(m, 96, 64, 2, 7, orientation, out, alpha, beta, mode, seed=out)
             assert (got == want) if out == U.I128 else np.array_equal(got, want), (out, alpha)
 
 
