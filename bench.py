@@ -502,13 +502,14 @@ def wl_trop(args, U, torch, rank):
     w.flush = False
 
     def roofline(avg_ms):
-        # one packed 16x2 add and one packed 16x2 max per two terms and lane
-        peak = 148 * 128 * 1.965e9 / 1e12
+        # one fused packed i16x2 add-max per two terms; the ALU pipe takes a packed 16x2
+        # instruction from 64 lanes per SM and clock
+        peak = 148 * 64 * 2 * 1.965e9 / 1e12
         ach = w.units / (avg_ms / 1e3) / 1e12
         return {"bound": "alu", "achieved": ach, "peak": peak, "unit": "Tterm/s",
                 "frac": ach / peak,
-                "peak_source": "nominal: 148 SMs x 128 lanes x 1.965 GHz, one packed i16x2 "
-                               "instruction per lane and clock, 2 instructions per 2 terms",
+                "peak_source": "nominal: 148 SMs x 64 lanes/clk (packed i16x2 ALU rate) x 2 "
+                               "terms per fused add-max x 1.965 GHz",
                 "traffic": None, "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
