@@ -560,51 +560,98 @@ __device__ __forceinline__ i128 fx_scaled(const FDec& d, int lo) {
     return d.sign ? -v : v;
 }
 
+// Balanced digits from plain bytes: with C_L = sum_{s<L} 128 256^s, x + C_L lies in
+// [0, 256^L) whenever x has an L-digit balanced form, and its byte s is d_s + 128; so digit
+// s is byte s of the unsigned 128-bit x + C_L with its top bit flipped.
+__device__ __forceinline__ void fx_biased(const FDec& d, int lo, u128 cl, uint64_t& ylo,
+                                          uint64_t& yhi) {
+    const u128 y = static_cast<u128>(fx_scaled(d, lo)) + cl;
+    ylo = static_cast<uint64_t>(y);
+    yhi = static_cast<uint64_t>(y >> 64);
+}
+
+// Byte s of four biased values, packed little-endian, as four digits.
+__device__ __forceinline__ uint32_t fx_pack_digits(const uint64_t (&lo)[4], const uint64_t (&hi)[4],
+                                                   int s) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint64_t v = s < 8 ? lo[c] >> (8 * s) : hi[c] >> (8 * (s - 8));
+        w |= static_cast<uint32_t>(v & 255u) << (8 * c);
+    }
+    return w ^ 0x80808080u;
+}
+
+// A (m x k) -> As[L][mp][kp]: four consecutive reduction positions per thread, one 4-byte
+// store per digit plane.
 __global__ void fx_slice_a_kernel(int8_t* __restrict__ as, int L, int mp, int kp,
                                   const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
-                                  bool f64, int m, int k, const int* __restrict__ lo) {
+                                  bool f64, int m, int k, const int* __restrict__ lo, u128 cl) {
+    const int qpr = kp >> 2;
+    const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < plane;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(idx / kp), p = static_cast<int>(idx % kp);
-        i128 x = 0;
-        if (i < m && p < k)
-            x = fx_scaled(fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, f64),
-                          lo[i]);
-        for (int s = 0; s < L; ++s) {
-            const int dgt = (static_cast<int>(static_cast<uint64_t>(x) & 255) ^ 128) - 128;
-            as[s * plane + idx] = static_cast<int8_t>(dgt);
-            x = (x - dgt) >> 8;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(t / qpr);
+        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+        uint64_t ylo[4], yhi[4];
+        const int li = i < m ? lo[i] : 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int p = p0 + c;
+            FDec d{};
+            d.kind = 0;
+            d.mant = 0;
+            if (i < m && p < k)
+                d = fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, f64);
+            fx_biased(d, li, cl, ylo[c], yhi[c]);
         }
+        int8_t* dst = as + static_cast<int64_t>(i) * kp + p0;
+#pragma unroll
+        for (int s = 0; s < 16; ++s)
+            if (s < L) *reinterpret_cast<uint32_t*>(dst + s * plane) = fx_pack_digits(ylo, yhi, s);
     }
 }
 
+// B (k x n) -> Bs[L][np][kp] (transposed) through a shared tile of 64 reduction positions x
+// 32 columns of biased values.
 __global__ void fx_slice_b_kernel(int8_t* __restrict__ bs, int L, int np, int kp,
                                   const uint8_t* __restrict__ b, int64_t rsb, int64_t csb,
-                                  bool f64, int k, int n, const int* __restrict__ lo) {
-    __shared__ i128 tile[32][33];
-    const int p0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
-    const int tx = threadIdx.x, ty = threadIdx.y;
-    for (int r = ty; r < 32; r += 8) {
-        const int p = p0 + r, j = j0 + tx;
-        i128 x = 0;
-        if (p < k && j < n)
-            x = fx_scaled(fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64),
-                          lo[j]);
-        tile[r][tx] = x;
-    }
-    __syncthreads();
+                                  bool f64, int k, int n, const int* __restrict__ lo, u128 cl) {
+    __shared__ uint64_t tlo[32][65], thi[32][65];
+    const int j0 = blockIdx.x * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     const int64_t plane = static_cast<int64_t>(np) * kp;
-    for (int r = ty; r < 32; r += 8) {
-        const int j = j0 + r, p = p0 + tx;
-        if (j < np && p < kp) {
-            i128 x = tile[tx][r];
-            for (int s = 0; s < L; ++s) {
-                const int dgt = (static_cast<int>(static_cast<uint64_t>(x) & 255) ^ 128) - 128;
-                bs[s * plane + static_cast<int64_t>(j) * kp + p] = static_cast<int8_t>(dgt);
-                x = (x - dgt) >> 8;
+    const int lj = j0 + tx < n ? lo[j0 + tx] : 0;
+    for (int p0 = blockIdx.y * 64; p0 < kp; p0 += gridDim.y * 64) {
+        for (int r = ty; r < 64; r += 8) {
+            const int p = p0 + r, j = j0 + tx;
+            FDec d{};
+            d.kind = 0;
+            d.mant = 0;
+            if (p < k && j < n)
+                d = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64);
+            fx_biased(d, lj, cl, tlo[tx][r], thi[tx][r]);
+        }
+        __syncthreads();
+        // 32 columns x 16 quads of reduction positions: two (column, quad) items per thread.
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int item = (ty * 2 + h) * 32 + tx;  // 0 .. 511
+            const int jj = item >> 4, q = item & 15;
+            const int j = j0 + jj, p = p0 + 4 * q;
+            if (j < np && p < kp) {
+                const uint64_t vlo[4] = {tlo[jj][4 * q], tlo[jj][4 * q + 1], tlo[jj][4 * q + 2],
+                                         tlo[jj][4 * q + 3]};
+                const uint64_t vhi[4] = {thi[jj][4 * q], thi[jj][4 * q + 1], thi[jj][4 * q + 2],
+                                         thi[jj][4 * q + 3]};
+                int8_t* dst = bs + static_cast<int64_t>(j) * kp + p;
+#pragma unroll
+                for (int s = 0; s < 16; ++s)
+                    if (s < L) *reinterpret_cast<uint32_t*>(dst + s * plane) = fx_pack_digits(vlo, vhi, s);
             }
         }
+        __syncthreads();
     }
 }
 
@@ -1172,13 +1219,18 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
     };
     if (!run_mma) return full_reduce();
 
-    const int64_t atotal = (int64_t)p.mp * kp;
-    const int sgrid = (int)(atotal / 256 + 1 < 148 * 32 ? atotal / 256 + 1 : 148 * 32);
+    auto bias = [](int L) {  // sum_{s<L} 128 256^s
+        u128 c = 0;
+        for (int q = 0; q < L; ++q) c |= static_cast<u128>(0x80) << (8 * q);
+        return c;
+    };
+    const int64_t aquads = (int64_t)p.mp * (kp / 4);
+    const int sgrid = (int)(aquads / 256 + 1 < 148 * 16 ? aquads / 256 + 1 : 148 * 16);
     fx_slice_a_kernel<<<sgrid, 256, 0, s>>>(as, La, p.mp, (int)kp, a, rsa, csa, e64, (int)m, (int)k,
-                                            rlo);
-    dim3 g2((unsigned)(p.np / 32), (unsigned)((kp + 31) / 32));
+                                            rlo, bias(La));
+    dim3 g2((unsigned)(p.np / 32), (unsigned)((kp + 63) / 64 < 65535 ? (kp + 63) / 64 : 65535));
     fx_slice_b_kernel<<<g2, dim3(32, 8), 0, s>>>(bs, Lb, p.np, (int)kp, b, rsb, csb, e64, (int)k,
-                                                 (int)n, clo);
+                                                 (int)n, clo, bias(Lb));
     if (route) {
         route->a_layout = (uint32_t)La;  // digits per A element
         route->b_layout = (uint32_t)Lb;
