@@ -773,6 +773,61 @@ __global__ void fx_reduce_kernel(const int32_t* __restrict__ part, int chunks, i
 // same bits, so does the exact alpha X; every other cell is listed and recomputed
 // exactly, all diagonals, from the digit slices (fx_fix_kernel).
 
+// encode_mag_fast for a magnitude below 2^128: the same steps in native 128-bit shifts.
+__device__ __forceinline__ uint64_t encode_u128(u128 mag, bool neg, int unit_exp, bool out64,
+                                                int mode, int min_exp_e) {
+    const int MANT = out64 ? 52 : 23, EXPO = out64 ? 11 : 8;
+    const int P = MANT + 1;
+    const int BIAS = (1 << (EXPO - 1)) - 1;
+    const int SUB = 1 - BIAS - MANT;
+    const uint64_t sign_bit = out64 ? (1ull << 63) : (1ull << 31);
+    const uint64_t exp_all = (1ull << EXPO) - 1;
+    const uint64_t hi = static_cast<uint64_t>(mag >> 64), lo64 = static_cast<uint64_t>(mag);
+    const int bl = hi ? 128 - __clzll(static_cast<long long>(hi))
+                      : (lo64 ? 64 - __clzll(static_cast<long long>(lo64)) : 0);
+    if (bl == 0) return 0;
+    const int exp = unit_exp + bl - 1;
+    int lsb_exp = exp - (P - 1) < SUB ? SUB : exp - (P - 1);
+    if (lsb_exp - min_exp_e < 0) return 0;
+    const int lsb = lsb_exp - unit_exp;
+    uint64_t sig;
+    bool round_bit = false, sticky = false;
+    if (lsb <= 0) {
+        sig = static_cast<uint64_t>(mag << (-lsb));  // exact: fewer than P bits
+    } else if (lsb >= 128) {
+        sig = 0;
+        if (lsb_exp - min_exp_e != 0) {
+            round_bit = lsb == 128 && (mag >> 127) != 0;
+            sticky = lsb == 128 ? (mag & ((static_cast<u128>(1) << 127) - 1)) != 0 : mag != 0;
+        }
+    } else {
+        sig = static_cast<uint64_t>(mag >> lsb) & ((1ull << P) - 1);
+        if (lsb_exp - min_exp_e != 0) {
+            round_bit = ((mag >> (lsb - 1)) & 1) != 0;
+            sticky = lsb >= 2 && (mag & ((static_cast<u128>(1) << (lsb - 1)) - 1)) != 0;
+        }
+    }
+    const bool inc = mode == MODE_NEAREST && round_bit && (sticky || (sig & 1));
+    sig += inc ? 1 : 0;
+    if (sig >> P) {
+        sig >>= 1;
+        lsb_exp += 1;
+    }
+    const uint64_t s = neg ? sign_bit : 0;
+    if (sig == 0) return s;
+    const int top = 63 - __clzll(static_cast<long long>(sig));
+    const int value_exp = lsb_exp + top;
+    if ((sig >> (P - 1)) == 1) {
+        const int biased = value_exp + BIAS;
+        if (biased >= static_cast<int>(exp_all)) {
+            if (mode == MODE_NEAREST) return s | (exp_all << MANT);
+            return s | ((exp_all - 1) << MANT) | ((1ull << MANT) - 1);
+        }
+        return s | (static_cast<uint64_t>(biased) << MANT) | (sig & ((1ull << MANT) - 1));
+    }
+    return s | sig;
+}
+
 template <int NW>
 __device__ __forceinline__ uint64_t encode_signed_scaled(uint64_t (&w)[NW], int64_t alpha, int ex,
                                                          const FxEpi& e) {
@@ -845,8 +900,25 @@ __global__ void fx_reduce_lazy_kernel(const int32_t* __restrict__ part, int chun
         lo[NQ + 1] = carry_lo < 0 ? ~0ull : 0ull;
         hi[NQ + 1] = carry_hi < 0 ? ~0ull : 0ull;
         const int ex = rlo[i] + clo[j] + 8 * D;
-        const uint64_t blo = encode_signed_scaled<NW>(lo, e.alpha, ex, e);
-        const uint64_t bhi = encode_signed_scaled<NW>(hi, e.alpha, ex, e);
+        uint64_t blo, bhi;
+        bool small = e.alpha == 1;
+#pragma unroll
+        for (int q = 2; q < NW; ++q) {
+            small = small && lo[q] == static_cast<uint64_t>(static_cast<int64_t>(lo[1]) >> 63) &&
+                    hi[q] == static_cast<uint64_t>(static_cast<int64_t>(hi[1]) >> 63);
+        }
+        if (small) {
+            // Both ends fit 128 bits (the common case): native arithmetic.
+            const i128 vl = static_cast<i128>((static_cast<u128>(lo[1]) << 64) | lo[0]);
+            const i128 vh = static_cast<i128>((static_cast<u128>(hi[1]) << 64) | hi[0]);
+            const u128 ml = vl < 0 ? static_cast<u128>(0) - static_cast<u128>(vl) : static_cast<u128>(vl);
+            const u128 mh = vh < 0 ? static_cast<u128>(0) - static_cast<u128>(vh) : static_cast<u128>(vh);
+            blo = encode_u128(ml, vl < 0, ex, e.out64, e.mode, e.min_exp_e);
+            bhi = encode_u128(mh, vh < 0, ex, e.out64, e.mode, e.min_exp_e);
+        } else {
+            blo = encode_signed_scaled<NW>(lo, e.alpha, ex, e);
+            bhi = encode_signed_scaled<NW>(hi, e.alpha, ex, e);
+        }
         if (blo == bhi) {
             store_float(e.c, e.out64, off, blo);
         } else {
