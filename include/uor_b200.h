@@ -102,7 +102,8 @@ typedef enum uor_b200_kernel {
     UOR_B200_KERNEL_TROPICAL = 3,      /* K4: packed max-plus on CUDA cores */
     UOR_B200_KERNEL_CODED_TCGEN05 = 4, /* K5: codebook decode feeding K1's MMA */
     UOR_B200_KERNEL_FLOAT_EXACT = 5,   /* K6+K7: exact float, one rounding */
-    UOR_B200_KERNEL_EPILOGUE_ONLY = 6  /* k == 0: C := encode(beta * C) */
+    UOR_B200_KERNEL_EPILOGUE_ONLY = 6, /* k == 0: C := encode(beta * C) */
+    UOR_B200_KERNEL_SKINNY = 7         /* <= 16 rows or columns: dp4a reduce / column kernels */
 } uor_b200_kernel;
 
 typedef struct uor_b200_route {

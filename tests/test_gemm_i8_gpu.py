@@ -173,7 +173,7 @@ def test_depth_past_the_lane_is_exact():
     route = U.Route()
     U.slice_gemm_ex(U.I8, U.I64, 1, k, 1, 1, a, k, b, 1, 0, c, 1, route=route)
     assert c[0] == k * 128 * 128
-    assert route.k_chunks == 2
+    assert route.k_chunks >= 2  # chunked within the s32 lane depth (skinny dp4a route here)
     # and a random deep product against the oracle, saturating into i32
     m, n, k = 6, 10, 140_000
     a, b = i8(13, m * k), i8(14, k * n)

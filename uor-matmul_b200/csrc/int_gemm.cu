@@ -50,6 +50,10 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
         if (route) route->kernel = UOR_B200_KERNEL_EPILOGUE_ONLY;
         return cuda_status(epilogue_only(c, rsc, csc, m, n, epi, s));
     }
+    if (i8_skinny_applies(m, k, n)) {
+        const int st = run_i8_skinny(ctx, a, rsa, csa, b, rsb, csb, c, rsc, csc, m, k, n, epi, route);
+        if (st != UOR_B200_UNSUPPORTED) return st;
+    }
 
     // ---- operand layouts
     uint64_t a_stride = 0, b_stride = 0;

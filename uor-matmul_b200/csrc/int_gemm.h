@@ -21,6 +21,14 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
                   ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
                   uor_b200_route* route);
 
+// Products with at most 16 rows or columns (k > 0): dp4a kernels on CUDA cores that
+// keep every SM busy where a tensor-core tile would be mostly padding. Returns
+// UOR_B200_UNSUPPORTED when the operands' layout suits neither factorization.
+bool i8_skinny_applies(size_t m, size_t k, size_t n);
+int run_i8_skinny(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa, const int8_t* b,
+                  ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc, ptrdiff_t csc, size_t m,
+                  size_t k, size_t n, const LinearEpi& epi, uor_b200_route* route);
+
 struct Operand;
 
 // Host-pointer i8 GEMM with the copies pipelined against the compute (row-major

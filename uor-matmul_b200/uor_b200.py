@@ -25,7 +25,7 @@ NEAREST, TOWARD_ZERO, SATURATING, WRAPPING = range(4)
 I8, I16, I32, I64, I128, F32, F64, TROP_I8, TROP_I16, TROP_I32, TROP_I64 = range(1, 12)
 DEVICE_POINTERS, ASYNC = 1, 2
 KERNEL_NAMES = {0: "none", 1: "i8_tcgen05", 2: "limb_tcgen05", 3: "tropical",
-                4: "coded_tcgen05", 5: "float_exact", 6: "epilogue_only"}
+                4: "coded_tcgen05", 5: "float_exact", 6: "epilogue_only", 7: "skinny_dp4a"}
 
 DTYPE_SIZE = {I8: 1, I16: 2, I32: 4, I64: 8, I128: 16, F32: 4, F64: 8,
               TROP_I8: 2, TROP_I16: 4, TROP_I32: 8, TROP_I64: 16}
