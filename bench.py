@@ -16,7 +16,8 @@ L2: three rotating operand sets (3 x 128 MiB > the 126 MB L2) plus a 256 MiB
 output written every step, so no step reads operands a previous step left in L2.
 
 --workload selects the other BASELINE configs for their own measurement lines
-(i8-512: configs[0]; codec: configs[1]; f32: configs[2]; wide: configs[3];
+(i8-512: configs[0]; gemv / gemv-t: the narrow-side kernels at 1 x 8192 x 8192 and
+8192 x 8192 x 1; codec: configs[1]; f32: configs[2]; wide: configs[3];
 wide-splitk: configs[3] with the reduction split across ranks and one NCCL
 all-reduce of exact limbs, strong scaling; trop: configs[4]'s max-plus half). They
 are opt-in; the driver's line is the default.
@@ -40,7 +41,7 @@ sys.path.insert(0, ROOT)
 
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
-WORKLOADS = ("i8", "i8-512", "codec", "f32", "wide", "wide-splitk", "trop")
+WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "f32", "wide", "wide-splitk", "trop")
 
 
 def parse():
@@ -158,7 +159,8 @@ def wl_i8(args, U, torch, rank, size, sets=3):
     B = [torch.from_numpy(U.corpus(2 + 100 * s + 1000 * rank, U.CORPUS_I8, k * n)).cuda()
          for s in range(sets)]
     C = torch.empty(m * n, dtype=torch.int32, device="cuda")
-    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=1)
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=1,
+                        graph_sets=sets if size < 2048 else 0)
 
     def step(i, ctx):
         U.gemm_i8_i32(m, k, n, A[i % sets], B[i % sets], C, ctx=ctx, route=w.route,
@@ -218,6 +220,79 @@ def wl_i8(args, U, torch, rank, size, sets=3):
                 "frac": ach / peak, "peak_source": src,
                 "frac_of_nominal_4500": ach / 4500.0,
                 "traffic": w.traffic, "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_gemv(args, U, torch, rank, thin_m, sets=3):
+    """The narrow-side shapes of the reduce factorization (spec.rs:474-526): 1 x 8192 x 8192
+    (thin_m, the column kernel) or 8192 x 8192 x 1 (the reduce kernel); HBM-bound: the long
+    operand is read once."""
+    import numpy as np
+    m, k, n = (1, 8192, 8192) if thin_m else (8192, 8192, 1)
+    A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() for s in range(sets)]
+    B = [torch.from_numpy(U.corpus(2 + 100 * s + 1000 * rank, U.CORPUS_I8, k * n)).cuda()
+         for s in range(sets)]
+    C = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    # the dp4a kernel and the exact chunk fold
+    # units scaled so that measure()'s units/s/1e12 reads GB/s
+    w = SimpleNamespace(route=U.Route(), units=float(m * k + k * n + 4 * m * n) * 1e3, launches=1,
+                        graph_sets=sets)
+
+    def step(i, ctx):
+        U.gemm_i8_i32(m, k, n, A[i % sets], B[i % sets], C, ctx=ctx, route=w.route,
+                      asynchronous=True)
+
+    def check(last):
+        s = last % sets
+        want = (A[s].view(m, k).double() @ B[s].view(k, n).double()).reshape(-1)
+        assert torch.equal(C.double(), want), "GEMV differs from the f64 product (exact here)"
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, b = A[0].cpu().numpy(), B[0].cpu().numpy()
+        threads = orc.max_threads()
+        c = np.zeros(m * n, np.int32)
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            orc.gemm_i8_blocked(a, b, c, m, k, n, threads=threads)
+            reps += 1
+            dt = time.perf_counter() - t0
+            if dt > budget_s / 4:
+                break
+        assert np.array_equal(c, C.cpu().numpy()), "GPU result differs from the oracle"
+        return {"value": reps * w.units / dt / 1e12, "unit": "GB/s", "cores": threads,
+                "kind": "port",
+                "sample": f"the whole {m}x{k}x{n} product, {reps} times ({dt:.2f} s), blocked C "
+                          "restatement; the GPU result was compared bit for bit"}
+
+    def e2e(steps, ctx, stream):
+        Ah, Bh = A[0].cpu().pin_memory(), B[0].cpu().pin_memory()
+        Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
+        return timed_host(lambda: U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx), steps, stream,
+                          m * k + k * n, 4 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = f"exact i8 GEMV GB/s, {m}x{k}x{n} (bit-exact, int32 out)"
+    w.unit, w.dtype = "GB/s", "int8 (dp4a)"
+    w.config = {"workload": f"i8 x i8 -> i32 {m}x{k}x{n} per GPU (narrow side: "
+                            f"{'column' if thin_m else 'reduce'} kernel), column-block sharded",
+                "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = f"{sets} rotating operand sets ({sets * (m * k + k * n) >> 20} MiB, > L2)"
+    w.algorithmic_bytes = m * k + k * n + 4 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        try:
+            peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]
+            src = "measured copy bandwidth (MEASURED_PEAKS.json hbm_gbs), of measured"
+        except Exception:
+            peak, src = 6650.0, "fallback 6.65 TB/s, of fallback"
+        ach = w.algorithmic_bytes / (avg_ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                "peak_source": src, "traffic": None, "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
 
@@ -569,6 +644,10 @@ def build_workload(name, args, U, torch, rank, world=1):
         return wl_i8(args, U, torch, rank, args.size or SIZE)
     if name == "i8-512":
         return wl_i8(args, U, torch, rank, args.size or 512, sets=1)
+    if name == "gemv":
+        return wl_gemv(args, U, torch, rank, True)
+    if name == "gemv-t":
+        return wl_gemv(args, U, torch, rank, False)
     if name == "codec":
         return wl_codec(args, U, torch, rank)
     if name == "f32":
@@ -604,6 +683,24 @@ def time_steps(w, ctx, stream, torch, dist, steps, warmup, local):
     assert ctx.sync() == 0
     w.check(warmup - 1)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if w.flush else None
+    run = lambda i: w.step(i, ctx)  # noqa: E731
+    graphs = []
+    if getattr(w, "graph_sets", 0):
+        # Steps shorter than the host's per-call work (argument marshalling, tensor maps,
+        # the launch) are replayed from CUDA graphs of the same library call, one per
+        # operand set, so the GPU is never starved between them.
+        try:
+            for gs in range(w.graph_sets):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    w.step(gs, ctx)
+                graphs.append(g)
+            torch.cuda.synchronize()
+            run = lambda i: graphs[i % len(graphs)].replay()  # noqa: E731
+            w.graphed = True
+        except Exception as exc:  # pragma: no cover - reported in the line
+            graphs = []
+            w.graphed = f"not captured: {exc}"
     clocks = Clocks(local)
     if dist:
         dist.barrier()
@@ -618,7 +715,7 @@ def time_steps(w, ctx, stream, torch, dist, steps, warmup, local):
         if flush is not None:
             flush.fill_(i & 0xFF)  # an L2-sized write between steps, outside the step events
         ev[i][0].record(stream)
-        w.step(warmup + i, ctx)
+        run(warmup + i)
         ev[i][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
@@ -626,6 +723,7 @@ def time_steps(w, ctx, stream, torch, dist, steps, warmup, local):
         dist.barrier()
     clk = clocks.stop()
     assert ctx.sync() == 0
+    del graphs
     step_ms = [a.elapsed_time(b) for a, b in ev]
     # With an L2 flush between steps the region holds the flushes too: count the steps.
     elapsed = sum(step_ms) if flush is not None else t_start.elapsed_time(t_end)
@@ -699,6 +797,7 @@ def measure(w, args, U, torch, dist, ctx, stream, rank, world, local):
                                            f"column blocks x{world}, no data-path collective")),
         "route": w.route.as_dict(),
         "roofline": w.roofline(statistics.mean(step_ms)),
+        "cuda_graph": getattr(w, "graphed", False),
         "gpu_launches": w.launches * args.steps,
         "clocks": clk,
     }

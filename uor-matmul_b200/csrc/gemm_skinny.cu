@@ -26,15 +26,33 @@ namespace uor {
 
 constexpr int SK_MAXV = 16;
 constexpr int64_t SK_REDUCE_CHUNK_MAX = 131056;  // multiple of 16 inside one s32 lane
-constexpr int SK_COLS_KT = 512;                  // A bytes per row staged per step
-constexpr int64_t SK_COLS_CHUNK_MAX = 130048;    // multiple of SK_COLS_KT inside one lane
+constexpr int SK_COLS_KT = 256;                  // A bytes per row staged per step
+constexpr int64_t SK_COLS_CHUNK_MAX = 130816;    // multiple of SK_COLS_KT inside one lane
 constexpr int SK_COLS_THREADS = 128;             // 4 columns each: 512 columns per block
+
+// Where the partial sums go: chunk planes for reduce_chunks, or -- with one chunk -- the
+// output itself through the Linear epilogue.
+struct SkOut {
+    int32_t* part;
+    int out_rows, out_cols;
+    bool direct;
+    void* c;
+    int64_t rsc, csc;
+    LinearEpi epi;
+};
+
+__device__ __forceinline__ void sk_emit(const SkOut& o, int q, int i, int j, int32_t v) {
+    if (o.direct)
+        finish_cell(o.epi, o.c, static_cast<int64_t>(i) * o.rsc + static_cast<int64_t>(j) * o.csc, v);
+    else
+        o.part[(static_cast<size_t>(q) * o.out_rows + i) * o.out_cols + j] = v;
+}
 
 template <int NV>
 __global__ void __launch_bounds__(128)
     sk_reduce_kernel(const int8_t* __restrict__ X, int64_t ldx, int rows,
                      const int8_t* __restrict__ V, int64_t ldv, int nv, int64_t k, int64_t kchunk,
-                     int32_t* __restrict__ part, int out_rows, int out_cols, bool swap) {
+                     SkOut o, bool swap) {
     const int q = blockIdx.y;
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -46,6 +64,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int v = 0; v < NV; ++v) acc[v] = 0;
     const int64_t full = k0 + ((k1 - k0) & ~static_cast<int64_t>(15));
+#pragma unroll 4
     for (int64_t p = k0 + lane * 16; p < full; p += 512) {
         const int4 xa = *reinterpret_cast<const int4*>(xr + p);
 #pragma unroll
@@ -71,13 +90,9 @@ __global__ void __launch_bounds__(128)
         for (int o = 16; o; o >>= 1) acc[v] += __shfl_xor_sync(0xffffffffu, acc[v], o);
     }
     if (lane == 0) {
-        int32_t* pq = part + static_cast<size_t>(q) * out_rows * out_cols;
 #pragma unroll
         for (int v = 0; v < NV; ++v)
-            if (v < nv) {
-                const int i = swap ? v : r, j = swap ? r : v;
-                pq[static_cast<size_t>(i) * out_cols + j] = acc[v];
-            }
+            if (v < nv) sk_emit(o, q, swap ? v : r, swap ? r : v, acc[v]);
     }
 }
 
@@ -96,7 +111,7 @@ template <int MM>
 __global__ void __launch_bounds__(SK_COLS_THREADS)
     sk_cols_kernel(const int8_t* __restrict__ A, int64_t rsa, int64_t csa, int m,
                    const int8_t* __restrict__ B, int64_t ldb, int n, int64_t k, int64_t kchunk,
-                   int32_t* __restrict__ part) {
+                   SkOut o) {
     __shared__ __align__(16) int8_t As[MM][SK_COLS_KT + 16];
     const int q = blockIdx.y;
     const int j0 = (blockIdx.x * SK_COLS_THREADS + threadIdx.x) * 4;
@@ -117,44 +132,48 @@ __global__ void __launch_bounds__(SK_COLS_THREADS)
         }
         __syncthreads();
         if (j0 < n) {
-            for (int pp = 0; pp < kt; pp += 4) {
-                uint32_t w[4];
+            // 16 rows per step: all sixteen row loads issued before any is used
+            for (int pp = 0; pp < kt; pp += 16) {
+                uint32_t w[16];
 #pragma unroll
-                for (int rr = 0; rr < 4; ++rr) {
-                    const int64_t p = t0 + pp + rr;
-                    const int8_t* row = B + p * ldb + j0;
+                for (int rr = 0; rr < 16; ++rr) {
+                    const int8_t* row = B + (t0 + pp + rr) * ldb + j0;
                     if (pp + rr >= kt) {
                         w[rr] = 0;
                     } else if (full_cols) {
-                        w[rr] = *reinterpret_cast<const uint32_t*>(row);
+                        w[rr] = __ldg(reinterpret_cast<const unsigned int*>(row));
                     } else {
                         uint32_t v = 0;
                         for (int cc = 0; cc < 4; ++cc)
-                            if (j0 + cc < n) v |= static_cast<uint32_t>(static_cast<uint8_t>(row[cc])) << (8 * cc);
+                            if (j0 + cc < n)
+                                v |= static_cast<uint32_t>(static_cast<uint8_t>(row[cc])) << (8 * cc);
                         w[rr] = v;
                     }
                 }
-                uint32_t col[4];
-                sk_transpose4(w[0], w[1], w[2], w[3], col);
 #pragma unroll
-                for (int i = 0; i < MM; ++i) {
-                    if (i < m) {
-                        const int aw = *reinterpret_cast<const int*>(&As[i][pp]);
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t col[4];
+                    sk_transpose4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3], col);
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) acc[i][c] = __dp4a(aw, static_cast<int>(col[c]), acc[i][c]);
+                    for (int i = 0; i < MM; ++i) {
+                        if (i < m) {
+                            const int aw = *reinterpret_cast<const int*>(&As[i][pp + 4 * g]);
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+                                acc[i][c] = __dp4a(aw, static_cast<int>(col[c]), acc[i][c]);
+                        }
                     }
                 }
             }
         }
     }
     if (j0 < n) {
-        int32_t* pq = part + static_cast<size_t>(q) * m * n;
 #pragma unroll
         for (int i = 0; i < MM; ++i)
             if (i < m)
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
-                    if (j0 + c < n) pq[static_cast<size_t>(i) * n + j0 + c] = acc[i][c];
+                    if (j0 + c < n) sk_emit(o, q, i, j0 + c, acc[i][c]);
     }
 }
 
@@ -212,7 +231,7 @@ int run_i8_skinny(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t c
     if (plan == COLS) {
         grid_x = (int)((n + 4 * SK_COLS_THREADS - 1) / (4 * SK_COLS_THREADS));
         const int64_t max_chunks = (int64_t)((k + SK_COLS_KT - 1) / SK_COLS_KT);
-        int64_t want = (2 * ctx->sm_count + grid_x - 1) / grid_x;
+        int64_t want = (4 * ctx->sm_count + grid_x - 1) / grid_x;
         const int64_t need = (int64_t)((k + SK_COLS_CHUNK_MAX - 1) / SK_COLS_CHUNK_MAX);
         want = want < max_chunks ? want : max_chunks;
         want = want > need ? want : need;
@@ -262,25 +281,33 @@ int run_i8_skinny(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t c
         }
     }
 
+    SkOut o{};
+    o.part = part;
+    o.out_rows = (int)m;
+    o.out_cols = (int)n;
+    o.direct = chunks == 1;  // one chunk: the kernel runs the epilogue itself
+    o.c = c;
+    o.rsc = rsc;
+    o.csc = csc;
+    o.epi = epi;
     if (plan == COLS) {
         const dim3 grid((unsigned)grid_x, (unsigned)chunks);
         switch (round_pow2_16((int)m)) {
-        case 1: sk_cols_kernel<1><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, part); break;
-        case 2: sk_cols_kernel<2><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, part); break;
-        case 4: sk_cols_kernel<4><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, part); break;
-        case 8: sk_cols_kernel<8><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, part); break;
-        default: sk_cols_kernel<16><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, part); break;
+        case 1: sk_cols_kernel<1><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, o); break;
+        case 2: sk_cols_kernel<2><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, o); break;
+        case 4: sk_cols_kernel<4><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, o); break;
+        case 8: sk_cols_kernel<8><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, o); break;
+        default: sk_cols_kernel<16><<<grid, SK_COLS_THREADS, 0, s>>>(a, rsa, csa, (int)m, b, rsb, (int)n, (int64_t)k, kchunk, o); break;
         }
     } else {
         const dim3 grid((unsigned)grid_x, (unsigned)chunks);
         const bool swap = plan == REDUCE_BT;
-        const int om = (int)m, on = (int)n;
         switch (round_pow2_16((int)nv)) {
-        case 1: sk_reduce_kernel<1><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, part, om, on, swap); break;
-        case 2: sk_reduce_kernel<2><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, part, om, on, swap); break;
-        case 4: sk_reduce_kernel<4><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, part, om, on, swap); break;
-        case 8: sk_reduce_kernel<8><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, part, om, on, swap); break;
-        default: sk_reduce_kernel<16><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, part, om, on, swap); break;
+        case 1: sk_reduce_kernel<1><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, o, swap); break;
+        case 2: sk_reduce_kernel<2><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, o, swap); break;
+        case 4: sk_reduce_kernel<4><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, o, swap); break;
+        case 8: sk_reduce_kernel<8><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, o, swap); break;
+        default: sk_reduce_kernel<16><<<grid, 128, 0, s>>>(X, ldx, (int)xrows, V, ldv, (int)nv, (int64_t)k, kchunk, o, swap); break;
         }
     }
     if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
@@ -296,6 +323,7 @@ int run_i8_skinny(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t c
         route->ctas = (uint32_t)(grid_x * chunks);
         route->pairs = 0;
     }
+    if (o.direct) return UOR_B200_OK;
     return cuda_status(reduce_chunks(part, chunks, m, n, c, rsc, csc, epi, s));
 }
 
