@@ -136,6 +136,15 @@ def load_traffic(name):
 
 # ---------------------------------------------------------------- CPU baseline
 
+def host_threads(orc):
+    """Every core this process may run on (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except Exception:
+        n = os.cpu_count() or 1
+    return max(n, orc.max_threads())
+
+
 def sample_rows(total_rows, run_rows, budget_s):
     """Time the oracle on a growing leading block of rows until it takes about a
     quarter of the budget; returns (rows, seconds, output of those rows)."""
@@ -179,7 +188,7 @@ def wl_i8(args, U, torch, rank, size, sets=3):
         step(0, ctx)
         ctx.sync()
         a, b = A[0].cpu().numpy(), B[0].cpu().numpy()
-        threads = orc.max_threads()
+        threads = host_threads(orc)
 
         def run(rows):
             c = np.zeros(rows * n, np.int32)
@@ -253,7 +262,7 @@ def wl_gemv(args, U, torch, rank, thin_m, sets=3):
         step(0, ctx)
         ctx.sync()
         a, b = A[0].cpu().numpy(), B[0].cpu().numpy()
-        threads = orc.max_threads()
+        threads = host_threads(orc)
         c = np.zeros(m * n, np.int32)
         reps, t0 = 0, time.perf_counter()
         while True:
@@ -330,7 +339,7 @@ def wl_codec(args, U, torch, rank, sets=3):
         step(0, ctx)
         ctx.sync()
         a, q, t = A[0].cpu().numpy(), Q[0].cpu().numpy(), table.cpu().numpy()
-        threads = orc.max_threads()
+        threads = host_threads(orc)
 
         def run(rows):
             c = np.zeros(rows * n, np.int32)
@@ -408,7 +417,7 @@ def wl_f32(args, U, torch, rank, size, sets=2):
         step(0, ctx)
         ctx.sync()
         a, b = host[0]
-        threads = orc.max_threads()
+        threads = host_threads(orc)
 
         def run(rows):
             c = np.zeros(rows * n, np.float32)
@@ -478,7 +487,7 @@ def wl_wide(args, U, torch, rank):
         step(0, ctx)
         ctx.sync()
         a, b = A.cpu().numpy(), B.cpu().numpy()
-        threads = orc.max_threads()
+        threads = host_threads(orc)
 
         def run(rows):
             c = np.zeros(rows * n * 2, np.int64)
@@ -543,7 +552,7 @@ def wl_trop(args, U, torch, rank):
         step(0, ctx)
         ctx.sync()
         a, b = A.cpu().numpy().view(TD[8]), B.cpu().numpy().view(TD[8])
-        threads = orc.max_threads()
+        threads = host_threads(orc)
 
         def run(rows):
             c = np.zeros(rows * n, TD[32])
@@ -746,7 +755,7 @@ def reference_arm(args, rank):
     size = args.size or SIZE
     k = n = size
     b = U.corpus(2, U.CORPUS_I8, k * n)
-    threads = orc.max_threads()
+    threads = host_threads(orc)
     a = U.corpus(1, U.CORPUS_I8, size * k)
 
     def run(r):

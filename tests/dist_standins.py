@@ -16,7 +16,7 @@ def _np(t, dtype):
     return t.numpy().view(dtype)
 
 
-def partial_cpu(elem, a, av, b, bv, limbs, ctx=None):
+def partial_cpu(elem, a, av, b, bv, limbs, ctx=None, asynchronous=False):
     """Exact sum over the views (oracle, i128 out, Wrapping) written as radix-2^40 limbs."""
     m, k = av[0], av[1]
     n = bv[1]
@@ -52,7 +52,7 @@ def _encode(v, bits, mode):
     return max(lo, min(hi, v))
 
 
-def finish_cpu(elem, out, limbs, c, cv, alpha=1, beta=0, encode=0, ctx=None):
+def finish_cpu(elem, out, limbs, c, cv, alpha=1, beta=0, encode=0, ctx=None, asynchronous=False):
     """Linear::finish over the i128 accumulator (epilogue.rs:79-93, 280-288)."""
     m, n, rs, cs = cv
     ln = limbs.numpy()

@@ -147,7 +147,8 @@ def splitk_gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=U.NEARES
     Every rank passes the same full views (flat tensors on its own device, non-negative
     strides) and the same C prior; every rank ends with the same bytes of C, equal to
     the single-device call's. ctx is bound to torch's current stream, on which the
-    all-reduce runs. elem in {I8, I16, I32}."""
+    all-reduce runs; the call returns with the work queued (ctx.sync() or a stream
+    synchronize collects it). elem in {I8, I16, I32}."""
     import torch
     import torch.distributed as dist
     rank, world = _rank_world(group)
@@ -164,9 +165,11 @@ def splitk_gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=U.NEARES
     per_b = U.DTYPE_SIZE[elem] // b.element_size()
     limbs = torch.zeros(m * n * U.SPLITK_LIMBS, dtype=torch.int64, device=a.device)
     if m and n:
+        # Stream-ordered throughout: the partial, the all-reduce and the finish queue on
+        # one stream without a host round trip between them.
         partial(elem, a[k0 * av[3] * per_a:], (m, k1 - k0, av[2], av[3]), b[k0 * bv[2] * per_b:],
-                (k1 - k0, n, bv[2], bv[3]), limbs, ctx=ctx)
+                (k1 - k0, n, bv[2], bv[3]), limbs, ctx=ctx, asynchronous=True)
         if world > 1:
             dist.all_reduce(limbs, op=dist.ReduceOp.SUM, group=group)
-        finish(elem, out, limbs, c, cv, alpha, beta, encode, ctx=ctx)
+        finish(elem, out, limbs, c, cv, alpha, beta, encode, ctx=ctx, asynchronous=True)
     return (k0, k1)
