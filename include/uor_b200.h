@@ -242,7 +242,8 @@ int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out, const uor_b2
  * (codecs.rs:80-196): B is k x n, each byte holds P sub-codes of 8/P bits, low
  * sub-code first; element (r, c) decodes table[sub % N] with
  * sub = (codes[r * (n / P) + c / P] >> ((8 / P) * (c % P))) & mask.
- * A is a dense i8 view; out in {I8 .. I128}. P in {1, 2}; 1 <= N <= 256. */
+ * A is a dense i8 view; out in {I8 .. I128}. P in {1, 2, 4, 8}; 1 <= N <= 256. P = 2 with
+ * N <= 16 runs the fused decode (K5); the rest decode to a dense workspace first. */
 int uor_b200_coded_gemm(uor_b200_dtype out, const uor_b200_view *a, const uint8_t *codes,
                         size_t codes_len, size_t k, size_t n, uint32_t per_byte,
                         const int8_t *table, size_t table_len, const uor_b200_view_mut *c,
@@ -254,6 +255,39 @@ int uor_b200_tabulated_gemm(uor_b200_dtype out, const uor_b200_view *a, const ui
                             size_t codes_len, size_t k, size_t n, uint32_t per_byte,
                             const int8_t *table, size_t table_len, const uor_b200_view_mut *c,
                             int64_t alpha, int64_t beta, const uor_b200_call *call);
+
+/* The other fixed-width tiers (crates/uor-matmul-codec/src/codecs.rs) through one
+ * descriptor, and Offset<C, zero> over any of them (decoded value minus zero, the image
+ * staying within i8, codecs.rs Offset::new). */
+typedef enum uor_b200_codec_tier {
+    UOR_B200_TIER_GRID = 0,    /* Packed<Grid<N>, P>: as uor_b200_coded_gemm (codecs.rs:80-196) */
+    UOR_B200_TIER_SIGN = 1,    /* Sign<BLK, K>: bit t of the code is element t, set +1, clear -1,
+                                  bits past the code's width -1 (codecs.rs:341-437) */
+    UOR_B200_TIER_TERNARY = 2, /* Ternary<BLK, K>: digit t (bits 2t, 2t+1): 0 -> -1, 2 -> +1,
+                                  1 and 3 -> 0; a digit past the code's width reads 0, so -1
+                                  (codecs.rs:438-520) */
+    UOR_B200_TIER_BOOK = 3     /* Book<N, BLK, K>: element t of block code q is table[q % N][t]
+                                  (codecs.rs:268-308) */
+} uor_b200_codec_tier;
+
+typedef struct uor_b200_codec {
+    uint32_t tier;        /* uor_b200_codec_tier */
+    uint32_t per_byte;    /* GRID: sub-codes per byte P */
+    uint32_t block;       /* SIGN / TERNARY / BOOK: elements per code (BLK) */
+    uint32_t code_bytes;  /* SIGN / TERNARY / BOOK: 1 (u8 codes) or 2 (u16, little-endian) */
+    const int8_t *table;  /* GRID: N entries; BOOK: N x BLK entries, row per code; else unused */
+    size_t table_len;     /* N */
+    int32_t zero;         /* Offset: subtracted from every decoded value (0: no offset) */
+} uor_b200_codec;
+
+/* coded_gemm (orientation 0: codes describe B, k x n) or gemm_tabulated's A W^T
+ * (orientation 1: codes describe W, n x k) for any tier above. The codes hold exactly
+ * rows * (cols / BLK) codes (CodedMatrix::new, matrix.rs:36-60), else DOES_NOT_FIT; a
+ * table whose offset image leaves i8 is INVALID_ARGUMENT. */
+int uor_b200_codec_gemm(uor_b200_dtype out, const uor_b200_view *a, const uor_b200_codec *codec,
+                        const uint8_t *codes, size_t codes_len, size_t k, size_t n,
+                        uint32_t orientation, const uor_b200_view_mut *c, int64_t alpha,
+                        int64_t beta, const uor_b200_call *call);
 
 /* ------------------------------------------------- split-K across devices */
 

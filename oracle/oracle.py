@@ -137,6 +137,44 @@ def coded_gemm(a: View, codes: np.ndarray, P: int, table: np.ndarray, c: View, k
                                 beta, c.ptr(), c.rs, c.cs, mode, threads)
 
 
+def decode_codec(tier, codes, rows, cols, table=None, per_byte=0, block=1, code_bytes=1, zero=0):
+    """The dense rows x cols int8 matrix a fixed-width coded matrix names.
+
+    CodedMatrix::at (crates/uor-matmul-codec/src/matrix.rs:202-207): code q of row r
+    holds elements q*BLK .. q*BLK+BLK-1. Tiers (codecs.rs): Packed<Grid<N>,P> (tier 0,
+    :181-195: sub-code c % P of byte c / P, low first, table[sub % N]); Sign (1,
+    :386-400: bit t set +1, else -1); Ternary (2, :480-496: digit t 0 -> -1, 2 -> +1,
+    else 0, a digit past the code's width reads 0); Book (3, :306-308:
+    table[code % N][t]). Offset (zero): every value minus zero."""
+    codes = np.asarray(codes, np.uint8)
+    out = np.zeros((rows, cols), np.int64)
+    if tier == 0:
+        bits = 8 // per_byte
+        mask = 0xFF if bits >= 8 else (1 << bits) - 1
+        tab = np.asarray(table, np.int64)
+        cpr = cols // per_byte
+        for r in range(rows):
+            for c in range(cols):
+                sub = (int(codes[r * cpr + c // per_byte]) >> (bits * (c % per_byte))) & mask
+                out[r, c] = tab[sub % len(tab)]
+    else:
+        cpr = cols // block
+        for r in range(rows):
+            for c in range(cols):
+                at = (r * cpr + c // block) * code_bytes
+                code = int(codes[at]) | (int(codes[at + 1]) << 8 if code_bytes == 2 else 0)
+                t = c % block
+                if tier == 1:
+                    out[r, c] = 1 if t < 8 * code_bytes and (code >> t) & 1 else -1
+                elif tier == 2:
+                    d = (code >> (2 * t)) & 3 if 2 * t < 8 * code_bytes else 0
+                    out[r, c] = -1 if d == 0 else (1 if d == 2 else 0)
+                else:
+                    tab = np.asarray(table, np.int64).reshape(-1, block)
+                    out[r, c] = tab[code % tab.shape[0], t]
+    return (out - zero).astype(np.int8)
+
+
 # --------------------------------------------------------------------------
 # Pure-Python restatements (small cases only)
 # --------------------------------------------------------------------------

@@ -1,0 +1,105 @@
+"""The other fixed-width codec tiers -- Sign, Ternary, Book, and Offset over any tier --
+through uor_b200_codec_gemm, against the oracle's decode restatement and integer GEMM,
+bit for bit; and the reference's spelling equivalences CK-11 / CK-12."""
+import numpy as np
+import pytest
+
+import uor_b200 as U
+from oracle import oracle as orc
+from gpu_util import i8, needs_gpu, out_array
+
+pytestmark = [pytest.mark.gpu, needs_gpu]
+
+
+def check(m, k, n, tier, codes, orientation=0, out=U.I32, alpha=1, beta=0, seed=0, **kw):
+    a = i8(60 + seed, m * k)
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    dense = orc.decode_codec(tier, codes, rows, cols, kw.get("table"), kw.get("per_byte", 0),
+                             kw.get("block", 1), kw.get("code_bytes", 1), kw.get("zero", 0))
+    c0 = out_array(out, m * n)
+    c0[:] = np.random.default_rng(seed).integers(-1000, 1000, size=c0.size)
+    got, want = c0.copy(), c0.copy()
+    route = U.Route()
+    U.codec_gemm(out, a, (m, k, k, 1), tier, codes, k, n, got, (m, n, n, 1), alpha=alpha,
+                 beta=beta, route=route, orientation=orientation, **kw)
+    bv = (k, n, n, 1) if orientation == 0 else (k, n, 1, k)
+    orc.gemm_int(orc.View(a, m, k, k, 1), orc.View(dense.reshape(-1), *bv),
+                 orc.View(want, m, n, n, 1), alpha=alpha, beta=beta,
+                 out_bits={U.I32: 32, U.I64: 64, U.I128: 128}[out])
+    assert np.array_equal(got, want)
+    return got, route
+
+
+def codes_for(rows, cols, block, code_bytes, seed):
+    count = rows * (cols // block) * code_bytes
+    return U.corpus(seed, U.CORPUS_RAW, count).astype(np.uint8)
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("block,cb", [(8, 1), (16, 2), (12, 2), (20, 2)])
+def test_sign(orientation, block, cb):
+    m, k, n = 70, 240, 240  # both multiples of every block width tested
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    codes = codes_for(rows, cols, block, cb, 5 + block)
+    for zero in (0, -3):
+        check(m, k, n, U.TIER_SIGN, codes, orientation, block=block, code_bytes=cb, zero=zero,
+              seed=block)
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("block,cb", [(4, 1), (8, 2), (6, 1), (12, 2)])
+def test_ternary(orientation, block, cb):
+    m, k, n = 300, 96, 144
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    codes = codes_for(rows, cols, block, cb, 9 + block)
+    for zero, out in ((0, U.I32), (2, U.I64)):
+        check(m, k, n, U.TIER_TERNARY, codes, orientation, out, 3, -1, block=block,
+              code_bytes=cb, zero=zero, seed=block)
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+def test_book(orientation):
+    # the E8 shape Book<256, 8> with u8 codes, and a wider book with u16 codes
+    for (N, block, cb) in [(256, 8, 1), (1000, 4, 2)]:
+        m, k, n = 130, 256, 192
+        table = U.corpus(7, U.CORPUS_I8, N * block)
+        rows, cols = (k, n) if orientation == 0 else (n, k)
+        codes = codes_for(rows, cols, block, cb, 11 + N)
+        check(m, k, n, U.TIER_BOOK, codes, orientation, table=table, block=block, code_bytes=cb,
+              seed=N)
+
+
+@pytest.mark.parametrize("P", [2, 4])
+def test_grid_with_offset(P):
+    m, k, n = 260, 128, 96
+    table = np.arange(-8, 8, dtype=np.int8)[: (16 if P == 2 else 4)]
+    codes = U.corpus(3, U.CORPUS_RAW, k * n // P).astype(np.uint8)
+    got, route = check(m, k, n, U.TIER_GRID, codes, table=table, per_byte=P, zero=5, seed=P)
+    assert route.kernel == 4
+
+
+def test_spellings_agree_ck11_ck12():
+    """Sign<8> is Packed<Grid<2>, 8> over {-1, +1}; Ternary<4> is Packed<Grid<4>, 4> over
+    {-1, 0, +1, 0}: the same bytes, the same product."""
+    m, k, n = 50, 64, 256
+    a = i8(70, m * k)
+    for tier, P, table in [(U.TIER_SIGN, 8, [-1, 1]), (U.TIER_TERNARY, 4, [-1, 0, 1, 0])]:
+        codes = U.corpus(13, U.CORPUS_RAW, k * n // P).astype(np.uint8)
+        x = np.zeros(m * n, np.int32)
+        y = np.zeros(m * n, np.int32)
+        U.codec_gemm(U.I32, a, (m, k, k, 1), tier, codes, k, n, x, (m, n, n, 1), block=P,
+                     code_bytes=1)
+        U.coded_gemm(U.I32, a, (m, k, k, 1), codes, k, n, P, np.array(table, np.int8), y,
+                     (m, n, n, 1))
+        assert np.array_equal(x, y), tier
+
+
+def test_validation():
+    a = np.zeros(4, np.int8)
+    c = np.zeros(4, np.int32)
+    with pytest.raises(U.DoesNotFit):  # codes for 3 of 4 rows
+        U.codec_gemm(U.I32, a, (1, 4, 4, 1), U.TIER_SIGN, np.zeros(3, np.uint8), 4, 4, c,
+                     (1, 4, 4, 1), block=4, code_bytes=1)
+    with pytest.raises(U.UorError):  # Offset image leaves i8
+        U.codec_gemm(U.I32, a, (1, 4, 4, 1), U.TIER_SIGN, np.zeros(4, np.uint8), 4, 4, c,
+                     (1, 4, 4, 1), block=4, code_bytes=1, zero=128)

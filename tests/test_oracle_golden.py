@@ -346,3 +346,21 @@ def test_complete_register_drops_out_of_range_coordinates():
         twin = orc.float_gemm_py([[1.0]], [[2.0]], 1, 1, [[prior]], False, True)[0][0]
         assert int(c.view(np.uint64)[0]) == twin
         assert c[0] == want
+
+
+def test_codec_tier_decode_restatement():
+    """The fixed-width tiers' decode (codecs.rs): Sign bit order (low first, set +1),
+    Ternary digits (0 -> -1, 1 -> 0, 2 -> +1, 3 -> 0; past the code's width -> -1),
+    Book rows, Offset, and Packed sub-code order (CK-03)."""
+    dec = orc.decode_codec
+    assert dec(1, np.array([0b10110001], np.uint8), 1, 8, block=8).tolist() == [
+        [1, -1, -1, -1, 1, 1, -1, 1]]
+    assert dec(1, np.array([0xFF, 0x01], np.uint8), 1, 20, block=20, code_bytes=2).tolist() == [
+        [1] * 9 + [-1] * 11]
+    assert dec(2, np.array([0b11100100], np.uint8), 1, 6, block=6).tolist() == [
+        [-1, 0, 1, 0, -1, -1]]
+    book = np.arange(-6, 6, dtype=np.int8)  # N = 3 rows of BLK = 4
+    assert dec(3, np.array([1, 5], np.uint8), 1, 8, table=book, block=4).tolist() == [
+        [-2, -1, 0, 1, 2, 3, 4, 5]]
+    assert dec(0, np.array([0x21], np.uint8), 1, 2, table=np.arange(16, dtype=np.int8),
+               per_byte=2, zero=3).tolist() == [[-2, -1]]

@@ -2,6 +2,7 @@
 // of gemm_tabulated (codes n x k), over Packed<Grid<N>, P> codes.
 #include <climits>
 #include <cstring>
+#include <vector>
 #include "aux.cuh"
 #include "gemm_coded.cuh"
 #include "gemm_i8.cuh"
@@ -37,7 +38,7 @@ __global__ void decode_dense_kernel(int8_t* __restrict__ out, const uint8_t* __r
 int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* codes,
                  size_t codes_len, size_t k, size_t n, uint32_t per_byte, const int8_t* table,
                  size_t table_len, const uor_b200_view_mut* c, int64_t alpha, int64_t beta,
-                 const uor_b200_call* call, int orientation) {
+                 const uor_b200_call* call, int orientation, bool table_on_host = false) {
     int kind;
     switch (out) {
     case UOR_B200_I8: kind = OUT_I8; break;
@@ -82,7 +83,7 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     // The 16-entry effective table the fused decode uses: table[v % N].
     int8_t tab[256];
     const size_t tl = table_len < 256 ? table_len : 256;
-    if (dev) {
+    if (dev && !table_on_host) {
         if (cudaMemcpy(tab, table, tl, cudaMemcpyDeviceToHost) != cudaSuccess)
             return UOR_B200_DEVICE_ERROR;
     } else {
@@ -228,6 +229,168 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     return finish_call(ctx, call);
 }
 
+// Sign / Ternary / Book codes of `cb` bytes per block of `blk` elements (little-endian
+// codes), decoded element by element exactly as CodedMatrix::at does for a fixed-width
+// tier (matrix.rs:202-207): code = codes[row * (cols / blk) + col / blk], element
+// col % blk of it; every value minus `zero` (Offset, codecs.rs: decode - zero).
+__global__ void decode_block_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
+                                    const int8_t* __restrict__ table, int tier, int N, int blk,
+                                    int cb, int zero, int orientation, int k, int n) {
+    const int64_t total = static_cast<int64_t>(k) * n;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+        const int row = orientation == 0 ? p : j, col = orientation == 0 ? j : p;
+        const int cols = orientation == 0 ? n : k;
+        const uint8_t* cp = codes + (static_cast<int64_t>(row) * (cols / blk) + col / blk) * cb;
+        const uint32_t code = cb == 1 ? cp[0] : (static_cast<uint32_t>(cp[0]) | (static_cast<uint32_t>(cp[1]) << 8));
+        const int t = col % blk;
+        int v;
+        if (tier == UOR_B200_TIER_SIGN) {
+            // bit t set: +1; clear, or past the code's width: -1 (codecs.rs:386-400)
+            v = (t < 8 * cb && ((code >> t) & 1u)) ? 1 : -1;
+        } else if (tier == UOR_B200_TIER_TERNARY) {
+            // digit t: 0 -> -1, 2 -> +1, 1 and 3 -> 0; a digit past the code's width reads
+            // as 0, so -1 (codecs.rs Ternary::decode_element)
+            const uint32_t d = 2 * t < 8 * cb ? (code >> (2 * t)) & 3u : 0u;
+            v = d == 0 ? -1 : (d == 2 ? 1 : 0);
+        } else {
+            // Book: table[code % N][t] (codecs.rs:306-308)
+            v = table[static_cast<int64_t>(code % static_cast<uint32_t>(N)) * blk + t];
+        }
+        out[idx] = static_cast<int8_t>(v - zero);
+    }
+}
+
+int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_codec* codec,
+                 const uint8_t* codes, size_t codes_len, size_t k, size_t n, uint32_t orientation,
+                 const uor_b200_view_mut* c, int64_t alpha, int64_t beta,
+                 const uor_b200_call* call) {
+    if (!codec || !a || !c || orientation > 1) return UOR_B200_INVALID_ARGUMENT;
+    const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
+    const int zero = codec->zero;
+    // The decoded range of each tier, for Offset::new's bound (the image must stay i8).
+    auto fits = [&](int lo, int hi) { return lo - zero >= -128 && hi - zero <= 127; };
+    if (codec->tier == UOR_B200_TIER_GRID) {
+        const size_t N = codec->table_len;
+        if (!codec->table || N == 0 || N > 256) return UOR_B200_INVALID_ARGUMENT;
+        int8_t tab[256];
+        if (dev) {
+            if (cudaMemcpy(tab, codec->table, N, cudaMemcpyDeviceToHost) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+        } else {
+            std::memcpy(tab, codec->table, N);
+        }
+        for (size_t q = 0; q < N; ++q) {
+            if (!fits(tab[q], tab[q])) return UOR_B200_INVALID_ARGUMENT;
+            tab[q] = static_cast<int8_t>(tab[q] - zero);
+        }
+        return coded_common(out, a, codes, codes_len, k, n, codec->per_byte, tab, N, c, alpha,
+                            beta, call, (int)orientation, true);
+    }
+    const int tier = (int)codec->tier;
+    const size_t blk = codec->block, cb = codec->code_bytes;
+    if (tier != UOR_B200_TIER_SIGN && tier != UOR_B200_TIER_TERNARY && tier != UOR_B200_TIER_BOOK)
+        return UOR_B200_UNSUPPORTED;
+    if (blk == 0 || (cb != 1 && cb != 2)) return UOR_B200_INVALID_ARGUMENT;
+    size_t N = 0, tbytes = 0;
+    if (tier == UOR_B200_TIER_BOOK) {
+        N = codec->table_len;
+        if (!codec->table || N == 0 || blk > 4096 || N > (size_t{1} << 20) / blk)
+            return UOR_B200_INVALID_ARGUMENT;
+        tbytes = N * blk;
+    } else if (!fits(-1, 1)) {
+        return UOR_B200_INVALID_ARGUMENT;
+    }
+    int kind;
+    switch (out) {
+    case UOR_B200_I8: kind = OUT_I8; break;
+    case UOR_B200_I16: kind = OUT_I16; break;
+    case UOR_B200_I32: kind = OUT_I32; break;
+    case UOR_B200_I64: kind = OUT_I64; break;
+    case UOR_B200_I128: kind = OUT_I128; break;
+    default: return UOR_B200_UNSUPPORTED;
+    }
+    const int mode = call ? (int)call->encode : MODE_NEAREST;
+    if (mode < 0 || mode > 3) return UOR_B200_INVALID_ARGUMENT;
+    // CodedMatrix::new (matrix.rs:36-60): whole blocks, and exactly the declared shape.
+    const size_t rows = orientation == 0 ? k : n, cols = orientation == 0 ? n : k;
+    if (cols % blk != 0 || rows * (cols / blk) * cb != codes_len) return UOR_B200_DOES_NOT_FIT;
+    Operand A, C;
+    int st;
+    if ((st = place_view(a->data, a->len, a->rows, a->cols, a->rs, a->cs, 1, &A))) return st;
+    if ((st = place_view(c->data, c->len, c->rows, c->cols, c->rs, c->cs, dtype_size(out), &C)))
+        return st;
+    if (a->cols != k || c->rows != a->rows || c->cols != n) return UOR_B200_NONCONFORMANT;
+    if (self_aliases(c->rows, c->cols, c->rs, c->cs)) return UOR_B200_OUTPUT_ALIASES;
+    uor_b200_route local{};
+    uor_b200_route* route = call && call->route ? call->route : &local;
+    *route = uor_b200_route{};
+    const size_t m = a->rows;
+    if (m == 0 || n == 0) return UOR_B200_OK;
+    if (m > (size_t)INT_MAX / 2 || n > (size_t)INT_MAX / 2 || k > (size_t)INT_MAX / 2)
+        return UOR_B200_UNSUPPORTED;
+    if (codes_len && !codes) return UOR_B200_INVALID_ARGUMENT;
+    if (tier == UOR_B200_TIER_BOOK) {
+        // Offset's bound over the whole book
+        int8_t lo = 127, hi = -128;
+        std::vector<int8_t> book(tbytes);
+        if (dev) {
+            if (cudaMemcpy(book.data(), codec->table, tbytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+        } else {
+            std::memcpy(book.data(), codec->table, tbytes);
+        }
+        for (int8_t v : book) lo = v < lo ? v : lo, hi = v > hi ? v : hi;
+        if (!fits(lo, hi)) return UOR_B200_INVALID_ARGUMENT;
+    }
+
+    uor_b200_ctx* ctx = resolve_ctx(call, &st);
+    if (!ctx) return st;
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    cudaStream_t s = ctx->stream;
+    const uint8_t* da = nullptr;
+    OutStage cs;
+    if ((st = stage_in(ctx, SLOT_A, A, dev, &da))) return st;
+    const uint8_t* dcodes = codes;
+    if (!dev && codes_len) {
+        uint8_t* d = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_B, codes_len, &st));
+        if (!d) return st;
+        if (cudaMemcpyAsync(d, codes, codes_len, cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+        dcodes = d;
+    }
+    if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs))) return st;
+    const size_t tb = (tbytes + 255) / 256 * 256;
+    uint8_t* buf = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, tb + k * n + 256, &st));
+    if (!buf) return st;
+    const int8_t* dtable = nullptr;
+    if (tbytes) {
+        if (cudaMemcpyAsync(buf, codec->table, tbytes,
+                            dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+        dtable = reinterpret_cast<const int8_t*>(buf);
+    }
+    int8_t* dense = reinterpret_cast<int8_t*>(buf + tb);
+    if (k) {
+        const int64_t total = (int64_t)k * n;
+        const int grid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+        decode_block_kernel<<<grid, 256, 0, s>>>(dense, dcodes, dtable, tier, (int)N, (int)blk,
+                                                 (int)cb, zero, (int)orientation, (int)k, (int)n);
+        if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    }
+    const LinearEpi epi{alpha, beta, mode, kind};
+    st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs, dense, (ptrdiff_t)n, 1,
+                     cs.dev_origin, C.rs, C.cs, m, k, n, epi, route);
+    if (st) return st;
+    route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
+    route->b_layout = 3;  // decoded to a dense workspace first
+    if (!dev && tbytes && (st = uor_b200_ctx_sync(ctx))) return st;  // the host book was read
+    if ((st = stage_out_end(ctx, cs))) return st;
+    if (!dev) return uor_b200_ctx_sync(ctx);
+    return finish_call(ctx, call);
+}
+
 }  // namespace
 
 extern "C" {
@@ -246,6 +409,13 @@ int uor_b200_tabulated_gemm(uor_b200_dtype out, const uor_b200_view* a, const ui
                             int64_t alpha, int64_t beta, const uor_b200_call* call) {
     return coded_common(out, a, codes, codes_len, k, n, per_byte, table, table_len, c, alpha, beta,
                         call, 1);
+}
+
+int uor_b200_codec_gemm(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_codec* codec,
+                        const uint8_t* codes, size_t codes_len, size_t k, size_t n,
+                        uint32_t orientation, const uor_b200_view_mut* c, int64_t alpha,
+                        int64_t beta, const uor_b200_call* call) {
+    return codec_common(out, a, codec, codes, codes_len, k, n, orientation, c, alpha, beta, call);
 }
 
 }  // extern "C"

@@ -63,6 +63,17 @@ class Route(ctypes.Structure):
         return d
 
 
+class Codec(ctypes.Structure):
+    """uor_b200_codec: a fixed-width codec tier and its parameters."""
+    _fields_ = [("tier", ctypes.c_uint32), ("per_byte", ctypes.c_uint32),
+                ("block", ctypes.c_uint32), ("code_bytes", ctypes.c_uint32),
+                ("table", ctypes.c_void_p), ("table_len", ctypes.c_size_t),
+                ("zero", ctypes.c_int32)]
+
+
+TIER_GRID, TIER_SIGN, TIER_TERNARY, TIER_BOOK = range(4)
+
+
 class Call(ctypes.Structure):
     _fields_ = [("encode", ctypes.c_uint32), ("flags", ctypes.c_uint32),
                 ("ctx", ctypes.c_void_p), ("route", ctypes.POINTER(Route))]
@@ -107,6 +118,8 @@ def lib():
             "uor_b200_gemm_tropical": ([I, I, VP, VP, VP, Trop, Trop, CP], I),
             "uor_b200_coded_gemm": ([I, VP, P, Z, Z, Z, U32, P, Z, VP, L64, L64, CP], I),
             "uor_b200_tabulated_gemm": ([I, VP, P, Z, Z, Z, U32, P, Z, VP, L64, L64, CP], I),
+            "uor_b200_codec_gemm": ([I, VP, ctypes.POINTER(Codec), P, Z, Z, Z, U32, VP, L64, L64,
+                                     CP], I),
             "uor_b200_gemm_partial_limbs": ([I, VP, VP, P, Z, CP], I),
             "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
             "uor_b200_status_string": ([I], ctypes.c_char_p),
@@ -332,6 +345,28 @@ def coded_gemm(out, a, av, codes, k, n, per_byte, table, c, cv, alpha=1, beta=0,
     fn = lib().uor_b200_tabulated_gemm if tabulated else lib().uor_b200_coded_gemm
     _check(fn(out, ctypes.byref(A), pc, lc, k, n, per_byte, pt, lt, ctypes.byref(C), alpha, beta,
               ctypes.byref(call)), "coded_gemm")
+
+
+def codec_gemm(out, a, av, tier, codes, k, n, c, cv, table=None, per_byte=0, block=0,
+               code_bytes=1, zero=0, alpha=1, beta=0, encode=NEAREST, ctx=None, route=None,
+               orientation=0, asynchronous=False):
+    """coded_gemm (orientation 0, codes k x n) / gemm_tabulated (1, codes n x k) for any
+    fixed-width tier: TIER_GRID (per_byte, table), TIER_SIGN / TIER_TERNARY (block,
+    code_bytes), TIER_BOOK (block, code_bytes, table of N x block); zero is Offset's."""
+    bufs = (a, codes, c) if table is None else (a, codes, table, c)
+    dev = _on_device(*bufs)
+    A, C = view(a, *av), view(c, *cv)
+    pc, lc, _ = _buffer(codes)
+    if table is not None:
+        pt, lt, _ = _buffer(table)
+        n_entries = lt if tier != TIER_BOOK else lt // max(block, 1)
+    else:
+        pt, n_entries = None, 0
+    cod = Codec(tier, per_byte, block, code_bytes, pt, n_entries, zero)
+    call = make_call(encode, dev, ctx, route, asynchronous)
+    _check(lib().uor_b200_codec_gemm(out, ctypes.byref(A), ctypes.byref(cod), pc, lc, k, n,
+                                     orientation, ctypes.byref(C), alpha, beta,
+                                     ctypes.byref(call)), "codec_gemm")
 
 
 # ------------------------------------------------------------------ split-K exchange
