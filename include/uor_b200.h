@@ -235,6 +235,18 @@ int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out, const uor_b2
                            const uor_b200_view *b, const uor_b200_view_mut *c,
                            uor_b200_trop alpha, uor_b200_trop beta, const uor_b200_call *call);
 
+/* driver::gemm_selected (crates/uor-matmul-gemm/src/selection.rs:212-330): the same
+ * product, and beside it a witness matrix (u64 elements, m x n, its own strides): for
+ * each cell the least index p attaining the maximum of the reduction (D-6's tie-break),
+ * or 0 when every term is the semiring zero or k is 0. The witness is of the reduction,
+ * before MaxPlus. A witness of another shape is NONCONFORMANT; one whose strides map two
+ * cells onto one is OUTPUT_ALIASES (SelectedTriple::new). */
+int uor_b200_gemm_tropical_selected(uor_b200_dtype elem, uor_b200_dtype out,
+                                    const uor_b200_view *a, const uor_b200_view *b,
+                                    const uor_b200_view_mut *c, const uor_b200_view_mut *witness,
+                                    uor_b200_trop alpha, uor_b200_trop beta,
+                                    const uor_b200_call *call);
+
 /* ----------------------------------------------------------- codec family */
 
 /* coded_gemm (crates/uor-matmul-gemm/src/coded.rs:98-142) with B a CodedMatrix

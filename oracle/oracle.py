@@ -175,6 +175,24 @@ def decode_codec(tier, codes, rows, cols, table=None, per_byte=0, block=1, code_
     return (out - zero).astype(np.int8)
 
 
+def trop_witness(av, af, bv, bf):
+    """D-6's witness (crates/uor-matmul-gemm/src/selection.rs; the differential reference of
+    validate/tests/selection.rs): per cell the least index attaining the maximum of the
+    finite terms a_ip + b_pj, and 0 when no term is finite (or k is 0). av/af are the
+    m x k values and finite flags of A, bv/bf the k x n ones of B."""
+    m, k = av.shape
+    n = bv.shape[1]
+    w = np.zeros((m, n), np.uint64)
+    if k == 0:
+        return w
+    big = np.int64(-(1 << 62))
+    for i in range(m):
+        terms = np.where(af[i][:, None] & bf, av[i].astype(np.int64)[:, None] + bv.astype(np.int64),
+                         big)  # k x n
+        w[i] = np.argmax(terms, axis=0)  # the first maximum: the least index
+    return w
+
+
 # --------------------------------------------------------------------------
 # Pure-Python restatements (small cases only)
 # --------------------------------------------------------------------------

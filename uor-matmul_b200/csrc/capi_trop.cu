@@ -20,16 +20,19 @@ int trop_bytes(uor_b200_dtype t) {
 
 }  // namespace
 
-extern "C" int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out,
-                                      const uor_b200_view* a, const uor_b200_view* b,
-                                      const uor_b200_view_mut* c, uor_b200_trop alpha,
-                                      uor_b200_trop beta, const uor_b200_call* call) {
+namespace {
+
+// driver::gemm / gemm_selected over Trop<E> with MaxPlus; `w` (a u64 view, or null) takes
+// the selection witness.
+int trop_common(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a,
+                const uor_b200_view* b, const uor_b200_view_mut* c, const uor_b200_view_mut* w,
+                uor_b200_trop alpha, uor_b200_trop beta, const uor_b200_call* call) {
     if (!a || !b || !c) return UOR_B200_INVALID_ARGUMENT;
     const int eb = trop_bytes(elem), ob = trop_bytes(out);
     if (!eb || !ob) return UOR_B200_UNSUPPORTED;
     const int mode = call ? (int)call->encode : MODE_NEAREST;
     if (mode < 0 || mode > 3) return UOR_B200_INVALID_ARGUMENT;
-    Operand A, B, C;
+    Operand A, B, C, W;
     int st;
     if ((st = place_view(a->data, a->len, a->rows, a->cols, a->rs, a->cs, dtype_size(elem), &A)))
         return st;
@@ -37,8 +40,12 @@ extern "C" int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out,
         return st;
     if ((st = place_view(c->data, c->len, c->rows, c->cols, c->rs, c->cs, dtype_size(out), &C)))
         return st;
+    if (w && (st = place_view(w->data, w->len, w->rows, w->cols, w->rs, w->cs, 8, &W))) return st;
     if (a->cols != b->rows || c->rows != a->rows || c->cols != b->cols) return UOR_B200_NONCONFORMANT;
     if (self_aliases(c->rows, c->cols, c->rs, c->cs)) return UOR_B200_OUTPUT_ALIASES;
+    // SelectedTriple::new (selection.rs:76-98): the witness is m x n and injective.
+    if (w && (w->rows != a->rows || w->cols != b->cols)) return UOR_B200_NONCONFORMANT;
+    if (w && self_aliases(w->rows, w->cols, w->rs, w->cs)) return UOR_B200_OUTPUT_ALIASES;
     uor_b200_route local{};
     uor_b200_route* route = call && call->route ? call->route : &local;
     *route = uor_b200_route{};
@@ -52,10 +59,11 @@ extern "C" int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out,
     std::lock_guard<std::mutex> lock(ctx->mu);
     const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
     const uint8_t *da = nullptr, *db = nullptr;
-    OutStage cs;
+    OutStage cs, ws_out;
     if ((st = stage_in(ctx, SLOT_A, A, dev, &da))) return st;
     if ((st = stage_in(ctx, SLOT_B, B, dev, &db))) return st;
     if ((st = stage_out_begin(ctx, C, dev, beta.finite != 0, &cs))) return st;
+    if (w && (st = stage_out_begin(ctx, W, dev, false, &ws_out, SLOT_AUX))) return st;
 
     TropEpi e{};
     e.alpha = alpha.value;
@@ -71,22 +79,49 @@ extern "C" int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out,
     e.n = (int)n;
     route->kernel = UOR_B200_KERNEL_TROPICAL;
     cudaError_t err;
-    if (eb == 1) {
-        void* ws = ctx_buffer(ctx, SLOT_WS, trop_i8_workspace((int)m, (int)k, (int)n), &st);
+    uint64_t* wd = w ? reinterpret_cast<uint64_t*>(ws_out.dev_origin) : nullptr;
+    if (eb == 1 && (!w || k <= (size_t)TROP_WITNESS_MAX_K)) {
+        const size_t wsb = w ? trop_witness_workspace((int)m, (int)k, (int)n)
+                             : trop_i8_workspace((int)m, (int)k, (int)n);
+        void* ws = ctx_buffer(ctx, SLOT_WS, wsb, &st);
         if (!ws) return st;
         route->tile_m = 128;
         route->tile_n = 128;
-        route->tile_k = 32;
-        err = trop_i8_launch(da, A.rs, A.cs, db, B.rs, B.cs, (int)m, (int)k, (int)n, ws, e,
-                             ctx->stream);
+        route->tile_k = w ? 16 : 32;
+        err = w ? trop_i8_witness_launch(da, A.rs, A.cs, db, B.rs, B.cs, (int)m, (int)k, (int)n, ws,
+                                         e, wd, W.rs, W.cs, ctx->stream)
+                : trop_i8_launch(da, A.rs, A.cs, db, B.rs, B.cs, (int)m, (int)k, (int)n, ws, e,
+                                 ctx->stream);
     } else {
         route->tile_m = 16;
         route->tile_n = 16;
-        err = trop_generic_launch(da, A.rs, A.cs, db, B.rs, B.cs, eb, (int)m, (int)k, (int)n, e,
-                                  ctx->stream);
+        err = w ? trop_generic_witness_launch(da, A.rs, A.cs, db, B.rs, B.cs, eb, (int)m, (int)k,
+                                              (int)n, e, wd, W.rs, W.cs, ctx->stream)
+                : trop_generic_launch(da, A.rs, A.cs, db, B.rs, B.cs, eb, (int)m, (int)k, (int)n,
+                                      e, ctx->stream);
     }
     if (err != cudaSuccess) return UOR_B200_DEVICE_ERROR;
     if ((st = stage_out_end(ctx, cs))) return st;
+    if (w && (st = stage_out_end(ctx, ws_out))) return st;
     if (!dev) return uor_b200_ctx_sync(ctx);
     return finish_call(ctx, call);
+}
+
+}  // namespace
+
+extern "C" int uor_b200_gemm_tropical(uor_b200_dtype elem, uor_b200_dtype out,
+                                      const uor_b200_view* a, const uor_b200_view* b,
+                                      const uor_b200_view_mut* c, uor_b200_trop alpha,
+                                      uor_b200_trop beta, const uor_b200_call* call) {
+    return trop_common(elem, out, a, b, c, nullptr, alpha, beta, call);
+}
+
+extern "C" int uor_b200_gemm_tropical_selected(uor_b200_dtype elem, uor_b200_dtype out,
+                                               const uor_b200_view* a, const uor_b200_view* b,
+                                               const uor_b200_view_mut* c,
+                                               const uor_b200_view_mut* witness,
+                                               uor_b200_trop alpha, uor_b200_trop beta,
+                                               const uor_b200_call* call) {
+    if (!witness) return UOR_B200_INVALID_ARGUMENT;
+    return trop_common(elem, out, a, b, c, witness, alpha, beta, call);
 }

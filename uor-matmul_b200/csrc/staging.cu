@@ -53,7 +53,7 @@ int stage_in(uor_b200_ctx* ctx, int slot, const Operand& op, bool device, const 
 }
 
 int stage_out_begin(uor_b200_ctx* ctx, const Operand& op, bool device, bool reads_c,
-                    OutStage* st) {
+                    OutStage* st, int slot) {
     st->device = device;
     if (device || op.rows == 0 || op.cols == 0) {
         st->dev_origin = const_cast<uint8_t*>(op.origin);
@@ -62,7 +62,7 @@ int stage_out_begin(uor_b200_ctx* ctx, const Operand& op, bool device, bool read
     const size_t span = (size_t)(op.hi - op.lo + 1);
     st->bytes = span * op.es;
     int s = UOR_B200_OK;
-    auto* d = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_C, st->bytes, &s));
+    auto* d = static_cast<uint8_t*>(ctx_buffer(ctx, slot, st->bytes, &s));
     if (!d) return s;
     st->dev_lo = d;
     st->host_lo = const_cast<uint8_t*>(op.origin) + op.lo * (ptrdiff_t)op.es;

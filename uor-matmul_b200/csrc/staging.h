@@ -41,7 +41,7 @@ struct OutStage {
     bool device = false;
 };
 int stage_out_begin(uor_b200_ctx* ctx, const Operand& op, bool device, bool reads_c,
-                    OutStage* st);
+                    OutStage* st, int slot = SLOT_C);
 int stage_out_end(uor_b200_ctx* ctx, const OutStage& st);
 
 }  // namespace uor

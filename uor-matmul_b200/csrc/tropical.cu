@@ -14,6 +14,7 @@
 // over 128x128 tiles staged through shared memory with cp.async.
 // Any result below -8192 decodes to -inf.
 #include <cuda_runtime.h>
+#include <climits>
 #include "tropical.cuh"
 
 namespace uor {
@@ -233,6 +234,149 @@ __global__ void trop_generic_kernel(const uint8_t* __restrict__ a, int64_t rsa, 
     trop_finish(e, static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc, have, best);
 }
 
+// ------------------------------------------------------------ selection witness
+//
+// One key per term carries both halves of D-6's order: key = (a + b) 2^16 + (65535 - p)
+// for finite a, b -- a greater sum wins, and on equal sums the smaller index, exactly
+// Lex::combine (selection.rs) -- so one fused add-max per term reduces value and witness
+// together. A semiring zero contributes -2^30 to its side, which keeps every key it
+// touches below -2^29 while every finite key lies in [-2^24, 2^24]; a cell whose best key
+// is that low has no finite term, and its witness is 0 (the least index, selection.rs).
+constexpr int TW_BM = 128, TW_BN = 128, TW_BK = 16, TW_THREADS = 256;
+constexpr int32_t TW_ZERO = -(1 << 30);
+
+__global__ void trop_witness_pack_a_kernel(int32_t* __restrict__ at, int mp, int kp,
+                                           const uint8_t* __restrict__ a, int64_t rsa,
+                                           int64_t csa, int m, int k) {
+    const int64_t total = static_cast<int64_t>(mp) * kp;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(idx / mp), i = static_cast<int>(idx % mp);
+        int32_t v = TW_ZERO;
+        if (i < m && p < k) {
+            const uint8_t* el = a + (static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa) * 2;
+            if (el[1]) v = static_cast<int32_t>(static_cast<int8_t>(el[0])) * 65536;
+        }
+        at[idx] = v;
+    }
+}
+
+__global__ void trop_witness_pack_b_kernel(int32_t* __restrict__ bt, int np, int kp,
+                                           const uint8_t* __restrict__ b, int64_t rsb,
+                                           int64_t csb, int k, int n) {
+    const int64_t total = static_cast<int64_t>(np) * kp;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(idx / np), j = static_cast<int>(idx % np);
+        int32_t v = TW_ZERO;
+        if (j < n && p < k) {
+            const uint8_t* el = b + (static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb) * 2;
+            if (el[1]) v = static_cast<int32_t>(static_cast<int8_t>(el[0])) * 65536 + (65535 - p);
+        }
+        bt[idx] = v;
+    }
+}
+
+__global__ void __launch_bounds__(TW_THREADS)
+    trop_i8_witness_kernel(const int32_t* __restrict__ at, const int32_t* __restrict__ bt, int mp,
+                           int np, int kp, TropEpi e, uint64_t* __restrict__ w, int64_t rsw,
+                           int64_t csw) {
+    __shared__ __align__(16) int32_t As[2][TW_BK][TW_BM];
+    __shared__ __align__(16) int32_t Bs[2][TW_BK][TW_BN];
+    const int t = threadIdx.x;
+    const int m0 = blockIdx.y * TW_BM, n0 = blockIdx.x * TW_BN;
+    const int ty = t >> 4, tx = t & 15;
+
+    auto load_tile = [&](int buf, int k0) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {  // A: 16 rows x 512 B = 512 chunks of 16 B
+            const int c = t * 2 + q, r = c >> 5, col = (c & 31) * 4;
+            cp_async16(&As[buf][r][col], at + static_cast<int64_t>(k0 + r) * mp + m0 + col);
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int c = t * 2 + q, r = c >> 5, col = (c & 31) * 4;
+            cp_async16(&Bs[buf][r][col], bt + static_cast<int64_t>(k0 + r) * np + n0 + col);
+        }
+        cp_async_commit();
+    };
+
+    int32_t acc[8][8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[r][q] = INT_MIN;
+
+    const int tiles = kp / TW_BK;
+    if (tiles > 0) load_tile(0, 0);
+    for (int kt = 0; kt < tiles; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < tiles) {
+            load_tile(buf ^ 1, (kt + 1) * TW_BK);
+            cp_async_wait_1();
+        } else {
+            cp_async_wait_0();
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int kk = 0; kk < TW_BK; ++kk) {
+            const int4 a0 = *reinterpret_cast<const int4*>(&As[buf][kk][ty * 8]);
+            const int4 a1 = *reinterpret_cast<const int4*>(&As[buf][kk][ty * 8 + 4]);
+            const int4 b0 = *reinterpret_cast<const int4*>(&Bs[buf][kk][tx * 8]);
+            const int4 b1 = *reinterpret_cast<const int4*>(&Bs[buf][kk][tx * 8 + 4]);
+            const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const int bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[r][q] = __viaddmax_s32(av[r], bv[q], acc[r][q]);
+        }
+        __syncthreads();
+    }
+
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const int i = m0 + ty * 8 + r;
+        if (i >= e.m) continue;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int j = n0 + tx * 8 + q;
+            if (j >= e.n) continue;
+            const int32_t key = acc[r][q];
+            const bool fin = key > -(1 << 29);
+            const int32_t v = fin ? (key >> 16) : 0;  // floor: the index field is non-negative
+            const uint64_t at_p = fin ? static_cast<uint64_t>(65535 - (key & 0xFFFF)) : 0;
+            trop_finish(e, static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc, fin,
+                        static_cast<i128>(v));
+            w[static_cast<int64_t>(i) * rsw + static_cast<int64_t>(j) * csw] = at_p;
+        }
+    }
+}
+
+// Any Trop<E>: the reduction in 128-bit arithmetic with D-6's witness.
+__global__ void trop_generic_witness_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
+                                            const uint8_t* __restrict__ b, int64_t rsb, int64_t csb,
+                                            int ebytes, int k, TropEpi e, uint64_t* __restrict__ w,
+                                            int64_t rsw, int64_t csw) {
+    const int i = blockIdx.y * blockDim.y + threadIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= e.m || j >= e.n) return;
+    bool have = false;
+    i128 best = 0;
+    int64_t at_p = 0;
+    for (int p = 0; p < k; ++p) {
+        i128 x, y;
+        const bool fx = trop_load(a, ebytes, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, &x);
+        const bool fy = trop_load(b, ebytes, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, &y);
+        if (fx && fy) {
+            const i128 s = x + y;
+            if (!have || s > best) best = s, have = true, at_p = p;  // strictly greater: least index
+        }
+    }
+    trop_finish(e, static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc, have, best);
+    w[static_cast<int64_t>(i) * rsw + static_cast<int64_t>(j) * csw] = static_cast<uint64_t>(at_p);
+}
+
 static int grid_for(int64_t total) {
     const int64_t g = (total + 255) / 256;
     return static_cast<int>(g < 148 * 32 ? g : 148 * 32);
@@ -270,6 +414,44 @@ cudaError_t trop_generic_launch(const uint8_t* a, int64_t rsa, int64_t csa, cons
     dim3 block(16, 16);
     dim3 grid((n + 15) / 16, (m + 15) / 16);
     trop_generic_kernel<<<grid, block, 0, s>>>(a, rsa, csa, b, rsb, csb, ebytes, k, e);
+    return cudaGetLastError();
+}
+
+size_t trop_witness_workspace(int m, int k, int n) {
+    const size_t mp = (m + TW_BM - 1) / TW_BM * TW_BM;
+    const size_t np = (n + TW_BN - 1) / TW_BN * TW_BN;
+    const size_t kp = (k + TW_BK - 1) / TW_BK * TW_BK;
+    return kp * (mp + np) * 4;
+}
+
+cudaError_t trop_i8_witness_launch(const uint8_t* a, int64_t rsa, int64_t csa, const uint8_t* b,
+                                   int64_t rsb, int64_t csb, int m, int k, int n, void* ws,
+                                   const TropEpi& e, uint64_t* w, int64_t rsw, int64_t csw,
+                                   cudaStream_t s) {
+    const int mp = (m + TW_BM - 1) / TW_BM * TW_BM;
+    const int np = (n + TW_BN - 1) / TW_BN * TW_BN;
+    const int kp = (k + TW_BK - 1) / TW_BK * TW_BK;
+    int32_t* at = static_cast<int32_t*>(ws);
+    int32_t* bt = at + static_cast<int64_t>(mp) * kp;
+    if (kp > 0) {
+        trop_witness_pack_a_kernel<<<grid_for(static_cast<int64_t>(mp) * kp), 256, 0, s>>>(
+            at, mp, kp, a, rsa, csa, m, k);
+        trop_witness_pack_b_kernel<<<grid_for(static_cast<int64_t>(np) * kp), 256, 0, s>>>(
+            bt, np, kp, b, rsb, csb, k, n);
+    }
+    dim3 grid(np / TW_BN, mp / TW_BM);
+    trop_i8_witness_kernel<<<grid, TW_THREADS, 0, s>>>(at, bt, mp, np, kp, e, w, rsw, csw);
+    return cudaGetLastError();
+}
+
+cudaError_t trop_generic_witness_launch(const uint8_t* a, int64_t rsa, int64_t csa,
+                                        const uint8_t* b, int64_t rsb, int64_t csb, int ebytes,
+                                        int m, int k, int n, const TropEpi& e, uint64_t* w,
+                                        int64_t rsw, int64_t csw, cudaStream_t s) {
+    dim3 block(16, 16);
+    dim3 grid((n + 15) / 16, (m + 15) / 16);
+    trop_generic_witness_kernel<<<grid, block, 0, s>>>(a, rsa, csa, b, rsb, csb, ebytes, k, e, w,
+                                                       rsw, csw);
     return cudaGetLastError();
 }
 

@@ -29,4 +29,21 @@ cudaError_t trop_generic_launch(const uint8_t* a, int64_t rsa, int64_t csa, cons
                                 int64_t rsb, int64_t csb, int ebytes, int m, int k, int n,
                                 const TropEpi& e, cudaStream_t s);
 
+// driver::gemm_selected (crates/uor-matmul-gemm/src/selection.rs:212-330): the product
+// and, per cell, the least index attaining the maximum of the reduction (D-6); 0 when
+// every term is the semiring zero or k is 0. `w` is the witness (u64) view's origin.
+// Trop<i8> with k <= 65536: one pass over (value, index) keys; `ws` holds
+// trop_witness_workspace() bytes.
+cudaError_t trop_i8_witness_launch(const uint8_t* a, int64_t rsa, int64_t csa, const uint8_t* b,
+                                   int64_t rsb, int64_t csb, int m, int k, int n, void* ws,
+                                   const TropEpi& e, uint64_t* w, int64_t rsw, int64_t csw,
+                                   cudaStream_t s);
+size_t trop_witness_workspace(int m, int k, int n);
+constexpr int TROP_WITNESS_MAX_K = 65536;
+// Any Trop<E>, any k: one thread per cell.
+cudaError_t trop_generic_witness_launch(const uint8_t* a, int64_t rsa, int64_t csa,
+                                        const uint8_t* b, int64_t rsb, int64_t csb, int ebytes,
+                                        int m, int k, int n, const TropEpi& e, uint64_t* w,
+                                        int64_t rsw, int64_t csw, cudaStream_t s);
+
 }  // namespace uor

@@ -116,6 +116,7 @@ def lib():
             "uor_b200_sgemm": ([Z, Z, Z, L64, P, D, D, P, D, D, L64, P, D, D, CP], I),
             "uor_b200_dgemm": ([Z, Z, Z, L64, P, D, D, P, D, D, L64, P, D, D, CP], I),
             "uor_b200_gemm_tropical": ([I, I, VP, VP, VP, Trop, Trop, CP], I),
+            "uor_b200_gemm_tropical_selected": ([I, I, VP, VP, VP, VP, Trop, Trop, CP], I),
             "uor_b200_coded_gemm": ([I, VP, P, Z, Z, Z, U32, P, Z, VP, L64, L64, CP], I),
             "uor_b200_tabulated_gemm": ([I, VP, P, Z, Z, Z, U32, P, Z, VP, L64, L64, CP], I),
             "uor_b200_codec_gemm": ([I, VP, ctypes.POINTER(Codec), P, Z, Z, Z, U32, VP, L64, L64,
@@ -330,6 +331,19 @@ def gemm_tropical(elem, out, a, av, b, bv, c, cv, alpha=(0, True), beta=(0, Fals
                                         ctypes.byref(C), Trop(alpha[0], int(alpha[1])),
                                         Trop(beta[0], int(beta[1])), ctypes.byref(call)),
            "gemm_tropical")
+
+
+def gemm_tropical_selected(elem, out, a, av, b, bv, c, cv, w, wv, alpha=(0, True),
+                           beta=(0, False), encode=NEAREST, ctx=None, route=None):
+    """driver::gemm_selected: the product and the least-index witness (u64 view w)."""
+    dev = _on_device(a, b, c, w)
+    A, B, C, W = view(a, *av), view(b, *bv), view(c, *cv), view(w, *wv)
+    call = make_call(encode, dev, ctx, route)
+    _check(lib().uor_b200_gemm_tropical_selected(elem, out, ctypes.byref(A), ctypes.byref(B),
+                                                 ctypes.byref(C), ctypes.byref(W),
+                                                 Trop(alpha[0], int(alpha[1])),
+                                                 Trop(beta[0], int(beta[1])), ctypes.byref(call)),
+           "gemm_tropical_selected")
 
 
 # ------------------------------------------------------------------ codec
