@@ -41,7 +41,8 @@ sys.path.insert(0, ROOT)
 
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
-WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "f32", "wide", "wide-splitk", "trop")
+WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "f32", "wide", "wide-splitk", "trop",
+             "trop-witness")
 
 
 def parse():
@@ -529,19 +530,25 @@ def wl_wide(args, U, torch, rank):
     return w
 
 
-def wl_trop(args, U, torch, rank):
-    """configs[4]'s max-plus half: Trop<i8> 8192^3 with 5 % -inf, Trop<i32> output."""
+def wl_trop(args, U, torch, rank, selected=False):
+    """configs[4]'s max-plus half: Trop<i8> 8192^3 with 5 % -inf, Trop<i32> output; with
+    `selected`, gemm_selected's witness (the least index attaining each maximum) too."""
     import numpy as np
     m = k = n = 8192
     A = torch.from_numpy(U.corpus(1, U.CORPUS_TROP_I8, m * k)).cuda()
     B = torch.from_numpy(U.corpus(2 + 1000 * rank, U.CORPUS_TROP_I8, k * n)).cuda()
     C = torch.zeros(m * n * 8, dtype=torch.uint8, device="cuda")
-    # A and B packing into i16x2 lanes, the max-plus kernel
+    Wt = torch.zeros(m * n, dtype=torch.int64, device="cuda") if selected else None
+    # A and B packing, the max-plus kernel
     w = SimpleNamespace(route=U.Route(), units=float(m) * k * n, launches=3)
 
     def step(i, ctx):
-        U.gemm_tropical(U.TROP_I8, U.TROP_I32, A, (m, k, k, 1), B, (k, n, n, 1), C, (m, n, n, 1),
-                        ctx=ctx, route=w.route, asynchronous=True)
+        if selected:
+            U.gemm_tropical_selected(U.TROP_I8, U.TROP_I32, A, (m, k, k, 1), B, (k, n, n, 1), C,
+                                     (m, n, n, 1), Wt, (m, n, n, 1), ctx=ctx, route=w.route)
+        else:
+            U.gemm_tropical(U.TROP_I8, U.TROP_I32, A, (m, k, k, 1), B, (k, n, n, 1), C,
+                            (m, n, n, 1), ctx=ctx, route=w.route, asynchronous=True)
 
     def check(last):
         pass  # checked bit for bit on rows by the CPU leg and the GPU tests
@@ -596,6 +603,24 @@ def wl_trop(args, U, torch, rank):
                                "terms per fused add-max x 1.965 GHz",
                 "traffic": None, "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
+    if selected:
+        # one fused 32-bit add-max per term on (value, index) keys: half the packed rate
+        w.e2e = None
+        w.metric = ("exact max-plus GEMM with selection witness Tterm/s, Trop<i8> 8192^3 "
+                    "(bit-exact, Trop<i32> + least-index witness out)")
+        w.algorithmic_bytes = 4 * (m * k + k * n) + 16 * m * n
+        w.dtype = "int32 (value, index) keys"
+        w.config = dict(w.config, workload="Trop<i8> max-plus 8192^3 + gemm_selected witness "
+                                           "per GPU, column-block sharded")
+
+        def roofline_sel(avg_ms):
+            r = roofline(avg_ms)
+            r["peak"] = r["peak"] / 2
+            r["frac"] = r["achieved"] / r["peak"]
+            r["peak_source"] = ("nominal: 148 SMs x 64 lanes/clk x 1 term per fused 32-bit "
+                                "add-max x 1.965 GHz")
+            return r
+        w.roofline = roofline_sel
     return w
 
 
@@ -665,7 +690,7 @@ def build_workload(name, args, U, torch, rank, world=1):
         return wl_wide(args, U, torch, rank)
     if name == "wide-splitk":
         return wl_wide_splitk(args, U, torch, rank, world)
-    return wl_trop(args, U, torch, rank)
+    return wl_trop(args, U, torch, rank, selected=name == "trop-witness")
 
 
 # ---------------------------------------------------------------- timing
