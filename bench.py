@@ -42,7 +42,7 @@ sys.path.insert(0, ROOT)
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
 WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "f32", "wide", "wide-splitk", "trop",
-             "trop-witness")
+             "trop-witness", "complex")
 
 
 def parse():
@@ -530,6 +530,73 @@ def wl_wide(args, U, torch, rank):
     return w
 
 
+def wl_complex(args, U, torch, rank):
+    """Complex<i32> full range, 1024 x 16384 x 1024, exact Complex<i128> output: the real
+    product of the operands' real images (1024 x 32768 x 2048) on the limb path."""
+    import numpy as np
+    m, k, n = 1024, 16384, 1024
+    A = torch.from_numpy(U.corpus(4, U.CORPUS_I32_FULL, 2 * m * k)).cuda()
+    B = torch.from_numpy(U.corpus(5 + 1000 * rank, U.CORPUS_I32_FULL, 2 * k * n)).cuda()
+    C = torch.zeros(m * n * 4, dtype=torch.int64, device="cuda")
+    # A and B byte slicing (B into its real image), the limb-pair GEMM, the recombination
+    w = SimpleNamespace(route=U.Route(), units=8.0 * m * k * n, launches=4)
+
+    def step(i, ctx):
+        U.gemm_complex(U.I32, U.I128, A, (m, k, k, 1), B, (k, n, n, 1), C, (m, n, n, 1),
+                       ctx=ctx, route=w.route, asynchronous=True)
+
+    def check(last):
+        pass  # checked bit for bit by the CPU leg and the GPU tests
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, b = A.cpu().numpy(), B.cpu().numpy()
+        threads = host_threads(orc)
+
+        def run(rows):
+            c = np.zeros(rows * n * 4, np.int64)
+            orc.gemm_complex(orc.View(a, rows, k, k, 1), orc.View(b, k, n, n, 1),
+                             orc.View(c, rows, n, n, 1), out_bits=128, threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        assert np.array_equal(c, C[:rows * n * 4].cpu().numpy()), "GPU rows differ"
+        return {"value": 8.0 * rows * k * n / dt / 1e12, "unit": "TOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), C restatement of the Complex<i32> "
+                          "componentwise mac into i128 parts, OpenMP over rows; the GPU's rows "
+                          "were compared"}
+
+    def e2e(steps, ctx, stream):
+        Ah, Bh = A.cpu().pin_memory(), B.cpu().pin_memory()
+        Ch = torch.empty(m * n * 4, dtype=torch.int64).pin_memory()
+        return timed_host(lambda: U.gemm_complex(U.I32, U.I128, Ah, (m, k, k, 1), Bh,
+                                                 (k, n, n, 1), Ch, (m, n, n, 1), ctx=ctx),
+                          steps, stream, 8 * (m * k + k * n), 32 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = "exact Complex<i32> -> Complex<i128> GEMM TOPS (8 integer ops per complex mac), " \
+               "1024x16384x1024 (bit-exact)"
+    w.unit, w.dtype = "TOPS", "Complex<int32> in (4 x 4 int8 limb pairs), Complex<int128> out"
+    w.config = {"workload": "Complex<i32> GEMM 1024x16384x1024 per GPU (alphabet.rs Complex), "
+                            "column-block sharded", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = "256 MiB of operands per step (> L2)"
+    w.algorithmic_bytes = 8 * (m * k + k * n) + 32 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        ach = 16 * w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "basis": "int8 limb-pair ops (16 x 2 x m x 2k x 2n) over the whole call "
+                         "(slicing, GEMM, recombination)",
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
 def wl_trop(args, U, torch, rank, selected=False):
     """configs[4]'s max-plus half: Trop<i8> 8192^3 with 5 % -inf, Trop<i32> output; with
     `selected`, gemm_selected's witness (the least index attaining each maximum) too."""
@@ -690,6 +757,8 @@ def build_workload(name, args, U, torch, rank, world=1):
         return wl_wide(args, U, torch, rank)
     if name == "wide-splitk":
         return wl_wide_splitk(args, U, torch, rank, world)
+    if name == "complex":
+        return wl_complex(args, U, torch, rank)
     return wl_trop(args, U, torch, rank, selected=name == "trop-witness")
 
 

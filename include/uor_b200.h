@@ -192,6 +192,19 @@ int uor_b200_gemm_ex_i8_i32(size_t m, size_t k, size_t n, int64_t alpha, const i
                             size_t lda, const int8_t *b, size_t ldb, int64_t beta, int32_t *c,
                             size_t ldc, const uor_b200_call *call);
 
+/* driver::gemm (crates/uor-matmul-gemm/src/driver.rs:67-79) over Complex<elem>
+ * (crates/uor-matmul-core/src/alphabet.rs:656-776), encoding into Complex<out>
+ * componentwise (EncodeFrom<ComplexAcc>, alphabet.rs:765-776). elem in {I32, I64}
+ * (accumulators i128 and Limbs<3> per part); out in {I8, I16, I32, I64, I128}.
+ * Buffers hold repr(C) {re, im} pairs; len, rows, cols and strides count complex
+ * elements. The mac is re += a.re*w.re + a.im*(-w.im), im += a.re*w.im + a.im*w.re
+ * with -w.im negated modulo 2^bits (the release build's negation: -MIN is MIN).
+ * alpha and beta scale each part as Linear scales a scalar accumulator; alpha = 1,
+ * beta = 0 is the plain encode. */
+int uor_b200_gemm_complex(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view *a,
+                          const uor_b200_view *b, const uor_b200_view_mut *c, int64_t alpha,
+                          int64_t beta, const uor_b200_call *call);
+
 /* ----------------------------------------------------------- float family */
 
 /* gemm_float_packed over a Triple (crates/uor-matmul-gemm/src/float.rs:1824)

@@ -59,6 +59,8 @@ def lib():
                                               I, I]
         _LIB.uor_oracle_coded_gemm.argtypes = [I, Z, Z, Z, L, P, D, D, P, I, P, Z, I, L, P, D, D,
                                                I, I]
+        _LIB.uor_oracle_gemm_complex.argtypes = [I, I, Z, Z, Z, L, P, D, D, P, D, D, L, P, D, D,
+                                                 I, I]
         _LIB.uor_oracle_max_threads.restype = I
         _LIB.uor_oracle_gemm_i8_blocked.argtypes = [Z, Z, Z, L, P, P, L, P, Z, I, I]
     return _LIB
@@ -104,6 +106,23 @@ def gemm_int(a: View, b: View, c: View, alpha=1, beta=0, mode=NEAREST, threads=0
     obits = out_bits or _bits_of(c.arr.dtype)
     lib().uor_oracle_gemm_int(ebits, obits, a.rows, a.cols, b.cols, alpha, a.ptr(), a.rs, a.cs,
                               b.ptr(), b.rs, b.cs, beta, c.ptr(), c.rs, c.cs, mode, threads)
+
+
+def gemm_complex(a: View, b: View, c: View, alpha=1, beta=0, mode=NEAREST, threads=0,
+                 out_bits=None):
+    """Complex<i32|i64> GEMM (alphabet.rs:656-776) with the per-part epilogue.
+
+    Each view's ``arr`` holds the interleaved parts (re, im); ``rows``, ``cols``,
+    strides and ``origin`` count whole complex elements."""
+    ebits = _bits_of(a.arr.dtype)
+    obits = out_bits or _bits_of(c.arr.dtype)
+
+    def ptr(v, bits):
+        return v.arr.ctypes.data + 2 * v.origin * (bits // 8)
+
+    lib().uor_oracle_gemm_complex(ebits, obits, a.rows, a.cols, b.cols, alpha, ptr(a, ebits),
+                                  a.rs, a.cs, ptr(b, ebits), b.rs, b.cs, beta, ptr(c, obits), c.rs,
+                                  c.cs, mode, threads)
 
 
 def gemm_i8_blocked(a, b, c, m, k, n, alpha=1, beta=0, ldc=None, mode=NEAREST, threads=0):
@@ -278,6 +297,44 @@ def int_gemm_py(A, B, alpha=1, beta=0, C=None, out_bits=32, mode=NEAREST):
             row.append(tot)
         out.append(row)
     return out
+
+
+def complex_gemm_py(A, B, ebits=32, alpha=1, beta=0, C=None, out_bits=32, mode=NEAREST):
+    """Pure-Python twin of gemm_complex on nested lists of (re, im) pairs.
+
+    mac: re += a.re w.re + a.im (-w.im), im += a.re w.im + a.im w.re
+    (alphabet.rs:712-717), -w.im wrapping in ebits (the release build's negation)."""
+    half = 1 << (ebits - 1)
+
+    def wrapneg(v):
+        v = (-v) & ((1 << ebits) - 1)
+        return v - (1 << ebits) if v >= half else v
+
+    m, k, n = len(A), len(B), len(B[0]) if B else 0
+    re = [[sum(A[i][p][0] * B[p][j][0] + A[i][p][1] * wrapneg(B[p][j][1]) for p in range(k))
+           for j in range(n)] for i in range(m)]
+    im = [[sum(A[i][p][0] * B[p][j][1] + A[i][p][1] * B[p][j][0] for p in range(k))
+           for j in range(n)] for i in range(m)]
+    acc_bits = 192 if ebits == 64 else 128
+    lo, hi = -(1 << (acc_bits - 1)), (1 << (acc_bits - 1)) - 1
+    mn, mx = -(1 << (out_bits - 1)), (1 << (out_bits - 1)) - 1
+
+    def wrap(v, bits):
+        v &= (1 << bits) - 1
+        return v - (1 << bits) if v >> (bits - 1) else v
+
+    def part(acc, prior):
+        # ScaleExact: saturating for i128 (epilogue.rs:280-288), modular for Limbs<3>.
+        tot = wrap(acc * alpha, 192) if ebits == 64 else max(lo, min(hi, acc * alpha))
+        if beta != 0:
+            pr = wrap(prior * beta, 192) if ebits == 64 else max(lo, min(hi, prior * beta))
+            tot = wrap(tot + pr, acc_bits)
+        if mode == WRAPPING:
+            return wrap(tot, out_bits)
+        return max(mn, min(mx, tot))
+
+    return [[(part(re[i][j], C[i][j][0] if C else 0), part(im[i][j], C[i][j][1] if C else 0))
+             for j in range(n)] for i in range(m)]
 
 
 # ---- float twin: exact rationals, one RNE encode (acc.rs:1734-1868) ------

@@ -234,6 +234,73 @@ int uor_oracle_gemm_int(int ebits, int obits, size_t m, size_t k, size_t n, int6
 }
 
 /* ------------------------------------------------------------------------- */
+/* Complex<i32 | i64> elements                                                */
+/* ------------------------------------------------------------------------- */
+
+/* Complex<T> is repr(C) {T re; T im} (alphabet.rs:656-663); strides count whole
+ * complex elements, part h of element e sits at scalar offset 2e + h. The mac is the
+ * scalar mac applied to (re, re), (im, -w.im), (re, w.im), (im, re) (alphabet.rs:
+ * 712-717); -w.im is the release build's wrapping negation, so -MIN is MIN. Each part
+ * has its own exact accumulator (ComplexAcc: i128 for i32, Limbs<3> for i64) and is
+ * encoded on its own (EncodeFrom<ComplexAcc>, alphabet.rs:765-776). alpha and beta
+ * apply to each part as Linear applies to a scalar accumulator (epilogue.rs:79-93);
+ * alpha = 1, beta = 0 is the plain encode. */
+static inline i128 wrapneg(i128 y, int ebits) {
+    if (ebits == 64) return (i128)(int64_t)(0 - (uint64_t)(int64_t)y);
+    return (i128)(int32_t)(0u - (uint32_t)(int32_t)y);
+}
+
+int uor_oracle_gemm_complex(int ebits, int obits, size_t m, size_t k, size_t n, int64_t alpha,
+                            const void *a, ptrdiff_t rsa, ptrdiff_t csa, const void *b,
+                            ptrdiff_t rsb, ptrdiff_t csb, int64_t beta, void *c, ptrdiff_t rsc,
+                            ptrdiff_t csc, int mode, int threads) {
+    if (m == 0 || n == 0) return 0;
+    set_threads(threads);
+    long long mm = (long long)m;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (long long ii = 0; ii < mm; ii++) {
+        size_t i = (size_t)ii;
+        for (size_t j = 0; j < n; j++) {
+            limbs3 acc3[2] = {{{0, 0, 0}}, {{0, 0, 0}}};
+            i128 acc[2] = {0, 0};
+            for (size_t p = 0; p < k; p++) {
+                ptrdiff_t ao = 2 * ((ptrdiff_t)i * rsa + (ptrdiff_t)p * csa);
+                ptrdiff_t bo = 2 * ((ptrdiff_t)p * rsb + (ptrdiff_t)j * csb);
+                i128 are = load_int(a, ebits, ao), aim = load_int(a, ebits, ao + 1);
+                i128 bre = load_int(b, ebits, bo), bim = load_int(b, ebits, bo + 1);
+                i128 t[4] = {are * bre, aim * wrapneg(bim, ebits), are * bim, aim * bre};
+                if (ebits == 64) {
+                    for (int q = 0; q < 4; q++) l3_add_i128(&acc3[q >> 1], t[q]);
+                } else {
+                    acc[0] += t[0] + t[1];
+                    acc[1] += t[2] + t[3];
+                }
+            }
+            for (int h = 0; h < 2; h++) {
+                ptrdiff_t co = 2 * ((ptrdiff_t)i * rsc + (ptrdiff_t)j * csc) + h;
+                i128 outv;
+                if (ebits == 64) {
+                    limbs3 tot = l3_scale(acc3[h], alpha);
+                    if (beta != 0) {
+                        limbs3 pr = {{0, 0, 0}};
+                        l3_add_i128(&pr, load_int(c, obits, co));
+                        tot = l3_combine(tot, l3_scale(pr, beta));
+                    }
+                    outv = l3_encode(tot, obits, mode);
+                } else {
+                    i128 tot = sat_mul_i128(acc[h], alpha);
+                    if (beta != 0)
+                        tot = (i128)((u128)tot + (u128)sat_mul_i128(load_int(c, obits, co), beta));
+                    outv = encode_i128_into(tot, out_min(obits), out_max(obits), mode);
+                }
+                store_int(c, obits, co, outv);
+            }
+        }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------------- */
 /* Codec tier: Packed<Grid<N>, P> over i8                                     */
 /* ------------------------------------------------------------------------- */
 

@@ -213,6 +213,31 @@ def test_host_pointer_pipeline_blocks_are_exact():
         assert np.array_equal(got, want), (alpha, beta)
 
 
+@pytest.mark.parametrize("pinned", [False, True])
+def test_host_pipeline_split_first_row_and_whole_blocks(pinned):
+    """Several row and column blocks: the first row of blocks is cut into narrower
+    pieces, the rows after it into whole blocks; a pinned C takes the interleaved
+    copy-out. Every cell, with and without a read C."""
+    m, k, n = 4400, 96, 4200
+    a, b = i8(35, m * k), i8(36, k * n)
+    rng = np.random.default_rng(7)
+    prior = rng.integers(-(2**31), 2**31, size=m * n, dtype=np.int64).astype(np.int32)
+    for alpha, beta in [(1, 0), (-3, 2)]:
+        want = prior.copy()
+        oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), alpha, beta,
+                   U.NEAREST, U.I32)
+        if pinned:
+            host = torch.from_numpy(prior.copy()).pin_memory()
+            got = host.numpy()
+        else:
+            got = prior.copy()
+        route = U.Route()
+        U.gemm(U.I8, U.I32, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), alpha, beta,
+               route=route)
+        assert np.array_equal(got, want), (alpha, beta)
+        assert route.kernel == 1
+
+
 @pytest.mark.slow
 def test_headline_8192_cubed_checksums_and_samples():
     """At the headline size: Freivalds-style checksums (exact in int64) and sampled

@@ -364,3 +364,49 @@ def test_codec_tier_decode_restatement():
         [-2, -1, 0, 1, 2, 3, 4, 5]]
     assert dec(0, np.array([0x21], np.uint8), 1, 2, table=np.arange(16, dtype=np.int8),
                per_byte=2, zero=3).tolist() == [[-2, -1]]
+
+
+def test_complex_mac_kat():
+    """complex_mac_is_componentwise_ck_01 (alphabet.rs:824-833): (3 + 4i)(5 - 2i) = 23 + 14i."""
+    a, b = np.array([3, 4], np.int32), np.array([5, -2], np.int32)
+    c = np.zeros(2, np.int32)
+    orc.gemm_complex(View(a, 1, 1, 1, 1), View(b, 1, 1, 1, 1), View(c, 1, 1, 1, 1))
+    assert c.tolist() == [23, 14]
+    assert orc.complex_gemm_py([[(3, 4)]], [[(5, -2)]]) == [[(23, 14)]]
+
+
+def test_complex_negation_wraps_like_the_release_build():
+    """-w.im of MIN is MIN (Cargo.toml's release profile has overflow-checks off), so
+    a.im * (-w.im) = a.im * MIN there."""
+    for ebits, et in ((32, np.int32), (64, np.int64)):
+        lo = int(np.iinfo(et).min)
+        a, b = np.array([0, 1], et), np.array([0, lo], et)
+        c = np.zeros(4, np.int64)  # Complex<i128>
+        orc.gemm_complex(View(a, 1, 1, 1, 1), View(b, 1, 1, 1, 1), View(c, 1, 1, 1, 1),
+                         out_bits=128)
+        re = int(c[0].astype(np.uint64)) + (int(c[1]) << 64)
+        assert re == lo  # not -lo
+        assert orc.complex_gemm_py([[(0, 1)]], [[(0, lo)]], ebits, out_bits=128) == [[(lo, 0)]]
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_c_complex_matches_python_twin(seed):
+    rng = np.random.default_rng(100 + seed)
+    m, k, n = (int(x) for x in rng.integers(1, 7, size=3))
+    for ebits, obits in ((32, 32), (32, 64), (64, 64), (64, 16)):
+        et, ot = orc.INT_DTYPES[ebits], orc.INT_DTYPES[obits]
+        info, oinfo = np.iinfo(et), np.iinfo(ot)
+        a = rng.integers(info.min, info.max, size=2 * m * k, endpoint=True).astype(et)
+        b = rng.integers(info.min, info.max, size=2 * k * n, endpoint=True).astype(et)
+        b[1::7] = info.min  # imaginary parts at MIN exercise the wrapping negation
+        c0 = rng.integers(oinfo.min, oinfo.max, size=2 * m * n, endpoint=True).astype(ot)
+        pairs = lambda x, r, q: [[(int(x[2 * (i * q + j)]), int(x[2 * (i * q + j) + 1]))
+                                  for j in range(q)] for i in range(r)]
+        for alpha, beta in ((1, 0), (3, -1), (-(2**63), 2**62)):
+            for mode in (orc.NEAREST, orc.WRAPPING):
+                c = c0.copy()
+                orc.gemm_complex(View(a, m, k, k, 1), View(b, k, n, n, 1), View(c, m, n, n, 1),
+                                 alpha=alpha, beta=beta, mode=mode)
+                want = orc.complex_gemm_py(pairs(a, m, k), pairs(b, k, n), ebits, alpha, beta,
+                                           pairs(c0, m, n), obits, mode)
+                assert pairs(c, m, n) == want, (ebits, obits, alpha, beta, mode)

@@ -37,12 +37,12 @@ bool device_ptrs(const uor_b200_call* call) {
 // Everything after validation, with the context locked: stage, compute, stage back.
 int int_gemm_locked(uor_b200_ctx* ctx, uor_b200_dtype elem, int kind, const Operand& A,
                     const Operand& B, const Operand& C, int64_t alpha, int64_t beta, int mode,
-                    const uor_b200_call* call, uor_b200_route* route) {
+                    const uor_b200_call* call, uor_b200_route* route, bool cplx = false) {
     const size_t m = A.rows, k = A.cols, n = B.cols;
     int st = UOR_B200_OK;
     const bool dev = device_ptrs(call);
     const LinearEpi epi{alpha, beta, mode, kind};
-    if (!dev && elem == UOR_B200_I8 && i8_pipeline_applies(A, B, C)) {
+    if (!dev && !cplx && elem == UOR_B200_I8 && i8_pipeline_applies(A, B, C)) {
         st = run_i8_gemm_pipelined(ctx, A, B, C, epi, route);
         if (st != UOR_B200_UNSUPPORTED) return st;
     }
@@ -52,13 +52,13 @@ int int_gemm_locked(uor_b200_ctx* ctx, uor_b200_dtype elem, int kind, const Oper
     if ((st = stage_in(ctx, SLOT_B, B, dev, &db)) != UOR_B200_OK) return st;
     if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs)) != UOR_B200_OK) return st;
 
-    if (elem == UOR_B200_I8)
+    if (elem == UOR_B200_I8 && !cplx)
         st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs,
                          reinterpret_cast<const int8_t*>(db), B.rs, B.cs, cs.dev_origin, C.rs,
                          C.cs, m, k, n, epi, route);
     else
         st = run_wide_gemm(ctx, (int)dtype_size(elem), da, A.rs, A.cs, db, B.rs, B.cs,
-                           cs.dev_origin, C.rs, C.cs, m, k, n, epi, route);
+                           cs.dev_origin, C.rs, C.cs, m, k, n, epi, route, cplx);
     if (st != UOR_B200_OK) return st;
     if ((st = stage_out_end(ctx, cs)) != UOR_B200_OK) return st;
     if (!dev) return uor_b200_ctx_sync(ctx);
@@ -67,7 +67,7 @@ int int_gemm_locked(uor_b200_ctx* ctx, uor_b200_dtype elem, int kind, const Oper
 
 int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Operand& B,
                     const Operand& C, int64_t alpha, int64_t beta, int mode,
-                    const uor_b200_call* call) {
+                    const uor_b200_call* call, bool cplx = false) {
     uor_b200_route local_route{};
     uor_b200_route* route = call && call->route ? call->route : &local_route;
     *route = uor_b200_route{};
@@ -76,7 +76,7 @@ int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Opera
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
-    return int_gemm_locked(ctx, elem, kind, A, B, C, alpha, beta, mode, call, route);
+    return int_gemm_locked(ctx, elem, kind, A, B, C, alpha, beta, mode, call, route, cplx);
 }
 
 int gemm_views(uor_b200_dtype elem, uor_b200_dtype out, const void* a, size_t a_len, size_t am,
@@ -99,9 +99,40 @@ int gemm_views(uor_b200_dtype elem, uor_b200_dtype out, const void* a, size_t a_
     return int_gemm_placed(elem, kind, A, B, C, alpha, beta, mode, call);
 }
 
+// Complex<i32 | i64> (alphabet.rs:656-776): views count complex elements, each
+// {re, im} of the part type.
+int gemm_complex_views(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a,
+                       const uor_b200_view* b, const uor_b200_view_mut* c, int64_t alpha,
+                       int64_t beta, const uor_b200_call* call) {
+    int kind = 0, mode = 0;
+    if (!a || !b || !c) return UOR_B200_INVALID_ARGUMENT;
+    if ((elem != UOR_B200_I32 && elem != UOR_B200_I64) || !int_out(out, &kind))
+        return UOR_B200_UNSUPPORTED;
+    if (call_mode(call, &mode) != UOR_B200_OK) return UOR_B200_INVALID_ARGUMENT;
+    const size_t es = 2 * dtype_size(elem), os = 2 * dtype_size(out);
+    Operand A, B, C;
+    int st;
+    if ((st = place_view(a->data, a->len, a->rows, a->cols, a->rs, a->cs, es, &A)) != UOR_B200_OK)
+        return st;
+    if ((st = place_view(b->data, b->len, b->rows, b->cols, b->rs, b->cs, es, &B)) != UOR_B200_OK)
+        return st;
+    if ((st = place_view(c->data, c->len, c->rows, c->cols, c->rs, c->cs, os, &C)) != UOR_B200_OK)
+        return st;
+    if (a->cols != b->rows || c->rows != a->rows || c->cols != b->cols)
+        return UOR_B200_NONCONFORMANT;
+    if (self_aliases(c->rows, c->cols, c->rs, c->cs)) return UOR_B200_OUTPUT_ALIASES;
+    return int_gemm_placed(elem, kind, A, B, C, alpha, beta, mode, call, true);
+}
+
 }  // namespace
 
 extern "C" {
+
+int uor_b200_gemm_complex(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a,
+                          const uor_b200_view* b, const uor_b200_view_mut* c, int64_t alpha,
+                          int64_t beta, const uor_b200_call* call) {
+    return gemm_complex_views(elem, out, a, b, c, alpha, beta, call);
+}
 
 int uor_b200_gemm(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a,
                   const uor_b200_view* b, const uor_b200_view_mut* c, int64_t alpha,

@@ -52,18 +52,34 @@ int run_i8_gemm_pipelined(uor_b200_ctx* ctx, const Operand& A, const Operand& B,
     // About 2048 x 2048 blocks, at most 8 x 8 of them; block edges on 256-cell tiles.
     // Smaller blocks start the copy-out earlier but cost more in short copy rows and
     // launches than they win (8192^3 from pinned memory: 5.85 ms at 2048, 6.46 ms at
-    // 1024, 7.48 ms unpipelined).
+    // 1024, 7.48 ms unpipelined). Only the first row of blocks is cut finer: its first
+    // column block is split into quarter, quarter and half widths, so that the first
+    // copy-out waits for one A row block and a quarter of a B column block instead of a
+    // whole one. With row blocks of k/4 rows or more, each further B piece brings as
+    // many bytes of output as of input, so the copy-out stream stays busy from then on.
     auto blocks = [](size_t x) { return (int)std::min<size_t>(8, (x + 2047) / 2048); };
     const int R = blocks(m), S = blocks(n);
     const size_t rb = (m + R - 1) / R + 255 & ~(size_t)255;
     const size_t cb = (n + S - 1) / S + 255 & ~(size_t)255;
+    // B pieces in copy order: column ranges [pc[i], pc[i + 1]).
+    size_t pc[12];
+    int P = 0;
+    pc[0] = 0;
+    const size_t q = cb / 4 & ~(size_t)255;
+    if (S > 1 && q >= 256) {
+        pc[++P] = q;
+        pc[++P] = 2 * q;
+    }
+    for (size_t c0 = cb; c0 < n; c0 += cb) pc[++P] = c0;
+    pc[++P] = n;
     const auto* ha = A.origin;
     const auto* hb = B.origin;
     auto* hc = const_cast<uint8_t*>(C.origin);
     cudaStream_t in = ctx->copy_in, out = ctx->copy_out, cs = ctx->stream;
-    // events: [0, R) A blocks, [R, R+S) B blocks, then per block: C-in, C-done
+    // events: [0, R) A row blocks, [R, R + P) B pieces, then per C block: C-in, C-done
     auto ev = [&](int i) { return ctx_event(ctx, i, &st); };
-    for (int i = 0; i < R + S + 2 * R * S; ++i)
+    const int nblk = P + (R - 1) * S;
+    for (int i = 0; i < R + P + 2 * nblk; ++i)
         if (!ev(i)) return st;
     const bool reads_c = epi.beta != 0;
     cudaPointerAttributes pa{};
@@ -81,13 +97,13 @@ int run_i8_gemm_pipelined(uor_b200_ctx* ctx, const Operand& A, const Operand& B,
                               in);
         cudaEventRecord(ev(r), in);
     };
-    auto put_b = [&](int c) {
-        const size_t c0 = std::min(c * cb, n), nc = std::min(cb, n - c0);
+    auto put_b = [&](int i) {
+        const size_t c0 = pc[i], nc = pc[i + 1] - pc[i];
         if (nc) cudaMemcpy2DAsync(db + c0, n, hb + c0, B.rs, nc, k, cudaMemcpyHostToDevice, in);
-        cudaEventRecord(ev(R + c), in);
+        cudaEventRecord(ev(R + i), in);
     };
     put_a(0);
-    for (int c = 0; c < S; ++c) put_b(c);
+    for (int i = 0; i < P; ++i) put_b(i);
     for (int r = 1; r < R; ++r) put_a(r);
     // Copies already queued must finish before the host buffers are handed back, also
     // when a block fails to launch.
@@ -97,48 +113,60 @@ int run_i8_gemm_pipelined(uor_b200_ctx* ctx, const Operand& A, const Operand& B,
         cudaStreamSynchronize(out);
         return status;
     };
-    for (int r = 0; r < R; ++r) {
-        for (int c = 0; c < S; ++c) {
-            const size_t r0 = r * rb, c0 = c * cb;
-            if (r0 >= m || c0 >= n) continue;
-            const size_t mr = std::min(rb, m - r0), nc = std::min(cb, n - c0);
-            const int blk = r * S + c;
-            uint8_t* dcb = dc + (r0 * n + c0) * ob;
-            uint8_t* hcb = hc + (r0 * C.rs + c0) * ob;
-            if (reads_c) {
-                cudaMemcpy2DAsync(dcb, n * ob, hcb, C.rs * ob, nc * ob, mr, cudaMemcpyHostToDevice,
-                                  in);
-                cudaEventRecord(ev(R + S + 2 * blk), in);
-                cudaStreamWaitEvent(cs, ev(R + S + 2 * blk), 0);
-            }
-            cudaStreamWaitEvent(cs, ev(r), 0);
-            cudaStreamWaitEvent(cs, ev(R + c), 0);
-            uor_b200_route sub{};
-            st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da + r0 * k), (ptrdiff_t)k, 1,
-                             reinterpret_cast<const int8_t*>(db + c0), (ptrdiff_t)n, 1, dcb,
-                             (ptrdiff_t)n, 1, mr, k, nc, epi, &sub);
-            if (st) return drain(st);
-            if (route && blk == 0) *route = sub;
-            cudaEventRecord(ev(R + S + 2 * blk + 1), cs);
-            if (pinned_out) {
-                cudaStreamWaitEvent(out, ev(R + S + 2 * blk + 1), 0);
-                cudaMemcpy2DAsync(hcb, C.rs * ob, dcb, n * ob, nc * ob, mr, cudaMemcpyDeviceToHost,
-                                  out);
-            }
+    // The C blocks in launch order: the pieces along the first row, whole blocks after.
+    struct Blk {
+        size_t r0, mr, c0, nc;
+        int a_ev, b_ev;
+    };
+    auto block_at = [&](int i) {
+        Blk b{};
+        if (i < P) {
+            b = {0, std::min(rb, m), pc[i], pc[i + 1] - pc[i], 0, R + i};
+        } else {
+            const int r = 1 + (i - P) / S, c = (i - P) % S;
+            b.r0 = std::min(r * rb, m);
+            b.mr = std::min(rb, m - b.r0);
+            b.c0 = std::min(c * cb, n);
+            b.nc = std::min(cb, n - b.c0);
+            b.a_ev = r;  // queued after every B piece
+            b.b_ev = -1;
+        }
+        return b;
+    };
+    for (int i = 0; i < nblk; ++i) {
+        const Blk bk = block_at(i);
+        if (!bk.mr || !bk.nc) continue;
+        uint8_t* dcb = dc + (bk.r0 * n + bk.c0) * ob;
+        uint8_t* hcb = hc + (bk.r0 * C.rs + bk.c0) * ob;
+        if (reads_c) {
+            cudaMemcpy2DAsync(dcb, n * ob, hcb, C.rs * ob, bk.nc * ob, bk.mr,
+                              cudaMemcpyHostToDevice, in);
+            cudaEventRecord(ev(R + P + 2 * i), in);
+            cudaStreamWaitEvent(cs, ev(R + P + 2 * i), 0);
+        }
+        cudaStreamWaitEvent(cs, ev(bk.a_ev), 0);
+        if (bk.b_ev >= 0) cudaStreamWaitEvent(cs, ev(bk.b_ev), 0);
+        uor_b200_route sub{};
+        st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da + bk.r0 * k), (ptrdiff_t)k, 1,
+                         reinterpret_cast<const int8_t*>(db + bk.c0), (ptrdiff_t)n, 1, dcb,
+                         (ptrdiff_t)n, 1, bk.mr, k, bk.nc, epi, &sub);
+        if (st) return drain(st);
+        if (route && i == 0) *route = sub;
+        cudaEventRecord(ev(R + P + 2 * i + 1), cs);
+        if (pinned_out) {
+            cudaStreamWaitEvent(out, ev(R + P + 2 * i + 1), 0);
+            cudaMemcpy2DAsync(hcb, C.rs * ob, dcb, n * ob, bk.nc * ob, bk.mr,
+                              cudaMemcpyDeviceToHost, out);
         }
     }
     // Into pageable memory a copy-out returns only when it is done: queue those after
     // every block, so that they do not hold back the launches behind them.
-    for (int r = 0; r < R && !pinned_out; ++r) {
-        for (int c = 0; c < S; ++c) {
-            const size_t r0 = r * rb, c0 = c * cb;
-            if (r0 >= m || c0 >= n) continue;
-            const size_t mr = std::min(rb, m - r0), nc = std::min(cb, n - c0);
-            const int blk = r * S + c;
-            cudaStreamWaitEvent(out, ev(R + S + 2 * blk + 1), 0);
-            cudaMemcpy2DAsync(hc + (r0 * C.rs + c0) * ob, C.rs * ob, dc + (r0 * n + c0) * ob,
-                              n * ob, nc * ob, mr, cudaMemcpyDeviceToHost, out);
-        }
+    for (int i = 0; i < nblk && !pinned_out; ++i) {
+        const Blk bk = block_at(i);
+        if (!bk.mr || !bk.nc) continue;
+        cudaStreamWaitEvent(out, ev(R + P + 2 * i + 1), 0);
+        cudaMemcpy2DAsync(hc + (bk.r0 * C.rs + bk.c0) * ob, C.rs * ob, dc + (bk.r0 * n + bk.c0) * ob,
+                          n * ob, bk.nc * ob, bk.mr, cudaMemcpyDeviceToHost, out);
     }
     if (cudaGetLastError() != cudaSuccess) return drain(UOR_B200_DEVICE_ERROR);
     if (cudaStreamSynchronize(out) != cudaSuccess) return drain(UOR_B200_DEVICE_ERROR);

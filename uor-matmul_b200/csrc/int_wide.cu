@@ -49,10 +49,23 @@ __device__ __forceinline__ uint32_t pack_byte(const uint64_t (&v)[4], int s) {
 
 // A (m x k, EB-byte elements, strided view) -> As[EB][mp][kp], byte s of each element;
 // four consecutive reduction positions per thread, one 4-byte store per slice.
+//
+// With `cplx` the operand is Complex<T> (repr(C) {re, im}, alphabet.rs:656-663), its
+// strides count complex elements, and the sliced matrix is its real image: A's row i
+// is (re, im, re, im, ...) over 2k reduction positions, and B's 2k x 2n image holds
+// the 2 x 2 block [[w.re, w.im], [-w.im, w.re]] for each element w, so that one real
+// product gives (re, im) of every output cell in adjacent columns -- the mac
+// re += a.re w.re + a.im (-w.im), im += a.re w.im + a.im w.re (alphabet.rs:712-717).
+// -w.im is negated modulo 2^(8 EB), the reference's release-build negation (-MIN = MIN).
+__device__ __forceinline__ int64_t cplx_a_index(int i, int q, int64_t rsa, int64_t csa, bool cplx) {
+    return cplx ? 2 * (static_cast<int64_t>(i) * rsa + static_cast<int64_t>(q >> 1) * csa) + (q & 1)
+                : static_cast<int64_t>(i) * rsa + static_cast<int64_t>(q) * csa;
+}
+
 template <int EB>
 __global__ void slice_a_kernel(uint8_t* __restrict__ as, int mp, int kp,
                                const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
-                               bool aligned, int m, int k) {
+                               bool aligned, int m, int k, bool cplx) {
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
@@ -64,8 +77,7 @@ __global__ void slice_a_kernel(uint8_t* __restrict__ as, int mp, int kp,
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const int p = p0 + c;
-            v[c] = (i < m && p < k) ? load_elem<EB>(a, static_cast<int64_t>(i) * rsa +
-                                                           static_cast<int64_t>(p) * csa, aligned)
+            v[c] = (i < m && p < k) ? load_elem<EB>(a, cplx_a_index(i, p, rsa, csa, cplx), aligned)
                                     : 0;
         }
         uint8_t* dst = as + static_cast<int64_t>(i) * kp + p0;
@@ -79,7 +91,8 @@ __global__ void slice_a_kernel(uint8_t* __restrict__ as, int mp, int kp,
 template <int EB>
 __global__ void slice_b_kernel(uint8_t* __restrict__ bs, int np, int kp,
                                const uint8_t* __restrict__ b, int64_t rsb, int64_t csb,
-                               bool aligned, int k, int n) {
+                               bool aligned, int k, int n, bool cplx) {
+    constexpr uint64_t mask = EB == 8 ? ~0ull : (1ull << (8 * EB)) - 1;
     __shared__ uint64_t tile[32][129];
     const int j0 = blockIdx.x * 32;
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -87,10 +100,18 @@ __global__ void slice_b_kernel(uint8_t* __restrict__ bs, int np, int kp,
     for (int p0 = blockIdx.y * 128; p0 < kp; p0 += gridDim.y * 128) {
         for (int r = ty; r < 128; r += 8) {
             const int p = p0 + r, j = j0 + tx;
-            tile[tx][r] = (p < k && j < n) ? load_elem<EB>(b, static_cast<int64_t>(p) * rsb +
-                                                                  static_cast<int64_t>(j) * csb,
-                                                           aligned)
-                                           : 0;
+            uint64_t v = 0;
+            if (p < k && j < n) {
+                if (cplx) {
+                    const int64_t e = static_cast<int64_t>(p >> 1) * rsb + static_cast<int64_t>(j >> 1) * csb;
+                    v = load_elem<EB>(b, 2 * e + ((p ^ j) & 1), aligned);
+                    if ((p & 1) && !(j & 1)) v = (0ull - v) & mask;
+                } else {
+                    v = load_elem<EB>(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb,
+                                      aligned);
+                }
+            }
+            tile[tx][r] = v;
         }
         __syncthreads();
         const int p = p0 + 4 * tx;
@@ -113,14 +134,14 @@ __global__ void slice_b_kernel(uint8_t* __restrict__ bs, int np, int kp,
 template <int EB>
 static void launch_slicing(uint8_t* as, uint8_t* bs, int mp, int np, int kp, const uint8_t* a,
                            int64_t rsa, int64_t csa, const uint8_t* b, int64_t rsb, int64_t csb,
-                           int m, int k, int n, cudaStream_t s) {
+                           int m, int k, int n, bool cplx, cudaStream_t s) {
     const int64_t quads = static_cast<int64_t>(mp) * (kp / 4);
     const int grid = static_cast<int>(quads / 256 + 1 < 148 * 16 ? quads / 256 + 1 : 148 * 16);
     slice_a_kernel<EB><<<grid, 256, 0, s>>>(as, mp, kp, a, rsa, csa,
-                                            reinterpret_cast<uintptr_t>(a) % EB == 0, m, k);
+                                            reinterpret_cast<uintptr_t>(a) % EB == 0, m, k, cplx);
     const int gy = (kp + 127) / 128 < 65535 ? (kp + 127) / 128 : 65535;
     slice_b_kernel<EB><<<dim3(np / 32, gy), dim3(32, 8), 0, s>>>(
-        bs, np, kp, b, rsb, csb, reinterpret_cast<uintptr_t>(b) % EB == 0, k, n);
+        bs, np, kp, b, rsb, csb, reinterpret_cast<uintptr_t>(b) % EB == 0, k, n, cplx);
 }
 
 // ------------------------------------------------------------ exact recombination
@@ -195,6 +216,7 @@ __device__ __forceinline__ i128 l3_encode(L3 x, int bits, int mode) {
 struct WideEpi {
     LinearEpi lin;
     int limbs3;  // 1: i64 elements (Limbs<3> accumulator); 0: i16/i32 (i128 accumulator)
+    int cplx;    // 1: C is Complex<O>; real column j is part j & 1 of complex column j >> 1
 };
 
 // Group g is the diagonal d = g, weighted 2^(8 g). The partials of a cell are summed
@@ -236,7 +258,10 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
             }
         }
         const size_t i = idx / n, j = idx - (idx / n) * n;
-        const int64_t off = static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j) * csc;
+        const int64_t off =
+            e.cplx ? 2 * (static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j >> 1) * csc) +
+                         static_cast<int64_t>(j & 1)
+                   : static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j) * csc;
         const LinearEpi& L = e.lin;
         i128 outv;
         if (e.limbs3) {
@@ -262,10 +287,21 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
 
 static inline size_t rup(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+static void launch_wide_reduce(const int32_t* part, int chunks, int groups, size_t m, size_t n,
+                               void* c, ptrdiff_t rsc, ptrdiff_t csc, const WideEpi& we,
+                               cudaStream_t s) {
+    const size_t total = m * n;
+    const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+    if (groups <= 8)
+        wide_reduce_kernel<8><<<rgrid, 256, 0, s>>>(part, chunks, groups, m, n, c, rsc, csc, we);
+    else
+        wide_reduce_kernel<16><<<rgrid, 256, 0, s>>>(part, chunks, groups, m, n, c, rsc, csc, we);
+}
+
 int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
                   const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc,
                   ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
-                  uor_b200_route* route) {
+                  uor_b200_route* route, bool cplx) {
     cudaStream_t s = ctx->stream;
     if (route) {
         *route = uor_b200_route{};
@@ -274,11 +310,19 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
         route->tile_k = KS_BK;
     }
     if (m == 0 || n == 0) return UOR_B200_OK;
+    // A complex product is the real product of the operands' real images (2k x 2n B).
+    if (cplx) {
+        k *= 2;
+        n *= 2;
+    }
     if (m > (size_t)INT_MAX / 4 || n > (size_t)INT_MAX / 4 || k > (size_t)INT_MAX / 4)
         return UOR_B200_UNSUPPORTED;
+    const WideEpi we{epi, eb == 8 ? 1 : 0, cplx ? 1 : 0};
     if (k == 0) {
+        // A zero accumulator through the same epilogue, in the element's own accumulator.
         if (route) route->kernel = UOR_B200_KERNEL_EPILOGUE_ONLY;
-        return cuda_status(epilogue_only(c, rsc, csc, m, n, epi, s));
+        launch_wide_reduce(nullptr, 0, 0, m, n, c, rsc, csc, we, s);
+        return cuda_status(cudaGetLastError());
     }
     const int L = eb;
     // Slice pairs grouped by diagonal; under Wrapping into <= 64-bit outputs the
@@ -334,11 +378,11 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
     p.partial = part;
 
     if (eb == 2)
-        launch_slicing<2>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
+        launch_slicing<2>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, s);
     else if (eb == 4)
-        launch_slicing<4>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
+        launch_slicing<4>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, s);
     else
-        launch_slicing<8>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, s);
+        launch_slicing<8>(as, bs, p.mp, p.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, s);
     if (route) route->kernel = UOR_B200_KERNEL_LIMB_TCGEN05;
     if (route) route->k_chunks = (uint32_t)p.num_chunks;
     if (route) route->pairs = (uint32_t)npairs;
@@ -346,13 +390,7 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
         UOR_B200_OK)
         return st;
     if (route) route->tile_m = (uint32_t)(p.m > 128 ? 256 : KS_BM);
-    WideEpi we{epi, eb == 8 ? 1 : 0};
-    const size_t total = m * n;
-    const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-    if (ngroups <= 8)
-        wide_reduce_kernel<8><<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, m, n, c, rsc, csc, we);
-    else
-        wide_reduce_kernel<16><<<rgrid, 256, 0, s>>>(part, p.num_chunks, ngroups, m, n, c, rsc, csc, we);
+    launch_wide_reduce(part, p.num_chunks, ngroups, m, n, c, rsc, csc, we, s);
     return cuda_status(cudaGetLastError());
 }
 

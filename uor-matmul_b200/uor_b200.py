@@ -121,6 +121,7 @@ def lib():
             "uor_b200_tabulated_gemm": ([I, VP, P, Z, Z, Z, U32, P, Z, VP, L64, L64, CP], I),
             "uor_b200_codec_gemm": ([I, VP, ctypes.POINTER(Codec), P, Z, Z, Z, U32, VP, L64, L64,
                                      CP], I),
+            "uor_b200_gemm_complex": ([I, I, VP, VP, VP, L64, L64, CP], I),
             "uor_b200_gemm_partial_limbs": ([I, VP, VP, P, Z, CP], I),
             "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
             "uor_b200_status_string": ([I], ctypes.c_char_p),
@@ -240,6 +241,29 @@ def gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=No
     call = make_call(encode, dev, ctx, route, asynchronous)
     _check(lib().uor_b200_gemm(elem, out, ctypes.byref(A), ctypes.byref(B), ctypes.byref(C),
                                alpha, beta, ctypes.byref(call)), "gemm")
+
+
+def complex_view(buf, rows, cols, rs=None, cs=1):
+    """A MatView of Complex<T> over a flat buffer of interleaved (re, im) parts; the
+    length and strides count complex elements."""
+    ptr, n, _ = _buffer(buf)
+    return View(ptr, n // 2, rows, cols, cols if rs is None else rs, cs)
+
+
+def gemm_complex(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None,
+                 route=None, asynchronous=False):
+    """driver::gemm over Complex<elem> (alphabet.rs:656-776) into Complex<out>.
+
+    elem in {I32, I64} and out in {I8 .. I128} name the part types; a, b, c are flat
+    buffers of interleaved parts and av/bv/cv are (rows, cols, rs, cs) in complex
+    elements. Each part is encoded on its own (EncodeFrom<ComplexAcc>); alpha and beta
+    scale each part as Linear scales a scalar accumulator."""
+    dev = _on_device(a, b, c)
+    A, B, C = complex_view(a, *av), complex_view(b, *bv), complex_view(c, *cv)
+    call = make_call(encode, dev, ctx, route, asynchronous)
+    _check(lib().uor_b200_gemm_complex(elem, out, ctypes.byref(A), ctypes.byref(B),
+                                       ctypes.byref(C), alpha, beta, ctypes.byref(call)),
+           "gemm_complex")
 
 
 def slice_gemm_ex(elem, out, m, k, n, alpha, a, lda, b, ldb, beta, c, ldc, encode=NEAREST,
