@@ -314,6 +314,13 @@ int uor_b200_codec_gemm(uor_b200_dtype out, const uor_b200_view *a, const uor_b2
                         uint32_t orientation, const uor_b200_view_mut *c, int64_t alpha,
                         int64_t beta, const uor_b200_call *call);
 
+/* e8_table (crates/uor-matmul-codec/src/e8.rs:295-307): the E8 lattice codebook, 256
+ * codewords of 8 i8 (2048 bytes, row per code, code 0 the origin) for TIER_BOOK with
+ * block 8 -- e8_codec (u16 codes) or e8_codec_u8 (u8 codes). `bound` is the alphabet's
+ * magnitude bound (0: Full<i8>); a bound below 32 admits no table: UNSUPPORTED, the
+ * reference's None. DOES_NOT_FIT when len < 2048. Host only; no device work. */
+int uor_b200_e8_table(uint32_t bound, int8_t *out, size_t len);
+
 /* ------------------------------------------------- split-K across devices */
 
 /* The exact partial sum of one device's share of a split reduction, for an exchange

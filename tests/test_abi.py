@@ -109,3 +109,33 @@ def test_alias_and_placement_agree_with_the_reference_rules(seed):
             assert st == U.OK
         else:
             assert st in (U.OK, U.DEVICE_ERROR), (m, n, rsc, csc, st)
+
+
+def test_e8_table_is_the_reference_codebook():
+    """uor_b200_e8_table derives the E8 codebook (e8.rs) on the host; its bytes match
+    the digest of the reference's literal table, and it has the lattice property
+    e8_is_the_lattice_it_claims checks (e8.rs:335-365)."""
+    import hashlib
+    import json
+    rec = json.load(open(os.path.join(ROOT, "tests", "golden", "e8_digest.json")))
+    t = U.e8_table()
+    assert t.shape == (256, 8)
+    assert hashlib.sha256(t.tobytes()).hexdigest() == rec["sha256"]
+    assert not t[0].any()
+    for w in t[1:].astype(int):
+        all32 = all(v % 32 == 0 for v in w)
+        all16 = all(v % 32 == 16 for v in w)
+        assert all32 or all16
+        if all32:
+            assert (w // 32).sum() % 2 == 0
+    assert len({bytes(r) for r in t.view(np.uint8)}) == 256
+
+
+def test_e8_table_bound_and_length():
+    """a_bound_too_narrow_has_no_table (e8.rs:369-374): Bnd<8> has no table."""
+    assert U.e8_table(128).tobytes() == U.e8_table().tobytes()
+    assert U.e8_table(32).tobytes() == U.e8_table().tobytes()
+    with pytest.raises(U.UorError):
+        U.e8_table(8)
+    short = np.zeros(2047, np.int8)
+    assert U.lib().uor_b200_e8_table(0, short.ctypes.data, short.size) == U.DOES_NOT_FIT

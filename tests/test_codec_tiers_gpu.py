@@ -69,6 +69,23 @@ def test_book(orientation):
               seed=N)
 
 
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("cb", [1, 2])
+def test_e8_codebook(orientation, cb):
+    """e8_codec_u8 (u8 codes) and e8_codec (u16 codes, taken modulo 256 rows) over the
+    library's own E8 table (e8.rs); a zeroed code stream decodes to zero."""
+    m, k, n = 96, 512, 256
+    table = U.e8_table()
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    codes = codes_for(rows, cols, 8, cb, 21 + cb)
+    check(m, k, n, U.TIER_BOOK, codes, orientation, table=table, block=8, code_bytes=cb,
+          seed=30 + cb)
+    zeros = np.zeros_like(codes)
+    got, _ = check(m, k, n, U.TIER_BOOK, zeros, orientation, table=table, block=8,
+                   code_bytes=cb, seed=40)
+    assert not got.any()
+
+
 @pytest.mark.parametrize("P", [2, 4])
 def test_grid_with_offset(P):
     m, k, n = 260, 128, 96

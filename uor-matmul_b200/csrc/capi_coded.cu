@@ -1,5 +1,6 @@
 // capi_coded.cu -- the codec tier's C ABI: coded_gemm (codes k x n) and the product
 // of gemm_tabulated (codes n x k), over Packed<Grid<N>, P> codes.
+#include <algorithm>
 #include <climits>
 #include <cstring>
 #include <vector>
@@ -416,6 +417,49 @@ int uor_b200_codec_gemm(uor_b200_dtype out, const uor_b200_view* a, const uor_b2
                         uint32_t orientation, const uor_b200_view_mut* c, int64_t alpha,
                         int64_t beta, const uor_b200_call* call) {
     return codec_common(out, a, codec, codes, codes_len, k, n, orientation, c, alpha, beta, call);
+}
+
+// The E8 lattice codebook (crates/uor-matmul-codec/src/e8.rs): the lattice points
+// whose coordinates lie in {0, +-1/2, +-1} -- the integer vectors of D8 (even coordinate
+// sum) and the half-integer coset with an even count of negative coordinates -- scaled
+// by 32 into i8, ordered by norm and then lexicographically on the scaled coordinates,
+// first 256. Code 0 is the origin; codes 1..240 are the 240 minimal vectors.
+int uor_b200_e8_table(uint32_t bound, int8_t* out, size_t len) {
+    constexpr int kEntries = 256, kBlock = 8;
+    if (bound != 0 && bound < 32) return UOR_B200_UNSUPPORTED;  // e8_table's None
+    if (!out) return UOR_B200_INVALID_ARGUMENT;
+    if (len < (size_t)kEntries * kBlock) return UOR_B200_DOES_NOT_FIT;
+    struct Point {
+        int8_t v[kBlock];
+        int norm;
+    };
+    std::vector<Point> pts;
+    pts.reserve(6561 + 256);
+    for (int code = 0; code < 6561; ++code) {  // {-32, 0, 32}^8
+        Point p{};
+        int sum = 0, c = code;
+        for (int t = kBlock - 1; t >= 0; --t, c /= 3) {
+            p.v[t] = static_cast<int8_t>((c % 3 - 1) * 32);
+            sum += c % 3 - 1;
+            p.norm += p.v[t] * p.v[t];
+        }
+        if ((sum & 1) == 0) pts.push_back(p);
+    }
+    for (int bits = 0; bits < 256; ++bits) {  // {-16, 16}^8, an even count of -16
+        if (__builtin_popcount(bits) & 1) continue;
+        Point p{};
+        for (int t = 0; t < kBlock; ++t) {
+            p.v[t] = (bits >> (kBlock - 1 - t) & 1) ? -16 : 16;
+            p.norm += 256;
+        }
+        pts.push_back(p);
+    }
+    std::stable_sort(pts.begin(), pts.end(), [](const Point& x, const Point& y) {
+        if (x.norm != y.norm) return x.norm < y.norm;
+        return std::lexicographical_compare(x.v, x.v + kBlock, y.v, y.v + kBlock);
+    });
+    for (int e = 0; e < kEntries; ++e) std::memcpy(out + e * kBlock, pts[e].v, kBlock);
+    return UOR_B200_OK;
 }
 
 }  // extern "C"

@@ -122,6 +122,7 @@ def lib():
             "uor_b200_codec_gemm": ([I, VP, ctypes.POINTER(Codec), P, Z, Z, Z, U32, VP, L64, L64,
                                      CP], I),
             "uor_b200_gemm_complex": ([I, I, VP, VP, VP, L64, L64, CP], I),
+            "uor_b200_e8_table": ([U32, P, Z], I),
             "uor_b200_gemm_partial_limbs": ([I, VP, VP, P, Z, CP], I),
             "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
             "uor_b200_status_string": ([I], ctypes.c_char_p),
@@ -405,6 +406,18 @@ def codec_gemm(out, a, av, tier, codes, k, n, c, cv, table=None, per_byte=0, blo
     _check(lib().uor_b200_codec_gemm(out, ctypes.byref(A), ctypes.byref(cod), pc, lc, k, n,
                                      orientation, ctypes.byref(C), alpha, beta,
                                      ctypes.byref(call)), "codec_gemm")
+
+
+E8_ENTRIES, E8_BLOCK = 256, 8
+
+
+def e8_table(bound=0):
+    """e8_table (e8.rs:295-307): the E8 codebook as a (256, 8) int8 array, for
+    codec_gemm(tier=TIER_BOOK, block=8). bound = 0 is Full<i8>; a bound below 32
+    has no table (UorError UNSUPPORTED, the reference's None)."""
+    out = np.zeros((E8_ENTRIES, E8_BLOCK), np.int8)
+    _check(lib().uor_b200_e8_table(bound, out.ctypes.data, out.size), "e8_table")
+    return out
 
 
 # ------------------------------------------------------------------ split-K exchange
