@@ -321,6 +321,25 @@ int uor_b200_codec_gemm(uor_b200_dtype out, const uor_b200_view *a, const uor_b2
  * reference's None. DOES_NOT_FIT when len < 2048. Host only; no device work. */
 int uor_b200_e8_table(uint32_t bound, int8_t *out, size_t len);
 
+/* coded_gemm / gemm_tabulated over Arena<E, N, K> (crates/uor-matmul-codec/src/
+ * codecs.rs:894-985): each code (u8, code_bytes 1, or u16 little-endian, 2) indexes a
+ * table of N float symbols of elem's type modulo N, one element per code; the product
+ * with a float A is gemm_float's (exact accumulation, one rounding). elem in {F32, F64}
+ * names A's and the table's type, out in {F32, F64}. codes_len is in bytes and must be
+ * exactly k * n * code_bytes (CodedMatrix::new), else DOES_NOT_FIT; orientation 0: codes
+ * k x n, 1: codes n x k. */
+int uor_b200_arena_gemm(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view *a,
+                        const void *table, size_t table_len, const uint8_t *codes,
+                        size_t codes_len, uint32_t code_bytes, size_t k, size_t n,
+                        uint32_t orientation, const uor_b200_view_mut *c, int64_t alpha,
+                        int64_t beta, const uor_b200_call *call);
+
+/* canonicalize (codecs.rs:990-1003): sort `len` float symbols of elem's type in place by
+ * their bit patterns as unsigned integers and move the distinct patterns to the front;
+ * *distinct receives their count, values[0 .. *distinct) is the Arena table. -0.0 and
+ * +0.0, and NaNs with different payloads, are distinct symbols. Host only. */
+int uor_b200_arena_canonicalize(uor_b200_dtype elem, void *values, size_t len, size_t *distinct);
+
 /* ------------------------------------------------- split-K across devices */
 
 /* The exact partial sum of one device's share of a split reduction, for an exchange

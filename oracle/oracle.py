@@ -194,6 +194,18 @@ def decode_codec(tier, codes, rows, cols, table=None, per_byte=0, block=1, code_
     return (out - zero).astype(np.int8)
 
 
+def decode_arena(table, codes, rows, cols, code_bytes=1):
+    """Arena::decode_element (codecs.rs:961-965) over a CodedMatrix of one-element blocks:
+    element (r, c) is table[code % N] with code the (r * cols + c)-th u8 or little-endian
+    u16 code; the symbols are copied as bit patterns."""
+    codes = np.asarray(codes, np.uint8)
+    if code_bytes == 2:
+        idx = codes[0::2].astype(np.int64) | (codes[1::2].astype(np.int64) << 8)
+    else:
+        idx = codes.astype(np.int64)
+    return np.asarray(table)[idx[: rows * cols] % len(table)].reshape(rows, cols)
+
+
 def trop_witness(av, af, bv, bf):
     """D-6's witness (crates/uor-matmul-gemm/src/selection.rs; the differential reference of
     validate/tests/selection.rs): per cell the least index attaining the maximum of the

@@ -253,7 +253,7 @@ void uor_b200_ctx_destroy(uor_b200_ctx* ctx) {
     cudaGetDevice(&prev);
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-    for (int i = 0; i < 5; ++i)
+    for (int i = 0; i < uor_b200_ctx::kSlots; ++i)
         if (ctx->buf[i]) cudaFree(ctx->buf[i]);
     if (ctx->d_status) cudaFree(ctx->d_status);
     for (int i = 0; i < ctx->nevents; ++i) cudaEventDestroy(ctx->events[i]);

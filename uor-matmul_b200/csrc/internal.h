@@ -16,10 +16,12 @@ struct uor_b200_ctx {
     int sm_count = 148;
     std::mutex mu;
     // Growable device buffers: workspace (gathers, chunk partials), the three
-    // staging slots host-pointer calls copy operands through, and an auxiliary
-    // buffer for operands a path rebuilds (decoded codes).
-    void* buf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
-    size_t cap[5] = {0, 0, 0, 0, 0};
+    // staging slots host-pointer calls copy operands through, an auxiliary buffer
+    // for operands a path rebuilds (decoded codes), and a dense decoded operand
+    // handed to a driver that uses the auxiliary buffer itself.
+    static constexpr int kSlots = 6;
+    void* buf[kSlots] = {};
+    size_t cap[kSlots] = {};
     // Host-pointer pipelining: copy-in and copy-out streams and a pool of events,
     // created on first use.
     cudaStream_t copy_in = nullptr, copy_out = nullptr;
@@ -29,7 +31,7 @@ struct uor_b200_ctx {
 
 namespace uor {
 
-enum Slot { SLOT_WS = 0, SLOT_A = 1, SLOT_B = 2, SLOT_C = 3, SLOT_AUX = 4 };
+enum Slot { SLOT_WS = 0, SLOT_A = 1, SLOT_B = 2, SLOT_C = 3, SLOT_AUX = 4, SLOT_DECODED = 5 };
 
 // A device buffer of at least `bytes` in the given slot (grown with cudaMalloc;
 // the previous contents are not kept).

@@ -123,6 +123,8 @@ def lib():
                                      CP], I),
             "uor_b200_gemm_complex": ([I, I, VP, VP, VP, L64, L64, CP], I),
             "uor_b200_e8_table": ([U32, P, Z], I),
+            "uor_b200_arena_gemm": ([I, I, VP, P, Z, P, Z, U32, Z, Z, U32, VP, L64, L64, CP], I),
+            "uor_b200_arena_canonicalize": ([I, P, Z, ctypes.POINTER(Z)], I),
             "uor_b200_gemm_partial_limbs": ([I, VP, VP, P, Z, CP], I),
             "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
             "uor_b200_status_string": ([I], ctypes.c_char_p),
@@ -418,6 +420,32 @@ def e8_table(bound=0):
     out = np.zeros((E8_ENTRIES, E8_BLOCK), np.int8)
     _check(lib().uor_b200_e8_table(bound, out.ctypes.data, out.size), "e8_table")
     return out
+
+
+def arena_gemm(elem, out, a, av, table, codes, k, n, c, cv, code_bytes=1, orientation=0,
+               alpha=1, beta=0, encode=NEAREST, ctx=None, route=None, asynchronous=False):
+    """coded_gemm / gemm_tabulated over Arena<E, N, K> (codecs.rs:894-985): codes (u8 or
+    u16) index `table`, N float symbols of elem's type (F32 / F64), modulo N; the product
+    with the float A is gemm_float's. orientation 0: codes k x n, 1: n x k."""
+    dev = _on_device(a, table, codes, c)
+    A, C = view(a, *av), view(c, *cv)
+    pt, lt, _ = _buffer(table)
+    pc, _, _ = _buffer(codes)
+    nbytes = codes.numel() * codes.element_size() if _is_torch(codes) else np.asarray(codes).nbytes
+    call = make_call(encode, dev, ctx, route, asynchronous)
+    _check(lib().uor_b200_arena_gemm(elem, out, ctypes.byref(A), pt, lt, pc, nbytes, code_bytes,
+                                     k, n, orientation, ctypes.byref(C), alpha, beta,
+                                     ctypes.byref(call)), "arena_gemm")
+
+
+def arena_canonicalize(values):
+    """canonicalize (codecs.rs:990-1003) in place on a float32 / float64 NumPy array;
+    returns the count of distinct bit patterns now at the front."""
+    elem = {np.dtype(np.float32): F32, np.dtype(np.float64): F64}[values.dtype]
+    n = ctypes.c_size_t(0)
+    _check(lib().uor_b200_arena_canonicalize(elem, values.ctypes.data, values.size,
+                                             ctypes.byref(n)), "arena_canonicalize")
+    return n.value
 
 
 # ------------------------------------------------------------------ split-K exchange
