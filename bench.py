@@ -444,7 +444,8 @@ def wl_f32(args, U, torch, rank, size, sets=2):
 
     w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
     w.metric = f"exact f32 GEMM TFLOPS at {size}^3 (bit-exact, rounded once)"
-    w.unit, w.dtype = "TFLOPS", "f32 in, exact int8 digit slices + integer register"
+    w.unit, w.dtype = "TFLOPS", ("f32 in, int8 residue GEMMs modulo coprime moduli + CRT "
+                                 "(or exact int8 digit slices), rounded once")
     w.config = {"workload": f"gemm_float f32 {m}x{k}x{n} per GPU (configs[2] distribution), "
                             "column-block sharded", "m": m, "k": k, "n_per_gpu": n}
     w.l2 = f"{sets} rotating operand sets ({sets * 8 * m * k >> 20} MiB) + {4 * m * n >> 20} MiB output"
@@ -455,12 +456,17 @@ def wl_f32(args, U, torch, rank, size, sets=2):
         peak, src = tensor_peak()
         pairs = max(1, w.route.pairs)
         ach = pairs * w.units / (avg_ms / 1e3) / 1e12
+        if w.route.moduli:
+            basis = (f"int8 GEMM ops executed ({w.route.moduli} residue GEMMs modulo coprime "
+                     "moduli <= 256 x 2mnk) over the whole call (analysis, residue slicing, "
+                     "GEMMs, CRT and encode)")
+        else:
+            basis = (f"int8 slice-pair ops executed ({pairs} of {w.route.a_layout} x "
+                     f"{w.route.b_layout} digit pairs x 2mnk; {w.route.fixups} cells "
+                     "recomputed exactly) over the whole call (analysis, slicing, GEMM, "
+                     "interval test, fixups)")
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
-                "frac": ach / peak, "peak_source": src, "traffic": None,
-                "basis": f"int8 slice-pair ops executed ({pairs} of {w.route.a_layout} x "
-                         f"{w.route.b_layout} digit pairs x 2mnk; {w.route.fixups} cells "
-                         "recomputed exactly) over the whole call (analysis, slicing, GEMM, "
-                         "interval test, fixups)",
+                "frac": ach / peak, "peak_source": src, "traffic": None, "basis": basis,
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w

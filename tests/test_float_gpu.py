@@ -17,13 +17,14 @@ UT = {U.F32: np.uint32, U.F64: np.uint64}
 
 
 def run_both(elem, out, a, b, m, k, n, alpha=1, beta=0, c0=None, mode=U.NEAREST, av=None,
-             bv=None):
+             bv=None, digits=False):
     av = av or (m, k, k, 1)
     bv = bv or (k, n, n, 1)
     c0 = np.zeros(m * n, FT[out]) if c0 is None else c0
     got, want = c0.copy(), c0.copy()
     route = U.Route()
-    U.gemm_float(elem, out, a, av, b, bv, got, (m, n, n, 1), alpha, beta, mode, route=route)
+    U.gemm_float(elem, out, a, av, b, bv, got, (m, n, n, 1), alpha, beta, mode, route=route,
+                 digits=digits)
     oa = -orc.extent(*av)[0]
     ob = -orc.extent(*bv)[0]
     orc.gemm_float(View(a, *av, oa), View(b, *bv, ob), View(want, m, n, n, 1), alpha=alpha,
@@ -90,10 +91,12 @@ def test_random_bit_patterns_and_specials(elem, out):
                 assert np.array_equal(got, want), (m, k, n, specials, alpha, beta, mode)
 
 
+@pytest.mark.parametrize("digits", [False, True])
 @pytest.mark.parametrize("elem,out", [(U.F32, U.F32), (U.F64, U.F64), (U.F32, U.F64)])
 @pytest.mark.parametrize("shape", [(3, 10, 7), (130, 96, 270), (64, 700, 40), (257, 64, 130)])
-def test_moderate_exponents_tensor_route(elem, out, shape):
-    """Exponent spans small enough for the digit route (K6 on the tensor cores)."""
+def test_moderate_exponents_tensor_route(elem, out, shape, digits):
+    """Exponent spans small enough for the tensor cores: the modular route (residues and
+    the CRT) and, forced, the digit-slice route."""
     m, k, n = shape
     rng = np.random.default_rng(m + k + n)
     a = (rng.standard_normal(m * k) * np.exp2(rng.integers(-8, 8, m * k))).astype(FT[elem])
@@ -101,14 +104,17 @@ def test_moderate_exponents_tensor_route(elem, out, shape):
     b[::5] = 0.0
     c0 = rng.standard_normal(m * n).astype(FT[out])
     for alpha, beta, mode in [(1, 0, U.NEAREST), (-3, 2, U.NEAREST), (2**40, -1, U.TOWARD_ZERO)]:
-        got, want, route = run_both(elem, out, a, b, m, k, n, alpha, beta, c0, mode)
+        got, want, route = run_both(elem, out, a, b, m, k, n, alpha, beta, c0, mode,
+                                    digits=digits)
         assert np.array_equal(got, want), (alpha, beta, mode)
+        assert (route.moduli == 0) == digits
         if elem == U.F32:
             # 256-row tiles on CTA pairs past 128 rows, 128-row tiles below
             assert route.kernel == 5 and route.tile_m == (256 if m > 128 else 128)
 
 
-def test_nonfinite_on_the_tensor_route():
+@pytest.mark.parametrize("digits", [False, True])
+def test_nonfinite_on_the_tensor_route(digits):
     m, k, n = 70, 200, 90
     rng = np.random.default_rng(7)
     a = rng.standard_normal(m * k).astype(np.float32)
@@ -118,15 +124,19 @@ def test_nonfinite_on_the_tensor_route():
     b[3 * n + 4] = 0.0
     b[100 * n + 7] = np.nan
     b[50 * n + 11] = -np.inf
-    got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, 1, 0)
-    assert np.array_equal(got, want)
-    assert route.tile_m == 128
+    for alpha, beta in ((1, 0), (-2, 3)):
+        c0 = rng.standard_normal(m * n).astype(np.float32)
+        got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, alpha, beta, c0, digits=digits)
+        assert np.array_equal(got, want), (alpha, beta)
+        assert route.tile_m == 128 and (route.moduli == 0) == digits
 
 
-def test_config3_cancellation_moderate():
+@pytest.mark.parametrize("digits", [False, True])
+def test_config3_cancellation_moderate(digits):
     m, k, n = 96, 256, 130
     a, b = config3(m, k, n)
-    got, want, route = run_both(U.F32, U.F32, a.reshape(-1), b.reshape(-1), m, k, n)
+    got, want, route = run_both(U.F32, U.F32, a.reshape(-1), b.reshape(-1), m, k, n,
+                                digits=digits)
     assert np.array_equal(got, want)
     for j in range(0, n, 10):
         assert got[(j % m) * n + j] == 0, "an exactly cancelling row encodes +0"
@@ -140,7 +150,8 @@ def test_lazy_digits_interval_test_and_exact_fixups():
     a, b = config3(m, k, n)
     a, b = a.reshape(-1), b.reshape(-1)
     for alpha, mode in [(1, U.NEAREST), (-3, U.NEAREST), (5, U.TOWARD_ZERO)]:
-        got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, alpha, 0, None, mode)
+        got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, alpha, 0, None, mode,
+                                    digits=True)
         assert np.array_equal(got, want), (alpha, mode)
         assert route.pairs < route.a_layout * route.b_layout, "the low diagonals were skipped"
         assert route.fixups >= n // 10, "every cancelling cell is recomputed exactly"
@@ -148,9 +159,10 @@ def test_lazy_digits_interval_test_and_exact_fixups():
     a2, b2 = a.copy(), b.copy()
     a2[7 * k:8 * k] = 0.0
     b2[np.arange(k) * n + 3] = 0.0
-    got, want, route = run_both(U.F32, U.F32, a2, b2, m, k, n)
-    assert np.array_equal(got, want)
-    assert (got.reshape(m, n)[7] == 0).all() and (got.reshape(m, n)[:, 3] == 0).all()
+    for digits in (True, False):
+        got, want, route = run_both(U.F32, U.F32, a2, b2, m, k, n, digits=digits)
+        assert np.array_equal(got, want)
+        assert (got.reshape(m, n)[7] == 0).all() and (got.reshape(m, n)[:, 3] == 0).all()
 
 
 def test_lazy_digits_fall_back_when_many_cells_cancel():
@@ -163,7 +175,7 @@ def test_lazy_digits_fall_back_when_many_cells_cancel():
     for j in range(n):
         b[:kk, j] = a[j % m, np.arange(kk) ^ 1] * sign[:kk] * np.float32(2.0 ** ((j % 9) - 4))
     got, want, route = run_both(U.F32, U.F32, a.reshape(-1), np.ascontiguousarray(b).reshape(-1),
-                                m, k, n)
+                                m, k, n, digits=True)
     assert np.array_equal(got, want)
     assert route.fixups > 4096
     assert route.pairs == route.a_layout * route.b_layout
@@ -208,7 +220,8 @@ def test_config3_full_size_sampled():
     tc = torch.empty(m * n, dtype=torch.float32, device="cuda")
     route = U.Route()
     U.gemm_float(U.F32, U.F32, ta, (m, k, k, 1), tb, (k, n, n, 1), tc, (m, n, n, 1), route=route)
-    assert route.kernel == 5 and route.tile_m == 256 and route.a_layout == 11
+    # 24 moduli cover 2 k 2^(84 + 84) (M = 2^184.09); 45 digit pairs would run otherwise
+    assert route.kernel == 5 and route.tile_m == 256 and route.moduli == 24
     c = tc.cpu().numpy().view(np.uint32)
     cells = [(0, 0), (0, 1), (m - 1, n - 1), (123, 4000), (3000, 30), (40, 40)]
     for (i, j) in cells:
@@ -218,3 +231,47 @@ def test_config3_full_size_sampled():
         assert c[i * n + j] == w.view(np.uint32)[0], (i, j)
     for j in range(0, n, 10):
         assert c[(j % m) * n + j] == 0
+
+
+def test_modular_route_config3_all_epilogues():
+    """configs[2]'s distribution on the modular route: 24 int8 GEMMs and the CRT give the
+    oracle's bytes, cancelling cells (+0) included, under every epilogue."""
+    m, k, n = 300, 512, 260
+    a, b = config3(m, k, n)
+    a, b = a.reshape(-1), b.reshape(-1)
+    rng = np.random.default_rng(8)
+    c0 = rng.standard_normal(m * n).astype(np.float32)
+    for alpha, beta, mode in [(1, 0, U.NEAREST), (-3, 0, U.TOWARD_ZERO), (7, -2, U.NEAREST),
+                              (2**62, 1, U.SATURATING)]:
+        got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, alpha, beta, c0, mode)
+        assert np.array_equal(got, want), (alpha, beta, mode)
+        assert route.moduli > 0 and route.fixups == 0
+
+
+def test_modular_route_spans_past_sixteen_digits():
+    """Exponents over [-50, 50]: 124-bit spans, more than 16 base-256 digits (the digit
+    route would run on CUDA cores); 35 moduli cover them on the tensor cores."""
+    m, k, n = 70, 100, 60
+    rng = np.random.default_rng(21)
+
+    def wide(count):
+        mant = rng.integers(1 << 23, 1 << 24, size=count).astype(np.float64)
+        e = rng.integers(-50, 51, size=count)
+        s = rng.choice([-1.0, 1.0], size=count)
+        return (s * np.ldexp(mant, e - 23)).astype(np.float32)
+    a, b = wide(m * k), wide(k * n)
+    for out in (U.F32, U.F64):
+        got, want, route = run_both(U.F32, out, a, b, m, k, n, 3, 0)
+        assert np.array_equal(got, want)
+        assert route.moduli >= 30 and route.tile_k == 128
+
+
+def test_modular_route_two_reduction_chunks():
+    """k past 1023 blocks of 128: the residues of two reduction chunks are summed in the CRT."""
+    m, k, n = 6, 140000, 9
+    rng = np.random.default_rng(4)
+    a = (rng.standard_normal(m * k) * np.exp2(rng.integers(-4, 4, m * k))).astype(np.float32)
+    b = (rng.standard_normal(k * n) * np.exp2(rng.integers(-4, 4, k * n))).astype(np.float32)
+    got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, 1, 0)
+    assert np.array_equal(got, want)
+    assert route.moduli > 0 and route.k_chunks == 2

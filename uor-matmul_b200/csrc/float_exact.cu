@@ -25,6 +25,7 @@
 // extension word) on CUDA cores. Exact, and slow; it exists so that no input has
 // to be refused.
 #include <climits>
+#include <vector>
 #include "aux.cuh"
 #include "float_exact.h"
 #include "gemm_slices.cuh"
@@ -314,7 +315,7 @@ __device__ __forceinline__ bool reg_any_below(const uint64_t (&m)[NW], int pos) 
 // encode_words for a magnitude held in registers with its sign: the same rounding
 // steps (acc.rs:1734-1868), the significand and round bit read as one 64-bit window.
 template <int NW>
-__device__ uint64_t encode_mag_fast(const uint64_t (&mag)[NW], bool neg, int unit_exp, bool out64,
+__device__ __forceinline__ uint64_t encode_mag_fast(const uint64_t (&mag)[NW], bool neg, int unit_exp, bool out64,
                                     int mode, int min_exp_e) {
     const int MANT = out64 ? 52 : 23, EXPO = out64 ? 11 : 8;
     const int P = MANT + 1;
@@ -974,6 +975,440 @@ __global__ void fx_fix_kernel(const uint32_t* __restrict__ list, const uint32_t*
     }
 }
 
+// ------------------------------------------------------------ modular route
+//
+// Ozaki scheme II (Ozaki, Uchino and Imamura, "Ozaki Scheme II: A GEMM-oriented emulation
+// of floating-point matrix multiplication using an integer modular technique", 2025):
+// the scaled integers of the digit route (A_ip 2^-lo_i, B_pj 2^-lo_j) are reduced modulo
+// nm pairwise coprime moduli p_g <= 256 into balanced residues, which are int8; one int8
+// GEMM per modulus on the tensor cores gives S mod p_g exactly (the s32 accumulator is
+// reduced in the slice-pair kernel's epilogue); and the Chinese remainder theorem rebuilds
+// each cell's exact integer S from its nm residues. M = prod p_g is chosen above twice the
+// bound k (2^span_A - 1)(2^span_B - 1) on |S|, so S is the representative of X = sum_g
+// y_g M / p_g (y_g = r_g (M / p_g)^-1 mod p_g) nearest to zero: S = X - t M with t the
+// integer nearest X / M = sum_g y_g / p_g. With M > 2 (1 + 2^-10) bound, X / M lies within
+// 1/2 - 2^-11 of t, and the 32-bit fixed-point sum sum_g y_g ceil(2^32 / p_g) overshoots
+// X / M 2^32 by less than 40 * 255 (2^-18.6 after scaling), so rounding it finds t. X
+// itself is summed in base-256 columns, X_b = sum_g y_g digit_b(M / p_g), four moduli per
+// dp4a. Then the epilogue and encode of the digit route.
+
+constexpr int FM_MAX = 40;    // moduli
+constexpr int FM_LIMBS = 11;  // 32-bit limbs of X < nm M (the 40 moduli's product is 291 bits)
+constexpr int FM_TABLE_MAX = 48 * 1024;  // bytes of the 2^s table in shared memory
+// 2^8, 3 5 17, 11 23, 13 19 and primes: pairwise coprime, largest first.
+static const uint16_t kFmModuli[FM_MAX] = {256, 255, 253, 251, 247, 241, 239, 233, 229, 227,
+                                           223, 211, 199, 197, 193, 191, 181, 179, 173, 167,
+                                           163, 157, 151, 149, 139, 137, 131, 127, 113, 109,
+                                           107, 103, 101, 97,  89,  83,  79,  73,  71,  67};
+
+struct FmParams {
+    int nm;                              // moduli (even)
+    uint16_t p[FM_MAX];
+    uint16_t inv[FM_MAX];                // (M / p_g)^-1 mod p_g
+    uint32_t magic32[FM_MAX];            // ceil(2^32 / p_g)
+    uint32_t md[FM_MAX / 4][FM_MAX];     // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
+    uint8_t mmd[FM_MAX];                 // byte b of M (M < 2^(8 nm))
+};
+
+// x mod p for x < 2^24: floor(x ceil(2^32 / p) / 2^32) is exact there (the error term
+// x (ceil(2^32/p) - 2^32/p) / 2^32 < 2^-8 never reaches the next multiple).
+__device__ __forceinline__ uint32_t fm_mod24(uint32_t x, uint32_t p, uint32_t magic32) {
+    return x - __umulhi(x, magic32) * p;
+}
+
+// Balanced residue byte of +-mant 2^sh modulo p from u = sum_i byte_i(mant) (2^(sh + 8i)
+// mod p) (< 2^19): in [-(p-1)/2, (p-1)/2] for odd p, [-128, 127] for 256 (where -(-128)
+// is the same byte 128 modulo 256).
+__device__ __forceinline__ uint32_t fm_balanced(uint32_t u, uint32_t nmask, uint32_t p,
+                                                uint32_t magic32) {
+    const uint32_t r = fm_mod24(u, p, magic32);
+    const uint32_t b = r >= (p + 1) / 2 ? r - p : r;
+    return ((b ^ nmask) - nmask) & 255u;
+}
+
+// The table of words [2^sh, 2^(sh+8), 2^(sh+16), 0] mod p_g (f32 significands, W = 1), or
+// two words covering 2^(sh + 8i) for i < 8 (f64, W = 2), row sh holding W x NMP words.
+__device__ __forceinline__ void fm_fill_pow2(uint32_t* pw, const uint32_t* __restrict__ table,
+                                             int words) {
+    for (int idx = threadIdx.y * blockDim.x + threadIdx.x; idx < words;
+         idx += blockDim.x * blockDim.y)
+        pw[idx] = table[idx];
+}
+
+// One element's scaled integer as (odd-part mantissa, shift, sign); zero for a zero or
+// non-finite element (non-finite terms are resolved by the flags pass).
+__device__ __forceinline__ void fm_parts(const FDec& d, int lo, uint64_t& mant, int& sh, bool& neg) {
+    if (d.kind != 0 || d.mant == 0) {
+        mant = 0, sh = 0, neg = false;
+        return;
+    }
+    const int tz = __ffsll(static_cast<long long>(d.mant)) - 1;
+    mant = d.mant >> tz;
+    sh = d.exp + tz - lo;
+    neg = d.sign != 0;
+}
+
+// The residues of four elements for all NM moduli, packed four per 32-bit word and stored
+// to dst + g * plane (one word per modulus). W: table words per (shift, modulus).
+template <int NM>
+__device__ __forceinline__ void fm_store_residues(int8_t* dst, int64_t plane, const uint64_t (&mant)[4],
+                                                  const int (&sh)[4], const bool (&neg)[4],
+                                                  const uint32_t* pw, int W, const FmParams& f) {
+    constexpr int NMP = (NM + 3) / 4 * 4;
+    uint32_t out[NM];
+#pragma unroll
+    for (int g = 0; g < NM; ++g) out[g] = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        if (!mant[c]) continue;
+        const uint32_t nmask = neg[c] ? ~0u : 0u;
+        const uint32_t lo32 = static_cast<uint32_t>(mant[c]);
+        const uint32_t hi32 = static_cast<uint32_t>(mant[c] >> 32);
+        const uint4* row = reinterpret_cast<const uint4*>(pw + sh[c] * W * NMP);
+#pragma unroll
+        for (int g4 = 0; g4 < NMP / 4; ++g4) {
+            const uint4 cw = row[g4];
+            uint32_t u[4] = {__dp4a(lo32, cw.x, 0u), __dp4a(lo32, cw.y, 0u), __dp4a(lo32, cw.z, 0u),
+                             __dp4a(lo32, cw.w, 0u)};
+            if (W == 2) {
+                const uint4 ch = row[NMP / 4 + g4];
+                u[0] = __dp4a(hi32, ch.x, u[0]);
+                u[1] = __dp4a(hi32, ch.y, u[1]);
+                u[2] = __dp4a(hi32, ch.z, u[2]);
+                u[3] = __dp4a(hi32, ch.w, u[3]);
+            }
+#pragma unroll
+            for (int gi = 0; gi < 4; ++gi) {
+                const int g = 4 * g4 + gi;
+                if (g < NM) out[g] |= fm_balanced(u[gi], nmask, f.p[g], f.magic32[g]) << (8 * c);
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < NM; ++g) *reinterpret_cast<uint32_t*>(dst + g * plane) = out[g];
+}
+
+// A (m x k) -> residue planes As[NM][mp][kp]: four consecutive reduction positions per
+// thread, one 4-byte store per modulus.
+template <int NM>
+__global__ void fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const uint8_t* __restrict__ a,
+                                  int64_t rsa, int64_t csa, bool f64, int m, int k,
+                                  const int* __restrict__ lo, const uint32_t* __restrict__ pow2,
+                                  int shmax, FmParams f) {
+    constexpr int NMP = (NM + 3) / 4 * 4;
+    extern __shared__ __align__(16) uint32_t pw[];
+    const int W = f64 ? 2 : 1;
+    fm_fill_pow2(pw, pow2, shmax * W * NMP);
+    __syncthreads();
+    const int qpr = kp >> 2;
+    const int64_t total = static_cast<int64_t>(mp) * qpr;
+    const int64_t plane = static_cast<int64_t>(mp) * kp;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(t / qpr);
+        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+        uint64_t mant[4];
+        int sh[4];
+        bool neg[4];
+        const int li = i < m ? lo[i] : 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int p = p0 + c;
+            FDec d{};
+            if (i < m && p < k)
+                d = fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, f64);
+            fm_parts(d, li, mant[c], sh[c], neg[c]);
+        }
+        fm_store_residues<NM>(as + static_cast<int64_t>(i) * kp + p0, plane, mant, sh, neg, pw, W, f);
+    }
+}
+
+// B (k x n) -> residue planes Bs[NM][np][kp] (transposed) through a shared tile of 64
+// reduction positions x 32 columns of decoded elements.
+template <int NM>
+__global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const uint8_t* __restrict__ b,
+                                  int64_t rsb, int64_t csb, bool f64, int k, int n,
+                                  const int* __restrict__ lo, const uint32_t* __restrict__ pow2,
+                                  int shmax, FmParams f) {
+    constexpr int NMP = (NM + 3) / 4 * 4;
+    extern __shared__ __align__(16) uint32_t pw[];
+    __shared__ uint64_t tm[32][65];
+    __shared__ int ts[32][65];
+    const int W = f64 ? 2 : 1;
+    fm_fill_pow2(pw, pow2, shmax * W * NMP);
+    const int j0 = blockIdx.x * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    const int64_t plane = static_cast<int64_t>(np) * kp;
+    const int lj = j0 + tx < n ? lo[j0 + tx] : 0;
+    __syncthreads();
+    for (int p0 = blockIdx.y * 64; p0 < kp; p0 += gridDim.y * 64) {
+        for (int r = ty; r < 64; r += 8) {
+            const int p = p0 + r, j = j0 + tx;
+            FDec d{};
+            if (p < k && j < n)
+                d = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64);
+            uint64_t mant;
+            int sh;
+            bool neg;
+            fm_parts(d, lj, mant, sh, neg);
+            tm[tx][r] = mant;
+            ts[tx][r] = sh | (neg ? 1 << 30 : 0);
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+            const int item = (ty * 2 + h) * 32 + tx;  // 32 columns x 16 quads
+            const int jj = item >> 4, q = item & 15;
+            const int j = j0 + jj, p = p0 + 4 * q;
+            if (j < np && p < kp) {
+                uint64_t mant[4];
+                int sh[4];
+                bool neg[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    mant[c] = tm[jj][4 * q + c];
+                    sh[c] = ts[jj][4 * q + c] & ((1 << 30) - 1);
+                    neg[c] = (ts[jj][4 * q + c] >> 30) != 0;
+                }
+                fm_store_residues<NM>(bs + static_cast<int64_t>(j) * kp + p, plane, mant, sh, neg, pw, W, f);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// One thread per cell: y_g (stored by the GEMM epilogue when there is one reduction
+// chunk; else rebuilt from the chunks' residues), t, the base-256 columns of X - t M
+// carried into signed 32-bit limbs, then the fast encode (beta 0, finite terms) or
+// finish_float.
+template <int NM>
+__global__ void fm_crt_kernel(const uint8_t* __restrict__ res, int chunks, int m, int n,
+                              const int* __restrict__ rlo, const int* __restrict__ clo,
+                              const int* __restrict__ rspan, const int* __restrict__ cspan,
+                              const uint8_t* __restrict__ flags, FxEpi e, FmParams f) {
+    constexpr int NA = (NM + 3) / 4;       // packed words of y
+    constexpr int NB = NM;                 // base-256 columns of M / p_g and M
+    constexpr int NL = (NB + 1 + 3) / 4;   // 32-bit limbs of |S| < M / 2 < 2^(8 NM - 1)
+    constexpr int NW = (NL + 1) / 2 + 2;   // 64-bit words: the value, alpha's 64 bits, sign
+    const size_t total = static_cast<size_t>(m) * n;
+    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+        const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+        const int fl0 = flags ? flags[idx] : 0;
+        if (e.beta == 0 && !fl0 && (rspan[i] == 0 || cspan[j] == 0)) {
+            store_float(e.c, e.out64, off, 0);  // a row or column of zeros: S = 0
+            continue;
+        }
+        uint32_t y[NA * 4];
+#pragma unroll
+        for (int g = NM; g < NA * 4; ++g) y[g] = 0;
+        if (chunks == 1) {
+#pragma unroll
+            for (int g = 0; g < NM; ++g) y[g] = __ldg(res + g * total + idx);
+        } else {
+#pragma unroll
+            for (int g = 0; g < NM; ++g) y[g] = 0;
+            for (int q = 0; q < chunks; ++q) {
+#pragma unroll
+                for (int g = 0; g < NM; ++g) y[g] += __ldg(res + (static_cast<size_t>(q) * NM + g) * total + idx);
+            }
+#pragma unroll
+            for (int g = 0; g < NM; ++g)
+                y[g] = fm_mod24(fm_mod24(y[g], f.p[g], f.magic32[g]) * f.inv[g], f.p[g], f.magic32[g]);
+        }
+        uint64_t fx = 0x80000000ull;  // + 1/2 in the 32-bit fixed point
+        uint32_t ya[NA];
+#pragma unroll
+        for (int a = 0; a < NA; ++a) {
+            ya[a] = y[4 * a] | y[4 * a + 1] << 8 | y[4 * a + 2] << 16 | y[4 * a + 3] << 24;
+#pragma unroll
+            for (int gi = 0; gi < 4; ++gi)
+                if (4 * a + gi < NM) fx += static_cast<uint64_t>(y[4 * a + gi]) * f.magic32[4 * a + gi];
+        }
+        const int32_t t = static_cast<int32_t>(fx >> 32);
+        // Columns X_b - t M_b, each < NM 255^2 < 2^22 in magnitude.
+        int64_t carry = 0;
+        uint32_t limb[NL];
+#pragma unroll
+        for (int l = 0; l < NL; ++l) {
+            int64_t v = carry;
+#pragma unroll
+            for (int bi = 0; bi < 4; ++bi) {
+                const int b = 4 * l + bi;
+                if (b < NB) {
+                    uint32_t col = 0;
+#pragma unroll
+                    for (int a = 0; a < NA; ++a) col = __dp4a(ya[a], f.md[a][b], col);
+                    v += (static_cast<int64_t>(col) - static_cast<int64_t>(t) * f.mmd[b]) << (8 * bi);
+                }
+            }
+            limb[l] = static_cast<uint32_t>(v);
+            carry = v >> 32;
+        }
+        const uint64_t ext = carry < 0 ? ~0ull : 0ull;
+        uint64_t w[NW];
+#pragma unroll
+        for (int q = 0; q < NW; ++q) {
+            const uint64_t lo = 2 * q < NL ? limb[2 * q] : static_cast<uint32_t>(ext);
+            const uint64_t hi = 2 * q + 1 < NL ? limb[2 * q + 1] : static_cast<uint32_t>(ext);
+            w[q] = lo | hi << 32;
+        }
+        const int ex = rlo[i] + clo[j];
+        if (e.beta == 0 && !fl0) {
+            store_float(e.c, e.out64, off, encode_signed_scaled<NW>(w, e.alpha, ex, e));
+            continue;
+        }
+        Big X;
+#pragma unroll
+        for (int q = 0; q < BW; ++q) X.w[q] = q < NW ? w[q] : ext;
+        int fl = fl0;
+        bool zero_out;
+        if (scale_flags(fl, zero_out, e.alpha)) big_mul_i64(X, e.alpha);
+        if (zero_out) big_zero(X);
+        finish_float(e, off, X, ex, fl);
+    }
+}
+
+// Launches for a moduli count (even, 2 .. 40): the limbs of X < NM M with M < 2^(8 NM).
+template <int NM>
+static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, const uint8_t* a,
+                             int64_t rsa, int64_t csa, const uint8_t* b, int64_t rsb, int64_t csb,
+                             bool f64, int m, int k, int n, const int* rlo, const int* clo,
+                             const uint32_t* pw, int shmax, const FmParams& f, cudaStream_t s) {
+    constexpr int NMP = (NM + 3) / 4 * 4;
+    const size_t smem = static_cast<size_t>(shmax) * NMP * 4 * (f64 ? 2 : 1);
+    // The B kernel adds a 25 KB static tile: allow the table's largest size beside it.
+    cudaFuncSetAttribute(fm_slice_a_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
+    cudaFuncSetAttribute(fm_slice_b_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
+    const int64_t aquads = static_cast<int64_t>(mp) * (kp / 4);
+    const int sgrid = static_cast<int>(aquads / 256 + 1 < 148 * 16 ? aquads / 256 + 1 : 148 * 16);
+    fm_slice_a_kernel<NM><<<sgrid, 256, smem, s>>>(as, mp, kp, a, rsa, csa, f64, m, k, rlo, pw, shmax, f);
+    dim3 g2(static_cast<unsigned>(np / 32),
+            static_cast<unsigned>((kp + 63) / 64 < 65535 ? (kp + 63) / 64 : 65535));
+    fm_slice_b_kernel<NM><<<g2, dim3(32, 8), smem, s>>>(bs, np, kp, b, rsb, csb, f64, k, n, clo, pw, shmax, f);
+}
+
+template <int NM>
+static void fm_launch_crt(const uint8_t* res, int chunks, int m, int n, const int* rlo,
+                          const int* clo, const int* rspan, const int* cspan, const uint8_t* flags,
+                          const FxEpi& e, const FmParams& f, int grid, cudaStream_t s) {
+    fm_crt_kernel<NM><<<grid, 256, 0, s>>>(res, chunks, m, n, rlo, clo, rspan, cspan, flags, e, f);
+}
+
+#define FM_EVEN_COUNTS(X) X(2) X(4) X(6) X(8) X(10) X(12) X(14) X(16) X(18) X(20) X(22) X(24) \
+    X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40)
+
+// Host side: the smallest even prefix of the moduli whose product exceeds 2 (1 + 2^-10) k
+// (2^sa - 1)(2^sb - 1), and the CRT constants. Returns false when 40 moduli are not enough.
+namespace {
+struct HBig {
+    uint32_t l[FM_LIMBS + 2];
+};
+void hb_set(HBig& x, uint32_t v) {
+    for (auto& q : x.l) q = 0;
+    x.l[0] = v;
+}
+void hb_mul(HBig& x, uint32_t v) {
+    uint64_t c = 0;
+    for (auto& q : x.l) {
+        const uint64_t t = static_cast<uint64_t>(q) * v + c;
+        q = static_cast<uint32_t>(t);
+        c = t >> 32;
+    }
+}
+uint32_t hb_div(HBig& x, uint32_t v) {  // x /= v, returns the remainder
+    uint64_t r = 0;
+    for (int i = FM_LIMBS + 1; i >= 0; --i) {
+        const uint64_t cur = (r << 32) | x.l[i];
+        x.l[i] = static_cast<uint32_t>(cur / v);
+        r = cur % v;
+    }
+    return static_cast<uint32_t>(r);
+}
+void hb_shl1_sub1(HBig& x, int bits) {  // x := 2^bits - 1
+    for (auto& q : x.l) q = 0;
+    for (int b = 0; b < bits; ++b) x.l[b >> 5] |= 1u << (b & 31);
+}
+void hb_mul_big(HBig& x, const HBig& y) {
+    HBig r{};
+    for (int i = 0; i < FM_LIMBS + 2; ++i) {
+        uint64_t c = 0;
+        for (int j = 0; i + j < FM_LIMBS + 2; ++j) {
+            const uint64_t t = static_cast<uint64_t>(x.l[i]) * y.l[j] + r.l[i + j] + c;
+            r.l[i + j] = static_cast<uint32_t>(t);
+            c = t >> 32;
+        }
+    }
+    x = r;
+}
+bool hb_less(const HBig& x, const HBig& y) {
+    for (int i = FM_LIMBS + 1; i >= 0; --i)
+        if (x.l[i] != y.l[i]) return x.l[i] < y.l[i];
+    return false;
+}
+uint32_t inv_mod(uint32_t a, uint32_t p) {
+    int64_t t = 0, nt = 1, r = p, nr = a % p;
+    while (nr) {
+        const int64_t q = r / nr;
+        const int64_t tt = t - q * nt;
+        t = nt, nt = tt;
+        const int64_t rr = r - q * nr;
+        r = nr, nr = rr;
+    }
+    return static_cast<uint32_t>(t < 0 ? t + p : t);
+}
+}  // namespace
+
+static bool fm_plan(int span_a, int span_b, size_t k, FmParams& f) {
+    if (span_a <= 0 || span_b <= 0 || span_a + span_b > 280) return false;
+    // need := 2 (1 + 2^-20) k (2^sa - 1)(2^sb - 1), rounded up through 2^20 scaling
+    HBig need, y;
+    hb_shl1_sub1(need, span_a);
+    hb_shl1_sub1(y, span_b);
+    hb_mul_big(need, y);
+    hb_mul(need, static_cast<uint32_t>(k > 0xFFFFFFFFull ? 0xFFFFFFFFull : k));
+    if (k > 0xFFFFFFFFull) return false;
+    hb_mul(need, (1u << 10) + 1);  // compare M 2^10 > need
+    hb_mul(need, 2);
+    HBig M;
+    hb_set(M, 1);
+    int nm = 0;
+    for (; nm < FM_MAX; ++nm) {
+        HBig scaled = M;
+        hb_mul(scaled, 1u << 10);
+        if (hb_less(need, scaled)) break;
+        hb_mul(M, kFmModuli[nm]);
+    }
+    {
+        HBig scaled = M;
+        hb_mul(scaled, 1u << 10);
+        if (!hb_less(need, scaled)) return false;
+    }
+    if (nm & 1) {  // the kernels come in even moduli counts
+        if (nm == FM_MAX) return false;
+        hb_mul(M, kFmModuli[nm++]);
+    }
+    f = FmParams{};
+    f.nm = nm;
+    auto byte_of = [](const HBig& x, int b) {
+        return static_cast<uint32_t>((x.l[b >> 2] >> (8 * (b & 3))) & 255u);
+    };
+    for (int b = 0; b < nm; ++b) f.mmd[b] = static_cast<uint8_t>(byte_of(M, b));
+    for (int g = 0; g < nm; ++g) {
+        const uint32_t p = kFmModuli[g];
+        HBig mg = M;
+        hb_div(mg, p);
+        HBig t = mg;
+        const uint32_t mgmod = hb_div(t, p);
+        f.p[g] = static_cast<uint16_t>(p);
+        f.inv[g] = static_cast<uint16_t>(inv_mod(mgmod, p));
+        f.magic32[g] = static_cast<uint32_t>(((1ull << 32) + p - 1) / p);
+        for (int b = 0; b < nm; ++b) f.md[g / 4][b] |= byte_of(mg, b) << (8 * (g % 4));
+    }
+    return true;
+}
+
 // ------------------------------------------------------------ direct route
 
 // The reference's register, Complete<L, MIN_EXP>: L low limbs and an extension word,
@@ -1110,7 +1545,7 @@ constexpr int FX_MAX_DIGITS = 16;
 int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrdiff_t rsa,
                    ptrdiff_t csa, const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c,
                    ptrdiff_t rsc, ptrdiff_t csc, size_t m, size_t k, size_t n, int64_t alpha,
-                   int64_t beta, int mode, uor_b200_route* route) {
+                   int64_t beta, int mode, uor_b200_route* route, bool digits_only) {
     cudaStream_t s = ctx->stream;
     if (route) *route = uor_b200_route{};
     if (m == 0 || n == 0) return UOR_B200_OK;
@@ -1168,7 +1603,120 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
     const int Lb = g[1] ? (g[1] + 2 + 7) / 8 : 0;
     const bool any_nf = g[2] != 0;
 
+    // ---- modular route: nm int8 GEMMs and the CRT
+    FmParams fm;
+    const bool mod_ok = !digits_only && k > 0 && g[0] > 0 && g[1] > 0 && fm_plan(g[0], g[1], k, fm) &&
+                        (size_t)((g[0] > g[1] ? g[0] : g[1]) + 1) * ((fm.nm + 3) / 4 * 4) * 4 *
+                                (e64 ? 2 : 1) <= FM_TABLE_MAX;
+    auto run_modular = [&]() -> int {
+        const int nm = fm.nm;
+        KSParams q{};
+        q.num_groups = nm;
+        for (int gg = 0; gg < nm; ++gg) {
+            q.pair_begin[gg] = gg;
+            q.pair_a[gg] = q.pair_b[gg] = static_cast<uint8_t>(gg);
+            q.pair_sign[gg] = 3;  // balanced residues are signed on both sides
+            q.res_mod[gg] = fm.p[gg];
+            q.res_magic[gg] = fm.magic32[gg];
+            q.res_off[gg] = static_cast<uint32_t>(fm.p[gg] * ((0x80000000ull + fm.p[gg] - 1) / fm.p[gg]));
+        }
+        q.pair_begin[nm] = nm;
+        const int num_kb = (int)((k + KS_BK - 1) / KS_BK);
+        // |residue product| <= 2^14: 1023 blocks keep |acc| < 2^31 - 2^21 (the epilogue's
+        // 32-bit reduction relies on it)
+        const int64_t lane = (int64_t)INT_MAX / 16384 / KS_BK;
+        q.kb_per_chunk = (int)(lane < num_kb ? lane : num_kb);
+        q.num_chunks = (num_kb + q.kb_per_chunk - 1) / q.kb_per_chunk;
+        q.num_kb = num_kb;
+        q.m = (int)m;
+        q.n = (int)n;
+        q.mp = (int)ks_rows_pad(m);
+        q.np = (int)rup(n, KS_BN);
+        q.status = ctx->d_status;
+        q.budget_ns = ctx->budget_ns;
+        const size_t kp = rup(k, 16);
+        const int shmax = (g[0] > g[1] ? g[0] : g[1]) + 1;
+        const int nmp = (nm + 3) / 4 * 4;
+        const int W = e64 ? 2 : 1;  // table words per (shift, modulus): significand bytes / 4
+        if (q.num_chunks == 1)  // the epilogue stores y_g = r_g (M / p_g)^-1 mod p_g
+            for (int gg = 0; gg < nm; ++gg) q.res_inv[gg] = fm.inv[gg];
+        const size_t a_bytes = rup((size_t)nm * q.mp * kp, 256);
+        const size_t b_bytes = rup((size_t)nm * q.np * kp, 256);
+        const size_t res_bytes = rup((size_t)q.num_chunks * nm * m * n, 256);
+        const size_t flag_bytes = any_nf ? rup(m * n, 256) : 0;
+        const size_t pw_bytes = rup((size_t)nmp * shmax * W * 4, 256);
+        int st2 = UOR_B200_OK;
+        uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(
+            ctx, SLOT_WS, a_bytes + b_bytes + res_bytes + flag_bytes + pw_bytes + 256, &st2));
+        if (!ws) return st2;
+        int8_t* as = reinterpret_cast<int8_t*>(ws);
+        int8_t* bs = reinterpret_cast<int8_t*>(ws + a_bytes);
+        uint8_t* res = ws + a_bytes + b_bytes;
+        uint8_t* flags = any_nf ? res + res_bytes : nullptr;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(res + res_bytes + flag_bytes);
+        {
+            // row sh, word w, modulus g: bytes i of 2^(sh + 8 (4 w + i)) mod p_g
+            std::vector<uint32_t> tab((size_t)shmax * W * nmp, 0);
+            for (int gg = 0; gg < nm; ++gg) {
+                const uint32_t pg = fm.p[gg];
+                uint32_t v = 1 % pg;  // 2^sh mod p
+                for (int sh = 0; sh < shmax; ++sh) {
+                    uint32_t c = v;
+                    for (int bi = 0; bi < 4 * W; ++bi) {
+                        tab[((size_t)sh * W + bi / 4) * nmp + gg] |= c << (8 * (bi % 4));
+                        c = c * 256 % pg;
+                    }
+                    v = v * 2 % pg;
+                }
+            }
+            if (cudaMemcpyAsync(pw, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+        }
+        if (any_nf) {
+            dim3 grid((unsigned)((n + 127) / 128), (unsigned)(m < 65535 ? m : 65535));
+            fx_flags_kernel<<<grid, 128, 0, s>>>(a, rsa, csa, b, rsb, csb, e64, (int)m, (int)k, (int)n,
+                                                  rnf, cnf, flags);
+        }
+        switch (nm) {
+#define FM_SLICES(N)                                                                            \
+    case N:                                                                                     \
+        fm_launch_slices<N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, e64, (int)m, \
+                            (int)k, (int)n, rlo, clo, pw, shmax, fm, s);                        \
+        break;
+            FM_EVEN_COUNTS(FM_SLICES)
+#undef FM_SLICES
+        default: return UOR_B200_UNSUPPORTED;
+        }
+        if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        q.residue = res;
+        q.partial = nullptr;
+        if ((st2 = ks_run(as, nm, bs, nm, k, kp, q, ctx->sm_count, s, route ? &route->ctas : nullptr)) !=
+            UOR_B200_OK)
+            return st2;
+        const size_t total = m * n;
+        const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+        switch (nm) {
+#define FM_CRT(N)                                                                               \
+    case N:                                                                                     \
+        fm_launch_crt<N>(res, q.num_chunks, (int)m, (int)n, rlo, clo, rspan, cspan, flags, e, fm, \
+                         rgrid, s);                                                             \
+        break;
+            FM_EVEN_COUNTS(FM_CRT)
+#undef FM_CRT
+        default: return UOR_B200_UNSUPPORTED;
+        }
+        if (route) {
+            route->moduli = (uint32_t)nm;
+            route->pairs = (uint32_t)nm;
+            route->a_layout = route->b_layout = (uint32_t)nm;
+            route->k_chunks = (uint32_t)q.num_chunks;
+            route->tile_m = (uint32_t)(m > 128 ? 256 : KS_BM);
+        }
+        return cuda_status(cudaGetLastError());
+    };
+
     if (La > FX_MAX_DIGITS || Lb > FX_MAX_DIGITS) {
+        if (mod_ok) return run_modular();
         // Direct route: the reference's register per cell on CUDA cores.
         if (route) route->tile_m = route->tile_n = route->tile_k = 0;
         dim3 grid((unsigned)((n + 127) / 128), (unsigned)(m < 65535 ? m : 65535));
@@ -1207,6 +1755,12 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
             ebound = kk * 64 * pairs_on(D - 1) + (kk * pairs_on(D - 2) + 3) / 4 +
                      (kk * nmax + 1019) / 1020 + 1;
         }
+    }
+    if (mod_ok) {
+        // The modular route when it runs fewer GEMMs than the digit pairs would.
+        int digit_pairs = 0;
+        for (int d = D; d < G; ++d) digit_pairs += pairs_on(d);
+        if (fm.nm < digit_pairs) return run_modular();
     }
 
     // ---- digit slices and the slice-pair product of diagonals d >= d_lo

@@ -197,7 +197,14 @@ __global__ void __launch_bounds__(KS_THREADS, 1)
                 tmem_ld32(taddr, r);
                 tmem_ld_wait();
                 const int col0 = w.tn * KS_BN + cc * 32;
-                if (row_ok && col0 < p.n) {
+                if (p.residue) {
+                    if (row_ok && col0 < p.n)
+                        ks_store_residues(p.residue + (static_cast<size_t>(w.q) * p.num_groups + w.g) *
+                                                          static_cast<size_t>(p.m) * p.n +
+                                              static_cast<size_t>(row) * p.n + col0,
+                                          r, min(32, p.n - col0), p.res_mod[w.g], p.res_magic[w.g],
+                                          p.res_off[w.g], p.res_inv[w.g]);
+                } else if (row_ok && col0 < p.n) {
                     int32_t* dst = plane + static_cast<size_t>(row) * p.n + col0;
                     if (col0 + 32 <= p.n && (p.n & 3) == 0) {
 #pragma unroll
@@ -268,7 +275,7 @@ int ks_run(const void* as, int La, const void* bs, int Lb, size_t k, size_t kp, 
     } else {
         CUtensorMap tmC;
         const uint64_t planes = static_cast<uint64_t>(p.num_chunks) * p.num_groups;
-        p.tma_store = (p.n % 4) == 0 &&
+        p.tma_store = !p.residue && (p.n % 4) == 0 &&
                       make_tmap_s32_3d(&tmC, p.partial, p.n, p.m, planes, static_cast<uint64_t>(p.n) * 4,
                                        static_cast<uint64_t>(p.m) * p.n * 4, 32, 32);
         if (!p.tma_store) memset(&tmC, 0, sizeof(tmC));

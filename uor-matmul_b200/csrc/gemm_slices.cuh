@@ -39,12 +39,67 @@ struct KSParams {
     int* status;
     uint64_t budget_ns;
     int tma_store;            // pair kernel: partials written by TMA through a 3-D map
+    // Residue mode (residue != nullptr): instead of s32 partials, each unit writes its
+    // accumulator reduced modulo res_mod[group] as one byte in [0, res_mod) to
+    // residue[chunk][group][m][n]; res_magic[group] = ceil(2^64 / res_mod[group]).
+    // With res_inv[group] != 0 the stored byte is (r res_inv) mod res_mod instead.
+    // res_magic = ceil(2^32 / res_mod); res_off = res_mod ceil(2^31 / res_mod) mod 2^32.
+    uint8_t* residue;
+    uint16_t res_mod[KS_MAX_GROUPS];
+    uint16_t res_inv[KS_MAX_GROUPS];
+    uint32_t res_magic[KS_MAX_GROUPS];
+    uint32_t res_off[KS_MAX_GROUPS];
     int pair_begin[KS_MAX_GROUPS + 1];
     uint8_t pair_a[KS_MAX_PAIRS];
     uint8_t pair_b[KS_MAX_PAIRS];
     uint8_t pair_sign[KS_MAX_PAIRS];  // bit 0: A slice signed, bit 1: B slice signed
     uint32_t pair_idesc[KS_MAX_PAIRS];
 };
+
+// x mod p for 0 <= x < 2^40 and 2 <= p <= 256, with magic = ceil(2^64 / p): the quotient
+// floor(x magic / 2^64) is exact because x (magic - 2^64 / p) / 2^64 < 2^-24 stays below the
+// gap 1/p between x/p's fractional part and 1.
+__device__ __forceinline__ uint32_t ks_mod(uint64_t x, uint32_t p, uint64_t magic) {
+    const uint64_t q = __umul64hi(x, magic);
+    return static_cast<uint32_t>(x - q * p);
+}
+
+// One epilogue fragment in residue mode: 32 consecutive s32 accumulators of one row
+// (lim of them inside the output) reduced into [0, p), multiplied by inv modulo p when
+// inv is not 0, and stored as bytes. A chunk holds at most 1023 blocks of 128 products of
+// at most 2^14, so |acc| < 2^31 - 2^21 and x = acc + off (off = p ceil(2^31 / p) <=
+// 2^31 + 255) lies in [0, 2^32); the quotient estimate umulhi(x, ceil(2^32 / p)) is
+// floor(x / p) or one more, so one correction gives x mod p. (r inv < 2^16: the same
+// estimate is exact there.)
+__device__ __forceinline__ void ks_store_residues(uint8_t* dst, const uint32_t (&r)[32], int lim,
+                                                  uint32_t p, uint32_t magic, uint32_t off,
+                                                  uint32_t inv) {
+    uint32_t w[8];
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+        w[v] = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t x = r[4 * v + b] + off;
+            int32_t y = static_cast<int32_t>(x - __umulhi(x, magic) * p);
+            y += (y >> 31) & static_cast<int32_t>(p);
+            uint32_t u = static_cast<uint32_t>(y);
+            if (inv) {
+                u *= inv;
+                u -= __umulhi(u, magic) * p;
+            }
+            w[v] |= u << (8 * b);
+        }
+    }
+    if (lim == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < lim) dst[j] = static_cast<uint8_t>(w[j >> 2] >> (8 * (j & 3)));
+    }
+}
 
 // Rows per slice in the A stack: whole tiles of the kernel ks_run will choose.
 inline size_t ks_rows_pad(size_t m) {

@@ -232,7 +232,13 @@ __global__ void __launch_bounds__(KQ_THREADS, 1)
                     if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty0 + 8 * buf, 0));
                 }
                 const int col0 = w.tn * KQ_BN + cc * 32;
-                if (p.tma_store) {
+                if (p.residue) {
+                    if (row < p.m && col0 < p.n)
+                        ks_store_residues(p.residue + static_cast<size_t>(plane) * p.m * p.n +
+                                              static_cast<size_t>(row) * p.n + col0,
+                                          r, min(32, p.n - col0), p.res_mod[w.g], p.res_magic[w.g],
+                                          p.res_off[w.g], p.res_inv[w.g]);
+                } else if (p.tma_store) {
                     if (wrow0 < p.m && col0 < p.n) {
                         uint8_t* sb = stage_w + (nstore & 1) * 4096;
                         if (lane == 0) bulk_wait_read<1>();

@@ -23,7 +23,7 @@ OK, NONCONFORMANT, OUTPUT_ALIASES, DEVICE_ERROR, TIMEOUT, NCCL_ERROR, DOES_NOT_F
     INVALID_ARGUMENT, UNSUPPORTED = range(9)
 NEAREST, TOWARD_ZERO, SATURATING, WRAPPING = range(4)
 I8, I16, I32, I64, I128, F32, F64, TROP_I8, TROP_I16, TROP_I32, TROP_I64 = range(1, 12)
-DEVICE_POINTERS, ASYNC = 1, 2
+DEVICE_POINTERS, ASYNC, FLOAT_DIGITS = 1, 2, 4
 KERNEL_NAMES = {0: "none", 1: "i8_tcgen05", 2: "limb_tcgen05", 3: "tropical",
                 4: "coded_tcgen05", 5: "float_exact", 6: "epilogue_only", 7: "skinny_dp4a"}
 
@@ -55,7 +55,8 @@ class Route(ctypes.Structure):
                 ("tile_n", ctypes.c_uint32), ("tile_k", ctypes.c_uint32),
                 ("k_chunks", ctypes.c_uint32), ("a_layout", ctypes.c_uint32),
                 ("b_layout", ctypes.c_uint32), ("ctas", ctypes.c_uint32),
-                ("pairs", ctypes.c_uint32), ("fixups", ctypes.c_uint32)]
+                ("pairs", ctypes.c_uint32), ("fixups", ctypes.c_uint32),
+                ("moduli", ctypes.c_uint32)]
 
     def as_dict(self):
         d = {f: getattr(self, f) for f, _ in self._fields_}
@@ -304,10 +305,14 @@ def gemm_i8_i32(m, k, n, a, b, c, ctx=None, route=None, asynchronous=False):
 # ------------------------------------------------------------------ float
 
 def gemm_float(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None,
-               route=None, asynchronous=False):
+               route=None, asynchronous=False, digits=False):
+    """gemm_float over views; digits=True takes the digit-slice route even where the
+    modular route applies (the same bytes either way)."""
     dev = _on_device(a, b, c)
     A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
     call = make_call(encode, dev, ctx, route, asynchronous)
+    if digits:
+        call.flags |= FLOAT_DIGITS
     _check(lib().uor_b200_gemm_float(elem, out, ctypes.byref(A), ctypes.byref(B),
                                      ctypes.byref(C), alpha, beta, ctypes.byref(call)),
            "gemm_float")
