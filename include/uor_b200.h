@@ -115,21 +115,22 @@ typedef struct uor_b200_route {
     uint32_t ctas;        /* CTAs launched per chunk */
     uint32_t pairs;       /* int8 slice-pair GEMMs run on the tensor cores (1 for K1) */
     uint32_t fixups;      /* exact float: cells recomputed exactly after the lazy digits */
-    uint32_t moduli;      /* exact float: moduli of the modular route (0: digit slices) */
+    uint32_t moduli;      /* exact float / wide integers: moduli of the modular route (0: slices) */
 } uor_b200_route;
 
 #define UOR_B200_DEVICE_POINTERS 1u
 #define UOR_B200_ASYNC 2u
-/* Exact float only: take the digit-slice route even where the modular route would run
+/* Exact float and wide integers (i16 .. i64, Complex): take the digit / byte-slice route
+ * even where the modular route (residues modulo coprime moduli and the CRT) would run
  * fewer GEMMs. Both are exact; the bytes are the same. */
-#define UOR_B200_FLOAT_DIGITS 4u
+#define UOR_B200_DIGIT_SLICES 4u
 
 /* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)
  * plus where the pointers live. A NULL call means: Nearest, host pointers,
  * the default context of the current device. */
 typedef struct uor_b200_call {
     uint32_t encode;        /* uor_b200_encode */
-    uint32_t flags;         /* UOR_B200_DEVICE_POINTERS | UOR_B200_ASYNC | UOR_B200_FLOAT_DIGITS */
+    uint32_t flags;         /* UOR_B200_DEVICE_POINTERS | UOR_B200_ASYNC | UOR_B200_DIGIT_SLICES */
     uor_b200_ctx *ctx;      /* NULL: the current device's default context */
     uor_b200_route *route;  /* optional out */
 } uor_b200_call;

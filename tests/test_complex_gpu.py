@@ -35,7 +35,8 @@ def same(got, want, out):
 
 @pytest.mark.parametrize("bits", [32, 64])
 @pytest.mark.parametrize("out", [U.I32, U.I64, U.I128])
-def test_random_full_range(bits, out):
+@pytest.mark.parametrize("digits", [False, True])
+def test_random_full_range(bits, out, digits):
     rng = np.random.default_rng(bits + 7 * out)
     for (m, k, n) in [(1, 1, 1), (13, 17, 19), (130, 300, 135), (257, 64, 70)]:
         a = rand_parts(rng, bits, m * k)
@@ -47,7 +48,7 @@ def test_random_full_range(bits, out):
             got, want = c0.copy(), c0.copy()
             route = U.Route()
             U.gemm_complex(ELEM[bits], out, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1),
-                           alpha, beta, mode, route=route)
+                           alpha, beta, mode, route=route, digits=digits)
             oracle(a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), alpha, beta, mode, out)
             assert same(got, want, out), (m, k, n, alpha, beta, mode)
             assert route.kernel == 2  # the limb (byte-sliced) path
@@ -88,7 +89,8 @@ def test_strided_views_and_transposed_b():
     assert np.array_equal(got, want)
 
 
-def test_deep_reduction_several_chunks():
+@pytest.mark.parametrize("digits", [False, True])
+def test_deep_reduction_several_chunks(digits):
     rng = np.random.default_rng(11)
     m, k, n = 20, 20000, 12
     a = rand_parts(rng, 32, m * k)
@@ -96,10 +98,10 @@ def test_deep_reduction_several_chunks():
     got, want = out_array(U.I128, 2 * m * n), out_array(U.I128, 2 * m * n)
     route = U.Route()
     U.gemm_complex(U.I32, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1),
-                   route=route)
+                   route=route, digits=digits)
     oracle(a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), 1, 0, U.NEAREST, U.I128)
     assert same(got, want, U.I128)
-    assert route.k_chunks >= 2
+    assert route.k_chunks >= 2 if digits else route.moduli > 0
 
 
 def test_k_zero_applies_beta_in_the_accumulator():

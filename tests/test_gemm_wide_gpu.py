@@ -43,9 +43,12 @@ def rand_full(rng, bits, count):
     return rng.integers(info.min, info.max, size=count, endpoint=True).astype(NP[bits])
 
 
+@pytest.mark.parametrize("digits", [False, True])
 @pytest.mark.parametrize("bits", [16, 32, 64])
 @pytest.mark.parametrize("out", [U.I32, U.I64, U.I128])
-def test_random_full_range(bits, out):
+def test_random_full_range(bits, out, digits):
+    """i16 always, and i32 / i64 with digits=True, on the byte-slice pairs; i32 / i64
+    otherwise on the modular route (residue GEMMs and the CRT)."""
     rng = np.random.default_rng(bits * 10 + out)
     for (m, k, n) in [(1, 1, 1), (13, 17, 19), (130, 300, 270), (300, 200, 261)]:
         a, b = rand_full(rng, bits, m * k), rand_full(rng, bits, k * n)
@@ -56,7 +59,7 @@ def test_random_full_range(bits, out):
             got, want = c0.copy(), c0.copy()
             route = U.Route()
             U.gemm(ELEM[bits], out, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), alpha,
-                   beta, mode, route=route)
+                   beta, mode, route=route, digits=digits)
             oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), alpha, beta,
                        mode, out)
             if out == U.I128:
@@ -64,9 +67,11 @@ def test_random_full_range(bits, out):
             else:
                 assert np.array_equal(got, want), (m, k, n, alpha, beta, mode)
             assert route.kernel == 2
+            assert (route.moduli > 0) == (bits > 16 and not digits), route.as_dict()
 
 
-def test_deep_i32_chunks_and_strides():
+@pytest.mark.parametrize("digits", [False, True])
+def test_deep_i32_chunks_and_strides(digits):
     rng = np.random.default_rng(5)
     m, k, n = 40, 30000, 24
     a, b = rand_full(rng, 32, m * k), rand_full(rng, 32, k * n)
@@ -75,11 +80,41 @@ def test_deep_i32_chunks_and_strides():
     route = U.Route()
     # B read as its own transpose: stored n x k
     bt = np.ascontiguousarray(b.reshape(k, n).T).reshape(-1)
-    U.gemm(U.I32, U.I128, a, (m, k, k, 1), bt, (k, n, 1, k), got, (m, n, n, 1), route=route)
+    U.gemm(U.I32, U.I128, a, (m, k, k, 1), bt, (k, n, 1, k), got, (m, n, n, 1), route=route,
+           digits=digits)
     oracle_int(a, (m, k, k, 1, 0), bt, (k, n, 1, k, 0), want, (m, n, n, 1, 0), 1, 0, U.NEAREST,
                U.I128)
     assert i128_values(got) == i128_values(want)
-    assert route.k_chunks >= 3
+    # byte slices: an s32 diagonal lane holds ~8 Ki products; residues: 1023 blocks of 128
+    assert route.k_chunks >= 3 if digits else (route.k_chunks == 1 and route.moduli > 0)
+
+
+def test_modular_two_chunks_and_i64_extremes():
+    """k past 1023 blocks of 128 splits the residue GEMMs into two chunks summed in the
+    CRT; i64 MIN / MAX everywhere drive |S| to its bound k 2^126."""
+    rng = np.random.default_rng(9)
+    m, k, n = 5, 140000, 7
+    a, b = rand_full(rng, 32, m * k), rand_full(rng, 32, k * n)
+    got, want = np.zeros(m * n * 2, np.int64), np.zeros(m * n * 2, np.int64)
+    route = U.Route()
+    U.gemm(U.I32, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), route=route)
+    oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), 1, 0, U.NEAREST,
+               U.I128)
+    assert i128_values(got) == i128_values(want)
+    assert route.k_chunks == 2 and route.moduli > 0
+    m, k, n = 9, 3000, 11
+    lo, hi = np.iinfo(np.int64).min, np.iinfo(np.int64).max
+    a = rng.choice([lo, hi, lo + 1, -1, 0], size=m * k).astype(np.int64)
+    b = rng.choice([lo, hi, lo], size=k * n).astype(np.int64)
+    for mode in (U.NEAREST, U.WRAPPING):
+        got, want = np.zeros(m * n * 2, np.int64), np.zeros(m * n * 2, np.int64)
+        route = U.Route()
+        U.gemm(U.I64, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), 3, 0, mode,
+               route=route)
+        oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), 3, 0, mode,
+                   U.I128)
+        assert i128_values(got) == i128_values(want), mode
+        assert route.moduli > 0
 
 
 @pytest.mark.slow

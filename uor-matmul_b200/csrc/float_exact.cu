@@ -29,6 +29,7 @@
 #include "aux.cuh"
 #include "float_exact.h"
 #include "gemm_slices.cuh"
+#include "modular.cuh"
 #include "ptx.cuh"
 
 namespace uor {
@@ -977,54 +978,12 @@ __global__ void fx_fix_kernel(const uint32_t* __restrict__ list, const uint32_t*
 
 // ------------------------------------------------------------ modular route
 //
-// Ozaki scheme II (Ozaki, Uchino and Imamura, "Ozaki Scheme II: A GEMM-oriented emulation
-// of floating-point matrix multiplication using an integer modular technique", 2025):
-// the scaled integers of the digit route (A_ip 2^-lo_i, B_pj 2^-lo_j) are reduced modulo
-// nm pairwise coprime moduli p_g <= 256 into balanced residues, which are int8; one int8
-// GEMM per modulus on the tensor cores gives S mod p_g exactly (the s32 accumulator is
-// reduced in the slice-pair kernel's epilogue); and the Chinese remainder theorem rebuilds
-// each cell's exact integer S from its nm residues. M = prod p_g is chosen above twice the
-// bound k (2^span_A - 1)(2^span_B - 1) on |S|, so S is the representative of X = sum_g
-// y_g M / p_g (y_g = r_g (M / p_g)^-1 mod p_g) nearest to zero: S = X - t M with t the
-// integer nearest X / M = sum_g y_g / p_g. With M > 2 (1 + 2^-10) bound, X / M lies within
-// 1/2 - 2^-11 of t, and the 32-bit fixed-point sum sum_g y_g ceil(2^32 / p_g) overshoots
-// X / M 2^32 by less than 40 * 255 (2^-18.6 after scaling), so rounding it finds t. X
-// itself is summed in base-256 columns, X_b = sum_g y_g digit_b(M / p_g), four moduli per
-// dp4a. Then the epilogue and encode of the digit route.
+// The modular route (modular.cuh): the scaled integers of the digit route (A_ip 2^-lo_i,
+// B_pj 2^-lo_j) reduced modulo nm coprime moduli into balanced int8 residues, one int8 GEMM
+// per modulus, and the CRT rebuilding each cell's exact integer S, |S| <= k (2^span_A - 1)
+// (2^span_B - 1). Then the epilogue and encode of the digit route.
 
-constexpr int FM_MAX = 40;    // moduli
-constexpr int FM_LIMBS = 11;  // 32-bit limbs of X < nm M (the 40 moduli's product is 291 bits)
 constexpr int FM_TABLE_MAX = 48 * 1024;  // bytes of the 2^s table in shared memory
-// 2^8, 3 5 17, 11 23, 13 19 and primes: pairwise coprime, largest first.
-static const uint16_t kFmModuli[FM_MAX] = {256, 255, 253, 251, 247, 241, 239, 233, 229, 227,
-                                           223, 211, 199, 197, 193, 191, 181, 179, 173, 167,
-                                           163, 157, 151, 149, 139, 137, 131, 127, 113, 109,
-                                           107, 103, 101, 97,  89,  83,  79,  73,  71,  67};
-
-struct FmParams {
-    int nm;                              // moduli (even)
-    uint16_t p[FM_MAX];
-    uint16_t inv[FM_MAX];                // (M / p_g)^-1 mod p_g
-    uint32_t magic32[FM_MAX];            // ceil(2^32 / p_g)
-    uint32_t md[FM_MAX / 4][FM_MAX];     // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
-    uint8_t mmd[FM_MAX];                 // byte b of M (M < 2^(8 nm))
-};
-
-// x mod p for x < 2^24: floor(x ceil(2^32 / p) / 2^32) is exact there (the error term
-// x (ceil(2^32/p) - 2^32/p) / 2^32 < 2^-8 never reaches the next multiple).
-__device__ __forceinline__ uint32_t fm_mod24(uint32_t x, uint32_t p, uint32_t magic32) {
-    return x - __umulhi(x, magic32) * p;
-}
-
-// Balanced residue byte of +-mant 2^sh modulo p from u = sum_i byte_i(mant) (2^(sh + 8i)
-// mod p) (< 2^19): in [-(p-1)/2, (p-1)/2] for odd p, [-128, 127] for 256 (where -(-128)
-// is the same byte 128 modulo 256).
-__device__ __forceinline__ uint32_t fm_balanced(uint32_t u, uint32_t nmask, uint32_t p,
-                                                uint32_t magic32) {
-    const uint32_t r = fm_mod24(u, p, magic32);
-    const uint32_t b = r >= (p + 1) / 2 ? r - p : r;
-    return ((b ^ nmask) - nmask) & 255u;
-}
 
 // The table of words [2^sh, 2^(sh+8), 2^(sh+16), 0] mod p_g (f32 significands, W = 1), or
 // two words covering 2^(sh + 8i) for i < 8 (f64, W = 2), row sh holding W x NMP words.
@@ -1186,9 +1145,7 @@ __global__ void fm_crt_kernel(const uint8_t* __restrict__ res, int chunks, int m
                               const int* __restrict__ rlo, const int* __restrict__ clo,
                               const int* __restrict__ rspan, const int* __restrict__ cspan,
                               const uint8_t* __restrict__ flags, FxEpi e, FmParams f) {
-    constexpr int NA = (NM + 3) / 4;       // packed words of y
-    constexpr int NB = NM;                 // base-256 columns of M / p_g and M
-    constexpr int NL = (NB + 1 + 3) / 4;   // 32-bit limbs of |S| < M / 2 < 2^(8 NM - 1)
+    constexpr int NL = FmLimbs<NM>::value;
     constexpr int NW = (NL + 1) / 2 + 2;   // 64-bit words: the value, alpha's 64 bits, sign
     const size_t total = static_cast<size_t>(m) * n;
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -1200,53 +1157,10 @@ __global__ void fm_crt_kernel(const uint8_t* __restrict__ res, int chunks, int m
             store_float(e.c, e.out64, off, 0);  // a row or column of zeros: S = 0
             continue;
         }
-        uint32_t y[NA * 4];
-#pragma unroll
-        for (int g = NM; g < NA * 4; ++g) y[g] = 0;
-        if (chunks == 1) {
-#pragma unroll
-            for (int g = 0; g < NM; ++g) y[g] = __ldg(res + g * total + idx);
-        } else {
-#pragma unroll
-            for (int g = 0; g < NM; ++g) y[g] = 0;
-            for (int q = 0; q < chunks; ++q) {
-#pragma unroll
-                for (int g = 0; g < NM; ++g) y[g] += __ldg(res + (static_cast<size_t>(q) * NM + g) * total + idx);
-            }
-#pragma unroll
-            for (int g = 0; g < NM; ++g)
-                y[g] = fm_mod24(fm_mod24(y[g], f.p[g], f.magic32[g]) * f.inv[g], f.p[g], f.magic32[g]);
-        }
-        uint64_t fx = 0x80000000ull;  // + 1/2 in the 32-bit fixed point
-        uint32_t ya[NA];
-#pragma unroll
-        for (int a = 0; a < NA; ++a) {
-            ya[a] = y[4 * a] | y[4 * a + 1] << 8 | y[4 * a + 2] << 16 | y[4 * a + 3] << 24;
-#pragma unroll
-            for (int gi = 0; gi < 4; ++gi)
-                if (4 * a + gi < NM) fx += static_cast<uint64_t>(y[4 * a + gi]) * f.magic32[4 * a + gi];
-        }
-        const int32_t t = static_cast<int32_t>(fx >> 32);
-        // Columns X_b - t M_b, each < NM 255^2 < 2^22 in magnitude.
-        int64_t carry = 0;
+        uint32_t y[NM];
+        fm_load_y<NM>(res, chunks, total, idx, f, y);
         uint32_t limb[NL];
-#pragma unroll
-        for (int l = 0; l < NL; ++l) {
-            int64_t v = carry;
-#pragma unroll
-            for (int bi = 0; bi < 4; ++bi) {
-                const int b = 4 * l + bi;
-                if (b < NB) {
-                    uint32_t col = 0;
-#pragma unroll
-                    for (int a = 0; a < NA; ++a) col = __dp4a(ya[a], f.md[a][b], col);
-                    v += (static_cast<int64_t>(col) - static_cast<int64_t>(t) * f.mmd[b]) << (8 * bi);
-                }
-            }
-            limb[l] = static_cast<uint32_t>(v);
-            carry = v >> 32;
-        }
-        const uint64_t ext = carry < 0 ? ~0ull : 0ull;
+        const uint64_t ext = fm_crt<NM>(y, f, limb) ? ~0ull : 0ull;
         uint64_t w[NW];
 #pragma unroll
         for (int q = 0; q < NW; ++q) {
@@ -1294,119 +1208,6 @@ static void fm_launch_crt(const uint8_t* res, int chunks, int m, int n, const in
                           const int* clo, const int* rspan, const int* cspan, const uint8_t* flags,
                           const FxEpi& e, const FmParams& f, int grid, cudaStream_t s) {
     fm_crt_kernel<NM><<<grid, 256, 0, s>>>(res, chunks, m, n, rlo, clo, rspan, cspan, flags, e, f);
-}
-
-#define FM_EVEN_COUNTS(X) X(2) X(4) X(6) X(8) X(10) X(12) X(14) X(16) X(18) X(20) X(22) X(24) \
-    X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40)
-
-// Host side: the smallest even prefix of the moduli whose product exceeds 2 (1 + 2^-10) k
-// (2^sa - 1)(2^sb - 1), and the CRT constants. Returns false when 40 moduli are not enough.
-namespace {
-struct HBig {
-    uint32_t l[FM_LIMBS + 2];
-};
-void hb_set(HBig& x, uint32_t v) {
-    for (auto& q : x.l) q = 0;
-    x.l[0] = v;
-}
-void hb_mul(HBig& x, uint32_t v) {
-    uint64_t c = 0;
-    for (auto& q : x.l) {
-        const uint64_t t = static_cast<uint64_t>(q) * v + c;
-        q = static_cast<uint32_t>(t);
-        c = t >> 32;
-    }
-}
-uint32_t hb_div(HBig& x, uint32_t v) {  // x /= v, returns the remainder
-    uint64_t r = 0;
-    for (int i = FM_LIMBS + 1; i >= 0; --i) {
-        const uint64_t cur = (r << 32) | x.l[i];
-        x.l[i] = static_cast<uint32_t>(cur / v);
-        r = cur % v;
-    }
-    return static_cast<uint32_t>(r);
-}
-void hb_shl1_sub1(HBig& x, int bits) {  // x := 2^bits - 1
-    for (auto& q : x.l) q = 0;
-    for (int b = 0; b < bits; ++b) x.l[b >> 5] |= 1u << (b & 31);
-}
-void hb_mul_big(HBig& x, const HBig& y) {
-    HBig r{};
-    for (int i = 0; i < FM_LIMBS + 2; ++i) {
-        uint64_t c = 0;
-        for (int j = 0; i + j < FM_LIMBS + 2; ++j) {
-            const uint64_t t = static_cast<uint64_t>(x.l[i]) * y.l[j] + r.l[i + j] + c;
-            r.l[i + j] = static_cast<uint32_t>(t);
-            c = t >> 32;
-        }
-    }
-    x = r;
-}
-bool hb_less(const HBig& x, const HBig& y) {
-    for (int i = FM_LIMBS + 1; i >= 0; --i)
-        if (x.l[i] != y.l[i]) return x.l[i] < y.l[i];
-    return false;
-}
-uint32_t inv_mod(uint32_t a, uint32_t p) {
-    int64_t t = 0, nt = 1, r = p, nr = a % p;
-    while (nr) {
-        const int64_t q = r / nr;
-        const int64_t tt = t - q * nt;
-        t = nt, nt = tt;
-        const int64_t rr = r - q * nr;
-        r = nr, nr = rr;
-    }
-    return static_cast<uint32_t>(t < 0 ? t + p : t);
-}
-}  // namespace
-
-static bool fm_plan(int span_a, int span_b, size_t k, FmParams& f) {
-    if (span_a <= 0 || span_b <= 0 || span_a + span_b > 280) return false;
-    // need := 2 (1 + 2^-20) k (2^sa - 1)(2^sb - 1), rounded up through 2^20 scaling
-    HBig need, y;
-    hb_shl1_sub1(need, span_a);
-    hb_shl1_sub1(y, span_b);
-    hb_mul_big(need, y);
-    hb_mul(need, static_cast<uint32_t>(k > 0xFFFFFFFFull ? 0xFFFFFFFFull : k));
-    if (k > 0xFFFFFFFFull) return false;
-    hb_mul(need, (1u << 10) + 1);  // compare M 2^10 > need
-    hb_mul(need, 2);
-    HBig M;
-    hb_set(M, 1);
-    int nm = 0;
-    for (; nm < FM_MAX; ++nm) {
-        HBig scaled = M;
-        hb_mul(scaled, 1u << 10);
-        if (hb_less(need, scaled)) break;
-        hb_mul(M, kFmModuli[nm]);
-    }
-    {
-        HBig scaled = M;
-        hb_mul(scaled, 1u << 10);
-        if (!hb_less(need, scaled)) return false;
-    }
-    if (nm & 1) {  // the kernels come in even moduli counts
-        if (nm == FM_MAX) return false;
-        hb_mul(M, kFmModuli[nm++]);
-    }
-    f = FmParams{};
-    f.nm = nm;
-    auto byte_of = [](const HBig& x, int b) {
-        return static_cast<uint32_t>((x.l[b >> 2] >> (8 * (b & 3))) & 255u);
-    };
-    for (int b = 0; b < nm; ++b) f.mmd[b] = static_cast<uint8_t>(byte_of(M, b));
-    for (int g = 0; g < nm; ++g) {
-        const uint32_t p = kFmModuli[g];
-        HBig mg = M;
-        hb_div(mg, p);
-        HBig t = mg;
-        const uint32_t mgmod = hb_div(t, p);
-        f.p[g] = static_cast<uint16_t>(p);
-        f.inv[g] = static_cast<uint16_t>(inv_mod(mgmod, p));
-        f.magic32[g] = static_cast<uint32_t>(((1ull << 32) + p - 1) / p);
-        for (int b = 0; b < nm; ++b) f.md[g / 4][b] |= byte_of(mg, b) << (8 * (g % 4));
-    }
-    return true;
 }
 
 // ------------------------------------------------------------ direct route
@@ -1605,7 +1406,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
 
     // ---- modular route: nm int8 GEMMs and the CRT
     FmParams fm;
-    const bool mod_ok = !digits_only && k > 0 && g[0] > 0 && g[1] > 0 && fm_plan(g[0], g[1], k, fm) &&
+    const bool mod_ok = !digits_only && k > 0 && g[0] > 0 && g[1] > 0 && fm_plan_spans(g[0], g[1], k, fm) &&
                         (size_t)((g[0] > g[1] ? g[0] : g[1]) + 1) * ((fm.nm + 3) / 4 * 4) * 4 *
                                 (e64 ? 2 : 1) <= FM_TABLE_MAX;
     auto run_modular = [&]() -> int {

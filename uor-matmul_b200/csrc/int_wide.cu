@@ -17,6 +17,7 @@
 #include "int_gemm.h"
 #include "aux.cuh"
 #include "gemm_slices.cuh"
+#include "modular.cuh"
 #include "ptx.cuh"
 
 namespace uor {
@@ -219,6 +220,35 @@ struct WideEpi {
     int cplx;    // 1: C is Complex<O>; real column j is part j & 1 of complex column j >> 1
 };
 
+// The exact accumulator of cell idx (row-major over m x n) through the Linear epilogue
+// (epilogue.rs:79-93) in the element's own accumulator, encoded and stored.
+__device__ __forceinline__ void wide_finish(const WideEpi& e, const L3& acc, size_t idx, size_t n,
+                                            void* c, int64_t rsc, int64_t csc) {
+    const size_t i = idx / n, j = idx - (idx / n) * n;
+    const int64_t off =
+        e.cplx ? 2 * (static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j >> 1) * csc) +
+                     static_cast<int64_t>(j & 1)
+               : static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j) * csc;
+    const LinearEpi& L = e.lin;
+    i128 outv;
+    if (e.limbs3) {
+        L3 tot = L.alpha == 1 ? acc : l3_scale(acc, L.alpha);
+        if (L.beta != 0) {
+            const L3 pr = l3_scale(l3_of(load_out(c, L.kind, off)), L.beta);
+            l3_add(tot, pr);
+        }
+        outv = l3_encode(tot, out_bits(L.kind), L.mode);
+    } else {
+        const i128 a = static_cast<i128>((static_cast<u128>(acc.w[1]) << 64) | acc.w[0]);
+        i128 tot = L.alpha == 1 ? a : sat_mul(a, L.alpha);
+        if (L.beta != 0)
+            tot = static_cast<i128>(static_cast<u128>(tot) +
+                                    static_cast<u128>(sat_mul(load_out(c, L.kind, off), L.beta)));
+        outv = encode_int(tot, out_bits(L.kind), L.mode);
+    }
+    store_out(c, L.kind, off, outv);
+}
+
 // Group g is the diagonal d = g, weighted 2^(8 g). The partials of a cell are summed
 // in 128-bit column sums per 64-bit word (chunk by chunk, every load of a chunk issued
 // before any is used) and carried into 192-bit two's complement.
@@ -257,31 +287,150 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
                 acc.w[2] = carry < 0 ? ~0ull : 0ull;
             }
         }
-        const size_t i = idx / n, j = idx - (idx / n) * n;
-        const int64_t off =
-            e.cplx ? 2 * (static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j >> 1) * csc) +
-                         static_cast<int64_t>(j & 1)
-                   : static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j) * csc;
-        const LinearEpi& L = e.lin;
-        i128 outv;
-        if (e.limbs3) {
-            L3 tot = L.alpha == 1 ? acc : l3_scale(acc, L.alpha);
-            if (L.beta != 0) {
-                const L3 pr = l3_scale(l3_of(load_out(c, L.kind, off)), L.beta);
-                l3_add(tot, pr);
-            }
-            outv = l3_encode(tot, out_bits(L.kind), L.mode);
-        } else {
-            const i128 a = static_cast<i128>((static_cast<u128>(acc.w[1]) << 64) | acc.w[0]);
-            i128 tot = L.alpha == 1 ? a : sat_mul(a, L.alpha);
-            if (L.beta != 0)
-                tot = static_cast<i128>(static_cast<u128>(tot) +
-                                        static_cast<u128>(sat_mul(load_out(c, L.kind, off), L.beta)));
-            outv = encode_int(tot, out_bits(L.kind), L.mode);
-        }
-        store_out(c, L.kind, off, outv);
+        wide_finish(e, acc, idx, n, c, rsc, csc);
     }
 }
+
+// ------------------------------------------------------------ modular route
+//
+// The modular route (modular.cuh) for i32 / i64 elements: every element is an integer of
+// 8 EB bits, |S| <= k 2^(16 EB - 2), and nm coprime moduli cover twice that; one int8
+// GEMM per modulus replaces the L^2 byte-slice pairs whenever nm is smaller (10 moduli
+// against 16 pairs for i32 at k = 65536, 20 against 64 for i64).
+
+// Weights of an EB-byte two's-complement value's bytes modulo p_g.
+struct WmWeights {
+    uint32_t w0[FM_MAX];   // bytes i of 256^i mod p_g, i < 4
+    uint32_t w1[FM_MAX];   // bytes i - 4 of 256^i mod p_g, 4 <= i < 8
+    uint32_t neg[FM_MAX];  // p_g - (2^(8 EB) mod p_g): adds -2^(8 EB) modulo p_g
+};
+
+// A value (< 2^24) congruent modulo p_g to the signed EB-byte integer whose bytes are v.
+template <int EB>
+__device__ __forceinline__ uint32_t wm_congruent(uint64_t v, int g, const WmWeights& w) {
+    uint32_t u = __dp4a(static_cast<uint32_t>(v), w.w0[g], 0u);
+    if (EB == 8) u = __dp4a(static_cast<uint32_t>(v >> 32), w.w1[g], u);
+    if ((v >> (8 * EB - 1)) & 1) u += w.neg[g];
+    return u;
+}
+
+template <int EB, int NM>
+__device__ __forceinline__ void wm_store(int8_t* dst, int64_t plane, const uint64_t (&v)[4],
+                                         const FmParams& f, const WmWeights& w) {
+#pragma unroll
+    for (int g = 0; g < NM; ++g) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            word |= fm_balanced(wm_congruent<EB>(v[c], g, w), 0u, f.p[g], f.magic32[g]) << (8 * c);
+        *reinterpret_cast<uint32_t*>(dst + g * plane) = word;
+    }
+}
+
+// A (m x k, EB-byte elements) -> residue planes As[NM][mp][kp], four reduction positions
+// per thread (the complex real image as slice_a_kernel reads it).
+template <int EB, int NM>
+__global__ void wm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp,
+                                  const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
+                                  bool aligned, int m, int k, bool cplx, FmParams f, WmWeights w) {
+    const int qpr = kp >> 2;
+    const int64_t total = static_cast<int64_t>(mp) * qpr;
+    const int64_t plane = static_cast<int64_t>(mp) * kp;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int i = static_cast<int>(t / qpr);
+        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+        uint64_t v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int p = p0 + c;
+            v[c] = (i < m && p < k) ? load_elem<EB>(a, cplx_a_index(i, p, rsa, csa, cplx), aligned) : 0;
+        }
+        wm_store<EB, NM>(as + static_cast<int64_t>(i) * kp + p0, plane, v, f, w);
+    }
+}
+
+// B (k x n) -> residue planes Bs[NM][np][kp] (transposed) through a shared tile of 128
+// reduction positions x 32 columns, the complex real image as slice_b_kernel builds it.
+template <int EB, int NM>
+__global__ void wm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp,
+                                  const uint8_t* __restrict__ b, int64_t rsb, int64_t csb,
+                                  bool aligned, int k, int n, bool cplx, FmParams f, WmWeights w) {
+    constexpr uint64_t mask = EB == 8 ? ~0ull : (1ull << (8 * EB)) - 1;
+    __shared__ uint64_t tile[32][129];
+    const int j0 = blockIdx.x * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    const int64_t plane = static_cast<int64_t>(np) * kp;
+    for (int p0 = blockIdx.y * 128; p0 < kp; p0 += gridDim.y * 128) {
+        for (int r = ty; r < 128; r += 8) {
+            const int p = p0 + r, j = j0 + tx;
+            uint64_t v = 0;
+            if (p < k && j < n) {
+                if (cplx) {
+                    const int64_t e = static_cast<int64_t>(p >> 1) * rsb + static_cast<int64_t>(j >> 1) * csb;
+                    v = load_elem<EB>(b, 2 * e + ((p ^ j) & 1), aligned);
+                    if ((p & 1) && !(j & 1)) v = (0ull - v) & mask;
+                } else {
+                    v = load_elem<EB>(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb,
+                                      aligned);
+                }
+            }
+            tile[tx][r] = v;
+        }
+        __syncthreads();
+        const int p = p0 + 4 * tx;
+#pragma unroll 1
+        for (int q = 0; q < 4; ++q) {
+            const int jj = ty * 4 + q, j = j0 + jj;
+            if (j < np && p < kp) {
+                const uint64_t v[4] = {tile[jj][4 * tx], tile[jj][4 * tx + 1], tile[jj][4 * tx + 2],
+                                       tile[jj][4 * tx + 3]};
+                wm_store<EB, NM>(bs + static_cast<int64_t>(j) * kp + p, plane, v, f, w);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// One thread per cell: y, the CRT value, and the element's Linear epilogue and encode.
+template <int NM>
+__global__ void wm_crt_kernel(const uint8_t* __restrict__ res, int chunks, size_t m, size_t n,
+                              void* c, int64_t rsc, int64_t csc, WideEpi e, FmParams f) {
+    constexpr int NL = FmLimbs<NM>::value;
+    const size_t total = m * n;
+    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        uint32_t y[NM];
+        fm_load_y<NM>(res, chunks, total, idx, f, y);
+        uint32_t limb[NL];
+        const uint32_t ext = fm_crt<NM>(y, f, limb);
+        L3 acc;
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+            const uint64_t lo = 2 * q < NL ? limb[2 * q] : ext;
+            const uint64_t hi = 2 * q + 1 < NL ? limb[2 * q + 1] : ext;
+            acc.w[q] = lo | hi << 32;
+        }
+        wide_finish(e, acc, idx, n, c, rsc, csc);
+    }
+}
+
+template <int EB, int NM>
+static void wm_launch(int8_t* as, int mp, int8_t* bs, int np, int kp, const uint8_t* a,
+                      int64_t rsa, int64_t csa, const uint8_t* b, int64_t rsb, int64_t csb, int m,
+                      int k, int n, bool cplx, const FmParams& f, const WmWeights& w,
+                      cudaStream_t s) {
+    const int64_t quads = static_cast<int64_t>(mp) * (kp / 4);
+    const int grid = static_cast<int>(quads / 256 + 1 < 148 * 16 ? quads / 256 + 1 : 148 * 16);
+    wm_slice_a_kernel<EB, NM><<<grid, 256, 0, s>>>(as, mp, kp, a, rsa, csa,
+                                                   reinterpret_cast<uintptr_t>(a) % EB == 0, m, k,
+                                                   cplx, f, w);
+    const int gy = (kp + 127) / 128 < 65535 ? (kp + 127) / 128 : 65535;
+    wm_slice_b_kernel<EB, NM><<<dim3(np / 32, gy), dim3(32, 8), 0, s>>>(
+        bs, np, kp, b, rsb, csb, reinterpret_cast<uintptr_t>(b) % EB == 0, k, n, cplx, f, w);
+}
+
+#define WM_COUNTS(X) X(8) X(10) X(12) X(14) X(16) X(18) X(20) X(22) X(24)
 
 // ------------------------------------------------------------ driver
 
@@ -301,7 +450,7 @@ static void launch_wide_reduce(const int32_t* part, int chunks, int groups, size
 int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
                   const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc,
                   ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
-                  uor_b200_route* route, bool cplx) {
+                  uor_b200_route* route, bool cplx, bool digits_only) {
     cudaStream_t s = ctx->stream;
     if (route) {
         *route = uor_b200_route{};
@@ -351,6 +500,98 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
     }
     p.pair_begin[ngroups] = npairs;
     p.num_groups = ngroups;
+
+    // The modular route when it runs fewer GEMMs than the byte-slice pairs.
+    FmParams fm;
+    if (!digits_only && (eb == 4 || eb == 8) && fm_plan_ints(8 * eb, k, fm) && fm.nm >= 8 &&
+        fm.nm <= 24 && fm.nm < npairs) {
+        const int nm = fm.nm;
+        KSParams q{};
+        q.num_groups = nm;
+        for (int g = 0; g < nm; ++g) {
+            q.pair_begin[g] = g;
+            q.pair_a[g] = q.pair_b[g] = static_cast<uint8_t>(g);
+            q.pair_sign[g] = 3;
+            q.res_mod[g] = fm.p[g];
+            q.res_magic[g] = fm.magic32[g];
+            q.res_off[g] = static_cast<uint32_t>(fm.p[g] * ((0x80000000ull + fm.p[g] - 1) / fm.p[g]));
+        }
+        q.pair_begin[nm] = nm;
+        const int num_kb = static_cast<int>((k + KS_BK - 1) / KS_BK);
+        // |residue product| <= 2^14: 1023 blocks keep |acc| < 2^31 - 2^21
+        const int64_t lane_m = (int64_t)INT_MAX / 16384 / KS_BK;
+        q.kb_per_chunk = static_cast<int>(lane_m < num_kb ? lane_m : num_kb);
+        q.num_chunks = (num_kb + q.kb_per_chunk - 1) / q.kb_per_chunk;
+        q.num_kb = num_kb;
+        if (q.num_chunks == 1)
+            for (int g = 0; g < nm; ++g) q.res_inv[g] = fm.inv[g];
+        q.m = static_cast<int>(m);
+        q.n = static_cast<int>(n);
+        q.mp = static_cast<int>(ks_rows_pad(m));
+        q.np = static_cast<int>(rup(n, KS_BN));
+        q.status = ctx->d_status;
+        q.budget_ns = ctx->budget_ns;
+        WmWeights w{};
+        for (int g = 0; g < nm; ++g) {
+            const uint32_t pg = fm.p[g];
+            uint32_t c = 1 % pg;
+            for (int i = 0; i < 8; ++i) {
+                (i < 4 ? w.w0[g] : w.w1[g]) |= c << (8 * (i & 3));
+                c = c * 256 % pg;
+            }
+            w.neg[g] = (pg - c % pg) % pg;  // c = 256^8 mod p here; EB < 8 recomputed below
+            if (eb == 4) {
+                uint32_t c4 = 1 % pg;
+                for (int i = 0; i < 4; ++i) c4 = c4 * 256 % pg;
+                w.neg[g] = (pg - c4) % pg;
+            }
+        }
+        const size_t kp = rup(k, 16);
+        const size_t a_bytes = rup((size_t)nm * q.mp * kp, 256);
+        const size_t b_bytes = rup((size_t)nm * q.np * kp, 256);
+        const size_t res_bytes = rup((size_t)q.num_chunks * nm * m * n, 256);
+        int st = UOR_B200_OK;
+        uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, a_bytes + b_bytes + res_bytes, &st));
+        if (!ws) return st;
+        int8_t* as = reinterpret_cast<int8_t*>(ws);
+        int8_t* bs = reinterpret_cast<int8_t*>(ws + a_bytes);
+        uint8_t* res = ws + a_bytes + b_bytes;
+        switch (eb * 100 + nm) {
+#define WM_SLICE4(N) \
+    case 400 + N: wm_launch<4, N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, fm, w, s); break;
+#define WM_SLICE8(N) \
+    case 800 + N: wm_launch<8, N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, fm, w, s); break;
+            WM_COUNTS(WM_SLICE4)
+            WM_COUNTS(WM_SLICE8)
+#undef WM_SLICE4
+#undef WM_SLICE8
+        default: return UOR_B200_UNSUPPORTED;
+        }
+        if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        q.residue = res;
+        if (route) {
+            route->kernel = UOR_B200_KERNEL_LIMB_TCGEN05;
+            route->k_chunks = static_cast<uint32_t>(q.num_chunks);
+            route->pairs = static_cast<uint32_t>(nm);
+            route->moduli = static_cast<uint32_t>(nm);
+        }
+        if ((st = ks_run(as, nm, bs, nm, k, kp, q, ctx->sm_count, s, route ? &route->ctas : nullptr)) !=
+            UOR_B200_OK)
+            return st;
+        if (route) route->tile_m = static_cast<uint32_t>(q.m > 128 ? 256 : KS_BM);
+        const WideEpi we{epi, eb == 8 ? 1 : 0, cplx ? 1 : 0};
+        const size_t total = m * n;
+        const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+        switch (nm) {
+#define WM_CRT(N) \
+    case N: wm_crt_kernel<N><<<rgrid, 256, 0, s>>>(res, q.num_chunks, m, n, c, rsc, csc, we, fm); break;
+            WM_COUNTS(WM_CRT)
+#undef WM_CRT
+        default: return UOR_B200_UNSUPPORTED;
+        }
+        return cuda_status(cudaGetLastError());
+    }
+
     // The longest reduction a diagonal's s32 lane holds exactly, in whole blocks.
     const int64_t lane = (static_cast<int64_t>(INT_MAX) / worst) / KS_BK;
     const int num_kb = static_cast<int>((k + KS_BK - 1) / KS_BK);

@@ -1,0 +1,132 @@
+// modular.cuh -- exact integer products through residues modulo small coprime moduli,
+// the integer core of Ozaki scheme II (Ozaki, Uchino and Imamura, "Ozaki Scheme II: A
+// GEMM-oriented emulation of floating-point matrix multiplication using an integer
+// modular technique", 2025), shared by the exact float and the wide-integer paths.
+//
+// Integer operands are reduced modulo nm pairwise coprime moduli p_g <= 256 into balanced
+// residues, which are int8; one int8 GEMM per modulus on the tensor cores gives S mod p_g
+// exactly (the slice-pair kernel reduces its s32 accumulator in the epilogue, and with one
+// reduction chunk stores y_g = r_g (M / p_g)^-1 mod p_g directly); the Chinese remainder
+// theorem then rebuilds each cell's exact integer S. M = prod p_g is chosen above
+// 2 (1 + 2^-10) times a bound on |S|, so S is the representative of X = sum_g y_g M / p_g
+// nearest to zero: S = X - t M with t the integer nearest X / M = sum_g y_g / p_g. X / M
+// lies within 1/2 - 2^-11 of t, and the 32-bit fixed-point sum sum_g y_g ceil(2^32 / p_g)
+// overshoots X / M 2^32 by less than 40 * 255 (2^-18.6 after scaling), so rounding it
+// finds t. X is summed in base-256 columns, X_b = sum_g y_g byte_b(M / p_g), four moduli
+// per dp4a, and carried into signed 32-bit limbs.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace uor {
+
+constexpr int FM_MAX = 40;  // moduli (the 40 moduli's product is 291 bits)
+
+struct FmParams {
+    int nm;                           // moduli (even)
+    uint16_t p[FM_MAX];
+    uint16_t inv[FM_MAX];             // (M / p_g)^-1 mod p_g
+    uint32_t magic32[FM_MAX];         // ceil(2^32 / p_g)
+    uint32_t md[FM_MAX / 4][FM_MAX];  // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
+    uint8_t mmd[FM_MAX];              // byte b of M (M < 2^(8 nm))
+};
+
+// The smallest even prefix of the moduli (256, 255, 253, 251, 247 and primes) whose
+// product M exceeds 2 (1 + 2^-10) bound, and the CRT constants; bound is a little-endian
+// array of 32-bit limbs. False when 40 moduli are not enough.
+bool fm_plan_bound(const uint32_t* bound, int limbs, FmParams& f);
+// bound = k (2^sa - 1)(2^sb - 1): products of integers below 2^sa and 2^sb in magnitude.
+bool fm_plan_spans(int span_a, int span_b, size_t k, FmParams& f);
+// bound = k 2^(2 bits - 2): products of two's-complement integers of `bits` bits.
+bool fm_plan_ints(int bits, size_t k, FmParams& f);
+
+// x mod p for x < 2^24: floor(x ceil(2^32 / p) / 2^32) is exact there (the error term
+// x (ceil(2^32/p) - 2^32/p) / 2^32 < 2^-8 never reaches the next multiple).
+__device__ __forceinline__ uint32_t fm_mod24(uint32_t x, uint32_t p, uint32_t magic32) {
+    return x - __umulhi(x, magic32) * p;
+}
+
+// The balanced residue byte of a value congruent to u (< 2^24) modulo p, negated when
+// nmask is all ones: in [-(p-1)/2, (p-1)/2] for odd p, [-128, 127] for 256 (where -(-128)
+// is the same byte 128 modulo 256).
+__device__ __forceinline__ uint32_t fm_balanced(uint32_t u, uint32_t nmask, uint32_t p,
+                                                uint32_t magic32) {
+    const uint32_t r = fm_mod24(u, p, magic32);
+    const uint32_t b = r >= (p + 1) / 2 ? r - p : r;
+    return ((b ^ nmask) - nmask) & 255u;
+}
+
+// y_g of one cell from the residue planes res[chunk][g][total] (idx the cell): the
+// epilogue's y_g with one chunk, else rebuilt from the chunks' residues.
+template <int NM>
+__device__ __forceinline__ void fm_load_y(const uint8_t* __restrict__ res, int chunks, size_t total,
+                                          size_t idx, const FmParams& f, uint32_t (&y)[NM]) {
+    if (chunks == 1) {
+#pragma unroll
+        for (int g = 0; g < NM; ++g) y[g] = __ldg(res + g * total + idx);
+        return;
+    }
+#pragma unroll
+    for (int g = 0; g < NM; ++g) y[g] = 0;
+    for (int q = 0; q < chunks; ++q) {
+#pragma unroll
+        for (int g = 0; g < NM; ++g) y[g] += __ldg(res + (static_cast<size_t>(q) * NM + g) * total + idx);
+    }
+#pragma unroll
+    for (int g = 0; g < NM; ++g)
+        y[g] = fm_mod24(fm_mod24(y[g], f.p[g], f.magic32[g]) * f.inv[g], f.p[g], f.magic32[g]);
+}
+
+// 32-bit limbs of |S| < M / 2 < 2^(8 NM - 1), one spare for the sign.
+template <int NM>
+struct FmLimbs {
+    static constexpr int value = (NM + 1 + 3) / 4;
+};
+
+// S from y (two's complement limbs, least significant first); returns the sign extension
+// (0 or ~0) of the limbs above.
+template <int NM>
+__device__ __forceinline__ uint32_t fm_crt(const uint32_t (&y)[NM], const FmParams& f,
+                                           uint32_t (&limb)[FmLimbs<NM>::value]) {
+    constexpr int NA = (NM + 3) / 4;  // packed words of y
+    constexpr int NL = FmLimbs<NM>::value;
+    uint64_t fx = 0x80000000ull;  // + 1/2 in the 32-bit fixed point
+    uint32_t ya[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+        ya[a] = 0;
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+            if (4 * a + gi < NM) {
+                ya[a] |= y[4 * a + gi] << (8 * gi);
+                fx += static_cast<uint64_t>(y[4 * a + gi]) * f.magic32[4 * a + gi];
+            }
+        }
+    }
+    const int32_t t = static_cast<int32_t>(fx >> 32);
+    // Columns X_b - t M_b, each below NM 255^2 < 2^22 in magnitude.
+    int64_t carry = 0;
+#pragma unroll
+    for (int l = 0; l < NL; ++l) {
+        int64_t v = carry;
+#pragma unroll
+        for (int bi = 0; bi < 4; ++bi) {
+            const int b = 4 * l + bi;
+            if (b < NM) {
+                uint32_t col = 0;
+#pragma unroll
+                for (int a = 0; a < NA; ++a) col = __dp4a(ya[a], f.md[a][b], col);
+                v += (static_cast<int64_t>(col) - static_cast<int64_t>(t) * f.mmd[b]) << (8 * bi);
+            }
+        }
+        limb[l] = static_cast<uint32_t>(v);
+        carry = v >> 32;
+    }
+    return carry < 0 ? ~0u : 0u;
+}
+
+#define FM_EVEN_COUNTS(X) X(2) X(4) X(6) X(8) X(10) X(12) X(14) X(16) X(18) X(20) X(22) X(24) \
+    X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40)
+
+}  // namespace uor

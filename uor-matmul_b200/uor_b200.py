@@ -23,7 +23,7 @@ OK, NONCONFORMANT, OUTPUT_ALIASES, DEVICE_ERROR, TIMEOUT, NCCL_ERROR, DOES_NOT_F
     INVALID_ARGUMENT, UNSUPPORTED = range(9)
 NEAREST, TOWARD_ZERO, SATURATING, WRAPPING = range(4)
 I8, I16, I32, I64, I128, F32, F64, TROP_I8, TROP_I16, TROP_I32, TROP_I64 = range(1, 12)
-DEVICE_POINTERS, ASYNC, FLOAT_DIGITS = 1, 2, 4
+DEVICE_POINTERS, ASYNC, DIGIT_SLICES = 1, 2, 4
 KERNEL_NAMES = {0: "none", 1: "i8_tcgen05", 2: "limb_tcgen05", 3: "tropical",
                 4: "coded_tcgen05", 5: "float_exact", 6: "epilogue_only", 7: "skinny_dp4a"}
 
@@ -238,11 +238,14 @@ def _on_device(*bufs):
 # ------------------------------------------------------------------ integer
 
 def gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None, route=None,
-         asynchronous=False):
-    """uor_matmul::gemm over views: av/bv/cv are (rows, cols, rs, cs) tuples over buffers a/b/c."""
+         asynchronous=False, digits=False):
+    """uor_matmul::gemm over views: av/bv/cv are (rows, cols, rs, cs) tuples over buffers a/b/c.
+    digits=True keeps wide elements on the byte-slice route (the same bytes)."""
     dev = _on_device(a, b, c)
     A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
     call = make_call(encode, dev, ctx, route, asynchronous)
+    if digits:
+        call.flags |= DIGIT_SLICES
     _check(lib().uor_b200_gemm(elem, out, ctypes.byref(A), ctypes.byref(B), ctypes.byref(C),
                                alpha, beta, ctypes.byref(call)), "gemm")
 
@@ -255,7 +258,7 @@ def complex_view(buf, rows, cols, rs=None, cs=1):
 
 
 def gemm_complex(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None,
-                 route=None, asynchronous=False):
+                 route=None, asynchronous=False, digits=False):
     """driver::gemm over Complex<elem> (alphabet.rs:656-776) into Complex<out>.
 
     elem in {I32, I64} and out in {I8 .. I128} name the part types; a, b, c are flat
@@ -265,6 +268,8 @@ def gemm_complex(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST
     dev = _on_device(a, b, c)
     A, B, C = complex_view(a, *av), complex_view(b, *bv), complex_view(c, *cv)
     call = make_call(encode, dev, ctx, route, asynchronous)
+    if digits:
+        call.flags |= DIGIT_SLICES
     _check(lib().uor_b200_gemm_complex(elem, out, ctypes.byref(A), ctypes.byref(B),
                                        ctypes.byref(C), alpha, beta, ctypes.byref(call)),
            "gemm_complex")
@@ -312,7 +317,7 @@ def gemm_float(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, 
     A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
     call = make_call(encode, dev, ctx, route, asynchronous)
     if digits:
-        call.flags |= FLOAT_DIGITS
+        call.flags |= DIGIT_SLICES
     _check(lib().uor_b200_gemm_float(elem, out, ctypes.byref(A), ctypes.byref(B),
                                      ctypes.byref(C), alpha, beta, ctypes.byref(call)),
            "gemm_float")
