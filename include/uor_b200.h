@@ -124,13 +124,16 @@ typedef struct uor_b200_route {
  * even where the modular route (residues modulo coprime moduli and the CRT) would run
  * fewer GEMMs. Both are exact; the bytes are the same. */
 #define UOR_B200_DIGIT_SLICES 4u
+/* Exact float and wide integers: take the modular route wherever its moduli cover the
+ * product's bound, whatever the estimated cost. Exact; the same bytes. */
+#define UOR_B200_MODULAR 8u
 
 /* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)
  * plus where the pointers live. A NULL call means: Nearest, host pointers,
  * the default context of the current device. */
 typedef struct uor_b200_call {
     uint32_t encode;        /* uor_b200_encode */
-    uint32_t flags;         /* UOR_B200_DEVICE_POINTERS | UOR_B200_ASYNC | UOR_B200_DIGIT_SLICES */
+    uint32_t flags;         /* DEVICE_POINTERS | ASYNC | DIGIT_SLICES | MODULAR */
     uor_b200_ctx *ctx;      /* NULL: the current device's default context */
     uor_b200_route *route;  /* optional out */
 } uor_b200_call;

@@ -48,7 +48,7 @@ def test_random_full_range(bits, out, digits):
             got, want = c0.copy(), c0.copy()
             route = U.Route()
             U.gemm_complex(ELEM[bits], out, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1),
-                           alpha, beta, mode, route=route, digits=digits)
+                           alpha, beta, mode, route=route, digits=digits, modular=not digits)
             oracle(a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), alpha, beta, mode, out)
             assert same(got, want, out), (m, k, n, alpha, beta, mode)
             assert route.kernel == 2  # the limb (byte-sliced) path
@@ -98,7 +98,7 @@ def test_deep_reduction_several_chunks(digits):
     got, want = out_array(U.I128, 2 * m * n), out_array(U.I128, 2 * m * n)
     route = U.Route()
     U.gemm_complex(U.I32, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1),
-                   route=route, digits=digits)
+                   route=route, digits=digits, modular=not digits)
     oracle(a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), 1, 0, U.NEAREST, U.I128)
     assert same(got, want, U.I128)
     assert route.k_chunks >= 2 if digits else route.moduli > 0

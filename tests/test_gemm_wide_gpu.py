@@ -43,12 +43,12 @@ def rand_full(rng, bits, count):
     return rng.integers(info.min, info.max, size=count, endpoint=True).astype(NP[bits])
 
 
-@pytest.mark.parametrize("digits", [False, True])
+@pytest.mark.parametrize("path", ["auto", "digits", "modular"])
 @pytest.mark.parametrize("bits", [16, 32, 64])
 @pytest.mark.parametrize("out", [U.I32, U.I64, U.I128])
-def test_random_full_range(bits, out, digits):
-    """i16 always, and i32 / i64 with digits=True, on the byte-slice pairs; i32 / i64
-    otherwise on the modular route (residue GEMMs and the CRT)."""
+def test_random_full_range(bits, out, path):
+    """The byte-slice pairs (forced, and for i16 always), the modular route (residue GEMMs
+    and the CRT, forced for i32 / i64) and the library's own choice."""
     rng = np.random.default_rng(bits * 10 + out)
     for (m, k, n) in [(1, 1, 1), (13, 17, 19), (130, 300, 270), (300, 200, 261)]:
         a, b = rand_full(rng, bits, m * k), rand_full(rng, bits, k * n)
@@ -59,7 +59,7 @@ def test_random_full_range(bits, out, digits):
             got, want = c0.copy(), c0.copy()
             route = U.Route()
             U.gemm(ELEM[bits], out, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), alpha,
-                   beta, mode, route=route, digits=digits)
+                   beta, mode, route=route, digits=path == "digits", modular=path == "modular")
             oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), alpha, beta,
                        mode, out)
             if out == U.I128:
@@ -67,7 +67,10 @@ def test_random_full_range(bits, out, digits):
             else:
                 assert np.array_equal(got, want), (m, k, n, alpha, beta, mode)
             assert route.kernel == 2
-            assert (route.moduli > 0) == (bits > 16 and not digits), route.as_dict()
+            if path == "digits" or bits == 16:
+                assert route.moduli == 0, route.as_dict()
+            elif path == "modular":
+                assert route.moduli > 0, route.as_dict()
 
 
 @pytest.mark.parametrize("digits", [False, True])
@@ -81,7 +84,7 @@ def test_deep_i32_chunks_and_strides(digits):
     # B read as its own transpose: stored n x k
     bt = np.ascontiguousarray(b.reshape(k, n).T).reshape(-1)
     U.gemm(U.I32, U.I128, a, (m, k, k, 1), bt, (k, n, 1, k), got, (m, n, n, 1), route=route,
-           digits=digits)
+           digits=digits, modular=not digits)
     oracle_int(a, (m, k, k, 1, 0), bt, (k, n, 1, k, 0), want, (m, n, n, 1, 0), 1, 0, U.NEAREST,
                U.I128)
     assert i128_values(got) == i128_values(want)
@@ -97,7 +100,8 @@ def test_modular_two_chunks_and_i64_extremes():
     a, b = rand_full(rng, 32, m * k), rand_full(rng, 32, k * n)
     got, want = np.zeros(m * n * 2, np.int64), np.zeros(m * n * 2, np.int64)
     route = U.Route()
-    U.gemm(U.I32, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), route=route)
+    U.gemm(U.I32, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), route=route,
+           modular=True)
     oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), 1, 0, U.NEAREST,
                U.I128)
     assert i128_values(got) == i128_values(want)
@@ -110,7 +114,7 @@ def test_modular_two_chunks_and_i64_extremes():
         got, want = np.zeros(m * n * 2, np.int64), np.zeros(m * n * 2, np.int64)
         route = U.Route()
         U.gemm(U.I64, U.I128, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), 3, 0, mode,
-               route=route)
+               route=route, modular=True)
         oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), 3, 0, mode,
                    U.I128)
         assert i128_values(got) == i128_values(want), mode

@@ -31,7 +31,7 @@ int float_placed(uor_b200_dtype elem, uor_b200_dtype out, const Operand& A, cons
     if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs))) return st;
     st = run_float_gemm(ctx, elem == UOR_B200_F64, out == UOR_B200_F64, da, A.rs, A.cs, db, B.rs,
                         B.cs, cs.dev_origin, C.rs, C.cs, m, k, n, alpha, beta, mode, route,
-                        call && (call->flags & UOR_B200_DIGIT_SLICES));
+                        call ? call->flags & (UOR_B200_DIGIT_SLICES | UOR_B200_MODULAR) : 0u);
     if (st) return st;
     if ((st = stage_out_end(ctx, cs))) return st;
     if (!dev) return uor_b200_ctx_sync(ctx);

@@ -59,7 +59,7 @@ int int_gemm_locked(uor_b200_ctx* ctx, uor_b200_dtype elem, int kind, const Oper
     else
         st = run_wide_gemm(ctx, (int)dtype_size(elem), da, A.rs, A.cs, db, B.rs, B.cs,
                            cs.dev_origin, C.rs, C.cs, m, k, n, epi, route, cplx,
-                           call && (call->flags & UOR_B200_DIGIT_SLICES));
+                           call ? call->flags & (UOR_B200_DIGIT_SLICES | UOR_B200_MODULAR) : 0u);
     if (st != UOR_B200_OK) return st;
     if ((st = stage_out_end(ctx, cs)) != UOR_B200_OK) return st;
     if (!dev) return uor_b200_ctx_sync(ctx);

@@ -1020,15 +1020,18 @@ __device__ __forceinline__ void fm_store_residues(int8_t* dst, int64_t plane, co
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         if (!mant[c]) continue;
-        const uint32_t nmask = neg[c] ? ~0u : 0u;
         const uint32_t lo32 = static_cast<uint32_t>(mant[c]);
         const uint32_t hi32 = static_cast<uint32_t>(mant[c] >> 32);
-        const uint4* row = reinterpret_cast<const uint4*>(pw + sh[c] * W * NMP);
+        // rows 2 sh (positive) and 2 sh + 1 (the coefficients of -2^(sh + 8i))
+        const uint4* row = reinterpret_cast<const uint4*>(pw + (2 * sh[c] + (neg[c] ? 1 : 0)) * W * NMP);
 #pragma unroll
         for (int g4 = 0; g4 < NMP / 4; ++g4) {
             const uint4 cw = row[g4];
-            uint32_t u[4] = {__dp4a(lo32, cw.x, 0u), __dp4a(lo32, cw.y, 0u), __dp4a(lo32, cw.z, 0u),
-                             __dp4a(lo32, cw.w, 0u)};
+            const int gb = 4 * g4;
+            uint32_t u[4] = {__dp4a(lo32, cw.x, f.half[gb < NM ? gb : 0]),
+                             __dp4a(lo32, cw.y, f.half[gb + 1 < NM ? gb + 1 : 0]),
+                             __dp4a(lo32, cw.z, f.half[gb + 2 < NM ? gb + 2 : 0]),
+                             __dp4a(lo32, cw.w, f.half[gb + 3 < NM ? gb + 3 : 0])};
             if (W == 2) {
                 const uint4 ch = row[NMP / 4 + g4];
                 u[0] = __dp4a(hi32, ch.x, u[0]);
@@ -1039,7 +1042,7 @@ __device__ __forceinline__ void fm_store_residues(int8_t* dst, int64_t plane, co
 #pragma unroll
             for (int gi = 0; gi < 4; ++gi) {
                 const int g = 4 * g4 + gi;
-                if (g < NM) out[g] |= fm_balanced(u[gi], nmask, f.p[g], f.magic32[g]) << (8 * c);
+                if (g < NM) out[g] = fm_put_byte(out[g], fm_balanced(u[gi], f.p[g], f.magic32[g], f.half[g]), c);
             }
         }
     }
@@ -1057,7 +1060,7 @@ __global__ void fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const
     constexpr int NMP = (NM + 3) / 4 * 4;
     extern __shared__ __align__(16) uint32_t pw[];
     const int W = f64 ? 2 : 1;
-    fm_fill_pow2(pw, pow2, shmax * W * NMP);
+    fm_fill_pow2(pw, pow2, 2 * shmax * W * NMP);
     __syncthreads();
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
@@ -1094,7 +1097,7 @@ __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const
     __shared__ uint64_t tm[32][65];
     __shared__ int ts[32][65];
     const int W = f64 ? 2 : 1;
-    fm_fill_pow2(pw, pow2, shmax * W * NMP);
+    fm_fill_pow2(pw, pow2, 2 * shmax * W * NMP);
     const int j0 = blockIdx.x * 32;
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     const int64_t plane = static_cast<int64_t>(np) * kp;
@@ -1141,7 +1144,7 @@ __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const
 // carried into signed 32-bit limbs, then the fast encode (beta 0, finite terms) or
 // finish_float.
 template <int NM>
-__global__ void fm_crt_kernel(const uint8_t* __restrict__ res, int chunks, int m, int n,
+__global__ void __launch_bounds__(256, 4) fm_crt_kernel(const uint8_t* __restrict__ res, int chunks, int m, int n,
                               const int* __restrict__ rlo, const int* __restrict__ clo,
                               const int* __restrict__ rspan, const int* __restrict__ cspan,
                               const uint8_t* __restrict__ flags, FxEpi e, FmParams f) {
@@ -1191,7 +1194,7 @@ static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, con
                              bool f64, int m, int k, int n, const int* rlo, const int* clo,
                              const uint32_t* pw, int shmax, const FmParams& f, cudaStream_t s) {
     constexpr int NMP = (NM + 3) / 4 * 4;
-    const size_t smem = static_cast<size_t>(shmax) * NMP * 4 * (f64 ? 2 : 1);
+    const size_t smem = static_cast<size_t>(shmax) * 2 * NMP * 4 * (f64 ? 2 : 1);
     // The B kernel adds a 25 KB static tile: allow the table's largest size beside it.
     cudaFuncSetAttribute(fm_slice_a_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
     cudaFuncSetAttribute(fm_slice_b_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
@@ -1346,7 +1349,9 @@ constexpr int FX_MAX_DIGITS = 16;
 int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrdiff_t rsa,
                    ptrdiff_t csa, const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c,
                    ptrdiff_t rsc, ptrdiff_t csc, size_t m, size_t k, size_t n, int64_t alpha,
-                   int64_t beta, int mode, uor_b200_route* route, bool digits_only) {
+                   int64_t beta, int mode, uor_b200_route* route, uint32_t route_flags) {
+    const bool digits_only = (route_flags & UOR_B200_DIGIT_SLICES) != 0;
+    const bool force_modular = !digits_only && (route_flags & UOR_B200_MODULAR) != 0;
     cudaStream_t s = ctx->stream;
     if (route) *route = uor_b200_route{};
     if (m == 0 || n == 0) return UOR_B200_OK;
@@ -1407,7 +1412,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
     // ---- modular route: nm int8 GEMMs and the CRT
     FmParams fm;
     const bool mod_ok = !digits_only && k > 0 && g[0] > 0 && g[1] > 0 && fm_plan_spans(g[0], g[1], k, fm) &&
-                        (size_t)((g[0] > g[1] ? g[0] : g[1]) + 1) * ((fm.nm + 3) / 4 * 4) * 4 *
+                        (size_t)((g[0] > g[1] ? g[0] : g[1]) + 1) * 2 * ((fm.nm + 3) / 4 * 4) * 4 *
                                 (e64 ? 2 : 1) <= FM_TABLE_MAX;
     auto run_modular = [&]() -> int {
         const int nm = fm.nm;
@@ -1445,7 +1450,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         const size_t b_bytes = rup((size_t)nm * q.np * kp, 256);
         const size_t res_bytes = rup((size_t)q.num_chunks * nm * m * n, 256);
         const size_t flag_bytes = any_nf ? rup(m * n, 256) : 0;
-        const size_t pw_bytes = rup((size_t)nmp * shmax * W * 4, 256);
+        const size_t pw_bytes = rup((size_t)nmp * shmax * 2 * W * 4, 256);
         int st2 = UOR_B200_OK;
         uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(
             ctx, SLOT_WS, a_bytes + b_bytes + res_bytes + flag_bytes + pw_bytes + 256, &st2));
@@ -1456,15 +1461,17 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         uint8_t* flags = any_nf ? res + res_bytes : nullptr;
         uint32_t* pw = reinterpret_cast<uint32_t*>(res + res_bytes + flag_bytes);
         {
-            // row sh, word w, modulus g: bytes i of 2^(sh + 8 (4 w + i)) mod p_g
-            std::vector<uint32_t> tab((size_t)shmax * W * nmp, 0);
+            // row 2 sh + s, word w, modulus g: bytes i of (-1)^s 2^(sh + 8 (4 w + i)) mod p_g
+            std::vector<uint32_t> tab((size_t)shmax * 2 * W * nmp, 0);
             for (int gg = 0; gg < nm; ++gg) {
                 const uint32_t pg = fm.p[gg];
                 uint32_t v = 1 % pg;  // 2^sh mod p
                 for (int sh = 0; sh < shmax; ++sh) {
                     uint32_t c = v;
                     for (int bi = 0; bi < 4 * W; ++bi) {
-                        tab[((size_t)sh * W + bi / 4) * nmp + gg] |= c << (8 * (bi % 4));
+                        const uint32_t cn = (pg - c) % pg;
+                        tab[((size_t)(2 * sh) * W + bi / 4) * nmp + gg] |= c << (8 * (bi % 4));
+                        tab[((size_t)(2 * sh + 1) * W + bi / 4) * nmp + gg] |= cn << (8 * (bi % 4));
                         c = c * 256 % pg;
                     }
                     v = v * 2 % pg;
@@ -1561,7 +1568,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         // The modular route when it runs fewer GEMMs than the digit pairs would.
         int digit_pairs = 0;
         for (int d = D; d < G; ++d) digit_pairs += pairs_on(d);
-        if (fm.nm < digit_pairs) return run_modular();
+        if (force_modular || fm.nm < digit_pairs) return run_modular();
     }
 
     // ---- digit slices and the slice-pair product of diagonals d >= d_lo

@@ -20,10 +20,11 @@ struct FxEpi {
 
 // The exact float product: the modular route (Ozaki scheme II) where its moduli cover the
 // operands' exponent spans and it runs fewer GEMMs, else the digit-slice route, else the
-// direct route; digits_only skips the modular route.
+// direct route. route_flags: UOR_B200_DIGIT_SLICES skips the modular route,
+// UOR_B200_MODULAR takes it wherever the moduli cover the spans.
 int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrdiff_t rsa,
                    ptrdiff_t csa, const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c,
                    ptrdiff_t rsc, ptrdiff_t csc, size_t m, size_t k, size_t n, int64_t alpha,
-                   int64_t beta, int mode, uor_b200_route* route, bool digits_only = false);
+                   int64_t beta, int mode, uor_b200_route* route, uint32_t route_flags = 0);
 
 }  // namespace uor

@@ -16,13 +16,14 @@ int run_i8_gemm(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa
 
 // i16 / i32 / i64 GEMM (eb = element bytes): the modular route (residue GEMMs and the
 // CRT) where it runs fewer GEMMs, else byte slicing through the slice-pair kernel and an
-// exact recombination in the element's accumulator; digits_only keeps the byte slices. With `cplx` the
+// exact recombination in the element's accumulator. route_flags: UOR_B200_DIGIT_SLICES
+// keeps the byte slices, UOR_B200_MODULAR takes the modular route wherever it applies. With `cplx` the
 // operands and C are Complex<T> / Complex<O> (eb = bytes of one part; strides and
 // m, k, n in complex elements).
 int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
                   const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc,
                   ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
-                  uor_b200_route* route, bool cplx = false, bool digits_only = false);
+                  uor_b200_route* route, bool cplx = false, uint32_t route_flags = 0);
 
 // Products with at most 16 rows or columns (k > 0): dp4a kernels on CUDA cores that
 // keep every SM busy where a tensor-core tile would be mostly padding. Returns

@@ -298,31 +298,34 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
 // GEMM per modulus replaces the L^2 byte-slice pairs whenever nm is smaller (10 moduli
 // against 16 pairs for i32 at k = 65536, 20 against 64 for i64).
 
-// Weights of an EB-byte two's-complement value's bytes modulo p_g.
+// Weights of an EB-byte integer's bytes modulo p_g. The value x is read as the unsigned
+// x + 2^(8 EB - 1) (its sign bit flipped), and bias folds the -2^(8 EB - 1) back in
+// together with the balanced residue's shift half_g.
 struct WmWeights {
-    uint32_t w0[FM_MAX];   // bytes i of 256^i mod p_g, i < 4
-    uint32_t w1[FM_MAX];   // bytes i - 4 of 256^i mod p_g, 4 <= i < 8
-    uint32_t neg[FM_MAX];  // p_g - (2^(8 EB) mod p_g): adds -2^(8 EB) modulo p_g
+    uint32_t w0[FM_MAX];    // bytes i of 256^i mod p_g, i < 4
+    uint32_t w1[FM_MAX];    // bytes i - 4 of 256^i mod p_g, 4 <= i < 8
+    uint32_t bias[FM_MAX];  // half_g + (p_g - 2^(8 EB - 1) mod p_g)
 };
-
-// A value (< 2^24) congruent modulo p_g to the signed EB-byte integer whose bytes are v.
-template <int EB>
-__device__ __forceinline__ uint32_t wm_congruent(uint64_t v, int g, const WmWeights& w) {
-    uint32_t u = __dp4a(static_cast<uint32_t>(v), w.w0[g], 0u);
-    if (EB == 8) u = __dp4a(static_cast<uint32_t>(v >> 32), w.w1[g], u);
-    if ((v >> (8 * EB - 1)) & 1) u += w.neg[g];
-    return u;
-}
 
 template <int EB, int NM>
 __device__ __forceinline__ void wm_store(int8_t* dst, int64_t plane, const uint64_t (&v)[4],
                                          const FmParams& f, const WmWeights& w) {
+    constexpr uint64_t sign = 1ull << (8 * EB - 1);
+    uint32_t lo[4], hi[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        lo[c] = static_cast<uint32_t>(v[c] ^ sign);
+        hi[c] = static_cast<uint32_t>((v[c] ^ sign) >> 32);
+    }
 #pragma unroll
     for (int g = 0; g < NM; ++g) {
         uint32_t word = 0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            word |= fm_balanced(wm_congruent<EB>(v[c], g, w), 0u, f.p[g], f.magic32[g]) << (8 * c);
+        for (int c = 0; c < 4; ++c) {
+            uint32_t u = __dp4a(lo[c], w.w0[g], w.bias[g]);
+            if (EB == 8) u = __dp4a(hi[c], w.w1[g], u);
+            word = fm_put_byte(word, fm_balanced(u, f.p[g], f.magic32[g], f.half[g]), c);
+        }
         *reinterpret_cast<uint32_t*>(dst + g * plane) = word;
     }
 }
@@ -450,7 +453,9 @@ static void launch_wide_reduce(const int32_t* part, int chunks, int groups, size
 int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
                   const uint8_t* b, ptrdiff_t rsb, ptrdiff_t csb, void* c, ptrdiff_t rsc,
                   ptrdiff_t csc, size_t m, size_t k, size_t n, const LinearEpi& epi,
-                  uor_b200_route* route, bool cplx, bool digits_only) {
+                  uor_b200_route* route, bool cplx, uint32_t route_flags) {
+    const bool digits_only = (route_flags & UOR_B200_DIGIT_SLICES) != 0;
+    const bool force_modular = !digits_only && (route_flags & UOR_B200_MODULAR) != 0;
     cudaStream_t s = ctx->stream;
     if (route) {
         *route = uor_b200_route{};
@@ -501,10 +506,24 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
     p.pair_begin[ngroups] = npairs;
     p.num_groups = ngroups;
 
-    // The modular route when it runs fewer GEMMs than the byte-slice pairs.
+    // The modular route when its estimated time is below the byte-slice route's. Rates
+    // measured on B200 at 1024 x 65536 x 1024: a GEMM 8.1e-16 s per multiply-add;
+    // residue slicing 4.5e-13 s per element and modulus; byte slicing 5.1e-13 s per
+    // element and plane; the slice route's recombination 1.1e-12 s per cell and partial
+    // plane; the CRT 1.5e-11 s per cell.
     FmParams fm;
+    bool modular = false;
     if (!digits_only && (eb == 4 || eb == 8) && fm_plan_ints(8 * eb, k, fm) && fm.nm >= 8 &&
-        fm.nm <= 24 && fm.nm < npairs) {
+        fm.nm <= 24) {
+        const double mnk = static_cast<double>(m) * n * k, elems = static_cast<double>(k) * (m + n);
+        const double lane_d = static_cast<double>(INT_MAX) / worst;
+        const double chunks_d = static_cast<double>(k) / lane_d + 1.0;
+        const double t_mod = fm.nm * (mnk * 8.1e-16 + elems * 4.5e-13) + 1.5e-11 * m * n;
+        const double t_dig = npairs * mnk * 8.1e-16 + L * elems * 5.1e-13 +
+                             1.1e-12 * m * n * chunks_d * ngroups;
+        modular = force_modular || t_mod < t_dig;
+    }
+    if (modular) {
         const int nm = fm.nm;
         KSParams q{};
         q.num_groups = nm;
@@ -539,12 +558,9 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
                 (i < 4 ? w.w0[g] : w.w1[g]) |= c << (8 * (i & 3));
                 c = c * 256 % pg;
             }
-            w.neg[g] = (pg - c % pg) % pg;  // c = 256^8 mod p here; EB < 8 recomputed below
-            if (eb == 4) {
-                uint32_t c4 = 1 % pg;
-                for (int i = 0; i < 4; ++i) c4 = c4 * 256 % pg;
-                w.neg[g] = (pg - c4) % pg;
-            }
+            uint32_t top = 1 % pg;  // 2^(8 eb - 1) mod p
+            for (int i = 0; i < 8 * eb - 1; ++i) top = top * 2 % pg;
+            w.bias[g] = fm.half[g] + (pg - top) % pg;
         }
         const size_t kp = rup(k, 16);
         const size_t a_bytes = rup((size_t)nm * q.mp * kp, 256);

@@ -102,7 +102,7 @@ bool fm_plan_bound(const uint32_t* bound, int limbs, FmParams& f) {
     auto byte_of = [](const HBig& x, int b) {
         return static_cast<uint32_t>((x.l[b >> 2] >> (8 * (b & 3))) & 255u);
     };
-    for (int b = 0; b < nm; ++b) f.mmd[b] = static_cast<uint8_t>(byte_of(M, b));
+    for (int l = 0; l < FM_MAX / 4 + 1; ++l) f.mm[l] = M.l[l];
     for (int g = 0; g < nm; ++g) {
         const uint32_t p = kModuli[g];
         HBig mg = M;
@@ -112,6 +112,7 @@ bool fm_plan_bound(const uint32_t* bound, int limbs, FmParams& f) {
         f.p[g] = static_cast<uint16_t>(p);
         f.inv[g] = static_cast<uint16_t>(inv_mod(mgmod, p));
         f.magic32[g] = static_cast<uint32_t>(((1ull << 32) + p - 1) / p);
+        f.half[g] = p == 256 ? 127u : (p - 1) / 2;
         for (int b = 0; b < nm; ++b) f.md[g / 4][b] |= byte_of(mg, b) << (8 * (g % 4));
     }
     return true;

@@ -28,8 +28,9 @@ struct FmParams {
     uint16_t p[FM_MAX];
     uint16_t inv[FM_MAX];             // (M / p_g)^-1 mod p_g
     uint32_t magic32[FM_MAX];         // ceil(2^32 / p_g)
+    uint32_t half[FM_MAX];            // (p_g - 1) / 2, and 127 for 256
     uint32_t md[FM_MAX / 4][FM_MAX];  // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
-    uint8_t mmd[FM_MAX];              // byte b of M (M < 2^(8 nm))
+    uint32_t mm[FM_MAX / 4 + 1];      // 32-bit limbs of M (M < 2^(8 nm))
 };
 
 // The smallest even prefix of the moduli (256, 255, 253, 251, 247 and primes) whose
@@ -47,14 +48,20 @@ __device__ __forceinline__ uint32_t fm_mod24(uint32_t x, uint32_t p, uint32_t ma
     return x - __umulhi(x, magic32) * p;
 }
 
-// The balanced residue byte of a value congruent to u (< 2^24) modulo p, negated when
-// nmask is all ones: in [-(p-1)/2, (p-1)/2] for odd p, [-128, 127] for 256 (where -(-128)
-// is the same byte 128 modulo 256).
-__device__ __forceinline__ uint32_t fm_balanced(uint32_t u, uint32_t nmask, uint32_t p,
-                                                uint32_t magic32) {
-    const uint32_t r = fm_mod24(u, p, magic32);
-    const uint32_t b = r >= (p + 1) / 2 ? r - p : r;
-    return ((b ^ nmask) - nmask) & 255u;
+// The balanced residue of a value congruent to u - half modulo p (u < 2^24 already holds
+// the shift half = (p - 1) / 2, 127 for 256), in its low byte: (u mod p) - half lies in
+// [-(p-1)/2, (p-1)/2] for odd p and in [-127, 128] for 256, whose byte 128 is the int8
+// -128, the same residue modulo 256.
+__device__ __forceinline__ uint32_t fm_balanced(uint32_t u, uint32_t p, uint32_t magic32,
+                                                uint32_t half) {
+    return fm_mod24(u, p, magic32) - half;
+}
+
+// word with its byte c replaced by the low byte of b (c = 0 .. 3, a compile-time constant).
+__device__ __forceinline__ uint32_t fm_put_byte(uint32_t word, uint32_t b, int c) {
+    // __byte_perm selectors: 0-3 pick word's bytes, 4 picks b's low byte
+    const uint32_t sel = c == 0 ? 0x3214u : c == 1 ? 0x3240u : c == 2 ? 0x3410u : 0x4210u;
+    return __byte_perm(word, b, sel);
 }
 
 // y_g of one cell from the residue planes res[chunk][g][total] (idx the cell): the
@@ -104,12 +111,12 @@ __device__ __forceinline__ uint32_t fm_crt(const uint32_t (&y)[NM], const FmPara
             }
         }
     }
-    const int32_t t = static_cast<int32_t>(fx >> 32);
-    // Columns X_b - t M_b, each below NM 255^2 < 2^22 in magnitude.
+    const uint32_t t = static_cast<uint32_t>(fx >> 32);
+    // Columns X_b (each below NM 255^2 < 2^22), four to a limb, minus t M limb by limb.
     int64_t carry = 0;
 #pragma unroll
     for (int l = 0; l < NL; ++l) {
-        int64_t v = carry;
+        uint64_t v = 0;
 #pragma unroll
         for (int bi = 0; bi < 4; ++bi) {
             const int b = 4 * l + bi;
@@ -117,11 +124,13 @@ __device__ __forceinline__ uint32_t fm_crt(const uint32_t (&y)[NM], const FmPara
                 uint32_t col = 0;
 #pragma unroll
                 for (int a = 0; a < NA; ++a) col = __dp4a(ya[a], f.md[a][b], col);
-                v += (static_cast<int64_t>(col) - static_cast<int64_t>(t) * f.mmd[b]) << (8 * bi);
+                v += static_cast<uint64_t>(col) << (8 * bi);
             }
         }
-        limb[l] = static_cast<uint32_t>(v);
-        carry = v >> 32;
+        const uint32_t ml = l < FM_MAX / 4 + 1 ? f.mm[l] : 0u;
+        const int64_t sv = static_cast<int64_t>(v) + carry - static_cast<int64_t>(static_cast<uint64_t>(t) * ml);
+        limb[l] = static_cast<uint32_t>(sv);
+        carry = sv >> 32;
     }
     return carry < 0 ? ~0u : 0u;
 }

@@ -23,7 +23,7 @@ OK, NONCONFORMANT, OUTPUT_ALIASES, DEVICE_ERROR, TIMEOUT, NCCL_ERROR, DOES_NOT_F
     INVALID_ARGUMENT, UNSUPPORTED = range(9)
 NEAREST, TOWARD_ZERO, SATURATING, WRAPPING = range(4)
 I8, I16, I32, I64, I128, F32, F64, TROP_I8, TROP_I16, TROP_I32, TROP_I64 = range(1, 12)
-DEVICE_POINTERS, ASYNC, DIGIT_SLICES = 1, 2, 4
+DEVICE_POINTERS, ASYNC, DIGIT_SLICES, MODULAR = 1, 2, 4, 8
 KERNEL_NAMES = {0: "none", 1: "i8_tcgen05", 2: "limb_tcgen05", 3: "tropical",
                 4: "coded_tcgen05", 5: "float_exact", 6: "epilogue_only", 7: "skinny_dp4a"}
 
@@ -238,7 +238,7 @@ def _on_device(*bufs):
 # ------------------------------------------------------------------ integer
 
 def gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None, route=None,
-         asynchronous=False, digits=False):
+         asynchronous=False, digits=False, modular=False):
     """uor_matmul::gemm over views: av/bv/cv are (rows, cols, rs, cs) tuples over buffers a/b/c.
     digits=True keeps wide elements on the byte-slice route (the same bytes)."""
     dev = _on_device(a, b, c)
@@ -246,6 +246,8 @@ def gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=No
     call = make_call(encode, dev, ctx, route, asynchronous)
     if digits:
         call.flags |= DIGIT_SLICES
+    if modular:
+        call.flags |= MODULAR
     _check(lib().uor_b200_gemm(elem, out, ctypes.byref(A), ctypes.byref(B), ctypes.byref(C),
                                alpha, beta, ctypes.byref(call)), "gemm")
 
@@ -258,7 +260,7 @@ def complex_view(buf, rows, cols, rs=None, cs=1):
 
 
 def gemm_complex(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None,
-                 route=None, asynchronous=False, digits=False):
+                 route=None, asynchronous=False, digits=False, modular=False):
     """driver::gemm over Complex<elem> (alphabet.rs:656-776) into Complex<out>.
 
     elem in {I32, I64} and out in {I8 .. I128} name the part types; a, b, c are flat
@@ -270,6 +272,8 @@ def gemm_complex(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST
     call = make_call(encode, dev, ctx, route, asynchronous)
     if digits:
         call.flags |= DIGIT_SLICES
+    if modular:
+        call.flags |= MODULAR
     _check(lib().uor_b200_gemm_complex(elem, out, ctypes.byref(A), ctypes.byref(B),
                                        ctypes.byref(C), alpha, beta, ctypes.byref(call)),
            "gemm_complex")
@@ -310,7 +314,7 @@ def gemm_i8_i32(m, k, n, a, b, c, ctx=None, route=None, asynchronous=False):
 # ------------------------------------------------------------------ float
 
 def gemm_float(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=None,
-               route=None, asynchronous=False, digits=False):
+               route=None, asynchronous=False, digits=False, modular=False):
     """gemm_float over views; digits=True takes the digit-slice route even where the
     modular route applies (the same bytes either way)."""
     dev = _on_device(a, b, c)
@@ -318,6 +322,8 @@ def gemm_float(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST, 
     call = make_call(encode, dev, ctx, route, asynchronous)
     if digits:
         call.flags |= DIGIT_SLICES
+    if modular:
+        call.flags |= MODULAR
     _check(lib().uor_b200_gemm_float(elem, out, ctypes.byref(A), ctypes.byref(B),
                                      ctypes.byref(C), alpha, beta, ctypes.byref(call)),
            "gemm_float")
