@@ -526,11 +526,14 @@ def wl_wide(args, U, torch, rank):
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
-        ach = 16 * w.units / (avg_ms / 1e3) / 1e12
+        gemms = max(1, w.route.pairs)
+        ach = gemms * w.units / (avg_ms / 1e3) / 1e12
+        what = (f"{gemms} residue GEMMs modulo coprime moduli (modular route; 16 byte-slice "
+                "pairs otherwise)" if w.route.moduli else f"{gemms} int8 byte-slice pairs")
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src, "traffic": None,
-                "basis": "int8 limb-pair ops (16 x 2mnk) over the whole call "
-                         "(slicing, GEMM, recombination)",
+                "basis": f"int8 ops executed ({what} x 2mnk) over the whole call (slicing, "
+                         "GEMMs, recombination)",
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
@@ -593,11 +596,12 @@ def wl_complex(args, U, torch, rank):
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
-        ach = 16 * w.units / (avg_ms / 1e3) / 1e12
+        gemms = max(1, w.route.pairs)
+        ach = gemms * w.units / (avg_ms / 1e3) / 1e12  # one real-image GEMM is 8mkn ops
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src, "traffic": None,
-                "basis": "int8 limb-pair ops (16 x 2 x m x 2k x 2n) over the whole call "
-                         "(slicing, GEMM, recombination)",
+                "basis": f"int8 ops executed ({gemms} {'residue GEMMs' if w.route.moduli else 'byte-slice pairs'}"
+                         " x 2 x m x 2k x 2n) over the whole call (slicing, GEMMs, recombination)",
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
