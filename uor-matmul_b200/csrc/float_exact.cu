@@ -1201,9 +1201,14 @@ static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, con
     const int64_t aquads = static_cast<int64_t>(mp) * (kp / 4);
     const int sgrid = static_cast<int>(aquads / 256 + 1 < 148 * 16 ? aquads / 256 + 1 : 148 * 16);
     fm_slice_a_kernel<NM><<<sgrid, 256, smem, s>>>(as, mp, kp, a, rsa, csa, f64, m, k, rlo, pw, shmax, f);
-    dim3 g2(static_cast<unsigned>(np / 32),
-            static_cast<unsigned>((kp + 63) / 64 < 65535 ? (kp + 63) / 64 : 65535));
-    fm_slice_b_kernel<NM><<<g2, dim3(32, 8), smem, s>>>(bs, np, kp, b, rsb, csb, f64, k, n, clo, pw, shmax, f);
+    // Each block copies the coefficient table into shared memory once, so the blocks walk
+    // the reduction in strides: about eight blocks per SM in all.
+    const int gx = np / 32;
+    int gy = (kp + 63) / 64;
+    const int gy_cap = 148 * 8 / gx > 1 ? 148 * 8 / gx : 1;
+    if (gy > gy_cap) gy = gy_cap;
+    fm_slice_b_kernel<NM><<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), dim3(32, 8), smem, s>>>(
+        bs, np, kp, b, rsb, csb, f64, k, n, clo, pw, shmax, f);
 }
 
 template <int NM>
