@@ -42,7 +42,7 @@ sys.path.insert(0, ROOT)
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
 WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "f32", "wide", "wide-splitk", "trop",
-             "trop-witness", "complex")
+             "trop-witness", "complex", "codec-e8", "arena")
 
 
 def parse():
@@ -377,6 +377,150 @@ def wl_codec(args, U, torch, rank, sets=3):
         ach = w.units / (avg_ms / 1e3) / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src, "traffic": None,
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_codec_e8(args, U, torch, rank, sets=3):
+    """configs[1]'s shape over the E8 codebook: B = Book<256, 8> with u8 codes (e8_codec_u8,
+    0.125 bytes per weight), decoded on the GPU and multiplied on the tensor cores."""
+    import numpy as np
+    m, k, n = 2048, 8192, 8192
+    A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() for s in range(sets)]
+    Q = [torch.from_numpy(U.corpus(3 + 100 * s + 1000 * rank, U.CORPUS_RAW, k * n // 8)
+                          .astype(np.uint8)).cuda() for s in range(sets)]
+    table = torch.from_numpy(U.e8_table()).cuda()
+    C = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=2)
+
+    def step(i, ctx):
+        U.codec_gemm(U.I32, A[i % sets], (m, k, k, 1), U.TIER_BOOK, Q[i % sets], k, n, C,
+                     (m, n, n, 1), table=table, block=8, code_bytes=1, ctx=ctx, route=w.route,
+                     asynchronous=True)
+
+    def check(last):
+        s = last % sets
+        dense = table.to(torch.float64)[Q[s].to(torch.int64)].reshape(k, n)
+        x = torch.randint(-1, 2, (n,), device="cuda", dtype=torch.float64)
+        assert torch.equal(C.view(m, n).double() @ x, A[s].view(m, k).double() @ (dense @ x))
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, q, t = A[0].cpu().numpy(), Q[0].cpu().numpy(), table.cpu().numpy()
+        # Book<256, 8>: code q of row r decodes to table[q] (8 weights); a table lookup
+        dense = t[q.astype(np.int64)].reshape(k, n)
+        threads = host_threads(orc)
+
+        def run(rows):
+            c = np.zeros(rows * n, np.int32)
+            orc.gemm_int(orc.View(a, rows, k, k, 1), orc.View(dense.reshape(-1), k, n, n, 1),
+                         orc.View(c, rows, n, n, 1), threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        assert np.array_equal(c, C[:rows * n].cpu().numpy()), "GPU rows differ from the oracle"
+        return {"value": 2.0 * rows * k * n / dt / 1e12, "unit": "TOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), the Book table lookup then the "
+                          "C restatement's integer GEMM, OpenMP over rows; GPU rows compared"}
+
+    def e2e(steps, ctx, stream):
+        Ah, Qh = A[0].cpu().pin_memory(), Q[0].cpu().pin_memory()
+        Th = table.cpu().pin_memory()
+        Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
+        return timed_host(lambda: U.codec_gemm(U.I32, Ah, (m, k, k, 1), U.TIER_BOOK, Qh, k, n, Ch,
+                                               (m, n, n, 1), table=Th, block=8, code_bytes=1,
+                                               ctx=ctx),
+                          steps, stream, m * k + k * n // 8 + 2048, 4 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = "exact E8-codebook GEMM TOPS, 2048x8192x8192, Book<256,8> u8 codes (bit-exact, int32 out)"
+    w.unit, w.dtype = "TOPS", "int8 (decoded E8 codewords)"
+    w.config = {"workload": "codec_gemm Book<256,8> (E8, e8_codec_u8) 2048x8192x8192 per GPU, "
+                            "column-block sharded", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = f"{sets} rotating operand sets + 64 MiB output"
+    w.algorithmic_bytes = m * k + k * n // 8 + 4 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        ach = w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "basis": "2mnk int8 ops over the whole call (block decode to a workspace + K1)",
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_arena(args, U, torch, rank, sets=2):
+    """Arena<f32, 256, u8> (CK-14's dequantized-8-bit codebook) as gemm_tabulated holds it:
+    f32 A 2048 x 8192 against W 8192 x 8192 codes (n x k), exact f32 out."""
+    import numpy as np
+    m, k, n = 2048, 8192, 8192
+    vals = (np.arange(256, dtype=np.float32) - np.float32(127.5)) * np.float32(2.0 ** -6)
+    U.arena_canonicalize(vals)
+    table = torch.from_numpy(vals).cuda()
+    A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_F32_WIDE, m * k)).cuda() for s in range(sets)]
+    Q = [torch.from_numpy(U.corpus(5 + 100 * s + 1000 * rank, U.CORPUS_RAW, n * k).astype(np.uint8)).cuda()
+         for s in range(sets)]
+    C = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=7)
+
+    def step(i, ctx):
+        U.arena_gemm(U.F32, U.F32, A[i % sets], (m, k, k, 1), table, Q[i % sets], k, n, C,
+                     (m, n, n, 1), orientation=1, ctx=ctx, route=w.route, asynchronous=True)
+
+    def check(last):
+        pass  # bit for bit by the CPU leg and the GPU tests
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, q, t = A[0].cpu().numpy(), Q[0].cpu().numpy(), table.cpu().numpy()
+        dense = orc.decode_arena(t, q, n, k)
+        threads = host_threads(orc)
+
+        def run(rows):
+            c = np.zeros(rows * n, np.float32)
+            orc.gemm_float(orc.View(a, rows, k, k, 1), orc.View(dense.reshape(-1), k, n, 1, k),
+                           orc.View(c, rows, n, n, 1), threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        assert np.array_equal(c.view(np.uint32), C[:rows * n].cpu().numpy().view(np.uint32)), \
+            "GPU rows differ from the oracle"
+        return {"value": 2.0 * rows * k * n / dt / 1e12, "unit": "TFLOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), the oracle's Arena decode then the "
+                          "C restatement of gemm_float, OpenMP over rows; GPU rows compared"}
+
+    def e2e(steps, ctx, stream):
+        Ah, Qh = A[0].cpu().pin_memory(), Q[0].cpu().pin_memory()
+        Th = table.cpu().pin_memory()
+        Ch = torch.empty(m * n, dtype=torch.float32).pin_memory()
+        return timed_host(lambda: U.arena_gemm(U.F32, U.F32, Ah, (m, k, k, 1), Th, Qh, k, n, Ch,
+                                               (m, n, n, 1), orientation=1, ctx=ctx),
+                          steps, stream, 4 * m * k + n * k + 1024, 4 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = "exact Arena f32 GEMM TFLOPS, 2048x8192x8192, 256 f32 symbols, u8 codes (bit-exact)"
+    w.unit, w.dtype = "TFLOPS", "f32 (decoded symbols), exact float route"
+    w.config = {"workload": "gemm_tabulated Arena<f32,256,u8> (CK-14 codebook) 2048x8192x8192 per "
+                            "GPU, A from the configs[2] distribution", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = f"{sets} rotating operand sets + 64 MiB output"
+    w.algorithmic_bytes = 4 * m * k + n * k + 4 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        gemms = max(1, w.route.pairs)
+        ach = gemms * w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "basis": f"int8 ops executed ({gemms} GEMMs of the exact float route x 2mnk)",
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
@@ -769,6 +913,10 @@ def build_workload(name, args, U, torch, rank, world=1):
         return wl_wide_splitk(args, U, torch, rank, world)
     if name == "complex":
         return wl_complex(args, U, torch, rank)
+    if name == "codec-e8":
+        return wl_codec_e8(args, U, torch, rank)
+    if name == "arena":
+        return wl_arena(args, U, torch, rank)
     return wl_trop(args, U, torch, rank, selected=name == "trop-witness")
 
 

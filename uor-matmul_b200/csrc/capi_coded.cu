@@ -231,35 +231,49 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
 }
 
 // Sign / Ternary / Book codes of `cb` bytes per block of `blk` elements (little-endian
-// codes), decoded element by element exactly as CodedMatrix::at does for a fixed-width
-// tier (matrix.rs:202-207): code = codes[row * (cols / blk) + col / blk], element
-// col % blk of it; every value minus `zero` (Offset, codecs.rs: decode - zero).
+// codes), decoded exactly as CodedMatrix::at does for a fixed-width tier (matrix.rs:202-207):
+// code = codes[row * (cols / blk) + col / blk], element col % blk of it; every value minus
+// `zero` (Offset, codecs.rs: decode - zero). One thread per code writes the code's blk
+// elements, in the coded matrix's own rows x cols layout, four bytes to a store.
+__device__ __forceinline__ int decode_elem(int tier, uint32_t code, int t, int cb,
+                                           const int8_t* __restrict__ row) {
+    if (tier == UOR_B200_TIER_SIGN)  // bit t set: +1; clear, or past the code's width: -1
+        return (t < 8 * cb && ((code >> t) & 1u)) ? 1 : -1;
+    if (tier == UOR_B200_TIER_TERNARY) {
+        // digit t: 0 -> -1, 2 -> +1, 1 and 3 -> 0; a digit past the code's width reads 0, so -1
+        const uint32_t d = 2 * t < 8 * cb ? (code >> (2 * t)) & 3u : 0u;
+        return d == 0 ? -1 : (d == 2 ? 1 : 0);
+    }
+    return row[t];  // Book: table[code % N][t] (codecs.rs:306-308)
+}
+
 __global__ void decode_block_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
                                     const int8_t* __restrict__ table, int tier, int N, int blk,
-                                    int cb, int zero, int orientation, int k, int n) {
-    const int64_t total = static_cast<int64_t>(k) * n;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
-        const int row = orientation == 0 ? p : j, col = orientation == 0 ? j : p;
-        const int cols = orientation == 0 ? n : k;
-        const uint8_t* cp = codes + (static_cast<int64_t>(row) * (cols / blk) + col / blk) * cb;
+                                    int cb, int zero, int64_t rows, int64_t cols) {
+    const int64_t cpr = cols / blk;
+    const int64_t total = rows * cpr;
+    const bool words = (blk & 3) == 0;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint8_t* cp = codes + t * cb;
         const uint32_t code = cb == 1 ? cp[0] : (static_cast<uint32_t>(cp[0]) | (static_cast<uint32_t>(cp[1]) << 8));
-        const int t = col % blk;
-        int v;
-        if (tier == UOR_B200_TIER_SIGN) {
-            // bit t set: +1; clear, or past the code's width: -1 (codecs.rs:386-400)
-            v = (t < 8 * cb && ((code >> t) & 1u)) ? 1 : -1;
-        } else if (tier == UOR_B200_TIER_TERNARY) {
-            // digit t: 0 -> -1, 2 -> +1, 1 and 3 -> 0; a digit past the code's width reads
-            // as 0, so -1 (codecs.rs Ternary::decode_element)
-            const uint32_t d = 2 * t < 8 * cb ? (code >> (2 * t)) & 3u : 0u;
-            v = d == 0 ? -1 : (d == 2 ? 1 : 0);
+        const int8_t* brow = tier == UOR_B200_TIER_BOOK
+                                 ? table + static_cast<int64_t>(code % static_cast<uint32_t>(N)) * blk
+                                 : nullptr;
+        int8_t* dst = out + t * blk;  // row r = t / cpr, column block t % cpr
+        if (words) {
+            for (int e = 0; e < blk; e += 4) {
+                uint32_t w = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    w |= static_cast<uint32_t>(static_cast<uint8_t>(decode_elem(tier, code, e + q, cb, brow) - zero))
+                         << (8 * q);
+                *reinterpret_cast<uint32_t*>(dst + e) = w;
+            }
         } else {
-            // Book: table[code % N][t] (codecs.rs:306-308)
-            v = table[static_cast<int64_t>(code % static_cast<uint32_t>(N)) * blk + t];
+            for (int e = 0; e < blk; ++e)
+                dst[e] = static_cast<int8_t>(decode_elem(tier, code, e, cb, brow) - zero);
         }
-        out[idx] = static_cast<int8_t>(v - zero);
     }
 }
 
@@ -376,12 +390,16 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
     if (k) {
         const int64_t total = (int64_t)k * n;
         const int grid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+        // dense holds the coded matrix itself: k x n (orientation 0) or n x k (1)
         decode_block_kernel<<<grid, 256, 0, s>>>(dense, dcodes, dtable, tier, (int)N, (int)blk,
-                                                 (int)cb, zero, (int)orientation, (int)k, (int)n);
+                                                 (int)cb, zero, (int64_t)rows, (int64_t)cols);
         if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
     }
     const LinearEpi epi{alpha, beta, mode, kind};
-    st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs, dense, (ptrdiff_t)n, 1,
+    // B = dense (k x n row-major) or its transpose read K-major (dense n x k)
+    const ptrdiff_t rsb = orientation == 0 ? (ptrdiff_t)n : 1;
+    const ptrdiff_t csb = orientation == 0 ? 1 : (ptrdiff_t)k;
+    st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs, dense, rsb, csb,
                      cs.dev_origin, C.rs, C.cs, m, k, n, epi, route);
     if (st) return st;
     route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
