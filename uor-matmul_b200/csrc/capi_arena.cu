@@ -34,6 +34,31 @@ __global__ void arena_decode_kernel(W* __restrict__ out, const uint8_t* __restri
     }
 }
 
+// The same decode for codes laid n x k (gemm_tabulated's W), through a 32 x 32 shared tile:
+// codes are read along k and symbols written along n, both coalesced.
+template <typename W>
+__global__ void arena_decode_t_kernel(W* __restrict__ out, const uint8_t* __restrict__ codes,
+                                      const W* __restrict__ table, uint32_t N, int cb, int k, int n) {
+    __shared__ uint32_t tile[32][33];
+    const int p0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    for (int r = ty; r < 32; r += 8) {
+        const int j = j0 + r, p = p0 + tx;
+        uint32_t code = 0;
+        if (j < n && p < k) {
+            const int64_t at = static_cast<int64_t>(j) * k + p;
+            code = cb == 1 ? codes[at]
+                           : (static_cast<uint32_t>(codes[2 * at]) | static_cast<uint32_t>(codes[2 * at + 1]) << 8);
+        }
+        tile[r][tx] = code;
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int p = p0 + r, j = j0 + tx;
+        if (p < k && j < n) out[static_cast<int64_t>(p) * n + j] = table[tile[tx][r] % N];
+    }
+}
+
 bool float_type(uor_b200_dtype t) { return t == UOR_B200_F32 || t == UOR_B200_F64; }
 
 int arena_common(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a,
@@ -97,7 +122,17 @@ int arena_common(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a
         const int64_t total = (int64_t)k * n;
         const int grid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
         const uint32_t N = table_len > 0xFFFFFFFFull ? 0xFFFFFFFFu : (uint32_t)table_len;
-        if (es == 4)
+        const dim3 tg((unsigned)((k + 31) / 32), (unsigned)((n + 31) / 32));
+        if (orientation == 1 && n <= 65535 * 32) {
+            if (es == 4)
+                arena_decode_t_kernel<uint32_t><<<tg, dim3(32, 8), 0, s>>>(
+                    reinterpret_cast<uint32_t*>(dense), dcodes, reinterpret_cast<const uint32_t*>(buf), N,
+                    (int)code_bytes, (int)k, (int)n);
+            else
+                arena_decode_t_kernel<uint64_t><<<tg, dim3(32, 8), 0, s>>>(
+                    reinterpret_cast<uint64_t*>(dense), dcodes, reinterpret_cast<const uint64_t*>(buf), N,
+                    (int)code_bytes, (int)k, (int)n);
+        } else if (es == 4)
             arena_decode_kernel<uint32_t><<<grid, 256, 0, s>>>(
                 reinterpret_cast<uint32_t*>(dense), dcodes, reinterpret_cast<const uint32_t*>(buf), N,
                 (int)code_bytes, (int)orientation, (int)k, (int)n);
