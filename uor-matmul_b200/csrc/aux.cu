@@ -1,6 +1,7 @@
 // aux.cu -- helper kernels: strided gather, epilogue-only, chunk reduction,
 // and the bounded-wait self-test.
 #include "aux.cuh"
+#include "walk.cuh"
 #include "ptx.cuh"
 
 namespace uor {
@@ -47,9 +48,8 @@ cudaError_t gather_2d(void* dst, size_t ld, const void* src, size_t rows, size_t
 __global__ void epilogue_only_kernel(void* c, int64_t rsc, int64_t csc, size_t m, size_t n,
                                      LinearEpi e) {
     const size_t total = m * n;
-    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
-         idx += (size_t)gridDim.x * blockDim.x) {
-        const size_t i = idx / n, j = idx - (idx / n) * n;
+    for (GridWalk wk(n); wk.idx < total; wk.next()) {
+        const size_t i = wk.i, j = wk.j;
         finish_cell(e, c, (int64_t)i * rsc + (int64_t)j * csc, 0);
     }
 }
@@ -66,11 +66,11 @@ cudaError_t epilogue_only(void* c, int64_t rsc, int64_t csc, size_t m, size_t n,
 __global__ void reduce_chunks_kernel(const int32_t* __restrict__ part, int chunks, size_t m,
                                      size_t n, void* c, int64_t rsc, int64_t csc, LinearEpi e) {
     const size_t total = m * n;
-    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
-         idx += (size_t)gridDim.x * blockDim.x) {
+    for (GridWalk wk(n); wk.idx < total; wk.next()) {
+        const size_t idx = wk.idx;
         int64_t acc = 0;
         for (int q = 0; q < chunks; ++q) acc += part[(size_t)q * total + idx];
-        const size_t i = idx / n, j = idx - (idx / n) * n;
+        const size_t i = wk.i, j = wk.j;
         finish_cell(e, c, (int64_t)i * rsc + (int64_t)j * csc, acc);
     }
 }

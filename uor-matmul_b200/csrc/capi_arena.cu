@@ -9,6 +9,7 @@
 #include "float_exact.h"
 #include "internal.h"
 #include "staging.h"
+#include "walk.cuh"
 
 using namespace uor;
 
@@ -23,9 +24,9 @@ __global__ void arena_decode_kernel(W* __restrict__ out, const uint8_t* __restri
                                     const W* __restrict__ table, uint32_t N, int cb,
                                     int orientation, int k, int n) {
     const int64_t total = static_cast<int64_t>(k) * n;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(idx / n), j = static_cast<int>(idx - idx / n * n);
+    for (GridWalk wk(static_cast<size_t>(n)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int64_t idx = static_cast<int64_t>(wk.idx);
+        const int p = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
         const int64_t at = orientation == 0 ? idx : static_cast<int64_t>(j) * k + p;
         const uint32_t code =
             cb == 1 ? codes[at]

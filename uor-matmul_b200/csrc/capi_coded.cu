@@ -11,6 +11,7 @@
 #include "internal.h"
 #include "staging.h"
 #include "ptx.cuh"
+#include "walk.cuh"
 
 using namespace uor;
 
@@ -24,9 +25,9 @@ __global__ void decode_dense_kernel(int8_t* __restrict__ out, const uint8_t* __r
     const int64_t total = static_cast<int64_t>(k) * n;
     const int bits = 8 / P;
     const unsigned mask = bits >= 8 ? 0xFFu : ((1u << bits) - 1u);
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+    for (GridWalk wk(static_cast<size_t>(n)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int64_t idx = static_cast<int64_t>(wk.idx);
+        const int p = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
         // CodedMatrix::at (matrix.rs:202-207) on the codec's own rows and columns
         const int row = orientation == 0 ? p : j, col = orientation == 0 ? j : p;
         const int cols = orientation == 0 ? n : k;

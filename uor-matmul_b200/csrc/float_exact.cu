@@ -31,6 +31,7 @@
 #include "gemm_slices.cuh"
 #include "modular.cuh"
 #include "ptx.cuh"
+#include "walk.cuh"
 
 namespace uor {
 
@@ -592,10 +593,9 @@ __global__ void fx_slice_a_kernel(int8_t* __restrict__ as, int L, int mp, int kp
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
-    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
-         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(t / qpr);
-        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+    for (GridWalk wk(static_cast<size_t>(qpr)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int i = static_cast<int>(wk.i);
+        const int p0 = static_cast<int>(wk.j) * 4;
         uint64_t ylo[4], yhi[4];
         const int li = i < m ? lo[i] : 0;
 #pragma unroll
@@ -741,9 +741,9 @@ __global__ void fx_reduce_kernel(const int32_t* __restrict__ part, int chunks, i
                                  int n, const int* __restrict__ rlo, const int* __restrict__ clo,
                                  const uint8_t* __restrict__ flags, FxEpi e) {
     const size_t total = static_cast<size_t>(m) * n;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+    for (GridWalk wk(static_cast<size_t>(n)); wk.idx < total; wk.next()) {
+        const size_t idx = wk.idx;
+        const int i = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
         if (e.beta == 0 && !(flags && flags[idx])) {
             const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
             fx_reduce_fast<NG>(part, chunks, groups, total, idx, rlo[i] + clo[j], off, e);
@@ -868,9 +868,9 @@ __global__ void fx_reduce_lazy_kernel(const int32_t* __restrict__ part, int chun
     constexpr int NQ = (NG + 7) / 8;
     constexpr int NW = NQ + 2;
     const size_t total = static_cast<size_t>(m) * n;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+    for (GridWalk wk(static_cast<size_t>(n)); wk.idx < total; wk.next()) {
+        const size_t idx = wk.idx;
+        const int i = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
         const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
         if (rspan[i] == 0 || cspan[j] == 0) {  // a row or column of zeros: the sum is 0
             store_float(e.c, e.out64, off, 0);
@@ -1065,10 +1065,9 @@ __global__ void fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
-    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
-         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(t / qpr);
-        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+    for (GridWalk wk(static_cast<size_t>(qpr)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int i = static_cast<int>(wk.i);
+        const int p0 = static_cast<int>(wk.j) * 4;
         uint64_t mant[4];
         int sh[4];
         bool neg[4];
@@ -1151,9 +1150,9 @@ __global__ void __launch_bounds__(256, 4) fm_crt_kernel(const uint8_t* __restric
     constexpr int NL = FmLimbs<NM>::value;
     constexpr int NW = (NL + 1) / 2 + 2;   // 64-bit words: the value, alpha's 64 bits, sign
     const size_t total = static_cast<size_t>(m) * n;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(idx / n), j = static_cast<int>(idx % n);
+    for (GridWalk wk(static_cast<size_t>(n)); wk.idx < total; wk.next()) {
+        const size_t idx = wk.idx;
+        const int i = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
         const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
         const int fl0 = flags ? flags[idx] : 0;
         if (e.beta == 0 && !fl0 && (rspan[i] == 0 || cspan[j] == 0)) {

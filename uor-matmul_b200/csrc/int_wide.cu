@@ -19,6 +19,7 @@
 #include "gemm_slices.cuh"
 #include "modular.cuh"
 #include "ptx.cuh"
+#include "walk.cuh"
 
 namespace uor {
 
@@ -70,10 +71,9 @@ __global__ void slice_a_kernel(uint8_t* __restrict__ as, int mp, int kp,
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
-    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
-         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(t / qpr);
-        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+    for (GridWalk wk(static_cast<size_t>(qpr)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int i = static_cast<int>(wk.i);
+        const int p0 = static_cast<int>(wk.j) * 4;
         uint64_t v[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -222,9 +222,8 @@ struct WideEpi {
 
 // The exact accumulator of cell idx (row-major over m x n) through the Linear epilogue
 // (epilogue.rs:79-93) in the element's own accumulator, encoded and stored.
-__device__ __forceinline__ void wide_finish(const WideEpi& e, const L3& acc, size_t idx, size_t n,
+__device__ __forceinline__ void wide_finish(const WideEpi& e, const L3& acc, size_t i, size_t j,
                                             void* c, int64_t rsc, int64_t csc) {
-    const size_t i = idx / n, j = idx - (idx / n) * n;
     const int64_t off =
         e.cplx ? 2 * (static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j >> 1) * csc) +
                      static_cast<int64_t>(j & 1)
@@ -259,8 +258,8 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
     constexpr int NQ = (NG + 7) / 8;
     static_assert(NQ <= 2, "at most 16 diagonals");
     const size_t total = m * n;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    for (GridWalk wk(n); wk.idx < total; wk.next()) {
+        const size_t idx = wk.idx;
         i128 col[NQ];
 #pragma unroll
         for (int q = 0; q < NQ; ++q) col[q] = 0;
@@ -287,7 +286,7 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
                 acc.w[2] = carry < 0 ? ~0ull : 0ull;
             }
         }
-        wide_finish(e, acc, idx, n, c, rsc, csc);
+        wide_finish(e, acc, wk.i, wk.j, c, rsc, csc);
     }
 }
 
@@ -339,10 +338,9 @@ __global__ void wm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp,
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
-    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
-         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int i = static_cast<int>(t / qpr);
-        const int p0 = static_cast<int>(t - static_cast<int64_t>(i) * qpr) * 4;
+    for (GridWalk wk(static_cast<size_t>(qpr)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int i = static_cast<int>(wk.i);
+        const int p0 = static_cast<int>(wk.j) * 4;
         uint64_t v[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -401,8 +399,8 @@ __global__ void wm_crt_kernel(const uint8_t* __restrict__ res, int chunks, size_
                               void* c, int64_t rsc, int64_t csc, WideEpi e, FmParams f) {
     constexpr int NL = FmLimbs<NM>::value;
     const size_t total = m * n;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    for (GridWalk wk(n); wk.idx < total; wk.next()) {
+        const size_t idx = wk.idx;
         uint32_t y[NM];
         fm_load_y<NM>(res, chunks, total, idx, f, y);
         uint32_t limb[NL];
@@ -414,7 +412,7 @@ __global__ void wm_crt_kernel(const uint8_t* __restrict__ res, int chunks, size_
             const uint64_t hi = 2 * q + 1 < NL ? limb[2 * q + 1] : ext;
             acc.w[q] = lo | hi << 32;
         }
-        wide_finish(e, acc, idx, n, c, rsc, csc);
+        wide_finish(e, acc, wk.i, wk.j, c, rsc, csc);
     }
 }
 

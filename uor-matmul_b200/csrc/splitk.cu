@@ -1,6 +1,7 @@
 // splitk.cu -- the limb conversion and finish kernels of the split-K exchange
 // (see splitk.cuh). Both are HBM-bound elementwise passes.
 #include "splitk.cuh"
+#include "walk.cuh"
 
 namespace uor {
 
@@ -22,12 +23,12 @@ __global__ void i128_to_limbs_kernel(const uint64_t* __restrict__ x, int64_t* __
 __global__ void limbs_finish_kernel(const int64_t* __restrict__ limbs, size_t m, size_t n, void* c,
                                     int64_t rsc, int64_t csc, LinearEpi e) {
     const size_t total = m * n;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    for (GridWalk wk(n); wk.idx < total; wk.next()) {
+        const size_t idx = wk.idx;
         const i128 x = static_cast<i128>(limbs[3 * idx]) +
                        (static_cast<i128>(limbs[3 * idx + 1]) << SPLITK_LIMB_BITS) +
                        (static_cast<i128>(limbs[3 * idx + 2]) << (2 * SPLITK_LIMB_BITS));
-        const size_t i = idx / n, j = idx - i * n;
+        const size_t i = wk.i, j = wk.j;
         const int64_t off = static_cast<int64_t>(i) * rsc + static_cast<int64_t>(j) * csc;
         i128 tot = e.alpha == 1 ? x : sat_mul(x, e.alpha);
         if (e.beta != 0)

@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 #include <climits>
 #include "tropical.cuh"
+#include "walk.cuh"
 
 namespace uor {
 
@@ -117,9 +118,9 @@ __global__ void trop_pack_b_kernel(int16_t* __restrict__ bt, int np, int kp,
                                    const uint8_t* __restrict__ b, int64_t rsb, int64_t csb, int k,
                                    int n) {
     const int64_t total = static_cast<int64_t>(np) * kp;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(idx / np), j = static_cast<int>(idx % np);
+    for (GridWalk wk(static_cast<size_t>(np)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int64_t idx = static_cast<int64_t>(wk.idx);
+        const int p = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
         int v = TR_ZERO16;
         if (j < n && p < k) {
             const uint8_t* e = b + (static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb) * 2;
@@ -265,9 +266,9 @@ __global__ void trop_witness_pack_b_kernel(int32_t* __restrict__ bt, int np, int
                                            const uint8_t* __restrict__ b, int64_t rsb,
                                            int64_t csb, int k, int n) {
     const int64_t total = static_cast<int64_t>(np) * kp;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(idx / np), j = static_cast<int>(idx % np);
+    for (GridWalk wk(static_cast<size_t>(np)); wk.idx < static_cast<size_t>(total); wk.next()) {
+        const int64_t idx = static_cast<int64_t>(wk.idx);
+        const int p = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
         int32_t v = TW_ZERO;
         if (j < n && p < k) {
             const uint8_t* el = b + (static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb) * 2;
