@@ -42,7 +42,7 @@ sys.path.insert(0, ROOT)
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
 WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "f32", "wide", "wide-splitk", "trop",
-             "trop-witness", "complex", "codec-e8", "arena")
+             "trop-witness", "complex", "codec-e8", "arena", "f64")
 
 
 def parse():
@@ -616,6 +616,81 @@ def wl_f32(args, U, torch, rank, size, sets=2):
     return w
 
 
+def wl_f64(args, U, torch, rank, size, sets=2):
+    """raw::dgemm (exact f64, rounded once) at configs[2]'s shape and exponent range with
+    full 53-bit significands: +-m 2^(e - 52), m in [2^52, 2^53), e in [-30, 30]."""
+    import numpy as np
+    m = k = n = size
+    rng = np.random.default_rng(64 + rank)
+
+    def draw(count):
+        mant = rng.integers(1 << 52, 1 << 53, size=count, dtype=np.int64).astype(np.float64)
+        e = rng.integers(-30, 31, size=count)
+        sgn = rng.choice([-1.0, 1.0], size=count)
+        return sgn * np.ldexp(mant, e - 52)
+    host = [(draw(m * k), draw(k * n)) for _ in range(sets)]
+    A = [torch.from_numpy(h[0]).cuda() for h in host]
+    B = [torch.from_numpy(h[1]).cuda() for h in host]
+    C = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=6)
+
+    def step(i, ctx):
+        U.gemm_float(U.F64, U.F64, A[i % sets], (m, k, k, 1), B[i % sets], (k, n, n, 1), C,
+                     (m, n, n, 1), ctx=ctx, route=w.route, asynchronous=True)
+
+    def check(last):
+        pass  # bit for bit by the CPU leg and the GPU tests
+
+    def cpu(budget_s, ctx):
+        from oracle import oracle as orc
+        step(0, ctx)
+        ctx.sync()
+        a, b = host[0]
+        threads = host_threads(orc)
+
+        def run(rows):
+            c = np.zeros(rows * n, np.float64)
+            orc.gemm_float(orc.View(a, rows, k, k, 1), orc.View(b, k, n, n, 1),
+                           orc.View(c, rows, n, n, 1), threads=threads)
+            return c
+        rows, dt, c = sample_rows(m, run, budget_s)
+        assert np.array_equal(c.view(np.uint64), C[:rows * n].cpu().numpy().view(np.uint64)), \
+            "GPU rows differ"
+        return {"value": 2.0 * rows * k * n / dt / 1e12, "unit": "TFLOPS", "cores": threads,
+                "kind": "port",
+                "sample": f"{rows} of {m} rows ({dt:.2f} s), C restatement of the f64 Complete "
+                          "register accumulation, OpenMP over rows; GPU rows compared bit for bit"}
+
+    def e2e(steps, ctx, stream):
+        Ah = torch.from_numpy(host[0][0]).pin_memory()
+        Bh = torch.from_numpy(host[0][1]).pin_memory()
+        Ch = torch.empty(m * n, dtype=torch.float64).pin_memory()
+        return timed_host(lambda: U.gemm_float(U.F64, U.F64, Ah, (m, k, k, 1), Bh, (k, n, n, 1),
+                                               Ch, (m, n, n, 1), ctx=ctx),
+                          steps, stream, 16 * m * k, 8 * m * n)
+
+    w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
+    w.metric = f"exact f64 GEMM TFLOPS at {size}^3 (raw::dgemm, bit-exact, rounded once)"
+    w.unit, w.dtype = "TFLOPS", "f64 in, int8 residue GEMMs modulo coprime moduli + CRT"
+    w.config = {"workload": f"dgemm f64 {m}x{k}x{n} per GPU (53-bit significands, exponents "
+                            "in [-30, 30]), column-block sharded", "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = f"{sets} rotating operand sets ({sets * 16 * m * k >> 20} MiB) + {8 * m * n >> 20} MiB output"
+    w.algorithmic_bytes = 16 * m * k + 8 * m * n
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        gemms = max(1, w.route.pairs)
+        ach = gemms * w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "basis": f"int8 ops executed ({gemms} GEMMs x 2mnk; moduli {w.route.moduli}) "
+                         "over the whole call",
+                "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
 def wl_wide(args, U, torch, rank):
     """i32 x i32 full range, 1024 x 65536 x 1024, exact i128 output."""
     import numpy as np
@@ -917,6 +992,8 @@ def build_workload(name, args, U, torch, rank, world=1):
         return wl_codec_e8(args, U, torch, rank)
     if name == "arena":
         return wl_arena(args, U, torch, rank)
+    if name == "f64":
+        return wl_f64(args, U, torch, rank, args.size or 4096)
     return wl_trop(args, U, torch, rank, selected=name == "trop-witness")
 
 

@@ -983,7 +983,8 @@ __global__ void fx_fix_kernel(const uint32_t* __restrict__ list, const uint32_t*
 // per modulus, and the CRT rebuilding each cell's exact integer S, |S| <= k (2^span_A - 1)
 // (2^span_B - 1). Then the epilogue and encode of the digit route.
 
-constexpr int FM_TABLE_MAX = 48 * 1024;  // bytes of the 2^s table in shared memory
+// Bytes of the 2^s table in shared memory (beside the B slicer's 25 KB static tile).
+constexpr int FM_TABLE_MAX = 160 * 1024;
 
 // The table of words [2^sh, 2^(sh+8), 2^(sh+16), 0] mod p_g (f32 significands, W = 1), or
 // two words covering 2^(sh + 8i) for i < 8 (f64, W = 2), row sh holding W x NMP words.
