@@ -1061,6 +1061,9 @@ __global__ void fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const
     constexpr int NMP = (NM + 3) / 4 * 4;
     extern __shared__ __align__(16) uint32_t pw[];
     const int W = f64 ? 2 : 1;
+    // f32 rows with unit column stride on 16-byte boundaries take one vector load per thread
+    const bool vec = !f64 && csa == 1 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                     ((rsa * 4) & 15) == 0;
     fm_fill_pow2(pw, pow2, 2 * shmax * W * NMP);
     __syncthreads();
     const int qpr = kp >> 2;
@@ -1073,13 +1076,22 @@ __global__ void fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const
         int sh[4];
         bool neg[4];
         const int li = i < m ? lo[i] : 0;
+        if (vec && i < m && p0 + 3 < k) {
+            // four consecutive f32 elements in one 16-byte load
+            const uint4 q = *reinterpret_cast<const uint4*>(a + (static_cast<int64_t>(i) * rsa + p0) * 4);
+            const uint32_t bits[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int p = p0 + c;
-            FDec d{};
-            if (i < m && p < k)
-                d = fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, f64);
-            fm_parts(d, li, mant[c], sh[c], neg[c]);
+            for (int c = 0; c < 4; ++c) fm_parts(fdecode(reinterpret_cast<const uint8_t*>(bits), c, false), li,
+                                                 mant[c], sh[c], neg[c]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int p = p0 + c;
+                FDec d{};
+                if (i < m && p < k)
+                    d = fdecode(a, static_cast<int64_t>(i) * rsa + static_cast<int64_t>(p) * csa, f64);
+                fm_parts(d, li, mant[c], sh[c], neg[c]);
+            }
         }
         fm_store_residues<NM>(as + static_cast<int64_t>(i) * kp + p0, plane, mant, sh, neg, pw, W, f);
     }

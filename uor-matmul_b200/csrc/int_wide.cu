@@ -335,6 +335,10 @@ template <int EB, int NM>
 __global__ void wm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp,
                                   const uint8_t* __restrict__ a, int64_t rsa, int64_t csa,
                                   bool aligned, int m, int k, bool cplx, FmParams f, WmWeights w) {
+    // Rows of consecutive elements (unit column stride; a complex row's parts are then
+    // consecutive too) starting on 16-byte boundaries take vector loads.
+    const bool vec = csa == 1 && (EB == 4 || EB == 8) &&
+                     (reinterpret_cast<uintptr_t>(a) & 15) == 0 && ((rsa * EB * (cplx ? 2 : 1)) & 15) == 0;
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
@@ -342,10 +346,28 @@ __global__ void wm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp,
         const int i = static_cast<int>(wk.i);
         const int p0 = static_cast<int>(wk.j) * 4;
         uint64_t v[4];
+        const int64_t e0 = cplx_a_index(i, p0, rsa, csa, cplx);
+        if (vec && i < m && p0 + 3 < k) {
+            // four consecutive elements in one or two 16-byte loads
+            const uint8_t* src = a + e0 * EB;
+            if (EB == 4) {
+                const uint4 q = *reinterpret_cast<const uint4*>(src);
+                v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+            } else if (EB == 8) {
+                const uint4 q0 = reinterpret_cast<const uint4*>(src)[0];
+                const uint4 q1 = reinterpret_cast<const uint4*>(src)[1];
+                v[0] = q0.x | static_cast<uint64_t>(q0.y) << 32, v[1] = q0.z | static_cast<uint64_t>(q0.w) << 32;
+                v[2] = q1.x | static_cast<uint64_t>(q1.y) << 32, v[3] = q1.z | static_cast<uint64_t>(q1.w) << 32;
+            } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const int p = p0 + c;
-            v[c] = (i < m && p < k) ? load_elem<EB>(a, cplx_a_index(i, p, rsa, csa, cplx), aligned) : 0;
+                for (int c = 0; c < 4; ++c) v[c] = load_elem<EB>(a, e0 + c, aligned);
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int p = p0 + c;
+                v[c] = (i < m && p < k) ? load_elem<EB>(a, cplx_a_index(i, p, rsa, csa, cplx), aligned) : 0;
+            }
         }
         wm_store<EB, NM>(as + static_cast<int64_t>(i) * kp + p0, plane, v, f, w);
     }
