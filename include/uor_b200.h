@@ -217,7 +217,12 @@ int uor_b200_gemm_complex(uor_b200_dtype elem, uor_b200_dtype out, const uor_b20
 
 /* gemm_float_packed over a Triple (crates/uor-matmul-gemm/src/float.rs:1824)
  * with Linear: C := RNE-once(alpha * exact(A B) + beta * C).
- * elem in {F32, F64}; out in {F32, F64}. */
+ * elem in {F32, F64}; out in {F32, F64}. Also the entry for gemm_float
+ * (float.rs:1761) and gemm_float_bridged (float.rs:1897): their pa/pb, scaled
+ * and scratch offers are caches that never change bytes, so none is passed here,
+ * and the size queries suggested_float_panels / suggested_bridge_scaled
+ * (float.rs:1862-1882) have no device counterpart -- any offer, empty included,
+ * gives these bytes. */
 int uor_b200_gemm_float(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view *a,
                         const uor_b200_view *b, const uor_b200_view_mut *c, int64_t alpha,
                         int64_t beta, const uor_b200_call *call);
