@@ -275,3 +275,38 @@ def test_modular_route_two_reduction_chunks():
     got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, 1, 0)
     assert np.array_equal(got, want)
     assert route.moduli > 0 and route.k_chunks == 2
+
+
+@pytest.mark.parametrize("elem,m,k,n", [(U.F32, 1000, 300, 4096), (U.F64, 1100, 64, 4096)])
+def test_modular_route_tall_products(elem, m, k, n):
+    """Tall, wide products on the modular route (several row tiles of CTA pairs, a ragged
+    last tile): the whole result equals the digit-slice route's bit for bit, and rows
+    spread over the tiles equal the oracle's, under beta != 0 with non-finite values in
+    two rows."""
+    rng = np.random.default_rng(30 + m)
+    dt = FT[elem]
+    if elem == U.F32:
+        a, b = config3(m, k, n)
+        a, b = a.reshape(-1).copy(), b.reshape(-1).copy()
+    else:
+        def draw(count):
+            mant = rng.integers(1 << 52, 1 << 53, size=count, dtype=np.int64).astype(np.float64)
+            return rng.choice([-1.0, 1.0], size=count) * np.ldexp(mant, rng.integers(-30, 31, count) - 52)
+        a, b = draw(m * k), draw(k * n)
+    a[900 * k + 5] = np.inf
+    a[950 * k + 7] = np.nan
+    c0 = rng.standard_normal(m * n).astype(dt)
+    outs = {}
+    for digits in (False, True):
+        c = c0.copy()
+        route = U.Route()
+        U.gemm_float(elem, elem, a, (m, k, k, 1), b, (k, n, n, 1), c, (m, n, n, 1), 3, -2,
+                     route=route, digits=digits)
+        outs[digits] = c.view(UT[elem])
+        assert (route.moduli > 0) != digits
+    assert np.array_equal(outs[False], outs[True])
+    for i in (0, 511, 512, 767, 768, 900, 950, m - 1):
+        w = c0[i * n:(i + 1) * n].copy()
+        orc.gemm_float(View(a, 1, k, k, 1, i * k), View(b, k, n, n, 1), View(w, 1, n, n, 1),
+                       alpha=3, beta=-2)
+        assert np.array_equal(outs[False][i * n:(i + 1) * n], w.view(UT[elem])), i
