@@ -1151,17 +1151,125 @@ __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const
     }
 }
 
+// The encode of S 2^ex from its 32-bit limbs (two's complement, sign extension ext) for
+// alpha 1, rounding to nearest and a normal result: the top nonzero limb and the two below
+// it, shifted so the leading one is bit 95, give the significand, the round bit and the
+// window's sticky bits; the limbs further down only feed the sticky bit. False (nothing
+// stored) when the result would be subnormal, overflow or sit at the element register's
+// lowest bit; encode_mag_fast covers those.
+template <int NL>
+__device__ __forceinline__ bool fm_encode_fast(const uint32_t (&limb)[NL], uint32_t ext, int ex,
+                                               const FxEpi& e, uint64_t& bits) {
+    const bool neg = ext != 0;
+    const uint32_t flip = neg ? ~0u : 0u;
+    uint32_t mag[NL];
+    uint32_t c = neg ? 1u : 0u;
+#pragma unroll
+    for (int l = 0; l < NL; ++l) {
+        const uint64_t sum = static_cast<uint64_t>(limb[l] ^ flip) + c;
+        mag[l] = static_cast<uint32_t>(sum);
+        c = static_cast<uint32_t>(sum >> 32);
+    }
+    int h = -1;
+    uint32_t top = 0, t1 = 0, t2 = 0, below = 0, acc = 0;  // acc: OR of mag[0 .. l - 3]
+#pragma unroll
+    for (int l = 0; l < NL; ++l) {
+        if (mag[l]) {
+            h = l;
+            top = mag[l];
+            t1 = l >= 1 ? mag[l >= 1 ? l - 1 : 0] : 0u;
+            t2 = l >= 2 ? mag[l >= 2 ? l - 2 : 0] : 0u;
+            below = acc;
+        }
+        if (l >= 2) acc |= mag[l >= 2 ? l - 2 : 0];
+    }
+    if (h < 0) {
+        bits = 0;  // exact zero encodes +0
+        return true;
+    }
+    const int lz = __clz(top);
+    const uint32_t w_hi = __funnelshift_l(t1, top, lz);
+    const uint32_t w_mid = __funnelshift_l(t2, t1, lz);
+    const uint32_t w_lo = t2 << lz;
+    const int exp = ex + 32 * h + 31 - lz;  // exponent of the leading one
+    const int MANT = e.out64 ? 52 : 23;
+    const int BIAS = e.out64 ? 1023 : 127;
+    if (exp < 1 - BIAS || exp > BIAS - 1 || exp - MANT <= e.min_exp_e) return false;
+    uint64_t sig;
+    bool rnd, sticky;
+    if (!e.out64) {
+        sig = w_hi >> 8;
+        rnd = ((w_hi >> 7) & 1u) != 0;
+        sticky = ((w_hi & 0x7Fu) | w_mid | w_lo | below) != 0;
+    } else {
+        const uint64_t w64 = (static_cast<uint64_t>(w_hi) << 32) | w_mid;
+        sig = w64 >> 11;
+        rnd = ((w64 >> 10) & 1u) != 0;
+        sticky = ((w_mid & 0x3FFu) | w_lo | below) != 0;
+    }
+    sig += (rnd && (sticky || (sig & 1))) ? 1 : 0;
+    int be = exp + BIAS;
+    if (sig >> (MANT + 1)) {
+        sig >>= 1;
+        ++be;
+    }
+    const uint64_t sgn = neg ? (e.out64 ? 1ull << 63 : 1ull << 31) : 0ull;
+    bits = sgn | (static_cast<uint64_t>(be) << MANT) | (sig & ((1ull << MANT) - 1));
+    return true;
+}
+
+// beta != 0 or non-finite terms: the register form and finish_float.
+template <int NW>
+__device__ __forceinline__ void fm_finish_slow(const uint64_t (&w)[NW], uint64_t ext, int64_t off, int ex,
+                                            int fl0, const FxEpi& e) {
+    Big X;
+#pragma unroll
+    for (int q = 0; q < BW; ++q) X.w[q] = q < NW ? w[q] : ext;
+    int fl = fl0;
+    bool zero_out;
+    if (scale_flags(fl, zero_out, e.alpha)) big_mul_i64(X, e.alpha);
+    if (zero_out) big_zero(X);
+    finish_float(e, off, X, ex, fl);
+}
+
+// A cell's limbs of S (sign extension ext) to its output: the fast encode (beta 0, finite
+// terms) or finish_float.
+template <int NM>
+__device__ __forceinline__ void fm_finish_cell(const uint32_t (&limb)[FmLimbs<NM>::value], uint32_t ext32,
+                                               int64_t off, int ex, int fl0, const FxEpi& e) {
+    constexpr int NL = FmLimbs<NM>::value;
+    constexpr int NW = (NL + 1) / 2 + 2;  // 64-bit words: the value, alpha's 64 bits, sign
+    if (e.beta == 0 && !fl0 && e.alpha == 1 && e.mode == MODE_NEAREST) {
+        uint64_t bits;
+        if (fm_encode_fast<NL>(limb, ext32, ex, e, bits)) {
+            store_float(e.c, e.out64, off, bits);
+            return;
+        }
+    }
+    const uint64_t ext = ext32 ? ~0ull : 0ull;
+    uint64_t w[NW];
+#pragma unroll
+    for (int q = 0; q < NW; ++q) {
+        const uint64_t lo = 2 * q < NL ? limb[2 * q] : ext32;
+        const uint64_t hi = 2 * q + 1 < NL ? limb[2 * q + 1] : ext32;
+        w[q] = lo | hi << 32;
+    }
+    if (e.beta == 0 && !fl0) {
+        store_float(e.c, e.out64, off, encode_signed_scaled<NW>(w, e.alpha, ex, e));
+        return;
+    }
+    fm_finish_slow<NW>(w, ext, off, ex, fl0, e);
+}
+
 // One thread per cell: y_g (stored by the GEMM epilogue when there is one reduction
 // chunk; else rebuilt from the chunks' residues), t, the base-256 columns of X - t M
-// carried into signed 32-bit limbs, then the fast encode (beta 0, finite terms) or
-// finish_float.
+// carried into signed 32-bit limbs, then the encode.
 template <int NM>
 __global__ void __launch_bounds__(256, 4) fm_crt_kernel(const uint8_t* __restrict__ res, int chunks, int m, int n,
                               const int* __restrict__ rlo, const int* __restrict__ clo,
                               const int* __restrict__ rspan, const int* __restrict__ cspan,
                               const uint8_t* __restrict__ flags, FxEpi e, FmParams f) {
     constexpr int NL = FmLimbs<NM>::value;
-    constexpr int NW = (NL + 1) / 2 + 2;   // 64-bit words: the value, alpha's 64 bits, sign
     const size_t total = static_cast<size_t>(m) * n;
     for (GridWalk wk(static_cast<size_t>(n)); wk.idx < total; wk.next()) {
         const size_t idx = wk.idx;
@@ -1175,27 +1283,54 @@ __global__ void __launch_bounds__(256, 4) fm_crt_kernel(const uint8_t* __restric
         uint32_t y[NM];
         fm_load_y<NM>(res, chunks, total, idx, f, y);
         uint32_t limb[NL];
-        const uint64_t ext = fm_crt<NM>(y, f, limb) ? ~0ull : 0ull;
-        uint64_t w[NW];
+        const uint32_t ext = fm_crt<NM>(y, f, limb);
+        fm_finish_cell<NM>(limb, ext, off, rlo[i] + clo[j], fl0, e);
+    }
+}
+
+// The same for one reduction chunk and rows of a multiple of four cells, four cells per
+// thread: one 32-bit load per residue plane covers the four cells' y_g, and two byte_perm
+// per four moduli gather one cell's packed words (the residue planes are modulus-major, the
+// columns want four moduli of one cell per word).
+template <int NM>
+__global__ void __launch_bounds__(256, 3) fm_crt4_kernel(const uint8_t* __restrict__ res, int m, int n,
+                              const int* __restrict__ rlo, const int* __restrict__ clo,
+                              const int* __restrict__ rspan, const int* __restrict__ cspan,
+                              const uint8_t* __restrict__ flags, FxEpi e, FmParams f) {
+    constexpr int NA = (NM + 3) / 4;
+    constexpr int NL = FmLimbs<NM>::value;
+    const size_t total = static_cast<size_t>(m) * n;
+    const size_t quads = total >> 2;
+    for (GridWalk wk(static_cast<size_t>(n >> 2)); wk.idx < quads; wk.next()) {
+        const int i = static_cast<int>(wk.i), j0 = static_cast<int>(wk.j) * 4;
+        const size_t idx0 = wk.idx * 4;
+        uint32_t wq[4 * NA];  // wq[g]: y_g of the four cells, one per byte
 #pragma unroll
-        for (int q = 0; q < NW; ++q) {
-            const uint64_t lo = 2 * q < NL ? limb[2 * q] : static_cast<uint32_t>(ext);
-            const uint64_t hi = 2 * q + 1 < NL ? limb[2 * q + 1] : static_cast<uint32_t>(ext);
-            w[q] = lo | hi << 32;
-        }
-        const int ex = rlo[i] + clo[j];
-        if (e.beta == 0 && !fl0) {
-            store_float(e.c, e.out64, off, encode_signed_scaled<NW>(w, e.alpha, ex, e));
-            continue;
-        }
-        Big X;
+        for (int g = 0; g < 4 * NA; ++g)
+            wq[g] = g < NM ? __ldg(reinterpret_cast<const uint32_t*>(res + static_cast<size_t>(g) * total + idx0)) : 0u;
+        const int li = rlo[i];
+        const bool row_zero = rspan[i] == 0;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+            const int j = j0 + c;
+            const size_t idx = idx0 + c;
+            const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+            const int fl0 = flags ? flags[idx] : 0;
+            if (e.beta == 0 && !fl0 && (row_zero || cspan[j] == 0)) {
+                store_float(e.c, e.out64, off, 0);  // a row or column of zeros: S = 0
+                continue;
+            }
+            // byte c of four words: [w0.c, w1.c] then [w2.c, w3.c], joined
+            const uint32_t sel = static_cast<uint32_t>(c) | (static_cast<uint32_t>(c + 4) << 4);
+            uint32_t ya[NA];
 #pragma unroll
-        for (int q = 0; q < BW; ++q) X.w[q] = q < NW ? w[q] : ext;
-        int fl = fl0;
-        bool zero_out;
-        if (scale_flags(fl, zero_out, e.alpha)) big_mul_i64(X, e.alpha);
-        if (zero_out) big_zero(X);
-        finish_float(e, off, X, ex, fl);
+            for (int a = 0; a < NA; ++a)
+                ya[a] = __byte_perm(__byte_perm(wq[4 * a], wq[4 * a + 1], sel),
+                                    __byte_perm(wq[4 * a + 2], wq[4 * a + 3], sel), 0x5410);
+            uint32_t limb[NL];
+            const uint32_t ext = fm_crt_packed<NM>(ya, f, limb);
+            fm_finish_cell<NM>(limb, ext, off, li + clo[j], fl0, e);
+        }
     }
 }
 
@@ -1227,7 +1362,13 @@ template <int NM>
 static void fm_launch_crt(const uint8_t* res, int chunks, int m, int n, const int* rlo,
                           const int* clo, const int* rspan, const int* cspan, const uint8_t* flags,
                           const FxEpi& e, const FmParams& f, int grid, cudaStream_t s) {
-    fm_crt_kernel<NM><<<grid, 256, 0, s>>>(res, chunks, m, n, rlo, clo, rspan, cspan, flags, e, f);
+    if (chunks == 1 && (n & 3) == 0) {
+        const size_t quads = static_cast<size_t>(m) * n / 4;
+        const int g4 = static_cast<int>((quads + 255) / 256 < 148 * 16 ? (quads + 255) / 256 : 148 * 16);
+        fm_crt4_kernel<NM><<<g4, 256, 0, s>>>(res, m, n, rlo, clo, rspan, cspan, flags, e, f);
+    } else {
+        fm_crt_kernel<NM><<<grid, 256, 0, s>>>(res, chunks, m, n, rlo, clo, rspan, cspan, flags, e, f);
+    }
 }
 
 // ------------------------------------------------------------ direct route

@@ -109,9 +109,10 @@ bool fm_plan_bound(const uint32_t* bound, int limbs, FmParams& f) {
         hb_div(mg, p);
         HBig t = mg;
         const uint32_t mgmod = hb_div(t, p);
-        f.p[g] = static_cast<uint16_t>(p);
-        f.inv[g] = static_cast<uint16_t>(inv_mod(mgmod, p));
+        f.p[g] = p;
+        f.inv[g] = inv_mod(mgmod, p);
         f.magic32[g] = static_cast<uint32_t>(((1ull << 32) + p - 1) / p);
+        for (int b = 0; b < 4; ++b) f.mg[g / 4][b] |= ((f.magic32[g] >> (8 * b)) & 255u) << (8 * (g % 4));
         f.half[g] = p == 256 ? 127u : (p - 1) / 2;
         for (int b = 0; b < nm; ++b) f.md[g / 4][b] |= byte_of(mg, b) << (8 * (g % 4));
     }

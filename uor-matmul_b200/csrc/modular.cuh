@@ -25,9 +25,10 @@ constexpr int FM_MAX = 40;  // moduli (the 40 moduli's product is 291 bits)
 
 struct FmParams {
     int nm;                           // moduli (even)
-    uint16_t p[FM_MAX];
-    uint16_t inv[FM_MAX];             // (M / p_g)^-1 mod p_g
+    uint32_t p[FM_MAX];               // 32-bit words: kernels read them as instruction operands
+    uint32_t inv[FM_MAX];             // (M / p_g)^-1 mod p_g
     uint32_t magic32[FM_MAX];         // ceil(2^32 / p_g)
+    uint32_t mg[FM_MAX / 4][4];       // [a][b]: byte b of ceil(2^32 / p_g) for g = 4a .. 4a + 3
     uint32_t half[FM_MAX];            // (p_g - 1) / 2, and 127 for 256
     uint32_t md[FM_MAX / 4][FM_MAX];  // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
     uint32_t mm[FM_MAX / 4 + 1];      // 32-bit limbs of M (M < 2^(8 nm))
@@ -91,48 +92,63 @@ struct FmLimbs {
     static constexpr int value = (NM + 1 + 3) / 4;
 };
 
-// S from y (two's complement limbs, least significant first); returns the sign extension
-// (0 or ~0) of the limbs above.
+// S from the packed y words ya[a] (byte gi = y_{4a+gi}) as two's complement limbs, least
+// significant first; returns the sign extension (0 or ~0) of the limbs above. t comes from
+// the fixed-point sum in four byte columns of ceil(2^32 / p_g) (F_b below NM 255^2 < 2^22,
+// so F_0 + 2^8 F_1 and F_2 + 2^8 F_3 stay in 32 bits), the same integer as the sum of the
+// products; each limb of X is four base-256 columns joined the same way.
 template <int NM>
-__device__ __forceinline__ uint32_t fm_crt(const uint32_t (&y)[NM], const FmParams& f,
-                                           uint32_t (&limb)[FmLimbs<NM>::value]) {
-    constexpr int NA = (NM + 3) / 4;  // packed words of y
+__device__ __forceinline__ uint32_t fm_crt_packed(const uint32_t (&ya)[(NM + 3) / 4], const FmParams& f,
+                                                  uint32_t (&limb)[FmLimbs<NM>::value]) {
+    constexpr int NA = (NM + 3) / 4;
     constexpr int NL = FmLimbs<NM>::value;
-    uint64_t fx = 0x80000000ull;  // + 1/2 in the 32-bit fixed point
-    uint32_t ya[NA];
+    uint32_t F[4];
 #pragma unroll
-    for (int a = 0; a < NA; ++a) {
-        ya[a] = 0;
+    for (int b = 0; b < 4; ++b) {
+        F[b] = 0;
 #pragma unroll
-        for (int gi = 0; gi < 4; ++gi) {
-            if (4 * a + gi < NM) {
-                ya[a] |= y[4 * a + gi] << (8 * gi);
-                fx += static_cast<uint64_t>(y[4 * a + gi]) * f.magic32[4 * a + gi];
-            }
-        }
+        for (int a = 0; a < NA; ++a) F[b] = __dp4a(ya[a], f.mg[a][b], F[b]);
     }
+    const uint64_t fx = (static_cast<uint64_t>(F[2] + (F[3] << 8)) << 16) + (F[0] + (F[1] << 8)) +
+                        0x80000000ull;  // + 1/2
     const uint32_t t = static_cast<uint32_t>(fx >> 32);
     // Columns X_b (each below NM 255^2 < 2^22), four to a limb, minus t M limb by limb.
     int64_t carry = 0;
 #pragma unroll
     for (int l = 0; l < NL; ++l) {
-        uint64_t v = 0;
+        uint32_t col[4];
 #pragma unroll
         for (int bi = 0; bi < 4; ++bi) {
             const int b = 4 * l + bi;
+            col[bi] = 0;
             if (b < NM) {
-                uint32_t col = 0;
 #pragma unroll
-                for (int a = 0; a < NA; ++a) col = __dp4a(ya[a], f.md[a][b], col);
-                v += static_cast<uint64_t>(col) << (8 * bi);
+                for (int a = 0; a < NA; ++a) col[bi] = __dp4a(ya[a], f.md[a][b], col[bi]);
             }
         }
+        const uint64_t v = (static_cast<uint64_t>(col[2] + (col[3] << 8)) << 16) + (col[0] + (col[1] << 8));
         const uint32_t ml = l < FM_MAX / 4 + 1 ? f.mm[l] : 0u;
         const int64_t sv = static_cast<int64_t>(v) + carry - static_cast<int64_t>(static_cast<uint64_t>(t) * ml);
         limb[l] = static_cast<uint32_t>(sv);
         carry = sv >> 32;
     }
     return carry < 0 ? ~0u : 0u;
+}
+
+// The same from the unpacked y_g.
+template <int NM>
+__device__ __forceinline__ uint32_t fm_crt(const uint32_t (&y)[NM], const FmParams& f,
+                                           uint32_t (&limb)[FmLimbs<NM>::value]) {
+    constexpr int NA = (NM + 3) / 4;
+    uint32_t ya[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+        ya[a] = 0;
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi)
+            if (4 * a + gi < NM) ya[a] |= y[4 * a + gi] << (8 * gi);
+    }
+    return fm_crt_packed<NM>(ya, f, limb);
 }
 
 #define FM_EVEN_COUNTS(X) X(2) X(4) X(6) X(8) X(10) X(12) X(14) X(16) X(18) X(20) X(22) X(24) \
