@@ -1010,57 +1010,63 @@ __device__ __forceinline__ void fm_parts(const FDec& d, int lo, uint64_t& mant, 
 
 // The residues of four elements for all NM moduli, packed four per 32-bit word and stored
 // to dst + g * plane (one word per modulus). W: table words per (shift, modulus).
-template <int NM>
+template <int NM, int W>
 __device__ __forceinline__ void fm_store_residues(int8_t* dst, int64_t plane, const uint64_t (&mant)[4],
                                                   const int (&sh)[4], const bool (&neg)[4],
-                                                  const uint32_t* pw, int W, const FmParams& f) {
+                                                  const uint32_t* pw, const FmParams& f) {
     constexpr int NMP = (NM + 3) / 4 * 4;
-    uint32_t out[NM];
-#pragma unroll
-    for (int g = 0; g < NM; ++g) out[g] = 0;
+    // Modulus-outer: each modulus's constants and each element's coefficient words are read
+    // once for the four elements, and each output word is stored as soon as it is complete.
+    // A zero element reads row 0 and its residue comes out 0 (u = half).
+    uint32_t lo32[4], hi32[4];
+    const uint4* row[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        if (!mant[c]) continue;
-        const uint32_t lo32 = static_cast<uint32_t>(mant[c]);
-        const uint32_t hi32 = static_cast<uint32_t>(mant[c] >> 32);
+        lo32[c] = static_cast<uint32_t>(mant[c]);
+        hi32[c] = static_cast<uint32_t>(mant[c] >> 32);
         // rows 2 sh (positive) and 2 sh + 1 (the coefficients of -2^(sh + 8i))
-        const uint4* row = reinterpret_cast<const uint4*>(pw + (2 * sh[c] + (neg[c] ? 1 : 0)) * W * NMP);
-#pragma unroll
-        for (int g4 = 0; g4 < NMP / 4; ++g4) {
-            const uint4 cw = row[g4];
-            const int gb = 4 * g4;
-            uint32_t u[4] = {__dp4a(lo32, cw.x, f.half[gb < NM ? gb : 0]),
-                             __dp4a(lo32, cw.y, f.half[gb + 1 < NM ? gb + 1 : 0]),
-                             __dp4a(lo32, cw.z, f.half[gb + 2 < NM ? gb + 2 : 0]),
-                             __dp4a(lo32, cw.w, f.half[gb + 3 < NM ? gb + 3 : 0])};
-            if (W == 2) {
-                const uint4 ch = row[NMP / 4 + g4];
-                u[0] = __dp4a(hi32, ch.x, u[0]);
-                u[1] = __dp4a(hi32, ch.y, u[1]);
-                u[2] = __dp4a(hi32, ch.z, u[2]);
-                u[3] = __dp4a(hi32, ch.w, u[3]);
-            }
-#pragma unroll
-            for (int gi = 0; gi < 4; ++gi) {
-                const int g = 4 * g4 + gi;
-                if (g < NM) out[g] = fm_put_byte(out[g], fm_balanced(u[gi], f.p[g], f.magic32[g], f.half[g]), c);
-            }
-        }
+        row[c] = reinterpret_cast<const uint4*>(pw + (2 * sh[c] + (neg[c] ? 1 : 0)) * W * NMP);
     }
 #pragma unroll
-    for (int g = 0; g < NM; ++g) *reinterpret_cast<uint32_t*>(dst + g * plane) = out[g];
+    for (int g4 = 0; g4 < NMP / 4; ++g4) {
+        uint4 cw[4], ch[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            cw[c] = row[c][g4];
+            ch[c] = W == 2 ? row[c][NMP / 4 + g4] : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int gi = 0; gi < 4; ++gi) {
+            const int g = 4 * g4 + gi;
+            if (g >= NM) break;
+            const uint32_t p = f.p[g], mg = f.magic32[g], hf = f.half[g];
+            uint32_t word = 0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t lo = gi == 0 ? cw[c].x : gi == 1 ? cw[c].y : gi == 2 ? cw[c].z : cw[c].w;
+                uint32_t u = __dp4a(lo32[c], lo, hf);
+                if (W == 2) {
+                    const uint32_t hi = gi == 0 ? ch[c].x : gi == 1 ? ch[c].y : gi == 2 ? ch[c].z : ch[c].w;
+                    u = __dp4a(hi32[c], hi, u);
+                }
+                word = fm_put_byte(word, fm_balanced(u, p, mg, hf), c);
+            }
+            *reinterpret_cast<uint32_t*>(dst + g * plane) = word;
+        }
+    }
 }
 
 // A (m x k) -> residue planes As[NM][mp][kp]: four consecutive reduction positions per
 // thread, one 4-byte store per modulus.
-template <int NM>
-__global__ void fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const uint8_t* __restrict__ a,
-                                  int64_t rsa, int64_t csa, bool f64, int m, int k,
+template <int NM, bool F64>
+__global__ void __launch_bounds__(256, 4) fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const uint8_t* __restrict__ a,
+                                  int64_t rsa, int64_t csa, int m, int k,
                                   const int* __restrict__ lo, const uint32_t* __restrict__ pow2,
                                   int shmax, FmParams f) {
     constexpr int NMP = (NM + 3) / 4 * 4;
     extern __shared__ __align__(16) uint32_t pw[];
-    const int W = f64 ? 2 : 1;
+    constexpr bool f64 = F64;
+    constexpr int W = F64 ? 2 : 1;
     // f32 rows with unit column stride on 16-byte boundaries take one vector load per thread
     const bool vec = !f64 && csa == 1 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
                      ((rsa * 4) & 15) == 0;
@@ -1093,22 +1099,23 @@ __global__ void fm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp, const
                 fm_parts(d, li, mant[c], sh[c], neg[c]);
             }
         }
-        fm_store_residues<NM>(as + static_cast<int64_t>(i) * kp + p0, plane, mant, sh, neg, pw, W, f);
+        fm_store_residues<NM, W>(as + static_cast<int64_t>(i) * kp + p0, plane, mant, sh, neg, pw, f);
     }
 }
 
 // B (k x n) -> residue planes Bs[NM][np][kp] (transposed) through a shared tile of 64
 // reduction positions x 32 columns of decoded elements.
-template <int NM>
+template <int NM, bool F64>
 __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const uint8_t* __restrict__ b,
-                                  int64_t rsb, int64_t csb, bool f64, int k, int n,
+                                  int64_t rsb, int64_t csb, int k, int n,
                                   const int* __restrict__ lo, const uint32_t* __restrict__ pow2,
                                   int shmax, FmParams f) {
     constexpr int NMP = (NM + 3) / 4 * 4;
     extern __shared__ __align__(16) uint32_t pw[];
     __shared__ uint64_t tm[32][65];
     __shared__ int ts[32][65];
-    const int W = f64 ? 2 : 1;
+    constexpr bool f64 = F64;
+    constexpr int W = F64 ? 2 : 1;
     fm_fill_pow2(pw, pow2, 2 * shmax * W * NMP);
     const int j0 = blockIdx.x * 32;
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -1144,7 +1151,7 @@ __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const
                     sh[c] = ts[jj][4 * q + c] & ((1 << 30) - 1);
                     neg[c] = (ts[jj][4 * q + c] >> 30) != 0;
                 }
-                fm_store_residues<NM>(bs + static_cast<int64_t>(j) * kp + p, plane, mant, sh, neg, pw, W, f);
+                fm_store_residues<NM, W>(bs + static_cast<int64_t>(j) * kp + p, plane, mant, sh, neg, pw, f);
             }
         }
         __syncthreads();
@@ -1343,19 +1350,21 @@ static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, con
     constexpr int NMP = (NM + 3) / 4 * 4;
     const size_t smem = static_cast<size_t>(shmax) * 2 * NMP * 4 * (f64 ? 2 : 1);
     // The B kernel adds a 25 KB static tile: allow the table's largest size beside it.
-    cudaFuncSetAttribute(fm_slice_a_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
-    cudaFuncSetAttribute(fm_slice_b_kernel<NM>, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
+    auto ka = f64 ? fm_slice_a_kernel<NM, true> : fm_slice_a_kernel<NM, false>;
+    auto kb = f64 ? fm_slice_b_kernel<NM, true> : fm_slice_b_kernel<NM, false>;
+    cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
+    cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, FM_TABLE_MAX);
     const int64_t aquads = static_cast<int64_t>(mp) * (kp / 4);
     const int sgrid = static_cast<int>(aquads / 256 + 1 < 148 * 16 ? aquads / 256 + 1 : 148 * 16);
-    fm_slice_a_kernel<NM><<<sgrid, 256, smem, s>>>(as, mp, kp, a, rsa, csa, f64, m, k, rlo, pw, shmax, f);
+    ka<<<sgrid, 256, smem, s>>>(as, mp, kp, a, rsa, csa, m, k, rlo, pw, shmax, f);
     // Each block copies the coefficient table into shared memory once, so the blocks walk
     // the reduction in strides: about eight blocks per SM in all.
     const int gx = np / 32;
     int gy = (kp + 63) / 64;
     const int gy_cap = 148 * 8 / gx > 1 ? 148 * 8 / gx : 1;
     if (gy > gy_cap) gy = gy_cap;
-    fm_slice_b_kernel<NM><<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), dim3(32, 8), smem, s>>>(
-        bs, np, kp, b, rsb, csb, f64, k, n, clo, pw, shmax, f);
+    kb<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), dim3(32, 8), smem, s>>>(
+        bs, np, kp, b, rsb, csb, k, n, clo, pw, shmax, f);
 }
 
 template <int NM>
