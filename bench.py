@@ -317,7 +317,8 @@ def wl_codec(args, U, torch, rank, sets=3):
          for s in range(sets)]
     table = torch.from_numpy(U.corpus(7, U.CORPUS_I8, 16)).cuda()
     C = torch.empty(m * n, dtype=torch.int32, device="cuda")
-    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=1)
+    # the one-pass nibble decode, then K1 (2048 activation rows: decoded once, not per tile)
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=2)
 
     def step(i, ctx):
         U.coded_gemm(U.I32, A[i % sets], (m, k, k, 1), Q[i % sets], k, n, 2, table, C,

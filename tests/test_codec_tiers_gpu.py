@@ -59,14 +59,18 @@ def test_ternary(orientation, block, cb):
 
 @pytest.mark.parametrize("orientation", [0, 1])
 def test_book(orientation):
-    # the E8 shape Book<256, 8> with u8 codes, and a wider book with u16 codes
-    for (N, block, cb) in [(256, 8, 1), (1000, 4, 2)]:
+    # the E8 shape Book<256, 8> with u8 codes, a wider book with u16 codes, and 16-byte
+    # blocks of a 300-entry book behind an Offset (u16 codes reduced modulo 300)
+    for (N, block, cb, zero) in [(256, 8, 1, 0), (1000, 4, 2, 0), (300, 16, 2, -3)]:
         m, k, n = 130, 256, 192
         table = U.corpus(7, U.CORPUS_I8, N * block)
+        if zero:
+            # decode minus zero must stay i8 (Offset::new)
+            table = np.clip(table, max(-128, -128 + zero), min(127, 127 + zero)).astype(np.int8)
         rows, cols = (k, n) if orientation == 0 else (n, k)
         codes = codes_for(rows, cols, block, cb, 11 + N)
         check(m, k, n, U.TIER_BOOK, codes, orientation, table=table, block=block, code_bytes=cb,
-              seed=N)
+              zero=zero, seed=N)
 
 
 @pytest.mark.parametrize("orientation", [0, 1])

@@ -1,5 +1,6 @@
-"""K5 (codebook decode fused into the tensor-core pipeline) against the oracle's
-coded_gemm / gemm_tabulated restatement."""
+"""K5 (codebook decode fused into the tensor-core pipeline) and, from 512 activation rows
+up, the one-pass nibble decode followed by K1, against the oracle's coded_gemm /
+gemm_tabulated restatement."""
 import numpy as np
 import pytest
 
@@ -70,6 +71,18 @@ def test_fused_nibbles(orientation, shape):
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
+def test_decoded_nibbles_many_rows(orientation):
+    """512 activation rows and more: the codes are decoded once to dense int8 (flat over the
+    code bytes, low nibble first) and K1 runs on them, K-major for the n x k codes."""
+    for m, k, n, out, alpha, beta, N in [(512, 256, 96, U.I32, 1, 0, 16),
+                                         (600, 320, 64, U.I64, 3, -1, 7),
+                                         (1030, 96, 288, U.I8, -2, 5, 16)]:
+        got, want, route = run(m, k, n, 2, N, orientation, out, alpha, beta, seed=m + N)
+        assert np.array_equal(got, want), (m, k, n, out)
+        assert route.kernel == 4 and route.b_layout == 3
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
 @pytest.mark.parametrize("m", [70, 260])  # one CTA per tile / CTA pairs
 def test_short_table_alpha_beta_outputs(orientation, m):
     for out in (U.I8, U.I32, U.I64, U.I128):
@@ -114,7 +127,7 @@ def test_config2_full_size_checksum():
     tc = torch.empty(m * n, dtype=torch.int32, device="cuda")
     route = U.Route()
     U.coded_gemm(U.I32, ta, (m, k, k, 1), tcodes, k, n, 2, ttab, tc, (m, n, n, 1), route=route)
-    assert route.kernel == 4 and route.b_layout == 1
+    assert route.kernel == 4 and route.b_layout == 3  # decoded once, then K1
     # independent decode of the nibbles (low first) for the checksum
     lo = (tcodes & 0xF).long()
     hi = (tcodes >> 4).long()

@@ -37,6 +37,33 @@ __global__ void decode_dense_kernel(int8_t* __restrict__ out, const uint8_t* __r
     }
 }
 
+// Packed<Grid<N>, 2> codes decoded to dense int8 in the coded matrix's own layout: byte b
+// holds elements 2b (low nibble) and 2b + 1, so the map is flat over the code bytes. Sixteen
+// code bytes per thread through the 16-entry register table (dec8), 32 bytes stored.
+__global__ void decode_nibbles_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
+                                      size_t bytes, uint32_t t0, uint32_t t1, uint32_t t2,
+                                      uint32_t t3) {
+    const size_t groups = bytes / 16;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t gi = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; gi < groups; gi += stride) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(codes) + gi);
+        const uint2 a = dec8(w.x, t0, t1, t2, t3), b = dec8(w.y, t0, t1, t2, t3);
+        const uint2 c = dec8(w.z, t0, t1, t2, t3), d = dec8(w.w, t0, t1, t2, t3);
+        uint4* o = reinterpret_cast<uint4*>(out + 32 * gi);
+        o[0] = make_uint4(a.x, a.y, b.x, b.y);
+        o[1] = make_uint4(c.x, c.y, d.x, d.y);
+    }
+    // the last bytes % 16 code bytes, one byte per thread
+    const size_t tail = bytes - 16 * groups;
+    const size_t t = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+    if (t < tail) {
+        const uint32_t code = codes[16 * groups + t];
+        const uint2 v = dec8(code, t0, t1, t2, t3);
+        out[32 * groups + 2 * t] = static_cast<int8_t>(v.x & 0xFF);
+        out[32 * groups + 2 * t + 1] = static_cast<int8_t>((v.x >> 8) & 0xFF);
+    }
+}
+
 int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* codes,
                  size_t codes_len, size_t k, size_t n, uint32_t per_byte, const int8_t* table,
                  size_t table_len, const uor_b200_view_mut* c, int64_t alpha, int64_t beta,
@@ -109,7 +136,33 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool fused = per_byte == 2 && table_len <= 16 && k > 0 &&
                        (orientation == 0 ? (n % 32 == 0) : (k % 32 == 0)) &&
                        (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
-    if (!fused) {
+    // From two activation tiles of rows up, decoding every weight once into HBM and running
+    // K1 beats decoding it again for each tile inside K5 (K5 is bound by the decode's issue
+    // slots, not by its tensor pipe).
+    if (fused && m >= 2 * (size_t)K5_BN) {
+        uint8_t* dense = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, k * n + 256, &st));
+        if (!dense) return st;
+        uint32_t tw[4];
+        for (int w = 0; w < 4; ++w) {
+            tw[w] = 0;
+            for (int bpos = 0; bpos < 4; ++bpos)
+                tw[w] |= (uint32_t)(uint8_t)tab[(4 * w + bpos) % table_len] << (8 * bpos);
+        }
+        const size_t groups = codes_len / 16;
+        const int grid = (int)((groups + 255) / 256 < 148 * 8 ? (groups + 255) / 256 + 1 : 148 * 8);
+        decode_nibbles_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<int8_t*>(dense), dcodes, codes_len,
+                                                   tw[0], tw[1], tw[2], tw[3]);
+        if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        // orientation 0: dense k x n row-major; 1: n x k row-major, i.e. B K-major
+        const ptrdiff_t rsb = orientation == 0 ? (ptrdiff_t)n : 1;
+        const ptrdiff_t csb = orientation == 0 ? 1 : (ptrdiff_t)k;
+        st = run_i8_gemm(ctx, reinterpret_cast<const int8_t*>(da), A.rs, A.cs,
+                         reinterpret_cast<const int8_t*>(dense), rsb, csb, cs.dev_origin, C.rs, C.cs,
+                         m, k, n, epi, route);
+        if (st) return st;
+        route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
+        route->b_layout = 3;  // decoded to a dense workspace first
+    } else if (!fused) {
         // Off the fused path (P != 2, N > 16, or code rows the TMA cannot address):
         // decode to a dense row-major k x n int8 matrix in the auxiliary slot, then K1.
         uint8_t* buf = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, 256 + k * n, &st));
@@ -278,6 +331,23 @@ __global__ void decode_block_kernel(int8_t* __restrict__ out, const uint8_t* __r
     }
 }
 
+// Book codes whose block is a whole number of 8-byte words, against a book already minus
+// `zero`: each code's row copied word by word (the E8 codebook: one 8-byte load, one store).
+__global__ void decode_book8_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
+                                    const int8_t* __restrict__ table, uint32_t N, int blk, int cb,
+                                    int64_t ncodes) {
+    const int words = blk / 8;
+    for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < ncodes;
+         t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t code = cb == 1 ? codes[t]
+                                      : (static_cast<uint32_t>(codes[2 * t]) | (static_cast<uint32_t>(codes[2 * t + 1]) << 8));
+        const uint32_t r = code < N ? code : code % N;  // Book::decode: table[code % N]
+        const uint2* src = reinterpret_cast<const uint2*>(table + static_cast<int64_t>(r) * blk);
+        uint2* dst = reinterpret_cast<uint2*>(out + t * blk);
+        for (int e = 0; e < words; ++e) dst[e] = __ldg(src + e);
+    }
+}
+
 int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_codec* codec,
                  const uint8_t* codes, size_t codes_len, size_t k, size_t n, uint32_t orientation,
                  const uor_b200_view_mut* c, int64_t alpha, int64_t beta,
@@ -347,10 +417,11 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
     if (m > (size_t)INT_MAX / 2 || n > (size_t)INT_MAX / 2 || k > (size_t)INT_MAX / 2)
         return UOR_B200_UNSUPPORTED;
     if (codes_len && !codes) return UOR_B200_INVALID_ARGUMENT;
+    std::vector<int8_t> book;
     if (tier == UOR_B200_TIER_BOOK) {
         // Offset's bound over the whole book
         int8_t lo = 127, hi = -128;
-        std::vector<int8_t> book(tbytes);
+        book.resize(tbytes);
         if (dev) {
             if (cudaMemcpy(book.data(), codec->table, tbytes, cudaMemcpyDeviceToHost) != cudaSuccess)
                 return UOR_B200_DEVICE_ERROR;
@@ -381,14 +452,27 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
     uint8_t* buf = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, tb + k * n + 256, &st));
     if (!buf) return st;
     const int8_t* dtable = nullptr;
-    if (tbytes) {
+    // Books of whole 8-byte words take the word-copy decode from the book minus zero.
+    const bool book8 = tier == UOR_B200_TIER_BOOK && blk % 8 == 0;
+    if (book8) {
+        for (auto& v : book) v = static_cast<int8_t>(v - zero);
+        if (cudaMemcpyAsync(buf, book.data(), tbytes, cudaMemcpyHostToDevice, s) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+        dtable = reinterpret_cast<const int8_t*>(buf);
+    } else if (tbytes) {
         if (cudaMemcpyAsync(buf, codec->table, tbytes,
                             dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s) != cudaSuccess)
             return UOR_B200_DEVICE_ERROR;
         dtable = reinterpret_cast<const int8_t*>(buf);
     }
     int8_t* dense = reinterpret_cast<int8_t*>(buf + tb);
-    if (k) {
+    if (k && book8) {
+        const int64_t ncodes = (int64_t)rows * (int64_t)(cols / blk);
+        const int grid = (int)((ncodes + 255) / 256 < 148 * 16 ? (ncodes + 255) / 256 : 148 * 16);
+        decode_book8_kernel<<<grid, 256, 0, s>>>(dense, dcodes, dtable, (uint32_t)N, (int)blk, (int)cb,
+                                                 ncodes);
+        if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    } else if (k) {
         const int64_t total = (int64_t)k * n;
         const int grid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
         // dense holds the coded matrix itself: k x n (orientation 0) or n x k (1)

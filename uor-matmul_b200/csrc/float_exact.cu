@@ -987,7 +987,10 @@ __global__ void fx_fix_kernel(const uint32_t* __restrict__ list, const uint32_t*
 constexpr int FM_TABLE_MAX = 160 * 1024;
 
 // The table of words [2^sh, 2^(sh+8), 2^(sh+16), 0] mod p_g (f32 significands, W = 1), or
-// two words covering 2^(sh + 8i) for i < 8 (f64, W = 2), row sh holding W x NMP words.
+// two words covering 2^(sh + 8i) for i < 8 (f64, W = 2), in 16-byte columns of four moduli
+// (column w NMP/4 + g/4 holds word w of moduli 4(g/4) .. 4(g/4) + 3), each column the rows
+// 2 sh (positive) and 2 sh + 1 (negative) one after another: lanes reading different rows
+// of one column spread over all the banks.
 __device__ __forceinline__ void fm_fill_pow2(uint32_t* pw, const uint32_t* __restrict__ table,
                                              int words) {
     for (int idx = threadIdx.y * blockDim.x + threadIdx.x; idx < words;
@@ -1013,27 +1016,28 @@ __device__ __forceinline__ void fm_parts(const FDec& d, int lo, uint64_t& mant, 
 template <int NM, int W>
 __device__ __forceinline__ void fm_store_residues(int8_t* dst, int64_t plane, const uint64_t (&mant)[4],
                                                   const int (&sh)[4], const bool (&neg)[4],
-                                                  const uint32_t* pw, const FmParams& f) {
+                                                  const uint32_t* pw, int rows, const FmParams& f) {
     constexpr int NMP = (NM + 3) / 4 * 4;
     // Modulus-outer: each modulus's constants and each element's coefficient words are read
     // once for the four elements, and each output word is stored as soon as it is complete.
     // A zero element reads row 0 and its residue comes out 0 (u = half).
     uint32_t lo32[4], hi32[4];
-    const uint4* row[4];
+    int row[4];
+    const uint4* tab = reinterpret_cast<const uint4*>(pw);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         lo32[c] = static_cast<uint32_t>(mant[c]);
         hi32[c] = static_cast<uint32_t>(mant[c] >> 32);
         // rows 2 sh (positive) and 2 sh + 1 (the coefficients of -2^(sh + 8i))
-        row[c] = reinterpret_cast<const uint4*>(pw + (2 * sh[c] + (neg[c] ? 1 : 0)) * W * NMP);
+        row[c] = 2 * sh[c] + (neg[c] ? 1 : 0);
     }
 #pragma unroll
     for (int g4 = 0; g4 < NMP / 4; ++g4) {
         uint4 cw[4], ch[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            cw[c] = row[c][g4];
-            ch[c] = W == 2 ? row[c][NMP / 4 + g4] : make_uint4(0, 0, 0, 0);
+            cw[c] = tab[g4 * rows + row[c]];
+            ch[c] = W == 2 ? tab[(NMP / 4 + g4) * rows + row[c]] : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int gi = 0; gi < 4; ++gi) {
@@ -1099,7 +1103,7 @@ __global__ void __launch_bounds__(256, 4) fm_slice_a_kernel(int8_t* __restrict__
                 fm_parts(d, li, mant[c], sh[c], neg[c]);
             }
         }
-        fm_store_residues<NM, W>(as + static_cast<int64_t>(i) * kp + p0, plane, mant, sh, neg, pw, f);
+        fm_store_residues<NM, W>(as + static_cast<int64_t>(i) * kp + p0, plane, mant, sh, neg, pw, 2 * shmax, f);
     }
 }
 
@@ -1151,7 +1155,7 @@ __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const
                     sh[c] = ts[jj][4 * q + c] & ((1 << 30) - 1);
                     neg[c] = (ts[jj][4 * q + c] >> 30) != 0;
                 }
-                fm_store_residues<NM, W>(bs + static_cast<int64_t>(j) * kp + p, plane, mant, sh, neg, pw, f);
+                fm_store_residues<NM, W>(bs + static_cast<int64_t>(j) * kp + p, plane, mant, sh, neg, pw, 2 * shmax, f);
             }
         }
         __syncthreads();
@@ -1628,7 +1632,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         uint8_t* flags = any_nf ? res + res_bytes : nullptr;
         uint32_t* pw = reinterpret_cast<uint32_t*>(res + res_bytes + flag_bytes);
         {
-            // row 2 sh + s, word w, modulus g: bytes i of (-1)^s 2^(sh + 8 (4 w + i)) mod p_g
+            // column (w, g / 4), row 2 sh + s, word g % 4: bytes i of (-1)^s 2^(sh + 8 (4 w + i)) mod p_g
             std::vector<uint32_t> tab((size_t)shmax * 2 * W * nmp, 0);
             for (int gg = 0; gg < nm; ++gg) {
                 const uint32_t pg = fm.p[gg];
@@ -1637,8 +1641,9 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
                     uint32_t c = v;
                     for (int bi = 0; bi < 4 * W; ++bi) {
                         const uint32_t cn = (pg - c) % pg;
-                        tab[((size_t)(2 * sh) * W + bi / 4) * nmp + gg] |= c << (8 * (bi % 4));
-                        tab[((size_t)(2 * sh + 1) * W + bi / 4) * nmp + gg] |= cn << (8 * (bi % 4));
+                        const size_t col = (size_t)(bi / 4) * (nmp / 4) + gg / 4;  // 16-byte column
+                        tab[((col * 2 * shmax + 2 * sh) * 4) + gg % 4] |= c << (8 * (bi % 4));
+                        tab[((col * 2 * shmax + 2 * sh + 1) * 4) + gg % 4] |= cn << (8 * (bi % 4));
                         c = c * 256 % pg;
                     }
                     v = v * 2 % pg;

@@ -31,21 +31,6 @@ __device__ __forceinline__ void k5_tile(int t, const K5Params& p, int& tj, int& 
     ti = r / rows;
 }
 
-// Eight nibbles (first element lowest) -> eight table bytes (.x: elements 0-3, .y: 4-7).
-// __byte_perm reads three bits of each selector nibble (and only the low 16 bits of the
-// selector), so the code nibbles themselves pick among table[0..7] (t0:t1) and
-// table[8..15] (t2:t3); a third permute takes, byte by byte, the half that the
-// nibble's bit 3 names.
-__device__ __forceinline__ uint2 dec8(uint32_t w, uint32_t t0, uint32_t t1, uint32_t t2,
-                                     uint32_t t3) {
-    const uint32_t pick = ((w >> 1) & 0x44444444u) | 0x32103210u;
-    const uint32_t wh = w >> 16, ph = pick >> 16;
-    uint2 r;
-    r.x = __byte_perm(__byte_perm(t0, t1, w), __byte_perm(t2, t3, w), pick);
-    r.y = __byte_perm(__byte_perm(t0, t1, wh), __byte_perm(t2, t3, wh), ph);
-    return r;
-}
-
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
