@@ -42,7 +42,18 @@ __global__ void decode_dense_kernel(int8_t* __restrict__ out, const uint8_t* __r
 // code bytes per thread through the 16-entry register table (dec8), 32 bytes stored.
 __global__ void decode_nibbles_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
                                       size_t bytes, uint32_t t0, uint32_t t1, uint32_t t2,
-                                      uint32_t t3) {
+                                      uint32_t t3, const int8_t* __restrict__ dtab, int N) {
+    if (dtab) {  // the table in device memory: the register words table[v % N], v < 16
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            w[q] = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                w[q] |= static_cast<uint32_t>(static_cast<uint8_t>(__ldg(dtab + (4 * q + b) % N))) << (8 * b);
+        }
+        t0 = w[0], t1 = w[1], t2 = w[2], t3 = w[3];
+    }
     const size_t groups = bytes / 16;
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t gi = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; gi < groups; gi += stride) {
@@ -109,16 +120,6 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
     cudaStream_t s = ctx->stream;
 
-    // The 16-entry effective table the fused decode uses: table[v % N].
-    int8_t tab[256];
-    const size_t tl = table_len < 256 ? table_len : 256;
-    if (dev && !table_on_host) {
-        if (cudaMemcpy(tab, table, tl, cudaMemcpyDeviceToHost) != cudaSuccess)
-            return UOR_B200_DEVICE_ERROR;
-    } else {
-        std::memcpy(tab, table, tl);
-    }
-
     const uint8_t* da = nullptr;
     OutStage cs;
     if ((st = stage_in(ctx, SLOT_A, A, dev, &da))) return st;
@@ -136,22 +137,34 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool fused = per_byte == 2 && table_len <= 16 && k > 0 &&
                        (orientation == 0 ? (n % 32 == 0) : (k % 32 == 0)) &&
                        (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
+    const bool decode_once = fused && m >= 2 * (size_t)K5_BN;
+    // The 16-entry effective table the fused decode uses: table[v % N]; a device table on
+    // the decode-once route is read by the decode kernel itself (no host round trip).
+    const bool table_in_kernel = decode_once && dev && !table_on_host;
+    int8_t tab[256];
+    const size_t tl = table_len < 256 ? table_len : 256;
+    if (dev && !table_on_host) {
+        if (!table_in_kernel && cudaMemcpy(tab, table, tl, cudaMemcpyDeviceToHost) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+    } else {
+        std::memcpy(tab, table, tl);
+    }
     // From two activation tiles of rows up, decoding every weight once into HBM and running
     // K1 beats decoding it again for each tile inside K5 (K5 is bound by the decode's issue
     // slots, not by its tensor pipe).
-    if (fused && m >= 2 * (size_t)K5_BN) {
+    if (decode_once) {
         uint8_t* dense = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, k * n + 256, &st));
         if (!dense) return st;
-        uint32_t tw[4];
-        for (int w = 0; w < 4; ++w) {
-            tw[w] = 0;
-            for (int bpos = 0; bpos < 4; ++bpos)
-                tw[w] |= (uint32_t)(uint8_t)tab[(4 * w + bpos) % table_len] << (8 * bpos);
-        }
+        uint32_t tw[4] = {0, 0, 0, 0};
+        if (!table_in_kernel)
+            for (int w = 0; w < 4; ++w)
+                for (int bpos = 0; bpos < 4; ++bpos)
+                    tw[w] |= (uint32_t)(uint8_t)tab[(4 * w + bpos) % table_len] << (8 * bpos);
         const size_t groups = codes_len / 16;
         const int grid = (int)((groups + 255) / 256 < 148 * 8 ? (groups + 255) / 256 + 1 : 148 * 8);
         decode_nibbles_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<int8_t*>(dense), dcodes, codes_len,
-                                                   tw[0], tw[1], tw[2], tw[3]);
+                                                   tw[0], tw[1], tw[2], tw[3],
+                                                   table_in_kernel ? table : nullptr, (int)table_len);
         if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
         // orientation 0: dense k x n row-major; 1: n x k row-major, i.e. B K-major
         const ptrdiff_t rsb = orientation == 0 ? (ptrdiff_t)n : 1;
@@ -418,8 +431,8 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
         return UOR_B200_UNSUPPORTED;
     if (codes_len && !codes) return UOR_B200_INVALID_ARGUMENT;
     std::vector<int8_t> book;
-    if (tier == UOR_B200_TIER_BOOK) {
-        // Offset's bound over the whole book
+    if (tier == UOR_B200_TIER_BOOK && zero != 0) {
+        // Offset's bound over the whole book (with zero 0 every i8 entry fits)
         int8_t lo = 127, hi = -128;
         book.resize(tbytes);
         if (dev) {
@@ -454,7 +467,7 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
     const int8_t* dtable = nullptr;
     // Books of whole 8-byte words take the word-copy decode from the book minus zero.
     const bool book8 = tier == UOR_B200_TIER_BOOK && blk % 8 == 0;
-    if (book8) {
+    if (book8 && zero != 0) {
         for (auto& v : book) v = static_cast<int8_t>(v - zero);
         if (cudaMemcpyAsync(buf, book.data(), tbytes, cudaMemcpyHostToDevice, s) != cudaSuccess)
             return UOR_B200_DEVICE_ERROR;
