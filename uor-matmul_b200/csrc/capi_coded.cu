@@ -55,14 +55,26 @@ __global__ void decode_nibbles_kernel(int8_t* __restrict__ out, const uint8_t* _
         t0 = w[0], t1 = w[1], t2 = w[2], t3 = w[3];
     }
     const size_t groups = bytes / 16;
-    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-    for (size_t gi = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; gi < groups; gi += stride) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(codes) + gi);
-        const uint2 a = dec8(w.x, t0, t1, t2, t3), b = dec8(w.y, t0, t1, t2, t3);
-        const uint2 c = dec8(w.z, t0, t1, t2, t3), d = dec8(w.w, t0, t1, t2, t3);
-        uint4* o = reinterpret_cast<uint4*>(out + 32 * gi);
-        o[0] = make_uint4(a.x, a.y, b.x, b.y);
-        o[1] = make_uint4(c.x, c.y, d.x, d.y);
+    const size_t nt = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t tid = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+    // four groups in flight per thread, each load coalesced across the warp
+    for (size_t g0 = tid; g0 < groups; g0 += 4 * nt) {
+        uint4 w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const size_t gi = g0 + u * nt;
+            w[u] = gi < groups ? __ldg(reinterpret_cast<const uint4*>(codes) + gi) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const size_t gi = g0 + u * nt;
+            if (gi >= groups) break;
+            const uint2 a = dec8(w[u].x, t0, t1, t2, t3), b = dec8(w[u].y, t0, t1, t2, t3);
+            const uint2 c = dec8(w[u].z, t0, t1, t2, t3), d = dec8(w[u].w, t0, t1, t2, t3);
+            uint4* o = reinterpret_cast<uint4*>(out + 32 * gi);
+            o[0] = make_uint4(a.x, a.y, b.x, b.y);
+            o[1] = make_uint4(c.x, c.y, d.x, d.y);
+        }
     }
     // the last bytes % 16 code bytes, one byte per thread
     const size_t tail = bytes - 16 * groups;
@@ -361,6 +373,29 @@ __global__ void decode_book8_kernel(int8_t* __restrict__ out, const uint8_t* __r
     }
 }
 
+// The E8 shape (8-byte codewords, u8 codes, N = 256 so code % N is the code): eight codes
+// per thread from one 8-byte load, their codewords from the book in shared memory, 64 bytes
+// stored. ncodes % 8 == 0.
+__global__ void decode_book8_u8_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
+                                       const int8_t* __restrict__ table, int64_t ncodes) {
+    __shared__ uint2 book[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) book[i] = __ldg(reinterpret_cast<const uint2*>(table) + i);
+    __syncthreads();
+    const int64_t groups = ncodes / 8;
+    for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < groups;
+         gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint2 c = __ldg(reinterpret_cast<const uint2*>(codes) + gi);
+        uint4* o = reinterpret_cast<uint4*>(out + 64 * gi);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t word = q < 2 ? c.x : c.y;
+            const int sh = 16 * (q & 1);
+            const uint2 e0 = book[(word >> sh) & 255u], e1 = book[(word >> (sh + 8)) & 255u];
+            o[q] = make_uint4(e0.x, e0.y, e1.x, e1.y);
+        }
+    }
+}
+
 int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_codec* codec,
                  const uint8_t* codes, size_t codes_len, size_t k, size_t n, uint32_t orientation,
                  const uor_b200_view_mut* c, int64_t alpha, int64_t beta,
@@ -482,8 +517,14 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
     if (k && book8) {
         const int64_t ncodes = (int64_t)rows * (int64_t)(cols / blk);
         const int grid = (int)((ncodes + 255) / 256 < 148 * 16 ? (ncodes + 255) / 256 : 148 * 16);
-        decode_book8_kernel<<<grid, 256, 0, s>>>(dense, dcodes, dtable, (uint32_t)N, (int)blk, (int)cb,
-                                                 ncodes);
+        if (blk == 8 && cb == 1 && N == 256 && ncodes % 8 == 0 && (reinterpret_cast<uintptr_t>(dcodes) & 7) == 0) {
+            const int64_t groups = ncodes / 8;
+            const int g8 = (int)((groups + 255) / 256 < 148 * 8 ? (groups + 255) / 256 : 148 * 8);
+            decode_book8_u8_kernel<<<g8, 256, 0, s>>>(dense, dcodes, dtable, ncodes);
+        } else {
+            decode_book8_kernel<<<grid, 256, 0, s>>>(dense, dcodes, dtable, (uint32_t)N, (int)blk, (int)cb,
+                                                     ncodes);
+        }
         if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
     } else if (k) {
         const int64_t total = (int64_t)k * n;
