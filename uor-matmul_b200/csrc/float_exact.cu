@@ -478,6 +478,21 @@ __device__ void finish_float(const FxEpi& e, int64_t off, Big& X, int ex, int fl
 // collects SPAN_CAP - (smallest nonzero span), gmax[0] the largest span.
 constexpr int SPAN_CAP = 1 << 20;
 
+// One f32 element's part of a row's or column's statistics from its bit pattern: the same
+// exponents fdecode gives (bit 0 of the odd part, leading one), in 32-bit arithmetic.
+__device__ __forceinline__ void fx_stat32(uint32_t bits, int& l, int& h, int& f) {
+    const uint32_t biased = (bits >> 23) & 0xFFu, frac = bits & 0x7FFFFFu;
+    if (biased == 0xFFu) {
+        f = 1;
+        return;
+    }
+    const uint32_t mant = biased ? (frac | 0x800000u) : frac;
+    if (!mant) return;
+    const int e = (biased ? static_cast<int>(biased) : 1) - 150;
+    l = min(l, e + __ffs(static_cast<int>(mant)) - 1);
+    h = max(h, e + 31 - __clz(static_cast<int>(mant)));
+}
+
 __global__ void fx_rows_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64_t csa, int m,
                                int k, bool f64, int* __restrict__ lo, int* __restrict__ span,
                                uint8_t* __restrict__ nf, int* __restrict__ gmax) {
@@ -485,7 +500,22 @@ __global__ void fx_rows_kernel(const uint8_t* __restrict__ a, int64_t rsa, int64
     const int lane = threadIdx.x & 31;
     if (warp >= m) return;
     int l = INT_MAX, h = INT_MIN, f = 0;
-    for (int p = lane; p < k; p += 32) {
+    // f32 rows of unit stride on 16-byte boundaries: four elements per load, four loads
+    // in flight per lane
+    const bool vec = !f64 && csa == 1 && (k & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(a) | static_cast<uintptr_t>(rsa * 4)) & 15) == 0;
+    if (vec) {
+        const uint4* row = reinterpret_cast<const uint4*>(a + static_cast<int64_t>(warp) * rsa * 4);
+#pragma unroll 4
+        for (int q = lane; q < (k >> 2); q += 32) {
+            const uint4 v = __ldg(row + q);
+            fx_stat32(v.x, l, h, f);
+            fx_stat32(v.y, l, h, f);
+            fx_stat32(v.z, l, h, f);
+            fx_stat32(v.w, l, h, f);
+        }
+    }
+    for (int p = vec ? k : lane; p < k; p += 32) {
         const FDec d = fdecode(a, static_cast<int64_t>(warp) * rsa + static_cast<int64_t>(p) * csa, f64);
         if (d.kind != 0) f = 1;
         else if (d.mant) {
@@ -551,6 +581,87 @@ __global__ void fx_cols_kernel(const uint8_t* __restrict__ b, int64_t rsb, int64
             atomicMax(&gmax[4], SPAN_CAP - (h - l + 1));
         }
         if (f) atomicOr(&gmax[2], 1);
+    }
+}
+
+// f32 columns of a row-major B with rows on 16-byte boundaries: 128 columns by a range of
+// rows per block of 32 x 8 threads, lane x reading columns j0 + 4x .. j0 + 4x + 3 as one
+// 16-byte load, warp y rows y, y + 8, ...; the block's partial minimum / maximum / flag per
+// column meet in shared memory and then in the per-column words cl, ch, cf by atomics
+// (cl starts at FX_CL0 = 0x7F7F7F7F, ch at 0x80808080, both beyond any exponent), which
+// fx_cols_finish turns into lo, span, nf.
+constexpr int FX_CL0 = 0x7F7F7F7F;
+
+__global__ void fx_cols4_kernel(const uint8_t* __restrict__ b, int64_t rsb, int k, int n,
+                                int rows_per_block, int* __restrict__ cl, int* __restrict__ ch,
+                                int* __restrict__ cf) {
+    __shared__ int sl[8][128], sh[8][128], sf[8][128];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int j = blockIdx.x * 128 + 4 * tx;
+    const int p0 = blockIdx.y * rows_per_block;
+    const int p1 = min(k, p0 + rows_per_block);
+    int l[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX}, h[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN};
+    int f[4] = {0, 0, 0, 0};
+    if (j < n) {
+#pragma unroll 4
+        for (int p = p0 + ty; p < p1; p += 8) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(b + (static_cast<int64_t>(p) * rsb + j) * 4));
+            fx_stat32(v.x, l[0], h[0], f[0]);
+            fx_stat32(v.y, l[1], h[1], f[1]);
+            fx_stat32(v.z, l[2], h[2], f[2]);
+            fx_stat32(v.w, l[3], h[3], f[3]);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        sl[ty][4 * tx + c] = l[c];
+        sh[ty][4 * tx + c] = h[c];
+        sf[ty][4 * tx + c] = f[c];
+    }
+    __syncthreads();
+    const int t = ty * 32 + tx;
+    if (t < 128) {
+        int L = INT_MAX, H = INT_MIN, F = 0;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            L = min(L, sl[r][t]);
+            H = max(H, sh[r][t]);
+            F |= sf[r][t];
+        }
+        const int jj = blockIdx.x * 128 + t;
+        if (jj < n) {
+            if (L != INT_MAX) {
+                atomicMin(cl + jj, L);
+                atomicMax(ch + jj, H);
+            }
+            if (F) atomicOr(cf + jj, 1);
+        }
+    }
+}
+
+__global__ void fx_cols_finish(int n, const int* __restrict__ cl, const int* __restrict__ ch,
+                               const int* __restrict__ cf, int* __restrict__ lo,
+                               int* __restrict__ span, uint8_t* __restrict__ nf,
+                               int* __restrict__ gmax) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool in = j < n;
+    const int l = in ? cl[j] : FX_CL0;
+    const bool any = l != FX_CL0;
+    const int sp = any ? ch[j] - l + 1 : 0;
+    const int fl = in ? cf[j] : 0;
+    if (in) {
+        lo[j] = any ? l : 0;
+        span[j] = sp;
+        nf[j] = static_cast<uint8_t>(fl != 0);
+    }
+    // one atomic per warp for each global word
+    const int mspan = __reduce_max_sync(0xffffffffu, any ? sp : 0);
+    const int mcap = __reduce_max_sync(0xffffffffu, any ? SPAN_CAP - sp : 0);
+    const int mf = __reduce_or_sync(0xffffffffu, fl != 0 ? 1 : 0);
+    if ((threadIdx.x & 31) == 0) {
+        if (mspan) atomicMax(&gmax[1], mspan);
+        if (mcap) atomicMax(&gmax[4], mcap);
+        if (mf) atomicOr(&gmax[2], 1);
     }
 }
 
@@ -1548,7 +1659,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
 
     // ---- analysis: per-row / per-column exponent spans and non-finite markers
     int st = UOR_B200_OK;
-    const size_t an_bytes = 2 * rup(m * 4, 256) + 2 * rup(n * 4, 256) + rup(m, 256) + rup(n, 256) + 256;
+    const size_t an_bytes = 2 * rup(m * 4, 256) + 5 * rup(n * 4, 256) + rup(m, 256) + rup(n, 256) + 256;
     uint8_t* an = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, an_bytes, &st));
     if (!an) return st;
     int* rlo = reinterpret_cast<int*>(an);
@@ -1562,8 +1673,29 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
     if (k > 0) {
         fx_rows_kernel<<<(int)((m * 32 + 255) / 256), 256, 0, s>>>(a, rsa, csa, (int)m, (int)k, e64,
                                                                    rlo, rspan, rnf, gmax);
-        fx_cols_kernel<<<(int)((n + 31) / 32), dim3(32, 32), 0, s>>>(b, rsb, csb, (int)k, (int)n,
-                                                                      e64, clo, cspan, cnf, gmax);
+        const bool cvec = !e64 && csb == 1 && (n & 3) == 0 &&
+                          ((reinterpret_cast<uintptr_t>(b) | static_cast<uintptr_t>(rsb * 4)) & 15) == 0;
+        if (cvec) {
+            int* cl = reinterpret_cast<int*>(gmax + 64);
+            int* ch = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(cl) + rup(n * 4, 256));
+            int* cf = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ch) + rup(n * 4, 256));
+            if (cudaMemsetAsync(cl, 0x7F, n * 4, s) != cudaSuccess ||
+                cudaMemsetAsync(ch, 0x80, n * 4, s) != cudaSuccess ||
+                cudaMemsetAsync(cf, 0, n * 4, s) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+            const int gx = (int)((n + 127) / 128);
+            int gy = 148 * 8 / gx;
+            const int gy_max = (int)((k + 63) / 64);
+            gy = gy < 1 ? 1 : gy > gy_max ? gy_max : gy;
+            const int rows = (int)(((k + gy - 1) / gy + 7) / 8 * 8);
+            gy = (int)((k + rows - 1) / rows);
+            fx_cols4_kernel<<<dim3((unsigned)gx, (unsigned)gy), dim3(32, 8), 0, s>>>(b, rsb, (int)k, (int)n,
+                                                                                     rows, cl, ch, cf);
+            fx_cols_finish<<<(int)((n + 255) / 256), 256, 0, s>>>((int)n, cl, ch, cf, clo, cspan, cnf, gmax);
+        } else {
+            fx_cols_kernel<<<(int)((n + 31) / 32), dim3(32, 32), 0, s>>>(b, rsb, csb, (int)k, (int)n,
+                                                                          e64, clo, cspan, cnf, gmax);
+        }
     } else {
         cudaMemsetAsync(rlo, 0, m * 4, s);
         cudaMemsetAsync(clo, 0, n * 4, s);
