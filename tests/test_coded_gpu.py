@@ -83,6 +83,28 @@ def test_decoded_nibbles_many_rows(orientation):
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
+def test_decoded_nibbles_device_table(orientation):
+    """Device pointers on the decode-once route: the decode kernel builds the register table
+    from the device table itself (a 7-entry book, so table[v % 7])."""
+    m, k, n, N = 640, 192, 160, 7
+    rng = np.random.default_rng(70 + orientation)
+    a = rng.integers(-128, 128, size=m * k).astype(np.int8)
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    codes = make_codes(rng, rows, cols, 2)
+    table = rng.integers(-128, 128, size=N).astype(np.int8)
+    want = np.zeros(m * n, np.int32)
+    orc.coded_gemm(orc.View(a, m, k, k, 1), codes, 2, table, orc.View(want, m, n, n, 1), k, n,
+                   orientation)
+    tc = torch.zeros(m * n, dtype=torch.int32, device="cuda")
+    route = U.Route()
+    U.coded_gemm(U.I32, torch.from_numpy(a).cuda(), (m, k, k, 1), torch.from_numpy(codes).cuda(),
+                 k, n, 2, torch.from_numpy(table).cuda(), tc, (m, n, n, 1), route=route,
+                 tabulated=orientation == 1)
+    assert np.array_equal(tc.cpu().numpy(), want)
+    assert route.kernel == 4 and route.b_layout == 3
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
 @pytest.mark.parametrize("m", [70, 260])  # one CTA per tile / CTA pairs
 def test_short_table_alpha_beta_outputs(orientation, m):
     for out in (U.I8, U.I32, U.I64, U.I128):
