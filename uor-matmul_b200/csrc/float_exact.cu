@@ -25,6 +25,7 @@
 // extension word) on CUDA cores. Exact, and slow; it exists so that no input has
 // to be refused.
 #include <climits>
+#include <type_traits>
 #include <vector>
 #include "aux.cuh"
 #include "float_exact.h"
@@ -44,11 +45,11 @@ struct FDec {
     int exp;
 };
 
-// FloatElement::decode (alphabet.rs:905-946).
-__device__ __forceinline__ FDec fdecode(const uint8_t* base, int64_t idx, bool f64) {
+// FloatElement::decode (alphabet.rs:905-946) of a bit pattern (f32 in the low 32 bits).
+__device__ __forceinline__ FDec fdecode_bits(uint64_t raw, bool f64) {
     FDec d;
     if (f64) {
-        const uint64_t bits = reinterpret_cast<const uint64_t*>(base)[idx];
+        const uint64_t bits = raw;
         const uint64_t frac = bits & 0xFFFFFFFFFFFFFull, biased = (bits >> 52) & 0x7FF;
         d.sign = static_cast<int>(bits >> 63);
         if (biased == 0x7FF) {
@@ -59,7 +60,7 @@ __device__ __forceinline__ FDec fdecode(const uint8_t* base, int64_t idx, bool f
         if (biased == 0) d.mant = frac, d.exp = 1 - 1023 - 52;
         else d.mant = frac | (1ull << 52), d.exp = static_cast<int>(biased) - 1023 - 52;
     } else {
-        const uint32_t bits = reinterpret_cast<const uint32_t*>(base)[idx];
+        const uint32_t bits = static_cast<uint32_t>(raw);
         const uint32_t frac = bits & 0x7FFFFF, biased = (bits >> 23) & 0xFF;
         d.sign = static_cast<int>(bits >> 31);
         if (biased == 0xFF) {
@@ -71,6 +72,13 @@ __device__ __forceinline__ FDec fdecode(const uint8_t* base, int64_t idx, bool f
         else d.mant = frac | 0x800000u, d.exp = static_cast<int>(biased) - 127 - 23;
     }
     return d;
+}
+
+// FloatElement::decode of element idx of an f32 / f64 array.
+__device__ __forceinline__ FDec fdecode(const uint8_t* base, int64_t idx, bool f64) {
+    return fdecode_bits(f64 ? reinterpret_cast<const uint64_t*>(base)[idx]
+                            : reinterpret_cast<const uint32_t*>(base)[idx],
+                        f64);
 }
 
 // Product flags of one term (alphabet.rs:862-873): bit 0 NaN, bit 1 +inf, bit 2 -inf.
@@ -1154,17 +1162,18 @@ __device__ __forceinline__ void fm_store_residues(int8_t* dst, int64_t plane, co
         for (int gi = 0; gi < 4; ++gi) {
             const int g = 4 * g4 + gi;
             if (g >= NM) break;
-            const uint32_t p = f.p[g], mg = f.magic32[g], hf = f.half[g];
+            const uint32_t p = f.p[g], mg = f.magic32[g];
+            const uint64_t hm = f.hm[g];
             uint32_t word = 0;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const uint32_t lo = gi == 0 ? cw[c].x : gi == 1 ? cw[c].y : gi == 2 ? cw[c].z : cw[c].w;
-                uint32_t u = __dp4a(lo32[c], lo, hf);
+                uint32_t v = __dp4a(lo32[c], lo, 0u);
                 if (W == 2) {
                     const uint32_t hi = gi == 0 ? ch[c].x : gi == 1 ? ch[c].y : gi == 2 ? ch[c].z : ch[c].w;
-                    u = __dp4a(hi32[c], hi, u);
+                    v = __dp4a(hi32[c], hi, v);
                 }
-                word = fm_put_byte(word, fm_balanced(u, p, mg, hf), c);
+                word = fm_put_byte(word, fm_balanced_v(v, p, mg, hm), c);
             }
             *reinterpret_cast<uint32_t*>(dst + g * plane) = word;
         }
@@ -1190,20 +1199,36 @@ __global__ void __launch_bounds__(256, 4) fm_slice_a_kernel(int8_t* __restrict__
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
-    for (GridWalk wk(static_cast<size_t>(qpr)); wk.idx < static_cast<size_t>(total); wk.next()) {
+    // Each step's 16 bytes and row exponent are loaded one step ahead, so the loads are in
+    // flight while the previous quad's residues are computed.
+    auto fetch = [&](const GridWalk& w, uint4& q, int& l) {
+        const int i = static_cast<int>(w.i), p0 = static_cast<int>(w.j) * 4;
+        l = i < m ? __ldg(lo + i) : 0;
+        q = (vec && i < m && p0 + 3 < k)
+                ? __ldg(reinterpret_cast<const uint4*>(a + (static_cast<int64_t>(i) * rsa + p0) * 4))
+                : make_uint4(0, 0, 0, 0);
+    };
+    GridWalk wk(static_cast<size_t>(qpr));
+    uint4 qc = make_uint4(0, 0, 0, 0);
+    int lc = 0;
+    if (wk.idx < static_cast<size_t>(total)) fetch(wk, qc, lc);
+    while (wk.idx < static_cast<size_t>(total)) {
+        GridWalk nx = wk;
+        nx.next();
+        uint4 qn = make_uint4(0, 0, 0, 0);
+        int ln = 0;
+        if (nx.idx < static_cast<size_t>(total)) fetch(nx, qn, ln);
         const int i = static_cast<int>(wk.i);
         const int p0 = static_cast<int>(wk.j) * 4;
         uint64_t mant[4];
         int sh[4];
         bool neg[4];
-        const int li = i < m ? lo[i] : 0;
+        const int li = lc;
         if (vec && i < m && p0 + 3 < k) {
-            // four consecutive f32 elements in one 16-byte load
-            const uint4 q = *reinterpret_cast<const uint4*>(a + (static_cast<int64_t>(i) * rsa + p0) * 4);
-            const uint32_t bits[4] = {q.x, q.y, q.z, q.w};
+            // four consecutive f32 elements, one 16-byte load
+            const uint32_t bits[4] = {qc.x, qc.y, qc.z, qc.w};
 #pragma unroll
-            for (int c = 0; c < 4; ++c) fm_parts(fdecode(reinterpret_cast<const uint8_t*>(bits), c, false), li,
-                                                 mant[c], sh[c], neg[c]);
+            for (int c = 0; c < 4; ++c) fm_parts(fdecode_bits(bits[c], false), li, mant[c], sh[c], neg[c]);
         } else {
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -1215,6 +1240,9 @@ __global__ void __launch_bounds__(256, 4) fm_slice_a_kernel(int8_t* __restrict__
             }
         }
         fm_store_residues<NM, W>(as + static_cast<int64_t>(i) * kp + p0, plane, mant, sh, neg, pw, 2 * shmax, f);
+        wk = nx;
+        qc = qn;
+        lc = ln;
     }
 }
 
@@ -1227,7 +1255,8 @@ __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const
                                   int shmax, FmParams f) {
     constexpr int NMP = (NM + 3) / 4 * 4;
     extern __shared__ __align__(16) uint32_t pw[];
-    __shared__ uint64_t tm[32][65];
+    using MT = typename std::conditional<F64, uint64_t, uint32_t>::type;  // significand < 2^24 for f32
+    __shared__ MT tm[32][65];
     __shared__ int ts[32][65];
     constexpr bool f64 = F64;
     constexpr int W = F64 ? 2 : 1;
@@ -1238,16 +1267,28 @@ __global__ void fm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp, const
     const int lj = j0 + tx < n ? lo[j0 + tx] : 0;
     __syncthreads();
     for (int p0 = blockIdx.y * 64; p0 < kp; p0 += gridDim.y * 64) {
-        for (int r = ty; r < 64; r += 8) {
-            const int p = p0 + r, j = j0 + tx;
+        // eight rows per thread, their loads issued before any decode
+        uint64_t raw[8];
+        bool ok[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int p = p0 + ty + 8 * i, j = j0 + tx;
+            ok[i] = p < k && j < n;
+            const int64_t at = static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb;
+            raw[i] = !ok[i] ? 0ull
+                     : f64  ? __ldg(reinterpret_cast<const unsigned long long*>(b) + at)
+                            : __ldg(reinterpret_cast<const uint32_t*>(b) + at);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int r = ty + 8 * i;
             FDec d{};
-            if (p < k && j < n)
-                d = fdecode(b, static_cast<int64_t>(p) * rsb + static_cast<int64_t>(j) * csb, f64);
+            if (ok[i]) d = fdecode_bits(raw[i], f64);
             uint64_t mant;
             int sh;
             bool neg;
             fm_parts(d, lj, mant, sh, neg);
-            tm[tx][r] = mant;
+            tm[tx][r] = static_cast<MT>(mant);
             ts[tx][r] = sh | (neg ? 1 << 30 : 0);
         }
         __syncthreads();

@@ -99,7 +99,10 @@ __global__ void slice_b_kernel(uint8_t* __restrict__ bs, int np, int kp,
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     const int64_t plane = static_cast<int64_t>(np) * kp;
     for (int p0 = blockIdx.y * 128; p0 < kp; p0 += gridDim.y * 128) {
-        for (int r = ty; r < 128; r += 8) {
+        // sixteen rows per thread with a fixed trip count, so their loads issue together
+#pragma unroll 8
+        for (int ri = 0; ri < 16; ++ri) {
+            const int r = ty + 8 * ri;
             const int p = p0 + r, j = j0 + tx;
             uint64_t v = 0;
             if (p < k && j < n) {
@@ -298,12 +301,12 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
 // against 16 pairs for i32 at k = 65536, 20 against 64 for i64).
 
 // Weights of an EB-byte integer's bytes modulo p_g. The value x is read as the unsigned
-// x + 2^(8 EB - 1) (its sign bit flipped), and bias folds the -2^(8 EB - 1) back in
-// together with the balanced residue's shift half_g.
+// x + 2^(8 EB - 1) (its sign bit flipped), and bias folds the -2^(8 EB - 1) back in; the
+// balanced residue's shift half_g rides in the quotient (fm_balanced_v).
 struct WmWeights {
     uint32_t w0[FM_MAX];    // bytes i of 256^i mod p_g, i < 4
     uint32_t w1[FM_MAX];    // bytes i - 4 of 256^i mod p_g, 4 <= i < 8
-    uint32_t bias[FM_MAX];  // half_g + (p_g - 2^(8 EB - 1) mod p_g)
+    uint32_t bias[FM_MAX];  // p_g - 2^(8 EB - 1) mod p_g
 };
 
 template <int EB, int NM>
@@ -321,9 +324,9 @@ __device__ __forceinline__ void wm_store(int8_t* dst, int64_t plane, const uint6
         uint32_t word = 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            uint32_t u = __dp4a(lo[c], w.w0[g], w.bias[g]);
-            if (EB == 8) u = __dp4a(hi[c], w.w1[g], u);
-            word = fm_put_byte(word, fm_balanced(u, f.p[g], f.magic32[g], f.half[g]), c);
+            uint32_t v = __dp4a(lo[c], w.w0[g], w.bias[g]);
+            if (EB == 8) v = __dp4a(hi[c], w.w1[g], v);
+            word = fm_put_byte(word, fm_balanced_v(v, f.p[g], f.magic32[g], f.hm[g]), c);
         }
         *reinterpret_cast<uint32_t*>(dst + g * plane) = word;
     }
@@ -342,22 +345,36 @@ __global__ void wm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp,
     const int qpr = kp >> 2;
     const int64_t total = static_cast<int64_t>(mp) * qpr;
     const int64_t plane = static_cast<int64_t>(mp) * kp;
-    for (GridWalk wk(static_cast<size_t>(qpr)); wk.idx < static_cast<size_t>(total); wk.next()) {
+    // The vector loads of the next step are issued before this step's residues (in flight
+    // while they are computed).
+    auto fetch = [&](const GridWalk& wv, uint4& q0, uint4& q1) {
+        const int i = static_cast<int>(wv.i), p0 = static_cast<int>(wv.j) * 4;
+        q0 = q1 = make_uint4(0, 0, 0, 0);
+        if (vec && i < m && p0 + 3 < k) {
+            const uint4* src = reinterpret_cast<const uint4*>(a + cplx_a_index(i, p0, rsa, csa, cplx) * EB);
+            q0 = __ldg(src);
+            if (EB == 8) q1 = __ldg(src + 1);
+        }
+    };
+    GridWalk wk(static_cast<size_t>(qpr));
+    uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
+    if (wk.idx < static_cast<size_t>(total)) fetch(wk, c0, c1);
+    while (wk.idx < static_cast<size_t>(total)) {
+        GridWalk nx = wk;
+        nx.next();
+        uint4 n0 = make_uint4(0, 0, 0, 0), n1 = n0;
+        if (nx.idx < static_cast<size_t>(total)) fetch(nx, n0, n1);
         const int i = static_cast<int>(wk.i);
         const int p0 = static_cast<int>(wk.j) * 4;
         uint64_t v[4];
         const int64_t e0 = cplx_a_index(i, p0, rsa, csa, cplx);
         if (vec && i < m && p0 + 3 < k) {
             // four consecutive elements in one or two 16-byte loads
-            const uint8_t* src = a + e0 * EB;
             if (EB == 4) {
-                const uint4 q = *reinterpret_cast<const uint4*>(src);
-                v[0] = q.x, v[1] = q.y, v[2] = q.z, v[3] = q.w;
+                v[0] = c0.x, v[1] = c0.y, v[2] = c0.z, v[3] = c0.w;
             } else if (EB == 8) {
-                const uint4 q0 = reinterpret_cast<const uint4*>(src)[0];
-                const uint4 q1 = reinterpret_cast<const uint4*>(src)[1];
-                v[0] = q0.x | static_cast<uint64_t>(q0.y) << 32, v[1] = q0.z | static_cast<uint64_t>(q0.w) << 32;
-                v[2] = q1.x | static_cast<uint64_t>(q1.y) << 32, v[3] = q1.z | static_cast<uint64_t>(q1.w) << 32;
+                v[0] = c0.x | static_cast<uint64_t>(c0.y) << 32, v[1] = c0.z | static_cast<uint64_t>(c0.w) << 32;
+                v[2] = c1.x | static_cast<uint64_t>(c1.y) << 32, v[3] = c1.z | static_cast<uint64_t>(c1.w) << 32;
             } else {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) v[c] = load_elem<EB>(a, e0 + c, aligned);
@@ -370,6 +387,9 @@ __global__ void wm_slice_a_kernel(int8_t* __restrict__ as, int mp, int kp,
             }
         }
         wm_store<EB, NM>(as + static_cast<int64_t>(i) * kp + p0, plane, v, f, w);
+        wk = nx;
+        c0 = n0;
+        c1 = n1;
     }
 }
 
@@ -580,7 +600,7 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
             }
             uint32_t top = 1 % pg;  // 2^(8 eb - 1) mod p
             for (int i = 0; i < 8 * eb - 1; ++i) top = top * 2 % pg;
-            w.bias[g] = fm.half[g] + (pg - top) % pg;
+            w.bias[g] = (pg - top) % pg;
         }
         const size_t kp = rup(k, 16);
         const size_t a_bytes = rup((size_t)nm * q.mp * kp, 256);

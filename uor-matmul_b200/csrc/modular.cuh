@@ -30,6 +30,7 @@ struct FmParams {
     uint32_t magic32[FM_MAX];         // ceil(2^32 / p_g)
     uint32_t mg[FM_MAX / 4][4];       // [a][b]: byte b of ceil(2^32 / p_g) for g = 4a .. 4a + 3
     uint32_t half[FM_MAX];            // (p_g - 1) / 2, and 127 for 256
+    uint64_t hm[FM_MAX];              // half_g ceil(2^32 / p_g): the shift folded into a quotient
     uint32_t md[FM_MAX / 4][FM_MAX];  // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
     uint32_t mm[FM_MAX / 4 + 1];      // 32-bit limbs of M (M < 2^(8 nm))
 };
@@ -56,6 +57,14 @@ __device__ __forceinline__ uint32_t fm_mod24(uint32_t x, uint32_t p, uint32_t ma
 __device__ __forceinline__ uint32_t fm_balanced(uint32_t u, uint32_t p, uint32_t magic32,
                                                 uint32_t half) {
     return fm_mod24(u, p, magic32) - half;
+}
+
+// The balanced residue of v < 2^24 - half (v - q p, q = floor((v + half) / p)) in its low
+// byte, q from one widening multiply-add: (v ceil(2^32/p) + half ceil(2^32/p)) / 2^32 is
+// floor((v + half) / p) by fm_mod24's bound.
+__device__ __forceinline__ uint32_t fm_balanced_v(uint32_t v, uint32_t p, uint32_t magic32, uint64_t hm) {
+    const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(v) * magic32 + hm) >> 32);
+    return v - q * p;
 }
 
 // word with its byte c replaced by the low byte of b (c = 0 .. 3, a compile-time constant).
