@@ -14,6 +14,7 @@
 // two's complement, then runs the Linear epilogue in the element's own accumulator
 // (i128 for i16/i32, Limbs<3> for i64) and encodes once.
 #include <climits>
+#include <type_traits>
 #include "int_gemm.h"
 #include "aux.cuh"
 #include "gemm_slices.cuh"
@@ -400,12 +401,19 @@ __global__ void wm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp,
                                   const uint8_t* __restrict__ b, int64_t rsb, int64_t csb,
                                   bool aligned, int k, int n, bool cplx, FmParams f, WmWeights w) {
     constexpr uint64_t mask = EB == 8 ? ~0ull : (1ull << (8 * EB)) - 1;
-    __shared__ uint64_t tile[32][129];
+    // Elements of up to four bytes sit in 32-bit words with 16-byte rows, so a quad is one
+    // 16-byte read; 8-byte elements keep an odd row stride.
+    using TT = typename std::conditional<EB == 8, uint64_t, uint32_t>::type;
+    constexpr int TS = EB == 8 ? 129 : 132;
+    __shared__ __align__(16) TT tile[32][TS];
     const int j0 = blockIdx.x * 32;
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     const int64_t plane = static_cast<int64_t>(np) * kp;
     for (int p0 = blockIdx.y * 128; p0 < kp; p0 += gridDim.y * 128) {
-        for (int r = ty; r < 128; r += 8) {
+        // sixteen rows per thread with a fixed trip count, so their loads issue together
+#pragma unroll 8
+        for (int ri = 0; ri < 16; ++ri) {
+            const int r = ty + 8 * ri;
             const int p = p0 + r, j = j0 + tx;
             uint64_t v = 0;
             if (p < k && j < n) {
@@ -418,7 +426,7 @@ __global__ void wm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp,
                                       aligned);
                 }
             }
-            tile[tx][r] = v;
+            tile[tx][r] = static_cast<TT>(v);
         }
         __syncthreads();
         const int p = p0 + 4 * tx;
@@ -426,8 +434,14 @@ __global__ void wm_slice_b_kernel(int8_t* __restrict__ bs, int np, int kp,
         for (int q = 0; q < 4; ++q) {
             const int jj = ty * 4 + q, j = j0 + jj;
             if (j < np && p < kp) {
-                const uint64_t v[4] = {tile[jj][4 * tx], tile[jj][4 * tx + 1], tile[jj][4 * tx + 2],
-                                       tile[jj][4 * tx + 3]};
+                uint64_t v[4];
+                if (EB == 8) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) v[c] = tile[jj][4 * tx + c];
+                } else {
+                    const uint4 t4 = *reinterpret_cast<const uint4*>(&tile[jj][4 * tx]);
+                    v[0] = t4.x, v[1] = t4.y, v[2] = t4.z, v[3] = t4.w;
+                }
                 wm_store<EB, NM>(bs + static_cast<int64_t>(j) * kp + p, plane, v, f, w);
             }
         }
