@@ -26,7 +26,7 @@ namespace uor {
 
 constexpr int SK_MAXV = 16;
 constexpr int64_t SK_REDUCE_CHUNK_MAX = 131056;  // multiple of 16 inside one s32 lane
-constexpr int SK_COLS_KT = 256;                  // A bytes per row staged per step
+constexpr int SK_COLS_KT = 128;                  // A bytes per row staged per step
 constexpr int64_t SK_COLS_CHUNK_MAX = 130816;    // multiple of SK_COLS_KT inside one lane
 constexpr int SK_COLS_THREADS = 128;             // 4 columns each: 512 columns per block
 
@@ -132,9 +132,9 @@ __global__ void __launch_bounds__(SK_COLS_THREADS)
         }
         __syncthreads();
         if (j0 < n) {
-            // 16 rows per step: all sixteen row loads issued before any is used
-            for (int pp = 0; pp < kt; pp += 16) {
-                uint32_t w[16];
+            // 16 rows per step, all sixteen loads issued before any is used, and the next
+            // step's sixteen issued before this step's products (two steps in flight)
+            auto load16 = [&](int pp, uint32_t (&w)[16]) {
 #pragma unroll
                 for (int rr = 0; rr < 16; ++rr) {
                     const int8_t* row = B + (t0 + pp + rr) * ldb + j0;
@@ -150,6 +150,14 @@ __global__ void __launch_bounds__(SK_COLS_THREADS)
                         w[rr] = v;
                     }
                 }
+            };
+            uint32_t wn[16];
+            load16(0, wn);
+            for (int pp = 0; pp < kt; pp += 16) {
+                uint32_t w[16];
+#pragma unroll
+                for (int rr = 0; rr < 16; ++rr) w[rr] = wn[rr];
+                if (pp + 16 < kt) load16(pp + 16, wn);
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
                     uint32_t col[4];
@@ -231,7 +239,7 @@ int run_i8_skinny(uor_b200_ctx* ctx, const int8_t* a, ptrdiff_t rsa, ptrdiff_t c
     if (plan == COLS) {
         grid_x = (int)((n + 4 * SK_COLS_THREADS - 1) / (4 * SK_COLS_THREADS));
         const int64_t max_chunks = (int64_t)((k + SK_COLS_KT - 1) / SK_COLS_KT);
-        int64_t want = (4 * ctx->sm_count + grid_x - 1) / grid_x;
+        int64_t want = (8 * ctx->sm_count + grid_x - 1) / grid_x;
         const int64_t need = (int64_t)((k + SK_COLS_CHUNK_MAX - 1) / SK_COLS_CHUNK_MAX);
         want = want < max_chunks ? want : max_chunks;
         want = want > need ? want : need;
