@@ -50,17 +50,10 @@ __device__ __forceinline__ uint32_t fm_mod24(uint32_t x, uint32_t p, uint32_t ma
     return x - __umulhi(x, magic32) * p;
 }
 
-// The balanced residue of a value congruent to u - half modulo p (u < 2^24 already holds
-// the shift half = (p - 1) / 2, 127 for 256), in its low byte: (u mod p) - half lies in
-// [-(p-1)/2, (p-1)/2] for odd p and in [-127, 128] for 256, whose byte 128 is the int8
-// -128, the same residue modulo 256.
-__device__ __forceinline__ uint32_t fm_balanced(uint32_t u, uint32_t p, uint32_t magic32,
-                                                uint32_t half) {
-    return fm_mod24(u, p, magic32) - half;
-}
-
-// The balanced residue of v < 2^24 - half (v - q p, q = floor((v + half) / p)) in its low
-// byte, q from one widening multiply-add: (v ceil(2^32/p) + half ceil(2^32/p)) / 2^32 is
+// The balanced residue of v < 2^24 - half (v - q p, q = floor((v + half) / p), half =
+// (p - 1) / 2 and 127 for 256) in its low byte: it lies in [-(p-1)/2, (p-1)/2] for odd p
+// and in [-127, 128] for 256, whose byte 128 is the int8 -128, the same residue modulo 256.
+// q comes from one widening multiply-add: (v ceil(2^32/p) + half ceil(2^32/p)) / 2^32 is
 // floor((v + half) / p) by fm_mod24's bound.
 __device__ __forceinline__ uint32_t fm_balanced_v(uint32_t v, uint32_t p, uint32_t magic32, uint64_t hm) {
     const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(v) * magic32 + hm) >> 32);
