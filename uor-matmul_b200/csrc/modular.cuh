@@ -114,7 +114,10 @@ __device__ __forceinline__ uint32_t fm_crt_packed(const uint32_t (&ya)[(NM + 3) 
     const uint64_t fx = (static_cast<uint64_t>(F[2] + (F[3] << 8)) << 16) + (F[0] + (F[1] << 8)) +
                         0x80000000ull;  // + 1/2
     const uint32_t t = static_cast<uint32_t>(fx >> 32);
-    // Columns X_b (each below NM 255^2 < 2^22), four to a limb, minus t M limb by limb.
+    // Columns X_b (each below NM 255^2 < 2^22), four to a limb, minus t M limb by limb. From
+    // three moduli on, M / p_g is a product of NM - 1 moduli of which at most one is 256, so
+    // it stays below 256^(NM - 1) and its byte NM - 1 (the last column) is zero.
+    constexpr int NB = NM >= 3 ? NM - 1 : NM;
     int64_t carry = 0;
 #pragma unroll
     for (int l = 0; l < NL; ++l) {
@@ -123,7 +126,7 @@ __device__ __forceinline__ uint32_t fm_crt_packed(const uint32_t (&ya)[(NM + 3) 
         for (int bi = 0; bi < 4; ++bi) {
             const int b = 4 * l + bi;
             col[bi] = 0;
-            if (b < NM) {
+            if (b < NB) {
 #pragma unroll
                 for (int a = 0; a < NA; ++a) col[bi] = __dp4a(ya[a], f.md[a][b], col[bi]);
             }
