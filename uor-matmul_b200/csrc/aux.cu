@@ -68,8 +68,18 @@ __global__ void reduce_chunks_kernel(const int32_t* __restrict__ part, int chunk
     const size_t total = m * n;
     for (GridWalk wk(n); wk.idx < total; wk.next()) {
         const size_t idx = wk.idx;
+        // sixteen planes' loads in flight at a time (few cells over many chunk planes would
+        // otherwise wait on one load per plane); |sum| < chunks 2^31 fits an int64 in any order
         int64_t acc = 0;
-        for (int q = 0; q < chunks; ++q) acc += part[(size_t)q * total + idx];
+        int q = 0;
+        for (; q + 16 <= chunks; q += 16) {
+            int32_t v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = __ldg(part + (size_t)(q + u) * total + idx);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) acc += v[u];
+        }
+        for (; q < chunks; ++q) acc += __ldg(part + (size_t)q * total + idx);
         const size_t i = wk.i, j = wk.j;
         finish_cell(e, c, (int64_t)i * rsc + (int64_t)j * csc, acc);
     }
