@@ -53,10 +53,15 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="i8", choices=WORKLOADS)
     p.add_argument("--size", type=int, default=None, help="square size of i8 / f32 workloads")
+    p.add_argument("--batch", type=int, default=0,
+                   help="products per step of the i8 workloads (0: 16 at the 8192^3 headline, "
+                        "else 1)")
     p.add_argument("--e2e-steps", type=int, default=3)
-    p.add_argument("--f32-steps", type=int, default=3,
+    p.add_argument("--f32-steps", type=int, default=10,
                    help="timed steps of the exact f32 8192^3 half of the default line (0 skips)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the default line's extra keys (other configs, strong scaling)")
     return p.parse_args()
 
 
@@ -161,32 +166,50 @@ def sample_rows(total_rows, run_rows, budget_s):
 
 # ---------------------------------------------------------------- workloads
 
-def wl_i8(args, U, torch, rank, size, sets=3):
-    """configs[4] headline (size 8192) or configs[0] (size 512): i8 x i8 -> i32."""
+def i8_batch(args, size):
+    return args.batch if args.batch > 0 else (16 if size == SIZE else 1)
+
+
+def i8_line_config(size, batch, sets, world):
+    """The i8 line's config, printed identically by both arms."""
+    name = ("configs[4] headline" if size == SIZE else "configs[0]" if size == 512 else "square")
+    return {"workload": f"i8 x i8 -> i32 GEMM {size}x{size}x{size} per GPU ({name}), "
+                        f"{batch} products per step, column-block sharded",
+            "m": size, "k": size, "n_per_gpu": size, "batch": batch, "n_total": size * world,
+            "l2": (f"{sets} rotating operand sets ({sets * 2 * size * size >> 20} MiB) + "
+                   f"{4 * size * size >> 20} MiB output per product"),
+            "parallelism": f"column blocks x{world}, no data-path collective"}
+
+
+def wl_i8(args, U, torch, rank, size, sets=3, world=1):
+    """configs[4] headline (size 8192) or configs[0] (size 512): i8 x i8 -> i32. A step
+    is a batch of independent products over the rotating operand sets."""
     import numpy as np
     m = k = n = size
+    batch = i8_batch(args, size)
     A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() for s in range(sets)]
     B = [torch.from_numpy(U.corpus(2 + 100 * s + 1000 * rank, U.CORPUS_I8, k * n)).cuda()
          for s in range(sets)]
     C = torch.empty(m * n, dtype=torch.int32, device="cuda")
-    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n, launches=1,
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n * batch, launches=batch,
                         graph_sets=sets if size < 2048 else 0)
 
     def step(i, ctx):
-        U.gemm_i8_i32(m, k, n, A[i % sets], B[i % sets], C, ctx=ctx, route=w.route,
-                      asynchronous=True)
+        for j in range(batch):
+            s = (i * batch + j) % sets
+            U.gemm_i8_i32(m, k, n, A[s], B[s], C, ctx=ctx, route=w.route, asynchronous=True)
 
     def check(last):
         # Freivalds check in f64 on the last warm-up output (every partial < 2^53: exact)
         x = torch.randint(-1, 2, (n,), device="cuda", dtype=torch.float64)
-        s = last % sets
+        s = (last * batch + batch - 1) % sets
         lhs = C.view(m, n).double() @ x
         rhs = A[s].view(m, k).double() @ (B[s].view(k, n).double() @ x)
         assert torch.equal(lhs, rhs), "checksum mismatch"
 
     def cpu(budget_s, ctx):
         from oracle import oracle as orc
-        step(0, ctx)
+        U.gemm_i8_i32(m, k, n, A[0], B[0], C, ctx=ctx, asynchronous=True)
         ctx.sync()
         a, b = A[0].cpu().numpy(), B[0].cpu().numpy()
         threads = host_threads(orc)
@@ -204,31 +227,47 @@ def wl_i8(args, U, torch, rank, size, sets=3):
                           "rows were compared bit for bit"}
 
     def e2e(steps, ctx, stream):
-        Ah = torch.from_numpy(U.corpus(1, U.CORPUS_I8, m * k)).pin_memory()
         Bh = torch.from_numpy(U.corpus(2 + 1000 * rank, U.CORPUS_I8, k * n)).pin_memory()
         Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
-        return timed_host(lambda: U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx), steps, stream,
-                          m * k + k * n, 4 * m * n)
+        if world == 1:
+            Ah = torch.from_numpy(U.corpus(1, U.CORPUS_I8, m * k)).pin_memory()
+
+            def call():
+                for _ in range(batch):
+                    U.gemm_i8_i32(m, k, n, Ah, Bh, Ch, ctx=ctx)
+            return timed_host(call, steps, stream, batch * (m * k + k * n), batch * 4 * m * n)
+        # N > 1: A goes up once (rank 0) and is broadcast over NVLink; every rank uploads
+        # its own B block and reads back its own C block.
+        import uor_b200_dist as D
+        Ah = (torch.from_numpy(U.corpus(1, U.CORPUS_I8, m * k)).pin_memory() if rank == 0
+              else None)
+        work = D.HostStaging(m * k, k * n, 4 * m * n)
+
+        def call():
+            for _ in range(batch):
+                D.replicated_gemm_i8_host(m, k, n, Ah, Bh, Ch, work, ctx=ctx)
+        # whole-job bytes: A once, every rank's B block in, every rank's C block out
+        return timed_host(call, steps, stream, batch * (m * k + world * k * n),
+                          batch * world * 4 * m * n)
 
     w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
     w.metric = METRIC if size == SIZE else f"exact i8 GEMM TOPS at {size}^3 (bit-exact, int32 out)"
     w.unit, w.dtype = "TOPS", "int8"
-    w.config = {"workload": f"i8 x i8 -> i32 GEMM {m}x{k}x{n} per GPU "
-                            f"({'configs[4] headline' if size == SIZE else 'configs[0]' if size == 512 else 'square'}), "
-                            "column-block sharded",
-                "m": m, "k": k, "n_per_gpu": n}
-    w.l2 = (f"{sets} rotating operand sets ({sets * 2 * m * k >> 20} MiB) + "
-            f"{4 * m * n >> 20} MiB output per step")
+    w.full_config = i8_line_config(size, batch, sets, world)
+    w.config = {"workload": w.full_config["workload"], "m": m, "k": k, "n_per_gpu": n}
+    w.l2 = w.full_config["l2"]
     w.algorithmic_bytes = m * k + k * n + 4 * m * n
     w.traffic = load_traffic("k1_pair_i8_8192_traffic.json") if size == SIZE else None
     w.flush = sets * 2 * m * k < (256 << 20)
 
     def roofline(avg_ms):
+        # per launch: one product's work over the step time / the products in it
         peak, src = tensor_peak()
         ach = w.units / (avg_ms / 1e3) / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src,
                 "frac_of_nominal_4500": ach / 4500.0,
+                "launch_ms": avg_ms / batch,
                 "traffic": w.traffic, "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
@@ -546,10 +585,21 @@ def wl_f32(args, U, torch, rank, size, sets=2):
                      (m, n, n, 1), ctx=ctx, route=w.route, asynchronous=True)
 
     def check(last):
-        # Exactness is checked against the oracle by the CPU leg and the GPU tests; here
-        # only a sanity bound: the once-rounded result is within 2^-20 relative of an f64
-        # product on the rows without cancellation.
+        # Bit for bit against the oracle on a leading block of rows of the last warm-up
+        # product (rows 0 and 10 among them cancel to exactly zero), plus a sanity bound
+        # on every cell: within 2^-20 relative of an f64 product where nothing cancels.
+        from oracle import oracle as orc
         s = last % sets
+        rows = min(m, getattr(w, "check_rows", 16))
+        a, b = host[s]
+        want = np.zeros(rows * n, np.float32)
+        orc.gemm_float(orc.View(a.reshape(-1), rows, k, k, 1), orc.View(b.reshape(-1), k, n, n, 1),
+                       orc.View(want, rows, n, n, 1), threads=host_threads(orc))
+        got_rows = C[:rows * n].cpu().numpy()
+        assert np.array_equal(want.view(np.uint32), got_rows.view(np.uint32)), \
+            "f32 rows differ from the oracle"
+        w.checked = (f"rows 0..{rows - 1} of the last warm-up product bit for bit against the "
+                     "oracle; every cell within 2^-20 of f64 off the cancellation columns")
         ref = (A[s].view(m, k).double() @ B[s].view(k, n).double())
         got = C.view(m, n).double()
         keep = torch.ones(n, dtype=torch.bool, device="cuda")
@@ -970,9 +1020,93 @@ def wl_wide_splitk(args, U, torch, rank, world):
     return w
 
 
+def wl_i8_strong(args, U, torch, rank, world, dist, sets=3):
+    """The fixed 8192^3 i8 product sharded over the ranks by output column blocks
+    (partition.rs:34): rank r owns C[:, r n/N .. (r+1) n/N] and that block of B; A is
+    uploaded once and broadcast over NCCL before the timed region. The all-gather of
+    the C blocks is timed on its own (``collective``)."""
+    import uor_b200_dist as D
+    m = k = n = SIZE
+    batch = i8_batch(args, SIZE)
+    t = D.column_blocks(m, n, world).tile(rank)
+    cols = t.cols if t is not None else 0
+    A = []
+    for s in range(sets):
+        a = (torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() if rank == 0
+             else torch.empty(m * k, dtype=torch.int8, device="cuda"))
+        if dist:
+            dist.broadcast(a, src=0)
+        A.append(a)
+    B = []
+    for s in range(sets):
+        full = torch.from_numpy(U.corpus(2 + 100 * s, U.CORPUS_I8, k * n)).view(k, n)
+        B.append(full[:, t.col:t.col + cols].contiguous().view(-1).cuda())
+    C = torch.empty(m * max(cols, 1), dtype=torch.int32, device="cuda")
+    w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * cols * batch, launches=batch)
+
+    def step(i, ctx):
+        for j in range(batch):
+            s = (i * batch + j) % sets
+            U.gemm_i8_i32(m, k, cols, A[s], B[s], C, ctx=ctx, route=w.route, asynchronous=True)
+
+    def check(last):
+        x = torch.randint(-1, 2, (cols,), device="cuda", dtype=torch.float64)
+        s = (last * batch + batch - 1) % sets
+        lhs = C.view(m, cols).double() @ x
+        rhs = A[s].view(m, k).double() @ (B[s].view(k, cols).double() @ x)
+        assert torch.equal(lhs, rhs), "checksum mismatch"
+
+    def collective_ms(reps=5):
+        if not dist:
+            return None
+        full = torch.empty(world * C.numel(), dtype=torch.int32, device="cuda")
+        dist.all_gather_into_tensor(full, C)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            dist.all_gather_into_tensor(full, C)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda", dtype=torch.float64)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms.item())
+        return {"op": "NCCL all-gather of the C column blocks (outside the timed steps)",
+                "bytes_per_rank": 4 * C.numel(), "ms": ms,
+                "busbw_gbs": 4 * C.numel() * (world - 1) / (ms / 1e3) / 1e9}
+
+    w.step, w.check, w.e2e = step, check, None
+    w.cpu = None
+    w.collective_ms = collective_ms
+    w.metric = "exact i8 GEMM TOPS, one 8192^3 product sharded over the GPUs (bit-exact)"
+    w.unit, w.dtype = "TOPS", "int8"
+    w.scaling = "strong"
+    w.full_config = {
+        "workload": f"i8 x i8 -> i32 GEMM 8192x8192x8192 in total, {batch} products per step, "
+                    f"column blocks of {cols} per GPU", "m": m, "k": k, "n": n,
+        "n_per_gpu": cols, "batch": batch,
+        "l2": f"{sets} rotating operand sets ({sets * (m * k + k * cols) >> 20} MiB per GPU)",
+        "parallelism": f"column blocks x{world}; A broadcast once over NCCL before timing; "
+                       "no collective in the timed steps"}
+    w.config = w.full_config
+    w.algorithmic_bytes = m * k + k * cols + 4 * m * cols
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak, src = tensor_peak()
+        ach = w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
+                "frac": ach / peak, "peak_source": src, "launch_ms": avg_ms / batch,
+                "pair_tiles_per_launch": -(-m // 256) * -(-cols // 256),
+                "traffic": None, "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
 def build_workload(name, args, U, torch, rank, world=1):
     if name == "i8":
-        return wl_i8(args, U, torch, rank, args.size or SIZE)
+        return wl_i8(args, U, torch, rank, args.size or SIZE, world=world)
     if name == "i8-512":
         return wl_i8(args, U, torch, rank, args.size or 512, sets=1)
     if name == "gemv":
@@ -1076,18 +1210,19 @@ def time_steps(w, ctx, stream, torch, dist, steps, warmup, local):
 
 # ---------------------------------------------------------------- reference arm
 
-def reference_arm(args, rank):
-    """The reference's CPU path for the same workload on the host cores (rank 0)."""
+def reference_arm(args, rank, world):
+    """The reference's CPU path for the same workload on the host cores (rank 0). Only
+    the oracle runs here: its C restatement draws the operands and computes the rows."""
     if rank != 0:
         return
-    import numpy as np
-    import uor_b200 as U
     from oracle import oracle as orc
+    import numpy as np
     size = args.size or SIZE
+    batch = i8_batch(args, size)
     k = n = size
-    b = U.corpus(2, U.CORPUS_I8, k * n)
+    a = orc.corpus_i8(1, size * k)
+    b = orc.corpus_i8(2, k * n)
     threads = host_threads(orc)
-    a = U.corpus(1, U.CORPUS_I8, size * k)
 
     def run(r):
         c = np.zeros(r * n, np.int32)
@@ -1105,15 +1240,14 @@ def reference_arm(args, rank):
             steps.append(2.0 * rows * k * n / dt / 1e12)
     v = statistics.median(steps)
     base = {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {size} rows of the {size}^3 product per step ({dt:.2f} s), "
+            "sample": f"{rows} of {size} rows of one {size}^3 product per step ({dt:.2f} s), "
                       "blocked C restatement of gemm_auto's s8 path, OpenMP over rows"}
     line = {"impl": "reference", "metric": METRIC if size == SIZE else
             f"exact i8 GEMM TOPS at {size}^3 (bit-exact, int32 out)", "value": v, "unit": "TOPS",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (reference xorshift corpus, salts 1/2)",
-            "config": {"workload": f"i8 x i8 -> i32 GEMM {size}^3 (configs[4] headline)",
-                       "m": size, "k": size, "n": size},
+            "data": "synthetic (reference xorshift corpus)",
+            "config": i8_line_config(size, batch, 3, world),
             "cpu_baseline": base,
             "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -1131,16 +1265,21 @@ def measure(w, args, U, torch, dist, ctx, stream, rank, world, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps,
         "higher_is_better": True, "scaling": getattr(w, "scaling", "weak"), "vs_baseline": None,
         "dtype": w.dtype, "data": "synthetic (reference xorshift corpus)",
-        "config": dict(w.config, n_total=w.config["n_per_gpu"] * (
-                           world if getattr(w, "scaling", "weak") == "weak" else 1), l2=w.l2,
-                       parallelism=getattr(w, "parallelism",
-                                           f"column blocks x{world}, no data-path collective")),
+        "config": getattr(w, "full_config", None) or dict(
+            w.config, n_total=w.config["n_per_gpu"] * (
+                world if getattr(w, "scaling", "weak") == "weak" else 1), l2=w.l2,
+            parallelism=getattr(w, "parallelism",
+                                f"column blocks x{world}, no data-path collective")),
         "route": w.route.as_dict(),
         "roofline": w.roofline(statistics.mean(step_ms)),
         "cuda_graph": getattr(w, "graphed", False),
         "gpu_launches": w.launches * args.steps,
         "clocks": clk,
     }
+    if getattr(w, "checked", None):
+        line["checked"] = w.checked
+    if getattr(w, "collective_ms", None) is not None:
+        line["collective"] = w.collective_ms()
     if args.e2e_steps > 0 and w.e2e is not None:
         if dist:
             dist.barrier()
@@ -1157,11 +1296,17 @@ def measure(w, args, U, torch, dist, ctx, stream, rank, world, local):
     return line
 
 
+def sub_line(fl, keys=("metric", "value", "unit", "ms_per_step", "steps", "warmup", "scaling",
+                         "route", "roofline", "gpu_launches", "clocks", "config", "checked",
+                         "collective", "e2e", "cpu_baseline")):
+    return {k2: fl[k2] for k2 in keys if k2 in fl}
+
+
 def main():
     args = parse()
     rank, world, local = env_rank()
     if args.impl == "reference":
-        reference_arm(args, rank)
+        reference_arm(args, rank, world)
         return
 
     import torch
@@ -1172,6 +1317,9 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        import uor_b200_dist as D
+        # pinned host buffers of the e2e leg land in memory local to this GPU
+        D.bind_to_local_cpus(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=datetime.timedelta(seconds=180))
     ctx = U.Context(local)
@@ -1181,22 +1329,50 @@ def main():
 
     w = build_workload(args.workload, args, U, torch, rank, world)
     line = measure(w, args, U, torch, dist, ctx, stream, rank, world, local)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and w.cpu is not None:
         line["cpu_baseline"] = w.cpu(12.0, ctx)
     del w
     torch.cuda.empty_cache()
 
-    # The metric's second half: exact f32 GEMM at 8192^3, on every rank's own columns.
-    if args.workload == "i8" and args.f32_steps > 0 and (args.size or SIZE) == SIZE:
-        f = wl_f32(args, U, torch, rank, SIZE, sets=1)
+    def extra(build, steps, warmup=3, e2e_steps=0, cpu_budget=0.0):
         sub = argparse.Namespace(**vars(args))
-        sub.steps, sub.warmup, sub.e2e_steps = args.f32_steps, max(3, min(args.warmup, 3)), 0
+        sub.steps, sub.warmup, sub.e2e_steps = steps, warmup, e2e_steps
+        f = build()
         fl = measure(f, sub, U, torch, dist, ctx, stream, rank, world, local)
-        line["f32_exact_8192"] = {k2: fl[k2] for k2 in ("metric", "value", "unit", "ms_per_step",
-                                                        "steps", "warmup", "route", "roofline",
-                                                        "gpu_launches", "clocks")}
-        line["f32_exact_8192"]["config"] = fl["config"]
+        if cpu_budget and rank == 0 and world == 1 and not args.no_cpu_baseline and f.cpu:
+            fl["cpu_baseline"] = f.cpu(cpu_budget, ctx)
         del f
+        torch.cuda.empty_cache()
+        return sub_line(fl)
+
+    headline = args.workload == "i8" and (args.size or SIZE) == SIZE
+    # The metric's second half: exact f32 GEMM at 8192^3, on every rank's own columns.
+    if headline and args.f32_steps > 0:
+        line["f32_exact_8192"] = extra(lambda: wl_f32(args, U, torch, rank, SIZE, sets=1),
+                                       args.f32_steps)
+    if headline and not args.no_extras:
+        # Multi-GPU paths at every N (strong scaling: the same total work at every N).
+        line["i8_8192_sharded"] = extra(
+            lambda: wl_i8_strong(args, U, torch, rank, world, dist), args.steps)
+        line["wide_splitk"] = extra(
+            lambda: wl_wide_splitk(args, U, torch, rank, world), max(args.steps, 20))
+        if world == 1:
+            # every other BASELINE config on the same GPU, each with its own bit-exact
+            # row check against the oracle (the CPU leg)
+            line["configs"] = {
+                "configs[0] i8 512^3": extra(
+                    lambda: wl_i8(args, U, torch, rank, 512, sets=1), 200, e2e_steps=20,
+                    cpu_budget=2.0),
+                "configs[1] codec 2048x8192x8192": extra(
+                    lambda: wl_codec(args, U, torch, rank), 100, e2e_steps=3, cpu_budget=4.0),
+                "configs[2] exact f32 4096^3": extra(
+                    lambda: wl_f32(args, U, torch, rank, 4096), 60, e2e_steps=3,
+                    cpu_budget=4.0),
+                "configs[3] i32 -> i128 1024x65536x1024": extra(
+                    lambda: wl_wide(args, U, torch, rank), 100, e2e_steps=3, cpu_budget=4.0),
+                "configs[4] Trop<i8> 8192^3": extra(
+                    lambda: wl_trop(args, U, torch, rank), 6, e2e_steps=1, cpu_budget=4.0),
+            }
 
     ctx.close()
     if dist:

@@ -395,7 +395,9 @@ int uor_b200_limbs_finish(uor_b200_dtype elem, uor_b200_dtype out, const int64_t
  * which every GPU that loads this library holds until the process exits. A product
  * needing more (chunks * m * n * 4 bytes + 256) is refused with UOR_B200_SCRATCH_LIMIT.
  * The first call on a device looks up the array's device address (set-up done once
- * per device); make that first call before any stream capture. Every call shares the
+ * per device); make that first call before any stream capture. The address is kept for
+ * the life of the process, so a cudaDeviceReset after the first call on a device is not
+ * supported (the rebuilt context would not hold the cached address). Every call shares the
  * array, so calls that overlap on the GPU (other streams, other threads) race on it:
  * serialise them. Operands must be TMA-readable as given (16-byte-aligned pointers,
  * lda and ldb multiples of 16) or the call returns UOR_B200_UNSUPPORTED. Runs on

@@ -63,6 +63,7 @@ def lib():
                                                  I, I]
         _LIB.uor_oracle_max_threads.restype = I
         _LIB.uor_oracle_gemm_i8_blocked.argtypes = [Z, Z, Z, L, P, P, L, P, Z, I, I]
+        _LIB.uor_oracle_corpus_i8.argtypes = [ctypes.c_uint64, Z, P]
     return _LIB
 
 
@@ -529,3 +530,11 @@ def corpus_fill(salt: int, count: int) -> np.ndarray:
     """The validate harness fill (validate/tests/common/mod.rs:9-19): ``s >> 33``."""
     states, _ = xorshift_stream(0x243F6A8885A308D3 ^ salt, count)
     return states >> np.uint64(33)
+
+
+def corpus_i8(salt: int, count: int) -> np.ndarray:
+    """``corpus_fill(salt, count)`` cast to i8, from the C restatement (fast enough for
+    the 8192^3 operands the CPU baseline draws)."""
+    out = np.empty(count, dtype=np.int8)
+    lib().uor_oracle_corpus_i8(salt, count, out.ctypes.data)
+    return out

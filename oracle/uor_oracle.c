@@ -779,3 +779,17 @@ int uor_oracle_max_threads(void) {
     return 1;
 #endif
 }
+
+/* The validate harness fill (validate/tests/common/mod.rs:9-19): xorshift64 from
+ * 0x243F6A8885A308D3 ^ salt, each value `s >> 33` cast to i8 (massive.rs:130). Lets the
+ * CPU baseline draw the benchmark's operands without the product library. */
+int uor_oracle_corpus_i8(uint64_t salt, size_t count, int8_t *out) {
+    uint64_t s = 0x243F6A8885A308D3ull ^ salt;
+    for (size_t i = 0; i < count; i++) {
+        s ^= s << 13;
+        s ^= s >> 7;
+        s ^= s << 17;
+        out[i] = (int8_t)(s >> 33);
+    }
+    return 0;
+}

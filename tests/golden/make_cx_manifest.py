@@ -38,4 +38,6 @@ def main(root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_cx_manifest.py <path to the uor-matmul checkout>")
+    main(sys.argv[1])

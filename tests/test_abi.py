@@ -139,3 +139,26 @@ def test_e8_table_bound_and_length():
         U.e8_table(8)
     short = np.zeros(2047, np.int8)
     assert U.lib().uor_b200_e8_table(0, short.ctypes.data, short.size) == U.DOES_NOT_FIT
+
+
+def test_noalloc_refuses_oversized_products_before_any_device_work():
+    """The no-allocation entry compares chunks x m x n partials against its fixed array
+    without forming the product (which can wrap size_t for sizes near its INT_MAX / 2
+    cap); such calls return UOR_B200_SCRATCH_LIMIT before any CUDA call, so this runs
+    without a GPU. The pointers are never read."""
+    import ctypes
+    fn = U.lib().uor_b200_gemm_ex_i8_noalloc
+    fn.argtypes = [ctypes.c_int, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                   ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                   ctypes.c_size_t, ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t,
+                   ctypes.c_uint32, ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    fake = 1 << 20  # 16-byte aligned, non-null, never dereferenced
+    cap = (2**31 - 1) // 2
+    for m, k, n in [(cap, cap, cap), (2**29, 2**28, 2**29), (2**20, 140_000, 2**20),
+                    (1, cap, 2**22), (2048, 140_000, 1024)]:
+        st = fn(U.I64, m, k, n, 1, fake, k, fake, n, 0, fake, n, U.NEAREST, None)
+        assert st == 9, (m, k, n, st)  # UOR_B200_SCRATCH_LIMIT
+    # past the int-sized cap is unsupported, still before any device work
+    assert fn(U.I64, cap + 1, 140_000, 4, 1, fake, 140_000, fake, 4, 0, fake, 4, U.NEAREST,
+              None) == U.UNSUPPORTED

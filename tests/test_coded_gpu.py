@@ -136,30 +136,3 @@ def test_codes_must_describe_the_shape():
     with pytest.raises(U.DoesNotFit):
         U.coded_gemm(U.I32, a, (1, 4, 4, 1), codes, 4, 4, 2, np.zeros(16, np.int8), c,
                      (1, 4, 4, 1))
-
-
-@pytest.mark.slow
-def test_config2_full_size_checksum():
-    """2048 x 8192 activations, 8192 x 8192 nibble codes, 16-entry table (salts 1, 2, 7)."""
-    m, k, n = 2048, 8192, 8192
-    a = U.corpus(1, U.CORPUS_I8, m * k)
-    codes = U.corpus(2, U.CORPUS_NIBBLES, k * n)
-    table = U.corpus(7, U.CORPUS_I8, 16)
-    ta, tcodes, ttab = (torch.from_numpy(x).cuda() for x in (a, codes, table))
-    tc = torch.empty(m * n, dtype=torch.int32, device="cuda")
-    route = U.Route()
-    U.coded_gemm(U.I32, ta, (m, k, k, 1), tcodes, k, n, 2, ttab, tc, (m, n, n, 1), route=route)
-    assert route.kernel == 4 and route.b_layout == 3  # decoded once, then K1
-    # independent decode of the nibbles (low first) for the checksum
-    lo = (tcodes & 0xF).long()
-    hi = (tcodes >> 4).long()
-    sub = torch.stack([lo, hi], dim=1).reshape(k, n)
-    bdec = ttab.long()[sub].double()
-    x = torch.randint(-1, 2, (n,), device="cuda").double()
-    lhs = tc.view(m, n).double() @ x
-    rhs = ta.view(m, k).double() @ (bdec @ x)
-    assert torch.equal(lhs, rhs)
-    # a few cells exactly, from the independent decode
-    for (i, j) in [(0, 0), (m - 1, n - 1), (1000, 4097)]:
-        want = int((ta[i * k:(i + 1) * k].long() * ttab.long()[sub[:, j]]).sum())
-        assert int(tc[i * n + j]) == want

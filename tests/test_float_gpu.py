@@ -211,28 +211,6 @@ def test_raw_faces_negative_strides():
     assert c.tolist() == [0.0, 1.0, 2.0, 3.0]
 
 
-@pytest.mark.slow
-def test_config3_full_size_sampled():
-    m = k = n = 4096
-    a, b = config3(m, k, n)
-    ta = torch.from_numpy(a).reshape(-1).cuda()
-    tb = torch.from_numpy(b).reshape(-1).cuda()
-    tc = torch.empty(m * n, dtype=torch.float32, device="cuda")
-    route = U.Route()
-    U.gemm_float(U.F32, U.F32, ta, (m, k, k, 1), tb, (k, n, n, 1), tc, (m, n, n, 1), route=route)
-    # 24 moduli cover 2 k 2^(84 + 84) (M = 2^184.09); 45 digit pairs would run otherwise
-    assert route.kernel == 5 and route.tile_m == 256 and route.moduli == 24
-    c = tc.cpu().numpy().view(np.uint32)
-    cells = [(0, 0), (0, 1), (m - 1, n - 1), (123, 4000), (3000, 30), (40, 40)]
-    for (i, j) in cells:
-        w = np.zeros(1, np.float32)
-        orc.gemm_float(View(a.reshape(-1), 1, k, k, 1, i * k), View(b.reshape(-1), k, 1, n, 1, j),
-                       View(w, 1, 1, 1, 1))
-        assert c[i * n + j] == w.view(np.uint32)[0], (i, j)
-    for j in range(0, n, 10):
-        assert c[(j % m) * n + j] == 0
-
-
 def test_modular_route_config3_all_epilogues():
     """configs[2]'s distribution on the modular route: 24 int8 GEMMs and the CRT give the
     oracle's bytes, cancelling cells (+0) included, under every epilogue."""

@@ -238,36 +238,6 @@ def test_host_pipeline_split_first_row_and_whole_blocks(pinned):
         assert route.kernel == 1
 
 
-@pytest.mark.slow
-def test_headline_8192_cubed_checksums_and_samples():
-    """At the headline size: Freivalds-style checksums (exact in int64) and sampled
-    cells against the oracle."""
-    m = k = n = 8192
-    a, b = i8(1, m * k), i8(2, k * n)
-    ta = torch.from_numpy(a).cuda()
-    tb = torch.from_numpy(b).cuda()
-    tc = torch.empty(m * n, dtype=torch.int32, device="cuda")
-    U.gemm_i8_i32(m, k, n, ta, tb, tc)
-    A = ta.view(m, k).to(torch.float64)
-    B = tb.view(k, n).to(torch.float64)
-    C = tc.view(m, n).to(torch.float64)
-    rng = np.random.default_rng(0)
-    for _ in range(3):
-        # x has entries in {-1, 0, 1}: every partial is an integer < 2^53, so f64 is exact
-        x = torch.from_numpy(rng.integers(-1, 2, size=n).astype(np.float64)).cuda()
-        lhs = C @ x
-        rhs = A @ (B @ x)
-        assert torch.equal(lhs, rhs)
-    # sampled cells, bit-exact against the oracle
-    cells = [(0, 0), (m - 1, n - 1), (1234, 4321), (4095, 8191), (8191, 0)]
-    c = tc.view(m, n)
-    for i, j in cells:
-        w = np.zeros(1, np.int32)
-        orc.gemm_int(orc.View(a, 1, k, k, 1, i * k), orc.View(b, k, 1, n, 1, j),
-                     orc.View.row_major(w, 1, 1))
-        assert int(c[i, j]) == int(w[0]), (i, j)
-
-
 def test_bounded_wait_gives_up_and_context_survives():
     ctx = U.Context(0)
     assert U.selftest_wait_timeout(ctx, 50_000_000) == U.TIMEOUT

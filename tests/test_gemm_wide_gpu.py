@@ -119,28 +119,3 @@ def test_modular_two_chunks_and_i64_extremes():
                    U.I128)
         assert i128_values(got) == i128_values(want), mode
         assert route.moduli > 0
-
-
-@pytest.mark.slow
-def test_config4_full_size():
-    """1024 x 65536 x 1024, i32 full range -> exact i128: sampled cells against the
-    oracle and a Freivalds checksum modulo 2^64."""
-    m, n, k = 1024, 1024, 65536
-    a = U.corpus(4, U.CORPUS_I32_FULL, m * k)
-    b = U.corpus(5, U.CORPUS_I32_FULL, k * n)
-    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
-    tc = torch.zeros(m * n * 2, dtype=torch.int64, device="cuda")
-    route = U.Route()
-    U.gemm(U.I32, U.I128, ta, (m, k, k, 1), tb, (k, n, n, 1), tc, (m, n, n, 1), route=route)
-    c = tc.cpu().numpy()
-    vals = i128_values(c)
-    for (i, j) in [(0, 0), (m - 1, n - 1), (517, 33)]:
-        w = np.zeros(2, np.int64)
-        orc.gemm_int(orc.View(a, 1, k, k, 1, i * k), orc.View(b, k, 1, n, 1, j),
-                     orc.View(w, 1, 1, 1, 1), out_bits=128)
-        assert vals[i * n + j] == i128_values(w)[0], (i, j)
-    x = np.random.default_rng(0).integers(-1, 2, size=n).astype(np.int64)
-    low = c[0::2].reshape(m, n)  # C mod 2^64
-    lhs = low @ x
-    rhs = a.reshape(m, k).astype(np.int64) @ (b.reshape(k, n).astype(np.int64) @ x)
-    assert np.array_equal(lhs, rhs)

@@ -136,21 +136,3 @@ def test_strided_views():
     # A read as a transpose, B read backwards
     got, want, _ = both(ta, (m, k, 1, m), tb, (k, n, -n, 1), tc, (m, n, 1, m))
     assert same(got, want)
-
-
-@pytest.mark.slow
-def test_config5_shape_rows_sampled():
-    """Trop<i8> with the config-5 distribution at 2048 x 8192 x 2048, checked on rows."""
-    m, k, n = 2048, 8192, 2048
-    a = U.corpus(1, U.CORPUS_TROP_I8, m * k).view(TD[8])
-    b = U.corpus(2, U.CORPUS_TROP_I8, k * n).view(TD[8])
-    ta = torch.from_numpy(a.view(np.uint8)).cuda()
-    tb = torch.from_numpy(b.view(np.uint8)).cuda()
-    tc = torch.zeros(m * n * 8, dtype=torch.uint8, device="cuda")
-    U.gemm_tropical(U.TROP_I8, U.TROP_I32, ta, (m, k, k, 1), tb, (k, n, n, 1), tc, (m, n, n, 1))
-    c = tc.cpu().numpy().view(TD[32])
-    for i in (0, 1, 777, m - 1):
-        want = np.zeros(n, TD[32])
-        orc.gemm_trop(orc.View(a, 1, k, k, 1, i * k), orc.View(b, k, n, n, 1),
-                      orc.View(want, 1, n, n, 1), ebits=8, obits=32)
-        assert same(c[i * n:(i + 1) * n], want), i

@@ -3,10 +3,10 @@
 It serves callers that cannot let a library allocate device memory: hosts that fix
 their device memory budget at start-up, and callers relying on the reference's
 zero-allocation contract. Its working memory is one fixed static device array, so the
-test checks that two calls in a row (the second reusing the array the first left
-behind) give exactly what the ordinary entry point gives, and that a product larger
-than the array is refused. Collected last on purpose: it must pass both alone in a
-fresh process and after every other test.
+tests make two calls in a row (the second reusing the array the first left behind)
+and check each against the CPU oracle bit for bit, and against the ordinary
+allocating entry point; a product larger than the array is refused. Collected last on
+purpose: it must pass both alone in a fresh process and after every other test.
 """
 import ctypes
 
@@ -14,11 +14,13 @@ import numpy as np
 import pytest
 
 import uor_b200 as U
-from gpu_util import needs_gpu, torch
+from gpu_util import i128_values, needs_gpu, oracle_int, torch
 
 pytestmark = [pytest.mark.gpu, needs_gpu]
 
 SCRATCH_LIMIT = 9
+TORCH_OUT = {U.I8: "int8", U.I16: "int16", U.I32: "int32", U.I64: "int64", U.I128: "int64"}
+NP_OUT = {U.I8: np.int8, U.I16: np.int16, U.I32: np.int32, U.I64: np.int64, U.I128: np.int64}
 
 
 def _noalloc(out, m, k, n, alpha, a, lda, b, ldb, beta, c, ldc, encode=U.NEAREST, stream=None):
@@ -32,35 +34,57 @@ def _noalloc(out, m, k, n, alpha, a, lda, b, ldb, beta, c, ldc, encode=U.NEAREST
               encode, stream)
 
 
-def _reference_entry(out, m, k, n, alpha, a, b, beta, c):
-    U.slice_gemm_ex(U.I8, out, m, k, n, alpha, a, k, b, n, beta, c, n)
+def _prior(out, salt, cells):
+    """A prior C with values spread over the whole output range."""
+    raw = U.corpus(salt, U.CORPUS_RAW, cells * (2 if out == U.I128 else 1)).astype(np.uint64)
+    wide = (raw << np.uint64(31)) ^ raw
+    return wide.view(np.int64).astype(NP_OUT[out], casting="unsafe")
 
 
-@pytest.mark.parametrize("out,dtype", [(U.I64, torch.int64 if torch else None),
-                                       (U.I32, torch.int32 if torch else None)])
-def test_noalloc_matches_the_allocating_entry_on_two_calls(out, dtype):
-    m, k, n = 64, 140_000, 96  # past lane depth: two exact chunks live in the static scratch
-    for call, (alpha, beta) in enumerate([(1, 0), (3, -2)]):
-        a = torch.from_numpy(U.corpus(40 + call, U.CORPUS_I8, m * k)).cuda()
-        b = torch.from_numpy(U.corpus(50 + call, U.CORPUS_I8, k * n)).cuda()
-        prior = torch.from_numpy(
-            U.corpus(60 + call, U.CORPUS_RAW, m * n).astype(np.int64)).to(dtype).cuda()
-        got = prior.clone()
-        want = prior.clone()
-        assert _noalloc(out, m, k, n, alpha, a, k, b, n, beta, got, n) == U.OK
-        _reference_entry(out, m, k, n, alpha, a, b, beta, want)
-        assert torch.equal(got, want), f"call {call}"
+def _same(out, x, y):
+    if out == U.I128:
+        return i128_values(x) == i128_values(y)
+    return np.array_equal(x, y)
+
+
+def _check_two_calls(out, mode, m, k, n, lda, ldb, ldc, scalars, salt):
+    for call, (alpha, beta) in enumerate(scalars):
+        a = U.corpus(salt + call, U.CORPUS_I8, m * lda)
+        b = U.corpus(salt + 10 + call, U.CORPUS_I8, k * ldb)
+        prior = _prior(out, salt + 20 + call, m * ldc)
+        want = prior.copy()
+        oracle_int(a, (m, k, lda, 1, 0), b, (k, n, ldb, 1, 0), want, (m, n, ldc, 1, 0), alpha,
+                   beta, mode, out)
+        dt = getattr(torch, TORCH_OUT[out])
+        got = torch.from_numpy(prior.copy()).to(dt).cuda()
+        ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        assert _noalloc(out, m, k, n, alpha, ta, lda, tb, ldb, beta, got, ldc, mode) == U.OK
+        assert _same(out, got.cpu().numpy(), want), f"call {call} vs the oracle"
+        # and the same bytes as the allocating entry point
+        ordinary = torch.from_numpy(prior.copy()).to(dt).cuda()
+        U.slice_gemm_ex(U.I8, out, m, k, n, alpha, ta, lda, tb, ldb, beta, ordinary, ldc,
+                        encode=mode)
+        assert torch.equal(got, ordinary), f"call {call} vs uor_b200_slice_gemm_ex"
+
+
+@pytest.mark.parametrize("out", [U.I8, U.I16, U.I32, U.I64, U.I128])
+@pytest.mark.parametrize("mode", [U.NEAREST, U.SATURATING, U.WRAPPING])
+def test_noalloc_deep_product_two_calls_against_the_oracle(out, mode):
+    # past the s32 lane depth: two exact chunks live in the static scratch, and the
+    # second call reuses what the first left there
+    _check_two_calls(out, mode, 64, 140_000, 96, 140_000, 96, 96, [(1, 0), (3, -2)], 40)
+
+
+def test_noalloc_padded_output_rows_and_one_row():
+    # ldc > n leaves the gaps as they were; m == 1 takes the single-row stride path
+    _check_two_calls(U.I64, U.NEAREST, 48, 140_000, 80, 140_000, 80, 83,
+                     [(1, 1), (-5, 2)], 140)
+    _check_two_calls(U.I32, U.SATURATING, 1, 262_200, 128, 262_200, 128, 128,
+                     [(1, 0), (2**40, -1)], 160)
 
 
 def test_noalloc_shallow_and_refusals():
-    m, k, n = 200, 4096, 320
-    a = torch.from_numpy(U.corpus(70, U.CORPUS_I8, m * k)).cuda()
-    b = torch.from_numpy(U.corpus(71, U.CORPUS_I8, k * n)).cuda()
-    got = torch.zeros(m * n, dtype=torch.int32, device="cuda")
-    want = torch.zeros(m * n, dtype=torch.int32, device="cuda")
-    assert _noalloc(U.I32, m, k, n, 1, a, k, b, n, 0, got, n) == U.OK
-    _reference_entry(U.I32, m, k, n, 1, a, b, 0, want)
-    assert torch.equal(got, want)
+    _check_two_calls(U.I32, U.NEAREST, 200, 4096, 320, 4096, 320, 320, [(1, 0), (7, 1)], 70)
     # chunks * m * n * 4 bytes beyond the fixed array is refused, not allocated
     m2, k2, n2 = 2048, 140_000, 1024
     a2 = torch.zeros(m2 * k2, dtype=torch.int8, device="cuda")

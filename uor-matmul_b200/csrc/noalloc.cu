@@ -70,8 +70,12 @@ extern "C" int uor_b200_gemm_ex_i8_noalloc(uor_b200_dtype out, size_t m, size_t 
         return UOR_B200_UNSUPPORTED;
     const bool chunked = (int64_t)k > K1_LANE_DEPTH;
     const size_t chunks = chunked ? (k + K1_CHUNK_K - 1) / K1_CHUNK_K : 1;
-    if (chunked && chunks * m * n * sizeof(int32_t) > UOR_B200_NOALLOC_SCRATCH_BYTES - kStatusBytes)
-        return UOR_B200_SCRATCH_LIMIT;
+    if (chunked) {
+        // chunks * m * n s32 partials must fit; compared by division, so no product of
+        // the three sizes is formed (it could wrap size_t before the comparison).
+        const size_t cells = (UOR_B200_NOALLOC_SCRATCH_BYTES - kStatusBytes) / sizeof(int32_t);
+        if (m > cells / n || m * n > cells / chunks) return UOR_B200_SCRATCH_LIMIT;
+    }
     if (k && (!tma_readable(a, m, lda) || !tma_readable(b, k, ldb))) return UOR_B200_UNSUPPORTED;
 
     int st = UOR_B200_OK;

@@ -173,3 +173,82 @@ def splitk_gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=U.NEARES
             dist.all_reduce(limbs, op=dist.ReduceOp.SUM, group=group)
         finish(elem, out, limbs, c, cv, alpha, beta, encode, ctx=ctx, asynchronous=True)
     return (k0, k1)
+
+
+class HostStaging:
+    """Device buffers (and a copy-out stream) that ``replicated_gemm_i8_host`` stages
+    host operands through; allocate once and reuse across calls."""
+
+    def __init__(self, a_bytes: int, b_bytes: int, c_bytes: int):
+        import torch
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.a = torch.empty(a_bytes, dtype=torch.uint8, device=dev)
+        self.b = torch.empty(b_bytes, dtype=torch.uint8, device=dev)
+        self.c = torch.empty(c_bytes, dtype=torch.uint8, device=dev)
+        self.out_stream = torch.cuda.Stream(dev)
+
+
+def replicated_gemm_i8_host(m, k, n, a_host, b_host, c_host, work: HostStaging, ctx=None,
+                            group=None, root=0, row_blocks=4):
+    """C_r := A B_r (slice::gemm::<i8, i32>, row-major) on every rank from pinned HOST
+    buffers, with A shared: the root uploads A once and it is broadcast over NCCL to
+    every rank, instead of one host upload per GPU; each rank uploads its own B block
+    and reads back its own C block (the column-block Partition, partition.rs:34).
+
+    The product runs in row blocks of A: block i's upload and broadcast, its GEMM and
+    its C copy-out queue behind one another, and block i's copy-out overlaps block
+    i + 1's upload and GEMM. a_host is read on the root only (None elsewhere). Returns
+    when c_host holds the result."""
+    import torch
+    import torch.distributed as dist
+    rank, world = _rank_world(group)
+    if m == 0 or n == 0:
+        return
+    stream = torch.cuda.current_stream()
+    if ctx is not None:
+        ctx.set_stream(stream.cuda_stream)
+    a_all = work.a[: m * k].view(torch.int8)
+    b = work.b[: k * n].view(torch.int8)
+    c_all = work.c[: 4 * m * n].view(torch.int32)
+    b.copy_(b_host.view(torch.int8)[: k * n], non_blocking=True)
+    src = dist.get_global_rank(group, root) if (world > 1 and group is not None) else root
+    step = -(-m // max(1, row_blocks))
+    for i0 in range(0, m, step):
+        rows = min(step, m - i0)
+        a = a_all[i0 * k: (i0 + rows) * k]
+        if rank == root and k:
+            a.copy_(a_host.view(torch.int8)[i0 * k: (i0 + rows) * k], non_blocking=True)
+        if world > 1 and k:
+            dist.broadcast(a, src=src, group=group)
+        c = c_all[i0 * n: (i0 + rows) * n]
+        U.gemm_i8_i32(rows, k, n, a, b, c, ctx=ctx, asynchronous=True)
+        done = torch.cuda.Event()
+        done.record(stream)
+        work.out_stream.wait_event(done)
+        with torch.cuda.stream(work.out_stream):
+            c_host.view(torch.int32)[i0 * n: (i0 + rows) * n].copy_(c, non_blocking=True)
+    stream.wait_stream(work.out_stream)
+    stream.synchronize()
+
+
+def bind_to_local_cpus(device: int) -> int:
+    """Restrict this process to the host cores NVML reports as closest to `device`
+    (its NUMA node), so pinned host buffers it allocates afterwards sit in memory
+    local to the GPU's PCIe root. Returns the number of cores kept (0: unchanged)."""
+    import os
+    try:
+        import pynvml
+        import torch
+        p = torch.cuda.get_device_properties(device)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, 16)
+    except Exception:
+        return 0
+    cpus = {64 * w + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+    cpus &= set(os.sched_getaffinity(0))
+    if not cpus:
+        return 0
+    os.sched_setaffinity(0, cpus)
+    return len(cpus)
