@@ -985,7 +985,8 @@ def wl_wide_splitk(args, U, torch, rank, world):
     w = SimpleNamespace(route=U.Route(), units=2.0 * m * k * n / world, launches=6)
 
     def step(i, ctx):
-        D.splitk_gemm(U.I32, U.I128, A, (m, k, k, 1), B, (k, n, n, 1), C, (m, n, n, 1), ctx=ctx)
+        D.splitk_gemm(U.I32, U.I128, A, (m, k, k, 1), B, (k, n, n, 1), C, (m, n, n, 1), ctx=ctx,
+                      partial=lambda *a, **kw: U.gemm_partial_limbs(*a, route=w.route, **kw))
 
     def check(last):
         want = torch.zeros_like(C)
@@ -1099,6 +1100,52 @@ def wl_i8_strong(args, U, torch, rank, world, dist, sets=3):
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src, "launch_ms": avg_ms / batch,
                 "pair_tiles_per_launch": -(-m // 256) * -(-cols // 256),
+                "traffic": None, "algorithmic_bytes": w.algorithmic_bytes}
+    w.roofline = roofline
+    return w
+
+
+def wl_trop_strong(args, U, torch, rank, world, dist):
+    """configs[4]'s max-plus half as one fixed Trop<i8> 8192^3 product sharded over the
+    ranks by output column blocks (partition.rs:34): rank r owns C[:, r n/N ..] and that
+    block of B; A is broadcast once over NCCL before the timed region."""
+    import uor_b200_dist as D
+    m = k = n = SIZE
+    t = D.column_blocks(m, n, world).tile(rank)
+    cols = t.cols if t is not None else 0
+    A = (torch.from_numpy(U.corpus(1, U.CORPUS_TROP_I8, m * k)).cuda() if rank == 0
+         else torch.empty(2 * m * k, dtype=torch.uint8, device="cuda"))
+    if dist:
+        dist.broadcast(A, src=0)
+    full = torch.from_numpy(U.corpus(2, U.CORPUS_TROP_I8, k * n)).view(k, n, 2)
+    B = full[:, t.col:t.col + cols].contiguous().view(-1).cuda()
+    del full
+    C = torch.zeros(8 * m * max(cols, 1), dtype=torch.uint8, device="cuda")
+    w = SimpleNamespace(route=U.Route(), units=float(m) * k * cols, launches=3)
+
+    def step(i, ctx):
+        U.gemm_tropical(U.TROP_I8, U.TROP_I32, A, (m, k, k, 1), B, (k, cols, cols, 1), C,
+                        (m, cols, cols, 1), ctx=ctx, route=w.route, asynchronous=True)
+
+    w.step, w.check, w.e2e, w.cpu = step, (lambda last: None), None, None
+    w.metric = "exact max-plus GEMM Tterm/s, one Trop<i8> 8192^3 product sharded over the GPUs"
+    w.unit, w.dtype = "Tterm/s", "int16x2 packed lanes"
+    w.scaling = "strong"
+    w.full_config = {
+        "workload": f"Trop<i8> max-plus 8192x8192x8192 in total, column blocks of {cols} per GPU",
+        "m": m, "k": k, "n": n, "n_per_gpu": cols,
+        "l2": "256 MiB of operands per GPU at N = 1 (> L2)",
+        "parallelism": f"column blocks x{world}; A broadcast once over NCCL before timing; "
+                       "no collective in the timed steps"}
+    w.config = w.full_config
+    w.algorithmic_bytes = 2 * (m * k + k * cols) + 8 * m * cols
+    w.flush = False
+
+    def roofline(avg_ms):
+        peak = 148 * 64 * 2 * 1.965e9 / 1e12
+        ach = w.units / (avg_ms / 1e3) / 1e12
+        return {"bound": "alu", "achieved": ach, "peak": peak, "unit": "Tterm/s",
+                "frac": ach / peak, "peak_source": "nominal packed i16x2 ALU rate (see trop line)",
                 "traffic": None, "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
@@ -1356,6 +1403,8 @@ def main():
             lambda: wl_i8_strong(args, U, torch, rank, world, dist), args.steps)
         line["wide_splitk"] = extra(
             lambda: wl_wide_splitk(args, U, torch, rank, world), max(args.steps, 20))
+        line["trop_8192_sharded"] = extra(
+            lambda: wl_trop_strong(args, U, torch, rank, world, dist), 6)
         if world == 1:
             # every other BASELINE config on the same GPU, each with its own bit-exact
             # row check against the oracle (the CPU leg)

@@ -378,6 +378,26 @@ int uor_b200_limbs_finish(uor_b200_dtype elem, uor_b200_dtype out, const int64_t
                           size_t limbs_len, const uor_b200_view_mut *c, int64_t alpha,
                           int64_t beta, const uor_b200_call *call);
 
+/* ------------------------------------------- tropical split-K exchange */
+
+/* driver::gemm over Trop<E> (crates/uor-matmul-gemm/src/driver.rs:102-182) with the
+ * reduction cut into ranges, e.g. one per device: the (max, +) reduction of A and B's
+ * views (one range of the reduction) as int64 keys, keys[i n + j], row-major, with
+ * INT64_MIN where no pair of finite terms exists (the semiring zero). The element-wise
+ * maximum of several ranges' keys (an all-reduce with MAX) is the reduction over their
+ * union, because max is associative and commutative -- the tropical Partition's
+ * split-K form (partition.rs:34-111). elem in {TROP_I8, TROP_I16, TROP_I32} (every sum
+ * fits in int64). Device pointers only (call->flags DEVICE_POINTERS). */
+int uor_b200_trop_partial_keys(uor_b200_dtype elem, const uor_b200_view *a,
+                               const uor_b200_view *b, int64_t *keys, size_t keys_len,
+                               const uor_b200_call *call);
+/* MaxPlus::finish (epilogue.rs:137-186) and the tropical encode (tropical.rs:336-351)
+ * from summed keys: C := (alpha (x) X) (+) (beta (x) C) with X the keys (INT64_MIN =
+ * -inf); out in {TROP_I8 .. TROP_I64}. Device pointers only. */
+int uor_b200_trop_keys_finish(uor_b200_dtype out, const int64_t *keys, size_t keys_len,
+                              const uor_b200_view_mut *c, uor_b200_trop alpha, uor_b200_trop beta,
+                              const uor_b200_call *call);
+
 /* ------------------------------------------------- no-allocation variant */
 
 /* Size of the fixed device scratch the no-allocation entry point uses. */

@@ -86,3 +86,66 @@ def gemm_cpu(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=0, ctx=None
     cn = c.numpy()
     orc.gemm_int(orc.View(an, *av), orc.View(bn, *bv), orc.View(cn, *cv), alpha=alpha, beta=beta,
                  mode=encode, out_bits=OBITS[out])
+
+
+# ---- tropical (driver::gemm over Trop<E>, MaxPlus, the clamp encode)
+
+TBITS = {U.TROP_I8: 8, U.TROP_I16: 16, U.TROP_I32: 32, U.TROP_I64: 64}
+INT64_MIN = -(1 << 63)
+
+
+def trop_partial_cpu(elem, a, av, b, bv, keys, ctx=None, asynchronous=False):
+    """One range's (max, +) reduction as int64 keys, through the oracle (Trop<i64> out,
+    alpha the identity, no C read)."""
+    m, k = av[0], av[1]
+    n = bv[1]
+    TD = orc.TROP_DTYPES
+    eb = TBITS[elem]
+    an, bn = a.numpy().view(TD[eb]), b.numpy().view(TD[eb])
+    x = np.zeros(m * n, TD[64])
+    orc.gemm_trop(orc.View(an, m, k, av[2], av[3]), orc.View(bn, k, n, bv[2], bv[3]),
+                  orc.View(x, m, n, n, 1), ebits=eb, obits=64)
+    kn = keys.numpy()
+    kn[: m * n] = np.where(x["f"] != 0, x["v"], INT64_MIN)
+
+
+def trop_finish_cpu(out, keys, c, cv, alpha=(0, True), beta=(0, False), encode=0, ctx=None,
+                    asynchronous=False):
+    """MaxPlus::finish (epilogue.rs:137-186) and the clamp encode (tropical.rs:336-351)."""
+    m, n, rs, cs = cv
+    ob = TBITS[out]
+    cn = c.numpy().view(orc.TROP_DTYPES[ob])
+    kn = keys.numpy()
+    mx = (1 << (ob - 1)) - 2
+    mn = -mx - 1
+    for i in range(m):
+        for j in range(n):
+            key = int(kn[i * n + j])
+            fin = key != INT64_MIN and alpha[1]
+            tot = key + alpha[0] if fin else 0
+            off = i * rs + j * cs
+            if beta[1] and cn["f"][off]:
+                s = int(cn["v"][off]) + beta[0]
+                if not fin or s > tot:
+                    tot, fin = s, True
+            if fin:
+                if encode == orc.WRAPPING:
+                    span = mx - mn + 1
+                    tot = ((tot - mn) % (1 << 128)) % span + mn
+                    tot = tot - (1 << 128) if tot >= (1 << 127) else tot
+                else:
+                    tot = max(mn, min(mx, tot))
+            cn["v"][off] = tot if fin else 0
+            cn["f"][off] = 1 if fin else 0
+
+
+def trop_gemm_cpu(elem, out, a, av, b, bv, c, cv, alpha=(0, True), beta=(0, False), encode=0,
+                  ctx=None):
+    """driver::gemm over Trop<E> on host byte tensors, through the oracle."""
+    TD = orc.TROP_DTYPES
+    an = a.numpy().view(TD[TBITS[elem]])
+    bn = b.numpy().view(TD[TBITS[elem]])
+    cn = c.numpy().view(TD[TBITS[out]])
+    orc.gemm_trop(orc.View(an, *av), orc.View(bn, *bv), orc.View(cn, *cv), ebits=TBITS[elem],
+                  obits=TBITS[out], alpha=alpha, beta=beta, mode=encode)
+

@@ -58,6 +58,16 @@ def _free_port():
     return port
 
 
+def _trop_draw(salt, count, bits, lo=-64, hi=63):
+    """Trop<E> values in [lo, hi] with about 5 % at the semiring zero (value stored 0)."""
+    raw = U.corpus(salt, U.CORPUS_RAW, count)
+    t = np.zeros(count, orc.TROP_DTYPES[bits])
+    fin = (raw >> np.uint64(20)) % np.uint64(100) >= np.uint64(5)
+    t["v"] = np.where(fin, (raw % np.uint64(hi - lo + 1)).astype(np.int64) + lo, 0)
+    t["f"] = fin
+    return t
+
+
 def _worker(rank, world, port, case):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -89,6 +99,52 @@ def _worker(rank, world, port, case):
                              orc.View(want, m, n, n, 1), alpha=alpha, beta=beta, mode=mode,
                              out_bits=S.OBITS[out])
                 assert np.array_equal(c.numpy(), want), (rank, elem, out, m, k, n)
+        elif case == "trop-splitk":
+            # driver::gemm over Trop<E> with the reduction split across the two ranks:
+            # int64 keys, an all-reduce of MAX, MaxPlus and the encode once
+            TD = orc.TROP_DTYPES
+            for elem, out, (m, k, n), alpha, beta, mode in [
+                    (U.TROP_I8, U.TROP_I32, (5, 301, 7), (0, True), (0, False), U.NEAREST),
+                    (U.TROP_I8, U.TROP_I8, (4, 260, 6), (100, True), (-3, True), U.NEAREST),
+                    (U.TROP_I16, U.TROP_I16, (3, 129, 5), (2**14, True), (7, True), U.WRAPPING),
+                    (U.TROP_I8, U.TROP_I32, (6, 40, 4), (5, False), (1, True), U.NEAREST),
+                    (U.TROP_I8, U.TROP_I64, (2, 1, 3), (0, True), (0, False), U.NEAREST)]:
+                eb, ob = S.TBITS[elem], S.TBITS[out]
+                a = _trop_draw(11 + m, m * k, eb)
+                b = _trop_draw(12 + n, k * n, eb)
+                prior = _trop_draw(13, m * n, ob, lo=-100, hi=100)
+                c = torch.from_numpy(prior.copy().view(np.uint8))
+                D.splitk_gemm_tropical(elem, out, torch.from_numpy(a.view(np.uint8)),
+                                       (m, k, k, 1), torch.from_numpy(b.view(np.uint8)),
+                                       (k, n, n, 1), c, (m, n, n, 1), alpha, beta, mode,
+                                       partial=S.trop_partial_cpu, finish=S.trop_finish_cpu)
+                want = prior.copy()
+                orc.gemm_trop(orc.View(a, m, k, k, 1), orc.View(b, k, n, n, 1),
+                              orc.View(want, m, n, n, 1), ebits=eb, obits=ob, alpha=alpha,
+                              beta=beta, mode=mode)
+                got = c.numpy().view(TD[ob])
+                assert np.array_equal(got["f"], want["f"]), (rank, elem, out)
+                fin = want["f"] != 0
+                assert np.array_equal(got["v"][fin], want["v"][fin]), (rank, elem, out)
+        elif case == "trop-columns":
+            TD = orc.TROP_DTYPES
+            m, k, n = 6, 45, 11
+            a = _trop_draw(21, m * k, 8)
+            b = _trop_draw(22, k * n, 8)
+            c = torch.zeros(m * n * 8, dtype=torch.uint8)
+            t = D.column_block_gemm_tropical(U.TROP_I8, U.TROP_I32,
+                                             torch.from_numpy(a.view(np.uint8)), (m, k, k, 1),
+                                             torch.from_numpy(b.view(np.uint8)), (k, n, n, 1), c,
+                                             (m, n, n, 1), (4, True), gather=True,
+                                             gemm=S.trop_gemm_cpu)
+            assert t is not None and t.cols > 0
+            want = np.zeros(m * n, TD[32])
+            orc.gemm_trop(orc.View(a, m, k, k, 1), orc.View(b, k, n, n, 1),
+                          orc.View(want, m, n, n, 1), ebits=8, obits=32, alpha=(4, True))
+            got = c.numpy().view(TD[32])
+            assert np.array_equal(got["f"], want["f"]), rank
+            fin = want["f"] != 0
+            assert np.array_equal(got["v"][fin], want["v"][fin]), rank
         else:
             m, k, n = 7, 33, 13
             a = U.corpus(1, U.CORPUS_I8, m * k)
@@ -106,6 +162,6 @@ def _worker(rank, world, port, case):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["splitk", "columns"])
+@pytest.mark.parametrize("case", ["splitk", "columns", "trop-splitk", "trop-columns"])
 def test_two_ranks_gloo(case):
     mp.spawn(_worker, args=(2, _free_port(), case), nprocs=2, join=True)

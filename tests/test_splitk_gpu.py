@@ -56,6 +56,56 @@ def test_ranges_summed_on_one_gpu_equal_the_whole(elem, out, shape, alpha, beta,
         assert torch.equal(got, want), (world, shape)
 
 
+def _trop(salt, count, bits, lo=-64, hi=63):
+    """Trop<E> values in [lo, hi], about 5 % the semiring zero (value 0), as bytes on the GPU."""
+    from oracle import oracle as orc
+    raw = U.corpus(salt, U.CORPUS_RAW, count)
+    t = np.zeros(count, orc.TROP_DTYPES[bits])
+    fin = (raw >> np.uint64(20)) % np.uint64(100) >= np.uint64(5)
+    t["v"] = np.where(fin, (raw % np.uint64(hi - lo + 1)).astype(np.int64) + lo, 0)
+    t["f"] = fin
+    return t, torch.from_numpy(t.view(np.uint8).copy()).cuda()
+
+
+@pytest.mark.parametrize("elem,out,shape,alpha,beta,mode", [
+    (U.TROP_I8, U.TROP_I32, (64, 4096, 96), (0, True), (0, False), U.NEAREST),
+    (U.TROP_I8, U.TROP_I8, (33, 1000, 17), (90, True), (-2, True), U.NEAREST),
+    (U.TROP_I16, U.TROP_I16, (20, 300, 30), (2**14, True), (5, True), U.WRAPPING),
+    (U.TROP_I32, U.TROP_I64, (9, 100, 11), (-7, True), (0, False), U.NEAREST),
+    (U.TROP_I8, U.TROP_I32, (5, 0, 7), (3, True), (1, True), U.NEAREST),
+])
+def test_trop_ranges_maxed_on_one_gpu_equal_the_whole(elem, out, shape, alpha, beta, mode):
+    """Trop<E> split-K: each range's keys, their element-wise max, MaxPlus and the encode
+    once give the single call's bytes and the oracle's values."""
+    from oracle import oracle as orc
+    TD = orc.TROP_DTYPES
+    bits = {U.TROP_I8: 8, U.TROP_I16: 16, U.TROP_I32: 32, U.TROP_I64: 64}
+    m, k, n = shape
+    eb, ob = bits[elem], bits[out]
+    ah, a = _trop(31 + m, m * k, eb)
+    bh, b = _trop(32 + n, k * n, eb)
+    ph, prior = _trop(33, m * n, ob, -100, 100)
+    want = prior.clone()
+    U.gemm_tropical(elem, out, a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), alpha, beta,
+                    mode)
+    ref = ph.copy()
+    orc.gemm_trop(orc.View(ah, m, k, k, 1), orc.View(bh, k, n, n, 1), orc.View(ref, m, n, n, 1),
+                  ebits=eb, obits=ob, alpha=alpha, beta=beta, mode=mode)
+    w = want.cpu().numpy().view(TD[ob])
+    assert np.array_equal(w["f"], ref["f"]) and np.array_equal(w["v"], ref["v"])
+    esz = {8: 2, 16: 4, 32: 8}[eb]
+    for world in (1, 2, 3):
+        total = torch.full((m * n,), -(2**63), dtype=torch.int64, device="cuda")
+        for k0, k1 in D.k_ranges(k, world):
+            keys = torch.full((m * n,), 12345, dtype=torch.int64, device="cuda")
+            U.trop_partial_keys(elem, a[k0 * esz:], (m, k1 - k0, k, 1), b[k0 * n * esz:],
+                                (k1 - k0, n, n, 1), keys)
+            total = torch.maximum(total, keys)
+        got = prior.clone()
+        U.trop_keys_finish(out, total, got, (m, n, n, 1), alpha, beta, mode)
+        assert torch.equal(got, want), (world, shape)
+
+
 def test_partial_limbs_validation():
     a, b = _operands(U.I32, 4, 8, 4)
     limbs = torch.zeros(4 * 4 * 3 - 1, dtype=torch.int64, device="cuda")
@@ -104,6 +154,21 @@ def _worker(rank, world, port):
         w2 = torch.zeros_like(c)
         U.gemm(U.I32, U.I64, a, (m, k, k, 1), b, (k, n, n, 1), w2, (m, n, n, 1), ctx=ctx)
         assert torch.equal(c, w2), rank
+        # Trop<i8> split-K (all-reduce of MAX over keys) and column blocks
+        ah, ta = _trop(41, m * k, 8)
+        bh, tb = _trop(42, k * n, 8)
+        tc = torch.zeros(m * n * 8, dtype=torch.uint8, device="cuda")
+        D.splitk_gemm_tropical(U.TROP_I8, U.TROP_I32, ta, (m, k, k, 1), tb, (k, n, n, 1), tc,
+                               (m, n, n, 1), (3, True), ctx=ctx)
+        torch.cuda.synchronize()
+        tw = torch.zeros_like(tc)
+        U.gemm_tropical(U.TROP_I8, U.TROP_I32, ta, (m, k, k, 1), tb, (k, n, n, 1), tw,
+                        (m, n, n, 1), (3, True), ctx=ctx)
+        assert torch.equal(tc, tw), rank
+        tc.zero_()
+        D.column_block_gemm_tropical(U.TROP_I8, U.TROP_I32, ta, (m, k, k, 1), tb, (k, n, n, 1),
+                                     tc, (m, n, n, 1), (3, True), ctx=ctx, gather=True)
+        assert torch.equal(tc, tw), rank
         ctx.close()
     finally:
         dist.destroy_process_group()

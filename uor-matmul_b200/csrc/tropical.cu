@@ -67,6 +67,11 @@ __device__ __forceinline__ void trop_store(uint8_t* base, int obytes, int64_t id
 
 // MaxPlus::finish + the tropical encode, for one cell whose reduction is (fin, v).
 __device__ __forceinline__ void trop_finish(const TropEpi& e, int64_t off, bool fin, i128 v) {
+    if (e.obytes == 0) {
+        // split-K key: the raw reduction of this range, the semiring zero as INT64_MIN
+        static_cast<int64_t*>(e.c)[off] = fin ? static_cast<int64_t>(v) : INT64_MIN;
+        return;
+    }
     // alpha (x) acc: -inf absorbs (ShiftExact, epilogue.rs:199-215)
     bool f = fin && e.alpha_finite;
     i128 t = f ? v + static_cast<i128>(e.alpha) : 0;
@@ -378,6 +383,17 @@ __global__ void trop_generic_witness_kernel(const uint8_t* __restrict__ a, int64
     w[static_cast<int64_t>(i) * rsw + static_cast<int64_t>(j) * csw] = static_cast<uint64_t>(at_p);
 }
 
+// MaxPlus::finish and the encode over summed split-K keys (one thread per cell).
+__global__ void trop_keys_finish_kernel(const int64_t* __restrict__ keys, int m, int n, TropEpi e) {
+    const int64_t total = static_cast<int64_t>(m) * n;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t i = idx / n, j = idx - i * n;
+        const int64_t key = keys[idx];
+        trop_finish(e, i * e.rsc + j * e.csc, key != INT64_MIN, static_cast<i128>(key));
+    }
+}
+
 static int grid_for(int64_t total) {
     const int64_t g = (total + 255) / 256;
     return static_cast<int>(g < 148 * 32 ? g : 148 * 32);
@@ -453,6 +469,13 @@ cudaError_t trop_generic_witness_launch(const uint8_t* a, int64_t rsa, int64_t c
     dim3 grid((n + 15) / 16, (m + 15) / 16);
     trop_generic_witness_kernel<<<grid, block, 0, s>>>(a, rsa, csa, b, rsb, csb, ebytes, k, e, w,
                                                        rsw, csw);
+    return cudaGetLastError();
+}
+
+cudaError_t trop_keys_finish_launch(const int64_t* keys, const TropEpi& e, cudaStream_t s) {
+    const int64_t total = static_cast<int64_t>(e.m) * e.n;
+    if (total == 0) return cudaSuccess;
+    trop_keys_finish_kernel<<<grid_for(total), 256, 0, s>>>(keys, e.m, e.n, e);
     return cudaGetLastError();
 }
 

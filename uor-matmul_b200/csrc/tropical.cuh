@@ -7,7 +7,9 @@
 
 namespace uor {
 
-// MaxPlus{alpha, beta} and the output view (Trop<O>, obytes = sizeof(O)).
+// MaxPlus{alpha, beta} and the output view (Trop<O>, obytes = sizeof(O)). obytes == 0
+// selects the split-K key output: int64 per cell, the raw reduction (alpha and beta are
+// not applied) or INT64_MIN where no term is finite.
 struct TropEpi {
     int64_t alpha, beta;
     int alpha_finite, beta_finite;
@@ -45,5 +47,9 @@ cudaError_t trop_generic_witness_launch(const uint8_t* a, int64_t rsa, int64_t c
                                         const uint8_t* b, int64_t rsb, int64_t csb, int ebytes,
                                         int m, int k, int n, const TropEpi& e, uint64_t* w,
                                         int64_t rsw, int64_t csw, cudaStream_t s);
+
+// MaxPlus::finish and the encode into e's output view, from int64 keys (m x n, row-major;
+// INT64_MIN = no finite term), e.g. the element-wise max of several ranges' keys.
+cudaError_t trop_keys_finish_launch(const int64_t* keys, const TropEpi& e, cudaStream_t s);
 
 }  // namespace uor

@@ -128,6 +128,8 @@ def lib():
             "uor_b200_arena_canonicalize": ([I, P, Z, ctypes.POINTER(Z)], I),
             "uor_b200_gemm_partial_limbs": ([I, VP, VP, P, Z, CP], I),
             "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
+            "uor_b200_trop_partial_keys": ([I, VP, VP, P, Z, CP], I),
+            "uor_b200_trop_keys_finish": ([I, P, Z, VP, Trop, Trop, CP], I),
             "uor_b200_status_string": ([I], ctypes.c_char_p),
             "uor_b200_version": ([], I),
             "uor_b200_selftest_wait_timeout": ([P, U64], I),
@@ -491,6 +493,33 @@ def limbs_finish(elem, out, limbs, c, cv, alpha=1, beta=0, encode=NEAREST, ctx=N
     call = make_call(encode, True, ctx, None, asynchronous)
     _check(lib().uor_b200_limbs_finish(elem, out, pl, _int64_len(limbs, ll), ctypes.byref(C),
                                        alpha, beta, ctypes.byref(call)), "limbs_finish")
+
+
+def trop_partial_keys(elem, a, av, b, bv, keys, ctx=None, route=None, asynchronous=False):
+    """One range of a Trop<E> reduction as int64 keys [m][n] (INT64_MIN: no finite term);
+    the element-wise max of ranges' keys is the reduction of their union (device buffers)."""
+    if not _on_device(a, b, keys):
+        raise UorError(INVALID_ARGUMENT, "trop_partial_keys takes device buffers")
+    A, B = view(a, *av), view(b, *bv)
+    pk, lk, _ = _buffer(keys)
+    call = make_call(NEAREST, True, ctx, route, asynchronous)
+    _check(lib().uor_b200_trop_partial_keys(elem, ctypes.byref(A), ctypes.byref(B), pk,
+                                            _int64_len(keys, lk), ctypes.byref(call)),
+           "trop_partial_keys")
+
+
+def trop_keys_finish(out, keys, c, cv, alpha=(0, True), beta=(0, False), encode=NEAREST, ctx=None,
+                     asynchronous=False):
+    """C := (alpha (x) X) (+) (beta (x) C), encoded, from keys X (device buffers)."""
+    if not _on_device(keys, c):
+        raise UorError(INVALID_ARGUMENT, "trop_keys_finish takes device buffers")
+    C = view(c, *cv)
+    pk, lk, _ = _buffer(keys)
+    call = make_call(encode, True, ctx, None, asynchronous)
+    _check(lib().uor_b200_trop_keys_finish(out, pk, _int64_len(keys, lk), ctypes.byref(C),
+                                           Trop(alpha[0], int(alpha[1])),
+                                           Trop(beta[0], int(beta[1])), ctypes.byref(call)),
+           "trop_keys_finish")
 
 
 def _int64_len(limbs, count):

@@ -7,6 +7,11 @@ Two decompositions, both exact by construction:
   whole columns per rank. Every output element is one exact sum computed on one
   device, so there is no exchange on the data path; ``gather=True`` then shares the
   blocks (an all-gather of finished bytes, outside the arithmetic).
+* Tropical (``column_block_gemm_tropical``, ``splitk_gemm_tropical``): the same two
+  decompositions of driver::gemm over Trop<E> (driver.rs:67-182). Split-K exchanges
+  each range's (max, +) reduction as int64 keys with one all-reduce of MAX (max is
+  associative and commutative, so the union of ranges is their maximum) and applies
+  MaxPlus and the encode once (uor_b200_trop_keys_finish).
 * Split-K (``splitk_gemm``): each rank takes a contiguous range of the reduction,
   computes its exact partial sum as radix-2^40 int64 limbs (uor_b200_gemm_partial_limbs),
   the limbs are summed across ranks with one all-reduce, and every rank encodes the
@@ -172,6 +177,47 @@ def splitk_gemm(elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=U.NEARES
         if world > 1:
             dist.all_reduce(limbs, op=dist.ReduceOp.SUM, group=group)
         finish(elem, out, limbs, c, cv, alpha, beta, encode, ctx=ctx, asynchronous=True)
+    return (k0, k1)
+
+
+def column_block_gemm_tropical(elem, out, a, av, b, bv, c, cv, alpha=(0, True), beta=(0, False),
+                               encode=U.NEAREST, ctx=None, group=None, gather=False,
+                               gemm: Callable | None = None):
+    """This rank's column block of driver::gemm over Trop<E> with MaxPlus{alpha, beta}
+    (scalars are (value, finite) pairs); a, b, c are byte tensors of Trop<E> / Trop<O>
+    structs holding the full views. As column_block_gemm, gather=True shares the blocks."""
+    return column_block_gemm(elem, out, a, av, b, bv, c, cv, alpha, beta, encode, ctx=ctx,
+                             group=group, gather=gather, gemm=gemm or U.gemm_tropical)
+
+
+def splitk_gemm_tropical(elem, out, a, av, b, bv, c, cv, alpha=(0, True), beta=(0, False),
+                         encode=U.NEAREST, ctx=None, group=None, partial: Callable | None = None,
+                         finish: Callable | None = None):
+    """driver::gemm over Trop<E> with the reduction split across ranks: every rank's range
+    reduced to int64 keys, one all-reduce of MAX, MaxPlus and the encode on every rank.
+    Every rank passes the same full views and C prior and ends with the single-device
+    call's bytes. elem in {TROP_I8, TROP_I16, TROP_I32}; queued on torch's current stream."""
+    import torch
+    import torch.distributed as dist
+    rank, world = _rank_world(group)
+    m, k = av[0], av[1]
+    n = bv[1]
+    for v in (av, bv):
+        _nonneg(v)
+    partial = partial or U.trop_partial_keys
+    finish = finish or U.trop_keys_finish
+    if ctx is not None and a.is_cuda:
+        ctx.set_stream(torch.cuda.current_stream(a.device).cuda_stream)
+    k0, k1 = k_ranges(k, world)[rank]
+    per_a = U.DTYPE_SIZE[elem] // a.element_size()
+    per_b = U.DTYPE_SIZE[elem] // b.element_size()
+    keys = torch.empty(m * n, dtype=torch.int64, device=a.device)
+    if m and n:
+        partial(elem, a[k0 * av[3] * per_a:], (m, k1 - k0, av[2], av[3]), b[k0 * bv[2] * per_b:],
+                (k1 - k0, n, bv[2], bv[3]), keys, ctx=ctx, asynchronous=True)
+        if world > 1:
+            dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
+        finish(out, keys, c, cv, alpha, beta, encode, ctx=ctx, asynchronous=True)
     return (k0, k1)
 
 
