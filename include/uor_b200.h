@@ -79,7 +79,12 @@ typedef enum uor_b200_dtype {
 /* ----------------------------------------------------------------- context */
 
 /* A device, a stream, device workspaces, and a status word for bounded waits.
- * Distinct contexts may be used from distinct threads concurrently. */
+ * Distinct contexts may be used from distinct threads concurrently. The library orders
+ * its device work device-wide: each call's stream first waits for the work of the
+ * previous call on the same device (whichever context, stream or thread queued it), so
+ * calls on different streams run one after another on the GPU, never side by side.
+ * Calls queued into a CUDA graph capture and the no-allocation entry take no part in
+ * that order; their callers order them. */
 typedef struct uor_b200_ctx uor_b200_ctx;
 
 uor_b200_ctx *uor_b200_ctx_create(int device);

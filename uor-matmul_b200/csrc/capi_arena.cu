@@ -97,6 +97,7 @@ int arena_common(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     cudaStream_t s = ctx->stream;
     const uint8_t* da = nullptr;
     OutStage cs;

@@ -129,6 +129,7 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
     cudaStream_t s = ctx->stream;
 
@@ -483,6 +484,7 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     cudaStream_t s = ctx->stream;
     const uint8_t* da = nullptr;
     OutStage cs;

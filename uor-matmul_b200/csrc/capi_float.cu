@@ -23,6 +23,7 @@ int float_placed(uor_b200_dtype elem, uor_b200_dtype out, const Operand& A, cons
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
     const uint8_t *da = nullptr, *db = nullptr;
     OutStage cs;

@@ -77,6 +77,7 @@ int int_gemm_placed(uor_b200_dtype elem, int kind, const Operand& A, const Opera
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     return int_gemm_locked(ctx, elem, kind, A, B, C, alpha, beta, mode, call, route, cplx);
 }
 
@@ -214,6 +215,7 @@ int uor_b200_gemm_partial_limbs(uor_b200_dtype elem, const uor_b200_view* a,
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     uor_b200_route local_route{};
     uor_b200_route* route = call->route ? call->route : &local_route;
     *route = uor_b200_route{};
@@ -263,6 +265,7 @@ int uor_b200_limbs_finish(uor_b200_dtype elem, uor_b200_dtype out, const int64_t
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     if (call->route) *call->route = uor_b200_route{};
     const LinearEpi epi{alpha, beta, mode, kind};
     if (limbs_finish(limbs, m, n, const_cast<uint8_t*>(C.origin), C.rs, C.cs, epi, ctx->stream) !=

@@ -57,6 +57,7 @@ int trop_common(uor_b200_dtype elem, uor_b200_dtype out, const uor_b200_view* a,
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     const bool dev = call && (call->flags & UOR_B200_DEVICE_POINTERS);
     const uint8_t *da = nullptr, *db = nullptr;
     OutStage cs, ws_out;
@@ -153,6 +154,7 @@ extern "C" int uor_b200_trop_partial_keys(uor_b200_dtype elem, const uor_b200_vi
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     uor_b200_route local{};
     uor_b200_route* route = call->route ? call->route : &local;
     *route = uor_b200_route{};
@@ -206,6 +208,7 @@ extern "C" int uor_b200_trop_keys_finish(uor_b200_dtype out, const int64_t* keys
     uor_b200_ctx* ctx = resolve_ctx(call, &st);
     if (!ctx) return st;
     std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceTurn turn(ctx);
     TropEpi e{};
     e.alpha = alpha.value;
     e.beta = beta.value;

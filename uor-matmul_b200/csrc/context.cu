@@ -85,6 +85,44 @@ uor_b200_ctx* resolve_ctx(const uor_b200_call* call, int* status) {
     return ctx;
 }
 
+namespace {
+struct DeviceOrder {
+    std::mutex mu;
+    cudaEvent_t tail = nullptr;  // recorded after the last call's work on this device
+};
+DeviceOrder& device_order(int device) {
+    static DeviceOrder order[64];
+    return order[device & 63];
+}
+}  // namespace
+
+DeviceTurn::DeviceTurn(uor_b200_ctx* ctx) : ctx_(ctx) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(ctx->stream, &cap) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    if (cap != cudaStreamCaptureStatusNone) return;
+    DeviceOrder& o = device_order(ctx->device);
+    o.mu.lock();
+    held_ = true;
+    if (!o.tail) {
+        if (cudaEventCreateWithFlags(&o.tail, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            o.tail = nullptr;
+        }
+    } else if (cudaStreamWaitEvent(ctx->stream, o.tail, 0) != cudaSuccess) {
+        cudaGetLastError();
+    }
+}
+
+DeviceTurn::~DeviceTurn() {
+    if (!held_) return;
+    DeviceOrder& o = device_order(ctx_->device);
+    if (o.tail && cudaEventRecord(o.tail, ctx_->stream) != cudaSuccess) cudaGetLastError();
+    o.mu.unlock();
+}
+
 int finish_call(uor_b200_ctx* ctx, const uor_b200_call* call) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return UOR_B200_DEVICE_ERROR;

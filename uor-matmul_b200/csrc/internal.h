@@ -43,6 +43,26 @@ uor_b200_ctx* default_ctx(int* status);
 // Resolve the call's context and make its device current.
 uor_b200_ctx* resolve_ctx(const uor_b200_call* call, int* status);
 
+// Device-wide order of this library's device work. Held for the span of one call
+// (after the context's lock): the call's stream first waits for everything the
+// previous call on the same device queued, whichever context or stream issued it,
+// and the call's own work becomes what the next call waits for. So no two calls'
+// kernels ever run side by side on one GPU -- in particular no tensor-core kernel
+// shares its SMs with another kernel of this library. Calls queued while their
+// stream is being captured into a CUDA graph take no part (the graph's replays are
+// ordered by whoever replays them).
+class DeviceTurn {
+  public:
+    explicit DeviceTurn(uor_b200_ctx* ctx);
+    ~DeviceTurn();
+    DeviceTurn(const DeviceTurn&) = delete;
+    DeviceTurn& operator=(const DeviceTurn&) = delete;
+
+  private:
+    uor_b200_ctx* ctx_;
+    bool held_ = false;
+};
+
 // After device work: synchronise (unless async) and fold the status word in.
 int finish_call(uor_b200_ctx* ctx, const uor_b200_call* call);
 
