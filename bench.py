@@ -41,7 +41,7 @@ sys.path.insert(0, ROOT)
 
 SIZE = 8192
 METRIC = "exact i8 GEMM TOPS at 8192^3 (bit-exact, int32 out)"
-WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "f32", "wide", "wide-splitk", "trop",
+WORKLOADS = ("i8", "i8-512", "gemv", "gemv-t", "codec", "codec-on-chip", "f32", "wide", "wide-splitk", "trop",
              "trop-witness", "complex", "codec-e8", "arena", "f64")
 
 
@@ -346,9 +346,10 @@ def wl_gemv(args, U, torch, rank, thin_m, sets=3):
     return w
 
 
-def wl_codec(args, U, torch, rank, sets=3):
+def wl_codec(args, U, torch, rank, sets=3, on_chip=False):
     """A 2048 x 8192 i8, B 8192 x 8192 nibble codes through a 16-entry
-    codebook (Packed<Grid<16>, 2>), exact i32 output."""
+    codebook (Packed<Grid<16>, 2>), exact i32 output. on_chip: decoded in the GEMM's
+    shared-memory stages only (CODEC_ON_CHIP), never into a dense copy."""
     import numpy as np
     m, k, n = 2048, 8192, 8192
     A = [torch.from_numpy(U.corpus(1 + 100 * s, U.CORPUS_I8, m * k)).cuda() for s in range(sets)]
@@ -361,7 +362,7 @@ def wl_codec(args, U, torch, rank, sets=3):
 
     def step(i, ctx):
         U.coded_gemm(U.I32, A[i % sets], (m, k, k, 1), Q[i % sets], k, n, 2, table, C,
-                     (m, n, n, 1), ctx=ctx, route=w.route, asynchronous=True)
+                     (m, n, n, 1), ctx=ctx, route=w.route, asynchronous=True, on_chip=on_chip)
 
     def dense(s):
         q = Q[s].to(torch.int64)
@@ -400,7 +401,7 @@ def wl_codec(args, U, torch, rank, sets=3):
         Th = table.cpu().pin_memory()
         Ch = torch.empty(m * n, dtype=torch.int32).pin_memory()
         return timed_host(lambda: U.coded_gemm(U.I32, Ah, (m, k, k, 1), Qh, k, n, 2, Th, Ch,
-                                               (m, n, n, 1), ctx=ctx),
+                                               (m, n, n, 1), ctx=ctx, on_chip=on_chip),
                           steps, stream, m * k + k * n // 2 + 16, 4 * m * n)
 
     w.step, w.check, w.cpu, w.e2e = step, check, cpu, e2e
@@ -1162,6 +1163,8 @@ def build_workload(name, args, U, torch, rank, world=1):
         return wl_gemv(args, U, torch, rank, False)
     if name == "codec":
         return wl_codec(args, U, torch, rank)
+    if name == "codec-on-chip":
+        return wl_codec(args, U, torch, rank, on_chip=True)
     if name == "f32":
         return wl_f32(args, U, torch, rank, args.size or 4096)
     if name == "wide":
@@ -1414,6 +1417,8 @@ def main():
                     cpu_budget=2.0),
                 "configs[1] codec 2048x8192x8192": extra(
                     lambda: wl_codec(args, U, torch, rank), 100, e2e_steps=3, cpu_budget=4.0),
+                "configs[1] codec, decoded on chip only (CODEC_ON_CHIP)": extra(
+                    lambda: wl_codec(args, U, torch, rank, on_chip=True), 100, cpu_budget=2.0),
                 "configs[2] exact f32 4096^3": extra(
                     lambda: wl_f32(args, U, torch, rank, 4096), 60, e2e_steps=3,
                     cpu_budget=4.0),

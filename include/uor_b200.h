@@ -132,13 +132,20 @@ typedef struct uor_b200_route {
 /* Exact float and wide integers: take the modular route wherever its moduli cover the
  * product's bound, whatever the estimated cost. Exact; the same bytes. */
 #define UOR_B200_MODULAR 8u
+/* Codec tier (Packed<Grid<N>, 2>): decode the codes on chip only, never into a dense copy
+ * of the coded operand in device memory. From 256 activation rows up (k up to one s32
+ * lane, 131071) this runs K1's CTA-pair GEMM with the codes decoded straight into its
+ * shared-memory B stages; below that the fused K5 kernel. Without the flag, products of
+ * 512 rows and more decode once into a k x n workspace and run K1, which is faster
+ * (configs[1]: 2,380 against 1,500 TOPS). The same bytes either way. */
+#define UOR_B200_CODEC_ON_CHIP 16u
 
 /* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)
  * plus where the pointers live. A NULL call means: Nearest, host pointers,
  * the default context of the current device. */
 typedef struct uor_b200_call {
     uint32_t encode;        /* uor_b200_encode */
-    uint32_t flags;         /* DEVICE_POINTERS | ASYNC | DIGIT_SLICES | MODULAR */
+    uint32_t flags;         /* DEVICE_POINTERS | ASYNC | DIGIT_SLICES | MODULAR | CODEC_ON_CHIP */
     uor_b200_ctx *ctx;      /* NULL: the current device's default context */
     uor_b200_route *route;  /* optional out */
 } uor_b200_call;

@@ -1,6 +1,8 @@
-"""K5 (codebook decode fused into the tensor-core pipeline) and, from 512 activation rows
-up, the one-pass nibble decode followed by K1, against the oracle's coded_gemm /
-gemm_tabulated restatement."""
+"""The codec tier against the oracle's coded_gemm / gemm_tabulated restatement: K5 (the
+codebook decode fused into the tensor-core pipeline, decoded weights on the M side), the
+one-pass decode followed by K1 (the default from 512 activation rows up), and, with
+CODEC_ON_CHIP, K1C (K1's CTA-pair pipeline with the codes decoded into its B stages, no
+dense copy anywhere) from 256 rows up."""
 import numpy as np
 import pytest
 
@@ -21,7 +23,7 @@ def make_codes(rng, rows, cols, P):
 
 
 def run(m, k, n, P, N, orientation, out=U.I32, alpha=1, beta=0, mode=U.NEAREST, seed=0,
-        av=None):
+        av=None, on_chip=False):
     rng = np.random.default_rng(seed)
     a = rng.integers(-128, 128, size=m * k).astype(np.int8)
     rows, cols = (k, n) if orientation == 0 else (n, k)
@@ -33,7 +35,7 @@ def run(m, k, n, P, N, orientation, out=U.I32, alpha=1, beta=0, mode=U.NEAREST, 
     route = U.Route()
     av = av or (m, k, k, 1)
     U.coded_gemm(out, a, av, codes, k, n, P, table, got, (m, n, n, 1), alpha, beta, mode,
-                 route=route, tabulated=orientation == 1)
+                 route=route, tabulated=orientation == 1, on_chip=on_chip)
     obits = {U.I32: 32, U.I64: 64, U.I128: 128, U.I16: 16, U.I8: 8}[out]
     origin = -orc.extent(*av)[0]
     if out != U.I128:
@@ -72,10 +74,9 @@ def test_fused_nibbles(orientation, shape):
 
 @pytest.mark.parametrize("orientation", [0, 1])
 def test_decoded_nibbles_many_rows(orientation):
-    """512 activation rows and more: the codes are decoded once to dense int8 (flat over the
-    code bytes, low nibble first) and K1 runs on them, K-major for the n x k codes."""
+    """512 activation rows and more, by default: the codes are decoded once to dense int8
+    (flat over the code bytes, low nibble first) and K1 runs on them."""
     for m, k, n, out, alpha, beta, N in [(512, 256, 96, U.I32, 1, 0, 16),
-                                         (600, 320, 64, U.I64, 3, -1, 7),
                                          (1030, 96, 288, U.I8, -2, 5, 16)]:
         got, want, route = run(m, k, n, 2, N, orientation, out, alpha, beta, seed=m + N)
         assert np.array_equal(got, want), (m, k, n, out)
@@ -83,9 +84,46 @@ def test_decoded_nibbles_many_rows(orientation):
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
-def test_decoded_nibbles_device_table(orientation):
-    """Device pointers on the decode-once route: the decode kernel builds the register table
-    from the device table itself (a 7-entry book, so table[v % 7])."""
+def test_pair_decode_many_rows(orientation):
+    """CODEC_ON_CHIP, 256 activation rows and more: K1C decodes the nibbles into the
+    swizzled B stages of K1's CTA-pair pipeline (never a dense B); ragged rows, columns
+    and reductions (the TMA fills codes past the edge with zeros, which decode to
+    table[0] but meet zero activations), every output width and the exact Linear
+    epilogue."""
+    for m, k, n, out, alpha, beta, N in [(512, 256, 96, U.I32, 1, 0, 16),
+                                         (600, 320, 64, U.I64, 3, -1, 7),
+                                         (1030, 96, 288, U.I8, -2, 5, 16),
+                                         (256, 128, 512, U.I32, 1, 0, 16),
+                                         (777, 992, 608, U.I32, 1, 0, 16),
+                                         (520, 4096, 320, U.I128, 2**40, 1, 11)]:
+        got, want, route = run(m, k, n, 2, N, orientation, out, alpha, beta, seed=m + N,
+                               on_chip=True)
+        assert np.array_equal(got, want), (m, k, n, out)
+        assert route.kernel == 4 and route.b_layout != 3 and route.tile_m == 256
+
+
+def test_pair_decode_gathered_activations():
+    m, k, n = 320, 96, 64
+    got, want, route = run(m, k, n, 2, 16, 0, av=(m, k, 1, m), seed=19, on_chip=True)
+    assert np.array_equal(got, want)
+    assert route.a_layout == 2 and route.tile_m == 256
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+def test_decode_once_past_the_lane(orientation):
+    """k past the s32 lane depth with 512+ rows: decoded once to dense int8, then K1 in
+    exact chunks."""
+    m, k, n = 512, 131_200, 32
+    got, want, route = run(m, k, n, 2, 16, orientation, U.I64, seed=5)
+    assert np.array_equal(got, want)
+    assert route.kernel == 4 and route.b_layout == 3 and route.k_chunks == 2
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("on_chip", [False, True])
+def test_decoded_nibbles_device_table(orientation, on_chip):
+    """Device pointers and a device table (a 7-entry book, so table[v % 7]) read by the
+    kernels themselves: the one-pass decode, and K1C's decoders."""
     m, k, n, N = 640, 192, 160, 7
     rng = np.random.default_rng(70 + orientation)
     a = rng.integers(-128, 128, size=m * k).astype(np.int8)
@@ -99,9 +137,9 @@ def test_decoded_nibbles_device_table(orientation):
     route = U.Route()
     U.coded_gemm(U.I32, torch.from_numpy(a).cuda(), (m, k, k, 1), torch.from_numpy(codes).cuda(),
                  k, n, 2, torch.from_numpy(table).cuda(), tc, (m, n, n, 1), route=route,
-                 tabulated=orientation == 1)
+                 tabulated=orientation == 1, on_chip=on_chip)
     assert np.array_equal(tc.cpu().numpy(), want)
-    assert route.kernel == 4 and route.b_layout == 3
+    assert route.kernel == 4 and (route.b_layout != 3) == on_chip
 
 
 @pytest.mark.parametrize("orientation", [0, 1])

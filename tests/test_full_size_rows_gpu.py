@@ -88,15 +88,19 @@ def test_wide_i32_to_i128_config4_row_blocks():
     assert np.any((hi != 0) & (hi != -1)) or np.any((hi == 0) & (lo < 0))
 
 
-def test_codec_config2_row_blocks():
-    """2048 x 8192 activations, 8192 x 8192 nibble codes, 16-entry book."""
+@pytest.mark.parametrize("on_chip", [False, True])
+def test_codec_config2_row_blocks(on_chip):
+    """2048 x 8192 activations, 8192 x 8192 nibble codes, 16-entry book; by
+    default (decoded once, then K1) and decoded on chip only (K1C)."""
     m, k, n = 2048, 8192, 8192
     a = U.corpus(1, U.CORPUS_I8, m * k)
     q = U.corpus(2, U.CORPUS_NIBBLES, k * n)
     t = U.corpus(7, U.CORPUS_I8, 16)
     tc = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    route = U.Route()
     U.coded_gemm(U.I32, torch.from_numpy(a).cuda(), (m, k, k, 1), torch.from_numpy(q).cuda(), k,
-                 n, 2, torch.from_numpy(t).cuda(), tc, (m, n, n, 1))
+                 n, 2, torch.from_numpy(t).cuda(), tc, (m, n, n, 1), route=route, on_chip=on_chip)
+    assert (route.b_layout != 3) == on_chip
     c = tc.cpu().numpy()
     for r0, r1 in row_blocks(m):
         want = np.zeros((r1 - r0) * n, np.int32)

@@ -2,6 +2,7 @@
 // of gemm_tabulated (codes n x k), over Packed<Grid<N>, P> codes.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 #include "aux.cuh"
@@ -150,10 +151,18 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool fused = per_byte == 2 && table_len <= 16 && k > 0 &&
                        (orientation == 0 ? (n % 32 == 0) : (k % 32 == 0)) &&
                        (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
-    const bool decode_once = fused && m >= 2 * (size_t)K5_BN;
+    // On-chip decoding only (UOR_B200_CODEC_ON_CHIP): from one 256-row activation tile up,
+    // K1C -- K1's CTA-pair pipeline with the codes decoded into its B stages, no dense B
+    // anywhere; smaller products (and reductions deeper than one s32 lane) take K5. By
+    // default, products of two activation tiles and more decode every weight once into a
+    // workspace and run K1, which measured faster at configs[1] (0.115 against 0.184 ms):
+    // K1C's decoder warps spend about half the SM's issue slots on the decode.
+    const bool on_chip = call && (call->flags & UOR_B200_CODEC_ON_CHIP);
+    const bool pair_fused = fused && on_chip && m >= (size_t)K5_BN && (int64_t)k <= K1_LANE_DEPTH;
+    const bool decode_once = fused && !on_chip && m >= 2 * (size_t)K5_BN;
     // The 16-entry effective table the fused decode uses: table[v % N]; a device table on
     // the decode-once route is read by the decode kernel itself (no host round trip).
-    const bool table_in_kernel = decode_once && dev && !table_on_host;
+    const bool table_in_kernel = (decode_once || pair_fused) && dev && !table_on_host;
     int8_t tab[256];
     const size_t tl = table_len < 256 ? table_len : 256;
     if (dev && !table_on_host) {
@@ -188,6 +197,74 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         if (st) return st;
         route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
         route->b_layout = 3;  // decoded to a dense workspace first
+    } else if (pair_fused) {
+        // Activations as K1's A: K-major rows, gathered if TMA cannot read them as given.
+        const uint8_t* xa = da;
+        uint64_t xstride = 0;
+        const size_t ldk = (k + 15) / 16 * 16;
+        const bool a_ok = (reinterpret_cast<uintptr_t>(da) & 15u) == 0 && (k == 1 || A.cs == 1) &&
+                          (m == 1 || (A.rs > 0 && (size_t)A.rs >= k && (A.rs & 15) == 0));
+        if (a_ok) {
+            xstride = m == 1 ? ldk : (uint64_t)A.rs;
+        } else {
+            uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, (m * ldk + 255) / 256 * 256, &st));
+            if (!ws) return st;
+            if (gather_2d(ws, ldk, da, m, k, A.rs, A.cs, 1, s) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+            xa = ws;
+            xstride = ldk;
+        }
+        K1CParams p{};
+        if (table_in_kernel) {
+            p.dtable = table;  // the decoders read the device table themselves
+            p.table_len = (int)table_len;
+        } else {
+            for (int w = 0; w < 4; ++w) {
+                uint32_t word = 0;
+                for (int bpos = 0; bpos < 4; ++bpos)
+                    word |= (uint32_t)(uint8_t)tab[(4 * w + bpos) % table_len] << (8 * bpos);
+                p.table[w] = word;
+            }
+        }
+        CUtensorMap tmA, tmQ, tmO;
+        bool ok = make_tmap_u8(&tmA, xa, k, m, xstride, 128, 128);
+        if (orientation == 0)
+            ok = ok && make_tmap_u8(&tmQ, dcodes, n / 2, k, n / 2, 64, 128, false);
+        else
+            ok = ok && make_tmap_u8(&tmQ, dcodes, k / 2, n, k / 2, 64, 128, false);
+        if (!ok) return UOR_B200_DEVICE_ERROR;
+        p.m = (int)m;
+        p.n = (int)n;
+        p.k_begin = 0;
+        p.num_kb = (int)((k + K1_BK - 1) / K1_BK);
+        p.tiles_m = (int)((m + 255) / 256);
+        p.tiles_n = (int)((n + 255) / 256);
+        p.num_tiles = p.tiles_m * p.tiles_n;
+        p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
+        p.c = cs.dev_origin;
+        p.rsc = C.rs;
+        p.csc = C.cs;
+        p.epi = epi;
+        p.fast = kind == OUT_I32 && alpha == 1 && beta == 0 && C.cs == 1 &&
+                 (m == 1 || (C.rs > 0 && (C.rs & 3) == 0 && (size_t)C.rs >= n)) &&
+                 (reinterpret_cast<uintptr_t>(cs.dev_origin) & 15u) == 0;
+        p.tma_store = p.fast && make_tmap_s32(&tmO, cs.dev_origin, n, m,
+                                              (uint64_t)(m == 1 ? (n + 3) / 4 * 4 : (size_t)C.rs) * 4,
+                                              32, 32);
+        p.idesc = idesc_i8(256, 256, true, true, false, orientation == 0);
+        p.status = ctx->d_status;
+        p.budget_ns = ctx->budget_ns;
+        const int mc = k1c_max_clusters();
+        route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
+        route->tile_m = 256;
+        route->tile_n = 256;
+        route->tile_k = K1_BK;
+        route->k_chunks = 1;
+        route->ctas = (uint32_t)(2 * (p.num_tiles < mc ? p.num_tiles : mc));
+        route->pairs = 1;
+        route->a_layout = a_ok ? 0 : 2;
+        route->b_layout = orientation == 0 ? 1 : 0;  // decoded on chip, never materialised
+        if (k1c_launch(tmA, tmQ, tmO, orientation, p, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
     } else if (!fused) {
         // Off the fused path (P != 2, N > 16, or code rows the TMA cannot address):
         // decode to a dense row-major k x n int8 matrix in the auxiliary slot, then K1.

@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include "gemm_i8.cuh"
 #include "int_epilogue.cuh"
 
 namespace uor {
@@ -55,5 +56,20 @@ __device__ __forceinline__ uint2 dec8(uint32_t w, uint32_t t0, uint32_t t1, uint
 //   orientation 0: dims {n/2, k}; orientation 1: dims {k/2, n}.
 cudaError_t k5_launch(const CUtensorMap& tmX, const CUtensorMap& tmC, const K5Params& p, int grid,
                       cudaStream_t stream);
+
+// K1C: K1's CTA-pair GEMM (256 x 256 tiles, p.idesc M256 N256) with B decoded on chip from
+// nibble codes through the 16-entry table (4 words, table[v % N] for v in 0..15).
+struct K1CParams : K1Params {
+    uint32_t table[4];
+    const int8_t* dtable;  // when set: the table in device memory, read by the kernel
+    int table_len;         // its entries N (1..16)
+};
+// tmA: activations K-major, dims {k, m}, box {128, 128}, 128-byte swizzle.
+// tmQ: codes, no swizzle, box {64 bytes, 128 rows}: orientation 0 dims {n/2, k},
+//      orientation 1 dims {k/2, n}. With p.tma_store, tmC is the s32 output map
+//      (dims {n, m}, box {32, 32}, 128-byte swizzle). k must not exceed K1_LANE_DEPTH.
+cudaError_t k1c_launch(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
+                       int orientation, const K1CParams& p, cudaStream_t stream);
+int k1c_max_clusters();
 
 }  // namespace uor

@@ -1,0 +1,466 @@
+// gemm_coded_pair.cu -- K1C: the codec tier's product on CTA pairs with the codebook decode
+// inside the tensor-core pipeline.
+//
+// Replaces coded_gemm (crates/uor-matmul-gemm/src/coded.rs:98-142) and gemm_tabulated's
+// product (tabulated.rs:2555) for Packed<Grid<N>, 2> (codecs.rs:80-196) when there are
+// activation rows to fill 256-row tiles: C = A decode(codes), exact s32 accumulation.
+//
+// It is K1's pair kernel (gemm_i8_pair.cu: 256 x 256 output tile per cluster of two
+// CTAs, M256 N256 K32 tcgen05 MMAs issued by the leader, double-buffered TMEM
+// accumulators, TMA-store epilogue) with the B stage produced on chip instead of loaded:
+// the producer brings A (128 rows per CTA) and this CTA's 8 KiB of raw codes for 128
+// weight columns; eight decoder warps per CTA expand the nibbles through the 16-entry
+// codebook held in registers (dec8: byte permutes) straight into the 128-byte-swizzled
+// operand layout a TMA load of a dense B would have produced, fence the writes to the
+// async proxy, and arrive on the leader's dec barrier. No dense B exists anywhere: each
+// code byte is read from HBM/L2 once per 256-row activation tile and decoded once per
+// CTA pair tile.
+//
+// Orientation 0 (codes k x n, coded_gemm): B is MN-major, row r of the tile is k index r
+// and its 128 bytes are 128 consecutive weight columns. Orientation 1 (codes n x k,
+// gemm_tabulated's A W^T): B is K-major, row r is weight column r and its bytes are
+// consecutive k. The decode and the swizzled store are the same in both: code byte b of a
+// row holds elements 2b (low nibble) and 2b + 1 (high nibble); 16-byte unit q of row r is
+// stored at r * 128 + ((q ^ (r & 7)) << 4).
+//
+// Two rings. The A/B ring (KC_STAGES): TMA brings A; the decoders fill B. full[s]
+// (leader) counts both CTAs' A bytes and, as the sign that both CTAs' decoded halves are in
+// place, one 16-byte bulk copy from each CTA into the leader's shared memory, issued after
+// the CTA's decoder warps have fenced their stores to the async proxy and met at a named
+// barrier; empty[s] (each CTA) is the leader's MMA commit, multicast to the pair. The codes
+// ring (KC_QSTAGES, its own producer warp) runs ahead of it: cfull[q] counts a slot's code
+// bytes, cempty[q] takes one arrival per decoder warp once the slot is decoded. So every
+// wait on the MMA's path completes on an async-proxy event (TMA bytes, bulk-copy bytes,
+// tcgen05 commits), as in K1, and the codes' load latency is off that path.
+#include <cuda_runtime.h>
+#include "gemm_coded.cuh"
+#include "gemm_i8.cuh"
+#include "ptx.cuh"
+
+namespace uor {
+
+constexpr int KC_BM = 256, KC_BN = 256, KC_BK = 128;
+constexpr int KC_STAGES = 5;   // A/B ring
+constexpr int KC_QSTAGES = 6;  // codes ring
+constexpr int KC_DEC_WARPS = 8;
+// warp 0 A producer, 1 MMA, 2-5 epilogue, 6 codes producer, 7-14 decoders
+constexpr int KC_DEC_WARP0 = 7;
+constexpr int KC_THREADS = 32 * (KC_DEC_WARP0 + KC_DEC_WARPS);
+constexpr int KC_A_BYTES = 128 * KC_BK;      // this CTA's activation rows
+constexpr int KC_B_BYTES = 128 * KC_BK;      // this CTA's decoded weight columns
+constexpr int KC_C_BYTES = 128 * KC_BK / 2;  // their codes
+constexpr int KC_STAGE_BYTES = KC_A_BYTES + KC_B_BYTES;
+constexpr int KC_EPI_BYTES = 4 * 4096;  // one 32 x 32 s32 staging block per epilogue warp
+constexpr int KC_RELAY = 16;            // bytes of one decode-done signal copy
+constexpr int KC_SMEM_BYTES = KC_STAGES * KC_STAGE_BYTES + KC_QSTAGES * KC_C_BYTES +
+                              KC_EPI_BYTES + 1024 + 256 + 256;
+static_assert(KC_SMEM_BYTES <= 232448, "K1C exceeds the opt-in shared memory per block");
+static_assert(2 * (2 * KC_STAGES + 2 * KC_QSTAGES + 5) * 4 + 8 <= 256, "barrier area");
+
+__device__ __forceinline__ void kc_tile(int t, const K1CParams& p, int& tm, int& tn) {
+    const int group = p.group_m * p.tiles_n;
+    const int g = t / group;
+    const int first = g * p.group_m;
+    const int rows = min(p.tiles_m - first, p.group_m);
+    const int r = t - g * group;
+    tm = first + r % rows;
+    tn = r / rows;
+}
+
+template <bool B_MN>
+__global__ void __launch_bounds__(KC_THREADS, 1)
+    k1c_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmC, const K1CParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* codes = smem + KC_STAGES * KC_STAGE_BYTES;             // 1 KiB aligned
+    uint8_t* epi_smem = codes + KC_QSTAGES * KC_C_BYTES;             // 1 KiB aligned
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + KC_EPI_BYTES);
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + KC_STAGES);
+    const uint32_t cfull0 = smem_u32(bars + 2 * KC_STAGES);
+    const uint32_t cempty0 = smem_u32(bars + 2 * KC_STAGES + KC_QSTAGES);
+    const uint32_t tfull0 = smem_u32(bars + 2 * KC_STAGES + 2 * KC_QSTAGES);
+    const uint32_t tempty0 = tfull0 + 16;
+    const uint32_t drain = tfull0 + 32;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * KC_STAGES + 2 * KC_QSTAGES + 5);
+    // decode-done signals: a 16-byte source, and per stage and rank a 16-byte landing slot
+    // in the leader
+    const uint32_t relay_src = smem_u32(reinterpret_cast<uint8_t*>(bars) + 256);
+    const uint32_t relay_dst0 = relay_src + KC_RELAY;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cid = static_cast<int>(cluster_id_x());
+    const int ncl = static_cast<int>(nclusters_x());
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < KC_STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int q = 0; q < KC_QSTAGES; ++q) {
+            mbar_init(cfull0 + 8 * q, 1);
+            mbar_init(cempty0 + 8 * q, KC_DEC_WARPS);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull0 + 8 * b, 1);
+            mbar_init(tempty0 + 8 * b, 8);  // 4 epilogue warps in each CTA of the pair
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmQ);
+        if (p.tma_store) tma_prefetch_desc(&tmC);
+    }
+    if (warp == 1) tmem_alloc_pair(smem_u32(tmem_slot), 2 * KC_BN);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before either signals the other
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ A producer (both CTAs)
+        if (elect_one()) {
+            const uint64_t pol = l2_policy_evict_last();
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            bool armed[KC_STAGES];
+            uint32_t armed_parity[KC_STAGES];
+            for (int s = 0; s < KC_STAGES; ++s) armed[s] = false, armed_parity[s] = 0;
+            for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+                int tm, tn;
+                kc_tile(t, p, tm, tn);
+                const int row0 = tm * KC_BM + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
+                                   KERR_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb_local = full0 + 8 * stage;
+                    if (leader) {
+                        mbar_expect_tx(fb_local, 2 * KC_A_BYTES + 2 * KC_RELAY);
+                        armed[stage] = true;
+                        armed_parity[stage] = phase;
+                    }
+                    tma_load_2d_pair(smem_u32(smem + stage * KC_STAGE_BYTES), &tmA,
+                                     mapa_shared(fb_local, 0), kb * KC_BK, row0, pol);
+                    if (++stage == KC_STAGES) stage = 0, phase ^= 1;
+                }
+            }
+            if (!ok && leader)
+                for (int s = 0; s < KC_STAGES; ++s)
+                    if (armed[s])
+                        mbar_wait(full0 + 8 * s, armed_parity[s], p.budget_ns, p.status,
+                                  KERR_TIMEOUT_DRAIN);
+        }
+        __syncwarp();
+    } else if (warp == 6) {
+        // ------------------------------------------------------------ codes producer (both CTAs)
+        if (elect_one()) {
+            const uint64_t pol = l2_policy_evict_last();
+            int q = 0;
+            uint32_t qph = 0;
+            bool ok = true;
+            bool armed[KC_QSTAGES];
+            uint32_t armed_parity[KC_QSTAGES];
+            for (int i = 0; i < KC_QSTAGES; ++i) armed[i] = false, armed_parity[i] = 0;
+            for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+                int tm, tn;
+                kc_tile(t, p, tm, tn);
+                const int col0 = tn * KC_BN + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(cempty0 + 8 * q, qph ^ 1, p.budget_ns, p.status,
+                                   KERR_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t cb = cfull0 + 8 * q;
+                    mbar_expect_tx(cb, KC_C_BYTES);
+                    armed[q] = true;
+                    armed_parity[q] = qph;
+                    const uint32_t sq = smem_u32(codes + q * KC_C_BYTES);
+                    const int kc = kb * KC_BK;
+                    if (B_MN) tma_load_2d(sq, &tmQ, cb, col0 / 2, kc, pol);
+                    else tma_load_2d(sq, &tmQ, cb, kc / 2, col0, pol);
+                    if (++q == KC_QSTAGES) q = 0, qph ^= 1;
+                }
+            }
+            if (!ok)
+                for (int i = 0; i < KC_QSTAGES; ++i)
+                    if (armed[i])
+                        mbar_wait(cfull0 + 8 * i, armed_parity[i], p.budget_ns, p.status,
+                                  KERR_TIMEOUT_DRAIN);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA (leader only)
+        if (leader) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool ok = true, issued = false;
+            const uint32_t idesc = p.idesc;
+            for (int t = cid; t < p.num_tiles && ok; t += ncl, ++local) {
+                const int buf = local & 1;
+                const uint32_t aphase = (local >> 1) & 1;
+                if (!mbar_wait_warp(tempty0 + 8 * buf, aphase ^ 1, p.budget_ns, p.status,
+                                    KERR_TIMEOUT_MMA_ACC)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + buf * KC_BN;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait_warp(full0 + 8 * stage, phase, p.budget_ns, p.status,
+                                        KERR_TIMEOUT_MMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (elect_one()) {
+                        const uint32_t sa = smem_u32(smem + stage * KC_STAGE_BYTES);
+                        const uint32_t sb = sa + KC_A_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < KC_BK / 32; ++kk) {
+                            const uint64_t ad = smem_desc_sw128(sa + kk * 32, 16, 1024);
+                            const uint64_t bd = B_MN ? smem_desc_sw128(sb + kk * 4096, KC_BK * 128, 1024)
+                                                     : smem_desc_sw128(sb + kk * 32, 16, 1024);
+                            mma_i8_pair(d, ad, bd, idesc, (kb | kk) != 0);
+                        }
+                        mma_commit_pair(empty0 + 8 * stage, 0x3);
+                        issued = true;
+                    }
+                    __syncwarp();
+                    if (++stage == KC_STAGES) stage = 0, phase ^= 1;
+                }
+                if (!ok) break;
+                if (elect_one()) mma_commit_pair(tfull0 + 8 * buf, 0x3);
+                __syncwarp();
+            }
+            if (!ok) {
+                if (elect_one() && issued) {
+                    mma_commit_pair(drain, 0x1);
+                    mbar_wait(drain, 0, p.budget_ns, p.status, KERR_TIMEOUT_DRAIN);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int quarter = warp & 3;
+        const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + lane;
+        uint8_t* stage_w = epi_smem + quarter * 4096;
+        const uint64_t out_policy = l2_policy_evict_first();  // C is written once, never re-read
+        int local = 0;
+        for (int t = cid; t < p.num_tiles; t += ncl, ++local) {
+            const int buf = local & 1;
+            const uint32_t aphase = (local >> 1) & 1;
+            if (!mbar_wait_warp(tfull0 + 8 * buf, aphase, p.budget_ns, p.status,
+                                KERR_TIMEOUT_EPILOGUE))
+                break;
+            tc_fence_after();
+            int tm, tn;
+            kc_tile(t, p, tm, tn);
+            const int row = tm * KC_BM + row_in_tile;
+            const bool row_ok = row < p.m;
+            const int wrow0 = tm * KC_BM + static_cast<int>(rank) * 128 + quarter * 32;
+#pragma unroll 1
+            for (int cc = 0; cc < KC_BN / 32; ++cc) {
+                uint32_t r[32];
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                       buf * KC_BN + cc * 32;
+                __syncwarp();
+                tmem_ld32(taddr, r);
+                tmem_ld_wait();
+                if (cc == KC_BN / 32 - 1) {
+                    // the accumulator is in registers: hand TMEM back before storing
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty0 + 8 * buf, 0));
+                }
+                const int col0 = tn * KC_BN + cc * 32;
+                if (p.tma_store) {
+                    if (wrow0 < p.m && col0 < p.n) {
+                        if (lane == 0) bulk_wait_read<0>();  // the previous store has read it
+                        __syncwarp();
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            *reinterpret_cast<int4*>(stage_w + lane * 128 + ((v ^ (lane & 7)) << 4)) =
+                                make_int4(static_cast<int>(r[4 * v]), static_cast<int>(r[4 * v + 1]),
+                                          static_cast<int>(r[4 * v + 2]),
+                                          static_cast<int>(r[4 * v + 3]));
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d_hint(&tmC, smem_u32(stage_w), col0, wrow0, out_policy);
+                            bulk_commit();
+                        }
+                    }
+                } else if (row_ok && col0 < p.n) {
+                    const int lim = min(32, p.n - col0);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (j < lim) {
+                            const int64_t off = static_cast<int64_t>(row) * p.rsc +
+                                                static_cast<int64_t>(col0 + j) * p.csc;
+                            finish_cell(p.epi, p.c, off, static_cast<int32_t>(r[j]));
+                        }
+                    }
+                }
+            }
+        }
+        if (lane == 0) bulk_wait_all();  // every store has left shared memory
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ decoders (both CTAs)
+        const int dt = threadIdx.x - KC_DEC_WARP0 * 32;  // 0 .. 32 * KC_DEC_WARPS - 1
+        uint32_t tw[4] = {p.table[0], p.table[1], p.table[2], p.table[3]};
+        if (p.dtable) {
+            // the 16-entry table table[v % N], built from the device copy of the book
+            for (int w = 0; w < 4; ++w) {
+                uint32_t word = 0;
+                for (int b = 0; b < 4; ++b)
+                    word |= static_cast<uint32_t>(static_cast<uint8_t>(
+                                p.dtable[(4 * w + b) % p.table_len])) << (8 * b);
+                tw[w] = word;
+            }
+        }
+        const uint32_t t0 = tw[0], t1 = tw[1], t2 = tw[2], t3 = tw[3];
+        const uint32_t full_leader = mapa_shared(full0, 0);
+        const uint32_t slot_leader = mapa_shared(relay_dst0, 0) + rank * KC_RELAY;
+        int stage = 0, q = 0;
+        uint32_t phase = 0, qph = 0;
+        bool ok = true;
+        for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                // this step's codes have landed and the MMA is done with the B slot
+                const bool got =
+                    mbar_wait_warp(cfull0 + 8 * q, qph, p.budget_ns, p.status, KERR_TIMEOUT_MMA_FULL) &&
+                    mbar_wait_warp(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
+                                   KERR_TIMEOUT_MMA_FULL);
+                if (got) {
+                    uint8_t* sb = smem + stage * KC_STAGE_BYTES + KC_A_BYTES;
+                    const uint8_t* sq = codes + q * KC_C_BYTES;
+                    // all of this thread's code words first (loads in flight together), then
+                    // the decodes and the swizzled stores: 128 code rows x 8 groups of 8 bytes,
+                    // each group one 16-byte unit of an operand row
+                    constexpr int REPS = (128 * 8) / (32 * KC_DEC_WARPS);
+                    uint2 cw[REPS];
+#pragma unroll
+                    for (int rep = 0; rep < REPS; ++rep) {
+                        const int u = dt + rep * 32 * KC_DEC_WARPS;
+                        cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
+                    }
+#pragma unroll
+                    for (int rep = 0; rep < REPS; ++rep) {
+                        const int u = dt + rep * 32 * KC_DEC_WARPS;
+                        const int r = u >> 3, qq = u & 7;
+                        const uint2 d0 = dec8(cw[rep].x, t0, t1, t2, t3);
+                        const uint2 d1 = dec8(cw[rep].y, t0, t1, t2, t3);
+                        *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                            make_uint4(d0.x, d0.y, d1.x, d1.y);
+                    }
+                    // the codes slot is decoded: hand it back to the codes producer
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(cempty0 + 8 * q);
+                }
+                fence_proxy_async();  // the tensor core (async proxy) reads these bytes
+                // every decoder warp of this CTA is done with the step (or gave up: all of
+                // them reach this barrier every step and leave together, so none waits on a
+                // warp that left); one thread signals the leader's full barrier with a bulk
+                // copy (an async-proxy completion)
+                if (!bar_and_all(1, 32 * KC_DEC_WARPS, got)) {
+                    ok = false;
+                    break;
+                }
+                if (dt == 0)
+                    bulk_copy_s2c(slot_leader + 2 * KC_RELAY * stage, relay_src, KC_RELAY,
+                                  full_leader + 8 * stage);
+                if (++stage == KC_STAGES) stage = 0, phase ^= 1;
+                if (++q == KC_QSTAGES) q = 0, qph ^= 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // neither CTA leaves while the other may still signal it
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, 2 * KC_BN);
+    }
+}
+
+template <bool B_MN>
+static cudaError_t kc_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
+                               const K1CParams& p, int max_clusters, cudaStream_t stream) {
+    auto kern = k1c_pair_kernel<B_MN>;
+    static bool attr_done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_done[dev] = true;
+    }
+    const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(KC_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = KC_SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tmA, tmQ, tmC, p);
+}
+
+int k1c_max_clusters() {
+    static int cached[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+    auto kern = k1c_pair_kernel<true>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_SMEM_BYTES);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 512, 1, 1);
+    cfg.blockDim = dim3(KC_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = KC_SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        n = sms / 2;
+    }
+    if (dev >= 0 && dev < 64) cached[dev] = n;
+    return n;
+}
+
+cudaError_t k1c_launch(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
+                       int orientation, const K1CParams& p, cudaStream_t stream) {
+    const int mc = k1c_max_clusters();
+    return orientation == 0 ? kc_launch_t<true>(tmA, tmQ, tmC, p, mc, stream)
+                            : kc_launch_t<false>(tmA, tmQ, tmC, p, mc, stream);
+}
+
+}  // namespace uor

@@ -98,6 +98,19 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, ui
     return __all_sync(0xffffffffu, ok);
 }
 
+// Named barrier `id` over `count` threads that also ANDs a predicate across them: every
+// participant gets true only if all passed true.
+__device__ __forceinline__ bool bar_and_all(int id, int count, bool pred) {
+    uint32_t out;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(out)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+        : "memory");
+    return out != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -327,6 +340,17 @@ __device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap* map, uint32
         "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;" ::"l"(
             reinterpret_cast<uint64_t>(map)),
         "r"(src), "r"(x), "r"(y), "r"(z), "l"(policy)
+        : "memory");
+}
+// Shared-memory copy from this CTA to a CTA of the cluster (dst and bar are shared::cluster
+// addresses of the same CTA), counted in bytes on that CTA's mbarrier: an async-proxy
+// completion, i.e. the same kind of event a TMA load delivers.
+__device__ __forceinline__ void bulk_copy_s2c(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                              uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dst_cluster),
+        "r"(src), "r"(bytes), "r"(bar_cluster)
         : "memory");
 }
 __device__ __forceinline__ void bulk_commit() {

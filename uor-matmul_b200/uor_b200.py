@@ -23,7 +23,7 @@ OK, NONCONFORMANT, OUTPUT_ALIASES, DEVICE_ERROR, TIMEOUT, NCCL_ERROR, DOES_NOT_F
     INVALID_ARGUMENT, UNSUPPORTED = range(9)
 NEAREST, TOWARD_ZERO, SATURATING, WRAPPING = range(4)
 I8, I16, I32, I64, I128, F32, F64, TROP_I8, TROP_I16, TROP_I32, TROP_I64 = range(1, 12)
-DEVICE_POINTERS, ASYNC, DIGIT_SLICES, MODULAR = 1, 2, 4, 8
+DEVICE_POINTERS, ASYNC, DIGIT_SLICES, MODULAR, CODEC_ON_CHIP = 1, 2, 4, 8, 16
 KERNEL_NAMES = {0: "none", 1: "i8_tcgen05", 2: "limb_tcgen05", 3: "tropical",
                 4: "coded_tcgen05", 5: "float_exact", 6: "epilogue_only", 7: "skinny_dp4a"}
 
@@ -394,13 +394,17 @@ def gemm_tropical_selected(elem, out, a, av, b, bv, c, cv, w, wv, alpha=(0, True
 # ------------------------------------------------------------------ codec
 
 def coded_gemm(out, a, av, codes, k, n, per_byte, table, c, cv, alpha=1, beta=0,
-               encode=NEAREST, ctx=None, route=None, tabulated=False, asynchronous=False):
-    """coded_gemm (k x n codes) or, with tabulated=True, gemm_tabulated's A W^T (n x k codes)."""
+               encode=NEAREST, ctx=None, route=None, tabulated=False, asynchronous=False,
+               on_chip=False):
+    """coded_gemm (k x n codes) or, with tabulated=True, gemm_tabulated's A W^T (n x k codes).
+    on_chip=True never decodes the codes into a dense device copy (CODEC_ON_CHIP)."""
     dev = _on_device(a, codes, table, c)
     A, C = view(a, *av), view(c, *cv)
     pc, lc, _ = _buffer(codes)
     pt, lt, _ = _buffer(table)
     call = make_call(encode, dev, ctx, route, asynchronous)
+    if on_chip:
+        call.flags |= CODEC_ON_CHIP
     fn = lib().uor_b200_tabulated_gemm if tabulated else lib().uor_b200_coded_gemm
     _check(fn(out, ctypes.byref(A), pc, lc, k, n, per_byte, pt, lt, ctypes.byref(C), alpha, beta,
               ctypes.byref(call)), "coded_gemm")
