@@ -133,9 +133,9 @@ def tensor_peak():
         return 2.0 * 1590.0, "2x fallback bf16 1.59 PFLOP/s, of fallback"
 
 
-def load_traffic(name):
+def load_traffic(name, key="bytes_per_launch"):
     try:
-        return json.load(open(os.path.join(ROOT, "profiles", name))).get("bytes_per_launch")
+        return json.load(open(os.path.join(ROOT, "profiles", name))).get(key)
     except Exception:
         return None
 
@@ -412,12 +412,15 @@ def wl_codec(args, U, torch, rank, sets=3, on_chip=False):
     w.l2 = f"{sets} rotating operand sets ({sets * (m * k + k * n // 2) >> 20} MiB) + 64 MiB output"
     w.algorithmic_bytes = m * k + k * n // 2 + 4 * m * n
     w.flush = False
+    w.traffic = None if on_chip else load_traffic("codec_decode_k1_2048x8192x8192_traffic.json",
+                                                  "bytes_per_call")
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
         ach = w.units / (avg_ms / 1e3) / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
-                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "frac": ach / peak, "peak_source": src, "traffic": w.traffic,
+                "traffic_scope": "whole call (decode + K1), one ncu capture" if w.traffic else None,
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
@@ -647,6 +650,8 @@ def wl_f32(args, U, torch, rank, size, sets=2):
     w.l2 = f"{sets} rotating operand sets ({sets * 8 * m * k >> 20} MiB) + {4 * m * n >> 20} MiB output"
     w.algorithmic_bytes = 8 * m * k + 4 * m * n
     w.flush = False
+    w.traffic = (load_traffic("modular_f32_4096_traffic.json", "bytes_per_call") if size == 4096
+                 else None)
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
@@ -662,8 +667,11 @@ def wl_f32(args, U, torch, rank, size, sets=2):
                      "recomputed exactly) over the whole call (analysis, slicing, GEMM, "
                      "interval test, fixups)")
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
-                "frac": ach / peak, "peak_source": src, "traffic": None, "basis": basis,
-                "algorithmic_bytes": w.algorithmic_bytes}
+                "frac": ach / peak, "peak_source": src, "traffic": w.traffic,
+                "traffic_scope": ("whole call, one ncu capture" if w.traffic else
+                                  "not captured at this size (about 5 GB on the device); the "
+                                  "4096^3 call moves 13x its algorithmic bytes"),
+                "basis": basis, "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
 
@@ -794,6 +802,7 @@ def wl_wide(args, U, torch, rank):
     w.l2 = "512 MiB of operands per step (> L2)"
     w.algorithmic_bytes = 4 * (m * k + k * n) + 16 * m * n
     w.flush = False
+    w.traffic = load_traffic("modular_wide_i32_1024x65536x1024_traffic.json", "bytes_per_call")
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
@@ -802,7 +811,8 @@ def wl_wide(args, U, torch, rank):
         what = (f"{gemms} residue GEMMs modulo coprime moduli (modular route; 16 byte-slice "
                 "pairs otherwise)" if w.route.moduli else f"{gemms} int8 byte-slice pairs")
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
-                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "frac": ach / peak, "peak_source": src, "traffic": w.traffic,
+                "traffic_scope": "whole call (slicers, residue GEMMs, CRT), one ncu capture",
                 "basis": f"int8 ops executed ({what} x 2mnk) over the whole call (slicing, "
                          "GEMMs, recombination)",
                 "algorithmic_bytes": w.algorithmic_bytes}
