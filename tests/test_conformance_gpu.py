@@ -2,6 +2,8 @@
 GPU path through the C ABI, every result also compared with the CPU oracle bit for bit.
 
 CD-01  backend choice does not change bytes (byte slices, modular residues, default)
+CD-04  operand traversal and layout do not change bytes
+CD-05 / CD-28  for a fixed accumulation only the encode mode changes bytes
 CD-02  tile count and completion order do not change bytes
 CD-07  splitting the operand stream at any index sums the parts
 CD-10  every scratch offer gives the same bytes (slice::gemm_ex_full)
@@ -19,7 +21,7 @@ import uor_b200 as U
 import uor_b200_dist as D
 from oracle import oracle as orc
 from oracle.oracle import View
-from gpu_util import i8, i128_values, needs_gpu, oracle_int, out_array
+from gpu_util import i8, i128_values, needs_gpu, oracle_int, out_array, torch
 
 pytestmark = [pytest.mark.gpu, needs_gpu]
 
@@ -272,3 +274,61 @@ def test_cd24_selection_witness_is_invariant_under_partition_and_order():
     wi = orc.trop_witness(a["v"].reshape(m, k), a["f"].reshape(m, k) != 0,
                           b["v"].reshape(k, n), b["f"].reshape(k, n) != 0)
     assert np.array_equal(np.asarray(wi, np.uint64).reshape(-1), whole_w)
+
+
+# ------------------------------------------------------------------ CD-04, CD-05 / CD-28
+
+def test_cd04_traversal_and_layout_do_not_change_bytes():
+    """The same product through every operand layout the device path distinguishes (A
+    K-major, A MN-major, A gathered; B MN-major, K-major, read backwards, gathered), and
+    through the host-pointer pipeline and device pointers: one set of bytes."""
+    m, k, n = 288, 400, 272
+    a, b = i8(110, m * k), i8(111, k * n)
+    want = _oracle_i8(a, b, m, k, n, U.I64, 5, 0)
+    at = np.ascontiguousarray(a.reshape(m, k).T).reshape(-1)
+    bt = np.ascontiguousarray(b.reshape(k, n).T).reshape(-1)
+    brev = b.reshape(k, n)[::-1].copy().reshape(-1)
+    apad = np.zeros(m * (k + 3), np.int8)
+    apad.reshape(m, k + 3)[:, :k] = a.reshape(m, k)
+    cases = [(a, (m, k, k, 1), b, (k, n, n, 1)), (at, (m, k, 1, m), b, (k, n, n, 1)),
+             (a, (m, k, k, 1), bt, (k, n, 1, k)), (a, (m, k, k, 1), brev, (k, n, -n, 1)),
+             (apad, (m, k, k + 3, 1), b, (k, n, n, 1)), (at, (m, k, 1, m), bt, (k, n, 1, k))]
+    layouts = set()
+    for aa, av, bb, bv in cases:
+        got = np.zeros(m * n, np.int64)
+        route = U.Route()
+        U.gemm(U.I8, U.I64, aa, av, bb, bv, got, (m, n, n, 1), 5, 0, route=route)
+        assert np.array_equal(got, want), (av, bv)
+        layouts.add((route.a_layout, route.b_layout))
+    assert len(layouts) >= 4  # the cases really took different operand layouts
+    got = torch.zeros(m * n, dtype=torch.int64, device="cuda")
+    U.gemm(U.I8, U.I64, torch.from_numpy(a).cuda(), (m, k, k, 1), torch.from_numpy(b).cuda(),
+           (k, n, n, 1), got, (m, n, n, 1), 5, 0)
+    assert np.array_equal(got.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("out", [U.I8, U.I16, U.I32])
+def test_cd05_cd28_only_the_encode_mode_changes_bytes(out):
+    """For one fixed accumulation each encode gives the oracle's bytes (into an integer
+    output Nearest, TowardZero and Saturating all clamp, acc.rs:128-151, and Wrapping
+    truncates), and nothing else -- host or device buffers, a padded output -- changes the
+    bytes of a given encode."""
+    m, k, n = 40, 700, 56
+    a, b = i8(112, m * k), i8(113, k * n)
+    alpha = 2**20  # pushes most cells past the narrow output ranges
+    outs = {}
+    for mode in (U.NEAREST, U.TOWARD_ZERO, U.SATURATING, U.WRAPPING):
+        want = _oracle_i8(a, b, m, k, n, out, alpha, 0, mode=mode)
+        got = out_array(out, m * n)
+        U.gemm(U.I8, out, a, (m, k, k, 1), b, (k, n, n, 1), got, (m, n, n, 1), alpha, 0, mode)
+        assert np.array_equal(got, want), mode
+        # the same encode through device buffers and a padded output gives the same bytes
+        ldc = n + 5
+        dev = torch.zeros(m * ldc, dtype={U.I8: torch.int8, U.I16: torch.int16,
+                                          U.I32: torch.int32}[out], device="cuda")
+        U.gemm(U.I8, out, torch.from_numpy(a).cuda(), (m, k, k, 1), torch.from_numpy(b).cuda(),
+               (k, n, n, 1), dev, (m, n, ldc, 1), alpha, 0, mode)
+        assert np.array_equal(dev.cpu().numpy().reshape(m, ldc)[:, :n].reshape(-1), want), mode
+        outs[mode] = got.tobytes()
+    assert outs[U.NEAREST] == outs[U.SATURATING]  # Nearest saturates integer outputs
+    assert outs[U.WRAPPING] != outs[U.SATURATING]  # the wrap differs once cells overflow
