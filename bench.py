@@ -1373,13 +1373,15 @@ def main():
     import uor_b200 as U
 
     torch.cuda.set_device(local)
+    import uor_b200_dist as D
+    # pinned host buffers of the e2e leg land in memory local to this GPU (first touch by a
+    # thread on the GPU's NUMA node); the CPU baseline gets every core back below
+    all_cpus = os.sched_getaffinity(0)
+    D.bind_to_local_cpus(local)
     dist = None
     if world > 1:
         import datetime
         import torch.distributed as dist
-        import uor_b200_dist as D
-        # pinned host buffers of the e2e leg land in memory local to this GPU
-        D.bind_to_local_cpus(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=datetime.timedelta(seconds=180))
     ctx = U.Context(local)
@@ -1389,6 +1391,8 @@ def main():
 
     w = build_workload(args.workload, args, U, torch, rank, world)
     line = measure(w, args, U, torch, dist, ctx, stream, rank, world, local)
+    if world == 1:
+        os.sched_setaffinity(0, all_cpus)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and w.cpu is not None:
         line["cpu_baseline"] = w.cpu(12.0, ctx)
     del w
