@@ -162,3 +162,24 @@ def test_noalloc_refuses_oversized_products_before_any_device_work():
     # past the int-sized cap is unsupported, still before any device work
     assert fn(U.I64, cap + 1, 140_000, 4, 1, fake, 140_000, fake, 4, 0, fake, 4, U.NEAREST,
               None) == U.UNSUPPORTED
+
+
+def test_reference_arm_runs_without_the_product_library():
+    """bench.py --impl reference times the reference semantics through the oracle alone:
+    the process must never load libuor_b200.so (the comparison would not be against the
+    reference otherwise), and it prints the GPU arm's config."""
+    import json
+    import subprocess
+    import sys
+    code = ("import runpy, sys; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', "
+            "'--warmup', '0', '--size', '512']; runpy.run_path('bench.py', run_name='__main__'); "
+            "maps = open('/proc/self/maps').read(); "
+            "print('LOADED' if 'libuor_b200' in maps else 'CLEAN')")
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = out.stdout.strip().splitlines()
+    assert lines[-1] == "CLEAN"
+    line = json.loads(lines[-2])
+    assert line["impl"] == "reference" and line["config"]["m"] == 512
+    assert line["cpu_baseline"]["kind"] == "port"
