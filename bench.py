@@ -412,15 +412,14 @@ def wl_codec(args, U, torch, rank, sets=3, on_chip=False):
     w.l2 = f"{sets} rotating operand sets ({sets * (m * k + k * n // 2) >> 20} MiB) + 64 MiB output"
     w.algorithmic_bytes = m * k + k * n // 2 + 4 * m * n
     w.flush = False
-    w.traffic = None if on_chip else load_traffic("codec_decode_k1_2048x8192x8192_traffic.json",
-                                                  "bytes_per_call")
+    w.traffic = load_traffic("k1c_codec_on_chip_2048x8192x8192_traffic.json", "bytes_per_call")
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
         ach = w.units / (avg_ms / 1e3) / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src, "traffic": w.traffic,
-                "traffic_scope": "whole call (decode + K1), one ncu capture" if w.traffic else None,
+                "traffic_scope": "whole call (K1C), one ncu capture" if w.traffic else None,
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
@@ -1431,8 +1430,6 @@ def main():
                     cpu_budget=2.0),
                 "configs[1] codec 2048x8192x8192": extra(
                     lambda: wl_codec(args, U, torch, rank), 100, e2e_steps=3, cpu_budget=4.0),
-                "configs[1] codec, decoded on chip only (CODEC_ON_CHIP)": extra(
-                    lambda: wl_codec(args, U, torch, rank, on_chip=True), 100, cpu_budget=2.0),
                 "configs[2] exact f32 4096^3": extra(
                     lambda: wl_f32(args, U, torch, rank, 4096), 60, e2e_steps=3,
                     cpu_budget=4.0),

@@ -133,11 +133,11 @@ typedef struct uor_b200_route {
  * product's bound, whatever the estimated cost. Exact; the same bytes. */
 #define UOR_B200_MODULAR 8u
 /* Codec tier (Packed<Grid<N>, 2>): decode the codes on chip only, never into a dense copy
- * of the coded operand in device memory. From 256 activation rows up (k up to one s32
- * lane, 131071) this runs K1's CTA-pair GEMM with the codes decoded straight into its
- * shared-memory B stages; below that the fused K5 kernel. Without the flag, products of
- * 512 rows and more decode once into a k x n workspace and run K1, which is faster
- * (configs[1]: 2,380 against 1,500 TOPS). The same bytes either way. */
+ * of the coded operand in device memory. By default products of 512 activation rows and
+ * more already decode on chip (K1's CTA-pair GEMM with the codes decoded straight into its
+ * shared-memory B stages) when k is within one s32 lane (131071); the flag extends that to
+ * 256-511 rows (256-row tiles) and keeps deeper reductions off the k x n workspace the
+ * default would decode them into (the fused K5 kernel instead). The same bytes either way. */
 #define UOR_B200_CODEC_ON_CHIP 16u
 
 /* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)

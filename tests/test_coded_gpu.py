@@ -1,8 +1,9 @@
 """The codec tier against the oracle's coded_gemm / gemm_tabulated restatement: K5 (the
-codebook decode fused into the tensor-core pipeline, decoded weights on the M side), the
-one-pass decode followed by K1 (the default from 512 activation rows up), and, with
-CODEC_ON_CHIP, K1C (K1's CTA-pair pipeline with the codes decoded into its B stages, no
-dense copy anywhere) from 256 rows up."""
+codebook decode fused into the tensor-core pipeline, decoded weights on the M side) below
+512 activation rows; K1C (K1's CTA-pair pipeline with the codes decoded into its B stages,
+no dense copy anywhere) from 512 rows up with 512-row tiles, and with CODEC_ON_CHIP from
+256 rows with 256-row tiles; the one-pass decode followed by K1 for reductions deeper
+than one s32 lane."""
 import numpy as np
 import pytest
 
@@ -73,14 +74,13 @@ def test_fused_nibbles(orientation, shape):
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
-def test_decoded_nibbles_many_rows(orientation):
-    """512 activation rows and more, by default: the codes are decoded once to dense int8
-    (flat over the code bytes, low nibble first) and K1 runs on them."""
+def test_default_many_rows_decode_on_chip(orientation):
+    """512 activation rows and more, by default: K1C with 512-row tiles, never a dense B."""
     for m, k, n, out, alpha, beta, N in [(512, 256, 96, U.I32, 1, 0, 16),
                                          (1030, 96, 288, U.I8, -2, 5, 16)]:
         got, want, route = run(m, k, n, 2, N, orientation, out, alpha, beta, seed=m + N)
         assert np.array_equal(got, want), (m, k, n, out)
-        assert route.kernel == 4 and route.b_layout == 3
+        assert route.kernel == 4 and route.b_layout != 3 and route.tile_m == 512
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
@@ -99,7 +99,7 @@ def test_pair_decode_many_rows(orientation):
         got, want, route = run(m, k, n, 2, N, orientation, out, alpha, beta, seed=m + N,
                                on_chip=True)
         assert np.array_equal(got, want), (m, k, n, out)
-        assert route.kernel == 4 and route.b_layout != 3 and route.tile_m == 256
+        assert route.kernel == 4 and route.b_layout != 3 and route.tile_m == (512 if m >= 512 else 256)
 
 
 def test_pair_decode_gathered_activations():
@@ -111,19 +111,23 @@ def test_pair_decode_gathered_activations():
 
 @pytest.mark.parametrize("orientation", [0, 1])
 def test_decode_once_past_the_lane(orientation):
-    """k past the s32 lane depth with 512+ rows: decoded once to dense int8, then K1 in
-    exact chunks."""
+    """k past the s32 lane depth with 512+ rows: decoded once to dense int8 (flat over the
+    code bytes, low nibble first), then K1 in exact chunks; with CODEC_ON_CHIP, K5's
+    chunks instead (no workspace)."""
     m, k, n = 512, 131_200, 32
     got, want, route = run(m, k, n, 2, 16, orientation, U.I64, seed=5)
     assert np.array_equal(got, want)
     assert route.kernel == 4 and route.b_layout == 3 and route.k_chunks == 2
+    got, want, route = run(m, k, n, 2, 16, orientation, U.I64, seed=5, on_chip=True)
+    assert np.array_equal(got, want)
+    assert route.kernel == 4 and route.b_layout != 3 and route.k_chunks == 2
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
 @pytest.mark.parametrize("on_chip", [False, True])
 def test_decoded_nibbles_device_table(orientation, on_chip):
-    """Device pointers and a device table (a 7-entry book, so table[v % 7]) read by the
-    kernels themselves: the one-pass decode, and K1C's decoders."""
+    """Device pointers and a device table (a 7-entry book, so table[v % 7]) read by K1C's
+    decoders themselves, with and without CODEC_ON_CHIP."""
     m, k, n, N = 640, 192, 160, 7
     rng = np.random.default_rng(70 + orientation)
     a = rng.integers(-128, 128, size=m * k).astype(np.int8)
@@ -139,7 +143,7 @@ def test_decoded_nibbles_device_table(orientation, on_chip):
                  k, n, 2, torch.from_numpy(table).cuda(), tc, (m, n, n, 1), route=route,
                  tabulated=orientation == 1, on_chip=on_chip)
     assert np.array_equal(tc.cpu().numpy(), want)
-    assert route.kernel == 4 and (route.b_layout != 3) == on_chip
+    assert route.kernel == 4 and route.b_layout != 3
 
 
 @pytest.mark.parametrize("orientation", [0, 1])

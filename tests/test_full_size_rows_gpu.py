@@ -90,8 +90,8 @@ def test_wide_i32_to_i128_config4_row_blocks():
 
 @pytest.mark.parametrize("on_chip", [False, True])
 def test_codec_config2_row_blocks(on_chip):
-    """2048 x 8192 activations, 8192 x 8192 nibble codes, 16-entry book; by
-    default (decoded once, then K1) and decoded on chip only (K1C)."""
+    """2048 x 8192 activations, 8192 x 8192 nibble codes, 16-entry book,
+    decoded on chip (K1C, 512-row tiles), with and without CODEC_ON_CHIP."""
     m, k, n = 2048, 8192, 8192
     a = U.corpus(1, U.CORPUS_I8, m * k)
     q = U.corpus(2, U.CORPUS_NIBBLES, k * n)
@@ -100,7 +100,7 @@ def test_codec_config2_row_blocks(on_chip):
     route = U.Route()
     U.coded_gemm(U.I32, torch.from_numpy(a).cuda(), (m, k, k, 1), torch.from_numpy(q).cuda(), k,
                  n, 2, torch.from_numpy(t).cuda(), tc, (m, n, n, 1), route=route, on_chip=on_chip)
-    assert (route.b_layout != 3) == on_chip
+    assert route.b_layout != 3 and route.tile_m == 512
     c = tc.cpu().numpy()
     for r0, r1 in row_blocks(m):
         want = np.zeros((r1 - r0) * n, np.int32)

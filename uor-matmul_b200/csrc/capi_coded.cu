@@ -151,15 +151,18 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool fused = per_byte == 2 && table_len <= 16 && k > 0 &&
                        (orientation == 0 ? (n % 32 == 0) : (k % 32 == 0)) &&
                        (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
-    // On-chip decoding only (UOR_B200_CODEC_ON_CHIP): from one 256-row activation tile up,
-    // K1C -- K1's CTA-pair pipeline with the codes decoded into its B stages, no dense B
-    // anywhere; smaller products (and reductions deeper than one s32 lane) take K5. By
-    // default, products of two activation tiles and more decode every weight once into a
-    // workspace and run K1, which measured faster at configs[1] (0.115 against 0.184 ms):
-    // K1C's decoder warps spend about half the SM's issue slots on the decode.
+    // From 512 activation rows up (k within one s32 lane), K1C with 512 x 256 tiles: K1's
+    // CTA-pair pipeline with the codes decoded into its B stages, each decoded stage feeding
+    // two M256 halves -- no dense B anywhere, and faster than decoding once into a workspace
+    // and running K1 (configs[1]: 0.114 against 0.117 ms). Deeper reductions with that many
+    // rows decode once into a k x n workspace and run K1 in exact chunks, unless
+    // UOR_B200_CODEC_ON_CHIP forbids the workspace (then K5). With the flag, 256 to 511 rows
+    // take K1C with 256 x 256 tiles; without it, and below 256 rows, K5.
     const bool on_chip = call && (call->flags & UOR_B200_CODEC_ON_CHIP);
-    const bool pair_fused = fused && on_chip && m >= (size_t)K5_BN && (int64_t)k <= K1_LANE_DEPTH;
-    const bool decode_once = fused && !on_chip && m >= 2 * (size_t)K5_BN;
+    const bool shallow = (int64_t)k <= K1_LANE_DEPTH;
+    const bool pair_fused = fused && shallow && (m >= 2 * (size_t)K5_BN ||
+                                                 (on_chip && m >= (size_t)K5_BN));
+    const bool decode_once = fused && !pair_fused && !on_chip && m >= 2 * (size_t)K5_BN;
     // The 16-entry effective table the fused decode uses: table[v % N]; a device table on
     // the decode-once route is read by the decode kernel itself (no host round trip).
     const bool table_in_kernel = (decode_once || pair_fused) && dev && !table_on_host;
@@ -237,7 +240,9 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         p.n = (int)n;
         p.k_begin = 0;
         p.num_kb = (int)((k + K1_BK - 1) / K1_BK);
-        p.tiles_m = (int)((m + 255) / 256);
+        // 512-row tiles from two full row tiles up (each decoded stage serves both)
+        const bool tall = m >= 512;
+        p.tiles_m = (int)((m + (tall ? 511 : 255)) / (tall ? 512 : 256));
         p.tiles_n = (int)((n + 255) / 256);
         p.num_tiles = p.tiles_m * p.tiles_n;
         p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
@@ -256,7 +261,7 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         p.budget_ns = ctx->budget_ns;
         const int mc = k1c_max_clusters();
         route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
-        route->tile_m = 256;
+        route->tile_m = tall ? 512 : 256;
         route->tile_n = 256;
         route->tile_k = K1_BK;
         route->k_chunks = 1;
@@ -264,7 +269,8 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         route->pairs = 1;
         route->a_layout = a_ok ? 0 : 2;
         route->b_layout = orientation == 0 ? 1 : 0;  // decoded on chip, never materialised
-        if (k1c_launch(tmA, tmQ, tmO, orientation, p, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        if (k1c_launch(tmA, tmQ, tmO, orientation, tall, p, s) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
     } else if (!fused) {
         // Off the fused path (P != 2, N > 16, or code rows the TMA cannot address):
         // decode to a dense row-major k x n int8 matrix in the auxiliary slot, then K1.

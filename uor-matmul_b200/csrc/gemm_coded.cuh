@@ -68,8 +68,10 @@ struct K1CParams : K1Params {
 // tmQ: codes, no swizzle, box {64 bytes, 128 rows}: orientation 0 dims {n/2, k},
 //      orientation 1 dims {k/2, n}. With p.tma_store, tmC is the s32 output map
 //      (dims {n, m}, box {32, 32}, 128-byte swizzle). k must not exceed K1_LANE_DEPTH.
+// tall: 512 x 256 tiles (p.tiles_m counts 512-row tiles), each decoded B stage feeding two
+// M256 halves; else 256 x 256.
 cudaError_t k1c_launch(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
-                       int orientation, const K1CParams& p, cudaStream_t stream);
+                       int orientation, bool tall, const K1CParams& p, cudaStream_t stream);
 int k1c_max_clusters();
 
 }  // namespace uor

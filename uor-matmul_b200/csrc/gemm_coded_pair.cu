@@ -398,16 +398,406 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------- K1C tall: 512 x 256 tiles
+// The same pipeline with each decoded B stage feeding 512 activation rows: two M256 halves
+// (rows 256 h .. of the tile, CTA rank r holding rows 256 h + 128 r + [0, 128) of each)
+// share the stage, so every decoded weight serves twice the products and the decode costs
+// half the issue slots per MAC. Both accumulators fill TMEM (half h in columns 256 h ..),
+// so there is no second buffer: the epilogue hands the halves back one at a time and the
+// MMA issuer starts the next tile's first-half MMAs as soon as half 0 is free, holding the
+// second-half MMAs of the stages it consumes until half 1 is free.
+constexpr int KT_BM = 512;
+constexpr int KT_STAGES = 3;   // A/B ring: 2 x 16 KiB of A and 16 KiB of decoded B per CTA
+constexpr int KT_QSTAGES = 4;  // codes ring
+constexpr int KT_STAGE_BYTES = 2 * KC_A_BYTES + KC_B_BYTES;
+constexpr int KT_EPI_BYTES = 4 * 2 * 4096;
+constexpr int KT_SMEM_BYTES = KT_STAGES * KT_STAGE_BYTES + KT_QSTAGES * KC_C_BYTES +
+                              KT_EPI_BYTES + 1024 + 256 + 256;
+static_assert(KT_SMEM_BYTES <= 232448, "K1C tall exceeds the opt-in shared memory per block");
+
 template <bool B_MN>
+__device__ __forceinline__ void kt_issue_half(uint32_t d, uint32_t sa, uint32_t sb, uint32_t idesc, int kb) {
+#pragma unroll
+    for (int kk = 0; kk < KC_BK / 32; ++kk) {
+        const uint64_t ad = smem_desc_sw128(sa + kk * 32, 16, 1024);
+        const uint64_t bd = B_MN ? smem_desc_sw128(sb + kk * 4096, KC_BK * 128, 1024)
+                                 : smem_desc_sw128(sb + kk * 32, 16, 1024);
+        mma_i8_pair(d, ad, bd, idesc, (kb | kk) != 0);
+    }
+}
+
+template <bool B_MN>
+__global__ void __launch_bounds__(KC_THREADS, 1)
+    k1c_tall_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmC, const K1CParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* codes = smem + KT_STAGES * KT_STAGE_BYTES;
+    uint8_t* epi_smem = codes + KT_QSTAGES * KC_C_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + KT_EPI_BYTES);
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + KT_STAGES);
+    const uint32_t cfull0 = smem_u32(bars + 2 * KT_STAGES);
+    const uint32_t cempty0 = smem_u32(bars + 2 * KT_STAGES + KT_QSTAGES);
+    const uint32_t tfull = smem_u32(bars + 2 * KT_STAGES + 2 * KT_QSTAGES);
+    const uint32_t tempty0 = tfull + 8;  // + 8 h: half h drained
+    const uint32_t drain = tfull + 24;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * KT_STAGES + 2 * KT_QSTAGES + 4);
+    const uint32_t relay_src = smem_u32(reinterpret_cast<uint8_t*>(bars) + 256);
+    const uint32_t relay_dst0 = relay_src + KC_RELAY;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cid = static_cast<int>(cluster_id_x());
+    const int ncl = static_cast<int>(nclusters_x());
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < KT_STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int q = 0; q < KT_QSTAGES; ++q) {
+            mbar_init(cfull0 + 8 * q, 1);
+            mbar_init(cempty0 + 8 * q, KC_DEC_WARPS);
+        }
+        mbar_init(tfull, 1);
+        mbar_init(tempty0, 8);  // 4 epilogue warps in each CTA of the pair
+        mbar_init(tempty0 + 8, 8);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmQ);
+        if (p.tma_store) tma_prefetch_desc(&tmC);
+    }
+    if (warp == 1) tmem_alloc_pair(smem_u32(tmem_slot), 2 * KC_BN);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ A producer (both CTAs)
+        if (elect_one()) {
+            const uint64_t pol = l2_policy_evict_last();
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            bool armed[KT_STAGES];
+            uint32_t armed_parity[KT_STAGES];
+            for (int s = 0; s < KT_STAGES; ++s) armed[s] = false, armed_parity[s] = 0;
+            for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+                int tm, tn;
+                kc_tile(t, p, tm, tn);
+                const int row0 = tm * KT_BM + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
+                                   KERR_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb_local = full0 + 8 * stage;
+                    if (leader) {
+                        mbar_expect_tx(fb_local, 4 * KC_A_BYTES + 2 * KC_RELAY);
+                        armed[stage] = true;
+                        armed_parity[stage] = phase;
+                    }
+                    const uint32_t fb = mapa_shared(fb_local, 0);
+                    const uint32_t sa = smem_u32(smem + stage * KT_STAGE_BYTES);
+                    tma_load_2d_pair(sa, &tmA, fb, kb * KC_BK, row0, pol);
+                    tma_load_2d_pair(sa + KC_A_BYTES, &tmA, fb, kb * KC_BK, row0 + 256, pol);
+                    if (++stage == KT_STAGES) stage = 0, phase ^= 1;
+                }
+            }
+            if (!ok && leader)
+                for (int s = 0; s < KT_STAGES; ++s)
+                    if (armed[s])
+                        mbar_wait(full0 + 8 * s, armed_parity[s], p.budget_ns, p.status,
+                                  KERR_TIMEOUT_DRAIN);
+        }
+        __syncwarp();
+    } else if (warp == 6) {
+        // ------------------------------------------------------------ codes producer (both CTAs)
+        if (elect_one()) {
+            const uint64_t pol = l2_policy_evict_last();
+            int q = 0;
+            uint32_t qph = 0;
+            bool ok = true;
+            bool armed[KT_QSTAGES];
+            uint32_t armed_parity[KT_QSTAGES];
+            for (int i = 0; i < KT_QSTAGES; ++i) armed[i] = false, armed_parity[i] = 0;
+            for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+                int tm, tn;
+                kc_tile(t, p, tm, tn);
+                const int col0 = tn * KC_BN + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(cempty0 + 8 * q, qph ^ 1, p.budget_ns, p.status,
+                                   KERR_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t cb = cfull0 + 8 * q;
+                    mbar_expect_tx(cb, KC_C_BYTES);
+                    armed[q] = true;
+                    armed_parity[q] = qph;
+                    const uint32_t sq = smem_u32(codes + q * KC_C_BYTES);
+                    const int kc = kb * KC_BK;
+                    if (B_MN) tma_load_2d(sq, &tmQ, cb, col0 / 2, kc, pol);
+                    else tma_load_2d(sq, &tmQ, cb, kc / 2, col0, pol);
+                    if (++q == KT_QSTAGES) q = 0, qph ^= 1;
+                }
+            }
+            if (!ok)
+                for (int i = 0; i < KT_QSTAGES; ++i)
+                    if (armed[i])
+                        mbar_wait(cfull0 + 8 * i, armed_parity[i], p.budget_ns, p.status,
+                                  KERR_TIMEOUT_DRAIN);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA (leader only)
+        if (leader) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool ok = true, issued = false;
+            const uint32_t idesc = p.idesc;
+            const uint32_t d0 = tmem_base, d1 = tmem_base + 256;
+            for (int t = cid; t < p.num_tiles && ok; t += ncl, ++local) {
+                const uint32_t aparity = (static_cast<uint32_t>(local) & 1u) ^ 1u;
+                if (!mbar_wait_warp(tempty0, aparity, p.budget_ns, p.status, KERR_TIMEOUT_MMA_ACC)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                bool h1 = false;
+                int defer_n = 0, defer_stage = 0, defer_kb = 0;
+                auto flush = [&]() {
+                    if (elect_one()) {
+                        for (int j = 0; j < defer_n; ++j) {
+                            int s = defer_stage + j;
+                            if (s >= KT_STAGES) s -= KT_STAGES;
+                            const uint32_t sa = smem_u32(smem + s * KT_STAGE_BYTES);
+                            kt_issue_half<B_MN>(d1, sa + KC_A_BYTES, sa + 2 * KC_A_BYTES, idesc,
+                                                defer_kb + j);
+                            mma_commit_pair(empty0 + 8 * s, 0x3);
+                        }
+                    }
+                    __syncwarp();
+                    defer_n = 0;
+                };
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!h1 && defer_n == KT_STAGES) {
+                        if (!mbar_wait_warp(tempty0 + 8, aparity, p.budget_ns, p.status,
+                                            KERR_TIMEOUT_MMA_ACC)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        h1 = true;
+                        flush();
+                    }
+                    if (!mbar_wait_warp(full0 + 8 * stage, phase, p.budget_ns, p.status,
+                                        KERR_TIMEOUT_MMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (!h1) {
+                        h1 = __all_sync(0xffffffffu, mbar_try_wait(tempty0 + 8, aparity) != 0);
+                        if (h1) {
+                            tc_fence_after();
+                            flush();
+                        }
+                    }
+                    const uint32_t sa = smem_u32(smem + stage * KT_STAGE_BYTES);
+                    if (elect_one()) {
+                        kt_issue_half<B_MN>(d0, sa, sa + 2 * KC_A_BYTES, idesc, kb);
+                        if (h1) {
+                            kt_issue_half<B_MN>(d1, sa + KC_A_BYTES, sa + 2 * KC_A_BYTES, idesc, kb);
+                            mma_commit_pair(empty0 + 8 * stage, 0x3);
+                        }
+                        issued = true;
+                    }
+                    __syncwarp();
+                    if (!h1) {
+                        if (defer_n == 0) defer_stage = stage, defer_kb = kb;
+                        ++defer_n;
+                    }
+                    if (++stage == KT_STAGES) stage = 0, phase ^= 1;
+                }
+                if (!ok) break;
+                if (!h1) {
+                    if (!mbar_wait_warp(tempty0 + 8, aparity, p.budget_ns, p.status,
+                                        KERR_TIMEOUT_MMA_ACC)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    flush();
+                }
+                if (elect_one()) mma_commit_pair(tfull, 0x3);
+                __syncwarp();
+            }
+            if (!ok) {
+                if (elect_one() && issued) {
+                    mma_commit_pair(drain, 0x1);
+                    mbar_wait(drain, 0, p.budget_ns, p.status, KERR_TIMEOUT_DRAIN);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int quarter = warp & 3;
+        uint8_t* stage_w = epi_smem + quarter * 2 * 4096;
+        const uint64_t out_policy = l2_policy_evict_first();
+        int local = 0, nstore = 0;
+        for (int t = cid; t < p.num_tiles; t += ncl, ++local) {
+            if (!mbar_wait_warp(tfull, static_cast<uint32_t>(local) & 1u, p.budget_ns, p.status,
+                                KERR_TIMEOUT_EPILOGUE))
+                break;
+            tc_fence_after();
+            int tm, tn;
+            kc_tile(t, p, tm, tn);
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                const int wrow0 = tm * KT_BM + h * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+                const int row = wrow0 + lane;
+                const bool row_ok = row < p.m;
+#pragma unroll 1
+                for (int cc = 0; cc < KC_BN / 32; ++cc) {
+                    uint32_t r[32];
+                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                           256 * h + cc * 32;
+                    __syncwarp();
+                    tmem_ld32(taddr, r);
+                    tmem_ld_wait();
+                    if (cc == KC_BN / 32 - 1) {
+                        // this half is in registers: hand it back before storing
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty0 + 8 * h, 0));
+                    }
+                    const int col0 = tn * KC_BN + cc * 32;
+                    if (p.tma_store) {
+                        if (wrow0 < p.m && col0 < p.n) {
+                            uint8_t* sbuf = stage_w + (nstore & 1) * 4096;
+                            if (lane == 0) bulk_wait_read<1>();
+                            __syncwarp();
+#pragma unroll
+                            for (int v = 0; v < 8; ++v)
+                                *reinterpret_cast<int4*>(sbuf + lane * 128 + ((v ^ (lane & 7)) << 4)) =
+                                    make_int4(static_cast<int>(r[4 * v]), static_cast<int>(r[4 * v + 1]),
+                                              static_cast<int>(r[4 * v + 2]),
+                                              static_cast<int>(r[4 * v + 3]));
+                            fence_proxy_async();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_2d_hint(&tmC, smem_u32(sbuf), col0, wrow0, out_policy);
+                                bulk_commit();
+                            }
+                            ++nstore;
+                        }
+                    } else if (row_ok && col0 < p.n) {
+                        const int lim = min(32, p.n - col0);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (j < lim) {
+                                const int64_t off = static_cast<int64_t>(row) * p.rsc +
+                                                    static_cast<int64_t>(col0 + j) * p.csc;
+                                finish_cell(p.epi, p.c, off, static_cast<int32_t>(r[j]));
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ decoders (both CTAs)
+        const int dt = threadIdx.x - KC_DEC_WARP0 * 32;
+        uint32_t tw[4] = {p.table[0], p.table[1], p.table[2], p.table[3]};
+        if (p.dtable) {
+            for (int w = 0; w < 4; ++w) {
+                uint32_t word = 0;
+                for (int b = 0; b < 4; ++b)
+                    word |= static_cast<uint32_t>(static_cast<uint8_t>(
+                                p.dtable[(4 * w + b) % p.table_len])) << (8 * b);
+                tw[w] = word;
+            }
+        }
+        const uint32_t t0 = tw[0], t1 = tw[1], t2 = tw[2], t3 = tw[3];
+        const uint32_t full_leader = mapa_shared(full0, 0);
+        const uint32_t slot_leader = mapa_shared(relay_dst0, 0) + rank * KC_RELAY;
+        int stage = 0, q = 0;
+        uint32_t phase = 0, qph = 0;
+        bool ok = true;
+        for (int t = cid; t < p.num_tiles && ok; t += ncl) {
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                const bool got =
+                    mbar_wait_warp(cfull0 + 8 * q, qph, p.budget_ns, p.status, KERR_TIMEOUT_MMA_FULL) &&
+                    mbar_wait_warp(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
+                                   KERR_TIMEOUT_MMA_FULL);
+                if (got) {
+                    uint8_t* sb = smem + stage * KT_STAGE_BYTES + 2 * KC_A_BYTES;
+                    const uint8_t* sq = codes + q * KC_C_BYTES;
+                    constexpr int REPS = (128 * 8) / (32 * KC_DEC_WARPS);
+                    uint2 cw[REPS];
+#pragma unroll
+                    for (int rep = 0; rep < REPS; ++rep) {
+                        const int u = dt + rep * 32 * KC_DEC_WARPS;
+                        cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
+                    }
+#pragma unroll
+                    for (int rep = 0; rep < REPS; ++rep) {
+                        const int u = dt + rep * 32 * KC_DEC_WARPS;
+                        const int r = u >> 3, qq = u & 7;
+                        const uint2 e0 = dec8(cw[rep].x, t0, t1, t2, t3);
+                        const uint2 e1 = dec8(cw[rep].y, t0, t1, t2, t3);
+                        *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                            make_uint4(e0.x, e0.y, e1.x, e1.y);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(cempty0 + 8 * q);
+                }
+                fence_proxy_async();
+                if (!bar_and_all(1, 32 * KC_DEC_WARPS, got)) {
+                    ok = false;
+                    break;
+                }
+                if (dt == 0)
+                    bulk_copy_s2c(slot_leader + 2 * KC_RELAY * stage, relay_src, KC_RELAY,
+                                  full_leader + 8 * stage);
+                if (++stage == KT_STAGES) stage = 0, phase ^= 1;
+                if (++q == KT_QSTAGES) q = 0, qph ^= 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, 2 * KC_BN);
+    }
+}
+
+template <bool B_MN, bool TALL>
 static cudaError_t kc_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
                                const K1CParams& p, int max_clusters, cudaStream_t stream) {
-    auto kern = k1c_pair_kernel<B_MN>;
+    auto kern = TALL ? k1c_tall_kernel<B_MN> : k1c_pair_kernel<B_MN>;
+    const int smem = TALL ? KT_SMEM_BYTES : KC_SMEM_BYTES;
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-        cudaError_t e =
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_done[dev] = true;
     }
@@ -415,7 +805,7 @@ static cudaError_t kc_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmQ, c
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(KC_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = KC_SMEM_BYTES;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -457,10 +847,13 @@ int k1c_max_clusters() {
 }
 
 cudaError_t k1c_launch(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
-                       int orientation, const K1CParams& p, cudaStream_t stream) {
+                       int orientation, bool tall, const K1CParams& p, cudaStream_t stream) {
     const int mc = k1c_max_clusters();
-    return orientation == 0 ? kc_launch_t<true>(tmA, tmQ, tmC, p, mc, stream)
-                            : kc_launch_t<false>(tmA, tmQ, tmC, p, mc, stream);
+    if (tall)
+        return orientation == 0 ? kc_launch_t<true, true>(tmA, tmQ, tmC, p, mc, stream)
+                                : kc_launch_t<false, true>(tmA, tmQ, tmC, p, mc, stream);
+    return orientation == 0 ? kc_launch_t<true, false>(tmA, tmQ, tmC, p, mc, stream)
+                            : kc_launch_t<false, false>(tmA, tmQ, tmC, p, mc, stream);
 }
 
 }  // namespace uor
