@@ -121,6 +121,7 @@ typedef struct uor_b200_route {
     uint32_t pairs;       /* int8 slice-pair GEMMs run on the tensor cores (1 for K1) */
     uint32_t fixups;      /* exact float: cells recomputed exactly after the lazy digits */
     uint32_t moduli;      /* exact float / wide integers: moduli of the modular route (0: slices) */
+    uint32_t crt;         /* modular route: 1 when the CRT's columns ran on the tensor cores */
 } uor_b200_route;
 
 #define UOR_B200_DEVICE_POINTERS 1u

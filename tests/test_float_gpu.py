@@ -255,12 +255,38 @@ def test_modular_route_two_reduction_chunks():
     assert route.moduli > 0 and route.k_chunks == 2
 
 
+@pytest.mark.parametrize("exp_range,moduli", [(8, (2, 28)), (40, (29, 32)), (50, (33, 40))])
+@pytest.mark.parametrize("m,k,n", [(70, 100, 56), (200, 300, 200)])
+def test_modular_route_crt_on_tensor_cores(exp_range, moduli, m, k, n):
+    """The CRT's columns as a tensor-core product (one reduction chunk, finite operands,
+    m n a multiple of 16): W with 32 columns (up to 28 moduli), 64 columns, and two K32
+    steps past 32 moduli; 3920 cells leave a ragged last block of 128. Every epilogue,
+    f32 and f64 outputs, bit for bit against the oracle."""
+    rng = np.random.default_rng(exp_range * 1000 + m)
+
+    def draw(count):
+        mant = rng.integers(1 << 23, 1 << 24, size=count).astype(np.float64)
+        e = rng.integers(-exp_range, exp_range + 1, size=count)
+        return (rng.choice([-1.0, 1.0], size=count) * np.ldexp(mant, e - 23)).astype(np.float32)
+    a, b = draw(m * k), draw(k * n)
+    b[3 * n:4 * n] = 0.0  # a zero row of B
+    a[5 * k:6 * k] = 0.0  # a zero row of A: its output row is exactly +0
+    for out in (U.F32, U.F64):
+        c0 = rng.standard_normal(m * n).astype(FT[out])
+        for alpha, beta, mode in [(1, 0, U.NEAREST), (-3, 2, U.NEAREST), (2**40, -1, U.TOWARD_ZERO)]:
+            got, want, route = run_both(U.F32, out, a, b, m, k, n, alpha, beta, c0, mode)
+            assert np.array_equal(got, want), (out, alpha, beta, mode)
+            assert route.crt == 1 and moduli[0] <= route.moduli <= moduli[1], route.moduli
+
+
+@pytest.mark.parametrize("nonfinite", [True, False])
 @pytest.mark.parametrize("elem,m,k,n", [(U.F32, 1000, 300, 4096), (U.F64, 1100, 64, 4096)])
-def test_modular_route_tall_products(elem, m, k, n):
+def test_modular_route_tall_products(elem, m, k, n, nonfinite):
     """Tall, wide products on the modular route (several row tiles of CTA pairs, a ragged
     last tile): the whole result equals the digit-slice route's bit for bit, and rows
-    spread over the tiles equal the oracle's, under beta != 0 with non-finite values in
-    two rows."""
+    spread over the tiles equal the oracle's, under beta != 0, with non-finite values in
+    two rows (the CRT on CUDA cores) or without (its columns on the tensor cores, many
+    blocks of 128 cells per CTA)."""
     rng = np.random.default_rng(30 + m)
     dt = FT[elem]
     if elem == U.F32:
@@ -271,8 +297,9 @@ def test_modular_route_tall_products(elem, m, k, n):
             mant = rng.integers(1 << 52, 1 << 53, size=count, dtype=np.int64).astype(np.float64)
             return rng.choice([-1.0, 1.0], size=count) * np.ldexp(mant, rng.integers(-30, 31, count) - 52)
         a, b = draw(m * k), draw(k * n)
-    a[900 * k + 5] = np.inf
-    a[950 * k + 7] = np.nan
+    if nonfinite:
+        a[900 * k + 5] = np.inf
+        a[950 * k + 7] = np.nan
     c0 = rng.standard_normal(m * n).astype(dt)
     outs = {}
     for digits in (False, True):
@@ -282,6 +309,7 @@ def test_modular_route_tall_products(elem, m, k, n):
                      route=route, digits=digits)
         outs[digits] = c.view(UT[elem])
         assert (route.moduli > 0) != digits
+        assert route.crt == (not digits and not nonfinite)
     assert np.array_equal(outs[False], outs[True])
     for i in (0, 511, 512, 767, 768, 900, 950, m - 1):
         w = c0[i * n:(i + 1) * n].copy()

@@ -1381,6 +1381,49 @@ __device__ __forceinline__ bool fm_encode_fast(const uint32_t (&limb)[NL], uint3
     return true;
 }
 
+// The fast case for f32 results from a 64-bit window of S's limbs: the limb h at the top
+// that is not the sign's extension over the limb below it, or limb h alone under the
+// extension word when its top bit disagrees with the sign; either way at least 31
+// significant bits. The limbs under the window only decide whether S lies strictly
+// between two steps of the window, so their OR is jammed into bit 0, seven or more bits
+// below the round bit (a value strictly inside a step and the jammed window round alike;
+// bit 0 is never a halfway point there), and the int64 -> f32 conversion, round to
+// nearest even, rounds the window as it rounds S. The window's unit 2^(32 w + ex) then
+// goes into the exponent field. False under the same conditions as fm_encode_fast.
+template <int NL>
+__device__ __forceinline__ bool fm_encode_f32_window(const uint32_t (&limb)[NL], uint32_t ext, int ex,
+                                                     const FxEpi& e, uint64_t& bits) {
+    uint32_t hi = ext, lo = limb[0];
+    int w = 0;  // the window's low limb
+    bool found = false;
+#pragma unroll
+    for (int l = NL - 1; l >= 1; --l) {
+        const bool take = !found && limb[l] != ext;
+        hi = take ? limb[l] : hi;
+        lo = take ? limb[l - 1] : lo;
+        w = take ? l - 1 : w;
+        found = found || take;
+    }
+    if (found && ((hi ^ ext) >> 31) != 0) {
+        lo = hi;
+        hi = ext;
+        ++w;
+    }
+    uint32_t below = 0;
+#pragma unroll
+    for (int l = 0; l < NL - 1; ++l) below |= l < w ? limb[l] : 0u;
+    const int64_t W = static_cast<int64_t>((static_cast<uint64_t>(hi) << 32) | lo) | (below != 0 ? 1 : 0);
+    const uint64_t mag = ext != 0 ? 0ull - static_cast<uint64_t>(W) : static_cast<uint64_t>(W);
+    if (mag == 0) {
+        bits = 0;  // exact zero encodes +0
+        return true;
+    }
+    const int exp = ex + 32 * w + 63 - __clzll(static_cast<long long>(mag));  // of S's leading one
+    if (exp < 1 - 127 || exp > 127 || exp - 23 <= e.min_exp_e) return false;
+    bits = __float_as_uint(__ll2float_rn(W)) + static_cast<uint32_t>(ex + 32 * w) * (1u << 23);
+    return true;
+}
+
 // beta != 0 or non-finite terms: the register form and finish_float.
 template <int NW>
 __device__ __forceinline__ void fm_finish_slow(const uint64_t (&w)[NW], uint64_t ext, int64_t off, int ex,
@@ -1404,7 +1447,8 @@ __device__ __forceinline__ void fm_finish_cell(const uint32_t (&limb)[FmLimbs<NM
     constexpr int NW = (NL + 1) / 2 + 2;  // 64-bit words: the value, alpha's 64 bits, sign
     if (e.beta == 0 && !fl0 && e.alpha == 1 && e.mode == MODE_NEAREST) {
         uint64_t bits;
-        if (fm_encode_fast<NL>(limb, ext32, ex, e, bits)) {
+        if (e.out64 ? fm_encode_fast<NL>(limb, ext32, ex, e, bits)
+                    : fm_encode_f32_window<NL>(limb, ext32, ex, e, bits)) {
             store_float(e.c, e.out64, off, bits);
             return;
         }
@@ -1497,6 +1541,203 @@ __global__ void __launch_bounds__(256, 3) fm_crt4_kernel(const uint8_t* __restri
     }
 }
 
+// ---- the CRT's columns on the tensor cores
+//
+// With one reduction chunk the residue planes hold y_g of every cell, and the CRT's
+// columns are one small integer product per block of 128 cells: Y (cells x moduli, u8)
+// times W (moduli x columns, u8), W's columns the four bytes of ceil(2^32 / p_g) (the
+// fixed-point sum that gives t) and the NM - 1 bytes of M / p_g (X's base-256 columns).
+// Each plane is a row of the MN-major A operand, so TMA copies the planes' 128-byte runs
+// straight into it (moduli past NM read as zero) and tcgen05.mma.kind::i8 (M128, K32, N 32
+// or 64) sums the columns exactly in s32 TMEM lanes (each below NM 255^2 < 2^22). One
+// thread per cell then reads its lane, forms t and the limbs of X - t M and encodes, as
+// fm_crt4_kernel does from its dp4a columns. The per-cell encode is the cost, so one CTA
+// per SM keeps four epilogue warpgroups busy, each with its own blocks, and the whole TMEM
+// as slots of N columns, so the MMAs run up to 512 / N blocks ahead of the epilogues.
+//   warp 0      one elected thread: TMA of each block's planes into a ring of stages;
+//   warp 1      TMEM (512 columns), one elected thread issues the MMAs;
+//   warps 2-17  four warpgroups; block b of this CTA goes to warpgroup b % 4 and TMEM slot
+//               b % (512 / N); one cell per thread: the limbs, the encode and the store.
+template <int NM>
+struct FmTc {
+    static constexpr int NCOL = 4 + FmColumns<NM>::value;  // F_0 .. F_3, then X_b
+    static constexpr int N = NCOL <= 32 ? 32 : 64;
+    static constexpr int KCH = (NM + 31) / 32;              // K32 MMAs per block
+    static constexpr int STAGE = KCH * 4096;                // 32 planes x 128 cells each
+    static constexpr int STAGES = 16;
+    static constexpr int SLOTS = 512 / N;
+};
+constexpr int FMT_GROUPS = 4;
+constexpr int FMT_THREADS = 64 + 128 * FMT_GROUPS;
+// Waits suspend in hardware for up to this long per poll (the roles that wait most, the
+// producer and the MMA issuer, then take no issue slots from the epilogues).
+constexpr uint32_t FMT_HINT_NS = 100000;
+// More than half of an SM's shared memory: one CTA per SM, which owns the whole TMEM.
+constexpr int FMT_SMEM = 140 * 1024;
+
+template <int NM>
+__global__ void __launch_bounds__(FMT_THREADS, 1)
+    fm_crt_tc_kernel(const __grid_constant__ CUtensorMap tmY, size_t total, int n,
+                     const int* __restrict__ rlo, const int* __restrict__ clo,
+                     const int* __restrict__ rspan, const int* __restrict__ cspan, FxEpi e,
+                     const __grid_constant__ FmParams f, int* status, uint64_t budget_ns) {
+    using T = FmTc<NM>;
+    constexpr int NB = FmColumns<NM>::value;
+    constexpr int NL = FmLimbs<NM>::value;
+    constexpr int S = T::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* wmat = smem + S * T::STAGE;  // B: N rows (columns) x 128 bytes (moduli)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wmat + T::N * 128);
+    // bars: full[S], empty[S], tfull[SLOTS], tempty[SLOTS], drain
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + S);
+    const uint32_t tfull0 = smem_u32(bars + 2 * S);
+    const uint32_t tempty0 = smem_u32(bars + 2 * S + T::SLOTS);
+    const uint32_t drain = smem_u32(bars + 2 * S + 2 * T::SLOTS);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 2 * T::SLOTS + 1);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const size_t nblk = (total + 127) / 128;
+    // blocks of this CTA: blockIdx.x + b gridDim.x for b < nlocal
+    const int nlocal = blockIdx.x < nblk ? static_cast<int>((nblk - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+
+    // W, K-major with the 128-byte swizzle: column c's moduli in row c, byte g of a row
+    // at 16-byte chunk (g / 16) ^ (c % 8).
+    for (int x = threadIdx.x; x < T::N * 128; x += FMT_THREADS) {
+        const int c = x >> 7, g = x & 127;
+        uint32_t v = 0;
+        if (g < NM) {
+            if (c < 4) v = f.mg[g >> 2][c] >> (8 * (g & 3));
+            else if (c - 4 < NB) v = f.md[g >> 2][c - 4] >> (8 * (g & 3));
+        }
+        wmat[c * 128 + ((((g >> 4) ^ c) & 7) << 4) + (g & 15)] = static_cast<uint8_t>(v);
+    }
+    fence_proxy_async();  // the generic writes above, before the tensor core reads them
+    if (threadIdx.x == 0) {
+        for (int q = 0; q < S; ++q) {
+            mbar_init(full0 + 8 * q, 1);
+            mbar_init(empty0 + 8 * q, 1);
+        }
+        for (int q = 0; q < T::SLOTS; ++q) {
+            mbar_init(tfull0 + 8 * q, 1);
+            mbar_init(tempty0 + 8 * q, 4);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        tma_prefetch_desc(&tmY);
+    }
+    if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            const uint64_t pol = l2_policy_evict_first();
+            int issued = 0;  // blocks whose copies were started
+            bool ok = true;
+            for (int b = 0; b < nlocal; ++b) {
+                const int stage = b % S;
+                if (!mbar_wait_hint(empty0 + 8 * stage, ((b / S) & 1) ^ 1, budget_ns, status, KERR_TIMEOUT_PRODUCER,
+                                    FMT_HINT_NS)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t fb = full0 + 8 * stage;
+                mbar_expect_tx(fb, T::STAGE);
+                issued = b + 1;
+                const uint32_t sa = smem_u32(smem + stage * T::STAGE);
+                const int x = static_cast<int>((blockIdx.x + static_cast<size_t>(b) * gridDim.x) * 128);
+#pragma unroll
+                for (int kc = 0; kc < T::KCH; ++kc) tma_load_2d(sa + kc * 4096, &tmY, fb, x, kc * 32, pol);
+            }
+            if (!ok) {
+                // Let every copy in flight land before the CTA exits: those of the last S
+                // blocks issued, each on its stage's full barrier with its block's parity.
+                for (int b = issued > S ? issued - S : 0; b < issued; ++b)
+                    mbar_wait(full0 + 8 * (b % S), (b / S) & 1, budget_ns, status, KERR_TIMEOUT_DRAIN);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        constexpr uint32_t idesc = idesc_i8(128, T::N, false, false, true, false);
+        const uint32_t sw = smem_u32(wmat);
+        bool ok = true, issued = false;
+        for (int b = 0; b < nlocal; ++b) {
+            const int stage = b % S, slot = b % T::SLOTS;
+            if (!mbar_wait_warp_hint(tempty0 + 8 * slot, ((b / T::SLOTS) & 1) ^ 1, budget_ns, status,
+                                     KERR_TIMEOUT_MMA_ACC, FMT_HINT_NS) ||
+                !mbar_wait_warp_hint(full0 + 8 * stage, (b / S) & 1, budget_ns, status, KERR_TIMEOUT_MMA_FULL,
+                                     FMT_HINT_NS)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            if (elect_one()) {
+                const uint32_t sa = smem_u32(smem + stage * T::STAGE);
+#pragma unroll
+                for (int kc = 0; kc < T::KCH; ++kc)
+                    mma_i8(tmem_base + slot * T::N, smem_desc_sw128(sa + kc * 4096, 4096, 1024),
+                           smem_desc_sw128(sw + kc * 32, 16, 1024), idesc, kc != 0);
+                mma_commit(empty0 + 8 * stage);
+                mma_commit(tfull0 + 8 * slot);
+                issued = true;
+            }
+            __syncwarp();
+        }
+        if (!ok) {
+            if (elect_one() && issued) {
+                mma_commit(drain);
+                mbar_wait(drain, 0, budget_ns, status, KERR_TIMEOUT_DRAIN);
+            }
+            __syncwarp();
+        }
+    } else {
+        const int group = (warp - 2) >> 2;
+        const int quarter = warp & 3;  // the TMEM lane quarter this warp may read
+        const int row = quarter * 32 + lane;
+        GridWalk wk(static_cast<size_t>(n), (blockIdx.x + static_cast<size_t>(group) * gridDim.x) * 128 + row,
+                    static_cast<size_t>(FMT_GROUPS) * gridDim.x * 128);
+        for (int b = group; b < nlocal; b += FMT_GROUPS, wk.next()) {
+            const int slot = b % T::SLOTS;
+            if (!mbar_wait_warp_hint(tfull0 + 8 * slot, (b / T::SLOTS) & 1, budget_ns, status,
+                                     KERR_TIMEOUT_EPILOGUE, FMT_HINT_NS))
+                break;
+            tc_fence_after();
+            uint32_t r[T::N];
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + slot * T::N;
+            __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+            tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+            if constexpr (T::N == 64) tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty0 + 8 * slot);
+            if (wk.idx >= total) continue;
+            const int i = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
+            const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
+            if (e.beta == 0 && (rspan[i] == 0 || cspan[j] == 0)) {
+                store_float(e.c, e.out64, off, 0);  // a row or column of zeros: S = 0
+                continue;
+            }
+            const uint32_t F[4] = {r[0], r[1], r[2], r[3]};
+            uint32_t limb[NL];
+            const uint32_t ext = fm_crt_limbs_signed<NM>(fm_crt_t(F), f, [&](int c) { return r[4 + c]; }, limb);
+            fm_finish_cell<NM>(limb, ext, off, rlo[i] + clo[j], 0, e);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
 // Launches for a moduli count (even, 2 .. 40): the limbs of X < NM M with M < 2^(8 NM).
 template <int NM>
 static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, const uint8_t* a,
@@ -1523,10 +1764,25 @@ static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, con
         bs, np, kp, b, rsb, csb, k, n, clo, pw, shmax, f);
 }
 
+// True when the tensor-core columns ran.
 template <int NM>
-static void fm_launch_crt(const uint8_t* res, int chunks, int m, int n, const int* rlo,
+static bool fm_launch_crt(const uint8_t* res, int chunks, int m, int n, const int* rlo,
                           const int* clo, const int* rspan, const int* cspan, const uint8_t* flags,
-                          const FxEpi& e, const FmParams& f, int grid, cudaStream_t s) {
+                          const FxEpi& e, const FmParams& f, int grid, int sm_count, int* status,
+                          uint64_t budget_ns, cudaStream_t s) {
+    const size_t total = static_cast<size_t>(m) * n;
+    CUtensorMap tmY;
+    // The tensor-core columns: one chunk, no non-finite terms, planes TMA can address.
+    if (chunks == 1 && !flags && total % 16 == 0 && total < (size_t{1} << 31) &&
+        make_tmap_u8(&tmY, res, total, NM, total, 128, 32)) {
+        auto kern = fm_crt_tc_kernel<NM>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FMT_SMEM);
+        const size_t nblk = (total + 127) / 128;
+        const size_t cap = static_cast<size_t>(sm_count);
+        kern<<<static_cast<int>(nblk < cap ? nblk : cap), FMT_THREADS, FMT_SMEM, s>>>(
+            tmY, total, n, rlo, clo, rspan, cspan, e, f, status, budget_ns);
+        return true;
+    }
     if (chunks == 1 && (n & 3) == 0) {
         const size_t quads = static_cast<size_t>(m) * n / 4;
         const int g4 = static_cast<int>((quads + 255) / 256 < 148 * 16 ? (quads + 255) / 256 : 148 * 16);
@@ -1534,6 +1790,7 @@ static void fm_launch_crt(const uint8_t* res, int chunks, int m, int n, const in
     } else {
         fm_crt_kernel<NM><<<grid, 256, 0, s>>>(res, chunks, m, n, rlo, clo, rspan, cspan, flags, e, f);
     }
+    return false;
 }
 
 // ------------------------------------------------------------ direct route
@@ -1848,11 +2105,12 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
             return st2;
         const size_t total = m * n;
         const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+        bool crt_tc = false;
         switch (nm) {
 #define FM_CRT(N)                                                                               \
     case N:                                                                                     \
-        fm_launch_crt<N>(res, q.num_chunks, (int)m, (int)n, rlo, clo, rspan, cspan, flags, e, fm, \
-                         rgrid, s);                                                             \
+        crt_tc = fm_launch_crt<N>(res, q.num_chunks, (int)m, (int)n, rlo, clo, rspan, cspan, flags, e, fm, \
+                         rgrid, ctx->sm_count, ctx->d_status, ctx->budget_ns, s);               \
         break;
             FM_EVEN_COUNTS(FM_CRT)
 #undef FM_CRT
@@ -1864,6 +2122,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
             route->a_layout = route->b_layout = (uint32_t)nm;
             route->k_chunks = (uint32_t)q.num_chunks;
             route->tile_m = (uint32_t)(m > 128 ? 256 : KS_BM);
+            route->crt = crt_tc ? 1u : 0u;
         }
         return cuda_status(cudaGetLastError());
     };

@@ -103,6 +103,7 @@ bool fm_plan_bound(const uint32_t* bound, int limbs, FmParams& f) {
         return static_cast<uint32_t>((x.l[b >> 2] >> (8 * (b & 3))) & 255u);
     };
     for (int l = 0; l < FM_MAX / 4 + 1; ++l) f.mm[l] = M.l[l];
+    for (int b = 0; b < FM_MAX; ++b) f.nmb[b] = -static_cast<int32_t>(byte_of(M, b));
     for (int g = 0; g < nm; ++g) {
         const uint32_t p = kModuli[g];
         HBig mg = M;

@@ -33,6 +33,7 @@ struct FmParams {
     uint64_t hm[FM_MAX];              // half_g ceil(2^32 / p_g): the shift folded into a quotient
     uint32_t md[FM_MAX / 4][FM_MAX];  // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
     uint32_t mm[FM_MAX / 4 + 1];      // 32-bit limbs of M (M < 2^(8 nm))
+    int32_t nmb[FM_MAX];              // -byte b of M
 };
 
 // The smallest even prefix of the moduli (256, 255, 253, 251, 247 and primes) whose
@@ -94,16 +95,79 @@ struct FmLimbs {
     static constexpr int value = (NM + 1 + 3) / 4;
 };
 
-// S from the packed y words ya[a] (byte gi = y_{4a+gi}) as two's complement limbs, least
-// significant first; returns the sign extension (0 or ~0) of the limbs above. t comes from
-// the fixed-point sum in four byte columns of ceil(2^32 / p_g) (F_b below NM 255^2 < 2^22,
-// so F_0 + 2^8 F_1 and F_2 + 2^8 F_3 stay in 32 bits), the same integer as the sum of the
-// products; each limb of X is four base-256 columns joined the same way.
+// Base-256 columns X_b of X: from three moduli on, M / p_g is a product of NM - 1 moduli of
+// which at most one is 256, so it stays below 256^(NM - 1) and its byte NM - 1 is zero.
+template <int NM>
+struct FmColumns {
+    static constexpr int value = NM >= 3 ? NM - 1 : NM;
+};
+
+// t, the integer nearest X / M, from the four byte columns F_b of the fixed-point sum
+// sum_g y_g ceil(2^32 / p_g) (each F_b below NM 255^2 < 2^22, so F_0 + 2^8 F_1 and
+// F_2 + 2^8 F_3 stay in 32 bits).
+__device__ __forceinline__ uint32_t fm_crt_t(const uint32_t (&F)[4]) {
+    const uint64_t fx = (static_cast<uint64_t>(F[2] + (F[3] << 8)) << 16) + (F[0] + (F[1] << 8)) +
+                        0x80000000ull;  // + 1/2
+    return static_cast<uint32_t>(fx >> 32);
+}
+
+// S = X - t M as two's complement 32-bit limbs, least significant first, from the columns
+// col(b) = X_b (each below NM 255^2 < 2^22), four to a limb, minus t M limb by limb; returns
+// the sign extension (0 or ~0) of the limbs above.
+template <int NM, typename Col>
+__device__ __forceinline__ uint32_t fm_crt_limbs(uint32_t t, const FmParams& f, Col col,
+                                                 uint32_t (&limb)[FmLimbs<NM>::value]) {
+    constexpr int NL = FmLimbs<NM>::value;
+    constexpr int NB = FmColumns<NM>::value;
+    int64_t carry = 0;
+#pragma unroll
+    for (int l = 0; l < NL; ++l) {
+        uint32_t c[4];
+#pragma unroll
+        for (int bi = 0; bi < 4; ++bi) c[bi] = 4 * l + bi < NB ? col(4 * l + bi) : 0u;
+        const uint64_t v = (static_cast<uint64_t>(c[2] + (c[3] << 8)) << 16) + (c[0] + (c[1] << 8));
+        const uint32_t ml = l < FM_MAX / 4 + 1 ? f.mm[l] : 0u;
+        const int64_t sv = static_cast<int64_t>(v) + carry - static_cast<int64_t>(static_cast<uint64_t>(t) * ml);
+        limb[l] = static_cast<uint32_t>(sv);
+        carry = sv >> 32;
+    }
+    return carry < 0 ? ~0u : 0u;
+}
+
+// The same limbs from the signed byte columns d_b = X_b - t M_b, mostly multiply-adds: t is
+// below NM (X < NM M), so |d_b| < 2^22; e = d_4l + 2^8 d_4l+1 + carry and
+// e' = d_4l+2 + 2^8 d_4l+3 stay inside 31 bits, and L = 2^16 e' + e (|L| < 2^47) is one
+// widening multiply-add whose low word is the limb and whose high word is the next carry.
+template <int NM, typename Col>
+__device__ __forceinline__ uint32_t fm_crt_limbs_signed(uint32_t t, const FmParams& f, Col col,
+                                                        uint32_t (&limb)[FmLimbs<NM>::value]) {
+    constexpr int NL = FmLimbs<NM>::value;
+    constexpr int NB = FmColumns<NM>::value;
+    int32_t carry = 0;
+#pragma unroll
+    for (int l = 0; l < NL; ++l) {
+        int32_t d[4];
+#pragma unroll
+        for (int bi = 0; bi < 4; ++bi) {
+            const int b = 4 * l + bi;
+            const int32_t x = b < NB ? static_cast<int32_t>(col(b)) : 0;
+            d[bi] = b < FM_MAX ? x + static_cast<int32_t>(t) * f.nmb[b < FM_MAX ? b : 0] : x;
+        }
+        const int32_t e0 = d[0] + d[1] * 256 + carry;
+        const int32_t e1 = d[2] + d[3] * 256;
+        const int64_t L = static_cast<int64_t>(e1) * 65536 + e0;
+        limb[l] = static_cast<uint32_t>(L);
+        carry = static_cast<int32_t>(L >> 32);
+    }
+    return carry < 0 ? ~0u : 0u;
+}
+
+// S from the packed y words ya[a] (byte gi = y_{4a+gi}): the columns F_b and X_b by dp4a,
+// four moduli per instruction.
 template <int NM>
 __device__ __forceinline__ uint32_t fm_crt_packed(const uint32_t (&ya)[(NM + 3) / 4], const FmParams& f,
                                                   uint32_t (&limb)[FmLimbs<NM>::value]) {
     constexpr int NA = (NM + 3) / 4;
-    constexpr int NL = FmLimbs<NM>::value;
     uint32_t F[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
@@ -111,33 +175,12 @@ __device__ __forceinline__ uint32_t fm_crt_packed(const uint32_t (&ya)[(NM + 3) 
 #pragma unroll
         for (int a = 0; a < NA; ++a) F[b] = __dp4a(ya[a], f.mg[a][b], F[b]);
     }
-    const uint64_t fx = (static_cast<uint64_t>(F[2] + (F[3] << 8)) << 16) + (F[0] + (F[1] << 8)) +
-                        0x80000000ull;  // + 1/2
-    const uint32_t t = static_cast<uint32_t>(fx >> 32);
-    // Columns X_b (each below NM 255^2 < 2^22), four to a limb, minus t M limb by limb. From
-    // three moduli on, M / p_g is a product of NM - 1 moduli of which at most one is 256, so
-    // it stays below 256^(NM - 1) and its byte NM - 1 (the last column) is zero.
-    constexpr int NB = NM >= 3 ? NM - 1 : NM;
-    int64_t carry = 0;
+    return fm_crt_limbs<NM>(fm_crt_t(F), f, [&](int b) {
+        uint32_t c = 0;
 #pragma unroll
-    for (int l = 0; l < NL; ++l) {
-        uint32_t col[4];
-#pragma unroll
-        for (int bi = 0; bi < 4; ++bi) {
-            const int b = 4 * l + bi;
-            col[bi] = 0;
-            if (b < NB) {
-#pragma unroll
-                for (int a = 0; a < NA; ++a) col[bi] = __dp4a(ya[a], f.md[a][b], col[bi]);
-            }
-        }
-        const uint64_t v = (static_cast<uint64_t>(col[2] + (col[3] << 8)) << 16) + (col[0] + (col[1] << 8));
-        const uint32_t ml = l < FM_MAX / 4 + 1 ? f.mm[l] : 0u;
-        const int64_t sv = static_cast<int64_t>(v) + carry - static_cast<int64_t>(static_cast<uint64_t>(t) * ml);
-        limb[l] = static_cast<uint32_t>(sv);
-        carry = sv >> 32;
-    }
-    return carry < 0 ? ~0u : 0u;
+        for (int a = 0; a < NA; ++a) c = __dp4a(ya[a], f.md[a][b], c);
+        return c;
+    }, limb);
 }
 
 // The same from the unpacked y_g.

@@ -89,6 +89,41 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
     }
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase
+// completes or about hint_ns have passed, so a role that waits long takes no issue slots
+// from the warps doing the work.
+__device__ __forceinline__ uint32_t mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok;
+}
+
+// mbar_wait with hinted polls.
+__device__ __forceinline__ bool mbar_wait_hint(uint32_t bar, uint32_t parity, uint64_t budget_ns,
+                                               int* status, int code, uint32_t hint_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+        if (*(volatile int*)status != 0) return false;
+        if (globaltimer() - t0 > budget_ns) {
+            atomicCAS(status, 0, code);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ bool mbar_wait_warp_hint(uint32_t bar, uint32_t parity, uint64_t budget_ns,
+                                                    int* status, int code, uint32_t hint_ns) {
+    const bool ok = mbar_wait_hint(bar, parity, budget_ns, status, code, hint_ns);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // The same wait, made warp-uniform: every lane polls (each gets the acquire),
 // and the warp proceeds only if all lanes saw the phase complete, so a timeout
 // can never split the warp ahead of a .sync.aligned instruction.

@@ -19,6 +19,15 @@ struct GridWalk {
         step_i = step / n;
         step_j = step - step_i * n;
     }
+    // Cells first, first + stride, ... (a walk whose threads cover unequal spans).
+    __device__ __forceinline__ GridWalk(size_t cols, size_t first, size_t stride) : n(cols) {
+        idx = first;
+        step = stride;
+        i = idx / n;
+        j = idx - i * n;
+        step_i = step / n;
+        step_j = step - step_i * n;
+    }
     __device__ __forceinline__ void next() {
         idx += step;
         i += step_i;

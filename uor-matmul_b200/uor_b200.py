@@ -56,7 +56,7 @@ class Route(ctypes.Structure):
                 ("k_chunks", ctypes.c_uint32), ("a_layout", ctypes.c_uint32),
                 ("b_layout", ctypes.c_uint32), ("ctas", ctypes.c_uint32),
                 ("pairs", ctypes.c_uint32), ("fixups", ctypes.c_uint32),
-                ("moduli", ctypes.c_uint32)]
+                ("moduli", ctypes.c_uint32), ("crt", ctypes.c_uint32)]
 
     def as_dict(self):
         d = {f: getattr(self, f) for f, _ in self._fields_}
