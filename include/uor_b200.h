@@ -411,6 +411,36 @@ int uor_b200_trop_keys_finish(uor_b200_dtype out, const int64_t *keys, size_t ke
                               const uor_b200_view_mut *c, uor_b200_trop alpha, uor_b200_trop beta,
                               const uor_b200_call *call);
 
+/* ------------------------------------------------ split-K over NCCL */
+
+/* The exchanges above driven from here: one process (or thread) per GPU, each with its
+ * own context, all in one NCCL communicator (an ncclComm_t, passed as void*). Each rank
+ * passes A's columns and B's rows of its own range of the reduction and the whole C;
+ * the entry computes its partial, all-reduces it in place on the context's stream (sum
+ * of int64 limbs; max of int64 keys for Trop<E>) and encodes the total once, so every
+ * rank's C receives the single-device bytes. The three steps are queued on the context's
+ * stream without a host round trip; the call returns when C is written unless it sets
+ * UOR_B200_ASYNC. Every rank must make the same calls in the same order (NCCL's rule).
+ * Device pointers only (call->flags DEVICE_POINTERS); the communicator's device must be
+ * the context's. NCCL is loaded on first use (libnccl.so.2, the one the process already
+ * has if any); without it these return UOR_B200_NCCL_ERROR, as they do for an NCCL
+ * failure. route, when given, reports the partial's kernel. */
+int uor_b200_gemm_splitk_nccl(void *comm, uor_b200_dtype elem, uor_b200_dtype out,
+                              const uor_b200_view *a, const uor_b200_view *b,
+                              const uor_b200_view_mut *c, int64_t alpha, int64_t beta,
+                              const uor_b200_call *call);
+int uor_b200_gemm_tropical_splitk_nccl(void *comm, uor_b200_dtype elem, uor_b200_dtype out,
+                                       const uor_b200_view *a, const uor_b200_view *b,
+                                       const uor_b200_view_mut *c, uor_b200_trop alpha,
+                                       uor_b200_trop beta, const uor_b200_call *call);
+/* A communicator without linking NCCL: rank 0 makes the 128-byte id, the caller hands it
+ * to every rank (any channel), each rank joins on its context's device (NULL: the
+ * current device's default context). */
+int uor_b200_nccl_unique_id(uint8_t *id, size_t id_len);
+int uor_b200_nccl_comm_init(uor_b200_ctx *ctx, int nranks, const uint8_t *id, size_t id_len,
+                            int rank, void **comm);
+int uor_b200_nccl_comm_destroy(void *comm);
+
 /* ------------------------------------------------- no-allocation variant */
 
 /* Size of the fixed device scratch the no-allocation entry point uses. */

@@ -1,6 +1,7 @@
 """CPU-side checks of the C ABI: the library loads, exports every declared
 symbol, and performs the reference's host-side validation (MatView::new,
 Triple::new) before touching a device. No compute call runs here."""
+import ctypes
 import os
 import re
 
@@ -183,3 +184,27 @@ def test_reference_arm_runs_without_the_product_library():
     line = json.loads(lines[-2])
     assert line["impl"] == "reference" and line["config"]["m"] == 512
     assert line["cpu_baseline"]["kind"] == "port"
+
+
+def test_nccl_entries_validate_before_loading_nccl():
+    """The collective entries refuse a missing communicator, host pointers and a bad
+    rank before they load NCCL or touch a device."""
+    lib = U.lib()
+    A = U.View(0, 0, 0, 0, 0, 1)
+    C = U.View(0, 0, 0, 0, 0, 1)
+    call = U.make_call(U.NEAREST, True, None, None, False)
+    for fn in (lib.uor_b200_gemm_splitk_nccl,):
+        assert fn(None, U.I8, U.I32, ctypes.byref(A), ctypes.byref(A), ctypes.byref(C), 1, 0,
+                  ctypes.byref(call)) == U.INVALID_ARGUMENT
+    host = U.make_call(U.NEAREST, False, None, None, False)
+    assert lib.uor_b200_gemm_tropical_splitk_nccl(
+        1, U.TROP_I8, U.TROP_I32, ctypes.byref(A), ctypes.byref(A), ctypes.byref(C),
+        U.Trop(0, 1), U.Trop(0, 0), ctypes.byref(host)) == U.INVALID_ARGUMENT
+    out = ctypes.c_void_p()
+    uid = (ctypes.c_uint8 * 128)()
+    assert lib.uor_b200_nccl_comm_init(None, 2, ctypes.addressof(uid), 128, 2,
+                                       ctypes.byref(out)) == U.INVALID_ARGUMENT
+    assert lib.uor_b200_nccl_comm_init(None, 2, ctypes.addressof(uid), 100, 0,
+                                       ctypes.byref(out)) == U.INVALID_ARGUMENT
+    assert lib.uor_b200_nccl_unique_id(ctypes.addressof(uid), 64) == U.INVALID_ARGUMENT
+    assert lib.uor_b200_nccl_comm_destroy(None) == U.OK

@@ -1,6 +1,7 @@
 """The split-K exchange on the GPU: partial limbs and the finish kernel against the
 single-device call (bit for bit), one GPU emulating the ranks' ranges; and, where the
-box has two GPUs, two NCCL ranks through uor_b200_dist.splitk_gemm."""
+box has two GPUs, two NCCL ranks through uor_b200_dist.splitk_gemm and through the C ABI's
+own NCCL entry points (uor_b200_gemm_splitk_nccl, uor_b200_gemm_tropical_splitk_nccl)."""
 import os
 import socket
 
@@ -178,3 +179,74 @@ def _worker(rank, world, port):
 def test_two_nccl_ranks_match_one_device():
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _abi_worker(rank, world, port):
+    """The C ABI's collective entries: a communicator made with uor_b200_nccl_comm_init
+    (the id passed through a TCP store), each rank its own range of the reduction, every
+    rank's C equal to the single-device call's bytes."""
+    import datetime
+    import torch.distributed as dist
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=60))
+    if rank == 0:
+        store.set("uid", U.nccl_unique_id())
+    uid = store.get("uid")
+    ctx = U.Context(rank)
+    comm = U.NcclComm(world, uid, rank, ctx)
+    try:
+        for elem, out, (m, k, n), alpha, beta, mode in [
+                (U.I32, U.I128, (256, 65536, 128), 3, -1, U.NEAREST),
+                (U.I8, U.I32, (130, 5000, 70), -2, 1, U.SATURATING),
+                (U.I16, U.I64, (64, 777, 96), 1, 0, U.WRAPPING)]:
+            a, b = _operands(elem, m, k, n)
+            prior = _prior(out, m, n)
+            want = prior.clone()
+            U.gemm(elem, out, a, (m, k, k, 1), b, (k, n, n, 1), want, (m, n, n, 1), alpha, beta,
+                   mode, ctx=ctx)
+            k0, k1 = D.k_ranges(k, world)[rank]
+            got = prior.clone()
+            route = U.Route()
+            U.gemm_splitk_nccl(comm, elem, out, a[k0:], (m, k1 - k0, k, 1), b[k0 * n:],
+                               (k1 - k0, n, n, 1), got, (m, n, n, 1), alpha, beta, mode, ctx=ctx,
+                               route=route)
+            assert torch.equal(got, want), (rank, elem, out)
+            assert route.kernel != 0
+            # asynchronous: returns at once, the context's sync reports the status
+            got = prior.clone()
+            U.gemm_splitk_nccl(comm, elem, out, a[k0:], (m, k1 - k0, k, 1), b[k0 * n:],
+                               (k1 - k0, n, n, 1), got, (m, n, n, 1), alpha, beta, mode, ctx=ctx,
+                               asynchronous=True)
+            ctx.sync()
+            assert torch.equal(got, want), (rank, elem, out, "async")
+        m, k, n = 96, 4000, 80
+        ah, ta = _trop(43, m * k, 8)
+        bh, tb = _trop(44, k * n, 8)
+        ph, prior = _trop(45, m * n, 32, -100, 100)
+        want = prior.clone()
+        U.gemm_tropical(U.TROP_I8, U.TROP_I32, ta, (m, k, k, 1), tb, (k, n, n, 1), want,
+                        (m, n, n, 1), (3, True), (-5, True), ctx=ctx)
+        k0, k1 = D.k_ranges(k, world)[rank]
+        got = prior.clone()
+        U.gemm_tropical_splitk_nccl(comm, U.TROP_I8, U.TROP_I32, ta[2 * k0:], (m, k1 - k0, k, 1),
+                                    tb[2 * k0 * n:], (k1 - k0, n, n, 1), got, (m, n, n, 1),
+                                    (3, True), (-5, True), ctx=ctx)
+        assert torch.equal(got, want), rank
+        # a communicator of another device is refused before any work
+        with pytest.raises(U.UorError):
+            other = U.Context(1 - rank)
+            try:
+                U.gemm_splitk_nccl(comm, U.I8, U.I32, a, (4, 4, k, 1), b, (4, 4, n, 1), got,
+                                   (4, 4, n, 1), ctx=other)
+            finally:
+                other.close()
+    finally:
+        comm.destroy()
+        ctx.close()
+
+
+@pytest.mark.skipif(not torch or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_through_the_c_abi_nccl_entries():
+    import torch.multiprocessing as mp
+    mp.spawn(_abi_worker, args=(2, _free_port()), nprocs=2, join=True)

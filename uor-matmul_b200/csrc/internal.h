@@ -19,7 +19,8 @@ struct uor_b200_ctx {
     // staging slots host-pointer calls copy operands through, an auxiliary buffer
     // for operands a path rebuilds (decoded codes), and a dense decoded operand
     // handed to a driver that uses the auxiliary buffer itself.
-    static constexpr int kSlots = 6;
+    // A seventh slot holds the exchange buffer of the collective entry points.
+    static constexpr int kSlots = 7;
     void* buf[kSlots] = {};
     size_t cap[kSlots] = {};
     // Host-pointer pipelining: copy-in and copy-out streams and a pool of events,
@@ -31,7 +32,7 @@ struct uor_b200_ctx {
 
 namespace uor {
 
-enum Slot { SLOT_WS = 0, SLOT_A = 1, SLOT_B = 2, SLOT_C = 3, SLOT_AUX = 4, SLOT_DECODED = 5 };
+enum Slot { SLOT_WS = 0, SLOT_A = 1, SLOT_B = 2, SLOT_C = 3, SLOT_AUX = 4, SLOT_DECODED = 5, SLOT_XCHG = 6 };
 
 // A device buffer of at least `bytes` in the given slot (grown with cudaMalloc;
 // the previous contents are not kept).

@@ -130,6 +130,11 @@ def lib():
             "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
             "uor_b200_trop_partial_keys": ([I, VP, VP, P, Z, CP], I),
             "uor_b200_trop_keys_finish": ([I, P, Z, VP, Trop, Trop, CP], I),
+            "uor_b200_gemm_splitk_nccl": ([P, I, I, VP, VP, VP, L64, L64, CP], I),
+            "uor_b200_gemm_tropical_splitk_nccl": ([P, I, I, VP, VP, VP, Trop, Trop, CP], I),
+            "uor_b200_nccl_unique_id": ([P, Z], I),
+            "uor_b200_nccl_comm_init": ([P, I, P, Z, I, ctypes.POINTER(P)], I),
+            "uor_b200_nccl_comm_destroy": ([P], I),
             "uor_b200_status_string": ([I], ctypes.c_char_p),
             "uor_b200_version": ([], I),
             "uor_b200_selftest_wait_timeout": ([P, U64], I),
@@ -524,6 +529,72 @@ def trop_keys_finish(out, keys, c, cv, alpha=(0, True), beta=(0, False), encode=
                                            Trop(alpha[0], int(alpha[1])),
                                            Trop(beta[0], int(beta[1])), ctypes.byref(call)),
            "trop_keys_finish")
+
+
+# ------------------------------------------------------------------ split-K over NCCL
+
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """A new NCCL unique id (rank 0 makes it; every rank joins with it)."""
+    buf = (ctypes.c_uint8 * NCCL_ID_BYTES)()
+    _check(lib().uor_b200_nccl_unique_id(ctypes.addressof(buf), NCCL_ID_BYTES), "nccl_unique_id")
+    return bytes(buf)
+
+
+class NcclComm:
+    """An NCCL communicator made through the C ABI (uor_b200_nccl_comm_init) on the
+    context's device; destroy() (or the context manager) releases it."""
+
+    def __init__(self, nranks: int, uid: bytes, rank: int, ctx: "Context | None" = None):
+        if len(uid) != NCCL_ID_BYTES:
+            raise UorError(INVALID_ARGUMENT, "an NCCL id is 128 bytes")
+        buf = (ctypes.c_uint8 * NCCL_ID_BYTES).from_buffer_copy(uid)
+        out = ctypes.c_void_p()
+        _check(lib().uor_b200_nccl_comm_init(ctx.handle if ctx else None, nranks,
+                                             ctypes.addressof(buf), NCCL_ID_BYTES, rank,
+                                             ctypes.byref(out)), "nccl_comm_init")
+        self.handle = out.value
+
+    def destroy(self):
+        if self.handle:
+            _check(lib().uor_b200_nccl_comm_destroy(self.handle), "nccl_comm_destroy")
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.destroy()
+
+
+def gemm_splitk_nccl(comm, elem, out, a, av, b, bv, c, cv, alpha=1, beta=0, encode=NEAREST,
+                     ctx=None, route=None, asynchronous=False):
+    """This rank's range of the reduction (A's columns, B's rows) in, the whole exact C out
+    on every rank: partial limbs, an NCCL all-reduce and the finish (device buffers)."""
+    if not _on_device(a, b, c):
+        raise UorError(INVALID_ARGUMENT, "gemm_splitk_nccl takes device buffers")
+    A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
+    call = make_call(encode, True, ctx, route, asynchronous)
+    _check(lib().uor_b200_gemm_splitk_nccl(comm.handle if isinstance(comm, NcclComm) else comm,
+                                           elem, out, ctypes.byref(A), ctypes.byref(B),
+                                           ctypes.byref(C), alpha, beta, ctypes.byref(call)),
+           "gemm_splitk_nccl")
+
+
+def gemm_tropical_splitk_nccl(comm, elem, out, a, av, b, bv, c, cv, alpha=(0, True),
+                              beta=(0, False), encode=NEAREST, ctx=None, route=None,
+                              asynchronous=False):
+    """The same for Trop<E>: max-plus keys, an NCCL all-reduce with MAX, MaxPlus::finish."""
+    if not _on_device(a, b, c):
+        raise UorError(INVALID_ARGUMENT, "gemm_tropical_splitk_nccl takes device buffers")
+    A, B, C = view(a, *av), view(b, *bv), view(c, *cv)
+    call = make_call(encode, True, ctx, route, asynchronous)
+    _check(lib().uor_b200_gemm_tropical_splitk_nccl(
+        comm.handle if isinstance(comm, NcclComm) else comm, elem, out, ctypes.byref(A),
+        ctypes.byref(B), ctypes.byref(C), Trop(alpha[0], int(alpha[1])),
+        Trop(beta[0], int(beta[1])), ctypes.byref(call)), "gemm_tropical_splitk_nccl")
 
 
 def _int64_len(limbs, count):
