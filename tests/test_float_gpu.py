@@ -252,7 +252,7 @@ def test_modular_route_two_reduction_chunks():
     b = (rng.standard_normal(k * n) * np.exp2(rng.integers(-4, 4, k * n))).astype(np.float32)
     got, want, route = run_both(U.F32, U.F32, a, b, m, k, n, 1, 0)
     assert np.array_equal(got, want)
-    assert route.moduli > 0 and route.k_chunks == 2
+    assert route.moduli > 0 and route.k_chunks >= 2
 
 
 @pytest.mark.parametrize("exp_range,moduli", [(8, (2, 28)), (40, (29, 32)), (50, (33, 40))])

@@ -89,7 +89,8 @@ def test_deep_i32_chunks_and_strides(digits):
                U.I128)
     assert i128_values(got) == i128_values(want)
     # byte slices: an s32 diagonal lane holds ~8 Ki products; residues: 1023 blocks of 128
-    assert route.k_chunks >= 3 if digits else (route.k_chunks == 1 and route.moduli > 0)
+    # hold k, and the few tiles split it further so the waves fill (ks_balance_chunks)
+    assert route.k_chunks >= 3 if digits else (route.k_chunks > 1 and route.moduli > 0)
 
 
 def test_modular_two_chunks_and_i64_extremes():
@@ -105,7 +106,7 @@ def test_modular_two_chunks_and_i64_extremes():
     oracle_int(a, (m, k, k, 1, 0), b, (k, n, n, 1, 0), want, (m, n, n, 1, 0), 1, 0, U.NEAREST,
                U.I128)
     assert i128_values(got) == i128_values(want)
-    assert route.k_chunks == 2 and route.moduli > 0
+    assert route.k_chunks >= 2 and route.moduli > 0
     m, k, n = 9, 3000, 11
     lo, hi = np.iinfo(np.int64).min, np.iinfo(np.int64).max
     a = rng.choice([lo, hi, lo + 1, -1, 0], size=m * k).astype(np.int64)

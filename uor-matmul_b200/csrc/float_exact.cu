@@ -1162,18 +1162,17 @@ __device__ __forceinline__ void fm_store_residues(int8_t* dst, int64_t plane, co
         for (int gi = 0; gi < 4; ++gi) {
             const int g = 4 * g4 + gi;
             if (g >= NM) break;
-            const uint32_t p = f.p[g], mg = f.magic32[g];
-            const uint64_t hm = f.hm[g];
+            const uint32_t half = f.half[g], pneg = f.pneg[g], mg = f.magic32[g], hneg = f.hneg[g];
             uint32_t word = 0;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 const uint32_t lo = gi == 0 ? cw[c].x : gi == 1 ? cw[c].y : gi == 2 ? cw[c].z : cw[c].w;
-                uint32_t v = __dp4a(lo32[c], lo, 0u);
+                uint32_t v = __dp4a(lo32[c], lo, half);  // v + half
                 if (W == 2) {
                     const uint32_t hi = gi == 0 ? ch[c].x : gi == 1 ? ch[c].y : gi == 2 ? ch[c].z : ch[c].w;
                     v = __dp4a(hi32[c], hi, v);
                 }
-                word = fm_put_byte(word, fm_balanced_v(v, p, mg, hm), c);
+                word = fm_put_byte(word, fm_balanced_vh(v, pneg, mg, hneg), c);
             }
             *reinterpret_cast<uint32_t*>(dst + g * plane) = word;
         }
@@ -2039,6 +2038,7 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
         q.n = (int)n;
         q.mp = (int)ks_rows_pad(m);
         q.np = (int)rup(n, KS_BN);
+        ks_balance_chunks(q, ctx->sm_count);
         q.status = ctx->d_status;
         q.budget_ns = ctx->budget_ns;
         const size_t kp = rup(k, 16);

@@ -250,6 +250,29 @@ cudaError_t ks_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const KSPa
     return cudaGetLastError();
 }
 
+void ks_balance_chunks(KSParams& p, int sm_count) {
+    const bool pair = p.m > 128;
+    const int tiles = (p.mp / (pair ? 256 : KS_BM)) * (p.np / KS_BN);
+    const int resident = pair ? ks_pair_max_clusters() : sm_count;
+    const int per_chunk = p.num_groups * tiles;
+    const int c0 = p.num_chunks;
+    int c_max = 8 * c0;
+    if (c_max > p.num_kb / 16) c_max = p.num_kb / 16;
+    if (per_chunk <= 0 || resident <= 0 || c_max <= c0) return;
+    auto fill = [&](int c) {
+        const long long units = static_cast<long long>(per_chunk) * c;
+        const long long waves = (units + resident - 1) / resident;
+        return static_cast<double>(units) / (static_cast<double>(waves) * resident);
+    };
+    if (fill(c0) >= 0.9) return;  // already nine tenths full: more partials only cost
+    int best = c0;
+    double best_fill = fill(c0);
+    for (int c = c0 + 1; c <= c_max; ++c)
+        if (fill(c) > best_fill + 1e-9) best_fill = fill(c), best = c;
+    p.kb_per_chunk = (p.num_kb + best - 1) / best;
+    p.num_chunks = (p.num_kb + p.kb_per_chunk - 1) / p.kb_per_chunk;
+}
+
 int ks_run(const void* as, int La, const void* bs, int Lb, size_t k, size_t kp, KSParams& p,
            int sm_count, cudaStream_t s, uint32_t* ctas) {
     const bool pair = p.m > 128;

@@ -119,6 +119,16 @@ cudaError_t ks_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const
                            const KSParams& p, cudaStream_t stream);
 int ks_pair_max_clusters();
 
+// More reduction chunks than the lane bound asks for when the work units (groups x
+// chunks x tiles) would leave the last wave over the resident CTAs (pairs) mostly empty:
+// a deep product of few tiles (configs[3]: 10 moduli x 16 tiles = 160 units on 74 pairs,
+// its third wave 16 % full) splits k further, each chunk's partial summed afterwards as
+// any chunk's is. Unless the waves are nine tenths full already: between p.num_chunks and
+// 8 x that, at least 16 k-blocks a chunk, the count with the fullest waves (the smallest
+// on ties). Needs p.num_kb, p.kb_per_chunk,
+// p.num_groups, p.m, p.mp, p.np; updates p.kb_per_chunk and p.num_chunks.
+void ks_balance_chunks(KSParams& p, int sm_count);
+
 // Runs the slice-pair product: `as` is the A stack [La][mp][kp] (mp = ks_rows_pad(m)),
 // `bs` the B stack [Lb][np][kp] (np a multiple of 256). p holds m, n, mp, np, the
 // groups (pair_begin, pair_a, pair_b, pair_sign), the chunking and the partial buffer;

@@ -303,11 +303,11 @@ __global__ void wide_reduce_kernel(const int32_t* __restrict__ part, int chunks,
 
 // Weights of an EB-byte integer's bytes modulo p_g. The value x is read as the unsigned
 // x + 2^(8 EB - 1) (its sign bit flipped), and bias folds the -2^(8 EB - 1) back in; the
-// balanced residue's shift half_g rides in the quotient (fm_balanced_v).
+// balanced residue's shift half_g rides in it too (fm_balanced_vh).
 struct WmWeights {
     uint32_t w0[FM_MAX];    // bytes i of 256^i mod p_g, i < 4
     uint32_t w1[FM_MAX];    // bytes i - 4 of 256^i mod p_g, 4 <= i < 8
-    uint32_t bias[FM_MAX];  // p_g - 2^(8 EB - 1) mod p_g
+    uint32_t bias[FM_MAX];  // (p_g - 2^(8 EB - 1) mod p_g) + half_g
 };
 
 template <int EB, int NM>
@@ -325,9 +325,9 @@ __device__ __forceinline__ void wm_store(int8_t* dst, int64_t plane, const uint6
         uint32_t word = 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            uint32_t v = __dp4a(lo[c], w.w0[g], w.bias[g]);
+            uint32_t v = __dp4a(lo[c], w.w0[g], w.bias[g]);  // the bias includes half_g
             if (EB == 8) v = __dp4a(hi[c], w.w1[g], v);
-            word = fm_put_byte(word, fm_balanced_v(v, f.p[g], f.magic32[g], f.hm[g]), c);
+            word = fm_put_byte(word, fm_balanced_vh(v, f.pneg[g], f.magic32[g], f.hneg[g]), c);
         }
         *reinterpret_cast<uint32_t*>(dst + g * plane) = word;
     }
@@ -596,6 +596,10 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
         q.kb_per_chunk = static_cast<int>(lane_m < num_kb ? lane_m : num_kb);
         q.num_chunks = (num_kb + q.kb_per_chunk - 1) / q.kb_per_chunk;
         q.num_kb = num_kb;
+        q.m = static_cast<int>(m);
+        q.mp = static_cast<int>(ks_rows_pad(m));
+        q.np = static_cast<int>(rup(n, KS_BN));
+        ks_balance_chunks(q, ctx->sm_count);
         if (q.num_chunks == 1)
             for (int g = 0; g < nm; ++g) q.res_inv[g] = fm.inv[g];
         q.m = static_cast<int>(m);
@@ -614,7 +618,7 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
             }
             uint32_t top = 1 % pg;  // 2^(8 eb - 1) mod p
             for (int i = 0; i < 8 * eb - 1; ++i) top = top * 2 % pg;
-            w.bias[g] = (pg - top) % pg;
+            w.bias[g] = (pg - top) % pg + fm.half[g];  // and the balanced residue's shift
         }
         const size_t kp = rup(k, 16);
         const size_t a_bytes = rup((size_t)nm * q.mp * kp, 256);

@@ -115,7 +115,8 @@ bool fm_plan_bound(const uint32_t* bound, int limbs, FmParams& f) {
         f.magic32[g] = static_cast<uint32_t>(((1ull << 32) + p - 1) / p);
         for (int b = 0; b < 4; ++b) f.mg[g / 4][b] |= ((f.magic32[g] >> (8 * b)) & 255u) << (8 * (g % 4));
         f.half[g] = p == 256 ? 127u : (p - 1) / 2;
-        f.hm[g] = static_cast<uint64_t>(f.half[g]) * f.magic32[g];
+        f.pneg[g] = 0u - p;
+        f.hneg[g] = 0u - f.half[g];
         for (int b = 0; b < nm; ++b) f.md[g / 4][b] |= byte_of(mg, b) << (8 * (g % 4));
     }
     return true;

@@ -30,7 +30,8 @@ struct FmParams {
     uint32_t magic32[FM_MAX];         // ceil(2^32 / p_g)
     uint32_t mg[FM_MAX / 4][4];       // [a][b]: byte b of ceil(2^32 / p_g) for g = 4a .. 4a + 3
     uint32_t half[FM_MAX];            // (p_g - 1) / 2, and 127 for 256
-    uint64_t hm[FM_MAX];              // half_g ceil(2^32 / p_g): the shift folded into a quotient
+    uint32_t pneg[FM_MAX];            // 2^32 - p_g
+    uint32_t hneg[FM_MAX];            // 2^32 - half_g
     uint32_t md[FM_MAX / 4][FM_MAX];  // [a][b]: byte b of M / p_g for g = 4a .. 4a + 3
     uint32_t mm[FM_MAX / 4 + 1];      // 32-bit limbs of M (M < 2^(8 nm))
     int32_t nmb[FM_MAX];              // -byte b of M
@@ -54,11 +55,12 @@ __device__ __forceinline__ uint32_t fm_mod24(uint32_t x, uint32_t p, uint32_t ma
 // The balanced residue of v < 2^24 - half (v - q p, q = floor((v + half) / p), half =
 // (p - 1) / 2 and 127 for 256) in its low byte: it lies in [-(p-1)/2, (p-1)/2] for odd p
 // and in [-127, 128] for 256, whose byte 128 is the int8 -128, the same residue modulo 256.
-// q comes from one widening multiply-add: (v ceil(2^32/p) + half ceil(2^32/p)) / 2^32 is
-// floor((v + half) / p) by fm_mod24's bound.
-__device__ __forceinline__ uint32_t fm_balanced_v(uint32_t v, uint32_t p, uint32_t magic32, uint64_t hm) {
-    const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(v) * magic32 + hm) >> 32);
-    return v - q * p;
+// It takes vh = v + half (the slicers' dp4a adds half through its accumulator), so
+// q = floor(vh / p) is one high multiply (fm_mod24's bound), and vh - q p - half is one
+// multiply-add and one add with the negated constants: single-word operations only.
+__device__ __forceinline__ uint32_t fm_balanced_vh(uint32_t vh, uint32_t pneg, uint32_t magic32,
+                                                   uint32_t hneg) {
+    return vh + __umulhi(vh, magic32) * pneg + hneg;
 }
 
 // word with its byte c replaced by the low byte of b (c = 0 .. 3, a compile-time constant).
