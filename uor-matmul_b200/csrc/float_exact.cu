@@ -1579,7 +1579,7 @@ __global__ void __launch_bounds__(FMT_THREADS, 1)
     fm_crt_tc_kernel(const __grid_constant__ CUtensorMap tmY, size_t total, int n,
                      const int* __restrict__ rlo, const int* __restrict__ clo,
                      const int* __restrict__ rspan, const int* __restrict__ cspan, FxEpi e,
-                     const __grid_constant__ FmParams f, int* status, uint64_t budget_ns) {
+                     FmParams f, int* status, uint64_t budget_ns) {
     using T = FmTc<NM>;
     constexpr int NB = FmColumns<NM>::value;
     constexpr int NL = FmLimbs<NM>::value;
@@ -1698,9 +1698,15 @@ __global__ void __launch_bounds__(FMT_THREADS, 1)
         const int group = (warp - 2) >> 2;
         const int quarter = warp & 3;  // the TMEM lane quarter this warp may read
         const int row = quarter * 32 + lane;
-        GridWalk wk(static_cast<size_t>(n), (blockIdx.x + static_cast<size_t>(group) * gridDim.x) * 128 + row,
-                    static_cast<size_t>(FMT_GROUPS) * gridDim.x * 128);
-        for (int b = group; b < nlocal; b += FMT_GROUPS, wk.next()) {
+        // The cells of this thread, first and stride below 2^31 (total is), walked in 32 bits.
+        const uint32_t un = static_cast<uint32_t>(n);
+        const uint32_t stride = static_cast<uint32_t>(FMT_GROUPS) * gridDim.x * 128;
+        uint32_t cell = (blockIdx.x + static_cast<uint32_t>(group) * gridDim.x) * 128 + row;
+        uint32_t ci = cell / un, cj = cell - ci * un;
+        const uint32_t si = stride / un, sj = stride - si * un;
+        // alpha 1, beta 0, nearest, f32 out: the window encode, the rest through fm_finish_cell
+        const bool fast32 = e.beta == 0 && e.alpha == 1 && e.mode == MODE_NEAREST && !e.out64;
+        for (int b = group; b < nlocal; b += FMT_GROUPS) {
             const int slot = b % T::SLOTS;
             if (!mbar_wait_warp_hint(tfull0 + 8 * slot, (b / T::SLOTS) & 1, budget_ns, status,
                                      KERR_TIMEOUT_EPILOGUE, FMT_HINT_NS))
@@ -1715,17 +1721,30 @@ __global__ void __launch_bounds__(FMT_THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty0 + 8 * slot);
-            if (wk.idx >= total) continue;
-            const int i = static_cast<int>(wk.i), j = static_cast<int>(wk.j);
-            const int64_t off = static_cast<int64_t>(i) * e.rsc + static_cast<int64_t>(j) * e.csc;
-            if (e.beta == 0 && (rspan[i] == 0 || cspan[j] == 0)) {
-                store_float(e.c, e.out64, off, 0);  // a row or column of zeros: S = 0
-                continue;
+            if (cell < total) {
+                const int64_t off = static_cast<int64_t>(ci) * e.rsc + static_cast<int64_t>(cj) * e.csc;
+                if (e.beta == 0 && (rspan[ci] == 0 || cspan[cj] == 0)) {
+                    store_float(e.c, e.out64, off, 0);  // a row or column of zeros: S = 0
+                } else {
+                    const uint32_t F[4] = {r[0], r[1], r[2], r[3]};
+                    uint32_t limb[NL];
+                    const uint32_t ext =
+                        fm_crt_limbs_signed<NM>(fm_crt_t(F), f, [&](int c) { return r[4 + c]; }, limb);
+                    const int ex = rlo[ci] + clo[cj];
+                    uint64_t bits;
+                    if (fast32 && fm_encode_f32_window<NL>(limb, ext, ex, e, bits))
+                        reinterpret_cast<uint32_t*>(e.c)[off] = static_cast<uint32_t>(bits);
+                    else
+                        fm_finish_cell<NM>(limb, ext, off, ex, 0, e);
+                }
             }
-            const uint32_t F[4] = {r[0], r[1], r[2], r[3]};
-            uint32_t limb[NL];
-            const uint32_t ext = fm_crt_limbs_signed<NM>(fm_crt_t(F), f, [&](int c) { return r[4 + c]; }, limb);
-            fm_finish_cell<NM>(limb, ext, off, rlo[i] + clo[j], 0, e);
+            cell += stride;
+            ci += si;
+            cj += sj;
+            if (cj >= un) {
+                cj -= un;
+                ++ci;
+            }
         }
     }
 
