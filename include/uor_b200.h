@@ -213,6 +213,39 @@ int uor_b200_gemm_ex_i8_i32(size_t m, size_t k, size_t n, int64_t alpha, const i
                             size_t lda, const int8_t *b, size_t ldb, int64_t beta, int32_t *c,
                             size_t ldc, const uor_b200_call *call);
 
+/* One symbol per (element, output) monomorphisation of gemm_auto (kernel.rs:523; the slice
+ * face's slice::gemm::<E, O>, slice.rs:184) with the raw face's conventions
+ * (raw::sgemm, crates/uor-matmul/src/raw.rs:45-64): a pointer names element (0,0), strides
+ * are element strides of either sign, m == 0 or n == 0 returns at once, and a view that
+ * cannot exist (an overflowing reach, or an output that maps two cells onto one) returns
+ * without writing (raw.rs:137-148). C := encode(alpha A B + beta C) as uor_b200_gemm.
+ * i128 outputs are 16-byte little-endian two's complement; i64 elements accumulate in
+ * Limbs<3> (acc.rs:215-402) and encode into i128. */
+int uor_b200_raw_gemm_i8_i32(size_t m, size_t k, size_t n, int64_t alpha, const int8_t *a,
+                             ptrdiff_t rsa, ptrdiff_t csa, const int8_t *b, ptrdiff_t rsb,
+                             ptrdiff_t csb, int64_t beta, int32_t *c, ptrdiff_t rsc, ptrdiff_t csc,
+                             const uor_b200_call *call);
+int uor_b200_raw_gemm_i8_i64(size_t m, size_t k, size_t n, int64_t alpha, const int8_t *a,
+                             ptrdiff_t rsa, ptrdiff_t csa, const int8_t *b, ptrdiff_t rsb,
+                             ptrdiff_t csb, int64_t beta, int64_t *c, ptrdiff_t rsc, ptrdiff_t csc,
+                             const uor_b200_call *call);
+int uor_b200_raw_gemm_i16_i64(size_t m, size_t k, size_t n, int64_t alpha, const int16_t *a,
+                              ptrdiff_t rsa, ptrdiff_t csa, const int16_t *b, ptrdiff_t rsb,
+                              ptrdiff_t csb, int64_t beta, int64_t *c, ptrdiff_t rsc,
+                              ptrdiff_t csc, const uor_b200_call *call);
+int uor_b200_raw_gemm_i32_i64(size_t m, size_t k, size_t n, int64_t alpha, const int32_t *a,
+                              ptrdiff_t rsa, ptrdiff_t csa, const int32_t *b, ptrdiff_t rsb,
+                              ptrdiff_t csb, int64_t beta, int64_t *c, ptrdiff_t rsc,
+                              ptrdiff_t csc, const uor_b200_call *call);
+int uor_b200_raw_gemm_i32_i128(size_t m, size_t k, size_t n, int64_t alpha, const int32_t *a,
+                               ptrdiff_t rsa, ptrdiff_t csa, const int32_t *b, ptrdiff_t rsb,
+                               ptrdiff_t csb, int64_t beta, void *c, ptrdiff_t rsc, ptrdiff_t csc,
+                               const uor_b200_call *call);
+int uor_b200_raw_gemm_i64_i128(size_t m, size_t k, size_t n, int64_t alpha, const int64_t *a,
+                               ptrdiff_t rsa, ptrdiff_t csa, const int64_t *b, ptrdiff_t rsb,
+                               ptrdiff_t csb, int64_t beta, void *c, ptrdiff_t rsc, ptrdiff_t csc,
+                               const uor_b200_call *call);
+
 /* driver::gemm (crates/uor-matmul-gemm/src/driver.rs:67-79) over Complex<elem>
  * (crates/uor-matmul-core/src/alphabet.rs:656-776), encoding into Complex<out>
  * componentwise (EncodeFrom<ComplexAcc>, alphabet.rs:765-776). elem in {I32, I64}
@@ -286,6 +319,14 @@ int uor_b200_gemm_tropical_selected(uor_b200_dtype elem, uor_b200_dtype out,
                                     uor_b200_trop alpha, uor_b200_trop beta,
                                     const uor_b200_call *call);
 
+/* uor_b200_gemm_tropical for Trop<i8> -> Trop<i32> with the raw face's
+ * conventions (see uor_b200_raw_gemm_i8_i32): a and b are Trop<i8> (2 bytes each), c is
+ * Trop<i32> (8 bytes), strides count those elements. */
+int uor_b200_raw_gemm_trop_i8_i32(size_t m, size_t k, size_t n, uor_b200_trop alpha,
+                                  const void *a, ptrdiff_t rsa, ptrdiff_t csa, const void *b,
+                                  ptrdiff_t rsb, ptrdiff_t csb, uor_b200_trop beta, void *c,
+                                  ptrdiff_t rsc, ptrdiff_t csc, const uor_b200_call *call);
+
 /* ----------------------------------------------------------- codec family */
 
 /* coded_gemm (crates/uor-matmul-gemm/src/coded.rs:98-142) with B a CodedMatrix
@@ -306,6 +347,21 @@ int uor_b200_tabulated_gemm(uor_b200_dtype out, const uor_b200_view *a, const ui
                             size_t codes_len, size_t k, size_t n, uint32_t per_byte,
                             const int8_t *table, size_t table_len, const uor_b200_view_mut *c,
                             int64_t alpha, int64_t beta, const uor_b200_call *call);
+
+/* coded_gemm / gemm_tabulated for Packed<Grid<16>, 2> into i32 with the raw
+ * face's conventions for A and C (see uor_b200_raw_gemm_i8_i32): codes are the whole
+ * CodedMatrix, k x n (coded: k * n / 2 bytes, row-major) or n x k (tabulated: n * k / 2
+ * bytes), table its 16 entries; n (coded) or k (tabulated) even. */
+int uor_b200_raw_coded_grid16_i8_i32(size_t m, size_t k, size_t n, int64_t alpha,
+                                     const int8_t *a, ptrdiff_t rsa, ptrdiff_t csa,
+                                     const uint8_t *codes, const int8_t *table, int64_t beta,
+                                     int32_t *c, ptrdiff_t rsc, ptrdiff_t csc,
+                                     const uor_b200_call *call);
+int uor_b200_raw_tabulated_grid16_i8_i32(size_t m, size_t k, size_t n, int64_t alpha,
+                                         const int8_t *a, ptrdiff_t rsa, ptrdiff_t csa,
+                                         const uint8_t *codes, const int8_t *table, int64_t beta,
+                                         int32_t *c, ptrdiff_t rsc, ptrdiff_t csc,
+                                         const uor_b200_call *call);
 
 /* The other fixed-width tiers (crates/uor-matmul-codec/src/codecs.rs) through one
  * descriptor, and Offset<C, zero> over any of them (decoded value minus zero, the image

@@ -130,6 +130,11 @@ def lib():
             "uor_b200_limbs_finish": ([I, I, P, Z, VP, L64, L64, CP], I),
             "uor_b200_trop_partial_keys": ([I, VP, VP, P, Z, CP], I),
             "uor_b200_trop_keys_finish": ([I, P, Z, VP, Trop, Trop, CP], I),
+            "uor_b200_raw_gemm_trop_i8_i32": ([Z, Z, Z, Trop, P, D, D, P, D, D, Trop, P, D, D, CP],
+                                              I),
+            "uor_b200_raw_coded_grid16_i8_i32": ([Z, Z, Z, L64, P, D, D, P, P, L64, P, D, D, CP], I),
+            "uor_b200_raw_tabulated_grid16_i8_i32": ([Z, Z, Z, L64, P, D, D, P, P, L64, P, D, D, CP],
+                                                     I),
             "uor_b200_gemm_splitk_nccl": ([P, I, I, VP, VP, VP, L64, L64, CP], I),
             "uor_b200_gemm_tropical_splitk_nccl": ([P, I, I, VP, VP, VP, Trop, Trop, CP], I),
             "uor_b200_nccl_unique_id": ([P, Z], I),
@@ -140,6 +145,8 @@ def lib():
             "uor_b200_selftest_wait_timeout": ([P, U64], I),
             "uor_b200_corpus_fill": ([U64, U32, Z, P], I),
         }
+        for pair in ("i8_i32", "i8_i64", "i16_i64", "i32_i64", "i32_i128", "i64_i128"):
+            sig["uor_b200_raw_gemm_" + pair] = ([Z, Z, Z, L64, P, D, D, P, D, D, L64, P, D, D, CP], I)
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
