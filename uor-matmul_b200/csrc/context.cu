@@ -246,6 +246,24 @@ bool self_aliases(size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs) {
     return (b / g) < rows && (a / g) < cols;
 }
 
+cudaStream_t ctx_fork(uor_b200_ctx* ctx) {
+    if (!ctx->side && (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess ||
+                       cudaEventCreateWithFlags(&ctx->fork_ev, cudaEventDisableTiming) != cudaSuccess ||
+                       cudaEventCreateWithFlags(&ctx->join_ev, cudaEventDisableTiming) != cudaSuccess)) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (cudaEventRecord(ctx->fork_ev, ctx->stream) != cudaSuccess ||
+        cudaStreamWaitEvent(ctx->side, ctx->fork_ev, 0) != cudaSuccess)
+        return nullptr;
+    return ctx->side;
+}
+
+bool ctx_join(uor_b200_ctx* ctx) {
+    return cudaEventRecord(ctx->join_ev, ctx->side) == cudaSuccess &&
+           cudaStreamWaitEvent(ctx->stream, ctx->join_ev, 0) == cudaSuccess;
+}
+
 }  // namespace uor
 
 // ------------------------------------------------------------------ C ABI
@@ -295,6 +313,9 @@ void uor_b200_ctx_destroy(uor_b200_ctx* ctx) {
         if (ctx->buf[i]) cudaFree(ctx->buf[i]);
     if (ctx->d_status) cudaFree(ctx->d_status);
     for (int i = 0; i < ctx->nevents; ++i) cudaEventDestroy(ctx->events[i]);
+    if (ctx->side) cudaStreamDestroy(ctx->side);
+    if (ctx->fork_ev) cudaEventDestroy(ctx->fork_ev);
+    if (ctx->join_ev) cudaEventDestroy(ctx->join_ev);
     if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
     if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);

@@ -1761,7 +1761,8 @@ template <int NM>
 static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, const uint8_t* a,
                              int64_t rsa, int64_t csa, const uint8_t* b, int64_t rsb, int64_t csb,
                              bool f64, int m, int k, int n, const int* rlo, const int* clo,
-                             const uint32_t* pw, int shmax, const FmParams& f, cudaStream_t s) {
+                             const uint32_t* pw, int shmax, const FmParams& f, cudaStream_t s,
+                             cudaStream_t side) {
     constexpr int NMP = (NM + 3) / 4 * 4;
     const size_t smem = static_cast<size_t>(shmax) * 2 * NMP * 4 * (f64 ? 2 : 1);
     // The B kernel adds a 25 KB static tile: allow the table's largest size beside it.
@@ -1778,7 +1779,9 @@ static void fm_launch_slices(int8_t* as, int mp, int8_t* bs, int np, int kp, con
     int gy = (kp + 63) / 64;
     const int gy_cap = 148 * 8 / gx > 1 ? 148 * 8 / gx : 1;
     if (gy > gy_cap) gy = gy_cap;
-    kb<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), dim3(32, 8), smem, s>>>(
+    // B's slicer beside A's on the side stream (both CUDA-core kernels, each short of warps
+    // to hide its latency alone), when there is one.
+    kb<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), dim3(32, 8), smem, side ? side : s>>>(
         bs, np, kp, b, rsb, csb, k, n, clo, pw, shmax, f);
 }
 
@@ -2106,16 +2109,18 @@ int run_float_gemm(uor_b200_ctx* ctx, bool e64, bool o64, const uint8_t* a, ptrd
             fx_flags_kernel<<<grid, 128, 0, s>>>(a, rsa, csa, b, rsb, csb, e64, (int)m, (int)k, (int)n,
                                                   rnf, cnf, flags);
         }
+        cudaStream_t side = ctx_fork(ctx);
         switch (nm) {
 #define FM_SLICES(N)                                                                            \
     case N:                                                                                     \
         fm_launch_slices<N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, e64, (int)m, \
-                            (int)k, (int)n, rlo, clo, pw, shmax, fm, s);                        \
+                            (int)k, (int)n, rlo, clo, pw, shmax, fm, s, side);                  \
         break;
             FM_EVEN_COUNTS(FM_SLICES)
 #undef FM_SLICES
         default: return UOR_B200_UNSUPPORTED;
         }
+        if (side && !ctx_join(ctx)) return UOR_B200_DEVICE_ERROR;
         if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
         q.residue = res;
         q.partial = nullptr;

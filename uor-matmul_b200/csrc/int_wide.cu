@@ -476,14 +476,15 @@ template <int EB, int NM>
 static void wm_launch(int8_t* as, int mp, int8_t* bs, int np, int kp, const uint8_t* a,
                       int64_t rsa, int64_t csa, const uint8_t* b, int64_t rsb, int64_t csb, int m,
                       int k, int n, bool cplx, const FmParams& f, const WmWeights& w,
-                      cudaStream_t s) {
+                      cudaStream_t s, cudaStream_t side) {
     const int64_t quads = static_cast<int64_t>(mp) * (kp / 4);
     const int grid = static_cast<int>(quads / 256 + 1 < 148 * 16 ? quads / 256 + 1 : 148 * 16);
     wm_slice_a_kernel<EB, NM><<<grid, 256, 0, s>>>(as, mp, kp, a, rsa, csa,
                                                    reinterpret_cast<uintptr_t>(a) % EB == 0, m, k,
                                                    cplx, f, w);
     const int gy = (kp + 127) / 128 < 65535 ? (kp + 127) / 128 : 65535;
-    wm_slice_b_kernel<EB, NM><<<dim3(np / 32, gy), dim3(32, 8), 0, s>>>(
+    // B's slicer beside A's on the side stream when there is one (both CUDA-core kernels).
+    wm_slice_b_kernel<EB, NM><<<dim3(np / 32, gy), dim3(32, 8), 0, side ? side : s>>>(
         bs, np, kp, b, rsb, csb, reinterpret_cast<uintptr_t>(b) % EB == 0, k, n, cplx, f, w);
 }
 
@@ -630,17 +631,19 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
         int8_t* as = reinterpret_cast<int8_t*>(ws);
         int8_t* bs = reinterpret_cast<int8_t*>(ws + a_bytes);
         uint8_t* res = ws + a_bytes + b_bytes;
+        cudaStream_t side = ctx_fork(ctx);
         switch (eb * 100 + nm) {
 #define WM_SLICE4(N) \
-    case 400 + N: wm_launch<4, N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, fm, w, s); break;
+    case 400 + N: wm_launch<4, N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, fm, w, s, side); break;
 #define WM_SLICE8(N) \
-    case 800 + N: wm_launch<8, N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, fm, w, s); break;
+    case 800 + N: wm_launch<8, N>(as, q.mp, bs, q.np, (int)kp, a, rsa, csa, b, rsb, csb, (int)m, (int)k, (int)n, cplx, fm, w, s, side); break;
             WM_COUNTS(WM_SLICE4)
             WM_COUNTS(WM_SLICE8)
 #undef WM_SLICE4
 #undef WM_SLICE8
         default: return UOR_B200_UNSUPPORTED;
         }
+        if (side && !ctx_join(ctx)) return UOR_B200_DEVICE_ERROR;
         if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
         q.residue = res;
         if (route) {

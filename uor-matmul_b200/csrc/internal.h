@@ -26,6 +26,10 @@ struct uor_b200_ctx {
     // Host-pointer pipelining: copy-in and copy-out streams and a pool of events,
     // created on first use.
     cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    // A side stream for work of one call that runs beside the call's stream, and the two
+    // events that fork it from and join it back into the call's stream.
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     cudaEvent_t events[256] = {};
     int nevents = 0;
 };
@@ -63,6 +67,14 @@ class DeviceTurn {
     uor_b200_ctx* ctx_;
     bool held_ = false;
 };
+
+// The side stream, made to wait for everything the context's stream has queued so far
+// (created on first use); nullptr when it cannot be had, and the caller then queues
+// everything on the context's stream. ctx_join makes the context's stream wait for the
+// side stream's work. Both record and wait on events only, so they also work while the
+// context's stream is being captured into a CUDA graph.
+cudaStream_t ctx_fork(uor_b200_ctx* ctx);
+bool ctx_join(uor_b200_ctx* ctx);
 
 // After device work: synchronise (unless async) and fold the status word in.
 int finish_call(uor_b200_ctx* ctx, const uor_b200_call* call);
