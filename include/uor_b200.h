@@ -480,7 +480,12 @@ int uor_b200_trop_keys_finish(uor_b200_dtype out, const int64_t *keys, size_t ke
  * Device pointers only (call->flags DEVICE_POINTERS); the communicator's device must be
  * the context's. NCCL is loaded on first use (libnccl.so.2, the one the process already
  * has if any); without it these return UOR_B200_NCCL_ERROR, as they do for an NCCL
- * failure. route, when given, reports the partial's kernel. */
+ * failure. route, when given, reports the partial's kernel. A rank whose own partial
+ * fails (an argument its peers did not share) still joins the all-reduce, so no peer
+ * waits on it, and returns that status; in a synchronous call every other rank then
+ * returns UOR_B200_NCCL_ERROR (its C is not the product). The checks before the exchange
+ * (communicator, device, m and n, the exchange buffer) fail on every rank alike when the
+ * ranks' calls agree in m, n and elem, as NCCL requires. */
 int uor_b200_gemm_splitk_nccl(void *comm, uor_b200_dtype elem, uor_b200_dtype out,
                               const uor_b200_view *a, const uor_b200_view *b,
                               const uor_b200_view_mut *c, int64_t alpha, int64_t beta,

@@ -233,6 +233,22 @@ def _abi_worker(rank, world, port):
                                     tb[2 * k0 * n:], (k1 - k0, n, n, 1), got, (m, n, n, 1),
                                     (3, True), (-5, True), ctx=ctx)
         assert torch.equal(got, want), rank
+        # a partial that fails on one rank only (its A one column short of B's rows): that
+        # rank still joins the exchange and reports its own status, the other learns of it
+        m2, k2, n2 = 16, 64, 24
+        a2, b2 = _operands(U.I32, m2, k2, n2)
+        c2 = torch.zeros(m2 * n2 * 2, dtype=torch.int64, device="cuda")
+        kk = k2 - 1 if rank == 1 else k2
+        with pytest.raises(U.UorError) as exc:
+            U.gemm_splitk_nccl(comm, U.I32, U.I128, a2, (m2, kk, k2, 1), b2, (k2, n2, n2, 1), c2,
+                               (m2, n2, n2, 1), ctx=ctx)
+        assert exc.value.status == (U.NONCONFORMANT if rank == 1 else U.NCCL_ERROR), rank
+        # and the communicator still serves the next call on both ranks
+        got = prior.clone()
+        U.gemm_tropical_splitk_nccl(comm, U.TROP_I8, U.TROP_I32, ta[2 * k0:], (m, k1 - k0, k, 1),
+                                    tb[2 * k0 * n:], (k1 - k0, n, n, 1), got, (m, n, n, 1),
+                                    (3, True), (-5, True), ctx=ctx)
+        assert torch.equal(got, want), rank
         # a communicator of another device is refused before any work
         with pytest.raises(U.UorError):
             other = U.Context(1 - rank)

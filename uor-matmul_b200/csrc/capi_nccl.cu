@@ -70,6 +70,31 @@ int all_reduce(uor_b200_ctx* ctx, void* comm, int64_t* buf, size_t count, ncclRe
     return cuda_status(cudaGetLastError());
 }
 
+// The exchange with a failure flag: buf holds `count` values and one more int64, 0 from a
+// rank whose partial succeeded and nonzero (bytes of 1) from one whose partial failed, so
+// that a rank that fails after the checks still joins the collective (its peers never wait
+// on it) and every rank learns of it. Sum and max both keep a nonzero flag nonzero.
+int exchange(uor_b200_ctx* ctx, void* comm, int64_t* buf, size_t count, ncclRedOp_t op, int partial_status) {
+    {
+        std::lock_guard<std::mutex> lock(ctx->mu);
+        const bool failed = partial_status != UOR_B200_OK;
+        if (cudaMemsetAsync(failed ? buf : buf + count, failed ? 1 : 0,
+                            (failed ? count + 1 : 1) * sizeof(int64_t), ctx->stream) != cudaSuccess)
+            return UOR_B200_DEVICE_ERROR;
+    }
+    return all_reduce(ctx, comm, buf, count + 1, op);
+}
+
+// After a synchronous call: whether any rank's partial failed.
+bool peer_failed(const int64_t* buf, size_t count) {
+    int64_t flag = 0;
+    if (cudaMemcpy(&flag, buf + count, sizeof(flag), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return true;
+    }
+    return flag != 0;
+}
+
 // The checks every entry point shares: NCCL present, a communicator of this context's
 // device, device pointers.
 int check_call(void* comm, const uor_b200_call* call, uor_b200_ctx** ctx_out) {
@@ -135,16 +160,20 @@ int uor_b200_gemm_splitk_nccl(void* comm, uor_b200_dtype elem, uor_b200_dtype ou
     if (a->rows != c->rows || b->cols != c->cols) return UOR_B200_NONCONFORMANT;
     const size_t count = SPLITK_LIMBS * a->rows * b->cols;
     if (count == 0) return UOR_B200_OK;
-    int64_t* limbs = exchange_buffer(ctx, count, &st);
+    int64_t* limbs = exchange_buffer(ctx, count + 1, &st);
     if (!limbs) return st;
     uor_b200_call step = *call;
     step.ctx = ctx;
     step.flags |= UOR_B200_ASYNC;  // the steps stay on the stream; the last one syncs as asked
-    if ((st = uor_b200_gemm_partial_limbs(elem, a, b, limbs, count, &step)) != UOR_B200_OK) return st;
-    if ((st = all_reduce(ctx, comm, limbs, count, ncclSum)) != UOR_B200_OK) return st;
+    const int partial = uor_b200_gemm_partial_limbs(elem, a, b, limbs, count, &step);
+    if ((st = exchange(ctx, comm, limbs, count, ncclSum, partial)) != UOR_B200_OK) return st;
+    if (partial != UOR_B200_OK) return partial;
     step.flags = call->flags;
     step.route = nullptr;  // the route reported is the partial's
-    return uor_b200_limbs_finish(elem, out, limbs, count, c, alpha, beta, &step);
+    if ((st = uor_b200_limbs_finish(elem, out, limbs, count, c, alpha, beta, &step)) != UOR_B200_OK)
+        return st;
+    return !(call->flags & UOR_B200_ASYNC) && peer_failed(limbs, count) ? UOR_B200_NCCL_ERROR
+                                                                             : UOR_B200_OK;
 }
 
 int uor_b200_gemm_tropical_splitk_nccl(void* comm, uor_b200_dtype elem, uor_b200_dtype out,
@@ -158,16 +187,20 @@ int uor_b200_gemm_tropical_splitk_nccl(void* comm, uor_b200_dtype elem, uor_b200
     if (a->rows != c->rows || b->cols != c->cols) return UOR_B200_NONCONFORMANT;
     const size_t count = a->rows * b->cols;
     if (count == 0) return UOR_B200_OK;
-    int64_t* keys = exchange_buffer(ctx, count, &st);
+    int64_t* keys = exchange_buffer(ctx, count + 1, &st);
     if (!keys) return st;
     uor_b200_call step = *call;
     step.ctx = ctx;
     step.flags |= UOR_B200_ASYNC;
-    if ((st = uor_b200_trop_partial_keys(elem, a, b, keys, count, &step)) != UOR_B200_OK) return st;
-    if ((st = all_reduce(ctx, comm, keys, count, ncclMax)) != UOR_B200_OK) return st;
+    const int partial = uor_b200_trop_partial_keys(elem, a, b, keys, count, &step);
+    if ((st = exchange(ctx, comm, keys, count, ncclMax, partial)) != UOR_B200_OK) return st;
+    if (partial != UOR_B200_OK) return partial;
     step.flags = call->flags;
     step.route = nullptr;
-    return uor_b200_trop_keys_finish(out, keys, count, c, alpha, beta, &step);
+    if ((st = uor_b200_trop_keys_finish(out, keys, count, c, alpha, beta, &step)) != UOR_B200_OK)
+        return st;
+    return !(call->flags & UOR_B200_ASYNC) && peer_failed(keys, count) ? UOR_B200_NCCL_ERROR
+                                                                            : UOR_B200_OK;
 }
 
 }  // extern "C"
