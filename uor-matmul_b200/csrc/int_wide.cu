@@ -472,6 +472,57 @@ __global__ void wm_crt_kernel(const uint8_t* __restrict__ res, int chunks, size_
     }
 }
 
+// The same for rows of a multiple of four cells, four cells per thread: one 32-bit load per
+// chunk and residue plane covers the four cells, and the chunks' residues are summed two
+// cells to a register in 16-bit lanes (bytes 0 and 2, bytes 1 and 3; at most 256 chunks
+// of residues below 256 keep each lane below 2^16).
+template <int NM>
+__global__ void __launch_bounds__(256) wm_crt4_kernel(const uint8_t* __restrict__ res, int chunks,
+                                                      size_t m, size_t n, void* c, int64_t rsc,
+                                                      int64_t csc, WideEpi e, FmParams f) {
+    constexpr int NL = FmLimbs<NM>::value;
+    const size_t total = m * n;
+    const size_t quads = total >> 2;
+    for (GridWalk wk(n >> 2); wk.idx < quads; wk.next()) {
+        const size_t idx0 = wk.idx * 4;
+        uint32_t ev[NM], od[NM];
+#pragma unroll
+        for (int g = 0; g < NM; ++g) ev[g] = od[g] = 0;
+        for (int q = 0; q < chunks; ++q) {
+#pragma unroll
+            for (int g = 0; g < NM; ++g) {
+                const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(
+                    res + (static_cast<size_t>(q) * NM + g) * total + idx0));
+                ev[g] += w & 0x00FF00FFu;
+                od[g] += (w >> 8) & 0x00FF00FFu;
+            }
+        }
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+            uint32_t y[NM];
+#pragma unroll
+            for (int g = 0; g < NM; ++g) {
+                const uint32_t sum = (cc & 1) ? od[g] : ev[g];
+                const uint32_t v = (cc >> 1) ? sum >> 16 : sum & 0xFFFFu;
+                // one chunk: the epilogue stored y_g itself; more: the summed residues
+                y[g] = chunks == 1 ? v
+                                   : fm_mod24(fm_mod24(v, f.p[g], f.magic32[g]) * f.inv[g], f.p[g],
+                                              f.magic32[g]);
+            }
+            uint32_t limb[NL];
+            const uint32_t ext = fm_crt<NM>(y, f, limb);
+            L3 acc;
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+                const uint64_t lo = 2 * q < NL ? limb[2 * q] : ext;
+                const uint64_t hi = 2 * q + 1 < NL ? limb[2 * q + 1] : ext;
+                acc.w[q] = lo | hi << 32;
+            }
+            wide_finish(e, acc, wk.i, wk.j * 4 + cc, c, rsc, csc);
+        }
+    }
+}
+
 template <int EB, int NM>
 static void wm_launch(int8_t* as, int mp, int8_t* bs, int np, int kp, const uint8_t* a,
                       int64_t rsa, int64_t csa, const uint8_t* b, int64_t rsb, int64_t csb, int m,
@@ -659,9 +710,15 @@ int run_wide_gemm(uor_b200_ctx* ctx, int eb, const uint8_t* a, ptrdiff_t rsa, pt
         const WideEpi we{epi, eb == 8 ? 1 : 0, cplx ? 1 : 0};
         const size_t total = m * n;
         const int rgrid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+        const bool quad = n % 4 == 0 && q.num_chunks <= 256;
+        const size_t qn = total / 4;
+        const int qgrid = (int)((qn + 255) / 256 < 148 * 16 ? (qn + 255) / 256 : 148 * 16);
         switch (nm) {
-#define WM_CRT(N) \
-    case N: wm_crt_kernel<N><<<rgrid, 256, 0, s>>>(res, q.num_chunks, m, n, c, rsc, csc, we, fm); break;
+#define WM_CRT(N)                                                                                   \
+    case N:                                                                                         \
+        if (quad) wm_crt4_kernel<N><<<qgrid, 256, 0, s>>>(res, q.num_chunks, m, n, c, rsc, csc, we, fm); \
+        else wm_crt_kernel<N><<<rgrid, 256, 0, s>>>(res, q.num_chunks, m, n, c, rsc, csc, we, fm);      \
+        break;
             WM_COUNTS(WM_CRT)
 #undef WM_CRT
         default: return UOR_B200_UNSUPPORTED;
