@@ -405,7 +405,9 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
 // half the issue slots per MAC. Both accumulators fill TMEM (half h in columns 256 h ..),
 // so there is no second buffer: the epilogue hands the halves back one at a time and the
 // MMA issuer starts the next tile's first-half MMAs as soon as half 0 is free, holding the
-// second-half MMAs of the stages it consumes until half 1 is free.
+// second-half MMAs of the stages it consumes until half 1 is free. The decoder warps work
+// in two groups of four on alternate stages: each stage's chain of waits, decode, proxy
+// fence, named barrier and relay is latency, not issue, and two chains in flight overlap.
 constexpr int KT_BM = 512;
 constexpr int KT_STAGES = 3;   // A/B ring: 2 x 16 KiB of A and 16 KiB of decoded B per CTA
 constexpr int KT_QSTAGES = 4;  // codes ring
@@ -461,7 +463,7 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         }
         for (int q = 0; q < KT_QSTAGES; ++q) {
             mbar_init(cfull0 + 8 * q, 1);
-            mbar_init(cempty0 + 8 * q, KC_DEC_WARPS);
+            mbar_init(cempty0 + 8 * q, KC_DEC_WARPS / 2);  // the decoder group of that stage
         }
         mbar_init(tfull, 1);
         mbar_init(tempty0, 8);  // 4 epilogue warps in each CTA of the pair
@@ -737,42 +739,50 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         int stage = 0, q = 0;
         uint32_t phase = 0, qph = 0;
         bool ok = true;
+        // Two groups of four warps take alternate stages, so that one group's wait, fence,
+        // barrier and relay overlap the other's decode.
+        constexpr int GW = KC_DEC_WARPS / 2;
+        const int group = dt / (32 * GW);
+        const int gt = dt - group * 32 * GW;
+        int it = 0;
         for (int t = cid; t < p.num_tiles && ok; t += ncl) {
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                const bool got =
-                    mbar_wait_warp(cfull0 + 8 * q, qph, p.budget_ns, p.status, KERR_TIMEOUT_MMA_FULL) &&
-                    mbar_wait_warp(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
-                                   KERR_TIMEOUT_MMA_FULL);
-                if (got) {
-                    uint8_t* sb = smem + stage * KT_STAGE_BYTES + 2 * KC_A_BYTES;
-                    const uint8_t* sq = codes + q * KC_C_BYTES;
-                    constexpr int REPS = (128 * 8) / (32 * KC_DEC_WARPS);
-                    uint2 cw[REPS];
+            for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                if ((it & 1) == group) {
+                    const bool got =
+                        mbar_wait_warp(cfull0 + 8 * q, qph, p.budget_ns, p.status, KERR_TIMEOUT_MMA_FULL) &&
+                        mbar_wait_warp(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
+                                       KERR_TIMEOUT_MMA_FULL);
+                    if (got) {
+                        uint8_t* sb = smem + stage * KT_STAGE_BYTES + 2 * KC_A_BYTES;
+                        const uint8_t* sq = codes + q * KC_C_BYTES;
+                        constexpr int REPS = (128 * 8) / (32 * GW);
+                        uint2 cw[REPS];
 #pragma unroll
-                    for (int rep = 0; rep < REPS; ++rep) {
-                        const int u = dt + rep * 32 * KC_DEC_WARPS;
-                        cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
-                    }
+                        for (int rep = 0; rep < REPS; ++rep) {
+                            const int u = gt + rep * 32 * GW;
+                            cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
+                        }
 #pragma unroll
-                    for (int rep = 0; rep < REPS; ++rep) {
-                        const int u = dt + rep * 32 * KC_DEC_WARPS;
-                        const int r = u >> 3, qq = u & 7;
-                        const uint2 e0 = dec8(cw[rep].x, t0, t1, t2, t3);
-                        const uint2 e1 = dec8(cw[rep].y, t0, t1, t2, t3);
-                        *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
-                            make_uint4(e0.x, e0.y, e1.x, e1.y);
+                        for (int rep = 0; rep < REPS; ++rep) {
+                            const int u = gt + rep * 32 * GW;
+                            const int r = u >> 3, qq = u & 7;
+                            const uint2 e0 = dec8(cw[rep].x, t0, t1, t2, t3);
+                            const uint2 e1 = dec8(cw[rep].y, t0, t1, t2, t3);
+                            *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                                make_uint4(e0.x, e0.y, e1.x, e1.y);
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(cempty0 + 8 * q);
                     }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(cempty0 + 8 * q);
+                    fence_proxy_async();
+                    if (!bar_and_all(1 + group, 32 * GW, got)) {
+                        ok = false;
+                        break;
+                    }
+                    if (gt == 0)
+                        bulk_copy_s2c(slot_leader + 2 * KC_RELAY * stage, relay_src, KC_RELAY,
+                                      full_leader + 8 * stage);
                 }
-                fence_proxy_async();
-                if (!bar_and_all(1, 32 * KC_DEC_WARPS, got)) {
-                    ok = false;
-                    break;
-                }
-                if (dt == 0)
-                    bulk_copy_s2c(slot_leader + 2 * KC_RELAY * stage, relay_src, KC_RELAY,
-                                  full_leader + 8 * stage);
                 if (++stage == KT_STAGES) stage = 0, phase ^= 1;
                 if (++q == KT_QSTAGES) q = 0, qph ^= 1;
             }
