@@ -740,7 +740,13 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         uint32_t phase = 0, qph = 0;
         bool ok = true;
         // Two groups of four warps take alternate stages, so that one group's wait, fence,
-        // barrier and relay overlap the other's decode.
+        // barrier and relay overlap the other's decode. Not more than two: the waits below
+        // are parity waits, which cannot tell a barrier one phase behind from one that has
+        // caught up. A group reaching iteration i has finished iteration i - 2, whose wait
+        // needed MMA i - 5; the MMAs commit in order, so MMA i - 6 (the last use of this
+        // iteration's stage) is done as well, and the parity can only mean the right phase.
+        // With four groups iteration i - 4 would imply only MMA i - 7. The codes ring is
+        // safe the same way: its four stages make each stage's previous use the same group's.
         constexpr int GW = KC_DEC_WARPS / 2;
         const int group = dt / (32 * GW);
         const int gt = dt - group * 32 * GW;
