@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         }
         for (int q = 0; q < KC_QSTAGES; ++q) {
             mbar_init(cfull0 + 8 * q, 1);
-            mbar_init(cempty0 + 8 * q, KC_DEC_WARPS);
+            mbar_init(cempty0 + 8 * q, KC_DEC_WARPS / 2);  // the decoder group of that step
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
@@ -338,51 +338,61 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         int stage = 0, q = 0;
         uint32_t phase = 0, qph = 0;
         bool ok = true;
+        // Two groups of four warps take alternate steps, so that one group's waits, fence,
+        // barrier and relay overlap the other's decode; two and not more, for the reason the
+        // tall kernel's decoders give (with five A/B stages and six codes stages a group's
+        // previous step still implies the use of its stage before the awaited one).
+        constexpr int GW = KC_DEC_WARPS / 2;
+        const int group = dt / (32 * GW);
+        const int gt = dt - group * 32 * GW;
+        int it = 0;
         for (int t = cid; t < p.num_tiles && ok; t += ncl) {
-            for (int kb = 0; kb < p.num_kb; ++kb) {
-                // this step's codes have landed and the MMA is done with the B slot
-                const bool got =
-                    mbar_wait_warp(cfull0 + 8 * q, qph, p.budget_ns, p.status, KERR_TIMEOUT_MMA_FULL) &&
-                    mbar_wait_warp(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
-                                   KERR_TIMEOUT_MMA_FULL);
-                if (got) {
-                    uint8_t* sb = smem + stage * KC_STAGE_BYTES + KC_A_BYTES;
-                    const uint8_t* sq = codes + q * KC_C_BYTES;
-                    // all of this thread's code words first (loads in flight together), then
-                    // the decodes and the swizzled stores: 128 code rows x 8 groups of 8 bytes,
-                    // each group one 16-byte unit of an operand row
-                    constexpr int REPS = (128 * 8) / (32 * KC_DEC_WARPS);
-                    uint2 cw[REPS];
+            for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+                if ((it & 1) == group) {
+                    // this step's codes have landed and the MMA is done with the B slot
+                    const bool got =
+                        mbar_wait_warp(cfull0 + 8 * q, qph, p.budget_ns, p.status, KERR_TIMEOUT_MMA_FULL) &&
+                        mbar_wait_warp(empty0 + 8 * stage, phase ^ 1, p.budget_ns, p.status,
+                                       KERR_TIMEOUT_MMA_FULL);
+                    if (got) {
+                        uint8_t* sb = smem + stage * KC_STAGE_BYTES + KC_A_BYTES;
+                        const uint8_t* sq = codes + q * KC_C_BYTES;
+                        // all of this thread's code words first (loads in flight together),
+                        // then the decodes and the swizzled stores: 128 code rows x 8 groups
+                        // of 8 bytes, each group one 16-byte unit of an operand row
+                        constexpr int REPS = (128 * 8) / (32 * GW);
+                        uint2 cw[REPS];
 #pragma unroll
-                    for (int rep = 0; rep < REPS; ++rep) {
-                        const int u = dt + rep * 32 * KC_DEC_WARPS;
-                        cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
-                    }
+                        for (int rep = 0; rep < REPS; ++rep) {
+                            const int u = gt + rep * 32 * GW;
+                            cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
+                        }
 #pragma unroll
-                    for (int rep = 0; rep < REPS; ++rep) {
-                        const int u = dt + rep * 32 * KC_DEC_WARPS;
-                        const int r = u >> 3, qq = u & 7;
-                        const uint2 d0 = dec8(cw[rep].x, t0, t1, t2, t3);
-                        const uint2 d1 = dec8(cw[rep].y, t0, t1, t2, t3);
-                        *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
-                            make_uint4(d0.x, d0.y, d1.x, d1.y);
+                        for (int rep = 0; rep < REPS; ++rep) {
+                            const int u = gt + rep * 32 * GW;
+                            const int r = u >> 3, qq = u & 7;
+                            const uint2 d0 = dec8(cw[rep].x, t0, t1, t2, t3);
+                            const uint2 d1 = dec8(cw[rep].y, t0, t1, t2, t3);
+                            *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                                make_uint4(d0.x, d0.y, d1.x, d1.y);
+                        }
+                        // the codes slot is decoded: hand it back to the codes producer
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(cempty0 + 8 * q);
                     }
-                    // the codes slot is decoded: hand it back to the codes producer
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(cempty0 + 8 * q);
+                    fence_proxy_async();  // the tensor core (async proxy) reads these bytes
+                    // every warp of the group is done with the step (or gave up: all of them
+                    // reach this barrier every step of the group and leave together, so none
+                    // waits on a warp that left); one thread signals the leader's full barrier
+                    // with a bulk copy (an async-proxy completion)
+                    if (!bar_and_all(1 + group, 32 * GW, got)) {
+                        ok = false;
+                        break;
+                    }
+                    if (gt == 0)
+                        bulk_copy_s2c(slot_leader + 2 * KC_RELAY * stage, relay_src, KC_RELAY,
+                                      full_leader + 8 * stage);
                 }
-                fence_proxy_async();  // the tensor core (async proxy) reads these bytes
-                // every decoder warp of this CTA is done with the step (or gave up: all of
-                // them reach this barrier every step and leave together, so none waits on a
-                // warp that left); one thread signals the leader's full barrier with a bulk
-                // copy (an async-proxy completion)
-                if (!bar_and_all(1, 32 * KC_DEC_WARPS, got)) {
-                    ok = false;
-                    break;
-                }
-                if (dt == 0)
-                    bulk_copy_s2c(slot_leader + 2 * KC_RELAY * stage, relay_src, KC_RELAY,
-                                  full_leader + 8 * stage);
                 if (++stage == KC_STAGES) stage = 0, phase ^= 1;
                 if (++q == KC_QSTAGES) q = 0, qph ^= 1;
             }
@@ -743,10 +753,11 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         // barrier and relay overlap the other's decode. Not more than two: the waits below
         // are parity waits, which cannot tell a barrier one phase behind from one that has
         // caught up. A group reaching iteration i has finished iteration i - 2, whose wait
-        // needed MMA i - 5; the MMAs commit in order, so MMA i - 6 (the last use of this
-        // iteration's stage) is done as well, and the parity can only mean the right phase.
-        // With four groups iteration i - 4 would imply only MMA i - 7. The codes ring is
-        // safe the same way: its four stages make each stage's previous use the same group's.
+        // needed MMA i - 5; the MMAs commit in order, so MMA i - 6 (the use of this
+        // iteration's stage before the one it waits for) is done as well, and the parity can
+        // only mean the right phase. With four groups iteration i - 4 would imply only MMA
+        // i - 7. The codes ring is safe the same way: an even number of codes stages makes
+        // each stage's previous use the same group's.
         constexpr int GW = KC_DEC_WARPS / 2;
         const int group = dt / (32 * GW);
         const int gt = dt - group * 32 * GW;
