@@ -134,11 +134,11 @@ typedef struct uor_b200_route {
  * product's bound, whatever the estimated cost. Exact; the same bytes. */
 #define UOR_B200_MODULAR 8u
 /* Codec tier (Packed<Grid<N>, 2>): decode the codes on chip only, never into a dense copy
- * of the coded operand in device memory. By default products of 512 activation rows and
- * more already decode on chip (K1's CTA-pair GEMM with the codes decoded straight into its
- * shared-memory B stages) when k is within one s32 lane (131071); the flag extends that to
- * 256-511 rows (256-row tiles) and keeps deeper reductions off the k x n workspace the
- * default would decode them into (the fused K5 kernel instead). The same bytes either way. */
+ * of the coded operand in device memory. Reductions within one s32 lane (131071) always
+ * decode on chip (K1's CTA-pair GEMM with the codes decoded straight into its shared-memory
+ * B stages); the flag keeps deeper reductions of 512 rows and more off the k x n workspace
+ * the default would decode them into (the fused K5 kernel instead). The same bytes either
+ * way. */
 #define UOR_B200_CODEC_ON_CHIP 16u
 
 /* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)

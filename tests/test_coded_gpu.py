@@ -1,9 +1,9 @@
-"""The codec tier against the oracle's coded_gemm / gemm_tabulated restatement: K5 (the
-codebook decode fused into the tensor-core pipeline, decoded weights on the M side) below
-512 activation rows; K1C (K1's CTA-pair pipeline with the codes decoded into its B stages,
-no dense copy anywhere) from 512 rows up with 512-row tiles, and with CODEC_ON_CHIP from
-256 rows with 256-row tiles; the one-pass decode followed by K1 for reductions deeper
-than one s32 lane."""
+"""The codec tier against the oracle's coded_gemm / gemm_tabulated restatement: K1C (K1's
+CTA-pair pipeline with the codes decoded into its B stages, no dense copy anywhere) for
+reductions within one s32 lane, with 512-row tiles from 512 activation rows up and 256-row
+tiles below; for deeper reductions, the one-pass decode followed by K1 from 512 rows up,
+and K5 (the codebook decode fused into the tensor-core pipeline, decoded weights on the M
+side) below 512 rows or with CODEC_ON_CHIP."""
 import numpy as np
 import pytest
 
@@ -75,12 +75,16 @@ def test_fused_nibbles(orientation, shape):
 
 @pytest.mark.parametrize("orientation", [0, 1])
 def test_default_many_rows_decode_on_chip(orientation):
-    """512 activation rows and more, by default: K1C with 512-row tiles, never a dense B."""
+    """By default, any row count: K1C, 512-row tiles from 512 rows and 256-row tiles below,
+    never a dense B."""
     for m, k, n, out, alpha, beta, N in [(512, 256, 96, U.I32, 1, 0, 16),
-                                         (1030, 96, 288, U.I8, -2, 5, 16)]:
+                                         (1030, 96, 288, U.I8, -2, 5, 16),
+                                         (40, 512, 160, U.I32, 1, 0, 16),
+                                         (300, 320, 64, U.I64, 3, -1, 9)]:
         got, want, route = run(m, k, n, 2, N, orientation, out, alpha, beta, seed=m + N)
         assert np.array_equal(got, want), (m, k, n, out)
-        assert route.kernel == 4 and route.b_layout != 3 and route.tile_m == 512
+        assert route.kernel == 4 and route.b_layout != 3
+        assert route.tile_m == (512 if m >= 512 else 256)
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
@@ -121,6 +125,16 @@ def test_decode_once_past_the_lane(orientation):
     got, want, route = run(m, k, n, 2, 16, orientation, U.I64, seed=5, on_chip=True)
     assert np.array_equal(got, want)
     assert route.kernel == 4 and route.b_layout != 3 and route.k_chunks == 2
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+def test_k5_deep_reductions_below_512_rows(orientation):
+    """Fewer than 512 activation rows and k past the s32 lane: K5's exact chunks (no
+    workspace), a ragged row count on its 128-column tiles."""
+    m, k, n = 70, 131_200, 64
+    got, want, route = run(m, k, n, 2, 16, orientation, U.I64, 3, -1, seed=6)
+    assert np.array_equal(got, want)
+    assert route.kernel == 4 and route.b_layout != 3 and route.k_chunks == 2 and route.tile_m == 128
 
 
 @pytest.mark.parametrize("orientation", [0, 1])

@@ -151,17 +151,17 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool fused = per_byte == 2 && table_len <= 16 && k > 0 &&
                        (orientation == 0 ? (n % 32 == 0) : (k % 32 == 0)) &&
                        (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
-    // From 512 activation rows up (k within one s32 lane), K1C with 512 x 256 tiles: K1's
-    // CTA-pair pipeline with the codes decoded into its B stages, each decoded stage feeding
-    // two M256 halves -- no dense B anywhere, and faster than decoding once into a workspace
-    // and running K1 (configs[1]: 0.114 against 0.117 ms). Deeper reductions with that many
-    // rows decode once into a k x n workspace and run K1 in exact chunks, unless
-    // UOR_B200_CODEC_ON_CHIP forbids the workspace (then K5). With the flag, 256 to 511 rows
-    // take K1C with 256 x 256 tiles; without it, and below 256 rows, K5.
+    // Reductions within one s32 lane: K1C, K1's CTA-pair pipeline with the codes decoded
+    // into its B stages -- no dense B anywhere -- with 512 x 256 tiles (each decoded stage
+    // feeding two M256 halves) from 512 activation rows up, 256 x 256 tiles below (faster
+    // than K5 at every row count: 0.043 against 0.064 ms at 32 x 8192 x 8192, 0.046 against
+    // 0.085 at 384 rows; configs[1] 0.099-0.104 ms against 0.117 for decode-once). Deeper
+    // reductions: from 512 rows decode once into a k x n workspace and run K1 in exact
+    // chunks, unless UOR_B200_CODEC_ON_CHIP forbids the workspace; below 512 rows, or with
+    // the flag, K5's chunks.
     const bool on_chip = call && (call->flags & UOR_B200_CODEC_ON_CHIP);
     const bool shallow = (int64_t)k <= K1_LANE_DEPTH;
-    const bool pair_fused = fused && shallow && (m >= 2 * (size_t)K5_BN ||
-                                                 (on_chip && m >= (size_t)K5_BN));
+    const bool pair_fused = fused && shallow;
     const bool decode_once = fused && !pair_fused && !on_chip && m >= 2 * (size_t)K5_BN;
     // The 16-entry effective table the fused decode uses: table[v % N]; a device table on
     // the decode-once route is read by the decode kernel itself (no host round trip).
