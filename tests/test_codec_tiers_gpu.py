@@ -1,6 +1,8 @@
 """The other fixed-width codec tiers -- Sign, Ternary, Book, and Offset over any tier --
 through uor_b200_codec_gemm, against the oracle's decode restatement and integer GEMM,
-bit for bit; and the reference's spelling equivalences CK-11 / CK-12."""
+bit for bit, on both routes (code bytes of 4 or 8 whole elements decoded on chip, the
+other shapes through a dense workspace); and the reference's spelling equivalences
+CK-11 / CK-12."""
 import numpy as np
 import pytest
 
@@ -88,6 +90,32 @@ def test_e8_codebook(orientation, cb):
     got, _ = check(m, k, n, U.TIER_BOOK, zeros, orientation, table=table, block=8,
                    code_bytes=cb, seed=40)
     assert not got.any()
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("m", [1, 130, 600])
+@pytest.mark.parametrize("tier,block,cb,N,zero", [
+    (U.TIER_SIGN, 8, 1, 0, 0), (U.TIER_SIGN, 16, 2, 0, -3),
+    (U.TIER_TERNARY, 4, 1, 0, 2), (U.TIER_TERNARY, 8, 2, 0, 0),
+    (U.TIER_BOOK, 8, 1, 256, 0), (U.TIER_BOOK, 8, 1, 100, 0), (U.TIER_BOOK, 4, 1, 256, -3)])
+def test_byte_codes_on_chip(orientation, m, tier, block, cb, N, zero):
+    """Code bytes of 8 (Sign, Book<N, 8> with u8 codes) or 4 (Ternary, Book<N, 4>) whole
+    elements decode inside the tensor-core pipeline through the byte table it builds
+    (route.b_layout 1 or 0, never the dense workspace 3): 256-row tiles below 512 rows,
+    512-row tiles from there, a reduction that is not a whole number of stages in
+    orientation 0 and output columns that are not a whole number of tiles in orientation 1;
+    Offset and the general epilogue (i64, alpha 3, beta -1) beside the plain s32 store."""
+    k, n = (200, 384) if orientation == 0 else (384, 200)
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    kw = dict(block=block, code_bytes=cb, zero=zero)
+    if tier == U.TIER_BOOK:
+        table = U.corpus(17 + N, U.CORPUS_I8, N * block)
+        kw["table"] = np.clip(table, -128 + max(zero, 0), 127 + min(zero, 0)).astype(np.int8)
+    codes = codes_for(rows, cols, block, cb, 31 + block + N)
+    out, alpha, beta = (U.I64, 3, -1) if zero else (U.I32, 1, 0)
+    _, route = check(m, k, n, tier, codes, orientation, out, alpha, beta, seed=m + block, **kw)
+    assert route.b_layout == (1 if orientation == 0 else 0)
+    assert route.tile_m == (512 if m >= 512 else 256)
 
 
 @pytest.mark.parametrize("P", [2, 4])

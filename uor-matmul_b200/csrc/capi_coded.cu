@@ -1,5 +1,6 @@
 // capi_coded.cu -- the codec tier's C ABI: coded_gemm (codes k x n) and the product
-// of gemm_tabulated (codes n x k), over Packed<Grid<N>, P> codes.
+// of gemm_tabulated (codes n x k), over Packed<Grid<N>, P> codes, and codec_gemm over the
+// fixed-width tiers (Sign, Ternary, Book, Offset).
 #include <algorithm>
 #include <climits>
 #include <cstdlib>
@@ -86,6 +87,74 @@ __global__ void decode_nibbles_kernel(int8_t* __restrict__ out, const uint8_t* _
         out[32 * groups + 2 * t] = static_cast<int8_t>(v.x & 0xFF);
         out[32 * groups + 2 * t + 1] = static_cast<int8_t>((v.x >> 8) & 0xFF);
     }
+}
+
+// K1C (gemm_coded_pair.cu) over device codes of p.epb elements per code byte, p's decode
+// fields set by the caller: the activations as K1's A (K-major rows, gathered if TMA cannot
+// read them as given), the codes map, 512 x 256 tiles from 512 activation rows up (each
+// decoded stage serving both halves) and 256 x 256 below; fills the route.
+int launch_k1c(uor_b200_ctx* ctx, K1CParams p, const Operand& A, const uint8_t* da,
+               const uint8_t* dcodes, size_t m, size_t k, size_t n, int orientation, int kind,
+               int64_t alpha, int64_t beta, const LinearEpi& epi, const Operand& C,
+               const OutStage& cs, uor_b200_route* route) {
+    cudaStream_t s = ctx->stream;
+    int st = UOR_B200_OK;
+    const uint8_t* xa = da;
+    uint64_t xstride = 0;
+    const size_t ldk = (k + 15) / 16 * 16;
+    const bool a_ok = (reinterpret_cast<uintptr_t>(da) & 15u) == 0 && (k == 1 || A.cs == 1) &&
+                      (m == 1 || (A.rs > 0 && (size_t)A.rs >= k && (A.rs & 15) == 0));
+    if (a_ok) {
+        xstride = m == 1 ? ldk : (uint64_t)A.rs;
+    } else {
+        uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, (m * ldk + 255) / 256 * 256, &st));
+        if (!ws) return st;
+        if (gather_2d(ws, ldk, da, m, k, A.rs, A.cs, 1, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+        xa = ws;
+        xstride = ldk;
+    }
+    const uint32_t epb = (uint32_t)p.epb;
+    CUtensorMap tmA, tmQ, tmO;
+    bool ok = make_tmap_u8(&tmA, xa, k, m, xstride, 128, 128);
+    if (orientation == 0)
+        ok = ok && make_tmap_u8(&tmQ, dcodes, n / epb, k, n / epb, 128 / epb, 128, false);
+    else
+        ok = ok && make_tmap_u8(&tmQ, dcodes, k / epb, n, k / epb, 128 / epb, 128, false);
+    if (!ok) return UOR_B200_DEVICE_ERROR;
+    p.m = (int)m;
+    p.n = (int)n;
+    p.k_begin = 0;
+    p.num_kb = (int)((k + K1_BK - 1) / K1_BK);
+    const bool tall = m >= 512;
+    p.tiles_m = (int)((m + (tall ? 511 : 255)) / (tall ? 512 : 256));
+    p.tiles_n = (int)((n + 255) / 256);
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
+    p.c = cs.dev_origin;
+    p.rsc = C.rs;
+    p.csc = C.cs;
+    p.epi = epi;
+    p.fast = kind == OUT_I32 && alpha == 1 && beta == 0 && C.cs == 1 &&
+             (m == 1 || (C.rs > 0 && (C.rs & 3) == 0 && (size_t)C.rs >= n)) &&
+             (reinterpret_cast<uintptr_t>(cs.dev_origin) & 15u) == 0;
+    p.tma_store = p.fast && make_tmap_s32(&tmO, cs.dev_origin, n, m,
+                                          (uint64_t)(m == 1 ? (n + 3) / 4 * 4 : (size_t)C.rs) * 4,
+                                          32, 32);
+    p.idesc = idesc_i8(256, 256, true, true, false, orientation == 0);
+    p.status = ctx->d_status;
+    p.budget_ns = ctx->budget_ns;
+    const int mc = k1c_max_clusters();
+    route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
+    route->tile_m = tall ? 512 : 256;
+    route->tile_n = 256;
+    route->tile_k = K1_BK;
+    route->k_chunks = 1;
+    route->ctas = (uint32_t)(2 * (p.num_tiles < mc ? p.num_tiles : mc));
+    route->pairs = 1;
+    route->a_layout = a_ok ? 0 : 2;
+    route->b_layout = orientation == 0 ? 1 : 0;  // decoded on chip, never materialised
+    if (k1c_launch(tmA, tmQ, tmO, orientation, tall, p, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    return UOR_B200_OK;
 }
 
 int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* codes,
@@ -201,23 +270,8 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
         route->b_layout = 3;  // decoded to a dense workspace first
     } else if (pair_fused) {
-        // Activations as K1's A: K-major rows, gathered if TMA cannot read them as given.
-        const uint8_t* xa = da;
-        uint64_t xstride = 0;
-        const size_t ldk = (k + 15) / 16 * 16;
-        const bool a_ok = (reinterpret_cast<uintptr_t>(da) & 15u) == 0 && (k == 1 || A.cs == 1) &&
-                          (m == 1 || (A.rs > 0 && (size_t)A.rs >= k && (A.rs & 15) == 0));
-        if (a_ok) {
-            xstride = m == 1 ? ldk : (uint64_t)A.rs;
-        } else {
-            uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, (m * ldk + 255) / 256 * 256, &st));
-            if (!ws) return st;
-            if (gather_2d(ws, ldk, da, m, k, A.rs, A.cs, 1, s) != cudaSuccess)
-                return UOR_B200_DEVICE_ERROR;
-            xa = ws;
-            xstride = ldk;
-        }
         K1CParams p{};
+        p.epb = 2;
         if (table_in_kernel) {
             p.dtable = table;  // the decoders read the device table themselves
             p.table_len = (int)table_len;
@@ -229,48 +283,9 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
                 p.table[w] = word;
             }
         }
-        CUtensorMap tmA, tmQ, tmO;
-        bool ok = make_tmap_u8(&tmA, xa, k, m, xstride, 128, 128);
-        if (orientation == 0)
-            ok = ok && make_tmap_u8(&tmQ, dcodes, n / 2, k, n / 2, 64, 128, false);
-        else
-            ok = ok && make_tmap_u8(&tmQ, dcodes, k / 2, n, k / 2, 64, 128, false);
-        if (!ok) return UOR_B200_DEVICE_ERROR;
-        p.m = (int)m;
-        p.n = (int)n;
-        p.k_begin = 0;
-        p.num_kb = (int)((k + K1_BK - 1) / K1_BK);
-        // 512-row tiles from two full row tiles up (each decoded stage serves both)
-        const bool tall = m >= 512;
-        p.tiles_m = (int)((m + (tall ? 511 : 255)) / (tall ? 512 : 256));
-        p.tiles_n = (int)((n + 255) / 256);
-        p.num_tiles = p.tiles_m * p.tiles_n;
-        p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
-        p.c = cs.dev_origin;
-        p.rsc = C.rs;
-        p.csc = C.cs;
-        p.epi = epi;
-        p.fast = kind == OUT_I32 && alpha == 1 && beta == 0 && C.cs == 1 &&
-                 (m == 1 || (C.rs > 0 && (C.rs & 3) == 0 && (size_t)C.rs >= n)) &&
-                 (reinterpret_cast<uintptr_t>(cs.dev_origin) & 15u) == 0;
-        p.tma_store = p.fast && make_tmap_s32(&tmO, cs.dev_origin, n, m,
-                                              (uint64_t)(m == 1 ? (n + 3) / 4 * 4 : (size_t)C.rs) * 4,
-                                              32, 32);
-        p.idesc = idesc_i8(256, 256, true, true, false, orientation == 0);
-        p.status = ctx->d_status;
-        p.budget_ns = ctx->budget_ns;
-        const int mc = k1c_max_clusters();
-        route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
-        route->tile_m = tall ? 512 : 256;
-        route->tile_n = 256;
-        route->tile_k = K1_BK;
-        route->k_chunks = 1;
-        route->ctas = (uint32_t)(2 * (p.num_tiles < mc ? p.num_tiles : mc));
-        route->pairs = 1;
-        route->a_layout = a_ok ? 0 : 2;
-        route->b_layout = orientation == 0 ? 1 : 0;  // decoded on chip, never materialised
-        if (k1c_launch(tmA, tmQ, tmO, orientation, tall, p, s) != cudaSuccess)
-            return UOR_B200_DEVICE_ERROR;
+        if ((st = launch_k1c(ctx, p, A, da, dcodes, m, k, n, orientation, kind, alpha, beta, epi, C,
+                             cs, route)))
+            return st;
     } else if (!fused) {
         // Off the fused path (P != 2, N > 16, or code rows the TMA cannot address):
         // decode to a dense row-major k x n int8 matrix in the auxiliary slot, then K1.
@@ -581,6 +596,41 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
         dcodes = d;
     }
     if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs))) return st;
+    const LinearEpi epi{alpha, beta, mode, kind};
+    // Code bytes of 4 or 8 whole elements each (Book with one-byte codes and blocks of 4 or
+    // 8, Sign with 8 elements per code byte, Ternary with 4) and a reduction within one s32
+    // lane: K1C decodes them through a 256-entry byte table it builds in shared memory, so
+    // no dense B exists anywhere. The code rows must be whole 16-byte TMA strides.
+    int epb = 0, btier = K1C_BOOK;
+    if (tier == UOR_B200_TIER_BOOK && cb == 1 && (blk == 4 || blk == 8)) epb = (int)blk;
+    else if (tier == UOR_B200_TIER_SIGN && blk == 8 * cb) epb = 8, btier = K1C_SIGN;
+    else if (tier == UOR_B200_TIER_TERNARY && blk == 4 * cb) epb = 4, btier = K1C_TERNARY;
+    const bool chip = epb != 0 && k > 0 && (int64_t)k <= K1_LANE_DEPTH && (cols / epb) % 16 == 0 &&
+                      (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
+    if (chip) {
+        K1CParams p{};
+        p.epb = epb;
+        p.byte_tier = btier;
+        p.zero = zero;
+        if (tier == UOR_B200_TIER_BOOK) {
+            p.book = reinterpret_cast<const int8_t*>(codec->table);  // read by the kernel
+            p.book_n = (int)N;
+            if (!dev) {
+                uint8_t* db = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, (tbytes + 255) / 256 * 256, &st));
+                if (!db) return st;
+                if (cudaMemcpyAsync(db, codec->table, tbytes, cudaMemcpyHostToDevice, s) != cudaSuccess)
+                    return UOR_B200_DEVICE_ERROR;
+                p.book = reinterpret_cast<const int8_t*>(db);
+            }
+        }
+        if ((st = launch_k1c(ctx, p, A, da, dcodes, m, k, n, (int)orientation, kind, alpha, beta, epi,
+                             C, cs, route)))
+            return st;
+        if (!dev && tbytes && (st = uor_b200_ctx_sync(ctx))) return st;  // the host book was read
+        if ((st = stage_out_end(ctx, cs))) return st;
+        if (!dev) return uor_b200_ctx_sync(ctx);
+        return finish_call(ctx, call);
+    }
     const size_t tb = (tbytes + 255) / 256 * 256;
     uint8_t* buf = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, tb + k * n + 256, &st));
     if (!buf) return st;
@@ -619,7 +669,6 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
                                                  (int)cb, zero, (int64_t)rows, (int64_t)cols);
         if (cudaGetLastError() != cudaSuccess) return UOR_B200_DEVICE_ERROR;
     }
-    const LinearEpi epi{alpha, beta, mode, kind};
     // B = dense (k x n row-major) or its transpose read K-major (dense n x k)
     const ptrdiff_t rsb = orientation == 0 ? (ptrdiff_t)n : 1;
     const ptrdiff_t csb = orientation == 0 ? 1 : (ptrdiff_t)k;

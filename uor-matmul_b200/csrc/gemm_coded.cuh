@@ -57,16 +57,30 @@ __device__ __forceinline__ uint2 dec8(uint32_t w, uint32_t t0, uint32_t t1, uint
 cudaError_t k5_launch(const CUtensorMap& tmX, const CUtensorMap& tmC, const K5Params& p, int grid,
                       cudaStream_t stream);
 
-// K1C: K1's CTA-pair GEMM (256 x 256 tiles, p.idesc M256 N256) with B decoded on chip from
-// nibble codes through the 16-entry table (4 words, table[v % N] for v in 0..15).
+// K1C: K1's CTA-pair GEMM (256 x 256 tiles, p.idesc M256 N256) with B decoded on chip.
+// Code bytes of p.epb elements each:
+//   2: Packed<Grid<N>, 2> nibbles through the 16-entry table (4 words, table[v % N] for v
+//      in 0..15, or read from dtable);
+//   4, 8: one code byte holds epb consecutive elements of a coded row, decoded through a
+//      256-entry table the kernel builds in shared memory from byte_tier: K1C_BOOK
+//      (book[(b % book_n) * epb + t], Book with one-byte codes and blocks of epb), K1C_SIGN
+//      (bit t: +1 set, -1 clear; Sign with blocks of 8 per code byte) or K1C_TERNARY
+//      (digit t = bits 2t..2t+1: 0 -> -1, 2 -> +1, 1 and 3 -> 0; Ternary with blocks of 4
+//      per code byte), every value minus zero.
+constexpr int K1C_BOOK = 0, K1C_SIGN = 1, K1C_TERNARY = 2;
 struct K1CParams : K1Params {
     uint32_t table[4];
     const int8_t* dtable;  // when set: the table in device memory, read by the kernel
     int table_len;         // its entries N (1..16)
+    int epb;               // elements per code byte: 2, 4 or 8
+    int byte_tier;         // epb 4 or 8: K1C_BOOK, K1C_SIGN or K1C_TERNARY
+    const int8_t* book;    // K1C_BOOK: the book in device memory, book_n x epb bytes
+    int book_n;
+    int zero;              // subtracted from every decoded value (Offset)
 };
 // tmA: activations K-major, dims {k, m}, box {128, 128}, 128-byte swizzle.
-// tmQ: codes, no swizzle, box {64 bytes, 128 rows}: orientation 0 dims {n/2, k},
-//      orientation 1 dims {k/2, n}. With p.tma_store, tmC is the s32 output map
+// tmQ: codes, no swizzle, box {128 / epb bytes, 128 rows}: orientation 0 dims {n/epb, k},
+//      orientation 1 dims {k/epb, n}. With p.tma_store, tmC is the s32 output map
 //      (dims {n, m}, box {32, 32}, 128-byte swizzle). k must not exceed K1_LANE_DEPTH.
 // tall: 512 x 256 tiles (p.tiles_m counts 512-row tiles), each decoded B stage feeding two
 // M256 halves; else 256 x 256.

@@ -23,6 +23,12 @@
 // row holds elements 2b (low nibble) and 2b + 1 (high nibble); 16-byte unit q of row r is
 // stored at r * 128 + ((q ^ (r & 7)) << 4).
 //
+// The fixed-width tiers whose code byte holds EPB = 4 or 8 whole elements (Sign, Ternary,
+// Book with one-byte codes: codecs.rs:362-660, matrix.rs:202-207) take the same pipeline
+// with 128 / EPB code bytes per row and stage: byte b of a row holds elements EPB b ..
+// EPB b + EPB - 1, expanded through a 256-entry table of EPB bytes per code byte that the
+// decoder warps build once in shared memory.
+//
 // Two rings. The A/B ring (KC_STAGES): TMA brings A; the decoders fill B. full[s]
 // (leader) counts both CTAs' A bytes and, as the sign that both CTAs' decoded halves are in
 // place, one 16-byte bulk copy from each CTA into the leader's shared memory, issued after
@@ -67,7 +73,52 @@ __device__ __forceinline__ void kc_tile(int t, const K1CParams& p, int& tm, int&
     tn = r / rows;
 }
 
-template <bool B_MN>
+// Byte tiers (EPB 4 or 8 elements per code byte): the decoded elements of every code byte
+// b, the first in the lowest byte, minus zero, as table[b * EPB + t]. Built once by the
+// decoder warps (dt = 0 .. 32 * KC_DEC_WARPS - 1), which then meet at named barrier 3.
+template <int EPB>
+__device__ void kc_build_byte_table(uint8_t* tab, const K1CParams& p, int dt) {
+    for (int e = dt; e < 256 * EPB; e += 32 * KC_DEC_WARPS) {
+        const int b = e / EPB, t = e % EPB;
+        int v;
+        if (p.byte_tier == K1C_BOOK) {
+            v = p.book[static_cast<int64_t>(b % p.book_n) * EPB + t];  // Book: table[code % N]
+        } else if (p.byte_tier == K1C_SIGN) {
+            v = (b >> t) & 1 ? 1 : -1;
+        } else {
+            const int d = (b >> (2 * t)) & 3;
+            v = d == 0 ? -1 : (d == 2 ? 1 : 0);
+        }
+        tab[e] = static_cast<uint8_t>(v - p.zero);
+    }
+    asm volatile("bar.sync 3, %0;" ::"r"(32 * KC_DEC_WARPS) : "memory");
+}
+
+// The code bytes of 16-byte unit u (operand row u / 8, column group u % 8) of a codes slot
+// holding 128 / EPB bytes per row.
+template <int EPB>
+__device__ __forceinline__ uint32_t kc_byte_codes(const uint8_t* sq, int u) {
+    constexpr int QROW = 128 / EPB;
+    if constexpr (EPB == 8)
+        return *reinterpret_cast<const uint16_t*>(sq + (u >> 3) * QROW + (u & 7) * 2);
+    else
+        return *reinterpret_cast<const uint32_t*>(sq + (u >> 3) * QROW + (u & 7) * 4);
+}
+
+// Those code bytes decoded: sixteen operand bytes.
+template <int EPB>
+__device__ __forceinline__ uint4 kc_byte_unit(uint32_t c, const uint8_t* tab) {
+    if constexpr (EPB == 8) {
+        const uint2* t8 = reinterpret_cast<const uint2*>(tab);
+        const uint2 e0 = t8[c & 255u], e1 = t8[(c >> 8) & 255u];
+        return make_uint4(e0.x, e0.y, e1.x, e1.y);
+    } else {
+        const uint32_t* t4 = reinterpret_cast<const uint32_t*>(tab);
+        return make_uint4(t4[c & 255u], t4[(c >> 8) & 255u], t4[(c >> 16) & 255u], t4[c >> 24]);
+    }
+}
+
+template <bool B_MN, int EPB>
 __global__ void __launch_bounds__(KC_THREADS, 1)
     k1c_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmC, const K1CParams p) {
@@ -182,13 +233,13 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                         break;
                     }
                     const uint32_t cb = cfull0 + 8 * q;
-                    mbar_expect_tx(cb, KC_C_BYTES);
+                    mbar_expect_tx(cb, 128 * (KC_BK / EPB));  // 128 rows of 128 / EPB code bytes
                     armed[q] = true;
                     armed_parity[q] = qph;
                     const uint32_t sq = smem_u32(codes + q * KC_C_BYTES);
                     const int kc = kb * KC_BK;
-                    if (B_MN) tma_load_2d(sq, &tmQ, cb, col0 / 2, kc, pol);
-                    else tma_load_2d(sq, &tmQ, cb, kc / 2, col0, pol);
+                    if (B_MN) tma_load_2d(sq, &tmQ, cb, col0 / EPB, kc, pol);
+                    else tma_load_2d(sq, &tmQ, cb, kc / EPB, col0, pol);
                     if (++q == KC_QSTAGES) q = 0, qph ^= 1;
                 }
             }
@@ -322,7 +373,11 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         // ------------------------------------------------------------ decoders (both CTAs)
         const int dt = threadIdx.x - KC_DEC_WARP0 * 32;  // 0 .. 32 * KC_DEC_WARPS - 1
         uint32_t tw[4] = {p.table[0], p.table[1], p.table[2], p.table[3]};
-        if (p.dtable) {
+        // byte tiers: the 256-entry table in the tail of codes slot 0 (TMA fills only the
+        // first 128 x 128 / EPB bytes of each slot)
+        uint8_t* const btab = codes + 128 * (KC_BK / EPB);
+        if constexpr (EPB != 2) kc_build_byte_table<EPB>(btab, p, dt);
+        if (EPB == 2 && p.dtable) {
             // the 16-entry table table[v % N], built from the device copy of the book
             for (int w = 0; w < 4; ++w) {
                 uint32_t word = 0;
@@ -361,6 +416,20 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                         // then the decodes and the swizzled stores: 128 code rows x 8 groups
                         // of 8 bytes, each group one 16-byte unit of an operand row
                         constexpr int REPS = (128 * 8) / (32 * GW);
+                        if constexpr (EPB != 2) {
+                            // byte tiers: each unit's code bytes, then the table lookups
+                            uint32_t cb8[REPS];
+#pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep)
+                                cb8[rep] = kc_byte_codes<EPB>(sq, gt + rep * 32 * GW);
+#pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep) {
+                                const int u = gt + rep * 32 * GW;
+                                const int r = u >> 3, qq = u & 7;
+                                *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                                    kc_byte_unit<EPB>(cb8[rep], btab);
+                            }
+                        } else {
                         uint2 cw[REPS];
 #pragma unroll
                         for (int rep = 0; rep < REPS; ++rep) {
@@ -375,6 +444,7 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                             const uint2 d1 = dec8(cw[rep].y, t0, t1, t2, t3);
                             *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
                                 make_uint4(d0.x, d0.y, d1.x, d1.y);
+                        }
                         }
                         // the codes slot is decoded: hand it back to the codes producer
                         __syncwarp();
@@ -438,7 +508,7 @@ __device__ __forceinline__ void kt_issue_half(uint32_t d, uint32_t sa, uint32_t 
     }
 }
 
-template <bool B_MN>
+template <bool B_MN, int EPB>
 __global__ void __launch_bounds__(KC_THREADS, 1)
     k1c_tall_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmC, const K1CParams p) {
@@ -552,13 +622,13 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                         break;
                     }
                     const uint32_t cb = cfull0 + 8 * q;
-                    mbar_expect_tx(cb, KC_C_BYTES);
+                    mbar_expect_tx(cb, 128 * (KC_BK / EPB));  // 128 rows of 128 / EPB code bytes
                     armed[q] = true;
                     armed_parity[q] = qph;
                     const uint32_t sq = smem_u32(codes + q * KC_C_BYTES);
                     const int kc = kb * KC_BK;
-                    if (B_MN) tma_load_2d(sq, &tmQ, cb, col0 / 2, kc, pol);
-                    else tma_load_2d(sq, &tmQ, cb, kc / 2, col0, pol);
+                    if (B_MN) tma_load_2d(sq, &tmQ, cb, col0 / EPB, kc, pol);
+                    else tma_load_2d(sq, &tmQ, cb, kc / EPB, col0, pol);
                     if (++q == KT_QSTAGES) q = 0, qph ^= 1;
                 }
             }
@@ -734,7 +804,11 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
         // ------------------------------------------------------------ decoders (both CTAs)
         const int dt = threadIdx.x - KC_DEC_WARP0 * 32;
         uint32_t tw[4] = {p.table[0], p.table[1], p.table[2], p.table[3]};
-        if (p.dtable) {
+        // byte tiers: the 256-entry table in the tail of codes slot 0 (TMA fills only the
+        // first 128 x 128 / EPB bytes of each slot)
+        uint8_t* const btab = codes + 128 * (KC_BK / EPB);
+        if constexpr (EPB != 2) kc_build_byte_table<EPB>(btab, p, dt);
+        if (EPB == 2 && p.dtable) {
             for (int w = 0; w < 4; ++w) {
                 uint32_t word = 0;
                 for (int b = 0; b < 4; ++b)
@@ -773,6 +847,20 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                         uint8_t* sb = smem + stage * KT_STAGE_BYTES + 2 * KC_A_BYTES;
                         const uint8_t* sq = codes + q * KC_C_BYTES;
                         constexpr int REPS = (128 * 8) / (32 * GW);
+                        if constexpr (EPB != 2) {
+                            // byte tiers: each unit's code bytes, then the table lookups
+                            uint32_t cb8[REPS];
+#pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep)
+                                cb8[rep] = kc_byte_codes<EPB>(sq, gt + rep * 32 * GW);
+#pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep) {
+                                const int u = gt + rep * 32 * GW;
+                                const int r = u >> 3, qq = u & 7;
+                                *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                                    kc_byte_unit<EPB>(cb8[rep], btab);
+                            }
+                        } else {
                         uint2 cw[REPS];
 #pragma unroll
                         for (int rep = 0; rep < REPS; ++rep) {
@@ -787,6 +875,7 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                             const uint2 e1 = dec8(cw[rep].y, t0, t1, t2, t3);
                             *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
                                 make_uint4(e0.x, e0.y, e1.x, e1.y);
+                        }
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(cempty0 + 8 * q);
@@ -815,10 +904,10 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
     }
 }
 
-template <bool B_MN, bool TALL>
+template <bool B_MN, bool TALL, int EPB>
 static cudaError_t kc_launch_t(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
                                const K1CParams& p, int max_clusters, cudaStream_t stream) {
-    auto kern = TALL ? k1c_tall_kernel<B_MN> : k1c_pair_kernel<B_MN>;
+    auto kern = TALL ? k1c_tall_kernel<B_MN, EPB> : k1c_pair_kernel<B_MN, EPB>;
     const int smem = TALL ? KT_SMEM_BYTES : KC_SMEM_BYTES;
     static bool attr_done[64] = {};
     int dev = 0;
@@ -849,7 +938,7 @@ int k1c_max_clusters() {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
-    auto kern = k1c_pair_kernel<true>;
+    auto kern = k1c_pair_kernel<true, 2>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KC_SMEM_BYTES);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 512, 1, 1);
@@ -873,14 +962,23 @@ int k1c_max_clusters() {
     return n;
 }
 
+template <int EPB>
+static cudaError_t kc_launch_e(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
+                               int orientation, bool tall, const K1CParams& p, int mc, cudaStream_t stream) {
+    if (tall)
+        return orientation == 0 ? kc_launch_t<true, true, EPB>(tmA, tmQ, tmC, p, mc, stream)
+                                : kc_launch_t<false, true, EPB>(tmA, tmQ, tmC, p, mc, stream);
+    return orientation == 0 ? kc_launch_t<true, false, EPB>(tmA, tmQ, tmC, p, mc, stream)
+                            : kc_launch_t<false, false, EPB>(tmA, tmQ, tmC, p, mc, stream);
+}
+
 cudaError_t k1c_launch(const CUtensorMap& tmA, const CUtensorMap& tmQ, const CUtensorMap& tmC,
                        int orientation, bool tall, const K1CParams& p, cudaStream_t stream) {
     const int mc = k1c_max_clusters();
-    if (tall)
-        return orientation == 0 ? kc_launch_t<true, true>(tmA, tmQ, tmC, p, mc, stream)
-                                : kc_launch_t<false, true>(tmA, tmQ, tmC, p, mc, stream);
-    return orientation == 0 ? kc_launch_t<true, false>(tmA, tmQ, tmC, p, mc, stream)
-                            : kc_launch_t<false, false>(tmA, tmQ, tmC, p, mc, stream);
+    if (p.epb == 8) return kc_launch_e<8>(tmA, tmQ, tmC, orientation, tall, p, mc, stream);
+    if (p.epb == 4) return kc_launch_e<4>(tmA, tmQ, tmC, orientation, tall, p, mc, stream);
+    if (p.epb == 2) return kc_launch_e<2>(tmA, tmQ, tmC, orientation, tall, p, mc, stream);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace uor
