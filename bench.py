@@ -487,12 +487,14 @@ def wl_codec_e8(args, U, torch, rank, sets=3):
     w.l2 = f"{sets} rotating operand sets + 64 MiB output"
     w.algorithmic_bytes = m * k + k * n // 8 + 4 * m * n
     w.flush = False
+    w.traffic = load_traffic("k1c_e8_book_on_chip_2048x8192x8192_traffic.json", "bytes_per_call")
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
         ach = w.units / (avg_ms / 1e3) / 1e12
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
-                "frac": ach / peak, "peak_source": src, "traffic": None,
+                "frac": ach / peak, "peak_source": src, "traffic": w.traffic,
+                "traffic_scope": "whole call (K1C), one ncu capture" if w.traffic else None,
                 "basis": "2mnk int8 ops over the whole call (one K1C launch, the book decoded on chip)",
                 "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
