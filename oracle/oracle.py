@@ -195,6 +195,31 @@ def decode_codec(tier, codes, rows, cols, table=None, per_byte=0, block=1, code_
     return (out - zero).astype(np.int8)
 
 
+def decode_codec_np(tier, codes, rows, cols, table=None, block=1, code_bytes=1, zero=0):
+    """decode_codec's fixed-width tiers (Sign, Ternary, Book, Offset) as whole-array numpy
+    steps, for full-size cases: the same CodedMatrix::at indexing and per-tier rules
+    (matrix.rs:202-207, codecs.rs:306-308, :386-400, :480-496), checked against the
+    element loops above on the CPU."""
+    codes = np.asarray(codes, np.uint8)
+    cpr = cols // block
+    raw = codes[: rows * cpr * code_bytes].reshape(rows, cpr, code_bytes).astype(np.int64)
+    code = raw[..., 0] | (raw[..., 1] << 8) if code_bytes == 2 else raw[..., 0]
+    t = np.arange(block, dtype=np.int64)
+    width = 8 * code_bytes
+    if tier == 1:
+        bit = (code[..., None] >> np.minimum(t, 63)) & 1
+        out = np.where((t < width) & (bit == 1), 1, -1)
+    elif tier == 2:
+        d = np.where(2 * t < width, (code[..., None] >> np.minimum(2 * t, 63)) & 3, 0)
+        out = np.where(d == 0, -1, np.where(d == 2, 1, 0))
+    elif tier == 3:
+        tab = np.asarray(table, np.int64).reshape(-1, block)
+        out = tab[code % tab.shape[0]]
+    else:
+        raise ValueError("decode_codec_np covers tiers 1-3")
+    return (out.reshape(rows, cols) - zero).astype(np.int8)
+
+
 def decode_arena(table, codes, rows, cols, code_bytes=1):
     """Arena::decode_element (codecs.rs:961-965) over a CodedMatrix of one-element blocks:
     element (r, c) is table[code % N] with code the (r * cols + c)-th u8 or little-endian

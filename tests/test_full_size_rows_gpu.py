@@ -109,6 +109,34 @@ def test_codec_config2_row_blocks(on_chip):
         assert np.array_equal(c[r0 * n:r1 * n], want), (r0, r1)
 
 
+@pytest.mark.parametrize("tier,block,orientation", [(U.TIER_BOOK, 8, 0), (U.TIER_TERNARY, 4, 1)])
+def test_byte_codec_tiers_full_size_row_blocks(tier, block, orientation):
+    """configs[1]'s shape over codec tiers whose code byte holds whole elements, decoded on
+    chip through K1C's byte table: the E8 book (Book<256, 8>, u8 codes, the bench's
+    codec-e8 line) with codes k x n, and Ternary<4> with codes n x k (gemm_tabulated's
+    layout)."""
+    m, k, n = 2048, 8192, 8192
+    a = U.corpus(1, U.CORPUS_I8, m * k)
+    q = U.corpus(3, U.CORPUS_RAW, k * n // block).astype(np.uint8)
+    table = U.e8_table() if tier == U.TIER_BOOK else None
+    kw = {"table": torch.from_numpy(table).cuda()} if table is not None else {}
+    tc = torch.empty(m * n, dtype=torch.int32, device="cuda")
+    route = U.Route()
+    U.codec_gemm(U.I32, torch.from_numpy(a).cuda(), (m, k, k, 1), tier, torch.from_numpy(q).cuda(),
+                 k, n, tc, (m, n, n, 1), block=block, code_bytes=1, orientation=orientation,
+                 route=route, **kw)
+    assert route.b_layout == (1 if orientation == 0 else 0) and route.tile_m == 512
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    dense = orc.decode_codec_np(tier, q, rows, cols, table, block).reshape(-1)
+    bv = View(dense, k, n, n, 1) if orientation == 0 else View(dense, k, n, 1, k)
+    c = tc.cpu().numpy()
+    for r0, r1 in row_blocks(m):
+        want = np.zeros((r1 - r0) * n, np.int32)
+        orc.gemm_int(View(a, r1 - r0, k, k, 1, r0 * k), bv, View(want, r1 - r0, n, n, 1),
+                     threads=THREADS)
+        assert np.array_equal(c[r0 * n:r1 * n], want), (r0, r1)
+
+
 def test_tropical_config5_8192_cubed_row_blocks():
     """configs[4]'s max-plus half at its full size: Trop<i8> in [-64, 63] with 5 % -inf,
     Trop<i32> out; the value is compared where the cell is finite, the flag everywhere."""

@@ -366,6 +366,26 @@ def test_codec_tier_decode_restatement():
                per_byte=2, zero=3).tolist() == [[-2, -1]]
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_codec_decode_numpy_twin_matches_loops(seed):
+    """decode_codec_np (whole-array numpy, for full-size cases) against the element loops,
+    on random shapes of every fixed-width tier, u8 and u16 codes, widths past the code's
+    bits, and Offset."""
+    rng = np.random.default_rng(200 + seed)
+    for tier in (1, 2, 3):
+        for cb in (1, 2):
+            block = int(rng.integers(1, 21))
+            rows, cpr = int(rng.integers(1, 6)), int(rng.integers(1, 5))
+            cols = cpr * block
+            codes = rng.integers(0, 256, size=rows * cpr * cb).astype(np.uint8)
+            table = (rng.integers(-100, 100, size=int(rng.integers(1, 40)) * block)
+                     .astype(np.int8) if tier == 3 else None)
+            zero = int(rng.integers(-3, 4))
+            want = orc.decode_codec(tier, codes, rows, cols, table, 0, block, cb, zero)
+            got = orc.decode_codec_np(tier, codes, rows, cols, table, block, cb, zero)
+            assert np.array_equal(got, want), (tier, cb, block)
+
+
 def test_complex_mac_kat():
     """complex_mac_is_componentwise_ck_01 (alphabet.rs:824-833): (3 + 4i)(5 - 2i) = 23 + 14i."""
     a, b = np.array([3, 4], np.int32), np.array([5, -2], np.int32)
