@@ -1,9 +1,10 @@
 """The codec tier against the oracle's coded_gemm / gemm_tabulated restatement: K1C (K1's
 CTA-pair pipeline with the codes decoded into its B stages, no dense copy anywhere) for
 reductions within one s32 lane, with 512-row tiles from 512 activation rows up and 256-row
-tiles below; for deeper reductions, the one-pass decode followed by K1 from 512 rows up,
-and K5 (the codebook decode fused into the tensor-core pipeline, decoded weights on the M
-side) below 512 rows or with CODEC_ON_CHIP."""
+tiles below -- nibbles through the register table, 2- and 1-bit sub-codes through a byte
+table built on chip; for deeper nibble reductions, the one-pass decode followed by K1 from
+512 rows up, and K5 (the codebook decode fused into the tensor-core pipeline, decoded
+weights on the M side) below 512 rows or with CODEC_ON_CHIP."""
 import numpy as np
 import pytest
 
@@ -167,6 +168,40 @@ def test_short_table_alpha_beta_outputs(orientation, m):
         for alpha, beta, mode in [(3, -1, U.NEAREST), (-(2**63), 2**62, U.WRAPPING)]:
             got, want, _ = run(m, 96, 64, 2, 7, orientation, out, alpha, beta, mode, seed=out)
             assert (got == want) if out == U.I128 else np.array_equal(got, want), (out, alpha)
+
+
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("P,N", [(4, 4), (4, 3), (8, 2), (8, 200)])
+@pytest.mark.parametrize("m", [70, 520])
+def test_quarter_and_bit_packings_on_chip(P, N, orientation, m):
+    """Packed<Grid<N>, 4> and <N, 8> (2- and 1-bit sub-codes, table[sub % N]) decode inside
+    K1C through the byte table its decoders build from the N-entry table: route.b_layout
+    1 or 0, 256- or 512-row tiles, a reduction that is not a whole number of stages; the
+    general epilogue (i64, alpha 3, beta -1) beside the s32 store."""
+    k, n = (200, 256) if orientation == 0 else (256, 200)
+    for out, alpha, beta in ((U.I32, 1, 0), (U.I64, 3, -1)):
+        got, want, route = run(m, k, n, P, N, orientation, out, alpha, beta, seed=P * 7 + N + m)
+        assert np.array_equal(got, want), (out, alpha)
+        assert route.kernel == 4 and route.b_layout == (1 if orientation == 0 else 0)
+        assert route.tile_m == (512 if m >= 512 else 256)
+
+
+@pytest.mark.parametrize("P", [4, 8])
+def test_quarter_and_bit_packings_device_table(P):
+    """Device pointers and a device table read by K1C's decoders themselves."""
+    m, k, n, N = 300, 128, 384, 3
+    rng = np.random.default_rng(90 + P)
+    a = rng.integers(-128, 128, size=m * k).astype(np.int8)
+    codes = make_codes(rng, k, n, P)
+    table = rng.integers(-128, 128, size=N).astype(np.int8)
+    want = np.zeros(m * n, np.int32)
+    orc.coded_gemm(orc.View(a, m, k, k, 1), codes, P, table, orc.View(want, m, n, n, 1), k, n, 0)
+    tc = torch.zeros(m * n, dtype=torch.int32, device="cuda")
+    route = U.Route()
+    U.coded_gemm(U.I32, torch.from_numpy(a).cuda(), (m, k, k, 1), torch.from_numpy(codes).cuda(),
+                 k, n, P, torch.from_numpy(table).cuda(), tc, (m, n, n, 1), route=route)
+    assert np.array_equal(tc.cpu().numpy(), want)
+    assert route.kernel == 4 and route.b_layout == 1
 
 
 @pytest.mark.parametrize("P,N", [(1, 200), (4, 4), (8, 2), (2, 16)])

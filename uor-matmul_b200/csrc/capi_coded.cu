@@ -20,7 +20,8 @@ using namespace uor;
 namespace {
 
 // Decode a Packed<Grid<N>, P> coded matrix to a dense row-major int8 k x n matrix
-// (used only off the fused path: P != 2, N > 16, or rows the TMA cannot read).
+// (used only off the on-chip paths: P = 1, N > 16 with P = 2, P = 4 or 8 past one s32
+// lane, or code rows the TMA cannot read).
 __global__ void decode_dense_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
                                     const int8_t* __restrict__ table, int N, int P,
                                     int orientation, int k, int n) {
@@ -232,9 +233,16 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool shallow = (int64_t)k <= K1_LANE_DEPTH;
     const bool pair_fused = fused && shallow;
     const bool decode_once = fused && !pair_fused && !on_chip && m >= 2 * (size_t)K5_BN;
+    // Four or eight sub-codes per byte (Packed<Grid<N>, 4 | 8>) within one s32 lane: K1C
+    // with the byte table built on chip from the N-entry table (code rows whole 16-byte
+    // TMA strides).
+    const size_t code_cols = orientation == 0 ? n : k;
+    const bool byte_fused = (per_byte == 4 || per_byte == 8) && k > 0 && shallow &&
+                            (code_cols / per_byte) % 16 == 0 &&
+                            (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
     // The 16-entry effective table the fused decode uses: table[v % N]; a device table on
     // the decode-once route is read by the decode kernel itself (no host round trip).
-    const bool table_in_kernel = (decode_once || pair_fused) && dev && !table_on_host;
+    const bool table_in_kernel = (decode_once || pair_fused || byte_fused) && dev && !table_on_host;
     int8_t tab[256];
     const size_t tl = table_len < 256 ? table_len : 256;
     if (dev && !table_on_host) {
@@ -286,9 +294,27 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         if ((st = launch_k1c(ctx, p, A, da, dcodes, m, k, n, orientation, kind, alpha, beta, epi, C,
                              cs, route)))
             return st;
+    } else if (byte_fused) {
+        K1CParams p{};
+        p.epb = (int)per_byte;
+        p.byte_tier = K1C_GRID;
+        p.book_n = (int)table_len;
+        if (table_in_kernel) {
+            p.book = table;
+        } else {
+            // the first min(N, 256) entries: every sub-code is below 256
+            int8_t* dt = static_cast<int8_t*>(ctx_buffer(ctx, SLOT_AUX, 256, &st));
+            if (!dt) return st;
+            if (cudaMemcpyAsync(dt, tab, tl, cudaMemcpyHostToDevice, s) != cudaSuccess)
+                return UOR_B200_DEVICE_ERROR;
+            p.book = dt;
+        }
+        if ((st = launch_k1c(ctx, p, A, da, dcodes, m, k, n, orientation, kind, alpha, beta, epi, C,
+                             cs, route)))
+            return st;
     } else if (!fused) {
-        // Off the fused path (P != 2, N > 16, or code rows the TMA cannot address):
-        // decode to a dense row-major k x n int8 matrix in the auxiliary slot, then K1.
+        // Off the on-chip paths (see decode_dense_kernel): decode to a dense row-major
+        // k x n int8 matrix in the auxiliary slot, then K1.
         uint8_t* buf = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, 256 + k * n, &st));
         if (!buf) return st;
         int8_t* dtable = reinterpret_cast<int8_t*>(buf);

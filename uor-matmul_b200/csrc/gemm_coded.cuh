@@ -66,15 +66,17 @@ cudaError_t k5_launch(const CUtensorMap& tmX, const CUtensorMap& tmC, const K5Pa
 //      (book[(b % book_n) * epb + t], Book with one-byte codes and blocks of epb), K1C_SIGN
 //      (bit t: +1 set, -1 clear; Sign with blocks of 8 per code byte) or K1C_TERNARY
 //      (digit t = bits 2t..2t+1: 0 -> -1, 2 -> +1, 1 and 3 -> 0; Ternary with blocks of 4
-//      per code byte), every value minus zero.
-constexpr int K1C_BOOK = 0, K1C_SIGN = 1, K1C_TERNARY = 2;
+//      per code byte), K1C_GRID (Packed<Grid<N>, epb>: book[sub-code t % book_n], the
+//      sub-codes 8 / epb bits wide, low first), every value minus zero.
+constexpr int K1C_BOOK = 0, K1C_SIGN = 1, K1C_TERNARY = 2, K1C_GRID = 3;
 struct K1CParams : K1Params {
     uint32_t table[4];
     const int8_t* dtable;  // when set: the table in device memory, read by the kernel
     int table_len;         // its entries N (1..16)
     int epb;               // elements per code byte: 2, 4 or 8
-    int byte_tier;         // epb 4 or 8: K1C_BOOK, K1C_SIGN or K1C_TERNARY
-    const int8_t* book;    // K1C_BOOK: the book in device memory, book_n x epb bytes
+    int byte_tier;         // epb 4 or 8: K1C_BOOK, K1C_SIGN, K1C_TERNARY or K1C_GRID
+    const int8_t* book;    // K1C_BOOK: the book in device memory, book_n x epb bytes;
+                           // K1C_GRID: the book_n-entry table in device memory
     int book_n;
     int zero;              // subtracted from every decoded value (Offset)
 };

@@ -83,6 +83,10 @@ __device__ void kc_build_byte_table(uint8_t* tab, const K1CParams& p, int dt) {
         int v;
         if (p.byte_tier == K1C_BOOK) {
             v = p.book[static_cast<int64_t>(b % p.book_n) * EPB + t];  // Book: table[code % N]
+        } else if (p.byte_tier == K1C_GRID) {
+            // Packed<Grid<N>, EPB>: sub-code t is bits (8 / EPB) t .. of the byte, low first
+            constexpr int BITS = 8 / EPB;
+            v = p.book[((b >> (BITS * t)) & ((1 << BITS) - 1)) % p.book_n];
         } else if (p.byte_tier == K1C_SIGN) {
             v = (b >> t) & 1 ? 1 : -1;
         } else {
