@@ -392,9 +392,10 @@ typedef struct uor_b200_codec {
  * rows * (cols / BLK) codes (CodedMatrix::new, matrix.rs:36-60), else DOES_NOT_FIT; a
  * table whose offset image leaves i8 is INVALID_ARGUMENT. Code bytes of whole elements
  * (SIGN with BLK = 8 K, TERNARY with BLK = 4 K, BOOK with K = 1 and BLK 4 or 8) are
- * decoded inside the tensor-core pipeline when k fits one s32 lane and cols is a multiple
- * of 16 x the elements per code byte (route b_layout 1 or 0); other shapes decode once
- * into a dense workspace (b_layout 3). The bytes of C are the same either way. */
+ * decoded inside the tensor-core pipeline when cols is a multiple of 16 x the elements
+ * per code byte (route b_layout 1 or 0; past one s32 lane in exact k chunks, route
+ * k_chunks); other shapes decode once into a dense workspace (b_layout 3). The bytes of C
+ * are the same either way. */
 int uor_b200_codec_gemm(uor_b200_dtype out, const uor_b200_view *a, const uor_b200_codec *codec,
                         const uint8_t *codes, size_t codes_len, size_t k, size_t n,
                         uint32_t orientation, const uor_b200_view_mut *c, int64_t alpha,

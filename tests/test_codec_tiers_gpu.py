@@ -118,6 +118,34 @@ def test_byte_codes_on_chip(orientation, m, tier, block, cb, N, zero):
     assert route.tile_m == (512 if m >= 512 else 256)
 
 
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("m", [70, 520])
+@pytest.mark.parametrize("tier,block,cb", [(U.TIER_SIGN, 16, 2), (U.TIER_TERNARY, 4, 1),
+                                           (U.TIER_BOOK, 8, 1)])
+def test_byte_codes_on_chip_deep_reduction(orientation, m, tier, block, cb):
+    """A reduction deeper than one s32 lane (k = 131456: a full 130944 chunk and a ragged
+    512) still decodes on chip: K1C per exact chunk into s32 planes, folded in 64 bits by
+    the Linear epilogue (i64 out, alpha 3, beta -1)."""
+    k, n = 131456, 128
+    rows, cols = (k, n) if orientation == 0 else (n, k)
+    a = i8(80 + m, m * k)
+    codes = codes_for(rows, cols, block, cb, 50 + block)
+    table = U.corpus(23, U.CORPUS_I8, 256 * block) if tier == U.TIER_BOOK else None
+    dense = orc.decode_codec_np(tier, codes, rows, cols, table, block, cb).reshape(-1)
+    c0 = np.random.default_rng(m).integers(-1000, 1000, size=m * n).astype(np.int64)
+    got, want = c0.copy(), c0.copy()
+    route = U.Route()
+    kw = {"table": table} if table is not None else {}
+    U.codec_gemm(U.I64, a, (m, k, k, 1), tier, codes, k, n, got, (m, n, n, 1), alpha=3, beta=-1,
+                 route=route, orientation=orientation, block=block, code_bytes=cb, **kw)
+    bv = (k, n, n, 1) if orientation == 0 else (k, n, 1, k)
+    orc.gemm_int(orc.View(a, m, k, k, 1), orc.View(dense, *bv), orc.View(want, m, n, n, 1),
+                 alpha=3, beta=-1)
+    assert np.array_equal(got, want)
+    assert route.k_chunks == 2 and route.b_layout == (1 if orientation == 0 else 0)
+    assert route.tile_m == (512 if m >= 512 else 256)
+
+
 @pytest.mark.parametrize("P", [2, 4])
 def test_grid_with_offset(P):
     m, k, n = 260, 128, 96

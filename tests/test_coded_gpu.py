@@ -186,6 +186,18 @@ def test_quarter_and_bit_packings_on_chip(P, N, orientation, m):
         assert route.tile_m == (512 if m >= 512 else 256)
 
 
+@pytest.mark.parametrize("orientation", [0, 1])
+@pytest.mark.parametrize("P", [4, 8])
+def test_quarter_and_bit_packings_deep_reduction(P, orientation):
+    """Past one s32 lane (k = 131200: a 130944 chunk and 256 more) the byte-table route
+    runs K1C per exact chunk and folds the s32 planes in 64 bits."""
+    m, k, n = 300, 131200, 128
+    got, want, route = run(m, k, n, P, 3, orientation, U.I64, 3, -1, seed=P + orientation)
+    assert np.array_equal(got, want)
+    assert route.kernel == 4 and route.k_chunks == 2
+    assert route.b_layout == (1 if orientation == 0 else 0)
+
+
 @pytest.mark.parametrize("P", [4, 8])
 def test_quarter_and_bit_packings_device_table(P):
     """Device pointers and a device table read by K1C's decoders themselves."""

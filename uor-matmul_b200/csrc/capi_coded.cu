@@ -20,8 +20,8 @@ using namespace uor;
 namespace {
 
 // Decode a Packed<Grid<N>, P> coded matrix to a dense row-major int8 k x n matrix
-// (used only off the on-chip paths: P = 1, N > 16 with P = 2, P = 4 or 8 past one s32
-// lane, or code rows the TMA cannot read).
+// (used only off the on-chip paths: P = 1, N > 16 with P = 2, or code rows the TMA
+// cannot read).
 __global__ void decode_dense_kernel(int8_t* __restrict__ out, const uint8_t* __restrict__ codes,
                                     const int8_t* __restrict__ table, int N, int P,
                                     int orientation, int k, int n) {
@@ -93,54 +93,50 @@ __global__ void decode_nibbles_kernel(int8_t* __restrict__ out, const uint8_t* _
 // K1C (gemm_coded_pair.cu) over device codes of p.epb elements per code byte, p's decode
 // fields set by the caller: the activations as K1's A (K-major rows, gathered if TMA cannot
 // read them as given), the codes map, 512 x 256 tiles from 512 activation rows up (each
-// decoded stage serving both halves) and 256 x 256 below; fills the route.
+// decoded stage serving both halves) and 256 x 256 below; fills the route. A reduction
+// deeper than one s32 lane runs as exact chunks of K1_CHUNK_K (whole stages), each launch
+// with its activation and code maps re-based at the chunk's first k and writing an s32
+// plane, folded in 64 bits by reduce_chunks with the Linear epilogue (the analogue of
+// run_chunked_depth, kernel.rs:1431).
 int launch_k1c(uor_b200_ctx* ctx, K1CParams p, const Operand& A, const uint8_t* da,
                const uint8_t* dcodes, size_t m, size_t k, size_t n, int orientation, int kind,
                int64_t alpha, int64_t beta, const LinearEpi& epi, const Operand& C,
                const OutStage& cs, uor_b200_route* route) {
     cudaStream_t s = ctx->stream;
     int st = UOR_B200_OK;
-    const uint8_t* xa = da;
-    uint64_t xstride = 0;
     const size_t ldk = (k + 15) / 16 * 16;
     const bool a_ok = (reinterpret_cast<uintptr_t>(da) & 15u) == 0 && (k == 1 || A.cs == 1) &&
                       (m == 1 || (A.rs > 0 && (size_t)A.rs >= k && (A.rs & 15) == 0));
+    const bool chunked = (int64_t)k > K1_LANE_DEPTH;
+    const int chunks = chunked ? (int)((k + K1_CHUNK_K - 1) / K1_CHUNK_K) : 1;
+    const size_t g_bytes = a_ok ? 0 : (m * ldk + 255) / 256 * 256;
+    size_t p_bytes = 0;
+    if (chunked && (__builtin_mul_overflow(m, n, &p_bytes) ||
+                    __builtin_mul_overflow(p_bytes, (size_t)chunks * sizeof(int32_t), &p_bytes)))
+        return UOR_B200_UNSUPPORTED;
+    uint8_t* ws = nullptr;
+    if (g_bytes + p_bytes) {
+        ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, g_bytes + p_bytes, &st));
+        if (!ws) return st;
+    }
+    const uint8_t* xa = da;
+    uint64_t xstride = 0;
     if (a_ok) {
         xstride = m == 1 ? ldk : (uint64_t)A.rs;
     } else {
-        uint8_t* ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, (m * ldk + 255) / 256 * 256, &st));
-        if (!ws) return st;
         if (gather_2d(ws, ldk, da, m, k, A.rs, A.cs, 1, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
         xa = ws;
         xstride = ldk;
     }
-    const uint32_t epb = (uint32_t)p.epb;
-    CUtensorMap tmA, tmQ, tmO;
-    bool ok = make_tmap_u8(&tmA, xa, k, m, xstride, 128, 128);
-    if (orientation == 0)
-        ok = ok && make_tmap_u8(&tmQ, dcodes, n / epb, k, n / epb, 128 / epb, 128, false);
-    else
-        ok = ok && make_tmap_u8(&tmQ, dcodes, k / epb, n, k / epb, 128 / epb, 128, false);
-    if (!ok) return UOR_B200_DEVICE_ERROR;
+    const size_t epb = (size_t)p.epb;
     p.m = (int)m;
     p.n = (int)n;
     p.k_begin = 0;
-    p.num_kb = (int)((k + K1_BK - 1) / K1_BK);
     const bool tall = m >= 512;
     p.tiles_m = (int)((m + (tall ? 511 : 255)) / (tall ? 512 : 256));
     p.tiles_n = (int)((n + 255) / 256);
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.group_m = p.tiles_m < 16 ? p.tiles_m : 16;
-    p.c = cs.dev_origin;
-    p.rsc = C.rs;
-    p.csc = C.cs;
-    p.epi = epi;
-    p.fast = kind == OUT_I32 && alpha == 1 && beta == 0 && C.cs == 1 &&
-             (m == 1 || (C.rs > 0 && (C.rs & 3) == 0 && (size_t)C.rs >= n)) &&
-             (reinterpret_cast<uintptr_t>(cs.dev_origin) & 15u) == 0;
-    p.tma_store = p.fast && make_tmap_s32(&tmO, cs.dev_origin, n, m,
-                                          (uint64_t)(m == 1 ? (n + 3) / 4 * 4 : (size_t)C.rs) * 4,
-                                          32, 32);
     p.idesc = idesc_i8(256, 256, true, true, false, orientation == 0);
     p.status = ctx->d_status;
     p.budget_ns = ctx->budget_ns;
@@ -149,12 +145,50 @@ int launch_k1c(uor_b200_ctx* ctx, K1CParams p, const Operand& A, const uint8_t* 
     route->tile_m = tall ? 512 : 256;
     route->tile_n = 256;
     route->tile_k = K1_BK;
-    route->k_chunks = 1;
+    route->k_chunks = (uint32_t)chunks;
     route->ctas = (uint32_t)(2 * (p.num_tiles < mc ? p.num_tiles : mc));
     route->pairs = 1;
     route->a_layout = a_ok ? 0 : 2;
     route->b_layout = orientation == 0 ? 1 : 0;  // decoded on chip, never materialised
-    if (k1c_launch(tmA, tmQ, tmO, orientation, tall, p, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    int32_t* part = chunked ? reinterpret_cast<int32_t*>(ws + g_bytes) : nullptr;
+    for (int q = 0; q < chunks; ++q) {
+        const size_t k0 = (size_t)q * K1_CHUNK_K;  // a multiple of 128: every base stays aligned
+        const size_t kl = chunked ? std::min((size_t)K1_CHUNK_K, k - k0) : k;
+        CUtensorMap tmA, tmQ, tmO;
+        bool ok = make_tmap_u8(&tmA, xa + k0, kl, m, xstride, 128, 128);
+        if (orientation == 0)
+            ok = ok && make_tmap_u8(&tmQ, dcodes + k0 * (n / epb), n / epb, kl, n / epb, 128 / epb, 128,
+                                    false);
+        else
+            ok = ok && make_tmap_u8(&tmQ, dcodes + k0 / epb, kl / epb, n, k / epb, 128 / epb, 128, false);
+        if (!ok) return UOR_B200_DEVICE_ERROR;
+        p.num_kb = (int)((kl + K1_BK - 1) / K1_BK);
+        if (chunked) {
+            // this chunk's exact s32 plane, m x n row-major
+            int32_t* plane = part + (size_t)q * m * n;
+            p.c = plane;
+            p.rsc = (int64_t)n;
+            p.csc = 1;
+            p.epi = LinearEpi{1, 0, MODE_NEAREST, OUT_I32};
+            p.fast = 1;
+            p.tma_store = n % 4 == 0 && (reinterpret_cast<uintptr_t>(plane) & 15u) == 0 &&
+                          make_tmap_s32(&tmO, plane, n, m, (uint64_t)n * 4, 32, 32);
+        } else {
+            p.c = cs.dev_origin;
+            p.rsc = C.rs;
+            p.csc = C.cs;
+            p.epi = epi;
+            p.fast = kind == OUT_I32 && alpha == 1 && beta == 0 && C.cs == 1 &&
+                     (m == 1 || (C.rs > 0 && (C.rs & 3) == 0 && (size_t)C.rs >= n)) &&
+                     (reinterpret_cast<uintptr_t>(cs.dev_origin) & 15u) == 0;
+            p.tma_store = p.fast && make_tmap_s32(&tmO, cs.dev_origin, n, m,
+                                                  (uint64_t)(m == 1 ? (n + 3) / 4 * 4 : (size_t)C.rs) * 4,
+                                                  32, 32);
+        }
+        if (k1c_launch(tmA, tmQ, tmO, orientation, tall, p, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
+    }
+    if (chunked && reduce_chunks(part, chunks, m, n, cs.dev_origin, C.rs, C.cs, epi, s) != cudaSuccess)
+        return UOR_B200_DEVICE_ERROR;
     return UOR_B200_OK;
 }
 
@@ -233,11 +267,11 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool shallow = (int64_t)k <= K1_LANE_DEPTH;
     const bool pair_fused = fused && shallow;
     const bool decode_once = fused && !pair_fused && !on_chip && m >= 2 * (size_t)K5_BN;
-    // Four or eight sub-codes per byte (Packed<Grid<N>, 4 | 8>) within one s32 lane: K1C
-    // with the byte table built on chip from the N-entry table (code rows whole 16-byte
-    // TMA strides).
+    // Four or eight sub-codes per byte (Packed<Grid<N>, 4 | 8>): K1C with the byte table
+    // built on chip from the N-entry table, in exact chunks past one s32 lane (code rows
+    // whole 16-byte TMA strides).
     const size_t code_cols = orientation == 0 ? n : k;
-    const bool byte_fused = (per_byte == 4 || per_byte == 8) && k > 0 && shallow &&
+    const bool byte_fused = (per_byte == 4 || per_byte == 8) && k > 0 &&
                             (code_cols / per_byte) % 16 == 0 &&
                             (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
     // The 16-entry effective table the fused decode uses: table[v % N]; a device table on
@@ -624,14 +658,14 @@ int codec_common(uor_b200_dtype out, const uor_b200_view* a, const uor_b200_code
     if ((st = stage_out_begin(ctx, C, dev, beta != 0, &cs))) return st;
     const LinearEpi epi{alpha, beta, mode, kind};
     // Code bytes of 4 or 8 whole elements each (Book with one-byte codes and blocks of 4 or
-    // 8, Sign with 8 elements per code byte, Ternary with 4) and a reduction within one s32
-    // lane: K1C decodes them through a 256-entry byte table it builds in shared memory, so
-    // no dense B exists anywhere. The code rows must be whole 16-byte TMA strides.
+    // 8, Sign with 8 elements per code byte, Ternary with 4): K1C decodes them through a
+    // 256-entry byte table it builds in shared memory, in exact chunks past one s32 lane,
+    // so no dense B exists anywhere. The code rows must be whole 16-byte TMA strides.
     int epb = 0, btier = K1C_BOOK;
     if (tier == UOR_B200_TIER_BOOK && cb == 1 && (blk == 4 || blk == 8)) epb = (int)blk;
     else if (tier == UOR_B200_TIER_SIGN && blk == 8 * cb) epb = 8, btier = K1C_SIGN;
     else if (tier == UOR_B200_TIER_TERNARY && blk == 4 * cb) epb = 4, btier = K1C_TERNARY;
-    const bool chip = epb != 0 && k > 0 && (int64_t)k <= K1_LANE_DEPTH && (cols / epb) % 16 == 0 &&
+    const bool chip = epb != 0 && k > 0 && (cols / epb) % 16 == 0 &&
                       (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
     if (chip) {
         K1CParams p{};
