@@ -105,7 +105,7 @@ typedef enum uor_b200_kernel {
     UOR_B200_KERNEL_I8_TCGEN05 = 1,    /* K1: s8 x s8 -> s32 TMEM, exact epilogue */
     UOR_B200_KERNEL_LIMB_TCGEN05 = 2,  /* K2: byte-sliced limb GEMMs, exact recombination */
     UOR_B200_KERNEL_TROPICAL = 3,      /* K4: packed max-plus on CUDA cores */
-    UOR_B200_KERNEL_CODED_TCGEN05 = 4, /* K5: codebook decode feeding K1's MMA */
+    UOR_B200_KERNEL_CODED_TCGEN05 = 4, /* K1C: codebook decode feeding K1's MMA */
     UOR_B200_KERNEL_FLOAT_EXACT = 5,   /* K6+K7: exact float, one rounding */
     UOR_B200_KERNEL_EPILOGUE_ONLY = 6, /* k == 0: C := encode(beta * C) */
     UOR_B200_KERNEL_SKINNY = 7         /* <= 16 rows or columns: dp4a reduce / column kernels */
@@ -134,11 +134,11 @@ typedef struct uor_b200_route {
  * product's bound, whatever the estimated cost. Exact; the same bytes. */
 #define UOR_B200_MODULAR 8u
 /* Codec tier (Packed<Grid<N>, 2>): decode the codes on chip only, never into a dense copy
- * of the coded operand in device memory. Reductions within one s32 lane (131071) always
- * decode on chip (K1's CTA-pair GEMM with the codes decoded straight into its shared-memory
- * B stages); the flag keeps deeper reductions of 512 rows and more off the k x n workspace
- * the default would decode them into (the fused K5 kernel instead). The same bytes either
- * way. */
+ * of the coded operand in device memory. The codes are decoded on chip (K1's CTA-pair GEMM
+ * with the codes decoded straight into its shared-memory B stages, in exact k chunks past
+ * one s32 lane) except for reductions past one s32 lane with 512 rows or more, which the
+ * default decodes once into a k x n workspace; the flag keeps those on chip too. The same
+ * bytes either way. */
 #define UOR_B200_CODEC_ON_CHIP 16u
 
 /* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)
@@ -335,7 +335,8 @@ int uor_b200_raw_gemm_trop_i8_i32(size_t m, size_t k, size_t n, uor_b200_trop al
  * sub-code first; element (r, c) decodes table[sub % N] with
  * sub = (codes[r * (n / P) + c / P] >> ((8 / P) * (c % P))) & mask.
  * A is a dense i8 view; out in {I8 .. I128}. P in {1, 2, 4, 8}; 1 <= N <= 256. P = 2 with
- * N <= 16 runs the fused decode (K5); the rest decode to a dense workspace first. */
+ * N <= 16, and P = 4 or 8 with code rows of whole 16-byte strides, decode on chip (K1C,
+ * see UOR_B200_CODEC_ON_CHIP); the rest decode to a dense workspace first. */
 int uor_b200_coded_gemm(uor_b200_dtype out, const uor_b200_view *a, const uint8_t *codes,
                         size_t codes_len, size_t k, size_t n, uint32_t per_byte,
                         const int8_t *table, size_t table_len, const uor_b200_view_mut *c,

@@ -1,10 +1,9 @@
 """The codec tier against the oracle's coded_gemm / gemm_tabulated restatement: K1C (K1's
-CTA-pair pipeline with the codes decoded into its B stages, no dense copy anywhere) for
-reductions within one s32 lane, with 512-row tiles from 512 activation rows up and 256-row
-tiles below -- nibbles through the register table, 2- and 1-bit sub-codes through a byte
-table built on chip; for deeper nibble reductions, the one-pass decode followed by K1 from
-512 rows up, and K5 (the codebook decode fused into the tensor-core pipeline, decoded
-weights on the M side) below 512 rows or with CODEC_ON_CHIP."""
+CTA-pair pipeline with the codes decoded into its B stages, no dense copy anywhere), with
+512-row tiles from 512 activation rows up and 256-row tiles below -- nibbles through the
+register table, 2- and 1-bit sub-codes through a byte table built on chip -- in exact
+chunks past one s32 lane; deep nibble products of 512 rows and more decode once into a
+dense workspace and run K1's chunks unless CODEC_ON_CHIP forbids the workspace."""
 import numpy as np
 import pytest
 
@@ -117,7 +116,7 @@ def test_pair_decode_gathered_activations():
 @pytest.mark.parametrize("orientation", [0, 1])
 def test_decode_once_past_the_lane(orientation):
     """k past the s32 lane depth with 512+ rows: decoded once to dense int8 (flat over the
-    code bytes, low nibble first), then K1 in exact chunks; with CODEC_ON_CHIP, K5's
+    code bytes, low nibble first), then K1 in exact chunks; with CODEC_ON_CHIP, K1C's
     chunks instead (no workspace)."""
     m, k, n = 512, 131_200, 32
     got, want, route = run(m, k, n, 2, 16, orientation, U.I64, seed=5)
@@ -126,16 +125,17 @@ def test_decode_once_past_the_lane(orientation):
     got, want, route = run(m, k, n, 2, 16, orientation, U.I64, seed=5, on_chip=True)
     assert np.array_equal(got, want)
     assert route.kernel == 4 and route.b_layout != 3 and route.k_chunks == 2
+    assert route.tile_m == 512
 
 
 @pytest.mark.parametrize("orientation", [0, 1])
-def test_k5_deep_reductions_below_512_rows(orientation):
-    """Fewer than 512 activation rows and k past the s32 lane: K5's exact chunks (no
-    workspace), a ragged row count on its 128-column tiles."""
+def test_deep_reductions_below_512_rows_on_chip(orientation):
+    """Fewer than 512 activation rows and k past the s32 lane: K1C's exact chunks on
+    256-row tiles (no workspace), a ragged row count, chunk planes folded in 64 bits."""
     m, k, n = 70, 131_200, 64
     got, want, route = run(m, k, n, 2, 16, orientation, U.I64, 3, -1, seed=6)
     assert np.array_equal(got, want)
-    assert route.kernel == 4 and route.b_layout != 3 and route.k_chunks == 2 and route.tile_m == 128
+    assert route.kernel == 4 and route.b_layout != 3 and route.k_chunks == 2 and route.tile_m == 256
 
 
 @pytest.mark.parametrize("orientation", [0, 1])

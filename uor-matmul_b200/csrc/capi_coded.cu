@@ -255,18 +255,18 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     const bool fused = per_byte == 2 && table_len <= 16 && k > 0 &&
                        (orientation == 0 ? (n % 32 == 0) : (k % 32 == 0)) &&
                        (reinterpret_cast<uintptr_t>(dcodes) & 15u) == 0;
-    // Reductions within one s32 lane: K1C, K1's CTA-pair pipeline with the codes decoded
-    // into its B stages -- no dense B anywhere -- with 512 x 256 tiles (each decoded stage
-    // feeding two M256 halves) from 512 activation rows up, 256 x 256 tiles below (faster
-    // than K5 at every row count: 0.043 against 0.064 ms at 32 x 8192 x 8192, 0.046 against
-    // 0.085 at 384 rows; configs[1] 0.099-0.104 ms against 0.117 for decode-once). Deeper
-    // reductions: from 512 rows decode once into a k x n workspace and run K1 in exact
-    // chunks, unless UOR_B200_CODEC_ON_CHIP forbids the workspace; below 512 rows, or with
-    // the flag, K5's chunks.
+    // K1C, K1's CTA-pair pipeline with the codes decoded into its B stages -- no dense B
+    // anywhere -- with 512 x 256 tiles (each decoded stage feeding two M256 halves) from 512
+    // activation rows up and 256 x 256 tiles below (configs[1] 0.099-0.104 ms against 0.117
+    // for decode-once; at 32 x 8192 x 8192 0.043 ms and at 384 rows 0.046, against 0.064
+    // and 0.085 for the former fused kernel that put the decoded weights on the M side).
+    // Past one s32 lane it runs in exact chunks, except that from 512 rows the default
+    // decodes once into a k x n workspace and runs K1's chunks, unless
+    // UOR_B200_CODEC_ON_CHIP forbids the workspace.
     const bool on_chip = call && (call->flags & UOR_B200_CODEC_ON_CHIP);
     const bool shallow = (int64_t)k <= K1_LANE_DEPTH;
-    const bool pair_fused = fused && shallow;
-    const bool decode_once = fused && !pair_fused && !on_chip && m >= 2 * (size_t)K5_BN;
+    const bool decode_once = fused && !shallow && !on_chip && m >= 512;
+    const bool pair_fused = fused && !decode_once;
     // Four or eight sub-codes per byte (Packed<Grid<N>, 4 | 8>): K1C with the byte table
     // built on chip from the N-entry table, in exact chunks past one s32 lane (code rows
     // whole 16-byte TMA strides).
@@ -285,9 +285,6 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     } else {
         std::memcpy(tab, table, tl);
     }
-    // From two activation tiles of rows up, decoding every weight once into HBM and running
-    // K1 beats decoding it again for each tile inside K5 (K5 is bound by the decode's issue
-    // slots, not by its tensor pipe).
     if (decode_once) {
         uint8_t* dense = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, k * n + 256, &st));
         if (!dense) return st;
@@ -346,7 +343,7 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         if ((st = launch_k1c(ctx, p, A, da, dcodes, m, k, n, orientation, kind, alpha, beta, epi, C,
                              cs, route)))
             return st;
-    } else if (!fused) {
+    } else {
         // Off the on-chip paths (see decode_dense_kernel): decode to a dense row-major
         // k x n int8 matrix in the auxiliary slot, then K1.
         uint8_t* buf = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_AUX, 256 + k * n, &st));
@@ -367,101 +364,6 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
         if (st) return st;
         route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
         route->b_layout = 3;  // decoded to a dense workspace first
-    } else {
-        K5Params p{};
-        p.m = (int)m;
-        p.n = (int)n;
-        p.k = (int)k;
-        p.orientation = orientation;
-        for (int w = 0; w < 4; ++w) {
-            uint32_t word = 0;
-            for (int bpos = 0; bpos < 4; ++bpos)
-                word |= (uint32_t)(uint8_t)tab[(4 * w + bpos) % table_len] << (8 * bpos);
-            p.table[w] = word;
-        }
-        // Activations as the N operand: K-major rows of A, gathered if TMA cannot read them.
-        const uint8_t* xa = da;
-        uint64_t xstride = 0;
-        bool gathered = false;
-        const size_t ldk = (k + 15) / 16 * 16;
-        const bool a_ok = (reinterpret_cast<uintptr_t>(da) & 15u) == 0 && (k == 1 || A.cs == 1) &&
-                          (m == 1 || (A.rs > 0 && (size_t)A.rs >= k && (A.rs & 15) == 0));
-        const bool chunked = (int64_t)k > K1_LANE_DEPTH;
-        const int chunks = chunked ? (int)((k + K1_CHUNK_K - 1) / K1_CHUNK_K) : 1;
-        const size_t g_bytes = a_ok ? 0 : (m * ldk + 255) / 256 * 256;
-        const size_t p_bytes = chunked ? (size_t)chunks * m * n * 4 : 0;
-        uint8_t* ws = nullptr;
-        if (g_bytes + p_bytes) {
-            ws = static_cast<uint8_t*>(ctx_buffer(ctx, SLOT_WS, g_bytes + p_bytes, &st));
-            if (!ws) return st;
-        }
-        if (a_ok) {
-            xstride = m == 1 ? ldk : (uint64_t)A.rs;
-        } else {
-            if (gather_2d(ws, ldk, da, m, k, A.rs, A.cs, 1, s) != cudaSuccess)
-                return UOR_B200_DEVICE_ERROR;
-            xa = ws;
-            xstride = ldk;
-            gathered = true;
-        }
-        CUtensorMap tmX, tmC;
-        bool ok = make_tmap_u8(&tmX, xa, k, m, xstride, 128, 256);
-        if (orientation == 0)
-            ok = ok && make_tmap_u8(&tmC, dcodes, n / 2, k, n / 2, 64, 128, false);
-        else
-            ok = ok && make_tmap_u8(&tmC, dcodes, k / 2, n, k / 2, 64, 128, false);
-        if (!ok) return UOR_B200_DEVICE_ERROR;
-        p.tiles_j = (int)((n + K5_BM - 1) / K5_BM);
-        p.tiles_i = (int)((m + K5_BN - 1) / K5_BN);
-        p.num_tiles = p.tiles_j * p.tiles_i;
-        p.group_j = p.tiles_j < 16 ? p.tiles_j : 16;
-        p.idesc = idesc_i8(K5_BM, K5_BN, true, true, orientation == 0, false);
-        p.status = ctx->d_status;
-        p.budget_ns = ctx->budget_ns;
-        const int grid = p.num_tiles < ctx->sm_count ? p.num_tiles : ctx->sm_count;
-        route->kernel = UOR_B200_KERNEL_CODED_TCGEN05;
-        route->tile_m = K5_BM;
-        route->tile_n = K5_BN;
-        route->tile_k = K5_BK;
-        route->k_chunks = (uint32_t)chunks;
-        route->ctas = (uint32_t)grid;
-        route->a_layout = gathered ? 2 : 0;
-        route->b_layout = orientation == 0 ? 1 : 0;
-        if (!chunked) {
-            p.num_kb = (int)((k + K5_BK - 1) / K5_BK);
-            p.c = cs.dev_origin;
-            p.rsc = C.rs;
-            p.csc = C.cs;
-            p.epi = epi;
-            p.fast = kind == OUT_I32 && alpha == 1 && beta == 0;
-            if (k5_launch(tmX, tmC, p, grid, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
-        } else {
-            // Deep reductions: exact s32 chunk planes, folded by reduce_chunks. The codes
-            // and activations are re-based per chunk through the TMA coordinates' origin.
-            int32_t* part = reinterpret_cast<int32_t*>(ws + g_bytes);
-            for (int q = 0; q < chunks; ++q) {
-                const size_t k0 = (size_t)q * K1_CHUNK_K;
-                const size_t kl = (k - k0) < (size_t)K1_CHUNK_K ? (k - k0) : (size_t)K1_CHUNK_K;
-                CUtensorMap tX, tC;
-                bool ok2 = make_tmap_u8(&tX, xa + k0, kl, m, xstride, 128, 256);
-                if (orientation == 0)
-                    ok2 = ok2 && make_tmap_u8(&tC, dcodes + k0 * (n / 2), n / 2, kl, n / 2, 64, 128,
-                                              false);
-                else
-                    ok2 = ok2 && make_tmap_u8(&tC, dcodes + k0 / 2, kl / 2 + (kl & 1), n, k / 2, 64,
-                                              128, false);
-                if (!ok2) return UOR_B200_DEVICE_ERROR;
-                p.num_kb = (int)((kl + K5_BK - 1) / K5_BK);
-                p.c = part + (size_t)q * m * n;
-                p.rsc = (int64_t)n;
-                p.csc = 1;
-                p.epi = LinearEpi{1, 0, MODE_NEAREST, OUT_I32};
-                p.fast = 1;
-                if (k5_launch(tX, tC, p, grid, s) != cudaSuccess) return UOR_B200_DEVICE_ERROR;
-            }
-            if (reduce_chunks(part, chunks, m, n, cs.dev_origin, C.rs, C.cs, epi, s) != cudaSuccess)
-                return UOR_B200_DEVICE_ERROR;
-        }
     }
     if ((st = stage_out_end(ctx, cs))) return st;
     if (!dev) return uor_b200_ctx_sync(ctx);

@@ -1,5 +1,5 @@
-// gemm_coded.cuh -- K5: exact GEMM against a nibble-coded operand, decoded in the
-// MMA pipeline (no dense copy of the coded operand ever reaches HBM).
+// gemm_coded.cuh -- the codec tier's decode helpers and K1C, K1's CTA-pair GEMM with the
+// coded operand decoded on chip (no dense copy of it ever reaches HBM).
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -8,33 +8,6 @@
 #include "int_epilogue.cuh"
 
 namespace uor {
-
-constexpr int K5_BM = 128;  // decoded weight columns j per tile (TMEM lanes)
-constexpr int K5_BN = 256;  // activation rows i per tile (TMEM columns)
-constexpr int K5_BK = 128;  // reduction per stage
-constexpr int K5_STAGES = 4;
-constexpr int K5_DEC_WARPS = 8;
-constexpr int K5_THREADS = 32 * (6 + K5_DEC_WARPS);  // TMA, MMA, 4 epilogue, decoders
-constexpr int K5_W_BYTES = K5_BM * K5_BK;            // decoded weights, 16 KiB
-constexpr int K5_X_BYTES = K5_BN * K5_BK;            // activations, 32 KiB
-constexpr int K5_C_BYTES = K5_BM * K5_BK / 2;        // codes, 8 KiB
-constexpr int K5_STAGE_BYTES = K5_W_BYTES + K5_X_BYTES + K5_C_BYTES;
-constexpr int K5_SMEM_BYTES = K5_STAGES * K5_STAGE_BYTES + 1024 + 256;
-
-struct K5Params {
-    int m, n, k;            // C is m x n; activations m x k; weights k x n (decoded)
-    int tiles_j, tiles_i, num_tiles, group_j;
-    int num_kb;
-    int orientation;        // 0: codes k x n (coded_gemm); 1: codes n x k (tabulated)
-    uint32_t table[4];      // 16 decoded int8 values, table[v % N] for v in 0..15
-    void* c;
-    int64_t rsc, csc;
-    LinearEpi epi;
-    int fast;               // s32 output, alpha 1, beta 0
-    uint32_t idesc;
-    int* status;
-    uint64_t budget_ns;
-};
 
 // Eight nibbles (first element lowest) -> eight table bytes (.x: elements 0-3, .y: 4-7).
 // __byte_perm reads three bits of each selector nibble (and only the low 16 bits of the
@@ -50,12 +23,6 @@ __device__ __forceinline__ uint2 dec8(uint32_t w, uint32_t t0, uint32_t t1, uint
     r.y = __byte_perm(__byte_perm(t0, t1, wh), __byte_perm(t2, t3, wh), ph);
     return r;
 }
-
-// tmX: activations K-major, dims {k, m}, box {128, 256}, 128-byte swizzle.
-// tmC: codes, no swizzle, box {64 bytes, 128 rows}:
-//   orientation 0: dims {n/2, k}; orientation 1: dims {k/2, n}.
-cudaError_t k5_launch(const CUtensorMap& tmX, const CUtensorMap& tmC, const K5Params& p, int grid,
-                      cudaStream_t stream);
 
 // K1C: K1's CTA-pair GEMM (256 x 256 tiles, p.idesc M256 N256) with B decoded on chip.
 // Code bytes of p.epb elements each:
