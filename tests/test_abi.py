@@ -208,3 +208,48 @@ def test_nccl_entries_validate_before_loading_nccl():
                                        ctypes.byref(out)) == U.INVALID_ARGUMENT
     assert lib.uor_b200_nccl_unique_id(ctypes.addressof(uid), 64) == U.INVALID_ARGUMENT
     assert lib.uor_b200_nccl_comm_destroy(None) == U.OK
+
+
+def _status(fn, *args, **kw):
+    try:
+        fn(*args, **kw)
+    except U.UorError as e:
+        return e.status
+    return U.OK
+
+
+def test_codec_entries_validate_before_any_device_work():
+    """coded_gemm / gemm_tabulated / codec_gemm report the reference's construction
+    failures from the host, before any device work: Packed::new (codecs.rs:166-172: P
+    divides 8, a table with entries), CodedMatrix::new (matrix.rs:36-60: the codes describe
+    exactly the declared shape), CodedTriple::new (coded.rs:48-70: conformance, then
+    aliasing), Offset::new (the offset image stays i8), an unknown tier; an empty product
+    returns at once."""
+    m, k, n = 2, 8, 16
+    a = np.zeros(m * k, np.int8)
+    c = np.zeros(m * n, np.int32)
+    t16 = np.arange(16, dtype=np.int8)
+    q2 = np.zeros(k * n // 2, np.uint8)
+    av, cv = (m, k, k, 1), (m, n, n, 1)
+    cg, xg = U.coded_gemm, U.codec_gemm
+    assert _status(cg, U.I32, a, av, q2, k, n, 3, t16, c, cv) == U.INVALID_ARGUMENT  # P = 3
+    assert _status(cg, U.I32, a, av, q2, k, n, 2, t16[:0], c, cv) == U.INVALID_ARGUMENT
+    assert _status(cg, U.I32, a, av, q2[:-1], k, n, 2, t16, c, cv) == U.DOES_NOT_FIT
+    assert _status(cg, U.I32, a, av, q2[:-1], k, n, 2, t16, c, cv, tabulated=True) == U.DOES_NOT_FIT
+    assert _status(cg, U.I32, a, (m, k - 1, k, 1), q2, k, n, 2, t16, c, cv) == U.NONCONFORMANT
+    assert _status(cg, U.I32, a, av, q2, k, n, 2, t16, c, (m, n, 0, 0)) == U.OUTPUT_ALIASES
+    assert _status(cg, U.I32, a[:0], (0, k, k, 1), q2, k, n, 2, t16, c[:0], (0, n, n, 1)) == U.OK
+    q8 = np.zeros(k * n // 8, np.uint8)
+    assert _status(xg, U.I32, a, av, 7, q8, k, n, c, cv, block=8) == U.UNSUPPORTED  # no tier 7
+    assert _status(xg, U.I32, a, av, U.TIER_SIGN, q8, k, n, c, cv, block=8,
+                   code_bytes=3) == U.INVALID_ARGUMENT
+    assert _status(xg, U.I32, a, av, U.TIER_SIGN, q8[:-1], k, n, c, cv, block=8) == U.DOES_NOT_FIT
+    assert _status(xg, U.I32, a, av, U.TIER_SIGN, q8, k, n, c, cv, block=8,
+                   zero=128) == U.INVALID_ARGUMENT  # -1 - 128 leaves i8
+    book = np.full(256 * 8, 100, np.int8)
+    assert _status(xg, U.I32, a, av, U.TIER_BOOK, q8, k, n, c, cv, table=book, block=8,
+                   zero=-28) == U.INVALID_ARGUMENT  # 100 + 28 leaves i8
+    assert _status(xg, U.I32, a, av, U.TIER_BOOK, q8, k, n, c, cv, table=book[:0],
+                   block=8) == U.INVALID_ARGUMENT  # a book with no rows
+    assert _status(xg, U.I32, a, av, U.TIER_TERNARY, np.zeros(k * n // 4, np.uint8), k, n, c,
+                   (m, n, 0, 0), block=4) == U.OUTPUT_ALIASES
