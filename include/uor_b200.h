@@ -136,9 +136,9 @@ typedef struct uor_b200_route {
 /* Codec tier (Packed<Grid<N>, 2>): decode the codes on chip only, never into a dense copy
  * of the coded operand in device memory. The codes are decoded on chip (K1's CTA-pair GEMM
  * with the codes decoded straight into its shared-memory B stages, in exact k chunks past
- * one s32 lane) except for reductions past one s32 lane with 512 rows or more, which the
- * default decodes once into a k x n workspace; the flag keeps those on chip too. The same
- * bytes either way. */
+ * one s32 lane) except for reductions past one s32 lane with 512 rows or more and fewer
+ * 512 x 256 output tiles than resident CTA pairs, which the default decodes once into a
+ * k x n workspace; the flag keeps those on chip too. The same bytes either way. */
 #define UOR_B200_CODEC_ON_CHIP 16u
 
 /* Per-call options: GemmOptions' encode (crates/uor-matmul-gemm/src/driver.rs:13-20)

@@ -260,12 +260,15 @@ int coded_common(uor_b200_dtype out, const uor_b200_view* a, const uint8_t* code
     // activation rows up and 256 x 256 tiles below (configs[1] 0.099-0.104 ms against 0.117
     // for decode-once; at 32 x 8192 x 8192 0.043 ms and at 384 rows 0.046, against 0.064
     // and 0.085 for the former fused kernel that put the decoded weights on the M side).
-    // Past one s32 lane it runs in exact chunks, except that from 512 rows the default
-    // decodes once into a k x n workspace and runs K1's chunks, unless
-    // UOR_B200_CODEC_ON_CHIP forbids the workspace.
+    // Past one s32 lane it runs in exact chunks, one launch per chunk, except where those
+    // launches would leave most CTA pairs idle: from 512 rows with fewer 512 x 256 tiles
+    // than resident pairs the default decodes once into a k x n workspace and runs K1's
+    // chunks (1024 x 262016 x 2048: 0.80 ms against 1.20; 2048 x 262016 x 8192, 128 tiles:
+    // 3.72 ms against 2.88 for K1C), unless UOR_B200_CODEC_ON_CHIP forbids the workspace.
     const bool on_chip = call && (call->flags & UOR_B200_CODEC_ON_CHIP);
     const bool shallow = (int64_t)k <= K1_LANE_DEPTH;
-    const bool decode_once = fused && !shallow && !on_chip && m >= 512;
+    const bool decode_once = fused && !shallow && !on_chip && m >= 512 &&
+                             ((m + 511) / 512) * ((n + 255) / 256) < (size_t)k1c_max_clusters();
     const bool pair_fused = fused && !decode_once;
     // Four or eight sub-codes per byte (Packed<Grid<N>, 4 | 8>): K1C with the byte table
     // built on chip from the N-entry table, in exact chunks past one s32 lane (code rows
