@@ -253,3 +253,35 @@ def test_codec_entries_validate_before_any_device_work():
                    block=8) == U.INVALID_ARGUMENT  # a book with no rows
     assert _status(xg, U.I32, a, av, U.TIER_TERNARY, np.zeros(k * n // 4, np.uint8), k, n, c,
                    (m, n, 0, 0), block=4) == U.OUTPUT_ALIASES
+
+
+def test_float_tropical_complex_entries_validate_before_any_device_work():
+    """gemm_float, driver::gemm over Trop<E> and over Complex<T> report Triple::new's two
+    failures (layout.rs:534-561), a short buffer and an unsupported pair from the host; an
+    empty product returns at once (raw.rs:137-148 for sgemm)."""
+    m, k, n = 2, 3, 4
+    af, bf = np.zeros(m * k, np.float32), np.zeros((k + 1) * n, np.float32)
+    cf = np.zeros(m * n, np.float32)
+    good, wide = (k, n, n, 1), (k + 1, n, n, 1)
+    g = U.gemm_float
+    assert _status(g, U.F32, U.F32, af, (m, k, k, 1), bf, wide, cf, (m, n, n, 1)) == U.NONCONFORMANT
+    assert _status(g, U.F32, U.F32, af, (m, k, k, 1), bf, good, cf, (m, n, 0, 0)) == U.OUTPUT_ALIASES
+    assert _status(g, U.F32, U.F32, af[:-1], (m, k, k, 1), bf, good, cf, (m, n, n, 1)) == U.DOES_NOT_FIT
+    assert _status(g, U.F32, U.I32, af, (m, k, k, 1), bf, good, cf, (m, n, n, 1)) == U.UNSUPPORTED
+    assert _status(g, U.F32, U.F32, af[:0], (0, k, k, 1), bf, good, cf[:0], (0, n, n, 1)) == U.OK
+    assert _status(U.sgemm, 0, k, n, 1, af, k, 1, bf, n, 1, 0, cf, n, 1) == U.OK
+    at = np.zeros(m * k * 2, np.uint8)   # Trop<i8>: 2 bytes
+    bt = np.zeros((k + 1) * n * 2, np.uint8)
+    ct = np.zeros(m * n * 8, np.uint8)   # Trop<i32>: 8 bytes
+    t = U.gemm_tropical
+    assert _status(t, U.TROP_I8, U.TROP_I32, at, (m, k, k, 1), bt, wide, ct,
+                   (m, n, n, 1)) == U.NONCONFORMANT
+    assert _status(t, U.TROP_I8, U.TROP_I32, at, (m, k, k, 1), bt, good, ct,
+                   (m, n, 0, 0)) == U.OUTPUT_ALIASES
+    assert _status(t, U.TROP_I8, U.TROP_I32, at[:0], (0, k, k, 1), bt, good, ct[:0],
+                   (0, n, n, 1)) == U.OK
+    ac, bc = np.zeros(2 * m * k, np.int32), np.zeros(2 * (k + 1) * n, np.int32)
+    cc = np.zeros(2 * m * n, np.int32)
+    x = U.gemm_complex
+    assert _status(x, U.I32, U.I32, ac, (m, k, k, 1), bc, wide, cc, (m, n, n, 1)) == U.NONCONFORMANT
+    assert _status(x, U.I32, U.I32, ac, (m, k, k, 1), bc, good, cc, (m, n, 0, 0)) == U.OUTPUT_ALIASES
