@@ -416,9 +416,9 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                     if (got) {
                         uint8_t* sb = smem + stage * KC_STAGE_BYTES + KC_A_BYTES;
                         const uint8_t* sq = codes + q * KC_C_BYTES;
-                        // all of this thread's code words first (loads in flight together),
-                        // then the decodes and the swizzled stores: 128 code rows x 8 groups
-                        // of 8 bytes, each group one 16-byte unit of an operand row
+                        // all of this thread's code bytes first (loads in flight together),
+                        // then the decodes and the swizzled stores: 128 code rows x 8 units,
+                        // each unit 16 bytes of an operand row
                         constexpr int REPS = (128 * 8) / (32 * GW);
                         if constexpr (EPB != 2) {
                             // byte tiers: each unit's code bytes, then the table lookups
@@ -434,21 +434,21 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                                     kc_byte_unit<EPB>(cb8[rep], btab);
                             }
                         } else {
-                        uint2 cw[REPS];
-#pragma unroll
-                        for (int rep = 0; rep < REPS; ++rep) {
-                            const int u = gt + rep * 32 * GW;
-                            cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
-                        }
-#pragma unroll
-                        for (int rep = 0; rep < REPS; ++rep) {
-                            const int u = gt + rep * 32 * GW;
-                            const int r = u >> 3, qq = u & 7;
-                            const uint2 d0 = dec8(cw[rep].x, t0, t1, t2, t3);
-                            const uint2 d1 = dec8(cw[rep].y, t0, t1, t2, t3);
-                            *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
-                                make_uint4(d0.x, d0.y, d1.x, d1.y);
-                        }
+                            uint2 cw[REPS];
+    #pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep) {
+                                const int u = gt + rep * 32 * GW;
+                                cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
+                            }
+    #pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep) {
+                                const int u = gt + rep * 32 * GW;
+                                const int r = u >> 3, qq = u & 7;
+                                const uint2 d0 = dec8(cw[rep].x, t0, t1, t2, t3);
+                                const uint2 d1 = dec8(cw[rep].y, t0, t1, t2, t3);
+                                *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                                    make_uint4(d0.x, d0.y, d1.x, d1.y);
+                            }
                         }
                         // the codes slot is decoded: hand it back to the codes producer
                         __syncwarp();
@@ -865,21 +865,21 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                                     kc_byte_unit<EPB>(cb8[rep], btab);
                             }
                         } else {
-                        uint2 cw[REPS];
-#pragma unroll
-                        for (int rep = 0; rep < REPS; ++rep) {
-                            const int u = gt + rep * 32 * GW;
-                            cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
-                        }
-#pragma unroll
-                        for (int rep = 0; rep < REPS; ++rep) {
-                            const int u = gt + rep * 32 * GW;
-                            const int r = u >> 3, qq = u & 7;
-                            const uint2 e0 = dec8(cw[rep].x, t0, t1, t2, t3);
-                            const uint2 e1 = dec8(cw[rep].y, t0, t1, t2, t3);
-                            *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
-                                make_uint4(e0.x, e0.y, e1.x, e1.y);
-                        }
+                            uint2 cw[REPS];
+    #pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep) {
+                                const int u = gt + rep * 32 * GW;
+                                cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
+                            }
+    #pragma unroll
+                            for (int rep = 0; rep < REPS; ++rep) {
+                                const int u = gt + rep * 32 * GW;
+                                const int r = u >> 3, qq = u & 7;
+                                const uint2 e0 = dec8(cw[rep].x, t0, t1, t2, t3);
+                                const uint2 e1 = dec8(cw[rep].y, t0, t1, t2, t3);
+                                *reinterpret_cast<uint4*>(sb + r * 128 + ((qq ^ (r & 7)) << 4)) =
+                                    make_uint4(e0.x, e0.y, e1.x, e1.y);
+                            }
                         }
                         __syncwarp();
                         if (lane == 0) mbar_arrive(cempty0 + 8 * q);
