@@ -435,12 +435,12 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                             }
                         } else {
                             uint2 cw[REPS];
-    #pragma unroll
+#pragma unroll
                             for (int rep = 0; rep < REPS; ++rep) {
                                 const int u = gt + rep * 32 * GW;
                                 cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
                             }
-    #pragma unroll
+#pragma unroll
                             for (int rep = 0; rep < REPS; ++rep) {
                                 const int u = gt + rep * 32 * GW;
                                 const int r = u >> 3, qq = u & 7;
@@ -866,12 +866,12 @@ __global__ void __launch_bounds__(KC_THREADS, 1)
                             }
                         } else {
                             uint2 cw[REPS];
-    #pragma unroll
+#pragma unroll
                             for (int rep = 0; rep < REPS; ++rep) {
                                 const int u = gt + rep * 32 * GW;
                                 cw[rep] = *reinterpret_cast<const uint2*>(sq + (u >> 3) * 64 + (u & 7) * 8);
                             }
-    #pragma unroll
+#pragma unroll
                             for (int rep = 0; rep < REPS; ++rep) {
                                 const int u = gt + rep * 32 * GW;
                                 const int r = u >> 3, qq = u & 7;
