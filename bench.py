@@ -652,8 +652,8 @@ def wl_f32(args, U, torch, rank, size, sets=2):
     w.l2 = f"{sets} rotating operand sets ({sets * 8 * m * k >> 20} MiB) + {4 * m * n >> 20} MiB output"
     w.algorithmic_bytes = 8 * m * k + 4 * m * n
     w.flush = False
-    w.traffic = (load_traffic("modular_f32_4096_traffic.json", "bytes_per_call") if size == 4096
-                 else None)
+    w.traffic = (load_traffic(f"modular_f32_{size}_traffic.json", "bytes_per_call")
+                 if size in (4096, 8192) else None)
 
     def roofline(avg_ms):
         peak, src = tensor_peak()
@@ -671,8 +671,8 @@ def wl_f32(args, U, torch, rank, size, sets=2):
         return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS",
                 "frac": ach / peak, "peak_source": src, "traffic": w.traffic,
                 "traffic_scope": ("whole call, one ncu capture" if w.traffic else
-                                  "not captured at this size (about 5 GB on the device); the "
-                                  "4096^3 call moves 13x its algorithmic bytes"),
+                                  "not captured at this size; the 4096^3 call moves 13x its "
+                                  "algorithmic bytes, the 8192^3 call 22x"),
                 "basis": basis, "algorithmic_bytes": w.algorithmic_bytes}
     w.roofline = roofline
     return w
